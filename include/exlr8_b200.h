@@ -1,0 +1,188 @@
+/*
+ * exlr8_b200 -- C ABI of the B200 (sm_100a) routed mixture-of-experts path.
+ *
+ * Drop-in boundary for the expert-operator surface of the reference package
+ * exlr8 (GordoAR/MLXLR8 v0.1.21): exlr8/trellis.py, exlr8/fast_router.py,
+ * exlr8/fast_decode.py, exlr8/fast_prefill.py, exlr8/joined_mxfp4.py and the
+ * MoE branch of exlr8/model.py (DecoderLayer.__call__).  Every entry point
+ * below names the reference function it replaces.
+ *
+ * Conventions
+ *  - All tensor pointers are device pointers owned by the caller.  Nothing
+ *    here allocates device memory: calls that need scratch take a caller
+ *    workspace whose size comes from the matching *_workspace() query.
+ *  - `stream` is a cudaStream_t (NULL = legacy default stream).  Every call
+ *    is ordered on that stream and returns without synchronising it.
+ *  - Activations are float32, float16 or bfloat16 (EXLR8_DTYPE_*), row-major.
+ *    Side-scale vectors are float16 (as in EXLR8 checkpoints) or float32.
+ *  - Trellis weights are the EXLR8 "grouped128" packed bytes exactly as
+ *    stored in the checkpoint (K*in*out/8 bytes per matrix, matrices
+ *    concatenated), 16-byte aligned.
+ *  - Return value: EXLR8_OK or a status code; exlr8_status_string() gives
+ *    the reference's error message for it.
+ */
+#ifndef EXLR8_B200_H
+#define EXLR8_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define EXLR8_ABI_VERSION 1
+
+#define EXLR8_DTYPE_F32 0
+#define EXLR8_DTYPE_F16 1
+#define EXLR8_DTYPE_BF16 2
+
+enum exlr8_status {
+  EXLR8_OK = 0,
+  EXLR8_ERR_WIDTH = 1,      /* "EXLR8 trellis width must be 2, 3, or 4"            trellis.py:54-55 */
+  EXLR8_ERR_DIMS = 2,       /* "trellis dimensions must be positive multiples of 128" trellis.py:56-57 */
+  EXLR8_ERR_SIDE = 3,       /* "sharded_side must be 0, 1, or 2"                    trellis.py:58-59 */
+  EXLR8_ERR_BYTES = 4,      /* "packed byte count does not match the trellis dimensions" trellis.py:61-63 */
+  EXLR8_ERR_SCALES = 5,     /* "expert side vectors must contain full signed channel scales" trellis.py:183-184 */
+  EXLR8_ERR_ROWS = 6,       /* "activation rows do not match the expert indices"   trellis.py:189-190 */
+  EXLR8_ERR_WIDTH_X = 7,    /* "activation width does not match in_features"       trellis.py:181-182 */
+  EXLR8_ERR_DTYPE = 8,      /* unsupported activation or scale type */
+  EXLR8_ERR_ALIGN = 9,      /* a pointer is not 16-byte aligned */
+  EXLR8_ERR_WORKSPACE = 10, /* workspace missing or smaller than the *_workspace() size */
+  EXLR8_ERR_ARG = 11,       /* null pointer or out-of-range argument */
+  EXLR8_ERR_CUDA = 12,      /* a CUDA runtime call failed (see exlr8_last_cuda_error) */
+  EXLR8_ERR_ID_RANGE = 13,  /* "Expert IDs must be in 0..256"                       experts.py:158-159 */
+  EXLR8_ERR_UNSUPPORTED = 14
+};
+
+/* Library ABI version (EXLR8_ABI_VERSION). */
+int exlr8_abi_version(void);
+
+/* Message for a status code (the reference's ValueError text where one exists). */
+const char* exlr8_status_string(int status);
+
+/* Text of the last CUDA error seen by this thread ("" if none). */
+const char* exlr8_last_cuda_error(void);
+
+/*
+ * Trellis expert weights: the `packed` and `scales` dictionaries of
+ * exlr8.experts.ExpertLayer (experts.py:97-124).  Index 0/1/2 = gate/up/down.
+ * Gate/up matrices are [hidden -> intermediate] stored side 1, down is
+ * [intermediate -> hidden] stored side 2.  in_scale[p] is [experts][in],
+ * out_scale[p] is [experts][out] (signed channel scales, fp16 or fp32).
+ */
+typedef struct exlr8_trellis_experts {
+  const void* packed[3];
+  int64_t packed_bytes[3];
+  const void* in_scale[3];
+  const void* out_scale[3];
+  int scale_dtype;
+  int64_t scale_experts; /* rows of every scale matrix */
+  int k;                 /* 2, 3 or 4 bits per weight */
+  int hidden;
+  int intermediate;
+} exlr8_trellis_experts;
+
+/*
+ * Dense bf16 shared expert (the BASELINE layout; the reference keeps the
+ * shared expert as trellis matrix 256, experts.py:116-124, which
+ * exlr8_trellis_experts also supports).  Row-major [out][in] bf16 matrices:
+ * gate/up [intermediate][hidden], down [hidden][intermediate].
+ */
+typedef struct exlr8_dense_expert {
+  const void* gate;
+  const void* up;
+  const void* down;
+} exlr8_dense_expert;
+
+/* ---- codec ------------------------------------------------------------ */
+
+/* Value of each 16-bit trellis state (exlr8/trellis.py:43-50 mcg_codebook;
+ * metal/fast_decode_common.metal:4-26 exlr8_decode / exlr8_decode2).
+ * paired != 0 uses the two-state vector form. values: float32[count]. */
+int exlr8_codebook(const uint32_t* states, float* values, int64_t count, int paired, void* stream);
+
+/* Host-only format check (exlr8/trellis.py:53-64 _check_format); writes the
+ * matrix count. */
+int exlr8_check_format(int64_t packed_bytes, int k, int in_features, int out_features, int sharded_side,
+                       int64_t* matrices);
+
+/* Decode matrix `matrix` of a packed buffer to inner weights float32
+ * [in][out] (metal/decode.metal; first stage of trellis.py:199-214). */
+int exlr8_decode_trellis(const void* packed, int64_t packed_bytes, int64_t matrix, int k, int in_features,
+                         int out_features, int sharded_side, float* inner, void* stream);
+
+/* Public dense matrix float32 [out][in] of a single-matrix buffer
+ * (exlr8/trellis.py:199-214 dequantize_trellis). */
+size_t exlr8_dequantize_trellis_workspace(int in_features, int out_features);
+int exlr8_dequantize_trellis(const void* packed, int64_t packed_bytes, const void* suh, const void* svh,
+                             int scale_dtype, int k, int in_features, int out_features, int sharded_side,
+                             float* weight, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- router ----------------------------------------------------------- */
+
+/* exlr8/fast_router.py:17-24 route(logits, bias): logits float32 [rows][256],
+ * bias float32 [256] -> indices uint32 [rows][9] (slot 8 = 256, the shared
+ * expert), scores float32 [rows][8]. */
+int exlr8_route(const float* logits, const float* bias, int64_t rows, uint32_t* indices, float* scores,
+                void* stream);
+
+/* Gate GEMV + route (model.py:366-371 gate in float32, fast_router.py:34):
+ * logits float32 [tokens][256] = x @ gate_weight^T with gate_weight float32
+ * [256][hidden]; then exlr8_route. */
+int exlr8_router(const void* x, int x_dtype, int64_t tokens, int hidden, const float* gate_weight,
+                 const float* bias, float* logits, uint32_t* indices, float* scores, void* stream);
+
+/* ---- trellis expert operators ----------------------------------------- */
+
+/* exlr8/trellis.py:172-196 expert_linear and fast_decode.py:153-165
+ * fast_expert_linear: out[t][s] = T(H(H(x*in_s[e]) @ W_e) * out_s[e]) for
+ * e = indices[t][s].  x is [tokens][in] (per_slot = 0) or
+ * [tokens][slots][in] (per_slot = 1); out is [tokens][slots][out] in x_dtype. */
+size_t exlr8_expert_linear_workspace(int64_t tokens, int slots, int in_features, int out_features,
+                                     int64_t experts);
+int exlr8_expert_linear(const void* x, int x_dtype, int per_slot, const uint32_t* indices, int64_t tokens,
+                        int slots, const void* packed, int64_t packed_bytes, const void* in_scale,
+                        const void* out_scale, int scale_dtype, int64_t scale_experts, int k, int in_features,
+                        int out_features, int sharded_side, void* out, void* workspace, size_t workspace_bytes,
+                        void* stream);
+
+/* exlr8/fast_decode.py:208-221 fast_expert_mlp (and experts.py:150-188
+ * ExpertLayer.__call__): gate/up, typed SwiGLU, down for every selected
+ * slot; out [tokens][slots][hidden] in x_dtype. */
+size_t exlr8_expert_mlp_workspace(int64_t tokens, int slots, int hidden, int intermediate, int64_t experts);
+int exlr8_expert_mlp(const void* x, int x_dtype, int per_slot, const uint32_t* indices, int64_t tokens, int slots,
+                     const exlr8_trellis_experts* experts, void* out, void* workspace, size_t workspace_bytes,
+                     void* stream);
+
+/* exlr8/fast_decode.py:224-244 compiled_expert_mlp_finish: nine slots per
+ * token (eight routed, slot 8 shared), scores float32 [tokens][8], residual
+ * [tokens][hidden]; out = residual + T(T(sum_r v_r*score_r) + v_shared).
+ * With `shared` non-null the shared expert is the dense bf16 expert and
+ * indices[t][8] is ignored. */
+size_t exlr8_expert_mlp_finish_workspace(int64_t tokens, int hidden, int intermediate, int64_t experts);
+int exlr8_expert_mlp_finish(const void* x, int x_dtype, const uint32_t* indices, const float* scores,
+                            const void* residual, int64_t tokens, const exlr8_trellis_experts* experts,
+                            const exlr8_dense_expert* shared, void* out, void* workspace, size_t workspace_bytes,
+                            void* stream);
+
+/* Whole routed-MoE layer: exlr8/fast_router.py:27-37 compiled_finish and the
+ * MoE branch of DecoderLayer.__call__ (model.py:385-418): router gate,
+ * route, experts, shared expert, combine with the residual.  indices/scores
+ * outputs are optional (may be NULL). */
+size_t exlr8_moe_layer_workspace(int64_t tokens, int hidden, int intermediate, int64_t experts);
+int exlr8_moe_layer(const void* x, int x_dtype, const void* residual, int64_t tokens, const float* gate_weight,
+                    const float* bias, const exlr8_trellis_experts* experts, const exlr8_dense_expert* shared,
+                    void* out, uint32_t* indices, float* scores, void* workspace, size_t workspace_bytes,
+                    void* stream);
+
+/* Device-side id check of the last call that used `workspace`: writes the
+ * number of expert ids that were out of range (those slots produce zeros).
+ * Synchronises `stream`. */
+int exlr8_workspace_bad_ids(const void* workspace, int64_t* bad_ids, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* EXLR8_B200_H */

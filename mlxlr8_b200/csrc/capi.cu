@@ -1,0 +1,475 @@
+// extern "C" entry points of include/exlr8_b200.h: argument validation with
+// the reference's error semantics, workspace layout and kernel sequencing.
+
+#include <cstdio>
+#include <cstring>
+
+#include "common.cuh"
+#include "dense.cuh"
+#include "router.cuh"
+#include "trellis_gemv.cuh"
+
+using namespace exlr8;
+
+namespace {
+
+thread_local char g_cuda_error[256] = "";
+
+int cuda_status(cudaError_t err) {
+  if (err == cudaSuccess) return EXLR8_OK;
+  std::snprintf(g_cuda_error, sizeof(g_cuda_error), "%s: %s", cudaGetErrorName(err), cudaGetErrorString(err));
+  return EXLR8_ERR_CUDA;
+}
+
+#define EXLR8_TRY(expr)                          \
+  do {                                           \
+    int _st = cuda_status(expr);                 \
+    if (_st != EXLR8_OK) return _st;             \
+  } while (0)
+
+#define EXLR8_CHECK(expr)                        \
+  do {                                           \
+    int _st = (expr);                            \
+    if (_st != EXLR8_OK) return _st;             \
+  } while (0)
+
+inline cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+inline bool valid_act(int d) { return d == EXLR8_DTYPE_F32 || d == EXLR8_DTYPE_F16 || d == EXLR8_DTYPE_BF16; }
+inline bool valid_scale(int d) { return d == EXLR8_DTYPE_F32 || d == EXLR8_DTYPE_F16; }
+
+constexpr size_t kAlign = 256;
+inline size_t align_up(size_t v) { return (v + kAlign - 1) / kAlign * kAlign; }
+
+// Linear workspace carve-out.
+struct Carver {
+  char* base;
+  size_t used = 0;
+  explicit Carver(void* b) : base(static_cast<char*>(b)) {}
+  template <typename T>
+  T* take(size_t bytes) {
+    T* p = reinterpret_cast<T*>(base ? base + used : nullptr);
+    used += align_up(bytes);
+    return p;
+  }
+};
+
+// Split counts (fast_decode.py:216: gate/up use min(8, max(1, hidden // 768));
+// the down product splits its 2048-deep reduction once more per 1024).
+inline int gate_up_splits(int hidden) {
+  int s = hidden / 768;
+  return s < 1 ? 1 : (s > 8 ? 8 : s);
+}
+inline int down_splits(int intermediate) {
+  int s = intermediate / 1024;
+  return s < 1 ? 1 : (s > 8 ? 8 : s);
+}
+inline int linear_splits(int in_features) {
+  int s = in_features / 768;
+  return s < 1 ? 1 : (s > 8 ? 8 : s);
+}
+inline int dense_splits(int k) {
+  int s = k / 768;
+  return s < 1 ? 1 : (s > 8 ? 8 : s);
+}
+
+int format_status(int64_t packed_bytes, int k, int in_f, int out_f, int side, int64_t* matrices) {
+  if (k != 2 && k != 3 && k != 4) return EXLR8_ERR_WIDTH;
+  if (in_f <= 0 || out_f <= 0 || in_f % 128 || out_f % 128) return EXLR8_ERR_DIMS;
+  if (side < 0 || side > 2) return EXLR8_ERR_SIDE;
+  const int64_t size = static_cast<int64_t>(in_f) * out_f * k / 8;
+  if (packed_bytes <= 0 || packed_bytes % size) return EXLR8_ERR_BYTES;
+  if (matrices) *matrices = packed_bytes / size;
+  return EXLR8_OK;
+}
+
+// Workspace of the trellis MLP over `rows` slots.
+struct MlpLayout {
+  int s1, s2;
+  size_t plan, xh, gu, dxh, dpart;
+  size_t total() const { return plan + xh + gu + dxh + dpart; }
+};
+
+MlpLayout mlp_layout(int64_t rows, int hidden, int inter, int64_t experts) {
+  MlpLayout l;
+  l.s1 = gate_up_splits(hidden);
+  l.s2 = down_splits(inter);
+  l.plan = align_up(plan_bytes(static_cast<int>(rows), static_cast<int>(experts)));
+  l.xh = align_up(2 * rows * hidden * sizeof(float));
+  l.gu = align_up(2 * rows * l.s1 * static_cast<size_t>(inter) * sizeof(float));
+  l.dxh = align_up(rows * static_cast<size_t>(inter) * sizeof(float));
+  l.dpart = align_up(rows * l.s2 * static_cast<size_t>(hidden) * sizeof(float));
+  return l;
+}
+
+struct DenseLayout {
+  int s1, s2;
+  size_t gate, up, h, down, values;
+  size_t total() const { return gate + up + h + down + values; }
+};
+
+DenseLayout dense_layout(int64_t tokens, int hidden, int inter) {
+  DenseLayout l;
+  l.s1 = dense_splits(hidden);
+  l.s2 = dense_splits(inter);
+  l.gate = align_up(l.s1 * tokens * static_cast<size_t>(inter) * sizeof(float));
+  l.up = l.gate;
+  l.h = align_up(tokens * static_cast<size_t>(inter) * sizeof(float));
+  l.down = align_up(l.s2 * tokens * static_cast<size_t>(hidden) * sizeof(float));
+  l.values = align_up(tokens * static_cast<size_t>(hidden) * sizeof(float));
+  return l;
+}
+
+int check_experts(const exlr8_trellis_experts* ex, int64_t* matrices) {
+  if (!ex) return EXLR8_ERR_ARG;
+  if (!valid_scale(ex->scale_dtype)) return EXLR8_ERR_DTYPE;
+  int64_t count = -1;
+  for (int p = 0; p < 3; ++p) {
+    const bool down = p == 2;
+    const int a = down ? ex->intermediate : ex->hidden, b = down ? ex->hidden : ex->intermediate;
+    int64_t m = 0;
+    EXLR8_CHECK(format_status(ex->packed_bytes[p], ex->k, a, b, down ? 2 : 1, &m));
+    if (!ex->packed[p] || !ex->in_scale[p] || !ex->out_scale[p]) return EXLR8_ERR_ARG;
+    if (!aligned16(ex->packed[p])) return EXLR8_ERR_ALIGN;
+    if (count >= 0 && m != count) return EXLR8_ERR_BYTES;
+    count = m;
+  }
+  if (ex->scale_experts != count) return EXLR8_ERR_SCALES;
+  *matrices = count;
+  return EXLR8_OK;
+}
+
+// The trellis MLP over all slots of `ids` ([rows] = tokens*slots).  Writes
+// fp32 down partials; the caller finishes them.  skip_slot (>= 0) leaves out
+// slot `skip_slot` of every token.
+int run_mlp(const void* x, int x_dtype, int per_slot, int slots, const uint32_t* ids, int64_t rows,
+            const exlr8_trellis_experts* ex, int64_t experts, int skip_slot, const MlpLayout& l, Carver& c,
+            float** down_partial, PlanView* plan_out, cudaStream_t s) {
+  const int h = ex->hidden, m = ex->intermediate;
+  PlanView plan = plan_view(c.take<int32_t>(l.plan), static_cast<int>(rows), static_cast<int>(experts));
+  float* xh = c.take<float>(l.xh);
+  float* gu = c.take<float>(l.gu);
+  float* dxh = c.take<float>(l.dxh);
+  float* dpart = c.take<float>(l.dpart);
+  EXLR8_TRY(launch_plan(ids, static_cast<int>(rows), static_cast<int>(experts), slots, skip_slot, plan, s));
+  EXLR8_TRY(launch_prep(x, x_dtype, per_slot, slots, ids, static_cast<int>(rows), ex->in_scale[0], ex->in_scale[1],
+                        ex->scale_dtype, h, static_cast<int>(experts), 2, xh, s));
+  GemvParams gp{};
+  gp.xh = xh;
+  gp.packed0 = static_cast<const uint32_t*>(ex->packed[0]);
+  gp.packed1 = static_cast<const uint32_t*>(ex->packed[1]);
+  gp.partial = gu;
+  gp.plan = plan;
+  gp.counter = 2;
+  gp.k = ex->k;
+  gp.side = 1;
+  gp.in_features = h;
+  gp.out_features = m;
+  gp.splits = l.s1;
+  gp.projections = 2;
+  gp.nslots = static_cast<int>(rows);
+  EXLR8_TRY(launch_gemv(gp, s));
+  EXLR8_TRY(launch_gate_finish(gu, l.s1, ids, static_cast<int>(rows), ex->out_scale[0], ex->out_scale[1],
+                               ex->in_scale[2], ex->scale_dtype, m, static_cast<int>(experts), x_dtype, dxh, s));
+  GemvParams dp = gp;
+  dp.xh = dxh;
+  dp.packed0 = static_cast<const uint32_t*>(ex->packed[2]);
+  dp.packed1 = nullptr;
+  dp.partial = dpart;
+  dp.counter = 3;
+  dp.side = 2;
+  dp.in_features = m;
+  dp.out_features = h;
+  dp.splits = l.s2;
+  dp.projections = 1;
+  EXLR8_TRY(launch_gemv(dp, s));
+  *down_partial = dpart;
+  if (plan_out) *plan_out = plan;
+  return EXLR8_OK;
+}
+
+int run_dense(const void* x, int64_t tokens, const exlr8_dense_expert* sh, int hidden, int inter, int act_dtype,
+              const DenseLayout& l, Carver& c, void** values, cudaStream_t s) {
+  float* gate = c.take<float>(l.gate);
+  float* up = c.take<float>(l.up);
+  void* h = c.take<void>(l.h);
+  float* down = c.take<float>(l.down);
+  void* out = c.take<void>(l.values);
+  const int t = static_cast<int>(tokens);
+  EXLR8_TRY(launch_dense_bf16_gemv(static_cast<const uint16_t*>(x), t, static_cast<const uint16_t*>(sh->gate), inter,
+                                   hidden, l.s1, gate, s));
+  EXLR8_TRY(launch_dense_bf16_gemv(static_cast<const uint16_t*>(x), t, static_cast<const uint16_t*>(sh->up), inter,
+                                   hidden, l.s1, up, s));
+  EXLR8_TRY(launch_dense_swiglu(gate, up, l.s1, t, inter, act_dtype, h, s));
+  EXLR8_TRY(launch_dense_bf16_gemv(static_cast<const uint16_t*>(h), t, static_cast<const uint16_t*>(sh->down), hidden,
+                                   inter, l.s2, down, s));
+  EXLR8_TRY(launch_dense_cast(down, l.s2, t, hidden, act_dtype, out, s));
+  *values = out;
+  return EXLR8_OK;
+}
+
+int check_dense(const exlr8_dense_expert* sh, int x_dtype, int hidden, int inter) {
+  if (!sh) return EXLR8_OK;
+  if (!sh->gate || !sh->up || !sh->down) return EXLR8_ERR_ARG;
+  if (x_dtype != EXLR8_DTYPE_BF16) return EXLR8_ERR_DTYPE;  // bf16 operands for the bf16 matrices
+  if (!aligned16(sh->gate) || !aligned16(sh->up) || !aligned16(sh->down)) return EXLR8_ERR_ALIGN;
+  if (hidden % 32 || inter % 32) return EXLR8_ERR_DIMS;
+  return EXLR8_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int exlr8_abi_version(void) { return EXLR8_ABI_VERSION; }
+
+const char* exlr8_status_string(int status) {
+  switch (status) {
+    case EXLR8_OK: return "ok";
+    case EXLR8_ERR_WIDTH: return "EXLR8 trellis width must be 2, 3, or 4";
+    case EXLR8_ERR_DIMS: return "trellis dimensions must be positive multiples of 128";
+    case EXLR8_ERR_SIDE: return "sharded_side must be 0, 1, or 2";
+    case EXLR8_ERR_BYTES: return "packed byte count does not match the trellis dimensions";
+    case EXLR8_ERR_SCALES: return "expert side vectors must contain full signed channel scales";
+    case EXLR8_ERR_ROWS: return "activation rows do not match the expert indices";
+    case EXLR8_ERR_WIDTH_X: return "activation width does not match in_features";
+    case EXLR8_ERR_DTYPE: return "unsupported activation or scale dtype";
+    case EXLR8_ERR_ALIGN: return "device pointers must be 16-byte aligned";
+    case EXLR8_ERR_WORKSPACE: return "workspace is missing or too small";
+    case EXLR8_ERR_ARG: return "invalid argument";
+    case EXLR8_ERR_CUDA: return "CUDA runtime error";
+    case EXLR8_ERR_ID_RANGE: return "Expert IDs must be in 0..256";
+    case EXLR8_ERR_UNSUPPORTED: return "unsupported configuration";
+    default: return "unknown status";
+  }
+}
+
+const char* exlr8_last_cuda_error(void) { return g_cuda_error; }
+
+int exlr8_codebook(const uint32_t* states, float* values, int64_t count, int paired, void* stream) {
+  if (count < 0 || (count > 0 && (!states || !values))) return EXLR8_ERR_ARG;
+  return cuda_status(launch_codebook(states, values, count, paired, as_stream(stream)));
+}
+
+int exlr8_check_format(int64_t packed_bytes, int k, int in_features, int out_features, int sharded_side,
+                       int64_t* matrices) {
+  return format_status(packed_bytes, k, in_features, out_features, sharded_side, matrices);
+}
+
+int exlr8_decode_trellis(const void* packed, int64_t packed_bytes, int64_t matrix, int k, int in_features,
+                         int out_features, int sharded_side, float* inner, void* stream) {
+  int64_t count = 0;
+  EXLR8_CHECK(format_status(packed_bytes, k, in_features, out_features, sharded_side, &count));
+  if (!packed || !inner || matrix < 0 || matrix >= count) return EXLR8_ERR_ARG;
+  return cuda_status(launch_decode_matrix(static_cast<const uint32_t*>(packed), matrix, k, in_features, out_features,
+                                          sharded_side, inner, as_stream(stream)));
+}
+
+size_t exlr8_dequantize_trellis_workspace(int in_features, int out_features) {
+  return align_up(static_cast<size_t>(in_features) * out_features * sizeof(float));
+}
+
+int exlr8_dequantize_trellis(const void* packed, int64_t packed_bytes, const void* suh, const void* svh,
+                             int scale_dtype, int k, int in_features, int out_features, int sharded_side,
+                             float* weight, void* workspace, size_t workspace_bytes, void* stream) {
+  int64_t count = 0;
+  EXLR8_CHECK(format_status(packed_bytes, k, in_features, out_features, sharded_side, &count));
+  if (count != 1) return EXLR8_ERR_BYTES;
+  if (!packed || !suh || !svh || !weight) return EXLR8_ERR_ARG;
+  if (!valid_scale(scale_dtype)) return EXLR8_ERR_DTYPE;
+  if (!workspace || workspace_bytes < exlr8_dequantize_trellis_workspace(in_features, out_features))
+    return EXLR8_ERR_WORKSPACE;
+  float* inner = static_cast<float*>(workspace);
+  EXLR8_TRY(launch_decode_matrix(static_cast<const uint32_t*>(packed), 0, k, in_features, out_features, sharded_side,
+                                 inner, as_stream(stream)));
+  return cuda_status(
+      launch_dequantize(inner, suh, svh, scale_dtype, in_features, out_features, weight, as_stream(stream)));
+}
+
+int exlr8_route(const float* logits, const float* bias, int64_t rows, uint32_t* indices, float* scores,
+                void* stream) {
+  if (rows < 0 || (rows > 0 && (!logits || !bias || !indices || !scores))) return EXLR8_ERR_ARG;
+  return cuda_status(launch_route(logits, bias, static_cast<int>(rows), indices, scores, 2.5f, 256u,
+                                  as_stream(stream)));
+}
+
+int exlr8_router(const void* x, int x_dtype, int64_t tokens, int hidden, const float* gate_weight, const float* bias,
+                 float* logits, uint32_t* indices, float* scores, void* stream) {
+  if (!valid_act(x_dtype)) return EXLR8_ERR_DTYPE;
+  if (tokens < 0 || hidden <= 0 || hidden % 4) return EXLR8_ERR_ARG;
+  if (tokens == 0) return EXLR8_OK;
+  if (!x || !gate_weight || !bias || !logits || !indices || !scores) return EXLR8_ERR_ARG;
+  if (!aligned16(gate_weight)) return EXLR8_ERR_ALIGN;
+  EXLR8_TRY(launch_gate_logits(x, x_dtype, static_cast<int>(tokens), hidden, gate_weight, logits, 256,
+                               as_stream(stream)));
+  return cuda_status(launch_route(logits, bias, static_cast<int>(tokens), indices, scores, 2.5f, 256u,
+                                  as_stream(stream)));
+}
+
+size_t exlr8_expert_linear_workspace(int64_t tokens, int slots, int in_features, int out_features, int64_t experts) {
+  const int64_t rows = tokens * slots;
+  const int s = linear_splits(in_features);
+  return align_up(plan_bytes(static_cast<int>(rows), static_cast<int>(experts))) +
+         align_up(rows * static_cast<size_t>(in_features) * sizeof(float)) +
+         align_up(rows * s * static_cast<size_t>(out_features) * sizeof(float));
+}
+
+int exlr8_expert_linear(const void* x, int x_dtype, int per_slot, const uint32_t* indices, int64_t tokens, int slots,
+                        const void* packed, int64_t packed_bytes, const void* in_scale, const void* out_scale,
+                        int scale_dtype, int64_t scale_experts, int k, int in_features, int out_features,
+                        int sharded_side, void* out, void* workspace, size_t workspace_bytes, void* stream) {
+  int64_t experts = 0;
+  EXLR8_CHECK(format_status(packed_bytes, k, in_features, out_features, sharded_side, &experts));
+  if (scale_experts != experts) return EXLR8_ERR_SCALES;
+  if (!valid_act(x_dtype) || !valid_scale(scale_dtype)) return EXLR8_ERR_DTYPE;
+  if (tokens < 0 || slots <= 0) return EXLR8_ERR_ROWS;
+  const int64_t rows = tokens * slots;
+  if (rows == 0) return EXLR8_OK;
+  if (!x || !indices || !packed || !in_scale || !out_scale || !out) return EXLR8_ERR_ARG;
+  if (!aligned16(packed)) return EXLR8_ERR_ALIGN;
+  if (rows > (1 << 20)) return EXLR8_ERR_UNSUPPORTED;
+  if (!workspace || workspace_bytes < exlr8_expert_linear_workspace(tokens, slots, in_features, out_features, experts))
+    return EXLR8_ERR_WORKSPACE;
+  cudaStream_t s = as_stream(stream);
+  const int splits = linear_splits(in_features);
+  Carver c(workspace);
+  PlanView plan = plan_view(c.take<int32_t>(plan_bytes(static_cast<int>(rows), static_cast<int>(experts))),
+                            static_cast<int>(rows), static_cast<int>(experts));
+  float* xh = c.take<float>(rows * static_cast<size_t>(in_features) * sizeof(float));
+  float* part = c.take<float>(rows * splits * static_cast<size_t>(out_features) * sizeof(float));
+  EXLR8_TRY(launch_plan(indices, static_cast<int>(rows), static_cast<int>(experts), slots, -1, plan, s));
+  EXLR8_TRY(launch_prep(x, x_dtype, per_slot, slots, indices, static_cast<int>(rows), in_scale, in_scale, scale_dtype,
+                        in_features, static_cast<int>(experts), 1, xh, s));
+  GemvParams gp{};
+  gp.xh = xh;
+  gp.packed0 = static_cast<const uint32_t*>(packed);
+  gp.packed1 = nullptr;
+  gp.partial = part;
+  gp.plan = plan;
+  gp.counter = 2;
+  gp.k = k;
+  gp.side = sharded_side;
+  gp.in_features = in_features;
+  gp.out_features = out_features;
+  gp.splits = splits;
+  gp.projections = 1;
+  gp.nslots = static_cast<int>(rows);
+  EXLR8_TRY(launch_gemv(gp, s));
+  return cuda_status(launch_finish(part, splits, indices, static_cast<int>(rows), out_scale, scale_dtype,
+                                   out_features, static_cast<int>(experts), x_dtype, out, s));
+}
+
+size_t exlr8_expert_mlp_workspace(int64_t tokens, int slots, int hidden, int intermediate, int64_t experts) {
+  return mlp_layout(tokens * slots, hidden, intermediate, experts).total();
+}
+
+int exlr8_expert_mlp(const void* x, int x_dtype, int per_slot, const uint32_t* indices, int64_t tokens, int slots,
+                     const exlr8_trellis_experts* ex, void* out, void* workspace, size_t workspace_bytes,
+                     void* stream) {
+  int64_t experts = 0;
+  EXLR8_CHECK(check_experts(ex, &experts));
+  if (!valid_act(x_dtype)) return EXLR8_ERR_DTYPE;
+  if (tokens < 0 || slots <= 0) return EXLR8_ERR_ROWS;
+  const int64_t rows = tokens * slots;
+  if (rows == 0) return EXLR8_OK;
+  if (!x || !indices || !out) return EXLR8_ERR_ARG;
+  if (rows > (1 << 20)) return EXLR8_ERR_UNSUPPORTED;
+  const MlpLayout l = mlp_layout(rows, ex->hidden, ex->intermediate, experts);
+  if (!workspace || workspace_bytes < l.total()) return EXLR8_ERR_WORKSPACE;
+  cudaStream_t s = as_stream(stream);
+  Carver c(workspace);
+  float* dpart = nullptr;
+  EXLR8_CHECK(run_mlp(x, x_dtype, per_slot, slots, indices, rows, ex, experts, -1, l, c, &dpart, nullptr, s));
+  return cuda_status(launch_finish(dpart, l.s2, indices, static_cast<int>(rows), ex->out_scale[2], ex->scale_dtype,
+                                   ex->hidden, static_cast<int>(experts), x_dtype, out, s));
+}
+
+size_t exlr8_expert_mlp_finish_workspace(int64_t tokens, int hidden, int intermediate, int64_t experts) {
+  return mlp_layout(tokens * 9, hidden, intermediate, experts).total() +
+         dense_layout(tokens, hidden, intermediate).total();
+}
+
+static int mlp_finish_body(const void* x, int x_dtype, const uint32_t* indices, const float* scores,
+                           const void* residual, int64_t tokens, const exlr8_trellis_experts* ex, int64_t experts,
+                           const exlr8_dense_expert* shared, void* out, Carver& c, cudaStream_t s) {
+  const int64_t rows = tokens * 9;
+  const MlpLayout l = mlp_layout(rows, ex->hidden, ex->intermediate, experts);
+  float* dpart = nullptr;
+  EXLR8_CHECK(run_mlp(x, x_dtype, 0, 9, indices, rows, ex, experts, shared ? 8 : -1, l, c, &dpart, nullptr, s));
+  void* shared_values = nullptr;
+  if (shared) {
+    const DenseLayout dl = dense_layout(tokens, ex->hidden, ex->intermediate);
+    EXLR8_CHECK(run_dense(x, tokens, shared, ex->hidden, ex->intermediate, x_dtype, dl, c, &shared_values, s));
+  }
+  return cuda_status(launch_finish_fused(dpart, l.s2, indices, static_cast<int>(tokens), ex->out_scale[2],
+                                         ex->scale_dtype, ex->hidden, static_cast<int>(experts), scores, residual,
+                                         shared_values, x_dtype, out, s));
+}
+
+int exlr8_expert_mlp_finish(const void* x, int x_dtype, const uint32_t* indices, const float* scores,
+                            const void* residual, int64_t tokens, const exlr8_trellis_experts* ex,
+                            const exlr8_dense_expert* shared, void* out, void* workspace, size_t workspace_bytes,
+                            void* stream) {
+  int64_t experts = 0;
+  EXLR8_CHECK(check_experts(ex, &experts));
+  if (!valid_act(x_dtype)) return EXLR8_ERR_DTYPE;
+  EXLR8_CHECK(check_dense(shared, x_dtype, ex->hidden, ex->intermediate));
+  if (tokens < 0) return EXLR8_ERR_ROWS;
+  if (tokens == 0) return EXLR8_OK;
+  if (!x || !indices || !scores || !residual || !out) return EXLR8_ERR_ARG;
+  if (tokens * 9 > (1 << 20)) return EXLR8_ERR_UNSUPPORTED;
+  if (!workspace || workspace_bytes < exlr8_expert_mlp_finish_workspace(tokens, ex->hidden, ex->intermediate, experts))
+    return EXLR8_ERR_WORKSPACE;
+  Carver c(workspace);
+  return mlp_finish_body(x, x_dtype, indices, scores, residual, tokens, ex, experts, shared, out, c,
+                         as_stream(stream));
+}
+
+size_t exlr8_moe_layer_workspace(int64_t tokens, int hidden, int intermediate, int64_t experts) {
+  return exlr8_expert_mlp_finish_workspace(tokens, hidden, intermediate, experts) +
+         align_up(tokens * 256 * sizeof(float)) + align_up(tokens * 9 * sizeof(uint32_t)) +
+         align_up(tokens * 8 * sizeof(float));
+}
+
+int exlr8_moe_layer(const void* x, int x_dtype, const void* residual, int64_t tokens, const float* gate_weight,
+                    const float* bias, const exlr8_trellis_experts* ex, const exlr8_dense_expert* shared, void* out,
+                    uint32_t* indices, float* scores, void* workspace, size_t workspace_bytes, void* stream) {
+  int64_t experts = 0;
+  EXLR8_CHECK(check_experts(ex, &experts));
+  if (!valid_act(x_dtype)) return EXLR8_ERR_DTYPE;
+  EXLR8_CHECK(check_dense(shared, x_dtype, ex->hidden, ex->intermediate));
+  if (!shared && experts < 257) return EXLR8_ERR_ID_RANGE;  // slot 8 routes to trellis matrix 256
+  if (tokens < 0) return EXLR8_ERR_ROWS;
+  if (tokens == 0) return EXLR8_OK;
+  if (!x || !residual || !gate_weight || !bias || !out) return EXLR8_ERR_ARG;
+  if (!aligned16(gate_weight)) return EXLR8_ERR_ALIGN;
+  if (tokens * 9 > (1 << 20)) return EXLR8_ERR_UNSUPPORTED;
+  if (!workspace || workspace_bytes < exlr8_moe_layer_workspace(tokens, ex->hidden, ex->intermediate, experts))
+    return EXLR8_ERR_WORKSPACE;
+  cudaStream_t s = as_stream(stream);
+  Carver c(workspace);
+  // The MLP part comes first so that the id-check header sits at offset 0.
+  Carver head(workspace);
+  head.used = exlr8_expert_mlp_finish_workspace(tokens, ex->hidden, ex->intermediate, experts);
+  float* logits = head.take<float>(tokens * 256 * sizeof(float));
+  uint32_t* ids_buf = head.take<uint32_t>(tokens * 9 * sizeof(uint32_t));
+  float* scores_buf = head.take<float>(tokens * 8 * sizeof(float));
+  uint32_t* ids = indices ? indices : ids_buf;
+  float* sc = scores ? scores : scores_buf;
+  EXLR8_TRY(launch_gate_logits(x, x_dtype, static_cast<int>(tokens), ex->hidden, gate_weight, logits, 256, s));
+  EXLR8_TRY(launch_route(logits, bias, static_cast<int>(tokens), ids, sc, 2.5f, 256u, s));
+  return mlp_finish_body(x, x_dtype, ids, sc, residual, tokens, ex, experts, shared, out, c, s);
+}
+
+int exlr8_workspace_bad_ids(const void* workspace, int64_t* bad_ids, void* stream) {
+  if (!workspace || !bad_ids) return EXLR8_ERR_ARG;
+  int32_t header[16];
+  EXLR8_TRY(cudaMemcpyAsync(header, workspace, sizeof(header), cudaMemcpyDeviceToHost, as_stream(stream)));
+  EXLR8_TRY(cudaStreamSynchronize(as_stream(stream)));
+  *bad_ids = header[8];
+  return EXLR8_OK;
+}
+
+}  // extern "C"

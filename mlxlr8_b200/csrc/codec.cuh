@@ -1,0 +1,118 @@
+// EXLR8 trellis codec on the device: codeword -> exact E4M3-rounded value,
+// the direct K4 codeword extraction, and the generic K sliding windows.
+//
+// Format (exlr8/trellis.py:43-50,78-102; metal/fast_decode_common.metal:4-26):
+// a 16-bit trellis state cw is hashed as (cw * 0xCBAC1FED mod 2^32) &
+// 0x8FFF8FFF ^ 0x3B603B60; the two 16-bit halves are float16 numbers, their
+// float16 sum rounded to E4M3 (nearest, ties to even) is the weight.  The
+// E4M3 rounding here is the hardware float16x2 -> e4m3x2 conversion
+// (round-to-nearest, finite saturation) and back, which the test-suite checks
+// against the reference codebook over all 65,536 states.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+namespace exlr8 {
+
+constexpr uint32_t kMcgMul = 0xCBAC1FEDu;
+constexpr uint32_t kMcgMask = 0x8FFF8FFFu;
+constexpr uint32_t kMcgXor = 0x3B603B60u;
+
+__device__ __forceinline__ uint32_t lop_mask_xor(uint32_t v) {
+  return (v & kMcgMask) ^ kMcgXor;
+}
+
+// Round an f16x2 to the nearest E4M3 pair and widen it back to f16x2.
+__device__ __forceinline__ uint32_t round_e4m3_f16x2(uint32_t h2) {
+  uint16_t e;
+  uint32_t r;
+  asm("cvt.rn.satfinite.e4m3x2.f16x2 %0, %1;" : "=h"(e) : "r"(h2));
+  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(r) : "h"(e));
+  return r;
+}
+
+// Values of two 16-bit states as an f16x2 (low half = state a).
+__device__ __forceinline__ uint32_t decode_pair(uint32_t cw_a, uint32_t cw_b) {
+  uint32_t pa = cw_a * kMcgMul;
+  uint32_t pb = cw_b * kMcgMul;
+  uint32_t lo = lop_mask_xor(__byte_perm(pa, pb, 0x5410));  // (pb.lo : pa.lo)
+  uint32_t hi = lop_mask_xor(__byte_perm(pa, pb, 0x7632));  // (pb.hi : pa.hi)
+  __half2 s = __hadd2(*reinterpret_cast<__half2*>(&lo), *reinterpret_cast<__half2*>(&hi));
+  return round_e4m3_f16x2(*reinterpret_cast<uint32_t*>(&s));
+}
+
+__device__ __forceinline__ float decode_value(uint32_t cw) {
+  uint32_t r = decode_pair(cw & 0xFFFFu, cw & 0xFFFFu);
+  return __half2float(__ushort_as_half(static_cast<uint16_t>(r & 0xFFFFu)));
+}
+
+// The eight codewords of lane l of a K4 tile: the stream window (prior:word)
+// where word is tile word l and prior is word l-1 (cyclic).  Codeword j ends
+// 4*(7-j) bits above bit 0 of word (fast_decode_linear.metal:147-155).
+__device__ __forceinline__ void k4_codewords(uint32_t word, uint32_t prior, uint32_t cw[8]) {
+  cw[0] = __funnelshift_r(word, prior, 28) & 0xFFFFu;
+  cw[1] = __funnelshift_r(word, prior, 24) & 0xFFFFu;
+  cw[2] = __funnelshift_r(word, prior, 20) & 0xFFFFu;
+  cw[3] = word >> 16;
+  cw[4] = (word >> 12) & 0xFFFFu;
+  cw[5] = (word >> 8) & 0xFFFFu;
+  cw[6] = (word >> 4) & 0xFFFFu;
+  cw[7] = word & 0xFFFFu;
+}
+
+// mma.sync m16n8k16 A-fragment registers of one decoded 16x16 tile.  With the
+// tile used as A = W^T (rows = output columns, k = input rows), the trellis
+// tensor-core permutation places codeword j of lane l at exactly the fragment
+// element the instruction expects: {a0,a1}=j0,j1  {a2,a3}=j4,j5
+// {a4,a5}=j2,j3  {a6,a7}=j6,j7.
+__device__ __forceinline__ void tile_fragment(const uint32_t cw[8], uint32_t a[4]) {
+  a[0] = decode_pair(cw[0], cw[1]);
+  a[1] = decode_pair(cw[4], cw[5]);
+  a[2] = decode_pair(cw[2], cw[3]);
+  a[3] = decode_pair(cw[6], cw[7]);
+}
+
+// Generic K: per lane two 64-bit windows (groups of four codewords); the
+// window of group g is words (left, right) of the tile, codeword 4g+q sits at
+// shift + (3-q)*K (trellis.metal:33-40, decode.metal:19-23).
+struct GenericGeometry {
+  uint32_t left[2], right[2], shift[2];
+};
+
+__device__ __forceinline__ GenericGeometry generic_geometry(int k, int lane) {
+  GenericGeometry g;
+  const uint32_t words = 8u * k;
+#pragma unroll
+  for (int grp = 0; grp < 2; ++grp) {
+    uint32_t last_bit = (lane * 8u + grp * 4u + 4u) * k + 256u * k;
+    uint32_t last_word = (last_bit - 1u) / 32u;
+    g.left[grp] = (last_word - 1u) % words;
+    g.right[grp] = last_word % words;
+    g.shift[grp] = (last_word + 1u) * 32u - last_bit;
+  }
+  return g;
+}
+
+__device__ __forceinline__ void generic_codewords(const uint32_t* tile, int k, const GenericGeometry& g,
+                                                  uint32_t cw[8]) {
+#pragma unroll
+  for (int grp = 0; grp < 2; ++grp) {
+    uint64_t merged = (static_cast<uint64_t>(tile[g.left[grp]]) << 32) | tile[g.right[grp]];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      cw[grp * 4 + q] = static_cast<uint32_t>(merged >> (g.shift[grp] + (3 - q) * k)) & 0xFFFFu;
+    }
+  }
+}
+
+// Storage index (in tiles) of tile (tk, tn) of matrix e: side 1/0 output
+// blocks first, side 2 input blocks first (fast_decode_linear.metal:91-95).
+__device__ __forceinline__ int64_t tile_index(int64_t e, int tk, int tn, int in_tiles, int out_tiles, int side) {
+  if (side == 2) {
+    return ((((e * (in_tiles / 8) + tk / 8) * (out_tiles / 8) + tn / 8) * 8 + tk % 8) * 8) + tn % 8;
+  }
+  return ((e * (out_tiles / 8) + tn / 8) * in_tiles + tk) * 8 + tn % 8;
+}
+
+}  // namespace exlr8

@@ -1,0 +1,70 @@
+"""C-ABI library: loads on a CPU-only machine, exports every declared symbol,
+and its host-side format checks raise the reference's errors."""
+
+import ctypes
+import re
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from mlxlr8_b200 import _lib
+
+HEADER = Path(__file__).resolve().parents[1] / "include" / "exlr8_b200.h"
+
+
+def declared_functions():
+    text = HEADER.read_text()
+    return sorted(set(re.findall(r"^\s*(?:int|size_t|const char\*)\s+(exlr8_\w+)\(", text, re.M)))
+
+
+def test_library_exports_every_declared_symbol():
+    lib = ctypes.CDLL(str(_lib.LIBRARY))
+    names = declared_functions()
+    assert len(names) >= 15
+    for name in names:
+        assert hasattr(lib, name), name
+    assert set(names) == set(_lib.EXPORTED)
+
+
+def test_abi_version_and_status_strings():
+    lib = _lib.load()
+    assert lib.exlr8_abi_version() == 1
+    assert lib.exlr8_status_string(4).decode() == "packed byte count does not match the trellis dimensions"
+    assert lib.exlr8_status_string(13).decode() == "Expert IDs must be in 0..256"
+
+
+@pytest.mark.parametrize("args, message", [
+    ((4, 4, 128, 128, 1), "byte count"),
+    ((8192, 5, 128, 128, 1), "width must be 2, 3, or 4"),
+    ((8192, 4, 100, 128, 1), "multiples of 128"),
+    ((8192, 4, 128, 128, 3), "sharded_side"),
+])
+def test_format_errors_match_reference(args, message):
+    from mlxlr8_b200.trellis import check_format
+
+    nbytes, k, a, b, side = args
+    with pytest.raises(ValueError, match=message):
+        check_format(np_bytes(nbytes), k, a, b, side)
+
+
+def np_bytes(n):
+    import torch
+
+    return torch.zeros(n, dtype=torch.uint8)
+
+
+def test_format_counts_matrices():
+    from mlxlr8_b200.trellis import check_format
+
+    assert check_format(np_bytes(3 * 128 * 256 // 2), 4, 128, 256, 1) == 3
+    assert check_format(np_bytes(2 * 128 * 256 * 3 // 8), 3, 256, 128, 2) == 2
+
+
+def test_operators_fail_loudly_without_cuda(monkeypatch):
+    import torch
+    from mlxlr8_b200 import trellis
+
+    monkeypatch.setattr(torch.cuda, "is_available", lambda: False)
+    with pytest.raises(RuntimeError, match="no CPU fallback"):
+        trellis.mcg_codebook()
