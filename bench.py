@@ -1,0 +1,366 @@
+"""Benchmark: one GLM-5-shape routed-MoE layer step (exlr8 MoE branch) on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--tokens T] [--impl {b200,reference}]
+
+Workload (decode): T tokens (default 1) through one MoE
+layer -- router (fp32 gate 6144->256, sigmoid + bias top-8, renormalised x2.5),
+256 routed K4-trellis SwiGLU experts (6144 -> 2048 -> 6144), the bf16 shared
+expert and the combine with the residual.  Weights are seeded synthetic
+tensors of that shape (no checkpoints here), one independent layer per step,
+cycling through --layers layers so each step streams weights that are not in
+L2 (every step touches > 233 MB; 8 layers hold ~39 GB).  A "step" is one layer
+pass over one batch of T tokens; the metric is tokens per second.
+
+value: device-resident inputs, the layer call replayed from a CUDA graph.
+e2e:   the public API (MoELayer.__call__) with pinned host buffers: per step
+       the H2D copy of x and residual and the D2H copy of the output are in
+       the timed region.
+roofline: the dominant kernel (trellis gate/up streaming GEMV), its launch
+       durations measured with CUDA events on the launching stream during a
+       profiled pass of the same K steps; algorithmic bytes = packed trellis
+       codes it must stream (U experts x 2 matrices x K*h*m/8).
+cpu_baseline: the C restatement of the layer (oracle/c, OpenMP) on the host's
+       cores, a bounded number of full layer steps.
+--impl reference: the reference's expert operators are Metal kernels
+       (unavailable here), so the reference arm is that same CPU restatement
+       of the reference's arithmetic, on all host threads.
+
+Under torchrun (N > 1) every rank runs its own layers (replicas, weak
+scaling); time is the max over ranks.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+HIDDEN, INTER, EXPERTS, K_BITS = 6144, 2048, 256, 4
+METRIC = "MoE-layer tokens/s (decode GB/s vs HBM; prefill TFLOPS) at 1/2/4/8 B200"
+
+# dram__bytes_read.sum + dram__bytes_write.sum per launch of the gate/up
+# streaming GEMV, from one ncu capture of a 9-expert case (18 expert matrices,
+# profiles/trellis_stream_gate_up_decode.txt), per expert matrix; the bench
+# scales it by the matrices its launches stream.
+TRAFFIC_PER_MATRIX = (113_756_928 + 0) / 18
+
+
+def parse():
+    p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=4000)
+    p.add_argument("--warmup", type=int, default=20)
+    p.add_argument("--tokens", type=int, default=1)
+    p.add_argument("--layers", type=int, default=8)
+    p.add_argument("--impl", choices=("b200", "reference"), default="b200")
+    p.add_argument("--cpu-seconds", type=float, default=10.0)
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    return p.parse_args()
+
+
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index):
+        self.device_index = device_index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.device_index}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+
+    def summary(self):
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in getattr(self, "lines", []):
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+            except ValueError:
+                continue
+            for name, flag in zip(names, f[5:9]):
+                if flag.lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def measured_peaks():
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        d = json.loads(path.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def cpu_baseline(layer, tokens, seconds, rank0=True):
+    """Time the C restatement of the layer on host copies of one layer."""
+    import numpy as np
+
+    from mlxlr8_b200.synthetic import host_copy
+    from oracle import c_oracle, trellis_oracle as ref
+
+    x, residual = layer.tokens(tokens, seed_offset=77)
+    hc = host_copy(layer)
+    shared = tuple(ref.bf16_bits(s) for s in hc["shared"])
+    xs, rs = x.float().cpu().numpy(), residual.float().cpu().numpy()
+    args = (xs, rs, hc["gate_weight"], hc["bias"], hc["packed"], hc["scales"], K_BITS, HIDDEN, INTER, shared)
+    t0 = time.perf_counter()
+    c_oracle.moe_layer(*args)
+    first = time.perf_counter() - t0
+    steps = max(2, int(seconds / max(first, 1e-3)))
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        c_oracle.moe_layer(*args)
+    dt = time.perf_counter() - t0
+    return steps, dt, c_oracle.threads()
+
+
+def reference_arm(args, world, rank):
+    """CPU restatement of the reference operators (the Metal kernels cannot run here)."""
+    if rank != 0:
+        return
+    import torch
+
+    from mlxlr8_b200.synthetic import make_layer
+
+    # Build one layer on the GPU when present (fast seeded generation), else on CPU.
+    device = "cuda" if torch.cuda.is_available() else "cpu"
+    layer = make_layer(seed=1000, device=device)
+    budget = 60.0
+    steps_done, dt, cores = cpu_baseline(layer, args.tokens, budget)
+    # Warm-up is the first call inside cpu_baseline; steps_done full layer steps timed.
+    value = steps_done * args.tokens / dt
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
+        "steps": steps_done, "warmup": 1, "ms_per_step": 1000 * dt / steps_done, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": f"decode T={args.tokens}, one GLM-5-shape MoE layer (256 K4 trellis experts + bf16 "
+                               "shared expert)", "tokens": args.tokens, "hidden": HIDDEN, "intermediate": INTER,
+                   "experts": EXPERTS, "k_bits": K_BITS},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
+                         "sample": f"{steps_done} full layer steps of T={args.tokens} (about {budget:.0f} s budget; "
+                                   f"--steps {args.steps} requested)"},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "exlr8's expert operators are Metal compute kernels (no CPU backend); this arm is the C restatement "
+                "of their arithmetic (oracle/c), timed on the host cores",
+    }
+    print(json.dumps(line), flush=True)
+
+
+def unique_experts(ids_list):
+    return [len(set(int(e) for e in ids[:, :8].reshape(-1).tolist())) for ids in ids_list]
+
+
+def main():
+    args = parse()
+    world, rank, local = dist_setup()
+    if args.impl == "reference":
+        reference_arm(args, world, rank)
+        return
+    import torch
+    import torch.distributed as dist
+
+    from mlxlr8_b200 import _lib
+    from mlxlr8_b200.moe import MoELayer
+    from mlxlr8_b200.synthetic import make_layer
+
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", init_method="env://", device_id=device)
+    T, L = args.tokens, args.layers
+
+    layers, moes, xs, rs = [], [], [], []
+    for i in range(L):
+        layer = make_layer(seed=1000 + 97 * i + 7919 * rank, device=device)
+        layers.append(layer)
+        moes.append(MoELayer(layer.gate_weight, layer.bias, layer.experts))
+        x, r = layer.tokens(T, seed_offset=i)
+        xs.append(x)
+        rs.append(r)
+    torch.cuda.synchronize()
+
+    # CUDA graphs of one layer call each (inputs resident in HBM).
+    outs, graphs = [], []
+    stream = torch.cuda.Stream(device)
+    with torch.cuda.stream(stream):
+        for i in range(L):
+            moes[i](xs[i], rs[i])  # allocate the cached workspace before capture
+        torch.cuda.synchronize()
+        for i in range(L):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                outs.append(moes[i](xs[i], rs[i]))
+            graphs.append(g)
+    torch.cuda.synchronize()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    # ---- headline: graph replay, device-resident inputs ----
+    with torch.cuda.stream(stream):
+        for s in range(args.warmup):
+            graphs[s % L].replay()
+    barrier()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        with torch.cuda.stream(stream):
+            start.record(stream)
+            for s in range(args.steps):
+                graphs[s % L].replay()
+            stop.record(stream)
+        stop.synchronize()
+    barrier()
+    elapsed = start.elapsed_time(stop)
+    if world > 1:
+        t = torch.tensor([elapsed], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        elapsed = float(t.item())
+    ms_per_step = elapsed / args.steps
+    value = world * T * args.steps / (elapsed / 1000.0)
+
+    # ---- profiled pass: per-kernel CUDA events on the launching stream ----
+    routing = []
+    with torch.cuda.stream(stream):
+        for s in range(min(args.warmup, L)):
+            moes[s % L](xs[s % L], rs[s % L])
+        torch.cuda.synchronize()
+        prof_steps = min(args.steps, 400)
+        _lib.profile_enable(True, capacity=prof_steps * 16 + 64)
+        for s in range(prof_steps):
+            moes[s % L](xs[s % L], rs[s % L])
+        torch.cuda.synchronize()
+        prof = _lib.profile_read()
+        _lib.profile_enable(False)
+        for i in range(L):
+            _, ids, _ = moes[i](xs[i], rs[i], return_routing=True)
+            routing.append(ids.cpu().numpy())
+    launches_per_step = sum(n for n, _ in prof.values()) / max(prof_steps, 1)
+    u = unique_experts(routing)
+    u_mean = sum(u) / len(u)
+    codes_per_matrix = HIDDEN * INTER * K_BITS // 8
+    gate_up_n, gate_up_ms = prof["gate_up"]
+    gate_up_avg_ms = gate_up_ms / max(gate_up_n, 1)
+    gate_up_bytes = u_mean * 2 * codes_per_matrix
+    achieved = gate_up_bytes / (gate_up_avg_ms / 1000.0) / 1e9
+    peak, peak_kind = measured_peaks()
+    share = {k: round(ms / max(sum(v for _, v in prof.values()), 1e-9), 4) for k, (n, ms) in prof.items()}
+
+    # Whole-step algorithmic bytes (SURVEY decode formula) for context.
+    step_bytes = u_mean * 3 * codes_per_matrix + u_mean * 49152 + 3 * HIDDEN * INTER * 2 + 256 * HIDDEN * 4 + 4 * T * HIDDEN
+
+    # ---- e2e through the public API with host buffers ----
+    xh = [x.cpu().pin_memory() for x in xs]
+    rh = [r.cpu().pin_memory() for r in rs]
+    oh = [torch.empty(T, HIDDEN, dtype=torch.bfloat16).pin_memory() for _ in range(L)]
+    xd = [torch.empty_like(x) for x in xs]
+    rd = [torch.empty_like(r) for r in rs]
+    e2e_steps = min(args.steps, 1000)
+    with torch.cuda.stream(stream):
+        for s in range(args.warmup):
+            i = s % L
+            xd[i].copy_(xh[i], non_blocking=True)
+            rd[i].copy_(rh[i], non_blocking=True)
+            oh[i].copy_(moes[i](xd[i], rd[i]), non_blocking=True)
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for s in range(e2e_steps):
+            i = s % L
+            xd[i].copy_(xh[i], non_blocking=True)
+            rd[i].copy_(rh[i], non_blocking=True)
+            oh[i].copy_(moes[i](xd[i], rd[i]), non_blocking=True)
+        e1.record(stream)
+        e1.synchronize()
+    e2e_ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e_value = world * T * e2e_steps / (e2e_ms / 1000.0)
+    h2d = 2 * T * HIDDEN * 2
+    d2h = T * HIDDEN * 2
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        steps_done, dt, cores = cpu_baseline(layers[0], T, args.cpu_seconds)
+        cpu = {"value": steps_done * T / dt, "unit": "tokens/s", "cores": cores, "kind": "port",
+               "sample": f"{steps_done} full layer steps of T={T} on host copies of one layer"}
+
+    if world > 1:
+        dist.barrier()
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": f"decode T={T}, one GLM-5-shape MoE layer (256 K4 trellis experts + bf16 shared "
+                                   f"expert, fp32 router)", "tokens": T, "hidden": HIDDEN, "intermediate": INTER,
+                       "experts": EXPERTS, "k_bits": K_BITS, "layers_cycled": L,
+                       "l2": "inputs larger than L2: each step is a different layer (>233 MB touched per step)",
+                       "parallelism": f"replicas x{world}" if world > 1 else "single GPU"},
+            "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "steps": e2e_steps},
+            "roofline": {"bound": "hbm", "kernel": "trellis_stream_kernel<4> (gate/up)", "achieved": achieved,
+                         "peak": peak, "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peak,
+                         "traffic": TRAFFIC_PER_MATRIX * 2 * u_mean,
+                         "algorithmic_bytes_per_launch": gate_up_bytes, "avg_launch_ms": gate_up_avg_ms,
+                         "unique_experts_mean": u_mean},
+            "step_roofline": {"algorithmic_bytes": step_bytes, "achieved_gbs": step_bytes / (ms_per_step / 1000) / 1e9,
+                              "frac": step_bytes / (ms_per_step / 1000) / 1e9 / peak},
+            "kernel_share": share,
+            "gpu_launches": int(round(launches_per_step * args.steps)),
+            "clocks": clocks.summary(),
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    # Release graphs before tearing down the process group.
+    del graphs
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

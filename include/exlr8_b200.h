@@ -176,6 +176,29 @@ int exlr8_moe_layer(const void* x, int x_dtype, const void* residual, int64_t to
                     void* out, uint32_t* indices, float* scores, void* workspace, size_t workspace_bytes,
                     void* stream);
 
+/* ---- kernel timing ----------------------------------------------------- */
+
+/* Kernel kinds reported by exlr8_profile_read. */
+enum exlr8_kernel_kind {
+  EXLR8_KERNEL_ROUTER = 0,       /* gate GEMV + top-8 selection */
+  EXLR8_KERNEL_PLAN = 1,         /* expert sort / group table */
+  EXLR8_KERNEL_PREP = 2,         /* input transform -> activation fragments */
+  EXLR8_KERNEL_GATE_UP = 3,      /* trellis gate/up streaming GEMV */
+  EXLR8_KERNEL_GATE_FINISH = 4,  /* gate/up finish -> down fragments */
+  EXLR8_KERNEL_DOWN = 5,         /* trellis down streaming GEMV */
+  EXLR8_KERNEL_FINISH = 6,       /* output finish / combine */
+  EXLR8_KERNEL_DENSE = 7,        /* bf16 shared expert */
+  EXLR8_KERNEL_KINDS = 8
+};
+
+/* Opt-in per-launch timing (the reference prints per-layer seconds with
+ * --trace, cli.py:51-63; this times every kernel): while enabled on the
+ * calling thread, each launch is bracketed by CUDA events on its stream, up
+ * to `capacity` launches.  exlr8_profile_read synchronises the recorded
+ * events and returns the launch count and total milliseconds of one kind. */
+int exlr8_profile_enable(int enable, int capacity);
+int exlr8_profile_read(int kind, int64_t* launches, double* total_ms);
+
 /* Device-side id check of the last call that used `workspace`: writes the
  * number of expert ids that were out of range (those slots produce zeros).
  * Synchronises `stream`. */

@@ -69,6 +69,8 @@ _SIGNATURES = {
     "exlr8_moe_layer": (c_int, [c_void_p, c_int, c_void_p, c_int64, c_void_p, c_void_p, POINTER(TrellisExperts),
                                 POINTER(DenseExpert), c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),
     "exlr8_workspace_bad_ids": (c_int, [c_void_p, POINTER(c_int64), c_void_p]),
+    "exlr8_profile_enable": (c_int, [c_int, c_int]),
+    "exlr8_profile_read": (c_int, [c_int, POINTER(c_int64), POINTER(ctypes.c_double)]),
 }
 
 EXPORTED = tuple(_SIGNATURES)
@@ -140,6 +142,25 @@ def scale_code(t: torch.Tensor) -> int:
         return SCALE_CODES[t.dtype]
     except KeyError:
         raise ValueError(f"unsupported side-scale dtype {t.dtype}") from None
+
+
+KERNEL_KINDS = ("router", "plan", "prep", "gate_up", "gate_finish", "down", "finish", "dense")
+
+
+def profile_enable(enable: bool, capacity: int = 65536) -> None:
+    """Bracket every library launch on this thread with CUDA events."""
+    check(load().exlr8_profile_enable(int(enable), capacity))
+
+
+def profile_read() -> dict:
+    """{kind: (launches, total_ms)} of the launches recorded since enabling."""
+    out = {}
+    for i, name in enumerate(KERNEL_KINDS):
+        n = ctypes.c_int64(0)
+        ms = ctypes.c_double(0.0)
+        check(load().exlr8_profile_read(i, ctypes.byref(n), ctypes.byref(ms)))
+        out[name] = (int(n.value), float(ms.value))
+    return out
 
 
 def workspace(nbytes: int, device: torch.device) -> torch.Tensor:

@@ -7,6 +7,7 @@
 #include "common.cuh"
 #include "dense.cuh"
 #include "router.cuh"
+#include "stream.cuh"
 #include "trellis_gemv.cuh"
 
 using namespace exlr8;
@@ -35,6 +36,36 @@ int cuda_status(cudaError_t err) {
 
 inline cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
 
+// ---- opt-in launch timing (exlr8_profile_*) --------------------------------
+struct Profiler {
+  bool on = false;
+  int capacity = 0, used = 0;
+  cudaEvent_t* events = nullptr;  // 2 * capacity
+  int* kinds = nullptr;
+};
+thread_local Profiler g_prof;
+
+struct ProfileScope {
+  int slot = -1;
+  cudaStream_t stream;
+  ProfileScope(int kind, cudaStream_t s) : stream(s) {
+    if (g_prof.on && g_prof.used < g_prof.capacity) {
+      slot = g_prof.used++;
+      g_prof.kinds[slot] = kind;
+      cudaEventRecord(g_prof.events[2 * slot], s);
+    }
+  }
+  ~ProfileScope() {
+    if (slot >= 0) cudaEventRecord(g_prof.events[2 * slot + 1], stream);
+  }
+};
+
+#define EXLR8_TIMED(kind, s, expr)   \
+  do {                               \
+    ProfileScope _scope(kind, s);    \
+    EXLR8_TRY(expr);                 \
+  } while (0)
+
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 inline bool valid_act(int d) { return d == EXLR8_DTYPE_F32 || d == EXLR8_DTYPE_F16 || d == EXLR8_DTYPE_BF16; }
@@ -56,23 +87,28 @@ struct Carver {
   }
 };
 
-// Split counts (fast_decode.py:216: gate/up use min(8, max(1, hidden // 768));
-// the down product splits its 2048-deep reduction once more per 1024).
-inline int gate_up_splits(int hidden) {
-  int s = hidden / 768;
-  return s < 1 ? 1 : (s > 8 ? 8 : s);
+// K splits.  Gate/up follow fast_decode.py:216 (min(8, max(1, hidden // 768)));
+// the down product splits once per 1024 inputs.  Splits are rounded to whole
+// 128-wide blocks (stream.cuh kt_per_split).
+struct Splits {
+  int kt, count;
+};
+inline Splits make_splits(int in_features, int nominal) {
+  if (nominal < 1) nominal = 1;
+  if (nominal > 8) nominal = 8;
+  Splits s;
+  s.kt = kt_per_split(in_features, nominal);
+  s.count = split_count(in_features, s.kt);
+  return s;
 }
-inline int down_splits(int intermediate) {
-  int s = intermediate / 1024;
-  return s < 1 ? 1 : (s > 8 ? 8 : s);
-}
-inline int linear_splits(int in_features) {
-  int s = in_features / 768;
-  return s < 1 ? 1 : (s > 8 ? 8 : s);
-}
+inline Splits gate_up_splits(int hidden) { return make_splits(hidden, hidden / 768); }
+inline Splits down_splits(int intermediate) { return make_splits(intermediate, intermediate / 1024); }
+inline Splits linear_splits(int in_features) { return make_splits(in_features, in_features / 768); }
+// The dense bf16 GEMV splits K into 384-wide pieces (enough warps in flight
+// to stream the weights at full bandwidth for one to a few tokens).
 inline int dense_splits(int k) {
-  int s = k / 768;
-  return s < 1 ? 1 : (s > 8 ? 8 : s);
+  int s = k / 384;
+  return s < 1 ? 1 : (s > 16 ? 16 : s);
 }
 
 int format_status(int64_t packed_bytes, int k, int in_f, int out_f, int side, int64_t* matrices) {
@@ -87,9 +123,9 @@ int format_status(int64_t packed_bytes, int k, int in_f, int out_f, int side, in
 
 // Workspace of the trellis MLP over `rows` slots.
 struct MlpLayout {
-  int s1, s2;
-  size_t plan, xh, gu, dxh, dpart;
-  size_t total() const { return plan + xh + gu + dxh + dpart; }
+  Splits s1, s2;
+  size_t plan, frag_gu, unscale_gu, gu, frag_d, unscale_d, dpart;
+  size_t total() const { return plan + frag_gu + unscale_gu + gu + frag_d + unscale_d + dpart; }
 };
 
 MlpLayout mlp_layout(int64_t rows, int hidden, int inter, int64_t experts) {
@@ -97,10 +133,12 @@ MlpLayout mlp_layout(int64_t rows, int hidden, int inter, int64_t experts) {
   l.s1 = gate_up_splits(hidden);
   l.s2 = down_splits(inter);
   l.plan = align_up(plan_bytes(static_cast<int>(rows), static_cast<int>(experts)));
-  l.xh = align_up(2 * rows * hidden * sizeof(float));
-  l.gu = align_up(2 * rows * l.s1 * static_cast<size_t>(inter) * sizeof(float));
-  l.dxh = align_up(rows * static_cast<size_t>(inter) * sizeof(float));
-  l.dpart = align_up(rows * l.s2 * static_cast<size_t>(hidden) * sizeof(float));
+  l.frag_gu = align_up(2 * rows * (hidden / 16) * static_cast<size_t>(64));
+  l.unscale_gu = align_up(2 * rows * l.s1.count * sizeof(float));
+  l.gu = align_up(2 * rows * l.s1.count * static_cast<size_t>(inter) * sizeof(float));
+  l.frag_d = align_up(rows * (inter / 16) * static_cast<size_t>(64));
+  l.unscale_d = align_up(rows * l.s2.count * sizeof(float));
+  l.dpart = align_up(rows * l.s2.count * static_cast<size_t>(hidden) * sizeof(float));
   return l;
 }
 
@@ -141,6 +179,16 @@ int check_experts(const exlr8_trellis_experts* ex, int64_t* matrices) {
   return EXLR8_OK;
 }
 
+StreamParams stream_params(const exlr8_trellis_experts* ex, PlanView plan, int counter, int rows) {
+  StreamParams sp{};
+  sp.plan = plan;
+  sp.counter = counter;
+  sp.k = ex ? ex->k : 4;
+  sp.nslots = rows;
+  sp.unit16 = 65536u;
+  return sp;
+}
+
 // The trellis MLP over all slots of `ids` ([rows] = tokens*slots).  Writes
 // fp32 down partials; the caller finishes them.  skip_slot (>= 0) leaves out
 // slot `skip_slot` of every token.
@@ -148,43 +196,45 @@ int run_mlp(const void* x, int x_dtype, int per_slot, int slots, const uint32_t*
             const exlr8_trellis_experts* ex, int64_t experts, int skip_slot, const MlpLayout& l, Carver& c,
             float** down_partial, PlanView* plan_out, cudaStream_t s) {
   const int h = ex->hidden, m = ex->intermediate;
-  PlanView plan = plan_view(c.take<int32_t>(l.plan), static_cast<int>(rows), static_cast<int>(experts));
-  float* xh = c.take<float>(l.xh);
+  const int n = static_cast<int>(rows), e = static_cast<int>(experts);
+  PlanView plan = plan_view(c.take<int32_t>(l.plan), n, e);
+  uint2* frag_gu = c.take<uint2>(l.frag_gu);
+  float* unscale_gu = c.take<float>(l.unscale_gu);
   float* gu = c.take<float>(l.gu);
-  float* dxh = c.take<float>(l.dxh);
+  uint2* frag_d = c.take<uint2>(l.frag_d);
+  float* unscale_d = c.take<float>(l.unscale_d);
   float* dpart = c.take<float>(l.dpart);
-  EXLR8_TRY(launch_plan(ids, static_cast<int>(rows), static_cast<int>(experts), slots, skip_slot, plan, s));
-  EXLR8_TRY(launch_prep(x, x_dtype, per_slot, slots, ids, static_cast<int>(rows), ex->in_scale[0], ex->in_scale[1],
-                        ex->scale_dtype, h, static_cast<int>(experts), 2, xh, s));
-  GemvParams gp{};
-  gp.xh = xh;
-  gp.packed0 = static_cast<const uint32_t*>(ex->packed[0]);
-  gp.packed1 = static_cast<const uint32_t*>(ex->packed[1]);
+  EXLR8_TIMED(EXLR8_KERNEL_PLAN, s, launch_plan(ids, n, e, slots, skip_slot, plan, s));
+  EXLR8_TIMED(EXLR8_KERNEL_PREP, s, launch_prep_frag(x, x_dtype, per_slot, slots, ids, n, ex->in_scale[0], ex->in_scale[1], ex->scale_dtype,
+                             h, e, 2, l.s1.kt, l.s1.count, frag_gu, unscale_gu, s));
+  StreamParams gp = stream_params(ex, plan, 2, n);
+  gp.packed[0] = static_cast<const uint32_t*>(ex->packed[0]);
+  gp.packed[1] = static_cast<const uint32_t*>(ex->packed[1]);
+  gp.frag = frag_gu;
+  gp.unscale = unscale_gu;
   gp.partial = gu;
-  gp.plan = plan;
-  gp.counter = 2;
-  gp.k = ex->k;
   gp.side = 1;
   gp.in_features = h;
   gp.out_features = m;
-  gp.splits = l.s1;
+  gp.kt_per_split = l.s1.kt;
+  gp.splits = l.s1.count;
   gp.projections = 2;
-  gp.nslots = static_cast<int>(rows);
-  EXLR8_TRY(launch_gemv(gp, s));
-  EXLR8_TRY(launch_gate_finish(gu, l.s1, ids, static_cast<int>(rows), ex->out_scale[0], ex->out_scale[1],
-                               ex->in_scale[2], ex->scale_dtype, m, static_cast<int>(experts), x_dtype, dxh, s));
-  GemvParams dp = gp;
-  dp.xh = dxh;
-  dp.packed0 = static_cast<const uint32_t*>(ex->packed[2]);
-  dp.packed1 = nullptr;
+  EXLR8_TIMED(EXLR8_KERNEL_GATE_UP, s, launch_stream(gp, s));
+  EXLR8_TIMED(EXLR8_KERNEL_GATE_FINISH, s, launch_gate_finish_frag(gu, l.s1.count, ids, n, ex->out_scale[0], ex->out_scale[1], ex->in_scale[2],
+                                    ex->scale_dtype, m, e, x_dtype, l.s2.kt, l.s2.count, frag_d, unscale_d, s));
+  StreamParams dp = stream_params(ex, plan, 3, n);
+  dp.packed[0] = static_cast<const uint32_t*>(ex->packed[2]);
+  dp.packed[1] = nullptr;
+  dp.frag = frag_d;
+  dp.unscale = unscale_d;
   dp.partial = dpart;
-  dp.counter = 3;
   dp.side = 2;
   dp.in_features = m;
   dp.out_features = h;
-  dp.splits = l.s2;
+  dp.kt_per_split = l.s2.kt;
+  dp.splits = l.s2.count;
   dp.projections = 1;
-  EXLR8_TRY(launch_gemv(dp, s));
+  EXLR8_TIMED(EXLR8_KERNEL_DOWN, s, launch_stream(dp, s));
   *down_partial = dpart;
   if (plan_out) *plan_out = plan;
   return EXLR8_OK;
@@ -198,14 +248,14 @@ int run_dense(const void* x, int64_t tokens, const exlr8_dense_expert* sh, int h
   float* down = c.take<float>(l.down);
   void* out = c.take<void>(l.values);
   const int t = static_cast<int>(tokens);
-  EXLR8_TRY(launch_dense_bf16_gemv(static_cast<const uint16_t*>(x), t, static_cast<const uint16_t*>(sh->gate), inter,
+  EXLR8_TIMED(EXLR8_KERNEL_DENSE, s, launch_dense_bf16_gemv(static_cast<const uint16_t*>(x), t, static_cast<const uint16_t*>(sh->gate), inter,
                                    hidden, l.s1, gate, s));
-  EXLR8_TRY(launch_dense_bf16_gemv(static_cast<const uint16_t*>(x), t, static_cast<const uint16_t*>(sh->up), inter,
+  EXLR8_TIMED(EXLR8_KERNEL_DENSE, s, launch_dense_bf16_gemv(static_cast<const uint16_t*>(x), t, static_cast<const uint16_t*>(sh->up), inter,
                                    hidden, l.s1, up, s));
-  EXLR8_TRY(launch_dense_swiglu(gate, up, l.s1, t, inter, act_dtype, h, s));
-  EXLR8_TRY(launch_dense_bf16_gemv(static_cast<const uint16_t*>(h), t, static_cast<const uint16_t*>(sh->down), hidden,
+  EXLR8_TIMED(EXLR8_KERNEL_DENSE, s, launch_dense_swiglu(gate, up, l.s1, t, inter, act_dtype, h, s));
+  EXLR8_TIMED(EXLR8_KERNEL_DENSE, s, launch_dense_bf16_gemv(static_cast<const uint16_t*>(h), t, static_cast<const uint16_t*>(sh->down), hidden,
                                    inter, l.s2, down, s));
-  EXLR8_TRY(launch_dense_cast(down, l.s2, t, hidden, act_dtype, out, s));
+  EXLR8_TIMED(EXLR8_KERNEL_DENSE, s, launch_dense_cast(down, l.s2, t, hidden, act_dtype, out, s));
   *values = out;
   return EXLR8_OK;
 }
@@ -310,10 +360,11 @@ int exlr8_router(const void* x, int x_dtype, int64_t tokens, int hidden, const f
 
 size_t exlr8_expert_linear_workspace(int64_t tokens, int slots, int in_features, int out_features, int64_t experts) {
   const int64_t rows = tokens * slots;
-  const int s = linear_splits(in_features);
+  const Splits sp = linear_splits(in_features);
   return align_up(plan_bytes(static_cast<int>(rows), static_cast<int>(experts))) +
-         align_up(rows * static_cast<size_t>(in_features) * sizeof(float)) +
-         align_up(rows * s * static_cast<size_t>(out_features) * sizeof(float));
+         align_up(rows * (in_features / 16) * static_cast<size_t>(64)) +
+         align_up(rows * sp.count * sizeof(float)) +
+         align_up(rows * sp.count * static_cast<size_t>(out_features) * sizeof(float));
 }
 
 int exlr8_expert_linear(const void* x, int x_dtype, int per_slot, const uint32_t* indices, int64_t tokens, int slots,
@@ -333,32 +384,31 @@ int exlr8_expert_linear(const void* x, int x_dtype, int per_slot, const uint32_t
   if (!workspace || workspace_bytes < exlr8_expert_linear_workspace(tokens, slots, in_features, out_features, experts))
     return EXLR8_ERR_WORKSPACE;
   cudaStream_t s = as_stream(stream);
-  const int splits = linear_splits(in_features);
+  const Splits sp = linear_splits(in_features);
+  const int n = static_cast<int>(rows), e = static_cast<int>(experts);
   Carver c(workspace);
-  PlanView plan = plan_view(c.take<int32_t>(plan_bytes(static_cast<int>(rows), static_cast<int>(experts))),
-                            static_cast<int>(rows), static_cast<int>(experts));
-  float* xh = c.take<float>(rows * static_cast<size_t>(in_features) * sizeof(float));
-  float* part = c.take<float>(rows * splits * static_cast<size_t>(out_features) * sizeof(float));
-  EXLR8_TRY(launch_plan(indices, static_cast<int>(rows), static_cast<int>(experts), slots, -1, plan, s));
-  EXLR8_TRY(launch_prep(x, x_dtype, per_slot, slots, indices, static_cast<int>(rows), in_scale, in_scale, scale_dtype,
-                        in_features, static_cast<int>(experts), 1, xh, s));
-  GemvParams gp{};
-  gp.xh = xh;
-  gp.packed0 = static_cast<const uint32_t*>(packed);
-  gp.packed1 = nullptr;
-  gp.partial = part;
-  gp.plan = plan;
-  gp.counter = 2;
+  PlanView plan = plan_view(c.take<int32_t>(plan_bytes(n, e)), n, e);
+  uint2* frag = c.take<uint2>(rows * (in_features / 16) * static_cast<size_t>(64));
+  float* unscale = c.take<float>(rows * sp.count * sizeof(float));
+  float* part = c.take<float>(rows * sp.count * static_cast<size_t>(out_features) * sizeof(float));
+  EXLR8_TRY(launch_plan(indices, n, e, slots, -1, plan, s));
+  EXLR8_TRY(launch_prep_frag(x, x_dtype, per_slot, slots, indices, n, in_scale, in_scale, scale_dtype, in_features, e,
+                             1, sp.kt, sp.count, frag, unscale, s));
+  StreamParams gp = stream_params(nullptr, plan, 2, n);
   gp.k = k;
+  gp.packed[0] = static_cast<const uint32_t*>(packed);
+  gp.packed[1] = nullptr;
+  gp.frag = frag;
+  gp.unscale = unscale;
+  gp.partial = part;
   gp.side = sharded_side;
   gp.in_features = in_features;
   gp.out_features = out_features;
-  gp.splits = splits;
+  gp.kt_per_split = sp.kt;
+  gp.splits = sp.count;
   gp.projections = 1;
-  gp.nslots = static_cast<int>(rows);
-  EXLR8_TRY(launch_gemv(gp, s));
-  return cuda_status(launch_finish(part, splits, indices, static_cast<int>(rows), out_scale, scale_dtype,
-                                   out_features, static_cast<int>(experts), x_dtype, out, s));
+  EXLR8_TRY(launch_stream(gp, s));
+  return cuda_status(launch_finish(part, sp.count, indices, n, out_scale, scale_dtype, out_features, e, x_dtype, out, s));
 }
 
 size_t exlr8_expert_mlp_workspace(int64_t tokens, int slots, int hidden, int intermediate, int64_t experts) {
@@ -382,7 +432,7 @@ int exlr8_expert_mlp(const void* x, int x_dtype, int per_slot, const uint32_t* i
   Carver c(workspace);
   float* dpart = nullptr;
   EXLR8_CHECK(run_mlp(x, x_dtype, per_slot, slots, indices, rows, ex, experts, -1, l, c, &dpart, nullptr, s));
-  return cuda_status(launch_finish(dpart, l.s2, indices, static_cast<int>(rows), ex->out_scale[2], ex->scale_dtype,
+  return cuda_status(launch_finish(dpart, l.s2.count, indices, static_cast<int>(rows), ex->out_scale[2], ex->scale_dtype,
                                    ex->hidden, static_cast<int>(experts), x_dtype, out, s));
 }
 
@@ -403,7 +453,8 @@ static int mlp_finish_body(const void* x, int x_dtype, const uint32_t* indices, 
     const DenseLayout dl = dense_layout(tokens, ex->hidden, ex->intermediate);
     EXLR8_CHECK(run_dense(x, tokens, shared, ex->hidden, ex->intermediate, x_dtype, dl, c, &shared_values, s));
   }
-  return cuda_status(launch_finish_fused(dpart, l.s2, indices, static_cast<int>(tokens), ex->out_scale[2],
+  ProfileScope scope(EXLR8_KERNEL_FINISH, s);
+  return cuda_status(launch_finish_fused(dpart, l.s2.count, indices, static_cast<int>(tokens), ex->out_scale[2],
                                          ex->scale_dtype, ex->hidden, static_cast<int>(experts), scores, residual,
                                          shared_values, x_dtype, out, s));
 }
@@ -458,9 +509,46 @@ int exlr8_moe_layer(const void* x, int x_dtype, const void* residual, int64_t to
   float* scores_buf = head.take<float>(tokens * 8 * sizeof(float));
   uint32_t* ids = indices ? indices : ids_buf;
   float* sc = scores ? scores : scores_buf;
-  EXLR8_TRY(launch_gate_logits(x, x_dtype, static_cast<int>(tokens), ex->hidden, gate_weight, logits, 256, s));
-  EXLR8_TRY(launch_route(logits, bias, static_cast<int>(tokens), ids, sc, 2.5f, 256u, s));
+  EXLR8_TIMED(EXLR8_KERNEL_ROUTER, s, launch_gate_logits(x, x_dtype, static_cast<int>(tokens), ex->hidden, gate_weight, logits, 256, s));
+  EXLR8_TIMED(EXLR8_KERNEL_ROUTER, s, launch_route(logits, bias, static_cast<int>(tokens), ids, sc, 2.5f, 256u, s));
   return mlp_finish_body(x, x_dtype, ids, sc, residual, tokens, ex, experts, shared, out, c, s);
+}
+
+int exlr8_profile_enable(int enable, int capacity) {
+  Profiler& p = g_prof;
+  if (p.events) {
+    for (int i = 0; i < 2 * p.capacity; ++i) cudaEventDestroy(p.events[i]);
+    delete[] p.events;
+    delete[] p.kinds;
+    p.events = nullptr;
+    p.kinds = nullptr;
+  }
+  p.on = false;
+  p.used = 0;
+  p.capacity = 0;
+  if (!enable) return EXLR8_OK;
+  if (capacity <= 0) return EXLR8_ERR_ARG;
+  p.events = new cudaEvent_t[2 * capacity];
+  p.kinds = new int[capacity];
+  for (int i = 0; i < 2 * capacity; ++i) EXLR8_TRY(cudaEventCreate(&p.events[i]));
+  p.capacity = capacity;
+  p.on = true;
+  return EXLR8_OK;
+}
+
+int exlr8_profile_read(int kind, int64_t* launches, double* total_ms) {
+  if (!launches || !total_ms) return EXLR8_ERR_ARG;
+  *launches = 0;
+  *total_ms = 0.0;
+  for (int i = 0; i < g_prof.used; ++i) {
+    if (g_prof.kinds[i] != kind) continue;
+    EXLR8_TRY(cudaEventSynchronize(g_prof.events[2 * i + 1]));
+    float ms = 0.f;
+    EXLR8_TRY(cudaEventElapsedTime(&ms, g_prof.events[2 * i], g_prof.events[2 * i + 1]));
+    *launches += 1;
+    *total_ms += ms;
+  }
+  return EXLR8_OK;
 }
 
 int exlr8_workspace_bad_ids(const void* workspace, int64_t* bad_ids, void* stream) {

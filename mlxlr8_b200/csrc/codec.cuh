@@ -25,10 +25,10 @@ __device__ __forceinline__ uint32_t lop_mask_xor(uint32_t v) {
 
 // Round an f16x2 to the nearest E4M3 pair and widen it back to f16x2.
 __device__ __forceinline__ uint32_t round_e4m3_f16x2(uint32_t h2) {
-  uint16_t e;
   uint32_t r;
-  asm("cvt.rn.satfinite.e4m3x2.f16x2 %0, %1;" : "=h"(e) : "r"(h2));
-  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(r) : "h"(e));
+  asm("{\n .reg .b16 t;\n cvt.rn.satfinite.e4m3x2.f16x2 t, %1;\n cvt.rn.f16x2.e4m3x2 %0, t;\n}\n"
+      : "=r"(r)
+      : "r"(h2));
   return r;
 }
 

@@ -1,23 +1,21 @@
-// Trellis expert kernels for small batches (decode): dispatch plan, input
-// transform, tensor-core decode GEMV, gate/up finish and output finishes.
+// Trellis expert kernels around the streaming GEMV (trellis_stream.cu):
+// dispatch plan, activation fragments, gate/up finish and output finishes.
 //
 // Reference roles (exlr8 v0.1.21):
-//   plan_kernel        -- fast_prefill.py:19-46 (sort slots by expert, segment table)
-//   prep_kernel        -- metal/fast_decode_prep.metal (x * in_scale, Hadamard-128)
-//   trellis_gemv_kernel-- metal/fast_decode_linear.metal (decode + dot, split-K partials)
-//   gate_finish_kernel -- metal/fast_decode_gate_finish.metal
-//   finish_kernel      -- metal/fast_decode_finish.metal
-//   finish_fused_kernel-- metal/fast_decode_finish_fused.metal
+//   plan_kernel             -- fast_prefill.py:19-46 (sort slots by expert, segments)
+//   prep_frag_kernel        -- metal/fast_decode_prep.metal (x * in_scale, Hadamard-128)
+//   gate_finish_frag_kernel -- metal/fast_decode_gate_finish.metal
+//   finish_kernel           -- metal/fast_decode_finish.metal
+//   finish_fused_kernel     -- metal/fast_decode_finish_fused.metal
 //
-// The GEMV decodes each 16x16 trellis tile straight into mma.sync A-fragment
-// registers (the trellis tensor-core permutation is the m16n8k16 A layout),
-// multiplies it with activations held as float16 hi/lo pairs (hi = f16(x),
-// lo = f16(x - hi), a per-row power-of-two scale keeps them in range) and
-// accumulates in float32 in the tensor cores.  Rows that share an expert
-// share the decoded tile (up to kMaxGroupRows rows, 16 MMA columns).
+// Activations reach the tensor cores as float16 hi/lo pieces (hi = f16(v),
+// lo = f16(v - hi)) of the value times a power-of-two scale chosen per
+// (row, K split), so products keep about 22 significant bits and the
+// float32 accumulation sees the full range.
 
 #include "common.cuh"
 #include "codec.cuh"
+#include "stream.cuh"
 #include "trellis_gemv.cuh"
 
 namespace exlr8 {
@@ -168,332 +166,189 @@ cudaError_t launch_plan(const uint32_t* ids, int rows, int experts, int period, 
 }
 
 // ---------------------------------------------------------------------------
-// Prep: xh[p][slot] = H(x[row] * in_scale_p[expert])  (float32)
+// Activation fragments.  One CTA per (K split, slot, projection): the split's
+// 128-wide blocks are transformed into shared memory, the split maximum picks
+// a power-of-two scale, and the scaled values are written as float16 hi/lo
+// B fragments (see stream.cuh).
 // ---------------------------------------------------------------------------
 
-__global__ void __launch_bounds__(128) prep_kernel(const void* __restrict__ x, int x_dtype, int per_slot,
-                                                   int slots_per_token, const uint32_t* __restrict__ ids, int nslots,
-                                                   const void* __restrict__ in0, const void* __restrict__ in1,
-                                                   int scale_dtype, int features, int experts,
-                                                   float* __restrict__ xh) {
-  const int lane = threadIdx.x & 31;
-  const int block = blockIdx.x * 4 + (threadIdx.x >> 5);
-  const int slot = blockIdx.y;
-  const int proj = blockIdx.z;
-  if (block * 128 >= features) return;
-  const uint32_t e = ids[slot];
-  float* out = xh + (static_cast<int64_t>(proj) * nslots + slot) * features;
-  if (e >= static_cast<uint32_t>(experts)) {  // unplanned row: zeros, never reads a scale
-#pragma unroll
-    for (int j = 0; j < 4; ++j) out[block * 128 + lane + 32 * j] = 0.0f;
-    return;
-  }
-  const int64_t row = per_slot ? slot : slot / slots_per_token;
-  const void* scale = proj ? in1 : in0;
-  float v[4];
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const int col = block * 128 + lane + 32 * j;
-    v[j] = __fmul_rn(load_act(x, x_dtype, row * features + col),
-                     load_scale(scale, scale_dtype, static_cast<int64_t>(e) * features + col));
-  }
-  hadamard128(v, lane);
-#pragma unroll
-  for (int j = 0; j < 4; ++j) out[block * 128 + lane + 32 * j] = v[j];
-}
-
-cudaError_t launch_prep(const void* x, int x_dtype, int per_slot, int slots_per_token, const uint32_t* ids,
-                        int nslots, const void* in0, const void* in1, int scale_dtype, int features,
-                        int experts, int projections, float* xh, cudaStream_t s) {
-  dim3 grid((features / 128 + 3) / 4, nslots, projections);
-  prep_kernel<<<grid, 128, 0, s>>>(x, x_dtype, per_slot, slots_per_token, ids, nslots, in0, in1, scale_dtype,
-                                   features, experts, xh);
-  return cudaGetLastError();
-}
-
-// ---------------------------------------------------------------------------
-// Decode GEMV
-// ---------------------------------------------------------------------------
-
-__device__ __forceinline__ uint32_t ld_stream(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.global.nc.L1::no_allocate.b32 %0, [%1];" : "=r"(v) : "l"(p));
-  return v;
-}
-
-__device__ __forceinline__ void mma_f16(float c[4], const uint32_t a[4], uint2 b) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-      "{%0,%1,%2,%3};\n"
-      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b.x), "r"(b.y));
-}
+constexpr int kFragThreads = 256;
 
 __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
   __half2 h = __floats2half2_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
-// hi or lo piece of a float as float16: hi = f16(v), lo = f16(v - hi).
 __device__ __forceinline__ float split_piece(float v, int piece) {
   const float hi = __half2float(__float2half_rn(v));
   return piece ? v - hi : hi;
 }
 
-template <int K>
-__global__ void __launch_bounds__(kGemvWarps * 32) trellis_gemv_kernel(GemvParams p) {
-  extern __shared__ __align__(16) unsigned char smem[];
-  __shared__ int s_unit;
-  __shared__ int s_rows[kMaxGroupRows];
-  __shared__ unsigned s_maxbits[kMaxGroupRows];
-  __shared__ float s_scale[kMaxGroupRows];
-  __shared__ float s_unscale[kMaxGroupRows];
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int it = p.in_features / 16, ot = p.out_features / 16, nblocks = ot / 8;
-  const int kt_per_split = (it + p.splits - 1) / p.splits;
-  const int words_per_tile = 8 * K;
-  const int groups = p.plan.header[0];
-  const int64_t total = static_cast<int64_t>(groups) * p.projections * nblocks * p.splits;
-  GenericGeometry geo;
-  if (K != 4) geo = generic_geometry(K, lane);
+// Scale exponent for a split maximum: the scaled maximum lies in [2^14, 2^15).
+__device__ __forceinline__ int piece_exponent(float m) {
+  int ex = 0;
+  if (m > 0.0f && m < 3.0e38f) {
+    frexpf(m, &ex);
+    ex -= 15;
+  }
+  return ex;
+}
 
-  for (;;) {
-    if (tid == 0) s_unit = atomicAdd(&p.plan.header[p.counter], 1);
-    __syncthreads();
-    const int64_t unit = s_unit;
-    if (unit >= total) break;
-    const int split = static_cast<int>(unit % p.splits);
-    const int nb = static_cast<int>((unit / p.splits) % nblocks);
-    const int proj = static_cast<int>((unit / (static_cast<int64_t>(p.splits) * nblocks)) % p.projections);
-    const int g = static_cast<int>(unit / (static_cast<int64_t>(p.splits) * nblocks * p.projections));
-    const int expert = p.plan.group_expert[g];
-    const int start = p.plan.group_start[g];
-    const int nr = p.plan.group_count[g];
-    const int ncg = (nr + 3) / 4;
-    const int kt0 = split * kt_per_split;
-    const int kt1 = min(kt0 + kt_per_split, it);
-    const int KT = kt1 - kt0;
-    if (tid < nr) {
-      s_rows[tid] = p.plan.order[start + tid];
-      s_maxbits[tid] = 0u;
-    }
-    __syncthreads();
-    const float* xbase = p.xh + static_cast<int64_t>(proj) * p.nslots * p.in_features;
-    // Per-row power-of-two scale so that hi/lo float16 pieces cover the row.
-    for (int idx = tid; idx < nr * KT * 16; idx += blockDim.x) {
-      const int r = idx / (KT * 16), kk = idx % (KT * 16);
-      const float v = xbase[static_cast<int64_t>(s_rows[r]) * p.in_features + kt0 * 16 + kk];
-      atomicMax(&s_maxbits[r], __float_as_uint(fabsf(v)) & 0x7fffffffu);
-    }
-    __syncthreads();
-    if (tid < nr) {
-      const float m = __uint_as_float(s_maxbits[tid]);
-      int ex = 0;
-      if (m > 0.0f && m < 3.0e38f) {
-        frexpf(m, &ex);
-        ex -= 15;
-      }
-      s_scale[tid] = ldexpf(1.0f, -ex);
-      s_unscale[tid] = ldexpf(1.0f, ex);
-    }
-    __syncthreads();
-    // B fragments [KT][ncg][32] of (hi, lo) float16 pairs.
-    uint2* bfrag = reinterpret_cast<uint2*>(smem);
-    for (int idx = tid; idx < KT * ncg * 32; idx += blockDim.x) {
-      const int l = idx & 31, cg = (idx >> 5) % ncg, ktl = idx / (32 * ncg);
-      const int n = l >> 2, tig = l & 3;
-      const int r = cg * 4 + (n >> 1), piece = n & 1;
-      uint2 b = make_uint2(0u, 0u);
-      if (r < nr) {
-        const float* src = xbase + static_cast<int64_t>(s_rows[r]) * p.in_features + (kt0 + ktl) * 16;
-        const float sc = s_scale[r];
-        const float f0 = split_piece(src[2 * tig] * sc, piece);
-        const float f1 = split_piece(src[2 * tig + 1] * sc, piece);
-        const float f2 = split_piece(src[2 * tig + 8] * sc, piece);
-        const float f3 = split_piece(src[2 * tig + 9] * sc, piece);
-        b.x = pack_half2(f0, f1);
-        b.y = pack_half2(f2, f3);
-      }
-      bfrag[idx] = b;
-    }
-    __syncthreads();
-
-    float acc[8][2][4];
-#pragma unroll
-    for (int t = 0; t < 8; ++t)
-#pragma unroll
-      for (int c = 0; c < 2; ++c)
-#pragma unroll
-        for (int i = 0; i < 4; ++i) acc[t][c][i] = 0.0f;
-
-    const uint32_t* packed = proj ? p.packed1 : p.packed0;
-    if (K == 4) {
-      uint32_t wcur[8], wnext[8];
-      int ktl = warp;
-      if (ktl < KT) {
-        const uint32_t* words = packed + tile_index(expert, kt0 + ktl, nb * 8, it, ot, p.side) * 32;
-#pragma unroll
-        for (int t = 0; t < 8; ++t) wcur[t] = ld_stream(words + t * 32 + lane);
-      }
-      for (; ktl < KT; ktl += kGemvWarps) {
-        const int nxt = ktl + kGemvWarps;
-        if (nxt < KT) {
-          const uint32_t* words = packed + tile_index(expert, kt0 + nxt, nb * 8, it, ot, p.side) * 32;
-#pragma unroll
-          for (int t = 0; t < 8; ++t) wnext[t] = ld_stream(words + t * 32 + lane);
-        }
-        uint2 b0 = bfrag[(ktl * ncg) * 32 + lane];
-        uint2 b1 = ncg > 1 ? bfrag[(ktl * ncg + 1) * 32 + lane] : make_uint2(0u, 0u);
-#pragma unroll
-        for (int t = 0; t < 8; ++t) {
-          const uint32_t prior = __shfl_sync(0xffffffffu, wcur[t], (lane + 31) & 31);
-          uint32_t cw[8], a[4];
-          k4_codewords(wcur[t], prior, cw);
-          tile_fragment(cw, a);
-          mma_f16(acc[t][0], a, b0);
-          if (ncg > 1) mma_f16(acc[t][1], a, b1);
-        }
-#pragma unroll
-        for (int t = 0; t < 8; ++t) wcur[t] = wnext[t];
-      }
-    } else {
-      for (int ktl = warp; ktl < KT; ktl += kGemvWarps) {
-        const uint32_t* words =
-            packed + tile_index(expert, kt0 + ktl, nb * 8, it, ot, p.side) * words_per_tile;
-        uint2 b0 = bfrag[(ktl * ncg) * 32 + lane];
-        uint2 b1 = ncg > 1 ? bfrag[(ktl * ncg + 1) * 32 + lane] : make_uint2(0u, 0u);
-#pragma unroll
-        for (int t = 0; t < 8; ++t) {
-          uint32_t cw[8], a[4];
-          generic_codewords(words + t * words_per_tile, K, geo, cw);
-          tile_fragment(cw, a);
-          mma_f16(acc[t][0], a, b0);
-          if (ncg > 1) mma_f16(acc[t][1], a, b1);
-        }
-      }
-    }
-    __syncthreads();  // B fragments are dead; reuse shared memory for the warp reduction
-    float4* red = reinterpret_cast<float4*>(smem);  // [warp][t][cg][lane]
-#pragma unroll
-    for (int t = 0; t < 8; ++t)
-#pragma unroll
-      for (int c = 0; c < 2; ++c)
-        red[((warp * 8 + t) * 2 + c) * 32 + lane] = make_float4(acc[t][c][0], acc[t][c][1], acc[t][c][2], acc[t][c][3]);
-    __syncthreads();
-    for (int idx = tid; idx < 8 * ncg * 32; idx += blockDim.x) {
-      const int l = idx & 31, c = (idx >> 5) % ncg, t = idx / (32 * ncg);
-      float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-      for (int w = 0; w < kGemvWarps; ++w) {
-        const float4 v = red[((w * 8 + t) * 2 + c) * 32 + l];
-        s.x += v.x;
-        s.y += v.y;
-        s.z += v.z;
-        s.w += v.w;
-      }
-      const int gid = l >> 2, tig = l & 3;
-      const int r = c * 4 + tig;
-      if (r < nr) {
-        float* dst = p.partial +
-                     ((static_cast<int64_t>(proj) * p.nslots + s_rows[r]) * p.splits + split) * p.out_features +
-                     nb * 128 + t * 16 + gid;
-        dst[0] = (s.x + s.y) * s_unscale[r];
-        dst[8] = (s.z + s.w) * s_unscale[r];
-      }
-    }
-    __syncthreads();
+// vals: the split's transformed values (kt_count*16 floats) in shared memory.
+__device__ __forceinline__ void write_fragments(const float* vals, int kt_count, float scale, uint2* dst) {
+  for (int idx = threadIdx.x; idx < kt_count * 8; idx += blockDim.x) {
+    const int ktl = idx >> 3, piece = (idx >> 2) & 1, tig = idx & 3;
+    const float* v = vals + ktl * 16;
+    uint2 b;
+    b.x = pack_half2(split_piece(v[2 * tig] * scale, piece), split_piece(v[2 * tig + 1] * scale, piece));
+    b.y = pack_half2(split_piece(v[2 * tig + 8] * scale, piece), split_piece(v[2 * tig + 9] * scale, piece));
+    dst[idx] = b;
   }
 }
 
-static size_t gemv_smem(int in_features, int splits) {
-  const int it = in_features / 16;
-  const int kt = (it + splits - 1) / splits;
-  const size_t frag = static_cast<size_t>(kt) * 2 * 32 * sizeof(uint2);
-  const size_t red = static_cast<size_t>(kGemvWarps) * 8 * 2 * 32 * sizeof(float4);
-  return frag > red ? frag : red;
+__device__ __forceinline__ float block_max(float m, float* red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+  if (lane == 0) red[warp] = m;
+  __syncthreads();
+  float r = 0.0f;
+  for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) r = fmaxf(r, red[w]);
+  return r;
 }
 
-template <int K>
-static cudaError_t launch_gemv_k(const GemvParams& p, cudaStream_t s) {
-  const size_t smem = gemv_smem(p.in_features, p.splits);
-  cudaError_t err = cudaFuncSetAttribute(trellis_gemv_kernel<K>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(smem));
-  if (err != cudaSuccess) return err;
-  int device = 0, sms = 0, per_sm = 0;
-  cudaGetDevice(&device);
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
-  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, trellis_gemv_kernel<K>, kGemvWarps * 32, smem);
-  if (per_sm < 1) per_sm = 1;
-  trellis_gemv_kernel<K><<<sms * per_sm, kGemvWarps * 32, smem, s>>>(p);
+__global__ void __launch_bounds__(kFragThreads) prep_frag_kernel(
+    const void* __restrict__ x, int x_dtype, int per_slot, int slots_per_token, const uint32_t* __restrict__ ids,
+    int nslots, const void* __restrict__ in0, const void* __restrict__ in1, int scale_dtype, int features,
+    int experts, int kt_split, int splits, uint2* __restrict__ frag, float* __restrict__ unscale) {
+  extern __shared__ float vals[];
+  __shared__ float red[kFragThreads / 32];
+  const int split = blockIdx.x, slot = blockIdx.y, proj = blockIdx.z;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int it = features / 16;
+  const int kt0 = split * kt_split;
+  const int kt_count = min(kt_split, it - kt0);
+  const uint32_t e = ids[slot];
+  const bool ok = e < static_cast<uint32_t>(experts);
+  const int64_t row = per_slot ? slot : slot / slots_per_token;
+  const void* scale = proj ? in1 : in0;
+  float m = 0.0f;
+  for (int b = warp; b < kt_count / 8; b += kFragThreads / 32) {
+    const int c0 = kt0 * 16 + b * 128;
+    float v[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int col = c0 + lane + 32 * j;
+      v[j] = ok ? __fmul_rn(load_act(x, x_dtype, row * features + col),
+                            load_scale(scale, scale_dtype, static_cast<int64_t>(e) * features + col))
+                : 0.0f;
+    }
+    hadamard128(v, lane);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      vals[b * 128 + lane + 32 * j] = v[j];
+      m = fmaxf(m, fabsf(v[j]));
+    }
+  }
+  const float mx = block_max(m, red);  // contains the barrier that publishes vals
+  const int ex = piece_exponent(mx);
+  const int64_t rbase = static_cast<int64_t>(proj) * nslots + slot;
+  write_fragments(vals, kt_count, ldexpf(1.0f, -ex), frag + (rbase * it + kt0) * 8);
+  if (threadIdx.x == 0) unscale[rbase * splits + split] = ldexpf(1.0f, ex);
+}
+
+cudaError_t launch_prep_frag(const void* x, int x_dtype, int per_slot, int slots_per_token, const uint32_t* ids,
+                             int nslots, const void* in0, const void* in1, int scale_dtype, int features, int experts,
+                             int projections, int kt_split, int splits, uint2* frag, float* unscale, cudaStream_t s) {
+  const size_t smem = static_cast<size_t>(kt_split) * 16 * sizeof(float);
+  if (smem > 48 * 1024) {
+    cudaError_t err =
+        cudaFuncSetAttribute(prep_frag_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (err != cudaSuccess) return err;
+  }
+  dim3 grid(splits, nslots, projections);
+  prep_frag_kernel<<<grid, kFragThreads, smem, s>>>(x, x_dtype, per_slot, slots_per_token, ids, nslots, in0, in1,
+                                                     scale_dtype, features, experts, kt_split, splits, frag, unscale);
   return cudaGetLastError();
 }
 
-cudaError_t launch_gemv(const GemvParams& p, cudaStream_t s) {
-  switch (p.k) {
-    case 2: return launch_gemv_k<2>(p, s);
-    case 3: return launch_gemv_k<3>(p, s);
-    default: return launch_gemv_k<4>(p, s);
+// gate/up split sum, Hadamard, output scales, typed SwiGLU, down input scale,
+// Hadamard -> down fragments.  One CTA per (down K split, slot).
+__global__ void __launch_bounds__(kFragThreads) gate_finish_frag_kernel(
+    const float* __restrict__ partial, int gu_splits, const uint32_t* __restrict__ ids, int nslots,
+    const void* __restrict__ out_gate, const void* __restrict__ out_up, const void* __restrict__ in_down,
+    int scale_dtype, int features, int experts, int act_dtype, int kt_split, int splits, uint2* __restrict__ frag,
+    float* __restrict__ unscale) {
+  extern __shared__ float vals[];
+  __shared__ float red[kFragThreads / 32];
+  const int split = blockIdx.x, slot = blockIdx.y;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int it = features / 16;
+  const int kt0 = split * kt_split;
+  const int kt_count = min(kt_split, it - kt0);
+  const int64_t e = ids[slot];
+  const bool ok = e < experts;
+  float m = 0.0f;
+  for (int b = warp; b < kt_count / 8; b += kFragThreads / 32) {
+    const int c0 = kt0 * 16 + b * 128;
+    float gate[4], up[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int col = c0 + lane + 32 * j;
+      float g = 0.f, u = 0.f;
+      if (ok) {
+        for (int s = 0; s < gu_splits; ++s) {
+          g += partial[(static_cast<int64_t>(slot) * gu_splits + s) * features + col];
+          u += partial[((static_cast<int64_t>(nslots) + slot) * gu_splits + s) * features + col];
+        }
+      }
+      gate[j] = g;
+      up[j] = u;
+    }
+    hadamard128(gate, lane);
+    hadamard128(up, lane);
+    float act[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int64_t si = e * features + c0 + lane + 32 * j;
+      act[j] = ok ? __fmul_rn(swiglu_typed(act_dtype, __fmul_rn(gate[j], load_scale(out_gate, scale_dtype, si)),
+                                           __fmul_rn(up[j], load_scale(out_up, scale_dtype, si))),
+                              load_scale(in_down, scale_dtype, si))
+                  : 0.0f;
+    }
+    hadamard128(act, lane);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      vals[b * 128 + lane + 32 * j] = act[j];
+      m = fmaxf(m, fabsf(act[j]));
+    }
   }
+  const float mx = block_max(m, red);
+  const int ex = piece_exponent(mx);
+  write_fragments(vals, kt_count, ldexpf(1.0f, -ex), frag + (static_cast<int64_t>(slot) * it + kt0) * 8);
+  if (threadIdx.x == 0) unscale[static_cast<int64_t>(slot) * splits + split] = ldexpf(1.0f, ex);
+}
+
+cudaError_t launch_gate_finish_frag(const float* partial, int gu_splits, const uint32_t* ids, int nslots,
+                                    const void* out_gate, const void* out_up, const void* in_down, int scale_dtype,
+                                    int features, int experts, int act_dtype, int kt_split, int splits, uint2* frag,
+                                    float* unscale, cudaStream_t s) {
+  const size_t smem = static_cast<size_t>(kt_split) * 16 * sizeof(float);
+  if (smem > 48 * 1024) {
+    cudaError_t err = cudaFuncSetAttribute(gate_finish_frag_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           static_cast<int>(smem));
+    if (err != cudaSuccess) return err;
+  }
+  dim3 grid(splits, nslots);
+  gate_finish_frag_kernel<<<grid, kFragThreads, smem, s>>>(partial, gu_splits, ids, nslots, out_gate, out_up, in_down,
+                                                            scale_dtype, features, experts, act_dtype, kt_split,
+                                                            splits, frag, unscale);
+  return cudaGetLastError();
 }
 
 // ---------------------------------------------------------------------------
 // Finishes
 // ---------------------------------------------------------------------------
-
-// gate/up split sum, Hadamard, output scales, typed SwiGLU, down input scale,
-// Hadamard -> down_xh (float32).  One warp per (slot, 128-block).
-__global__ void __launch_bounds__(128) gate_finish_kernel(const float* __restrict__ partial, int splits,
-                                                          const uint32_t* __restrict__ ids, int nslots,
-                                                          const void* __restrict__ out_gate,
-                                                          const void* __restrict__ out_up,
-                                                          const void* __restrict__ in_down, int scale_dtype,
-                                                          int features, int experts, int act_dtype,
-                                                          float* __restrict__ down_xh) {
-  const int lane = threadIdx.x & 31;
-  const int block = blockIdx.x * 4 + (threadIdx.x >> 5);
-  const int slot = blockIdx.y;
-  if (block * 128 >= features) return;
-  const int64_t e = ids[slot];
-  if (e >= experts) {
-#pragma unroll
-    for (int j = 0; j < 4; ++j) down_xh[static_cast<int64_t>(slot) * features + block * 128 + lane + 32 * j] = 0.0f;
-    return;
-  }
-  float gate[4], up[4];
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const int col = block * 128 + lane + 32 * j;
-    float g = 0.f, u = 0.f;
-    for (int s = 0; s < splits; ++s) {
-      g += partial[(static_cast<int64_t>(slot) * splits + s) * features + col];
-      u += partial[((static_cast<int64_t>(nslots) + slot) * splits + s) * features + col];
-    }
-    gate[j] = g;
-    up[j] = u;
-  }
-  hadamard128(gate, lane);
-  hadamard128(up, lane);
-  float act[4];
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const int64_t si = e * features + block * 128 + lane + 32 * j;
-    const float g = __fmul_rn(gate[j], load_scale(out_gate, scale_dtype, si));
-    const float u = __fmul_rn(up[j], load_scale(out_up, scale_dtype, si));
-    act[j] = __fmul_rn(swiglu_typed(act_dtype, g, u), load_scale(in_down, scale_dtype, si));
-  }
-  hadamard128(act, lane);
-#pragma unroll
-  for (int j = 0; j < 4; ++j) down_xh[static_cast<int64_t>(slot) * features + block * 128 + lane + 32 * j] = act[j];
-}
-
-cudaError_t launch_gate_finish(const float* partial, int splits, const uint32_t* ids, int nslots,
-                               const void* out_gate, const void* out_up, const void* in_down, int scale_dtype,
-                               int features, int experts, int act_dtype, float* down_xh, cudaStream_t s) {
-  dim3 grid((features / 128 + 3) / 4, nslots);
-  gate_finish_kernel<<<grid, 128, 0, s>>>(partial, splits, ids, nslots, out_gate, out_up, in_down, scale_dtype,
-                                          features, experts, act_dtype, down_xh);
-  return cudaGetLastError();
-}
 
 // Split sum, Hadamard, signed output scale, cast to the activation type.
 __global__ void __launch_bounds__(128) finish_kernel(const float* __restrict__ partial, int splits,
@@ -536,12 +391,14 @@ cudaError_t launch_finish(const float* partial, int splits, const uint32_t* ids,
   return cudaGetLastError();
 }
 
-// Nine slots per token (eight routed + shared): expert finish, routed
+// Nine slots per token (eight routed + shared), one warp per slot: expert
+// finish (split sum, Hadamard, out scale, cast), then warp 0 forms the routed
 // weighted sum in the order slot 0, then (slot r + 0) + total for r = 1..7,
-// T(routed), T(routed + T(shared)), T(residual + combined).  When
-// shared_values is given it holds the typed shared-expert output [tokens][h]
-// and slot 8 of partial is not read.
-__global__ void __launch_bounds__(128) finish_fused_kernel(const float* __restrict__ partial, int splits,
+// T(routed), T(routed + T(shared)), T(residual + combined)
+// (metal/fast_decode_finish_fused.metal:52-62).  When shared_values is given
+// it holds the typed shared-expert output [tokens][h] and slot 8 of partial is
+// not read.
+__global__ void __launch_bounds__(288) finish_fused_kernel(const float* __restrict__ partial, int splits,
                                                            const uint32_t* __restrict__ ids, int tokens,
                                                            const void* __restrict__ out_scale, int scale_dtype,
                                                            int features, int experts,
@@ -549,20 +406,16 @@ __global__ void __launch_bounds__(128) finish_fused_kernel(const float* __restri
                                                            const void* __restrict__ residual,
                                                            const void* __restrict__ shared_values, int act_dtype,
                                                            void* __restrict__ out) {
-  const int lane = threadIdx.x & 31;
-  const int block = blockIdx.x * 4 + (threadIdx.x >> 5);
-  const int token = blockIdx.y;
-  if (block * 128 >= features) return;
-  float total[4], shared[4];
-  for (int slot = 0; slot < 9; ++slot) {
-    const int row = token * 9 + slot;
-    if (slot == 8 && shared_values != nullptr) {
+  __shared__ float products[9][128];
+  const int lane = threadIdx.x & 31, slot = threadIdx.x >> 5;
+  const int block = blockIdx.x, token = blockIdx.y;
+  const int row = token * 9 + slot;
+  if (slot == 8 && shared_values != nullptr) {
 #pragma unroll
-      for (int j = 0; j < 4; ++j)
-        shared[j] = load_act(shared_values, act_dtype,
-                             static_cast<int64_t>(token) * features + block * 128 + lane + 32 * j);
-      break;
-    }
+    for (int j = 0; j < 4; ++j)
+      products[8][lane + 32 * j] =
+          load_act(shared_values, act_dtype, static_cast<int64_t>(token) * features + block * 128 + lane + 32 * j);
+  } else {
     const int64_t e = ids[row];
     const bool ok = e < experts;  // an out-of-range id contributes zero
     float v[4];
@@ -580,19 +433,20 @@ __global__ void __launch_bounds__(128) finish_fused_kernel(const float* __restri
       const int col = block * 128 + lane + 32 * j;
       const float value =
           ok ? round_to(act_dtype, __fmul_rn(v[j], load_scale(out_scale, scale_dtype, e * features + col))) : 0.0f;
-      if (slot < 8) {
-        const float prod = __fmul_rn(value, scores[token * 8 + slot]);
-        total[j] = slot == 0 ? __fadd_rn(prod, 0.0f) : __fadd_rn(__fadd_rn(prod, 0.0f), total[j]);
-      } else {
-        shared[j] = value;
-      }
+      products[slot][lane + 32 * j] = slot < 8 ? __fmul_rn(value, scores[token * 8 + slot]) : value;
     }
   }
+  __syncthreads();
+  if (slot != 0) return;
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
-    const int64_t off = static_cast<int64_t>(token) * features + block * 128 + lane + 32 * j;
-    const float routed = round_to(act_dtype, total[j]);
-    const float combined = round_to(act_dtype, __fadd_rn(routed, round_to(act_dtype, shared[j])));
+    const int c = lane + 32 * j;
+    float total = __fadd_rn(products[0][c], 0.0f);
+#pragma unroll
+    for (int r = 1; r < 8; ++r) total = __fadd_rn(__fadd_rn(products[r][c], 0.0f), total);
+    const int64_t off = static_cast<int64_t>(token) * features + block * 128 + c;
+    const float routed = round_to(act_dtype, total);
+    const float combined = round_to(act_dtype, __fadd_rn(routed, round_to(act_dtype, products[8][c])));
     store_act(out, act_dtype, off, __fadd_rn(load_act(residual, act_dtype, off), combined));
   }
 }
@@ -601,8 +455,8 @@ cudaError_t launch_finish_fused(const float* partial, int splits, const uint32_t
                                 const void* out_scale, int scale_dtype, int features, int experts,
                                 const float* scores, const void* residual, const void* shared_values, int act_dtype,
                                 void* out, cudaStream_t s) {
-  dim3 grid((features / 128 + 3) / 4, tokens);
-  finish_fused_kernel<<<grid, 128, 0, s>>>(partial, splits, ids, tokens, out_scale, scale_dtype, features, experts,
+  dim3 grid(features / 128, tokens);
+  finish_fused_kernel<<<grid, 288, 0, s>>>(partial, splits, ids, tokens, out_scale, scale_dtype, features, experts,
                                            scores, residual, shared_values, act_dtype, out);
   return cudaGetLastError();
 }

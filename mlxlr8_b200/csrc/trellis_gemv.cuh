@@ -7,7 +7,6 @@
 namespace exlr8 {
 
 constexpr int kMaxGroupRows = 8;  // rows (expert slots) sharing one decoded tile
-constexpr int kGemvWarps = 4;
 
 // Device-side dispatch plan: slots sorted by expert and cut into groups of at
 // most kMaxGroupRows rows of one expert.  Written by plan_kernel.
@@ -21,29 +20,12 @@ struct PlanView {
   int32_t* expert_start;  // [experts] first position in order
 };
 
-struct GemvParams {
-  const float* xh;           // [projections][nslots][in_features] transformed inputs
-  const uint32_t* packed0;   // trellis words of projection 0
-  const uint32_t* packed1;   // projection 1 (gate/up) or null
-  float* partial;            // [projections][nslots][splits][out_features]
-  PlanView plan;
-  int counter;               // index of the work counter in plan.header
-  int k, side, in_features, out_features, splits, projections, nslots;
-};
-
 size_t plan_bytes(int rows, int experts);
 PlanView plan_view(void* base, int rows, int experts);
 
 // Rows i with i % period == skip_slot are left out (skip_slot < 0: none).
 cudaError_t launch_plan(const uint32_t* ids, int rows, int experts, int period, int skip_slot, PlanView plan,
                         cudaStream_t s);
-cudaError_t launch_prep(const void* x, int x_dtype, int per_slot, int slots_per_token, const uint32_t* ids,
-                        int nslots, const void* in0, const void* in1, int scale_dtype, int features, int experts,
-                        int projections, float* xh, cudaStream_t s);
-cudaError_t launch_gemv(const GemvParams& p, cudaStream_t s);
-cudaError_t launch_gate_finish(const float* partial, int splits, const uint32_t* ids, int nslots,
-                               const void* out_gate, const void* out_up, const void* in_down, int scale_dtype,
-                               int features, int experts, int act_dtype, float* down_xh, cudaStream_t s);
 cudaError_t launch_finish(const float* partial, int splits, const uint32_t* ids, int nslots, const void* out_scale,
                           int scale_dtype, int features, int experts, int act_dtype, void* out, cudaStream_t s);
 cudaError_t launch_finish_fused(const float* partial, int splits, const uint32_t* ids, int tokens,

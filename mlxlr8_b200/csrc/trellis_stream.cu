@@ -1,0 +1,312 @@
+// Streaming trellis GEMV for selected experts (decode / small batches).
+//
+// Replaces metal/fast_decode_linear.metal (exlr8 v0.1.21).  One persistent
+// CTA per SM slot; warp 4 is the producer, warps 0-3 consume.
+//
+//   producer: takes work units (row group of one expert, projection, 128-wide
+//     output block, K split) from a global counter and streams each unit's
+//     packed tiles -- one contiguous run of 8 output tiles per K tile -- plus
+//     the unit rows' activation fragments into a ring of shared-memory stages
+//     with 1-D bulk copies (cp.async.bulk, no multicast) completing on
+//     mbarriers.  Units follow each other through the ring without draining.
+//   consumers: each of the eight warps owns one of the eight 16x16 output
+//     tiles and takes the stage's 8 K tiles at once (eight independent decode
+//     chains per warp).  A lane reads word l and word l-1 of a tile; every 32-bit window
+//     of that 64-bit stream carries two codewords, whose hashes come from three
+//     integer multiplies (V*C, (V>>16)*C and V*C - ((V>>16)*C << 16)), so the
+//     codeword masks disappear.  The half sums are rounded to E4M3 and placed
+//     directly in mma.sync m16n8k16 A fragments (the trellis tensor-core
+//     permutation is that layout); B holds float16 hi/lo pieces of up to four
+//     rows (eight columns) per fragment group; float32 accumulation.
+//   output: per unit, float32 partial sums [proj][slot][split][out].
+
+#include "codec.cuh"
+#include "common.cuh"
+#include "stream.cuh"
+#include "tma.cuh"
+
+namespace exlr8 {
+
+constexpr int kConsumers = 8;
+constexpr int kStreamThreads = (kConsumers + 1) * 32;
+constexpr int kStages = 4;
+constexpr int kStageTiles = 8;                       // K tiles per stage
+constexpr int kFragRowBytes = kStageTiles * 64 + 64;  // padded: rows hit different banks
+
+enum : int { kFirst = 1, kLast = 2, kEnd = 4 };
+
+template <int K>
+struct StageGeometry {
+  static constexpr int kTileWords = 8 * K;
+  static constexpr int kCodeBytes = kStageTiles * 8 * kTileWords * 4;
+  static constexpr int kFragBytes = kMaxGroupRows * kFragRowBytes;
+  static constexpr int kStageBytes = kCodeBytes + kFragBytes;
+};
+
+__device__ __forceinline__ void mma_f16(float c[4], const uint32_t a[4], uint2 b) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};\n"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b.x), "r"(b.y));
+}
+
+// f16x2 value pair of two hashed products (low half = a).
+__device__ __forceinline__ uint32_t pair_from_products(uint32_t pa, uint32_t pb) {
+  uint32_t lo = lop_mask_xor(__byte_perm(pa, pb, 0x5410));
+  uint32_t hi = lop_mask_xor(__byte_perm(pa, pb, 0x7632));
+  __half2 s = __hadd2(*reinterpret_cast<__half2*>(&lo), *reinterpret_cast<__half2*>(&hi));
+  return round_e4m3_f16x2(*reinterpret_cast<uint32_t*>(&s));
+}
+
+// A fragment of one K4 tile from tile word l and word l-1.  `unit16` is the
+// runtime value 65536: it keeps the high-half extraction an IMAD.HI on the
+// multiply pipe instead of a shift on the integer pipe.
+__device__ __forceinline__ void k4_fragment(uint32_t word, uint32_t prior, uint32_t unit16, uint32_t a[4]) {
+  const uint32_t v0 = word;                              // (cw3 : cw7)
+  const uint32_t v4 = __funnelshift_r(word, prior, 4);   // (cw2 : cw6)
+  const uint32_t v8 = __funnelshift_r(word, prior, 8);   // (cw1 : cw5)
+  const uint32_t v12 = __funnelshift_r(word, prior, 12); // (cw0 : cw4)
+  const uint32_t h0 = __umulhi(v0, unit16), h4 = __umulhi(v4, unit16);
+  const uint32_t h8 = __umulhi(v8, unit16), h12 = __umulhi(v12, unit16);
+  const uint32_t ph0 = h0 * kMcgMul, ph4 = h4 * kMcgMul, ph8 = h8 * kMcgMul, ph12 = h12 * kMcgMul;
+  // v*C - ph*2^16 (mod 2^32), one multiply-add each.
+  const uint32_t pl0 = v0 * kMcgMul + ph0 * 0xFFFF0000u, pl4 = v4 * kMcgMul + ph4 * 0xFFFF0000u;
+  const uint32_t pl8 = v8 * kMcgMul + ph8 * 0xFFFF0000u, pl12 = v12 * kMcgMul + ph12 * 0xFFFF0000u;
+  a[0] = pair_from_products(ph12, ph8);  // j0, j1
+  a[1] = pair_from_products(pl12, pl8);  // j4, j5
+  a[2] = pair_from_products(ph4, ph0);   // j2, j3
+  a[3] = pair_from_products(pl4, pl0);   // j6, j7
+}
+
+struct UnitInfo {
+  int group, proj, nb, split;
+};
+
+__device__ __forceinline__ UnitInfo decode_unit(int64_t unit, const StreamParams& p, int nblocks) {
+  UnitInfo u;
+  u.split = static_cast<int>(unit % p.splits);
+  u.nb = static_cast<int>((unit / p.splits) % nblocks);
+  u.proj = static_cast<int>((unit / (static_cast<int64_t>(p.splits) * nblocks)) % p.projections);
+  u.group = static_cast<int>(unit / (static_cast<int64_t>(p.splits) * nblocks * p.projections));
+  return u;
+}
+
+template <int K>
+__global__ void __launch_bounds__(kStreamThreads, 2) trellis_stream_kernel(StreamParams p) {
+  using G = StageGeometry<K>;
+  extern __shared__ __align__(128) unsigned char smem[];
+  __shared__ __align__(8) uint64_t full_bar[kStages];
+  __shared__ __align__(8) uint64_t empty_bar[kStages];
+  __shared__ int4 meta[kStages];  // unit, first K tile, K tiles, flags
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int it = p.in_features / 16, ot = p.out_features / 16, nblocks = ot / 8;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], kConsumers);
+    }
+    mbar_fence_init();
+  }
+  __syncthreads();
+
+  if (warp == kConsumers) {
+    // ---------------- producer ----------------
+    if (lane != 0) return;
+    const int groups = p.plan.header[0];
+    const int64_t total = static_cast<int64_t>(groups) * p.projections * nblocks * p.splits;
+    int stage = 0;
+    uint32_t phase = 0;
+    bool failed = false;
+    for (;;) {
+      const int64_t unit = atomicAdd(&p.plan.header[p.counter], 1);
+      if (!mbar_wait(&empty_bar[stage], phase ^ 1u)) {
+        failed = true;
+        break;
+      }
+      if (unit >= total) {
+        meta[stage] = make_int4(0, 0, 0, kEnd);
+        mbar_arrive(&full_bar[stage]);
+        break;
+      }
+      const UnitInfo u = decode_unit(unit, p, nblocks);
+      const int expert = p.plan.group_expert[u.group];
+      const int start = p.plan.group_start[u.group];
+      const int nr = p.plan.group_count[u.group];
+      const int kt0 = u.split * p.kt_per_split;
+      const int kt1 = min(kt0 + p.kt_per_split, it);
+      const uint32_t* words = p.packed[u.proj];
+      for (int kt = kt0; kt < kt1; kt += kStageTiles) {
+        if (kt != kt0) {
+          if (!mbar_wait(&empty_bar[stage], phase ^ 1u)) {
+            failed = true;
+            break;
+          }
+        }
+        const int n = min(kStageTiles, kt1 - kt);
+        meta[stage] = make_int4(static_cast<int>(unit), kt, n,
+                                (kt == kt0 ? kFirst : 0) | (kt + kStageTiles >= kt1 ? kLast : 0));
+        unsigned char* base = smem + stage * G::kStageBytes;
+        const uint32_t code_bytes = static_cast<uint32_t>(n) * 8u * G::kTileWords * 4u;
+        mbar_arrive_expect_tx(&full_bar[stage], code_bytes + static_cast<uint32_t>(nr) * n * 64u);
+        const uint32_t* src = words + tile_index(expert, kt, u.nb * 8, it, ot, p.side) * G::kTileWords;
+        bulk_copy_g2s(base, src, code_bytes, &full_bar[stage]);
+        for (int r = 0; r < nr; ++r) {
+          const int slot = p.plan.order[start + r];
+          const uint2* fsrc = p.frag + ((static_cast<int64_t>(u.proj) * p.nslots + slot) * it + kt) * 8;
+          bulk_copy_g2s(base + G::kCodeBytes + r * kFragRowBytes, fsrc, static_cast<uint32_t>(n) * 64u,
+                        &full_bar[stage]);
+        }
+        if (++stage == kStages) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      if (failed) break;
+    }
+    if (failed) {
+      atomicOr(&p.plan.header[9], 1);
+      // Copies already issued target valid addresses and land within
+      // microseconds; give them that time before this thread retires.
+      for (int i = 0; i < 1000; ++i) __nanosleep(1000);
+    }
+    return;
+  }
+
+  // ---------------- consumers ----------------
+  const int gid = lane >> 2, tig = lane & 3;
+  const uint32_t unit16 = p.unit16;
+  int stage = 0;
+  uint32_t phase = 0;
+  float acc[2][4];
+#pragma unroll
+  for (int c = 0; c < 2; ++c)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) acc[c][i] = 0.0f;
+  UnitInfo u{};
+  int nr = 0, ncg = 1, slot_a = -1, slot_b = -1;
+  float unscale_a = 1.0f, unscale_b = 1.0f;
+  GenericGeometry geo;
+  if (K != 4) geo = generic_geometry(K, lane);
+  const int r0 = gid >> 1, fpos = (gid & 1) * 4 + tig;
+
+  for (;;) {
+    if (!mbar_wait(&full_bar[stage], phase)) {
+      if (lane == 0) atomicOr(&p.plan.header[9], 2);
+      break;
+    }
+    const int4 m = meta[stage];
+    if (m.w & kEnd) break;
+    if (m.w & kFirst) {
+      u = decode_unit(m.x, p, nblocks);
+      const int start = p.plan.group_start[u.group];
+      nr = p.plan.group_count[u.group];
+      ncg = (nr + 3) >> 2;
+      slot_a = tig < nr ? p.plan.order[start + tig] : -1;
+      slot_b = 4 + tig < nr ? p.plan.order[start + 4 + tig] : -1;
+      const int64_t ubase = static_cast<int64_t>(u.proj) * p.nslots;
+      unscale_a = slot_a >= 0 ? p.unscale[(ubase + slot_a) * p.splits + u.split] : 1.0f;
+      unscale_b = slot_b >= 0 ? p.unscale[(ubase + slot_b) * p.splits + u.split] : 1.0f;
+    }
+    const unsigned char* base = smem + stage * G::kStageBytes;
+    const uint32_t* codes = reinterpret_cast<const uint32_t*>(base);
+    const uint2* frag = reinterpret_cast<const uint2*>(base + G::kCodeBytes);
+    // Every stage holds kStageTiles K tiles (splits are whole 128-wide blocks).
+    uint2 b0[kStageTiles], b1[kStageTiles];
+    const bool has0 = r0 < nr, has1 = 4 + r0 < nr;
+#pragma unroll
+    for (int kk = 0; kk < kStageTiles; ++kk) {
+      b0[kk] = has0 ? frag[(r0 * kFragRowBytes) / 8 + kk * 8 + fpos] : make_uint2(0u, 0u);
+      b1[kk] = has1 ? frag[((4 + r0) * kFragRowBytes) / 8 + kk * 8 + fpos] : make_uint2(0u, 0u);
+    }
+    if (K == 4) {
+      uint32_t word[kStageTiles], prior[kStageTiles];
+#pragma unroll
+      for (int kk = 0; kk < kStageTiles; ++kk) {
+        const uint32_t* tile = codes + (kk * 8 + warp) * 32;
+        word[kk] = tile[lane];
+        prior[kk] = tile[(lane + 31) & 31];
+      }
+      if (ncg > 1) {
+#pragma unroll
+        for (int kk = 0; kk < kStageTiles; ++kk) {
+          uint32_t a[4];
+          k4_fragment(word[kk], prior[kk], unit16, a);
+          mma_f16(acc[0], a, b0[kk]);
+          mma_f16(acc[1], a, b1[kk]);
+        }
+      } else {
+#pragma unroll
+        for (int kk = 0; kk < kStageTiles; ++kk) {
+          uint32_t a[4];
+          k4_fragment(word[kk], prior[kk], unit16, a);
+          mma_f16(acc[0], a, b0[kk]);
+        }
+      }
+    } else {
+#pragma unroll
+      for (int kk = 0; kk < kStageTiles; ++kk) {
+        uint32_t cw[8], a[4];
+        generic_codewords(codes + (kk * 8 + warp) * G::kTileWords, K, geo, cw);
+        tile_fragment(cw, a);
+        mma_f16(acc[0], a, b0[kk]);
+        if (ncg > 1) mma_f16(acc[1], a, b1[kk]);
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty_bar[stage]);
+    if (m.w & kLast) {
+      const int64_t ubase = static_cast<int64_t>(u.proj) * p.nslots;
+      const int col = u.nb * 128 + warp * 16 + gid;
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        const int slot = c == 0 ? slot_a : slot_b;
+        const float us = c == 0 ? unscale_a : unscale_b;
+        if (slot >= 0) {
+          float* dst = p.partial + ((ubase + slot) * p.splits + u.split) * p.out_features + col;
+          dst[0] = (acc[c][0] + acc[c][1]) * us;
+          dst[8] = (acc[c][2] + acc[c][3]) * us;
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) acc[c][i] = 0.0f;
+      }
+    }
+    if (++stage == kStages) {
+      stage = 0;
+      phase ^= 1u;
+    }
+  }
+}
+
+template <int K>
+static cudaError_t launch_stream_k(const StreamParams& p, cudaStream_t s) {
+  // Attribute and occupancy are queried once per process (the launch shape is
+  // fixed: one persistent CTA per resident slot).
+  static int grid = 0;
+  const int smem = kStages * StageGeometry<K>::kStageBytes;
+  if (grid == 0) {
+    cudaError_t err =
+        cudaFuncSetAttribute(trellis_stream_kernel<K>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (err != cudaSuccess) return err;
+    int device = 0, sms = 0, per_sm = 0;
+    if ((err = cudaGetDevice(&device)) != cudaSuccess) return err;
+    if ((err = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device)) != cudaSuccess) return err;
+    if ((err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, trellis_stream_kernel<K>, kStreamThreads,
+                                                             smem)) != cudaSuccess)
+      return err;
+    grid = sms * (per_sm < 1 ? 1 : per_sm);
+  }
+  trellis_stream_kernel<K><<<grid, kStreamThreads, smem, s>>>(p);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_stream(const StreamParams& p, cudaStream_t s) {
+  switch (p.k) {
+    case 2: return launch_stream_k<2>(p, s);
+    case 3: return launch_stream_k<3>(p, s);
+    default: return launch_stream_k<4>(p, s);
+  }
+}
+
+}  // namespace exlr8
