@@ -52,7 +52,8 @@ enum exlr8_status {
   EXLR8_ERR_ARG = 11,       /* null pointer or out-of-range argument */
   EXLR8_ERR_CUDA = 12,      /* a CUDA runtime call failed (see exlr8_last_cuda_error) */
   EXLR8_ERR_ID_RANGE = 13,  /* "Expert IDs must be in 0..256"                       experts.py:158-159 */
-  EXLR8_ERR_UNSUPPORTED = 14
+  EXLR8_ERR_UNSUPPORTED = 14,
+  EXLR8_ERR_STATIC_LIMIT = 15 /* needs more scratch than EXLR8_NOALLOC_SCRATCH_BYTES */
 };
 
 /* Library ABI version (EXLR8_ABI_VERSION). */
@@ -198,6 +199,28 @@ enum exlr8_kernel_kind {
  * events and returns the launch count and total milliseconds of one kind. */
 int exlr8_profile_enable(int enable, int capacity);
 int exlr8_profile_read(int kind, int64_t* launches, double* total_ms);
+
+/* ---- no-allocation variant ------------------------------------------------ */
+
+/* Size of the fixed device scratch used by exlr8_moe_layer_noalloc. */
+#define EXLR8_NOALLOC_SCRATCH_BYTES (16u * 1024u * 1024u)
+
+/* exlr8_moe_layer without a caller workspace.  No counterpart in the
+ * reference (exlr8 runs on MLX, which owns all of its memory); it serves
+ * hosts that hold device pointers but cannot allocate device memory, such as
+ * an FFI caller whose tensors come from another runtime or a server whose
+ * memory pool is fixed at start-up.  Scratch is one static device array of
+ * EXLR8_NOALLOC_SCRATCH_BYTES inside the library (held on every GPU that
+ * loads it until exit); nothing is allocated.  Requests whose
+ * exlr8_moe_layer_workspace() exceeds that size return
+ * EXLR8_ERR_STATIC_LIMIT (at GLM-5 size: up to 6 tokens).  The first call on
+ * a device looks up the array's device address; make it before any stream
+ * capture.  All calls share the array: calls that overlap on the GPU race
+ * and must be serialised by the caller. */
+int exlr8_moe_layer_noalloc(const void* x, int x_dtype, const void* residual, int64_t tokens,
+                            const float* gate_weight, const float* bias, const exlr8_trellis_experts* experts,
+                            const exlr8_dense_expert* shared, void* out, uint32_t* indices, float* scores,
+                            void* stream);
 
 /* Device-side id check of the last call that used `workspace`: writes the
  * number of expert ids that were out of range (those slots produce zeros).

@@ -20,7 +20,7 @@ DTYPE_CODES = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2}
 SCALE_CODES = {torch.float32: 0, torch.float16: 1}
 
 # Status codes whose reference behaviour is a ValueError.
-VALUE_ERRORS = {1, 2, 3, 4, 5, 6, 7, 8, 13}
+VALUE_ERRORS = {1, 2, 3, 4, 5, 6, 7, 8, 13, 15}
 
 
 class TrellisExperts(ctypes.Structure):
@@ -71,6 +71,9 @@ _SIGNATURES = {
     "exlr8_workspace_bad_ids": (c_int, [c_void_p, POINTER(c_int64), c_void_p]),
     "exlr8_profile_enable": (c_int, [c_int, c_int]),
     "exlr8_profile_read": (c_int, [c_int, POINTER(c_int64), POINTER(ctypes.c_double)]),
+    "exlr8_moe_layer_noalloc": (c_int, [c_void_p, c_int, c_void_p, c_int64, c_void_p, c_void_p,
+                                        POINTER(TrellisExperts), POINTER(DenseExpert), c_void_p, c_void_p, c_void_p,
+                                        c_void_p]),
 }
 
 EXPORTED = tuple(_SIGNATURES)

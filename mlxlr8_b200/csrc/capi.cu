@@ -292,6 +292,8 @@ const char* exlr8_status_string(int status) {
     case EXLR8_ERR_CUDA: return "CUDA runtime error";
     case EXLR8_ERR_ID_RANGE: return "Expert IDs must be in 0..256";
     case EXLR8_ERR_UNSUPPORTED: return "unsupported configuration";
+    case EXLR8_ERR_STATIC_LIMIT:
+      return "request needs more scratch than the fixed no-allocation buffer (EXLR8_NOALLOC_SCRATCH_BYTES)";
     default: return "unknown status";
   }
 }
