@@ -124,15 +124,21 @@ int format_status(int64_t packed_bytes, int k, int in_f, int out_f, int side, in
 // Workspace of the trellis MLP over `rows` slots.
 struct MlpLayout {
   Splits s1, s2;
-  size_t plan, frag_gu, unscale_gu, gu, frag_d, unscale_d, dpart;
-  size_t total() const { return plan + frag_gu + unscale_gu + gu + frag_d + unscale_d + dpart; }
+  size_t plan, counters, frag_gu, unscale_gu, gu, frag_d, unscale_d, dpart;
+  size_t total() const { return plan + counters + frag_gu + unscale_gu + gu + frag_d + unscale_d + dpart; }
 };
+
+// bf16 shared expert: K splits of the gate/up and down passes (enough warps
+// in flight to stream the weights at full bandwidth for a few tokens).
+constexpr int kDenseGateUpSplits = 32;
+constexpr int kDenseDownSplits = 8;
 
 MlpLayout mlp_layout(int64_t rows, int hidden, int inter, int64_t experts) {
   MlpLayout l;
   l.s1 = gate_up_splits(hidden);
   l.s2 = down_splits(inter);
   l.plan = align_up(plan_bytes(static_cast<int>(rows), static_cast<int>(experts)));
+  l.counters = align_up((static_cast<size_t>(inter) / 64 + 1) * sizeof(int32_t));
   l.frag_gu = align_up(2 * rows * (hidden / 16) * static_cast<size_t>(64));
   l.unscale_gu = align_up(2 * rows * l.s1.count * sizeof(float));
   l.gu = align_up(2 * rows * l.s1.count * static_cast<size_t>(inter) * sizeof(float));
@@ -143,20 +149,16 @@ MlpLayout mlp_layout(int64_t rows, int hidden, int inter, int64_t experts) {
 }
 
 struct DenseLayout {
-  int s1, s2;
-  size_t gate, up, h, down, values;
-  size_t total() const { return gate + up + h + down + values; }
+  size_t gate, up, h, down;
+  size_t total() const { return gate + up + h + down; }
 };
 
 DenseLayout dense_layout(int64_t tokens, int hidden, int inter) {
   DenseLayout l;
-  l.s1 = dense_splits(hidden);
-  l.s2 = dense_splits(inter);
-  l.gate = align_up(l.s1 * tokens * static_cast<size_t>(inter) * sizeof(float));
+  l.gate = align_up(kDenseGateUpSplits * tokens * static_cast<size_t>(inter) * sizeof(float));
   l.up = l.gate;
   l.h = align_up(tokens * static_cast<size_t>(inter) * sizeof(float));
-  l.down = align_up(l.s2 * tokens * static_cast<size_t>(hidden) * sizeof(float));
-  l.values = align_up(tokens * static_cast<size_t>(hidden) * sizeof(float));
+  l.down = align_up(kDenseDownSplits * tokens * static_cast<size_t>(hidden) * sizeof(float));
   return l;
 }
 
@@ -186,48 +188,97 @@ StreamParams stream_params(const exlr8_trellis_experts* ex, PlanView plan, int c
   sp.k = ex ? ex->k : 4;
   sp.nslots = rows;
   sp.unit16 = 65536u;
+  sp.mcg_mask = 0x8FFF8FFFu;
+  sp.mcg_xor = 0x3B603B60u;
   return sp;
 }
 
-// The trellis MLP over all slots of `ids` ([rows] = tokens*slots).  Writes
-// fp32 down partials; the caller finishes them.  skip_slot (>= 0) leaves out
-// slot `skip_slot` of every token.
-int run_mlp(const void* x, int x_dtype, int per_slot, int slots, const uint32_t* ids, int64_t rows,
-            const exlr8_trellis_experts* ex, int64_t experts, int skip_slot, const MlpLayout& l, Carver& c,
-            float** down_partial, PlanView* plan_out, cudaStream_t s) {
+// Buffers of one MLP call carved from the workspace.
+struct MlpBuffers {
+  PlanView plan;
+  int32_t* counters;
+  uint2* frag_gu;
+  float* unscale_gu;
+  float* gu;
+  uint2* frag_d;
+  float* unscale_d;
+  float* dpart;
+  // dense shared expert (null when absent)
+  float* dgate;
+  float* dup;
+  void* dh;
+  float* ddown;
+};
+
+MlpBuffers carve_mlp(const MlpLayout& l, int64_t rows, int64_t experts, bool dense, int64_t tokens, int hidden,
+                     int inter, Carver& c) {
+  MlpBuffers b{};
+  const int n = static_cast<int>(rows), e = static_cast<int>(experts);
+  b.plan = plan_view(c.take<int32_t>(l.plan), n, e);
+  b.counters = c.take<int32_t>(l.counters);
+  b.frag_gu = c.take<uint2>(l.frag_gu);
+  b.unscale_gu = c.take<float>(l.unscale_gu);
+  b.gu = c.take<float>(l.gu);
+  b.frag_d = c.take<uint2>(l.frag_d);
+  b.unscale_d = c.take<float>(l.unscale_d);
+  b.dpart = c.take<float>(l.dpart);
+  b.plan.zero = b.counters;
+  b.plan.zero_count = inter / 64;
+  if (dense) {
+    const DenseLayout dl = dense_layout(tokens, hidden, inter);
+    b.dgate = c.take<float>(dl.gate);
+    b.dup = c.take<float>(dl.up);
+    b.dh = c.take<void>(dl.h);
+    b.ddown = c.take<float>(dl.down);
+  }
+  return b;
+}
+
+// The trellis MLP over all slots of `ids` ([rows] = tokens*slots) after the
+// plan: activation fragments, the gate/up stream (with the gate/up finish as
+// its epilogue), the down stream.  With `shared` the bf16 shared expert runs
+// as dense units of the same two kernels.  Leaves fp32 down partials.
+int run_mlp_after_plan(const void* x, int x_dtype, int per_slot, int slots, const uint32_t* ids, int64_t rows,
+                       const exlr8_trellis_experts* ex, int64_t experts, const exlr8_dense_expert* shared,
+                       int64_t tokens, const MlpLayout& l, const MlpBuffers& b, cudaStream_t s) {
   const int h = ex->hidden, m = ex->intermediate;
   const int n = static_cast<int>(rows), e = static_cast<int>(experts);
-  PlanView plan = plan_view(c.take<int32_t>(l.plan), n, e);
-  uint2* frag_gu = c.take<uint2>(l.frag_gu);
-  float* unscale_gu = c.take<float>(l.unscale_gu);
-  float* gu = c.take<float>(l.gu);
-  uint2* frag_d = c.take<uint2>(l.frag_d);
-  float* unscale_d = c.take<float>(l.unscale_d);
-  float* dpart = c.take<float>(l.dpart);
-  EXLR8_TIMED(EXLR8_KERNEL_PLAN, s, launch_plan(ids, n, e, slots, skip_slot, plan, s));
-  EXLR8_TIMED(EXLR8_KERNEL_PREP, s, launch_prep_frag(x, x_dtype, per_slot, slots, ids, n, ex->in_scale[0], ex->in_scale[1], ex->scale_dtype,
-                             h, e, 2, l.s1.kt, l.s1.count, frag_gu, unscale_gu, s));
-  StreamParams gp = stream_params(ex, plan, 2, n);
+  EXLR8_TIMED(EXLR8_KERNEL_PREP, s,
+              launch_prep_frag(x, x_dtype, per_slot, slots, ids, n, ex->in_scale[0], ex->in_scale[1],
+                               ex->scale_dtype, h, e, 2, l.s1.kt, l.s1.count, b.frag_gu, b.unscale_gu, s));
+  StreamParams gp = stream_params(ex, b.plan, 2, n);
   gp.packed[0] = static_cast<const uint32_t*>(ex->packed[0]);
   gp.packed[1] = static_cast<const uint32_t*>(ex->packed[1]);
-  gp.frag = frag_gu;
-  gp.unscale = unscale_gu;
-  gp.partial = gu;
+  gp.frag = b.frag_gu;
+  gp.unscale = b.unscale_gu;
+  gp.partial = b.gu;
   gp.side = 1;
   gp.in_features = h;
   gp.out_features = m;
   gp.kt_per_split = l.s1.kt;
   gp.splits = l.s1.count;
   gp.projections = 2;
+  if (shared) {
+    EXLR8_TIMED(EXLR8_KERNEL_DENSE, s,
+                launch_dense_gate_up(static_cast<const uint16_t*>(x), static_cast<int>(tokens),
+                                     static_cast<const uint16_t*>(shared->gate),
+                                     static_cast<const uint16_t*>(shared->up), m, h, kDenseGateUpSplits, b.dgate,
+                                     b.dup, b.counters, x_dtype, b.dh, s));
+    EXLR8_TIMED(EXLR8_KERNEL_DENSE, s,
+                launch_dense_gemv(static_cast<const uint16_t*>(b.dh), static_cast<int>(tokens),
+                                  static_cast<const uint16_t*>(shared->down), h, m, kDenseDownSplits, b.ddown, s));
+  }
   EXLR8_TIMED(EXLR8_KERNEL_GATE_UP, s, launch_stream(gp, s));
-  EXLR8_TIMED(EXLR8_KERNEL_GATE_FINISH, s, launch_gate_finish_frag(gu, l.s1.count, ids, n, ex->out_scale[0], ex->out_scale[1], ex->in_scale[2],
-                                    ex->scale_dtype, m, e, x_dtype, l.s2.kt, l.s2.count, frag_d, unscale_d, s));
-  StreamParams dp = stream_params(ex, plan, 3, n);
+  EXLR8_TIMED(EXLR8_KERNEL_GATE_FINISH, s,
+              launch_gate_finish_frag(b.gu, l.s1.count, ids, n, ex->out_scale[0], ex->out_scale[1], ex->in_scale[2],
+                                      ex->scale_dtype, m, e, x_dtype, l.s2.kt, l.s2.count, b.frag_d, b.unscale_d,
+                                      s));
+  StreamParams dp = stream_params(ex, b.plan, 3, n);
   dp.packed[0] = static_cast<const uint32_t*>(ex->packed[2]);
   dp.packed[1] = nullptr;
-  dp.frag = frag_d;
-  dp.unscale = unscale_d;
-  dp.partial = dpart;
+  dp.frag = b.frag_d;
+  dp.unscale = b.unscale_d;
+  dp.partial = b.dpart;
   dp.side = 2;
   dp.in_features = m;
   dp.out_features = h;
@@ -235,28 +286,6 @@ int run_mlp(const void* x, int x_dtype, int per_slot, int slots, const uint32_t*
   dp.splits = l.s2.count;
   dp.projections = 1;
   EXLR8_TIMED(EXLR8_KERNEL_DOWN, s, launch_stream(dp, s));
-  *down_partial = dpart;
-  if (plan_out) *plan_out = plan;
-  return EXLR8_OK;
-}
-
-int run_dense(const void* x, int64_t tokens, const exlr8_dense_expert* sh, int hidden, int inter, int act_dtype,
-              const DenseLayout& l, Carver& c, void** values, cudaStream_t s) {
-  float* gate = c.take<float>(l.gate);
-  float* up = c.take<float>(l.up);
-  void* h = c.take<void>(l.h);
-  float* down = c.take<float>(l.down);
-  void* out = c.take<void>(l.values);
-  const int t = static_cast<int>(tokens);
-  EXLR8_TIMED(EXLR8_KERNEL_DENSE, s, launch_dense_bf16_gemv(static_cast<const uint16_t*>(x), t, static_cast<const uint16_t*>(sh->gate), inter,
-                                   hidden, l.s1, gate, s));
-  EXLR8_TIMED(EXLR8_KERNEL_DENSE, s, launch_dense_bf16_gemv(static_cast<const uint16_t*>(x), t, static_cast<const uint16_t*>(sh->up), inter,
-                                   hidden, l.s1, up, s));
-  EXLR8_TIMED(EXLR8_KERNEL_DENSE, s, launch_dense_swiglu(gate, up, l.s1, t, inter, act_dtype, h, s));
-  EXLR8_TIMED(EXLR8_KERNEL_DENSE, s, launch_dense_bf16_gemv(static_cast<const uint16_t*>(h), t, static_cast<const uint16_t*>(sh->down), hidden,
-                                   inter, l.s2, down, s));
-  EXLR8_TIMED(EXLR8_KERNEL_DENSE, s, launch_dense_cast(down, l.s2, t, hidden, act_dtype, out, s));
-  *values = out;
   return EXLR8_OK;
 }
 
@@ -265,7 +294,7 @@ int check_dense(const exlr8_dense_expert* sh, int x_dtype, int hidden, int inter
   if (!sh->gate || !sh->up || !sh->down) return EXLR8_ERR_ARG;
   if (x_dtype != EXLR8_DTYPE_BF16) return EXLR8_ERR_DTYPE;  // bf16 operands for the bf16 matrices
   if (!aligned16(sh->gate) || !aligned16(sh->up) || !aligned16(sh->down)) return EXLR8_ERR_ALIGN;
-  if (hidden % 32 || inter % 32) return EXLR8_ERR_DIMS;
+  if (hidden % 128 || inter % 128) return EXLR8_ERR_DIMS;
   return EXLR8_OK;
 }
 
@@ -353,7 +382,7 @@ int exlr8_router(const void* x, int x_dtype, int64_t tokens, int hidden, const f
   if (tokens < 0 || hidden <= 0 || hidden % 4) return EXLR8_ERR_ARG;
   if (tokens == 0) return EXLR8_OK;
   if (!x || !gate_weight || !bias || !logits || !indices || !scores) return EXLR8_ERR_ARG;
-  if (!aligned16(gate_weight)) return EXLR8_ERR_ALIGN;
+  if (!aligned16(gate_weight) || !aligned16(x)) return EXLR8_ERR_ALIGN;
   EXLR8_TRY(launch_gate_logits(x, x_dtype, static_cast<int>(tokens), hidden, gate_weight, logits, 256,
                                as_stream(stream)));
   return cuda_status(launch_route(logits, bias, static_cast<int>(tokens), indices, scores, 2.5f, 256u,
@@ -432,10 +461,13 @@ int exlr8_expert_mlp(const void* x, int x_dtype, int per_slot, const uint32_t* i
   if (!workspace || workspace_bytes < l.total()) return EXLR8_ERR_WORKSPACE;
   cudaStream_t s = as_stream(stream);
   Carver c(workspace);
-  float* dpart = nullptr;
-  EXLR8_CHECK(run_mlp(x, x_dtype, per_slot, slots, indices, rows, ex, experts, -1, l, c, &dpart, nullptr, s));
-  return cuda_status(launch_finish(dpart, l.s2.count, indices, static_cast<int>(rows), ex->out_scale[2], ex->scale_dtype,
-                                   ex->hidden, static_cast<int>(experts), x_dtype, out, s));
+  const MlpBuffers b = carve_mlp(l, rows, experts, false, tokens, ex->hidden, ex->intermediate, c);
+  EXLR8_TIMED(EXLR8_KERNEL_PLAN, s,
+              launch_plan(indices, static_cast<int>(rows), static_cast<int>(experts), slots, -1, b.plan, s));
+  EXLR8_CHECK(run_mlp_after_plan(x, x_dtype, per_slot, slots, indices, rows, ex, experts, nullptr, tokens, l, b, s));
+  ProfileScope scope(EXLR8_KERNEL_FINISH, s);
+  return cuda_status(launch_finish(b.dpart, l.s2.count, indices, static_cast<int>(rows), ex->out_scale[2],
+                                   ex->scale_dtype, ex->hidden, static_cast<int>(experts), x_dtype, out, s));
 }
 
 size_t exlr8_expert_mlp_finish_workspace(int64_t tokens, int hidden, int intermediate, int64_t experts) {
@@ -443,22 +475,17 @@ size_t exlr8_expert_mlp_finish_workspace(int64_t tokens, int hidden, int interme
          dense_layout(tokens, hidden, intermediate).total();
 }
 
-static int mlp_finish_body(const void* x, int x_dtype, const uint32_t* indices, const float* scores,
-                           const void* residual, int64_t tokens, const exlr8_trellis_experts* ex, int64_t experts,
-                           const exlr8_dense_expert* shared, void* out, Carver& c, cudaStream_t s) {
+// Nine-slot MLP + combine after the plan exists in `b`.
+static int mlp_finish_after_plan(const void* x, int x_dtype, const uint32_t* indices, const float* scores,
+                                 const void* residual, int64_t tokens, const exlr8_trellis_experts* ex,
+                                 int64_t experts, const exlr8_dense_expert* shared, void* out, const MlpLayout& l,
+                                 const MlpBuffers& b, cudaStream_t s) {
   const int64_t rows = tokens * 9;
-  const MlpLayout l = mlp_layout(rows, ex->hidden, ex->intermediate, experts);
-  float* dpart = nullptr;
-  EXLR8_CHECK(run_mlp(x, x_dtype, 0, 9, indices, rows, ex, experts, shared ? 8 : -1, l, c, &dpart, nullptr, s));
-  void* shared_values = nullptr;
-  if (shared) {
-    const DenseLayout dl = dense_layout(tokens, ex->hidden, ex->intermediate);
-    EXLR8_CHECK(run_dense(x, tokens, shared, ex->hidden, ex->intermediate, x_dtype, dl, c, &shared_values, s));
-  }
+  EXLR8_CHECK(run_mlp_after_plan(x, x_dtype, 0, 9, indices, rows, ex, experts, shared, tokens, l, b, s));
   ProfileScope scope(EXLR8_KERNEL_FINISH, s);
-  return cuda_status(launch_finish_fused(dpart, l.s2.count, indices, static_cast<int>(tokens), ex->out_scale[2],
+  return cuda_status(launch_finish_fused(b.dpart, l.s2.count, indices, static_cast<int>(tokens), ex->out_scale[2],
                                          ex->scale_dtype, ex->hidden, static_cast<int>(experts), scores, residual,
-                                         shared_values, x_dtype, out, s));
+                                         shared ? b.ddown : nullptr, kDenseDownSplits, x_dtype, out, s));
 }
 
 int exlr8_expert_mlp_finish(const void* x, int x_dtype, const uint32_t* indices, const float* scores,
@@ -475,15 +502,20 @@ int exlr8_expert_mlp_finish(const void* x, int x_dtype, const uint32_t* indices,
   if (tokens * 9 > (1 << 20)) return EXLR8_ERR_UNSUPPORTED;
   if (!workspace || workspace_bytes < exlr8_expert_mlp_finish_workspace(tokens, ex->hidden, ex->intermediate, experts))
     return EXLR8_ERR_WORKSPACE;
+  cudaStream_t s = as_stream(stream);
+  const int64_t rows = tokens * 9;
+  const MlpLayout l = mlp_layout(rows, ex->hidden, ex->intermediate, experts);
   Carver c(workspace);
-  return mlp_finish_body(x, x_dtype, indices, scores, residual, tokens, ex, experts, shared, out, c,
-                         as_stream(stream));
+  const MlpBuffers b = carve_mlp(l, rows, experts, shared != nullptr, tokens, ex->hidden, ex->intermediate, c);
+  EXLR8_TIMED(EXLR8_KERNEL_PLAN, s,
+              launch_plan(indices, static_cast<int>(rows), static_cast<int>(experts), 9, shared ? 8 : -1, b.plan, s));
+  return mlp_finish_after_plan(x, x_dtype, indices, scores, residual, tokens, ex, experts, shared, out, l, b, s);
 }
 
 size_t exlr8_moe_layer_workspace(int64_t tokens, int hidden, int intermediate, int64_t experts) {
   return exlr8_expert_mlp_finish_workspace(tokens, hidden, intermediate, experts) +
          align_up(tokens * 256 * sizeof(float)) + align_up(tokens * 9 * sizeof(uint32_t)) +
-         align_up(tokens * 8 * sizeof(float));
+         align_up(tokens * 8 * sizeof(float)) + align_up(sizeof(int));
 }
 
 int exlr8_moe_layer(const void* x, int x_dtype, const void* residual, int64_t tokens, const float* gate_weight,
@@ -497,23 +529,29 @@ int exlr8_moe_layer(const void* x, int x_dtype, const void* residual, int64_t to
   if (tokens < 0) return EXLR8_ERR_ROWS;
   if (tokens == 0) return EXLR8_OK;
   if (!x || !residual || !gate_weight || !bias || !out) return EXLR8_ERR_ARG;
-  if (!aligned16(gate_weight)) return EXLR8_ERR_ALIGN;
+  if (!aligned16(gate_weight) || !aligned16(x)) return EXLR8_ERR_ALIGN;
+  if (ex->hidden % 4) return EXLR8_ERR_DIMS;
   if (tokens * 9 > (1 << 20)) return EXLR8_ERR_UNSUPPORTED;
   if (!workspace || workspace_bytes < exlr8_moe_layer_workspace(tokens, ex->hidden, ex->intermediate, experts))
     return EXLR8_ERR_WORKSPACE;
   cudaStream_t s = as_stream(stream);
-  Carver c(workspace);
+  const int64_t rows = tokens * 9;
+  const MlpLayout l = mlp_layout(rows, ex->hidden, ex->intermediate, experts);
   // The MLP part comes first so that the id-check header sits at offset 0.
+  Carver c(workspace);
+  const MlpBuffers b = carve_mlp(l, rows, experts, shared != nullptr, tokens, ex->hidden, ex->intermediate, c);
   Carver head(workspace);
   head.used = exlr8_expert_mlp_finish_workspace(tokens, ex->hidden, ex->intermediate, experts);
   float* logits = head.take<float>(tokens * 256 * sizeof(float));
   uint32_t* ids_buf = head.take<uint32_t>(tokens * 9 * sizeof(uint32_t));
   float* scores_buf = head.take<float>(tokens * 8 * sizeof(float));
+  int* done = head.take<int>(sizeof(int));
   uint32_t* ids = indices ? indices : ids_buf;
   float* sc = scores ? scores : scores_buf;
-  EXLR8_TIMED(EXLR8_KERNEL_ROUTER, s, launch_gate_logits(x, x_dtype, static_cast<int>(tokens), ex->hidden, gate_weight, logits, 256, s));
-  EXLR8_TIMED(EXLR8_KERNEL_ROUTER, s, launch_route(logits, bias, static_cast<int>(tokens), ids, sc, 2.5f, 256u, s));
-  return mlp_finish_body(x, x_dtype, ids, sc, residual, tokens, ex, experts, shared, out, c, s);
+  EXLR8_TIMED(EXLR8_KERNEL_ROUTER, s,
+              launch_router_plan(x, x_dtype, static_cast<int>(tokens), ex->hidden, gate_weight, logits, bias, ids, sc,
+                                 done, static_cast<int>(experts), shared ? 8 : -1, b.plan, s));
+  return mlp_finish_after_plan(x, x_dtype, ids, sc, residual, tokens, ex, experts, shared, out, l, b, s);
 }
 
 int exlr8_profile_enable(int enable, int capacity) {

@@ -1,10 +1,10 @@
-// Dense helpers: codebook probe, whole-matrix trellis decode and dequantize
-// (exlr8 trellis.py:199-214, metal/decode.metal), and the bf16 shared expert
-// GEMV used when the shared expert is stored as bf16 matrices.
+// Codebook probe and whole-matrix trellis decode / dequantize
+// (exlr8 trellis.py:199-214, metal/decode.metal).
 
 #include "common.cuh"
 #include "codec.cuh"
 #include "dense.cuh"
+#include "dense_warp.cuh"
 
 namespace exlr8 {
 
@@ -109,129 +109,77 @@ cudaError_t launch_dequantize(const float* inner, const void* suh, const void* s
 }
 
 // ---------------------------------------------------------------------------
-// bf16 dense GEMV on mma.sync (bf16 x bf16 products are exact in float32).
-// Lane (gid, tig) loads 16 bytes of two weight rows (gid, gid+8) and 16 bytes
-// of token gid at k = 8*tig..8*tig+7 of each 32-wide step; the step is two
-// m16n8k16 MMAs whose k order is permuted identically in A and B.
+// bf16 shared expert (the BASELINE layout of the shared expert).
 // ---------------------------------------------------------------------------
 
-__device__ __forceinline__ uint4 ldg128_stream(const void* p) {
-  uint4 v;
-  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
-               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "l"(p));
-  return v;
-}
-
-__device__ __forceinline__ void mma_bf16(float c[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
-                                         uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-      "{%0,%1,%2,%3};\n"
-      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
-
 constexpr int kDenseWarps = 4;
-constexpr int kDenseUnroll = 4;
 
-__global__ void __launch_bounds__(kDenseWarps * 32) dense_bf16_gemv_kernel(const uint16_t* __restrict__ x, int tokens,
-                                                                           const uint16_t* __restrict__ w, int n,
-                                                                           int k, int splits,
-                                                                           float* __restrict__ partial) {
+// Gate and up products in one pass over x, split along k; the CTA that
+// completes the last split of a 64-row block writes h = SwiGLU(T(g), T(u))
+// for it.  `counters` ([n/64]) must be zero at launch.
+__global__ void __launch_bounds__(kDenseWarps * 32) dense_gate_up_kernel(
+    const uint16_t* __restrict__ x, int tokens, const uint16_t* __restrict__ wg, const uint16_t* __restrict__ wu,
+    int n, int k, int splits, float* __restrict__ gp, float* __restrict__ up, int* __restrict__ counters,
+    int act_dtype, void* __restrict__ h) {
+  __shared__ int s_last;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int gid = lane >> 2, tig = lane & 3;
+  const int n0 = (blockIdx.x * kDenseWarps + warp) * 16;
+  const int split = blockIdx.y;
+  const int steps = k / 32;
+  const int per = (steps + splits - 1) / splits;
+  const int s0 = split * per, s1 = min(s0 + per, steps);
+  const int64_t total = static_cast<int64_t>(tokens) * n;
+  if (n0 < n) dense_rows(x, tokens, wg, wu, n, k, n0, s0, s1, gp + split * total, up + split * total, lane);
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    s_last = atomicAdd(&counters[blockIdx.x], 1) == splits - 1;
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  const int rows = min(kDenseWarps * 16, n - static_cast<int>(blockIdx.x) * kDenseWarps * 16);
+  for (int idx = threadIdx.x; idx < tokens * rows; idx += blockDim.x) {
+    const int t = idx / rows;
+    const int64_t i = static_cast<int64_t>(t) * n + blockIdx.x * kDenseWarps * 16 + idx % rows;
+    float g = 0.f, u = 0.f;
+#pragma unroll 8
+    for (int sp = 0; sp < splits; ++sp) {
+      g += __ldcg(gp + sp * total + i);
+      u += __ldcg(up + sp * total + i);
+    }
+    store_act(h, act_dtype, i, swiglu_typed(act_dtype, g, u));
+  }
+}
+
+cudaError_t launch_dense_gate_up(const uint16_t* x, int tokens, const uint16_t* wg, const uint16_t* wu, int n, int k,
+                                 int splits, float* gate_partial, float* up_partial, int* counters, int act_dtype,
+                                 void* h, cudaStream_t s) {
+  dim3 grid((n / 16 + kDenseWarps - 1) / kDenseWarps, splits);
+  dense_gate_up_kernel<<<grid, kDenseWarps * 32, 0, s>>>(x, tokens, wg, wu, n, k, splits, gate_partial, up_partial,
+                                                          counters, act_dtype, h);
+  return cudaGetLastError();
+}
+
+// y partials [splits][tokens][n] of x @ W^T, W bf16 [n][k].
+__global__ void __launch_bounds__(kDenseWarps * 32) dense_gemv_kernel(const uint16_t* __restrict__ x, int tokens,
+                                                                      const uint16_t* __restrict__ w, int n, int k,
+                                                                      int splits, float* __restrict__ partial) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int n0 = (blockIdx.x * kDenseWarps + warp) * 16;
   if (n0 >= n) return;
   const int split = blockIdx.y;
   const int steps = k / 32;
   const int per = (steps + splits - 1) / splits;
   const int s0 = split * per, s1 = min(s0 + per, steps);
-  const uint16_t* w0 = w + static_cast<int64_t>(n0 + gid) * k + 8 * tig;
-  const uint16_t* w1 = w0 + static_cast<int64_t>(8) * k;
-  for (int t0 = 0; t0 < tokens; t0 += 8) {
-    const bool has_token = t0 + gid < tokens;
-    const uint16_t* xr = x + static_cast<int64_t>(has_token ? t0 + gid : 0) * k + 8 * tig;
-    float acc[4] = {0.f, 0.f, 0.f, 0.f};
-    int st = s0;
-    for (; st + kDenseUnroll <= s1; st += kDenseUnroll) {
-      uint4 a[kDenseUnroll], b[kDenseUnroll], xv[kDenseUnroll];
-#pragma unroll
-      for (int u = 0; u < kDenseUnroll; ++u) {
-        a[u] = ldg128_stream(w0 + (st + u) * 32);
-        b[u] = ldg128_stream(w1 + (st + u) * 32);
-        xv[u] = has_token ? *reinterpret_cast<const uint4*>(xr + (st + u) * 32) : make_uint4(0, 0, 0, 0);
-      }
-#pragma unroll
-      for (int u = 0; u < kDenseUnroll; ++u) {
-        mma_bf16(acc, a[u].x, b[u].x, a[u].y, b[u].y, xv[u].x, xv[u].y);
-        mma_bf16(acc, a[u].z, b[u].z, a[u].w, b[u].w, xv[u].z, xv[u].w);
-      }
-    }
-    for (; st < s1; ++st) {
-      const uint4 a = ldg128_stream(w0 + st * 32);
-      const uint4 b = ldg128_stream(w1 + st * 32);
-      const uint4 xv = has_token ? *reinterpret_cast<const uint4*>(xr + st * 32) : make_uint4(0, 0, 0, 0);
-      mma_bf16(acc, a.x, b.x, a.y, b.y, xv.x, xv.y);
-      mma_bf16(acc, a.z, b.z, a.w, b.w, xv.z, xv.w);
-    }
-    // c0,c1: row gid, tokens 2tig, 2tig+1; c2,c3: row gid+8.
-    const int ta = t0 + 2 * tig, tb = ta + 1;
-    float* out = partial + static_cast<int64_t>(split) * tokens * n;
-    if (ta < tokens) {
-      out[static_cast<int64_t>(ta) * n + n0 + gid] = acc[0];
-      out[static_cast<int64_t>(ta) * n + n0 + gid + 8] = acc[2];
-    }
-    if (tb < tokens) {
-      out[static_cast<int64_t>(tb) * n + n0 + gid] = acc[1];
-      out[static_cast<int64_t>(tb) * n + n0 + gid + 8] = acc[3];
-    }
-  }
+  dense_rows(x, tokens, w, nullptr, n, k, n0, s0, s1, partial + split * static_cast<int64_t>(tokens) * n, nullptr,
+             lane);
 }
 
-cudaError_t launch_dense_bf16_gemv(const uint16_t* x, int tokens, const uint16_t* w, int n, int k, int splits,
-                                   float* partial, cudaStream_t s) {
+cudaError_t launch_dense_gemv(const uint16_t* x, int tokens, const uint16_t* w, int n, int k, int splits,
+                              float* partial, cudaStream_t s) {
   dim3 grid((n / 16 + kDenseWarps - 1) / kDenseWarps, splits);
-  dense_bf16_gemv_kernel<<<grid, kDenseWarps * 32, 0, s>>>(x, tokens, w, n, k, splits, partial);
-  return cudaGetLastError();
-}
-
-__global__ void dense_swiglu_kernel(const float* __restrict__ gp, const float* __restrict__ up, int splits, int tokens,
-                                    int n, int act_dtype, void* __restrict__ h) {
-  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  const int64_t total = static_cast<int64_t>(tokens) * n;
-  if (i >= total) return;
-  float g = 0.f, u = 0.f;
-  for (int s = 0; s < splits; ++s) {
-    g += gp[s * total + i];
-    u += up[s * total + i];
-  }
-  store_act(h, act_dtype, i, swiglu_typed(act_dtype, g, u));
-}
-
-cudaError_t launch_dense_swiglu(const float* gate_partial, const float* up_partial, int splits, int tokens, int n,
-                                int act_dtype, void* h, cudaStream_t s) {
-  const int64_t total = static_cast<int64_t>(tokens) * n;
-  dense_swiglu_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, s>>>(gate_partial, up_partial, splits,
-                                                                                 tokens, n, act_dtype, h);
-  return cudaGetLastError();
-}
-
-__global__ void dense_cast_kernel(const float* __restrict__ partial, int splits, int tokens, int n, int act_dtype,
-                                  void* __restrict__ out) {
-  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  const int64_t total = static_cast<int64_t>(tokens) * n;
-  if (i >= total) return;
-  float a = 0.f;
-  for (int s = 0; s < splits; ++s) a += partial[s * total + i];
-  store_act(out, act_dtype, i, a);
-}
-
-cudaError_t launch_dense_cast(const float* partial, int splits, int tokens, int n, int act_dtype, void* out,
-                              cudaStream_t s) {
-  const int64_t total = static_cast<int64_t>(tokens) * n;
-  dense_cast_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, s>>>(partial, splits, tokens, n, act_dtype,
-                                                                               out);
+  dense_gemv_kernel<<<grid, kDenseWarps * 32, 0, s>>>(x, tokens, w, n, k, splits, partial);
   return cudaGetLastError();
 }
 

@@ -1,5 +1,4 @@
-// Dense helpers: codebook probe, whole-matrix trellis decode/dequantize and
-// the bf16 shared expert.
+// Codebook probe and whole-matrix trellis decode/dequantize.
 #pragma once
 
 #include <cuda_runtime.h>
@@ -13,15 +12,13 @@ cudaError_t launch_decode_matrix(const uint32_t* words, int64_t expert, int k, i
 cudaError_t launch_dequantize(const float* inner, const void* suh, const void* svh, int scale_dtype,
                               int in_features, int out_features, float* weight, cudaStream_t s);
 
-// bf16 shared expert: y[t][n] = sum_k x[t][k] * W[n][k] (float32 accumulate)
-// written as float32 split-K partials [splits][tokens][n].
-cudaError_t launch_dense_bf16_gemv(const uint16_t* x, int tokens, const uint16_t* w, int n, int k, int splits,
-                                   float* partial, cudaStream_t s);
-// Typed SwiGLU of the summed gate/up partials -> bf16 h [tokens][n].
-cudaError_t launch_dense_swiglu(const float* gate_partial, const float* up_partial, int splits, int tokens, int n,
-                                int act_dtype, void* h, cudaStream_t s);
-// Sum split partials and cast -> typed values [tokens][n].
-cudaError_t launch_dense_cast(const float* partial, int splits, int tokens, int n, int act_dtype, void* out,
-                              cudaStream_t s);
+// bf16 shared expert.  Gate and up in one pass, the last CTA of each 64-row
+// block writing h = SwiGLU(T(g), T(u)) in the activation type; `counters`
+// ([n/64] ints) must be zero at launch.  Partials are [splits][tokens][n].
+cudaError_t launch_dense_gate_up(const uint16_t* x, int tokens, const uint16_t* wg, const uint16_t* wu, int n, int k,
+                                 int splits, float* gate_partial, float* up_partial, int* counters, int act_dtype,
+                                 void* h, cudaStream_t s);
+cudaError_t launch_dense_gemv(const uint16_t* x, int tokens, const uint16_t* w, int n, int k, int splits,
+                              float* partial, cudaStream_t s);
 
 }  // namespace exlr8

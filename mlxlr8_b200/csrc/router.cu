@@ -4,11 +4,27 @@
 
 #include "common.cuh"
 #include "router.cuh"
+#include "plan.cuh"
+#include "trellis_gemv.cuh"
 
 namespace exlr8 {
 
 constexpr int kGateWarps = 8;
 constexpr int kGateTokens = 8;
+constexpr int kGateChunk = 6;  // float4 weight loads in flight per lane (hidden 6144: all of them)
+
+// Four consecutive activations (index a multiple of 4) as floats.
+__device__ __forceinline__ float4 load_act4(const void* base, int dtype, int64_t i) {
+  if (dtype == kF32) return *reinterpret_cast<const float4*>(static_cast<const float*>(base) + i);
+  const uint2 v = *reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(base) + i);
+  if (dtype == kF16) {
+    const __half2 a = *reinterpret_cast<const __half2*>(&v.x), b = *reinterpret_cast<const __half2*>(&v.y);
+    return make_float4(__low2float(a), __high2float(a), __low2float(b), __high2float(b));
+  }
+  const __nv_bfloat162 a = *reinterpret_cast<const __nv_bfloat162*>(&v.x);
+  const __nv_bfloat162 b = *reinterpret_cast<const __nv_bfloat162*>(&v.y);
+  return make_float4(__low2float(a), __high2float(a), __low2float(b), __high2float(b));
+}
 
 // One CTA per expert row of Wg; the 8 warps split the hidden dimension; each
 // warp keeps partial dot products for up to kGateTokens tokens at a time.
@@ -27,16 +43,25 @@ __global__ void __launch_bounds__(kGateWarps * 32) gate_logits_kernel(const void
     float acc[kGateTokens];
 #pragma unroll
     for (int t = 0; t < kGateTokens; ++t) acc[t] = 0.f;
-    for (int g = g0 + lane; g < g1; g += 32) {
-      const float4 wv = reinterpret_cast<const float4*>(w)[g];
+    // All of a lane's weight loads of a chunk are issued before any use.
+    for (int gc = g0 + lane; gc < g1; gc += 32 * kGateChunk) {
+      float4 wv[kGateChunk];
+#pragma unroll
+      for (int i = 0; i < kGateChunk; ++i)
+        wv[i] = gc + 32 * i < g1 ? reinterpret_cast<const float4*>(w)[gc + 32 * i] : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
       for (int t = 0; t < kGateTokens; ++t) {
         if (t0 + t < tokens) {
-          const int64_t base = static_cast<int64_t>(t0 + t) * hidden + 4 * g;
-          acc[t] = fmaf(load_act(x, x_dtype, base), wv.x, acc[t]);
-          acc[t] = fmaf(load_act(x, x_dtype, base + 1), wv.y, acc[t]);
-          acc[t] = fmaf(load_act(x, x_dtype, base + 2), wv.z, acc[t]);
-          acc[t] = fmaf(load_act(x, x_dtype, base + 3), wv.w, acc[t]);
+#pragma unroll
+          for (int i = 0; i < kGateChunk; ++i) {
+            if (gc + 32 * i < g1) {
+              const float4 xv = load_act4(x, x_dtype, static_cast<int64_t>(t0 + t) * hidden + 4 * (gc + 32 * i));
+              acc[t] = fmaf(xv.x, wv[i].x, acc[t]);
+              acc[t] = fmaf(xv.y, wv[i].y, acc[t]);
+              acc[t] = fmaf(xv.z, wv[i].z, acc[t]);
+              acc[t] = fmaf(xv.w, wv[i].w, acc[t]);
+            }
+          }
         }
       }
     }
@@ -66,22 +91,18 @@ cudaError_t launch_gate_logits(const void* x, int x_dtype, int tokens, int hidde
   return cudaGetLastError();
 }
 
-// One warp per row of 256 logits.  Lane l owns experts i*32 + l.  Each of
-// the eight rounds takes the largest remaining sigmoid(l)+bias (lowest expert
-// id on a tie), records its sigmoid, and removes it.  Weights are divided by
-// 1e-20 + their sum (accumulated in rank order) and multiplied by `scale`;
-// slot 8 holds the shared expert id.
-__global__ void __launch_bounds__(128) route_kernel(const float* __restrict__ logits, const float* __restrict__ bias,
-                                                    int rows, uint32_t* __restrict__ ids,
-                                                    float* __restrict__ scores, float scale, uint32_t shared_id) {
-  const int lane = threadIdx.x & 31;
-  const int row = blockIdx.x * 4 + (threadIdx.x >> 5);
-  if (row >= rows) return;
+// Selection for one row of 256 logits by one warp.  Lane l owns experts
+// i*32 + l.  Each of the eight rounds takes the largest remaining
+// sigmoid(l)+bias (lowest expert id on a tie), records its sigmoid, and
+// removes it.  Weights are divided by 1e-20 + their sum (accumulated in rank
+// order) and multiplied by `scale`; slot 8 holds the shared expert id.
+__device__ __forceinline__ void route_warp(const float* logits, const float* __restrict__ bias, uint32_t* ids,
+                                           float* scores, float scale, uint32_t shared_id, int lane) {
   float original[8], choice[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
     const int e = i * 32 + lane;
-    original[i] = sigmoid_select(logits[static_cast<int64_t>(row) * 256 + e]);
+    original[i] = sigmoid_select(__ldcg(logits + e));
     choice[i] = __fadd_rn(original[i], bias[e]);
   }
   float selected[8];
@@ -121,11 +142,110 @@ __global__ void __launch_bounds__(128) route_kernel(const float* __restrict__ lo
     for (int i = 0; i < 8; ++i) total = __fadd_rn(total, selected[i]);
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      ids[static_cast<int64_t>(row) * 9 + i] = winners[i];
-      scores[static_cast<int64_t>(row) * 8 + i] = __fmul_rn(__fdiv_rn(selected[i], total), scale);
+      ids[i] = winners[i];
+      scores[i] = __fmul_rn(__fdiv_rn(selected[i], total), scale);
     }
-    ids[static_cast<int64_t>(row) * 9 + 8] = shared_id;
+    ids[8] = shared_id;
   }
+}
+
+__global__ void __launch_bounds__(128) route_kernel(const float* __restrict__ logits, const float* __restrict__ bias,
+                                                    int rows, uint32_t* __restrict__ ids,
+                                                    float* __restrict__ scores, float scale, uint32_t shared_id) {
+  const int lane = threadIdx.x & 31;
+  const int row = blockIdx.x * 4 + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  route_warp(logits + static_cast<int64_t>(row) * 256, bias, ids + static_cast<int64_t>(row) * 9,
+             scores + static_cast<int64_t>(row) * 8, scale, shared_id, lane);
+}
+
+// Gate GEMV (one CTA per expert row, as gate_logits_kernel) whose last CTA to
+// finish routes every token and builds the dispatch plan of the 9*tokens
+// slots.  `done` must be zero at launch.
+__global__ void __launch_bounds__(kGateWarps * 32) router_plan_kernel(
+    const void* __restrict__ x, int x_dtype, int tokens, int hidden, const float* __restrict__ wg,
+    float* __restrict__ logits, const float* __restrict__ bias, uint32_t* __restrict__ ids,
+    float* __restrict__ scores, int* __restrict__ done, int plan_experts, int skip_slot, PlanView plan) {
+  extern __shared__ int sm[];
+  __shared__ float red[kGateWarps][kGateTokens];
+  __shared__ int s_last;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int e = blockIdx.x;
+  const float* w = wg + static_cast<int64_t>(e) * hidden;
+  const int per_warp = (hidden / 4 + kGateWarps - 1) / kGateWarps;
+  const int g0 = warp * per_warp;
+  const int g1 = min(g0 + per_warp, hidden / 4);
+  for (int t0 = 0; t0 < tokens; t0 += kGateTokens) {
+    float acc[kGateTokens];
+#pragma unroll
+    for (int t = 0; t < kGateTokens; ++t) acc[t] = 0.f;
+    // All of a lane's weight loads of a chunk are issued before any use.
+    for (int gc = g0 + lane; gc < g1; gc += 32 * kGateChunk) {
+      float4 wv[kGateChunk];
+#pragma unroll
+      for (int i = 0; i < kGateChunk; ++i)
+        wv[i] = gc + 32 * i < g1 ? reinterpret_cast<const float4*>(w)[gc + 32 * i] : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int t = 0; t < kGateTokens; ++t) {
+        if (t0 + t < tokens) {
+#pragma unroll
+          for (int i = 0; i < kGateChunk; ++i) {
+            if (gc + 32 * i < g1) {
+              const float4 xv = load_act4(x, x_dtype, static_cast<int64_t>(t0 + t) * hidden + 4 * (gc + 32 * i));
+              acc[t] = fmaf(xv.x, wv[i].x, acc[t]);
+              acc[t] = fmaf(xv.y, wv[i].y, acc[t]);
+              acc[t] = fmaf(xv.z, wv[i].z, acc[t]);
+              acc[t] = fmaf(xv.w, wv[i].w, acc[t]);
+            }
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int t = 0; t < kGateTokens; ++t) {
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) acc[t] += __shfl_xor_sync(0xffffffffu, acc[t], off);
+    }
+    if (lane == 0) {
+#pragma unroll
+      for (int t = 0; t < kGateTokens; ++t) red[warp][t] = acc[t];
+    }
+    __syncthreads();
+    if (threadIdx.x < kGateTokens && t0 + static_cast<int>(threadIdx.x) < tokens) {
+      float s = 0.f;
+#pragma unroll
+      for (int w2 = 0; w2 < kGateWarps; ++w2) s += red[w2][threadIdx.x];
+      logits[static_cast<int64_t>(t0 + threadIdx.x) * 256 + e] = s;
+    }
+    __syncthreads();
+  }
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) s_last = atomicAdd(done, 1) == static_cast<int>(gridDim.x) - 1;
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  for (int t = warp; t < tokens; t += kGateWarps)
+    route_warp(logits + static_cast<int64_t>(t) * 256, bias, ids + static_cast<int64_t>(t) * 9,
+               scores + static_cast<int64_t>(t) * 8, 2.5f, 256u, lane);
+  __syncthreads();
+  plan_body(ids, tokens * 9, plan_experts, 9, skip_slot, plan, sm);
+}
+
+cudaError_t launch_router_plan(const void* x, int x_dtype, int tokens, int hidden, const float* wg, float* logits,
+                               const float* bias, uint32_t* ids, float* scores, int* done, int plan_experts,
+                               int skip_slot, PlanView plan, cudaStream_t s) {
+  const size_t smem = plan_smem_bytes(plan_experts, kGateWarps);
+  if (smem > 48 * 1024) {
+    cudaError_t err = cudaFuncSetAttribute(router_plan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           static_cast<int>(smem));
+    if (err != cudaSuccess) return err;
+  }
+  cudaError_t err = cudaMemsetAsync(done, 0, sizeof(int), s);
+  if (err != cudaSuccess) return err;
+  router_plan_kernel<<<256, kGateWarps * 32, smem, s>>>(x, x_dtype, tokens, hidden, wg, logits, bias, ids, scores,
+                                                         done, plan_experts, skip_slot, plan);
+  return cudaGetLastError();
 }
 
 cudaError_t launch_route(const float* logits, const float* bias, int rows, uint32_t* ids, float* scores,

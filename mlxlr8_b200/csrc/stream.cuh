@@ -22,6 +22,7 @@ struct StreamParams {
   int counter;
   int k, side, in_features, out_features, kt_per_split, splits, projections, nslots;
   uint32_t unit16;  // 65536
+  uint32_t mcg_mask, mcg_xor;  // 0x8FFF8FFF, 0x3B603B60 (runtime values: one LOP3 each)
 };
 
 // K tiles per split: a multiple of 8 (one 128-wide Hadamard block) so that

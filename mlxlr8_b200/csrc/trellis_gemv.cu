@@ -17,6 +17,7 @@
 #include "codec.cuh"
 #include "stream.cuh"
 #include "trellis_gemv.cuh"
+#include "plan.cuh"
 
 namespace exlr8 {
 
@@ -50,112 +51,22 @@ PlanView plan_view(void* base, int rows, int experts) {
   v.expert_count = p;
   p += experts;
   v.expert_start = p;
+  v.zero = nullptr;
+  v.zero_count = 0;
   return v;
 }
 
 constexpr int kPlanThreads = 1024;
 
-// Single-CTA stable counting sort of the slot expert ids, then groups of at
-// most kMaxGroupRows rows.  Ids outside [0, experts) are counted in
-// header[8] and left out of every group.
 __global__ void __launch_bounds__(kPlanThreads) plan_kernel(const uint32_t* __restrict__ ids, int rows,
                                                             int experts, int period, int skip_slot, PlanView plan) {
   extern __shared__ int sm[];
-  int* hist = sm;                        // [experts]
-  int* base = hist + experts;            // [experts]
-  int* gbase = base + experts;           // [experts]
-  int* wcount = gbase + experts;         // [32][experts]
-  __shared__ int s_total_groups;
-  __shared__ int s_bad;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-
-  for (int e = tid; e < experts; e += blockDim.x) hist[e] = 0;
-  if (tid == 0) s_bad = 0;
-  __syncthreads();
-  for (int i = tid; i < rows; i += blockDim.x) {
-    if (skip_slot >= 0 && i % period == skip_slot) continue;
-    uint32_t e = ids[i];
-    if (e < static_cast<uint32_t>(experts)) atomicAdd(&hist[e], 1);
-    else atomicAdd(&s_bad, 1);
-  }
-  __syncthreads();
-  // Exclusive scans of row counts and group counts (one warp).
-  if (warp == 0) {
-    const int per = (experts + 31) / 32;
-    const int first = lane * per;
-    int rsum = 0, gsum = 0;
-    for (int e = first; e < min(first + per, experts); ++e) {
-      rsum += hist[e];
-      gsum += (hist[e] + kMaxGroupRows - 1) / kMaxGroupRows;
-    }
-    int rinc = rsum, ginc = gsum;
-#pragma unroll
-    for (int off = 1; off < 32; off <<= 1) {
-      int r = __shfl_up_sync(0xffffffffu, rinc, off);
-      int g = __shfl_up_sync(0xffffffffu, ginc, off);
-      if (lane >= off) {
-        rinc += r;
-        ginc += g;
-      }
-    }
-    int rrun = rinc - rsum, grun = ginc - gsum;
-    for (int e = first; e < min(first + per, experts); ++e) {
-      base[e] = rrun;
-      gbase[e] = grun;
-      plan.expert_start[e] = rrun;
-      plan.expert_count[e] = hist[e];
-      rrun += hist[e];
-      grun += (hist[e] + kMaxGroupRows - 1) / kMaxGroupRows;
-    }
-    if (lane == 31) s_total_groups = ginc;
-  }
-  __syncthreads();
-  // Groups.
-  for (int e = tid; e < experts; e += blockDim.x) {
-    const int n = hist[e];
-    for (int c = 0; c * kMaxGroupRows < n; ++c) {
-      const int g = gbase[e] + c;
-      plan.group_expert[g] = e;
-      plan.group_start[g] = base[e] + c * kMaxGroupRows;
-      plan.group_count[g] = min(kMaxGroupRows, n - c * kMaxGroupRows);
-    }
-  }
-  __syncthreads();
-  // Stable scatter, one chunk of blockDim slots at a time.
-  const unsigned lt_mask = (1u << lane) - 1u;
-  for (int chunk = 0; chunk < rows; chunk += blockDim.x) {
-    for (int j = tid; j < 32 * experts; j += blockDim.x) wcount[j] = 0;
-    __syncthreads();
-    const int i = chunk + tid;
-    const bool skipped = i < rows && skip_slot >= 0 && i % period == skip_slot;
-    const uint32_t raw = (i < rows && !skipped) ? ids[i] : 0xFFFFFFFFu;
-    const bool valid = raw < static_cast<uint32_t>(experts);
-    const uint32_t key = valid ? raw : 0xFFFFFFFFu;
-    const unsigned peers = __match_any_sync(0xffffffffu, key);
-    const int leader = __ffs(peers) - 1;
-    const int rank = __popc(peers & lt_mask);
-    if (valid && lane == leader) wcount[warp * experts + key] = __popc(peers);
-    __syncthreads();
-    if (valid) {
-      int prior = 0;
-      for (int w = 0; w < warp; ++w) prior += wcount[w * experts + key];
-      plan.order[base[key] + prior + rank] = i;
-    }
-    __syncthreads();
-    if (valid && lane == leader) atomicAdd(&base[key], __popc(peers));
-    __syncthreads();
-  }
-  if (tid == 0) {
-    plan.header[0] = s_total_groups;
-    plan.header[1] = rows;
-    for (int c = 2; c < 8; ++c) plan.header[c] = 0;
-    plan.header[8] = s_bad;
-  }
+  plan_body(ids, rows, experts, period, skip_slot, plan, sm);
 }
 
 cudaError_t launch_plan(const uint32_t* ids, int rows, int experts, int period, int skip_slot, PlanView plan,
                         cudaStream_t s) {
-  const size_t smem = (3 + 32) * static_cast<size_t>(experts) * sizeof(int);
+  const size_t smem = plan_smem_bytes(experts, kPlanThreads / 32);
   if (smem > 48 * 1024) {
     cudaError_t err = cudaFuncSetAttribute(plan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                            static_cast<int>(smem));
@@ -291,19 +202,19 @@ __global__ void __launch_bounds__(kFragThreads) gate_finish_frag_kernel(
   float m = 0.0f;
   for (int b = warp; b < kt_count / 8; b += kFragThreads / 32) {
     const int c0 = kt0 * 16 + b * 128;
-    float gate[4], up[4];
+    float gate[4] = {0.f, 0.f, 0.f, 0.f}, up[4] = {0.f, 0.f, 0.f, 0.f};
+    if (ok) {
+      // Splits outer, columns inner, unrolled: all loads of a step in flight.
+      const float* pg = partial + static_cast<int64_t>(slot) * gu_splits * features + c0 + lane;
+      const float* pu = partial + (static_cast<int64_t>(nslots) + slot) * gu_splits * features + c0 + lane;
+#pragma unroll 4
+      for (int s = 0; s < gu_splits; ++s) {
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int col = c0 + lane + 32 * j;
-      float g = 0.f, u = 0.f;
-      if (ok) {
-        for (int s = 0; s < gu_splits; ++s) {
-          g += partial[(static_cast<int64_t>(slot) * gu_splits + s) * features + col];
-          u += partial[((static_cast<int64_t>(nslots) + slot) * gu_splits + s) * features + col];
+        for (int j = 0; j < 4; ++j) {
+          gate[j] += pg[static_cast<int64_t>(s) * features + 32 * j];
+          up[j] += pu[static_cast<int64_t>(s) * features + 32 * j];
         }
       }
-      gate[j] = g;
-      up[j] = u;
     }
     hadamard128(gate, lane);
     hadamard128(up, lane);
@@ -366,13 +277,12 @@ __global__ void __launch_bounds__(128) finish_kernel(const float* __restrict__ p
     for (int j = 0; j < 4; ++j) store_act(out, act_dtype, static_cast<int64_t>(slot) * features + block * 128 + lane + 32 * j, 0.0f);
     return;
   }
-  float v[4];
+  float v[4] = {0.f, 0.f, 0.f, 0.f};
+  const float* ps = partial + static_cast<int64_t>(slot) * splits * features + block * 128 + lane;
+#pragma unroll 4
+  for (int s = 0; s < splits; ++s) {
 #pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const int col = block * 128 + lane + 32 * j;
-    float a = 0.f;
-    for (int s = 0; s < splits; ++s) a += partial[(static_cast<int64_t>(slot) * splits + s) * features + col];
-    v[j] = a;
+    for (int j = 0; j < 4; ++j) v[j] += ps[static_cast<int64_t>(s) * features + 32 * j];
   }
   hadamard128(v, lane);
 #pragma unroll
@@ -397,35 +307,43 @@ cudaError_t launch_finish(const float* partial, int splits, const uint32_t* ids,
 // T(routed), T(routed + T(shared)), T(residual + combined)
 // (metal/fast_decode_finish_fused.metal:52-62).  When shared_values is given
 // it holds the typed shared-expert output [tokens][h] and slot 8 of partial is
-// not read.
+// not read.  shared_values are the dense shared expert's float32 split
+// partials, summed and cast here.
 __global__ void __launch_bounds__(288) finish_fused_kernel(const float* __restrict__ partial, int splits,
                                                            const uint32_t* __restrict__ ids, int tokens,
                                                            const void* __restrict__ out_scale, int scale_dtype,
                                                            int features, int experts,
                                                            const float* __restrict__ scores,
                                                            const void* __restrict__ residual,
-                                                           const void* __restrict__ shared_values, int act_dtype,
-                                                           void* __restrict__ out) {
+                                                           const void* __restrict__ shared_values, int shared_splits,
+                                                           int act_dtype, void* __restrict__ out) {
   __shared__ float products[9][128];
   const int lane = threadIdx.x & 31, slot = threadIdx.x >> 5;
   const int block = blockIdx.x, token = blockIdx.y;
   const int row = token * 9 + slot;
   if (slot == 8 && shared_values != nullptr) {
+    // Dense shared expert: float32 split partials [shared_splits][tokens][h].
+    const int64_t total = static_cast<int64_t>(tokens) * features;
+    float a[4] = {0.f, 0.f, 0.f, 0.f};
+    const float* sv = static_cast<const float*>(shared_values) + static_cast<int64_t>(token) * features + block * 128 + lane;
+#pragma unroll 4
+    for (int sp = 0; sp < shared_splits; ++sp) {
 #pragma unroll
-    for (int j = 0; j < 4; ++j)
-      products[8][lane + 32 * j] =
-          load_act(shared_values, act_dtype, static_cast<int64_t>(token) * features + block * 128 + lane + 32 * j);
+      for (int j = 0; j < 4; ++j) a[j] += __ldcg(sv + sp * total + 32 * j);
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) products[8][lane + 32 * j] = round_to(act_dtype, a[j]);
   } else {
     const int64_t e = ids[row];
     const bool ok = e < experts;  // an out-of-range id contributes zero
-    float v[4];
+    float v[4] = {0.f, 0.f, 0.f, 0.f};
+    if (ok) {
+      const float* ps = partial + static_cast<int64_t>(row) * splits * features + block * 128 + lane;
+#pragma unroll 4
+      for (int s = 0; s < splits; ++s) {
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int col = block * 128 + lane + 32 * j;
-      float a = 0.f;
-      if (ok)
-        for (int s = 0; s < splits; ++s) a += partial[(static_cast<int64_t>(row) * splits + s) * features + col];
-      v[j] = a;
+        for (int j = 0; j < 4; ++j) v[j] += ps[static_cast<int64_t>(s) * features + 32 * j];
+      }
     }
     hadamard128(v, lane);
 #pragma unroll
@@ -453,11 +371,11 @@ __global__ void __launch_bounds__(288) finish_fused_kernel(const float* __restri
 
 cudaError_t launch_finish_fused(const float* partial, int splits, const uint32_t* ids, int tokens,
                                 const void* out_scale, int scale_dtype, int features, int experts,
-                                const float* scores, const void* residual, const void* shared_values, int act_dtype,
-                                void* out, cudaStream_t s) {
+                                const float* scores, const void* residual, const void* shared_values,
+                                int shared_splits, int act_dtype, void* out, cudaStream_t s) {
   dim3 grid(features / 128, tokens);
   finish_fused_kernel<<<grid, 288, 0, s>>>(partial, splits, ids, tokens, out_scale, scale_dtype, features, experts,
-                                           scores, residual, shared_values, act_dtype, out);
+                                           scores, residual, shared_values, shared_splits, act_dtype, out);
   return cudaGetLastError();
 }
 

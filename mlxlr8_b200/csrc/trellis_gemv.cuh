@@ -18,7 +18,14 @@ struct PlanView {
   int32_t* group_count;   // [max_groups]
   int32_t* expert_count;  // [experts] rows per expert
   int32_t* expert_start;  // [experts] first position in order
+  int32_t* zero;          // counters of later kernels, zeroed by the plan (may be null)
+  int zero_count;
 };
+
+// Shared memory of plan_body for `warps` warps.
+inline size_t plan_smem_bytes(int experts, int warps) {
+  return static_cast<size_t>(3 + warps) * experts * sizeof(int);
+}
 
 size_t plan_bytes(int rows, int experts);
 PlanView plan_view(void* base, int rows, int experts);
@@ -30,7 +37,7 @@ cudaError_t launch_finish(const float* partial, int splits, const uint32_t* ids,
                           int scale_dtype, int features, int experts, int act_dtype, void* out, cudaStream_t s);
 cudaError_t launch_finish_fused(const float* partial, int splits, const uint32_t* ids, int tokens,
                                 const void* out_scale, int scale_dtype, int features, int experts,
-                                const float* scores, const void* residual, const void* shared_values, int act_dtype,
-                                void* out, cudaStream_t s);
+                                const float* scores, const void* residual, const void* shared_values,
+                                int shared_splits, int act_dtype, void* out, cudaStream_t s);
 
 }  // namespace exlr8

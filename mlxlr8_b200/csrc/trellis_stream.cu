@@ -51,10 +51,17 @@ __device__ __forceinline__ void mma_f16(float c[4], const uint32_t a[4], uint2 b
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b.x), "r"(b.y));
 }
 
+// (v & mask) ^ xor as a single three-input logic op.
+__device__ __forceinline__ uint32_t lop_and_xor(uint32_t v, uint32_t mask, uint32_t xorv) {
+  uint32_t r;
+  asm("lop3.b32 %0, %1, %2, %3, 0x6A;" : "=r"(r) : "r"(v), "r"(mask), "r"(xorv));
+  return r;
+}
+
 // f16x2 value pair of two hashed products (low half = a).
-__device__ __forceinline__ uint32_t pair_from_products(uint32_t pa, uint32_t pb) {
-  uint32_t lo = lop_mask_xor(__byte_perm(pa, pb, 0x5410));
-  uint32_t hi = lop_mask_xor(__byte_perm(pa, pb, 0x7632));
+__device__ __forceinline__ uint32_t pair_from_products(uint32_t pa, uint32_t pb, uint32_t mask, uint32_t xorv) {
+  uint32_t lo = lop_and_xor(__byte_perm(pa, pb, 0x5410), mask, xorv);
+  uint32_t hi = lop_and_xor(__byte_perm(pa, pb, 0x7632), mask, xorv);
   __half2 s = __hadd2(*reinterpret_cast<__half2*>(&lo), *reinterpret_cast<__half2*>(&hi));
   return round_e4m3_f16x2(*reinterpret_cast<uint32_t*>(&s));
 }
@@ -62,7 +69,8 @@ __device__ __forceinline__ uint32_t pair_from_products(uint32_t pa, uint32_t pb)
 // A fragment of one K4 tile from tile word l and word l-1.  `unit16` is the
 // runtime value 65536: it keeps the high-half extraction an IMAD.HI on the
 // multiply pipe instead of a shift on the integer pipe.
-__device__ __forceinline__ void k4_fragment(uint32_t word, uint32_t prior, uint32_t unit16, uint32_t a[4]) {
+__device__ __forceinline__ void k4_fragment(uint32_t word, uint32_t prior, uint32_t unit16, uint32_t mask,
+                                            uint32_t xorv, uint32_t a[4]) {
   const uint32_t v0 = word;                              // (cw3 : cw7)
   const uint32_t v4 = __funnelshift_r(word, prior, 4);   // (cw2 : cw6)
   const uint32_t v8 = __funnelshift_r(word, prior, 8);   // (cw1 : cw5)
@@ -73,10 +81,10 @@ __device__ __forceinline__ void k4_fragment(uint32_t word, uint32_t prior, uint3
   // v*C - ph*2^16 (mod 2^32), one multiply-add each.
   const uint32_t pl0 = v0 * kMcgMul + ph0 * 0xFFFF0000u, pl4 = v4 * kMcgMul + ph4 * 0xFFFF0000u;
   const uint32_t pl8 = v8 * kMcgMul + ph8 * 0xFFFF0000u, pl12 = v12 * kMcgMul + ph12 * 0xFFFF0000u;
-  a[0] = pair_from_products(ph12, ph8);  // j0, j1
-  a[1] = pair_from_products(pl12, pl8);  // j4, j5
-  a[2] = pair_from_products(ph4, ph0);   // j2, j3
-  a[3] = pair_from_products(pl4, pl0);   // j6, j7
+  a[0] = pair_from_products(ph12, ph8, mask, xorv);  // j0, j1
+  a[1] = pair_from_products(pl12, pl8, mask, xorv);  // j4, j5
+  a[2] = pair_from_products(ph4, ph0, mask, xorv);   // j2, j3
+  a[3] = pair_from_products(pl4, pl0, mask, xorv);   // j6, j7
 }
 
 struct UnitInfo {
@@ -176,7 +184,7 @@ __global__ void __launch_bounds__(kStreamThreads, 2) trellis_stream_kernel(Strea
 
   // ---------------- consumers ----------------
   const int gid = lane >> 2, tig = lane & 3;
-  const uint32_t unit16 = p.unit16;
+  const uint32_t unit16 = p.unit16, mcg_mask = p.mcg_mask, mcg_xor = p.mcg_xor;
   int stage = 0;
   uint32_t phase = 0;
   float acc[2][4];
@@ -213,13 +221,9 @@ __global__ void __launch_bounds__(kStreamThreads, 2) trellis_stream_kernel(Strea
     const uint32_t* codes = reinterpret_cast<const uint32_t*>(base);
     const uint2* frag = reinterpret_cast<const uint2*>(base + G::kCodeBytes);
     // Every stage holds kStageTiles K tiles (splits are whole 128-wide blocks).
-    uint2 b0[kStageTiles], b1[kStageTiles];
     const bool has0 = r0 < nr, has1 = 4 + r0 < nr;
-#pragma unroll
-    for (int kk = 0; kk < kStageTiles; ++kk) {
-      b0[kk] = has0 ? frag[(r0 * kFragRowBytes) / 8 + kk * 8 + fpos] : make_uint2(0u, 0u);
-      b1[kk] = has1 ? frag[((4 + r0) * kFragRowBytes) / 8 + kk * 8 + fpos] : make_uint2(0u, 0u);
-    }
+    const uint2* f0 = frag + (r0 * kFragRowBytes) / 8 + fpos;
+    const uint2* f1 = frag + ((4 + r0) * kFragRowBytes) / 8 + fpos;
     if (K == 4) {
       uint32_t word[kStageTiles], prior[kStageTiles];
 #pragma unroll
@@ -232,16 +236,16 @@ __global__ void __launch_bounds__(kStreamThreads, 2) trellis_stream_kernel(Strea
 #pragma unroll
         for (int kk = 0; kk < kStageTiles; ++kk) {
           uint32_t a[4];
-          k4_fragment(word[kk], prior[kk], unit16, a);
-          mma_f16(acc[0], a, b0[kk]);
-          mma_f16(acc[1], a, b1[kk]);
+          k4_fragment(word[kk], prior[kk], unit16, mcg_mask, mcg_xor, a);
+          mma_f16(acc[0], a, has0 ? f0[kk * 8] : make_uint2(0u, 0u));
+          mma_f16(acc[1], a, has1 ? f1[kk * 8] : make_uint2(0u, 0u));
         }
       } else {
 #pragma unroll
         for (int kk = 0; kk < kStageTiles; ++kk) {
           uint32_t a[4];
-          k4_fragment(word[kk], prior[kk], unit16, a);
-          mma_f16(acc[0], a, b0[kk]);
+          k4_fragment(word[kk], prior[kk], unit16, mcg_mask, mcg_xor, a);
+          mma_f16(acc[0], a, has0 ? f0[kk * 8] : make_uint2(0u, 0u));
         }
       }
     } else {
@@ -250,8 +254,8 @@ __global__ void __launch_bounds__(kStreamThreads, 2) trellis_stream_kernel(Strea
         uint32_t cw[8], a[4];
         generic_codewords(codes + (kk * 8 + warp) * G::kTileWords, K, geo, cw);
         tile_fragment(cw, a);
-        mma_f16(acc[0], a, b0[kk]);
-        if (ncg > 1) mma_f16(acc[1], a, b1[kk]);
+        mma_f16(acc[0], a, has0 ? f0[kk * 8] : make_uint2(0u, 0u));
+        if (ncg > 1) mma_f16(acc[1], a, has1 ? f1[kk * 8] : make_uint2(0u, 0u));
       }
     }
     __syncwarp();
