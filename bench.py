@@ -46,11 +46,11 @@ sys.path.insert(0, str(ROOT))
 HIDDEN, INTER, EXPERTS, K_BITS = 6144, 2048, 256, 4
 METRIC = "MoE-layer tokens/s (decode GB/s vs HBM; prefill TFLOPS) at 1/2/4/8 B200"
 
-# dram__bytes_read.sum + dram__bytes_write.sum per launch of the gate/up
-# streaming GEMV, from one ncu capture of a 9-expert case (18 expert matrices,
-# profiles/trellis_stream_gate_up_decode.txt), per expert matrix; the bench
-# scales it by the matrices its launches stream.
-TRAFFIC_PER_MATRIX = (113_756_928 + 0) / 18
+# dram__bytes_read.sum + dram__bytes_write.sum of one gate/up streaming-GEMV
+# launch from an ncu capture of a nine-expert case (18 expert matrices,
+# profiles/trellis_stream_gate_up_decode.md), per expert matrix; the bench
+# scales it by the matrices its own launches stream.
+TRAFFIC_PER_MATRIX = (113_755_904 + 4_150_784) / 18
 
 
 def parse():
@@ -63,7 +63,37 @@ def parse():
     p.add_argument("--impl", choices=("b200", "reference"), default="b200")
     p.add_argument("--cpu-seconds", type=float, default=10.0)
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--ncu-driver", choices=("layer", "mlp"), default=None,
+                   help="untimed run for an ncu capture: 'layer' calls one resident layer --calls times; 'mlp' "
+                        "runs the nine-expert fast_expert_mlp at full size (about 170 MB of weights)")
+    p.add_argument("--calls", type=int, default=5)
     return p.parse_args()
+
+
+def ncu_driver(args):
+    """Small, untimed workload for ncu (no graphs, no clocks, one GPU)."""
+    import torch
+
+    from mlxlr8_b200.fast_decode import fast_expert_mlp
+    from mlxlr8_b200.moe import MoELayer
+    from mlxlr8_b200.synthetic import make_layer
+
+    torch.cuda.set_device(0)
+    if args.ncu_driver == "layer":
+        layer = make_layer(seed=1)
+        moe = MoELayer(layer.gate_weight, layer.bias, layer.experts)
+        x, r = layer.tokens(args.tokens)
+        for _ in range(args.calls):
+            moe(x, r)
+    else:
+        layer = make_layer(seed=1, routed=9, shared="none")
+        e = layer.experts
+        x, _ = layer.tokens(args.tokens)
+        ids = torch.arange(9, dtype=torch.int32, device="cuda").repeat(args.tokens, 1)
+        for _ in range(args.calls):
+            fast_expert_mlp(x, ids, e.packed, e.scales, K_BITS, HIDDEN, INTER)
+    torch.cuda.synchronize()
+    print("ncu driver done", flush=True)
 
 
 def dist_setup():
@@ -193,6 +223,9 @@ def unique_experts(ids_list):
 
 def main():
     args = parse()
+    if args.ncu_driver:
+        ncu_driver(args)
+        return
     world, rank, local = dist_setup()
     if args.impl == "reference":
         reference_arm(args, world, rank)
