@@ -227,6 +227,75 @@ int exlr8_moe_layer_noalloc(const void* x, int x_dtype, const void* residual, in
  * Synchronises `stream`. */
 int exlr8_workspace_bad_ids(const void* workspace, int64_t* bad_ids, void* stream);
 
+/* ---- joined MXFP4 experts (prefill) -------------------------------------- */
+
+/*
+ * Resident four-bit experts of exlr8.joined_mxfp4.JoinedMXFP4
+ * (joined_mxfp4.py:137-165): gate and up concatenated per expert as
+ * [2 * intermediate][hidden] (gate rows first, joined_mxfp4.py:41-45), down
+ * as [hidden][intermediate]; E2M1 values, eight per uint32 word with the low
+ * nibble first, and one E8M0 scale per 32 values along the input.  Scales are
+ * passed in the layout written by exlr8_mxfp4_prepare_scales.  `unit` is the
+ * sign vector folded into the gate/up input (joined_mxfp4.py:13);
+ * gate_out/up_out/down_in/down_out are the remaining signed channel scales
+ * (scales["gate"][1], scales["up"][1], scales["down"][0], scales["down"][1]).
+ * Requirements: hidden % 256 == 0, intermediate % 128 == 0, code buffers
+ * 32-byte aligned, scale buffers 16-byte aligned.
+ */
+typedef struct exlr8_joined_mxfp4 {
+  const void* gate_up;        /* uint32 [experts][2 * intermediate][hidden / 8] */
+  const void* gate_up_scales; /* prepared E8M0 of [experts * 2 * intermediate][hidden / 32] */
+  const void* down;           /* uint32 [experts][hidden][intermediate / 8] */
+  const void* down_scales;    /* prepared E8M0 of [experts * hidden][intermediate / 32] */
+  const void* unit;           /* [hidden] */
+  const void* gate_out;       /* [experts][intermediate] */
+  const void* up_out;         /* [experts][intermediate] */
+  const void* down_in;        /* [experts][intermediate] */
+  const void* down_out;       /* [experts][hidden] */
+  int scale_dtype;            /* EXLR8_DTYPE_F16 or EXLR8_DTYPE_F32 (unit and channel scales) */
+  int64_t experts;
+  int hidden;
+  int intermediate;
+} exlr8_joined_mxfp4;
+
+/* Re-lay E8M0 scales uint8 [rows][in_features / 32] (MLX quantize output,
+ * joined_mxfp4.py:32) for the tensor-core GEMM: 512-byte blocks of 128 rows x
+ * 4 scales, byte (r % 32) * 16 + (r % 128 / 32) * 4 + k % 4 of block
+ * [r / 128][k / 4].  rows and in_features must be multiples of 128. */
+size_t exlr8_mxfp4_prepared_scales_bytes(int64_t rows, int in_features);
+int exlr8_mxfp4_prepare_scales(const uint8_t* scales, int64_t rows, int in_features, uint8_t* prepared, void* stream);
+
+/* JoinedMXFP4.slots(x, ids) (joined_mxfp4.py:147-150): x [tokens][hidden],
+ * indices uint32 [tokens][slots] -> out [tokens][slots][hidden] in x's dtype,
+ * each slot T(H(v) * down_out[e]).  Ids outside [0, experts) give zeros. */
+size_t exlr8_joined_workspace(int64_t tokens, int slots, int hidden, int intermediate, int64_t experts);
+int exlr8_joined_slots(const void* x, int x_dtype, const uint32_t* indices, int64_t tokens, int slots,
+                       const exlr8_joined_mxfp4* weights, void* out, void* workspace, size_t workspace_bytes,
+                       void* stream);
+
+/* JoinedMXFP4.finish(x, ids, scores, residual) (joined_mxfp4.py:152-163):
+ * nine slots per token (slot 8 = shared expert), routing-weighted combine in
+ * the order of metal/fast_decode_finish_fused.metal plus the residual.
+ * Workspace: exlr8_joined_workspace(tokens, 9, ...). */
+int exlr8_joined_finish(const void* x, int x_dtype, const uint32_t* indices, const float* scores,
+                        const void* residual, int64_t tokens, const exlr8_joined_mxfp4* weights, void* out,
+                        void* workspace, size_t workspace_bytes, void* stream);
+
+/* Router + JoinedMXFP4.finish: the MoE branch of DecoderLayer
+ * (model.py:385-418) on the joined path.  experts must be >= 257 (expert 256
+ * is the shared expert).  indices/scores may be null. */
+size_t exlr8_joined_moe_layer_workspace(int64_t tokens, int hidden, int intermediate, int64_t experts);
+int exlr8_joined_moe_layer(const void* x, int x_dtype, const void* residual, int64_t tokens, const float* gate_weight,
+                           const float* bias, const exlr8_joined_mxfp4* weights, void* out, uint32_t* indices,
+                           float* scores, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Dispatch header of the last joined call that used `workspace` (sizes as
+ * given to that call): [0] chunks, [1] padded rows, [2..3] GEMM unit counters,
+ * [4] GEMM error code (0 = none; non-zero = a bounded wait timed out).
+ * Synchronises `stream`. */
+int exlr8_joined_status(const void* workspace, int64_t tokens, int slots, int64_t experts, int32_t* header,
+                        void* stream);
+
 #ifdef __cplusplus
 }
 #endif

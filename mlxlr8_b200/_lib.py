@@ -41,6 +41,24 @@ class DenseExpert(ctypes.Structure):
     _fields_ = [("gate", c_void_p), ("up", c_void_p), ("down", c_void_p)]
 
 
+class JoinedMXFP4Weights(ctypes.Structure):
+    _fields_ = [
+        ("gate_up", c_void_p),
+        ("gate_up_scales", c_void_p),
+        ("down", c_void_p),
+        ("down_scales", c_void_p),
+        ("unit", c_void_p),
+        ("gate_out", c_void_p),
+        ("up_out", c_void_p),
+        ("down_in", c_void_p),
+        ("down_out", c_void_p),
+        ("scale_dtype", c_int),
+        ("experts", c_int64),
+        ("hidden", c_int),
+        ("intermediate", c_int),
+    ]
+
+
 _SIGNATURES = {
     "exlr8_abi_version": (c_int, []),
     "exlr8_status_string": (c_char_p, [c_int]),
@@ -74,6 +92,18 @@ _SIGNATURES = {
     "exlr8_moe_layer_noalloc": (c_int, [c_void_p, c_int, c_void_p, c_int64, c_void_p, c_void_p,
                                         POINTER(TrellisExperts), POINTER(DenseExpert), c_void_p, c_void_p, c_void_p,
                                         c_void_p]),
+    "exlr8_mxfp4_prepared_scales_bytes": (c_size_t, [c_int64, c_int]),
+    "exlr8_mxfp4_prepare_scales": (c_int, [c_void_p, c_int64, c_int, c_void_p, c_void_p]),
+    "exlr8_joined_workspace": (c_size_t, [c_int64, c_int, c_int, c_int, c_int64]),
+    "exlr8_joined_slots": (c_int, [c_void_p, c_int, c_void_p, c_int64, c_int, POINTER(JoinedMXFP4Weights), c_void_p,
+                                   c_void_p, c_size_t, c_void_p]),
+    "exlr8_joined_finish": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_int64,
+                                    POINTER(JoinedMXFP4Weights), c_void_p, c_void_p, c_size_t, c_void_p]),
+    "exlr8_joined_moe_layer_workspace": (c_size_t, [c_int64, c_int, c_int, c_int64]),
+    "exlr8_joined_moe_layer": (c_int, [c_void_p, c_int, c_void_p, c_int64, c_void_p, c_void_p,
+                                       POINTER(JoinedMXFP4Weights), c_void_p, c_void_p, c_void_p, c_void_p, c_size_t,
+                                       c_void_p]),
+    "exlr8_joined_status": (c_int, [c_void_p, c_int64, c_int, c_int64, c_void_p, c_void_p]),
 }
 
 EXPORTED = tuple(_SIGNATURES)

@@ -4,6 +4,7 @@
 #include <cstdio>
 #include <cstring>
 
+#include "capi_util.cuh"
 #include "common.cuh"
 #include "dense.cuh"
 #include "router.cuh"
@@ -12,80 +13,12 @@
 
 using namespace exlr8;
 
-namespace {
-
+namespace exlr8 {
 thread_local char g_cuda_error[256] = "";
-
-int cuda_status(cudaError_t err) {
-  if (err == cudaSuccess) return EXLR8_OK;
-  std::snprintf(g_cuda_error, sizeof(g_cuda_error), "%s: %s", cudaGetErrorName(err), cudaGetErrorString(err));
-  return EXLR8_ERR_CUDA;
-}
-
-#define EXLR8_TRY(expr)                          \
-  do {                                           \
-    int _st = cuda_status(expr);                 \
-    if (_st != EXLR8_OK) return _st;             \
-  } while (0)
-
-#define EXLR8_CHECK(expr)                        \
-  do {                                           \
-    int _st = (expr);                            \
-    if (_st != EXLR8_OK) return _st;             \
-  } while (0)
-
-inline cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
-
-// ---- opt-in launch timing (exlr8_profile_*) --------------------------------
-struct Profiler {
-  bool on = false;
-  int capacity = 0, used = 0;
-  cudaEvent_t* events = nullptr;  // 2 * capacity
-  int* kinds = nullptr;
-};
 thread_local Profiler g_prof;
+}  // namespace exlr8
 
-struct ProfileScope {
-  int slot = -1;
-  cudaStream_t stream;
-  ProfileScope(int kind, cudaStream_t s) : stream(s) {
-    if (g_prof.on && g_prof.used < g_prof.capacity) {
-      slot = g_prof.used++;
-      g_prof.kinds[slot] = kind;
-      cudaEventRecord(g_prof.events[2 * slot], s);
-    }
-  }
-  ~ProfileScope() {
-    if (slot >= 0) cudaEventRecord(g_prof.events[2 * slot + 1], stream);
-  }
-};
-
-#define EXLR8_TIMED(kind, s, expr)   \
-  do {                               \
-    ProfileScope _scope(kind, s);    \
-    EXLR8_TRY(expr);                 \
-  } while (0)
-
-inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
-
-inline bool valid_act(int d) { return d == EXLR8_DTYPE_F32 || d == EXLR8_DTYPE_F16 || d == EXLR8_DTYPE_BF16; }
-inline bool valid_scale(int d) { return d == EXLR8_DTYPE_F32 || d == EXLR8_DTYPE_F16; }
-
-constexpr size_t kAlign = 256;
-inline size_t align_up(size_t v) { return (v + kAlign - 1) / kAlign * kAlign; }
-
-// Linear workspace carve-out.
-struct Carver {
-  char* base;
-  size_t used = 0;
-  explicit Carver(void* b) : base(static_cast<char*>(b)) {}
-  template <typename T>
-  T* take(size_t bytes) {
-    T* p = reinterpret_cast<T*>(base ? base + used : nullptr);
-    used += align_up(bytes);
-    return p;
-  }
-};
+namespace {
 
 // K splits.  Gate/up follow fast_decode.py:216 (min(8, max(1, hidden // 768)));
 // the down product splits once per 1024 inputs.  Splits are rounded to whole
@@ -439,7 +372,7 @@ int exlr8_expert_linear(const void* x, int x_dtype, int per_slot, const uint32_t
   gp.splits = sp.count;
   gp.projections = 1;
   EXLR8_TRY(launch_stream(gp, s));
-  return cuda_status(launch_finish(part, sp.count, indices, n, out_scale, scale_dtype, out_features, e, x_dtype, out, s));
+  return cuda_status(launch_finish(part, sp.count, nullptr, indices, n, out_scale, scale_dtype, out_features, e, x_dtype, out, s));
 }
 
 size_t exlr8_expert_mlp_workspace(int64_t tokens, int slots, int hidden, int intermediate, int64_t experts) {
@@ -466,7 +399,7 @@ int exlr8_expert_mlp(const void* x, int x_dtype, int per_slot, const uint32_t* i
               launch_plan(indices, static_cast<int>(rows), static_cast<int>(experts), slots, -1, b.plan, s));
   EXLR8_CHECK(run_mlp_after_plan(x, x_dtype, per_slot, slots, indices, rows, ex, experts, nullptr, tokens, l, b, s));
   ProfileScope scope(EXLR8_KERNEL_FINISH, s);
-  return cuda_status(launch_finish(b.dpart, l.s2.count, indices, static_cast<int>(rows), ex->out_scale[2],
+  return cuda_status(launch_finish(b.dpart, l.s2.count, nullptr, indices, static_cast<int>(rows), ex->out_scale[2],
                                    ex->scale_dtype, ex->hidden, static_cast<int>(experts), x_dtype, out, s));
 }
 
@@ -483,7 +416,7 @@ static int mlp_finish_after_plan(const void* x, int x_dtype, const uint32_t* ind
   const int64_t rows = tokens * 9;
   EXLR8_CHECK(run_mlp_after_plan(x, x_dtype, 0, 9, indices, rows, ex, experts, shared, tokens, l, b, s));
   ProfileScope scope(EXLR8_KERNEL_FINISH, s);
-  return cuda_status(launch_finish_fused(b.dpart, l.s2.count, indices, static_cast<int>(tokens), ex->out_scale[2],
+  return cuda_status(launch_finish_fused(b.dpart, l.s2.count, nullptr, indices, static_cast<int>(tokens), ex->out_scale[2],
                                          ex->scale_dtype, ex->hidden, static_cast<int>(experts), scores, residual,
                                          shared ? b.ddown : nullptr, kDenseDownSplits, x_dtype, out, s));
 }

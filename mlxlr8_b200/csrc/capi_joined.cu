@@ -1,0 +1,244 @@
+// extern "C" entry points of the joined MXFP4 path (exlr8 joined_mxfp4.py
+// JoinedMXFP4.slots / .finish and the prefill MoE layer around them).
+//
+// Sequence of one call (all on the caller's stream, no allocation):
+//   plan (expert sort) -> segments/row maps -> prep (H(x * unit), E4M3 hi/lo)
+//   -> grouped tcgen05 gate+up GEMM -> gate finish (SwiGLU, down input
+//   quantised) -> grouped tcgen05 down GEMM -> finish (per slot, or fused
+//   with the routing-weighted combine, the shared slot and the residual).
+
+#include "capi_util.cuh"
+#include "common.cuh"
+#include "joined.cuh"
+#include "mx_gemm.cuh"
+#include "router.cuh"
+#include "trellis_gemv.cuh"
+
+using namespace exlr8;
+
+namespace {
+
+struct JoinedLayout {
+  int64_t rows, padded, max_chunks;
+};
+
+JoinedLayout joined_layout(int64_t tokens, int slots, int64_t experts) {
+  JoinedLayout l;
+  l.rows = tokens * slots;
+  l.padded = mx_padded_rows(l.rows, experts);
+  l.max_chunks = mx_max_chunks(l.rows, experts);
+  return l;
+}
+
+struct JoinedBuffers {
+  PlanView plan;
+  MxChunks chunks;
+  uint8_t *x_hi, *x_lo, *x_scales;
+  float* gu;
+  uint8_t *h_hi, *h_lo, *h_scales;
+  float* v;
+};
+
+JoinedBuffers carve_joined(const JoinedLayout& l, int hidden, int inter, int64_t experts, Carver& c) {
+  JoinedBuffers b;
+  void* plan_base = c.take<char>(plan_bytes(static_cast<int>(l.rows), static_cast<int>(experts)));
+  b.plan = plan_view(plan_base, static_cast<int>(l.rows), static_cast<int>(experts));
+  b.chunks.header = c.take<int32_t>(16 * sizeof(int32_t));
+  b.chunks.chunk_start = c.take<int32_t>(l.max_chunks * sizeof(int32_t));
+  b.chunks.chunk_rows = c.take<int32_t>(l.max_chunks * sizeof(int32_t));
+  b.chunks.chunk_expert = c.take<int32_t>(l.max_chunks * sizeof(int32_t));
+  b.chunks.padded_start = c.take<int32_t>((experts + 1) * sizeof(int32_t));
+  b.chunks.row_slot = c.take<int32_t>(l.padded * sizeof(int32_t));
+  b.chunks.slot_row = c.take<int32_t>(l.rows * sizeof(int32_t));
+  b.x_hi = c.take<uint8_t>(l.padded * hidden);
+  b.x_lo = c.take<uint8_t>(l.padded * hidden);
+  b.x_scales = c.take<uint8_t>(l.padded * hidden / 32);
+  b.gu = c.take<float>(l.padded * 2 * inter * sizeof(float));
+  b.h_hi = c.take<uint8_t>(l.padded * inter);
+  b.h_lo = c.take<uint8_t>(l.padded * inter);
+  b.h_scales = c.take<uint8_t>(l.padded * inter / 32);
+  b.v = c.take<float>(l.padded * hidden * sizeof(float));
+  return b;
+}
+
+inline bool aligned32(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 31u) == 0; }
+
+int check_joined(const exlr8_joined_mxfp4* w) {
+  if (!w) return EXLR8_ERR_ARG;
+  if (w->experts <= 0 || w->hidden <= 0 || w->intermediate <= 0) return EXLR8_ERR_DIMS;
+  if (w->hidden % 256 || w->intermediate % 128) return EXLR8_ERR_DIMS;
+  if (w->experts * 2 * w->intermediate >= (int64_t(1) << 31) || w->experts * w->hidden >= (int64_t(1) << 31))
+    return EXLR8_ERR_UNSUPPORTED;
+  if (!valid_scale(w->scale_dtype)) return EXLR8_ERR_DTYPE;
+  if (!w->gate_up || !w->gate_up_scales || !w->down || !w->down_scales || !w->unit || !w->gate_out || !w->up_out ||
+      !w->down_in || !w->down_out)
+    return EXLR8_ERR_ARG;
+  if (!aligned32(w->gate_up) || !aligned32(w->down) || !aligned16(w->gate_up_scales) || !aligned16(w->down_scales))
+    return EXLR8_ERR_ALIGN;
+  return EXLR8_OK;
+}
+
+// Shared body: everything up to the float32 down products in b.v.
+int joined_products(const void* x, int x_dtype, const uint32_t* ids, int64_t tokens, int slots,
+                    const exlr8_joined_mxfp4* w, const JoinedLayout& l, const JoinedBuffers& b, cudaStream_t s) {
+  const int experts = static_cast<int>(w->experts);
+  const int h = w->hidden, m = w->intermediate;
+  EXLR8_TIMED(EXLR8_KERNEL_PLAN, s,
+              launch_plan(ids, static_cast<int>(l.rows), experts, slots, -1, b.plan, s));
+  EXLR8_TIMED(EXLR8_KERNEL_PLAN, s, launch_joined_segments(b.plan, experts, static_cast<int>(l.rows), b.chunks, s));
+  EXLR8_TIMED(EXLR8_KERNEL_PREP, s,
+              launch_joined_prep(x, x_dtype, w->unit, w->scale_dtype, slots, b.chunks, h, b.x_hi, b.x_lo,
+                                 b.x_scales, s));
+  MxGemmArgs g;
+  g.weights = w->gate_up;
+  g.weight_scales = static_cast<const uint8_t*>(w->gate_up_scales);
+  g.x_hi = b.x_hi;
+  g.x_lo = b.x_lo;
+  g.x_scales = b.x_scales;
+  g.chunks = b.chunks;
+  g.counter_index = 2;
+  g.experts = w->experts;
+  g.padded_rows = l.padded;
+  g.in_features = h;
+  g.out_features = 2 * m;
+  g.paired = 1;
+  g.out = b.gu;
+  EXLR8_TIMED(EXLR8_KERNEL_GATE_UP, s, launch_mx_gemm(g, s));
+  EXLR8_TIMED(EXLR8_KERNEL_GATE_FINISH, s,
+              launch_joined_gate_finish(b.gu, ids, b.chunks, w->gate_out, w->up_out, w->down_in, w->scale_dtype, m,
+                                        x_dtype, b.h_hi, b.h_lo, b.h_scales, s));
+  g.weights = w->down;
+  g.weight_scales = static_cast<const uint8_t*>(w->down_scales);
+  g.x_hi = b.h_hi;
+  g.x_lo = b.h_lo;
+  g.x_scales = b.h_scales;
+  g.counter_index = 3;
+  g.in_features = m;
+  g.out_features = h;
+  g.paired = 0;
+  g.out = b.v;
+  EXLR8_TIMED(EXLR8_KERNEL_DOWN, s, launch_mx_gemm(g, s));
+  return EXLR8_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+size_t exlr8_mxfp4_prepared_scales_bytes(int64_t rows, int in_features) {
+  if (rows <= 0 || in_features <= 0) return 0;
+  return static_cast<size_t>(rows) * static_cast<size_t>(in_features / 32);
+}
+
+int exlr8_mxfp4_prepare_scales(const uint8_t* scales, int64_t rows, int in_features, uint8_t* prepared, void* stream) {
+  if (rows < 0 || in_features <= 0 || rows % 128 || in_features % 128) return EXLR8_ERR_DIMS;
+  if (rows == 0) return EXLR8_OK;
+  if (!scales || !prepared) return EXLR8_ERR_ARG;
+  return cuda_status(launch_mx_prepare_scales(scales, rows, in_features / 32, prepared, as_stream(stream)));
+}
+
+size_t exlr8_joined_workspace(int64_t tokens, int slots, int hidden, int intermediate, int64_t experts) {
+  if (tokens <= 0 || slots <= 0) return 0;
+  Carver c(nullptr);
+  carve_joined(joined_layout(tokens, slots, experts), hidden, intermediate, experts, c);
+  return c.used;
+}
+
+int exlr8_joined_slots(const void* x, int x_dtype, const uint32_t* indices, int64_t tokens, int slots,
+                       const exlr8_joined_mxfp4* w, void* out, void* workspace, size_t workspace_bytes,
+                       void* stream) {
+  EXLR8_CHECK(check_joined(w));
+  if (!valid_act(x_dtype)) return EXLR8_ERR_DTYPE;
+  if (tokens < 0 || slots <= 0) return EXLR8_ERR_ROWS;
+  if (tokens == 0) return EXLR8_OK;
+  if (tokens * slots > (int64_t(1) << 24)) return EXLR8_ERR_UNSUPPORTED;
+  if (!x || !indices || !out) return EXLR8_ERR_ARG;
+  if (!workspace || workspace_bytes < exlr8_joined_workspace(tokens, slots, w->hidden, w->intermediate, w->experts))
+    return EXLR8_ERR_WORKSPACE;
+  cudaStream_t s = as_stream(stream);
+  const JoinedLayout l = joined_layout(tokens, slots, w->experts);
+  Carver c(workspace);
+  const JoinedBuffers b = carve_joined(l, w->hidden, w->intermediate, w->experts, c);
+  EXLR8_CHECK(joined_products(x, x_dtype, indices, tokens, slots, w, l, b, s));
+  EXLR8_TIMED(EXLR8_KERNEL_FINISH, s,
+              launch_finish(b.v, 1, b.chunks.slot_row, indices, static_cast<int>(l.rows), w->down_out,
+                            w->scale_dtype, w->hidden, static_cast<int>(w->experts), x_dtype, out, s));
+  return EXLR8_OK;
+}
+
+int exlr8_joined_finish(const void* x, int x_dtype, const uint32_t* indices, const float* scores,
+                        const void* residual, int64_t tokens, const exlr8_joined_mxfp4* w, void* out,
+                        void* workspace, size_t workspace_bytes, void* stream) {
+  EXLR8_CHECK(check_joined(w));
+  if (!valid_act(x_dtype)) return EXLR8_ERR_DTYPE;
+  if (tokens < 0) return EXLR8_ERR_ROWS;
+  if (tokens == 0) return EXLR8_OK;
+  if (tokens * 9 > (int64_t(1) << 24)) return EXLR8_ERR_UNSUPPORTED;
+  if (!x || !indices || !scores || !residual || !out) return EXLR8_ERR_ARG;
+  if (!workspace || workspace_bytes < exlr8_joined_workspace(tokens, 9, w->hidden, w->intermediate, w->experts))
+    return EXLR8_ERR_WORKSPACE;
+  cudaStream_t s = as_stream(stream);
+  const JoinedLayout l = joined_layout(tokens, 9, w->experts);
+  Carver c(workspace);
+  const JoinedBuffers b = carve_joined(l, w->hidden, w->intermediate, w->experts, c);
+  EXLR8_CHECK(joined_products(x, x_dtype, indices, tokens, 9, w, l, b, s));
+  EXLR8_TIMED(EXLR8_KERNEL_FINISH, s,
+              launch_finish_fused(b.v, 1, b.chunks.slot_row, indices, static_cast<int>(tokens), w->down_out,
+                                  w->scale_dtype, w->hidden, static_cast<int>(w->experts), scores, residual, nullptr,
+                                  0, x_dtype, out, s));
+  return EXLR8_OK;
+}
+
+size_t exlr8_joined_moe_layer_workspace(int64_t tokens, int hidden, int intermediate, int64_t experts) {
+  if (tokens <= 0) return 0;
+  return exlr8_joined_workspace(tokens, 9, hidden, intermediate, experts) + align_up(tokens * 256 * sizeof(float)) +
+         align_up(tokens * 9 * sizeof(uint32_t)) + align_up(tokens * 8 * sizeof(float));
+}
+
+int exlr8_joined_moe_layer(const void* x, int x_dtype, const void* residual, int64_t tokens, const float* gate_weight,
+                           const float* bias, const exlr8_joined_mxfp4* w, void* out, uint32_t* indices,
+                           float* scores, void* workspace, size_t workspace_bytes, void* stream) {
+  EXLR8_CHECK(check_joined(w));
+  if (!valid_act(x_dtype)) return EXLR8_ERR_DTYPE;
+  if (w->experts < 257) return EXLR8_ERR_ID_RANGE;  // slot 8 routes to expert 256 (the shared expert)
+  if (tokens < 0) return EXLR8_ERR_ROWS;
+  if (tokens == 0) return EXLR8_OK;
+  if (tokens * 9 > (int64_t(1) << 24)) return EXLR8_ERR_UNSUPPORTED;
+  if (!x || !residual || !gate_weight || !bias || !out) return EXLR8_ERR_ARG;
+  if (!aligned16(gate_weight) || !aligned16(x)) return EXLR8_ERR_ALIGN;
+  if (!workspace ||
+      workspace_bytes < exlr8_joined_moe_layer_workspace(tokens, w->hidden, w->intermediate, w->experts))
+    return EXLR8_ERR_WORKSPACE;
+  cudaStream_t s = as_stream(stream);
+  const JoinedLayout l = joined_layout(tokens, 9, w->experts);
+  Carver c(workspace);
+  const JoinedBuffers b = carve_joined(l, w->hidden, w->intermediate, w->experts, c);
+  float* logits = c.take<float>(tokens * 256 * sizeof(float));
+  uint32_t* ids_buf = c.take<uint32_t>(tokens * 9 * sizeof(uint32_t));
+  float* scores_buf = c.take<float>(tokens * 8 * sizeof(float));
+  uint32_t* ids = indices ? indices : ids_buf;
+  float* sc = scores ? scores : scores_buf;
+  EXLR8_TIMED(EXLR8_KERNEL_ROUTER, s,
+              launch_gate_logits(x, x_dtype, static_cast<int>(tokens), w->hidden, gate_weight, logits, 256, s));
+  EXLR8_TIMED(EXLR8_KERNEL_ROUTER, s, launch_route(logits, bias, static_cast<int>(tokens), ids, sc, 2.5f, 256u, s));
+  EXLR8_CHECK(joined_products(x, x_dtype, ids, tokens, 9, w, l, b, s));
+  EXLR8_TIMED(EXLR8_KERNEL_FINISH, s,
+              launch_finish_fused(b.v, 1, b.chunks.slot_row, ids, static_cast<int>(tokens), w->down_out,
+                                  w->scale_dtype, w->hidden, static_cast<int>(w->experts), sc, residual, nullptr, 0,
+                                  x_dtype, out, s));
+  return EXLR8_OK;
+}
+
+int exlr8_joined_status(const void* workspace, int64_t tokens, int slots, int64_t experts, int32_t* header_out,
+                        void* stream) {
+  if (!workspace || !header_out || tokens <= 0 || slots <= 0) return EXLR8_ERR_ARG;
+  const JoinedLayout l = joined_layout(tokens, slots, experts);
+  Carver c(const_cast<void*>(workspace));
+  // Only the carve offsets are used; hidden/intermediate do not move the header.
+  const JoinedBuffers b = carve_joined(l, 128, 128, experts, c);
+  EXLR8_TRY(cudaMemcpyAsync(header_out, b.chunks.header, 8 * sizeof(int32_t), cudaMemcpyDeviceToHost,
+                            as_stream(stream)));
+  return cuda_status(cudaStreamSynchronize(as_stream(stream)));
+}
+
+}  // extern "C"

@@ -1,0 +1,26 @@
+// Launchers of the joined MXFP4 path (joined.cu).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "mx_gemm.cuh"
+#include "trellis_gemv.cuh"
+
+namespace exlr8 {
+
+// Segments, chunks and row maps from an expert plan over `slots` slots.
+cudaError_t launch_joined_segments(PlanView plan, int experts, int slots, MxChunks c, cudaStream_t s);
+
+// GEMM activations of the gate/up product: H(x[token] * unit) per padded row.
+cudaError_t launch_joined_prep(const void* x, int act_dtype, const void* unit, int scale_dtype, int slots_per_token,
+                               MxChunks c, int hidden, uint8_t* hi, uint8_t* lo, uint8_t* scales, cudaStream_t s);
+
+// gate/up float32 rows -> GEMM activations of the down product.
+cudaError_t launch_joined_gate_finish(const float* gu, const uint32_t* ids, MxChunks c, const void* gate_out,
+                                      const void* up_out, const void* down_in, int scale_dtype, int intermediate,
+                                      int act_dtype, uint8_t* hi, uint8_t* lo, uint8_t* scales, cudaStream_t s);
+
+cudaError_t launch_mx_prepare_scales(const uint8_t* in, int64_t rows, int kblocks, uint8_t* out, cudaStream_t s);
+
+}  // namespace exlr8

@@ -263,6 +263,7 @@ cudaError_t launch_gate_finish_frag(const float* partial, int gu_splits, const u
 
 // Split sum, Hadamard, signed output scale, cast to the activation type.
 __global__ void __launch_bounds__(128) finish_kernel(const float* __restrict__ partial, int splits,
+                                                     const int32_t* __restrict__ row_map,
                                                      const uint32_t* __restrict__ ids, int nslots,
                                                      const void* __restrict__ out_scale, int scale_dtype,
                                                      int features, int experts, int act_dtype,
@@ -272,13 +273,14 @@ __global__ void __launch_bounds__(128) finish_kernel(const float* __restrict__ p
   const int slot = blockIdx.y;
   if (block * 128 >= features) return;
   const int64_t e = ids[slot];
-  if (e >= experts) {
+  const int64_t prow = row_map ? row_map[slot] : static_cast<int64_t>(slot) * splits;
+  if (e >= experts || prow < 0) {
 #pragma unroll
     for (int j = 0; j < 4; ++j) store_act(out, act_dtype, static_cast<int64_t>(slot) * features + block * 128 + lane + 32 * j, 0.0f);
     return;
   }
   float v[4] = {0.f, 0.f, 0.f, 0.f};
-  const float* ps = partial + static_cast<int64_t>(slot) * splits * features + block * 128 + lane;
+  const float* ps = partial + prow * features + block * 128 + lane;
 #pragma unroll 4
   for (int s = 0; s < splits; ++s) {
 #pragma unroll
@@ -293,10 +295,11 @@ __global__ void __launch_bounds__(128) finish_kernel(const float* __restrict__ p
   }
 }
 
-cudaError_t launch_finish(const float* partial, int splits, const uint32_t* ids, int nslots, const void* out_scale,
-                          int scale_dtype, int features, int experts, int act_dtype, void* out, cudaStream_t s) {
+cudaError_t launch_finish(const float* partial, int splits, const int32_t* row_map, const uint32_t* ids, int nslots,
+                          const void* out_scale, int scale_dtype, int features, int experts, int act_dtype, void* out,
+                          cudaStream_t s) {
   dim3 grid((features / 128 + 3) / 4, nslots);
-  finish_kernel<<<grid, 128, 0, s>>>(partial, splits, ids, nslots, out_scale, scale_dtype, features, experts,
+  finish_kernel<<<grid, 128, 0, s>>>(partial, splits, row_map, ids, nslots, out_scale, scale_dtype, features, experts,
                                      act_dtype, out);
   return cudaGetLastError();
 }
@@ -310,6 +313,7 @@ cudaError_t launch_finish(const float* partial, int splits, const uint32_t* ids,
 // not read.  shared_values are the dense shared expert's float32 split
 // partials, summed and cast here.
 __global__ void __launch_bounds__(288) finish_fused_kernel(const float* __restrict__ partial, int splits,
+                                                           const int32_t* __restrict__ row_map,
                                                            const uint32_t* __restrict__ ids, int tokens,
                                                            const void* __restrict__ out_scale, int scale_dtype,
                                                            int features, int experts,
@@ -335,10 +339,11 @@ __global__ void __launch_bounds__(288) finish_fused_kernel(const float* __restri
     for (int j = 0; j < 4; ++j) products[8][lane + 32 * j] = round_to(act_dtype, a[j]);
   } else {
     const int64_t e = ids[row];
-    const bool ok = e < experts;  // an out-of-range id contributes zero
+    const int64_t prow = row_map ? row_map[row] : static_cast<int64_t>(row) * splits;
+    const bool ok = e < experts && prow >= 0;  // an out-of-range id contributes zero
     float v[4] = {0.f, 0.f, 0.f, 0.f};
     if (ok) {
-      const float* ps = partial + static_cast<int64_t>(row) * splits * features + block * 128 + lane;
+      const float* ps = partial + prow * features + block * 128 + lane;
 #pragma unroll 4
       for (int s = 0; s < splits; ++s) {
 #pragma unroll
@@ -369,12 +374,12 @@ __global__ void __launch_bounds__(288) finish_fused_kernel(const float* __restri
   }
 }
 
-cudaError_t launch_finish_fused(const float* partial, int splits, const uint32_t* ids, int tokens,
+cudaError_t launch_finish_fused(const float* partial, int splits, const int32_t* row_map, const uint32_t* ids, int tokens,
                                 const void* out_scale, int scale_dtype, int features, int experts,
                                 const float* scores, const void* residual, const void* shared_values,
                                 int shared_splits, int act_dtype, void* out, cudaStream_t s) {
   dim3 grid(features / 128, tokens);
-  finish_fused_kernel<<<grid, 288, 0, s>>>(partial, splits, ids, tokens, out_scale, scale_dtype, features, experts,
+  finish_fused_kernel<<<grid, 288, 0, s>>>(partial, splits, row_map, ids, tokens, out_scale, scale_dtype, features, experts,
                                            scores, residual, shared_values, shared_splits, act_dtype, out);
   return cudaGetLastError();
 }

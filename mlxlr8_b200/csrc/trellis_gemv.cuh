@@ -33,9 +33,13 @@ PlanView plan_view(void* base, int rows, int experts);
 // Rows i with i % period == skip_slot are left out (skip_slot < 0: none).
 cudaError_t launch_plan(const uint32_t* ids, int rows, int experts, int period, int skip_slot, PlanView plan,
                         cudaStream_t s);
-cudaError_t launch_finish(const float* partial, int splits, const uint32_t* ids, int nslots, const void* out_scale,
-                          int scale_dtype, int features, int experts, int act_dtype, void* out, cudaStream_t s);
-cudaError_t launch_finish_fused(const float* partial, int splits, const uint32_t* ids, int tokens,
+// row_map (nullable): slot -> row of `partial` holding that slot's single
+// (unsplit) product; a negative row contributes zero.  Without it slot r
+// reads rows r * splits .. r * splits + splits - 1.
+cudaError_t launch_finish(const float* partial, int splits, const int32_t* row_map, const uint32_t* ids, int nslots,
+                          const void* out_scale, int scale_dtype, int features, int experts, int act_dtype, void* out,
+                          cudaStream_t s);
+cudaError_t launch_finish_fused(const float* partial, int splits, const int32_t* row_map, const uint32_t* ids, int tokens,
                                 const void* out_scale, int scale_dtype, int features, int experts,
                                 const float* scores, const void* residual, const void* shared_values,
                                 int shared_splits, int act_dtype, void* out, cudaStream_t s);

@@ -113,3 +113,106 @@ def host_copy(layer: SyntheticLayer, experts=None):
         "gate_weight": layer.gate_weight.cpu().numpy(),
         "bias": layer.bias.cpu().numpy(),
     }
+
+
+# ---------------------------------------------------------------------------
+# Joined MXFP4 layer (the prefill configuration).  Codes and E8M0 scales are
+# drawn directly from the seed (the reference derives them from trellis
+# experts with MLX quantize, which has no published rounding to restate):
+#
+#   gate_up codes  uniform uint32 (8 E2M1 values each)  seed + 50
+#   down codes     uniform uint32                        seed + 51
+#   E8M0 scales    uniform in [scale_lo, scale_hi]       seed + 52, 53
+#   unit           +-1 fp16                              seed + 54
+#   channel scales fp16 +-|N(1, 0.1)|                    seed + 55 .. 58
+#   router         as make_layer                         seed + 3, 4
+# ---------------------------------------------------------------------------
+
+@dataclass
+class SyntheticJoined:
+    unit: torch.Tensor
+    weights: dict
+    scales: dict
+    hidden: int
+    intermediate: int
+    gate_weight: torch.Tensor
+    bias: torch.Tensor
+    seed: int
+
+    @property
+    def experts(self) -> int:
+        return self.weights["gate_up"][0].shape[0]
+
+    def tokens(self, count: int, seed_offset: int = 0, dtype=torch.bfloat16):
+        device = self.unit.device
+        h = self.hidden
+        x = torch.randn(count, h, generator=_gen(self.seed + 1 + 1000 * seed_offset, device), device=device)
+        r = torch.randn(count, h, generator=_gen(self.seed + 2 + 1000 * seed_offset, device), device=device)
+        return x.to(dtype), r.to(dtype)
+
+
+def make_joined(seed: int = 0, hidden: int = 6144, intermediate: int = 2048, experts: int = 257, device="cuda",
+                scale_lo: int = 118, scale_hi: int = 127, scale_sigma: float = 0.1) -> SyntheticJoined:
+    """MXFP4 joined experts: ``experts`` matrices (expert 256 = shared when
+    experts == 257), gate/up concatenated [E, 2m, h/8] and down [E, h, m/8]."""
+    device = torch.device(device)
+    h, m = hidden, intermediate
+
+    def codes(shape, s):
+        raw = torch.randint(-(2 ** 31), 2 ** 31 - 1, shape, dtype=torch.int64, generator=_gen(s, device),
+                            device=device)
+        return raw.to(torch.int32)  # the bits of uint32 words
+
+    def e8m0(shape, s):
+        return torch.randint(scale_lo, scale_hi + 1, shape, dtype=torch.uint8, generator=_gen(s, device),
+                             device=device)
+
+    def mag(rows, cols, s):
+        return (1.0 + scale_sigma * torch.randn(rows, cols, generator=_gen(s, device), device=device)).abs()
+
+    def signs(rows, cols, s):
+        return torch.where(torch.rand(rows, cols, generator=_gen(s, device), device=device) < 0.5, -1.0, 1.0)
+
+    weights = {
+        "gate_up": (codes((experts, 2 * m, h // 8), seed + 50), e8m0((experts, 2 * m, h // 32), seed + 52), None),
+        "down": (codes((experts, h, m // 8), seed + 51), e8m0((experts, h, m // 32), seed + 53), None),
+    }
+    unit = signs(1, h, seed + 54).reshape(h).to(torch.float16)
+    scales = {
+        "gate": (None, (mag(experts, m, seed + 55) * signs(experts, m, seed + 60)).to(torch.float16)),
+        "up": (None, (mag(experts, m, seed + 56) * signs(experts, m, seed + 61)).to(torch.float16)),
+        "down": ((mag(experts, m, seed + 57) * signs(experts, m, seed + 62)).to(torch.float16),
+                 (mag(experts, h, seed + 58) * signs(experts, h, seed + 63)).to(torch.float16)),
+    }
+    gate_weight = 0.02 * torch.randn(256, h, generator=_gen(seed + 3, device), device=device)
+    bias = 0.01 * torch.randn(256, generator=_gen(seed + 4, device), device=device)
+    return SyntheticJoined(unit, weights, scales, h, m, gate_weight.float(), bias.float(), seed)
+
+
+def joined_host_copy(j: SyntheticJoined, experts=None):
+    """NumPy copies of a joined layer for the oracle (codes of the listed
+    experts only; the others are zero)."""
+    import numpy as np
+
+    count = j.experts
+    keep = range(count) if experts is None else sorted(set(int(i) for i in experts))
+
+    def take(t):
+        out = np.zeros(tuple(t.shape), dtype=np.uint32 if t.element_size() == 4 else np.uint8)
+        for i in keep:
+            out[i] = t[i].cpu().numpy().view(out.dtype)
+        return out
+
+
+    return {
+        "unit": j.unit.float().cpu().numpy(),
+        "gate_up": (take(j.weights["gate_up"][0]), take(j.weights["gate_up"][1])),
+        "down": (take(j.weights["down"][0]), take(j.weights["down"][1])),
+        "scales": {
+            "gate": j.scales["gate"][1].float().cpu().numpy(),
+            "up": j.scales["up"][1].float().cpu().numpy(),
+            "down": (j.scales["down"][0].float().cpu().numpy(), j.scales["down"][1].float().cpu().numpy()),
+        },
+        "gate_weight": j.gate_weight.cpu().numpy(),
+        "bias": j.bias.cpu().numpy(),
+    }

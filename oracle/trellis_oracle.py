@@ -487,11 +487,14 @@ def joined_slots(x, indices, unit, gate_up, down, scales, hidden, intermediate, 
     slots = indices.shape[-1]
     xh = hadamard128(tokens * np.asarray(unit, F32)[None, :])
     rows = xh[np.arange(ids.size) // slots]
-    out = np.empty((ids.size, hidden), F32)
+    out = np.zeros((ids.size, hidden), F32)  # ids outside [0, experts) stay zero
     d_in, d_out = (np.asarray(s, F32) for s in scales["down"])
     g_out = np.asarray(scales["gate"], F32)
     u_out = np.asarray(scales["up"], F32)
+    experts = np.asarray(gate_up[0]).shape[0]
     for e in np.unique(ids):
+        if e < 0 or e >= experts:
+            continue
         sel = np.nonzero(ids == e)[0]
         wgu = mxfp4_dequantize(gate_up[0][e:e + 1], gate_up[1][e:e + 1])[0]
         wd = mxfp4_dequantize(down[0][e:e + 1], down[1][e:e + 1])[0]
