@@ -63,9 +63,13 @@ def parse():
     p.add_argument("--impl", choices=("b200", "reference"), default="b200")
     p.add_argument("--cpu-seconds", type=float, default=10.0)
     p.add_argument("--no-cpu-baseline", action="store_true")
-    p.add_argument("--ncu-driver", choices=("layer", "mlp"), default=None,
+    p.add_argument("--ncu-driver", choices=("layer", "mlp", "joined"), default=None,
                    help="untimed run for an ncu capture: 'layer' calls one resident layer --calls times; 'mlp' "
-                        "runs the nine-expert fast_expert_mlp at full size (about 170 MB of weights)")
+                        "runs the nine-expert fast_expert_mlp at full size (about 170 MB of weights); 'joined' "
+                        "runs JoinedMXFP4.finish at full width over --experts experts (the last one shared) with "
+                        "--tokens tokens, top-8 uniform routing (about 4 GB on the device at 129 experts and 2048 "
+                        "tokens)")
+    p.add_argument("--experts", type=int, default=129)
     p.add_argument("--calls", type=int, default=5)
     return p.parse_args()
 
@@ -79,7 +83,22 @@ def ncu_driver(args):
     from mlxlr8_b200.synthetic import make_layer
 
     torch.cuda.set_device(0)
-    if args.ncu_driver == "layer":
+    if args.ncu_driver == "joined":
+        from mlxlr8_b200.joined_mxfp4 import JoinedMXFP4
+        from mlxlr8_b200.synthetic import make_joined
+
+        j = make_joined(seed=1, experts=args.experts)
+        joined = JoinedMXFP4(j.unit, j.weights, j.scales, j.hidden, j.intermediate)
+        t = args.tokens
+        g = torch.Generator(device="cuda")
+        g.manual_seed(1)
+        routed = torch.rand(t, args.experts - 1, generator=g, device="cuda").argsort(dim=1)[:, :8].int()
+        ids = torch.cat([routed, torch.full((t, 1), args.experts - 1, dtype=torch.int32, device="cuda")], dim=1)
+        scores = torch.rand(t, 8, generator=g, device="cuda")
+        x, r = j.tokens(t)
+        for _ in range(args.calls):
+            joined.finish(x, ids, scores, r)
+    elif args.ncu_driver == "layer":
         layer = make_layer(seed=1)
         moe = MoELayer(layer.gate_weight, layer.bias, layer.experts)
         x, r = layer.tokens(args.tokens)

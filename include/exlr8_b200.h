@@ -267,7 +267,8 @@ int exlr8_mxfp4_prepare_scales(const uint8_t* scales, int64_t rows, int in_featu
 
 /* JoinedMXFP4.slots(x, ids) (joined_mxfp4.py:147-150): x [tokens][hidden],
  * indices uint32 [tokens][slots] -> out [tokens][slots][hidden] in x's dtype,
- * each slot T(H(v) * down_out[e]).  Ids outside [0, experts) give zeros. */
+ * each slot T(H(v) * down_out[e]).  Ids outside [0, experts) give zeros.
+ * slots <= 32. */
 size_t exlr8_joined_workspace(int64_t tokens, int slots, int hidden, int intermediate, int64_t experts);
 int exlr8_joined_slots(const void* x, int x_dtype, const uint32_t* indices, int64_t tokens, int slots,
                        const exlr8_joined_mxfp4* weights, void* out, void* workspace, size_t workspace_bytes,
@@ -288,6 +289,16 @@ size_t exlr8_joined_moe_layer_workspace(int64_t tokens, int hidden, int intermed
 int exlr8_joined_moe_layer(const void* x, int x_dtype, const void* residual, int64_t tokens, const float* gate_weight,
                            const float* bias, const exlr8_joined_mxfp4* weights, void* out, uint32_t* indices,
                            float* scores, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Router gate product on the tensor cores for prefill batches:
+ * logits [tokens][256] float32 = x . gate_weight^T (model.py:366-371), as
+ * bf16 piece products that sum to the float32 product (the weight split into
+ * three bf16 pieces; float16 / float32 x into two / three).  hidden % 64 == 0;
+ * x, gate_weight and logits 16-byte aligned.  exlr8_joined_moe_layer uses it
+ * from 64 tokens up. */
+size_t exlr8_router_logits_workspace(int64_t tokens, int hidden, int x_dtype);
+int exlr8_router_logits(const void* x, int x_dtype, int64_t tokens, int hidden, const float* gate_weight,
+                        float* logits, void* workspace, size_t workspace_bytes, void* stream);
 
 /* Dispatch header of the last joined call that used `workspace` (sizes as
  * given to that call): [0] chunks, [1] padded rows, [2..3] GEMM unit counters,

@@ -104,6 +104,9 @@ _SIGNATURES = {
                                        POINTER(JoinedMXFP4Weights), c_void_p, c_void_p, c_void_p, c_void_p, c_size_t,
                                        c_void_p]),
     "exlr8_joined_status": (c_int, [c_void_p, c_int64, c_int, c_int64, c_void_p, c_void_p]),
+    "exlr8_router_logits_workspace": (c_size_t, [c_int64, c_int, c_int]),
+    "exlr8_router_logits": (c_int, [c_void_p, c_int, c_int64, c_int, c_void_p, c_void_p, c_void_p, c_size_t,
+                                    c_void_p]),
 }
 
 EXPORTED = tuple(_SIGNATURES)

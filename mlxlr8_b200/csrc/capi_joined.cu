@@ -12,6 +12,7 @@
 #include "joined.cuh"
 #include "mx_gemm.cuh"
 #include "router.cuh"
+#include "router_gemm.cuh"
 #include "trellis_gemv.cuh"
 
 using namespace exlr8;
@@ -87,8 +88,8 @@ int joined_products(const void* x, int x_dtype, const uint32_t* ids, int64_t tok
               launch_plan(ids, static_cast<int>(l.rows), experts, slots, -1, b.plan, s));
   EXLR8_TIMED(EXLR8_KERNEL_PLAN, s, launch_joined_segments(b.plan, experts, static_cast<int>(l.rows), b.chunks, s));
   EXLR8_TIMED(EXLR8_KERNEL_PREP, s,
-              launch_joined_prep(x, x_dtype, w->unit, w->scale_dtype, slots, b.chunks, h, b.x_hi, b.x_lo,
-                                 b.x_scales, s));
+              launch_joined_prep(x, x_dtype, w->unit, w->scale_dtype, slots, static_cast<int>(tokens), b.chunks, h,
+                                 b.x_hi, b.x_lo, b.x_scales, s));
   MxGemmArgs g;
   g.weights = w->gate_up;
   g.weight_scales = static_cast<const uint8_t*>(w->gate_up_scales);
@@ -105,8 +106,8 @@ int joined_products(const void* x, int x_dtype, const uint32_t* ids, int64_t tok
   g.out = b.gu;
   EXLR8_TIMED(EXLR8_KERNEL_GATE_UP, s, launch_mx_gemm(g, s));
   EXLR8_TIMED(EXLR8_KERNEL_GATE_FINISH, s,
-              launch_joined_gate_finish(b.gu, ids, b.chunks, w->gate_out, w->up_out, w->down_in, w->scale_dtype, m,
-                                        x_dtype, b.h_hi, b.h_lo, b.h_scales, s));
+              launch_joined_gate_finish(b.gu, ids, static_cast<int>(l.rows), b.chunks, w->gate_out, w->up_out,
+                                        w->down_in, w->scale_dtype, m, x_dtype, b.h_hi, b.h_lo, b.h_scales, s));
   g.weights = w->down;
   g.weight_scales = static_cast<const uint8_t*>(w->down_scales);
   g.x_hi = b.h_hi;
@@ -151,7 +152,7 @@ int exlr8_joined_slots(const void* x, int x_dtype, const uint32_t* indices, int6
   if (!valid_act(x_dtype)) return EXLR8_ERR_DTYPE;
   if (tokens < 0 || slots <= 0) return EXLR8_ERR_ROWS;
   if (tokens == 0) return EXLR8_OK;
-  if (tokens * slots > (int64_t(1) << 24)) return EXLR8_ERR_UNSUPPORTED;
+  if (slots > 32 || tokens * slots > (int64_t(1) << 24)) return EXLR8_ERR_UNSUPPORTED;
   if (!x || !indices || !out) return EXLR8_ERR_ARG;
   if (!workspace || workspace_bytes < exlr8_joined_workspace(tokens, slots, w->hidden, w->intermediate, w->experts))
     return EXLR8_ERR_WORKSPACE;
@@ -183,16 +184,17 @@ int exlr8_joined_finish(const void* x, int x_dtype, const uint32_t* indices, con
   const JoinedBuffers b = carve_joined(l, w->hidden, w->intermediate, w->experts, c);
   EXLR8_CHECK(joined_products(x, x_dtype, indices, tokens, 9, w, l, b, s));
   EXLR8_TIMED(EXLR8_KERNEL_FINISH, s,
-              launch_finish_fused(b.v, 1, b.chunks.slot_row, indices, static_cast<int>(tokens), w->down_out,
-                                  w->scale_dtype, w->hidden, static_cast<int>(w->experts), scores, residual, nullptr,
-                                  0, x_dtype, out, s));
+              launch_joined_finish(b.v, b.chunks.slot_row, indices, static_cast<int>(tokens), w->hidden,
+                                   static_cast<int>(w->experts), w->down_out, w->scale_dtype, scores, residual, x_dtype,
+                                   out, s));
   return EXLR8_OK;
 }
 
 size_t exlr8_joined_moe_layer_workspace(int64_t tokens, int hidden, int intermediate, int64_t experts) {
   if (tokens <= 0) return 0;
   return exlr8_joined_workspace(tokens, 9, hidden, intermediate, experts) + align_up(tokens * 256 * sizeof(float)) +
-         align_up(tokens * 9 * sizeof(uint32_t)) + align_up(tokens * 8 * sizeof(float));
+         align_up(tokens * 9 * sizeof(uint32_t)) + align_up(tokens * 8 * sizeof(float)) +
+         align_up(router_gemm_workspace(static_cast<int>(tokens), hidden, EXLR8_DTYPE_F32));
 }
 
 int exlr8_joined_moe_layer(const void* x, int x_dtype, const void* residual, int64_t tokens, const float* gate_weight,
@@ -216,17 +218,43 @@ int exlr8_joined_moe_layer(const void* x, int x_dtype, const void* residual, int
   float* logits = c.take<float>(tokens * 256 * sizeof(float));
   uint32_t* ids_buf = c.take<uint32_t>(tokens * 9 * sizeof(uint32_t));
   float* scores_buf = c.take<float>(tokens * 8 * sizeof(float));
+  void* router_ws = c.take<char>(router_gemm_workspace(static_cast<int>(tokens), w->hidden, EXLR8_DTYPE_F32));
   uint32_t* ids = indices ? indices : ids_buf;
   float* sc = scores ? scores : scores_buf;
-  EXLR8_TIMED(EXLR8_KERNEL_ROUTER, s,
-              launch_gate_logits(x, x_dtype, static_cast<int>(tokens), w->hidden, gate_weight, logits, 256, s));
+  if (tokens >= kRouterGemmMinTokens) {
+    EXLR8_TIMED(EXLR8_KERNEL_ROUTER, s,
+                launch_router_gemm(x, x_dtype, static_cast<int>(tokens), w->hidden, gate_weight, logits, router_ws,
+                                   s));
+  } else {
+    EXLR8_TIMED(EXLR8_KERNEL_ROUTER, s,
+                launch_gate_logits(x, x_dtype, static_cast<int>(tokens), w->hidden, gate_weight, logits, 256, s));
+  }
   EXLR8_TIMED(EXLR8_KERNEL_ROUTER, s, launch_route(logits, bias, static_cast<int>(tokens), ids, sc, 2.5f, 256u, s));
   EXLR8_CHECK(joined_products(x, x_dtype, ids, tokens, 9, w, l, b, s));
   EXLR8_TIMED(EXLR8_KERNEL_FINISH, s,
-              launch_finish_fused(b.v, 1, b.chunks.slot_row, ids, static_cast<int>(tokens), w->down_out,
-                                  w->scale_dtype, w->hidden, static_cast<int>(w->experts), sc, residual, nullptr, 0,
-                                  x_dtype, out, s));
+              launch_joined_finish(b.v, b.chunks.slot_row, ids, static_cast<int>(tokens), w->hidden,
+                                   static_cast<int>(w->experts), w->down_out, w->scale_dtype, sc, residual, x_dtype,
+                                   out, s));
   return EXLR8_OK;
+}
+
+size_t exlr8_router_logits_workspace(int64_t tokens, int hidden, int x_dtype) {
+  if (tokens <= 0 || hidden <= 0) return 0;
+  return router_gemm_workspace(static_cast<int>(tokens), hidden, x_dtype);
+}
+
+int exlr8_router_logits(const void* x, int x_dtype, int64_t tokens, int hidden, const float* gate_weight,
+                        float* logits, void* workspace, size_t workspace_bytes, void* stream) {
+  if (!valid_act(x_dtype)) return EXLR8_ERR_DTYPE;
+  if (tokens < 0 || hidden <= 0 || hidden % 64) return EXLR8_ERR_ARG;
+  if (tokens == 0) return EXLR8_OK;
+  if (tokens > (int64_t(1) << 24)) return EXLR8_ERR_UNSUPPORTED;
+  if (!x || !gate_weight || !logits) return EXLR8_ERR_ARG;
+  if (!aligned16(x) || !aligned16(gate_weight) || !aligned16(logits)) return EXLR8_ERR_ALIGN;
+  if (!workspace || workspace_bytes < router_gemm_workspace(static_cast<int>(tokens), hidden, x_dtype))
+    return EXLR8_ERR_WORKSPACE;
+  return cuda_status(launch_router_gemm(x, x_dtype, static_cast<int>(tokens), hidden, gate_weight, logits, workspace,
+                                        as_stream(stream)));
 }
 
 int exlr8_joined_status(const void* workspace, int64_t tokens, int slots, int64_t experts, int32_t* header_out,

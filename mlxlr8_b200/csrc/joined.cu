@@ -21,6 +21,8 @@
 
 #include <cuda_fp8.h>
 
+#include <type_traits>
+
 #include "common.cuh"
 #include "joined.cuh"
 #include "mx_gemm.cuh"
@@ -29,12 +31,6 @@
 namespace exlr8 {
 
 namespace {
-
-__device__ __forceinline__ float warp_max(float v) {
-#pragma unroll
-  for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-  return v;
-}
 
 // E8M0 code of the smallest power of two s with amax / s <= 448.
 __device__ __forceinline__ int e8m0_code(float amax) {
@@ -53,31 +49,51 @@ __device__ __forceinline__ float e8m0_inverse(int code) {
   return code <= 253 ? __uint_as_float(static_cast<uint32_t>(254 - code) << 23) : __uint_as_float(0x00400000u);
 }
 
-__device__ __forceinline__ uint8_t to_e4m3(float v) {
-  return static_cast<uint8_t>(__nv_cvt_float_to_fp8(v, __NV_SATFINITE, __NV_E4M3));
-}
-
-__device__ __forceinline__ float from_e4m3(uint8_t b) {
-  const __half_raw h = __nv_cvt_fp8_to_halfraw(static_cast<__nv_fp8_storage_t>(b), __NV_E4M3);
-  return __half2float(__half(h));
-}
-
 // Quantise one 128-value block held in Hadamard layout (value lane + 32 j in
-// v[j]) into row `row` of the hi/lo planes and the block-layout scales.
-__device__ __forceinline__ void quantize_block(const float (&v)[4], int64_t row, int block, int features,
-                                               uint8_t* __restrict__ hi, uint8_t* __restrict__ lo,
-                                               uint8_t* __restrict__ scales, int lane) {
-  const int64_t base = row * features + block * 128 + lane;
+// v[j]) for the hi/lo planes and the block-layout scales.  A warp-private
+// shared buffer (128 floats) turns the block around so that lane
+// l holds values 4l .. 4l+3: a 32-value scale block is then 8 lanes (three
+// shuffles for its maximum) and each plane is one 128-byte warp store.
+struct QuantWords {
+  uint32_t hi, lo;  // four E4M3 bytes of values 4l .. 4l+3
+  int code;         // E8M0 scale of the lane's 32-value block
+};
+
+__device__ __forceinline__ QuantWords quantize_words(const float (&v)[4], float* __restrict__ tbuf, int lane) {
 #pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const int code = e8m0_code(warp_max(fabsf(v[j])));
-    const float scaled = v[j] * e8m0_inverse(code);
-    const uint8_t h = to_e4m3(scaled);
-    const uint8_t l = to_e4m3(scaled - from_e4m3(h));
-    hi[base + 32 * j] = h;
-    lo[base + 32 * j] = l;
-    if (lane == j) scales[mx_scale_offset(row, 4 * block + j, features / 32)] = static_cast<uint8_t>(code);
-  }
+  for (int j = 0; j < 4; ++j) tbuf[lane + 32 * j] = v[j];
+  __syncwarp();
+  const float4 q = reinterpret_cast<const float4*>(tbuf)[lane];
+  __syncwarp();
+  float amax = fmaxf(fmaxf(fabsf(q.x), fabsf(q.y)), fmaxf(fabsf(q.z), fabsf(q.w)));
+  amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+  amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+  amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 4));
+  const int code = e8m0_code(amax);
+  const float inv = e8m0_inverse(code);
+  const float2 s01 = make_float2(q.x * inv, q.y * inv), s23 = make_float2(q.z * inv, q.w * inv);
+  const __nv_fp8x2_storage_t h01 = __nv_cvt_float2_to_fp8x2(s01, __NV_SATFINITE, __NV_E4M3);
+  const __nv_fp8x2_storage_t h23 = __nv_cvt_float2_to_fp8x2(s23, __NV_SATFINITE, __NV_E4M3);
+  const float2 b01 = __half22float2(__half2(__nv_cvt_fp8x2_to_halfraw2(h01, __NV_E4M3)));
+  const float2 b23 = __half22float2(__half2(__nv_cvt_fp8x2_to_halfraw2(h23, __NV_E4M3)));
+  const __nv_fp8x2_storage_t l01 =
+      __nv_cvt_float2_to_fp8x2(make_float2(s01.x - b01.x, s01.y - b01.y), __NV_SATFINITE, __NV_E4M3);
+  const __nv_fp8x2_storage_t l23 =
+      __nv_cvt_float2_to_fp8x2(make_float2(s23.x - b23.x, s23.y - b23.y), __NV_SATFINITE, __NV_E4M3);
+  QuantWords w;
+  w.hi = static_cast<uint32_t>(h01) | (static_cast<uint32_t>(h23) << 16);
+  w.lo = static_cast<uint32_t>(l01) | (static_cast<uint32_t>(l23) << 16);
+  w.code = code;
+  return w;
+}
+
+__device__ __forceinline__ void store_words(const QuantWords& w, int64_t row, int block, int features,
+                                            uint8_t* __restrict__ hi, uint8_t* __restrict__ lo,
+                                            uint8_t* __restrict__ scales, int lane) {
+  const int64_t base = row * features + block * 128 + 4 * lane;
+  *reinterpret_cast<uint32_t*>(hi + base) = w.hi;
+  *reinterpret_cast<uint32_t*>(lo + base) = w.lo;
+  if ((lane & 7) == 0) scales[mx_scale_offset(row, 4 * block + (lane >> 3), features / 32)] = static_cast<uint8_t>(w.code);
 }
 
 }  // namespace
@@ -85,7 +101,7 @@ __device__ __forceinline__ void quantize_block(const float (&v)[4], int64_t row,
 // ---------------------------------------------------------------------------
 // Segments: one CTA.  Expert e's sorted rows start at padded_start[e] (a
 // multiple of kMxRowAlign); an expert with at most kMxMaxN rows is one chunk,
-// a larger one is cut into 128-row chunks and a last chunk of 113..240 rows.
+// a larger one is cut into 128-row chunks and a last chunk of 33..160 rows.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ int chunk_count(int rows) {
   if (rows <= 0) return 0;
@@ -155,74 +171,132 @@ __global__ void __launch_bounds__(256) joined_rowmap_kernel(PlanView plan, MxChu
   }
 }
 
-// xh = H(x[token] * unit) for every padded row (zeros for padding), one warp
-// per (row, 128-block).
-__global__ void __launch_bounds__(256) joined_prep_kernel(const void* __restrict__ x, int act_dtype,
-                                                          const void* __restrict__ unit, int scale_dtype,
-                                                          int slots_per_token, MxChunks c, int hidden,
-                                                          uint8_t* __restrict__ hi, uint8_t* __restrict__ lo,
-                                                          uint8_t* __restrict__ scales) {
-  const int lane = threadIdx.x & 31;
+constexpr int kRowWarps = 8;  // warps per CTA of the row kernels
+
+// xh = H(x[token] * unit), quantised once per token and stored into the
+// padded row of each of the token's slots.  Padding rows are left as they
+// are: they only feed MMA columns whose results are never stored.
+template <int kAct, int kScale>
+__global__ void __launch_bounds__(kRowWarps * 32) joined_prep_kernel(const void* __restrict__ x,
+                                                                     const void* __restrict__ unit,
+                                                                     int slots_per_token, int tokens, MxChunks c,
+                                                                     int hidden, uint8_t* __restrict__ hi,
+                                                                     uint8_t* __restrict__ lo,
+                                                                     uint8_t* __restrict__ scales) {
+  __shared__ __align__(16) float tbuf[kRowWarps][128];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int blocks = hidden / 128;
-  const int64_t items = static_cast<int64_t>(c.header[1]) * blocks;
-  const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
-  for (int64_t item = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); item < items;
-       item += warps) {
-    const int64_t row = item / blocks;
-    const int block = static_cast<int>(item % blocks);
-    const int slot = c.row_slot[row];
-    float v[4] = {0.f, 0.f, 0.f, 0.f};
-    if (slot >= 0) {
-      const int64_t token = slot / slots_per_token;
+  for (int token = blockIdx.x * kRowWarps + warp; token < tokens; token += gridDim.x * kRowWarps) {
+    const int my_row = lane < slots_per_token ? c.slot_row[static_cast<int64_t>(token) * slots_per_token + lane] : -1;
+    const int64_t xrow = static_cast<int64_t>(token) * hidden;
+    for (int block = 0; block < blocks; ++block) {
+      float v[4];
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const int col = block * 128 + lane + 32 * j;
-        v[j] = __fmul_rn(load_act(x, act_dtype, token * hidden + col), load_scale(unit, scale_dtype, col));
+        v[j] = __fmul_rn(load_act(x, kAct, xrow + col), load_scale(unit, kScale, col));
       }
       hadamard128(v, lane);
+      const QuantWords w = quantize_words(v, tbuf[warp], lane);
+      for (int r = 0; r < slots_per_token; ++r) {
+        const int row = __shfl_sync(0xffffffffu, my_row, r);
+        if (row >= 0) store_words(w, row, block, hidden, hi, lo, scales, lane);
+      }
     }
-    quantize_block(v, row, block, hidden, hi, lo, scales, lane);
   }
 }
 
 // metal/joined_gate_finish.metal: gate and up halves of the joined product,
 // Hadamard, out scales, typed SwiGLU, down in scale, Hadamard; quantised into
-// the down GEMM's activation planes.
-__global__ void __launch_bounds__(256) joined_gate_finish_kernel(
-    const float* __restrict__ gu, const uint32_t* __restrict__ ids, MxChunks c, const void* __restrict__ gate_out,
-    const void* __restrict__ up_out, const void* __restrict__ down_in, int scale_dtype, int intermediate, int act_dtype,
-    uint8_t* __restrict__ hi, uint8_t* __restrict__ lo, uint8_t* __restrict__ scales) {
-  const int lane = threadIdx.x & 31;
+// the down GEMM's activation planes.  One warp per padded row.
+template <int kAct, int kScale>
+__global__ void __launch_bounds__(kRowWarps * 32) joined_gate_finish_kernel(
+    const float* __restrict__ gu, const uint32_t* __restrict__ ids, int slots, MxChunks c,
+    const void* __restrict__ gate_out, const void* __restrict__ up_out, const void* __restrict__ down_in,
+    int intermediate, uint8_t* __restrict__ hi, uint8_t* __restrict__ lo, uint8_t* __restrict__ scales) {
+  __shared__ __align__(16) float tbuf[kRowWarps][128];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int blocks = intermediate / 128;
-  const int64_t items = static_cast<int64_t>(c.header[1]) * blocks;
-  const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
-  for (int64_t item = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); item < items;
-       item += warps) {
-    const int64_t row = item / blocks;
-    const int block = static_cast<int>(item % blocks);
-    const int slot = c.row_slot[row];
-    float h[4] = {0.f, 0.f, 0.f, 0.f};
-    if (slot >= 0) {
-      const int64_t e = ids[slot];
-      const float* g_row = gu + row * 2 * intermediate + block * 128 + lane;
-      float g[4], u[4];
+  for (int slot = blockIdx.x * kRowWarps + warp; slot < slots; slot += gridDim.x * kRowWarps) {
+    const int row = c.slot_row[slot];
+    if (row < 0) continue;
+    const int64_t e = ids[slot];
+    const float* g_row = gu + static_cast<int64_t>(row) * 2 * intermediate + lane;
+    for (int block = 0; block < blocks; ++block) {
+      float g[4], u[4], h[4];
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        g[j] = __ldcs(g_row + 32 * j);
-        u[j] = __ldcs(g_row + intermediate + 32 * j);
+        g[j] = __ldcs(g_row + block * 128 + 32 * j);
+        u[j] = __ldcs(g_row + intermediate + block * 128 + 32 * j);
       }
       hadamard128(g, lane);
       hadamard128(u, lane);
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const int64_t si = e * intermediate + block * 128 + lane + 32 * j;
-        const float act = swiglu_typed(act_dtype, __fmul_rn(g[j], load_scale(gate_out, scale_dtype, si)),
-                                       __fmul_rn(u[j], load_scale(up_out, scale_dtype, si)));
-        h[j] = __fmul_rn(act, load_scale(down_in, scale_dtype, si));
+        const float act = swiglu_typed(kAct, __fmul_rn(g[j], load_scale(gate_out, kScale, si)),
+                                       __fmul_rn(u[j], load_scale(up_out, kScale, si)));
+        h[j] = __fmul_rn(act, load_scale(down_in, kScale, si));
       }
       hadamard128(h, lane);
+      store_words(quantize_words(h, tbuf[warp], lane), row, block, intermediate, hi, lo, scales, lane);
     }
-    quantize_block(h, row, block, intermediate, hi, lo, scales, lane);
+  }
+}
+
+// JoinedMXFP4.finish for prefill batches: one CTA (nine warps, one per slot)
+// per token, four 128-blocks per round.  Per slot T(H(v) * down_out[e]);
+// then the routed sum in the order of metal/fast_decode_finish_fused.metal
+// (slot 0, then (slot r + 0) + total for r = 1..7), T(routed),
+// T(routed + shared) and T(residual + combined).
+constexpr int kFinishGroup = 4;
+
+template <int kAct, int kScale>
+__global__ void __launch_bounds__(288) joined_finish_kernel(const float* __restrict__ v,
+                                                            const int32_t* __restrict__ slot_row,
+                                                            const uint32_t* __restrict__ ids, int features,
+                                                            int experts, const void* __restrict__ out_scale,
+                                                            const float* __restrict__ scores,
+                                                            const void* __restrict__ residual, void* __restrict__ out) {
+  __shared__ float products[9][kFinishGroup * 128];
+  const int lane = threadIdx.x & 31, slot = threadIdx.x >> 5;
+  const int64_t token = blockIdx.x;
+  const int64_t e = ids[token * 9 + slot];
+  const int prow = slot_row[token * 9 + slot];
+  const bool ok = e < experts && prow >= 0;
+  const float score = slot < 8 ? scores[token * 8 + slot] : 1.0f;
+  const float* src = v + static_cast<int64_t>(ok ? prow : 0) * features + lane;
+  const int blocks = features / 128;
+  for (int b0 = 0; b0 < blocks; b0 += kFinishGroup) {
+    const int nb = min(kFinishGroup, blocks - b0);
+    float val[kFinishGroup][4];
+#pragma unroll
+    for (int g = 0; g < kFinishGroup; ++g)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) val[g][j] = (ok && g < nb) ? __ldcs(src + (b0 + g) * 128 + 32 * j) : 0.0f;
+#pragma unroll
+    for (int g = 0; g < kFinishGroup; ++g) {
+      if (g >= nb) break;
+      hadamard128(val[g], lane);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int col = (b0 + g) * 128 + lane + 32 * j;
+        const float value =
+            ok ? round_to(kAct, __fmul_rn(val[g][j], load_scale(out_scale, kScale, e * features + col))) : 0.0f;
+        products[slot][g * 128 + lane + 32 * j] = slot < 8 ? __fmul_rn(value, score) : value;
+      }
+    }
+    __syncthreads();
+    for (int c = threadIdx.x; c < nb * 128; c += 288) {
+      float total = __fadd_rn(products[0][c], 0.0f);
+#pragma unroll
+      for (int r = 1; r < 8; ++r) total = __fadd_rn(__fadd_rn(products[r][c], 0.0f), total);
+      const int64_t off = token * features + b0 * 128 + c;
+      const float routed = round_to(kAct, total);
+      const float combined = round_to(kAct, __fadd_rn(routed, round_to(kAct, products[8][c])));
+      store_act(out, kAct, off, __fadd_rn(load_act(residual, kAct, off), combined));
+    }
+    __syncthreads();
   }
 }
 
@@ -262,19 +336,50 @@ cudaError_t launch_joined_segments(PlanView plan, int experts, int slots, MxChun
   return cudaGetLastError();
 }
 
-cudaError_t launch_joined_prep(const void* x, int act_dtype, const void* unit, int scale_dtype, int slots_per_token,
-                               MxChunks c, int hidden, uint8_t* hi, uint8_t* lo, uint8_t* scales, cudaStream_t s) {
-  joined_prep_kernel<<<worker_grid(), 256, 0, s>>>(x, act_dtype, unit, scale_dtype, slots_per_token, c, hidden, hi,
-                                                   lo, scales);
-  return cudaGetLastError();
+template <typename F>
+static cudaError_t dispatch_types(int act_dtype, int scale_dtype, F&& f) {
+  const bool f16s = scale_dtype == kF16;
+  switch (act_dtype) {
+    case kF32: return f16s ? f(std::integral_constant<int, kF32>{}, std::integral_constant<int, kF16>{})
+                           : f(std::integral_constant<int, kF32>{}, std::integral_constant<int, kF32>{});
+    case kF16: return f16s ? f(std::integral_constant<int, kF16>{}, std::integral_constant<int, kF16>{})
+                           : f(std::integral_constant<int, kF16>{}, std::integral_constant<int, kF32>{});
+    default: return f16s ? f(std::integral_constant<int, kBF16>{}, std::integral_constant<int, kF16>{})
+                         : f(std::integral_constant<int, kBF16>{}, std::integral_constant<int, kF32>{});
+  }
 }
 
-cudaError_t launch_joined_gate_finish(const float* gu, const uint32_t* ids, MxChunks c, const void* gate_out,
-                                      const void* up_out, const void* down_in, int scale_dtype, int intermediate,
-                                      int act_dtype, uint8_t* hi, uint8_t* lo, uint8_t* scales, cudaStream_t s) {
-  joined_gate_finish_kernel<<<worker_grid(), 256, 0, s>>>(gu, ids, c, gate_out, up_out, down_in, scale_dtype,
-                                                          intermediate, act_dtype, hi, lo, scales);
-  return cudaGetLastError();
+cudaError_t launch_joined_prep(const void* x, int act_dtype, const void* unit, int scale_dtype, int slots_per_token,
+                               int tokens, MxChunks c, int hidden, uint8_t* hi, uint8_t* lo, uint8_t* scales,
+                               cudaStream_t s) {
+  return dispatch_types(act_dtype, scale_dtype, [&](auto a, auto sc) {
+    joined_prep_kernel<decltype(a)::value, decltype(sc)::value>
+        <<<worker_grid(), kRowWarps * 32, 0, s>>>(x, unit, slots_per_token, tokens, c, hidden, hi, lo, scales);
+    return cudaGetLastError();
+  });
+}
+
+cudaError_t launch_joined_gate_finish(const float* gu, const uint32_t* ids, int slots, MxChunks c,
+                                      const void* gate_out, const void* up_out, const void* down_in, int scale_dtype,
+                                      int intermediate, int act_dtype, uint8_t* hi, uint8_t* lo, uint8_t* scales,
+                                      cudaStream_t s) {
+  return dispatch_types(act_dtype, scale_dtype, [&](auto a, auto sc) {
+    joined_gate_finish_kernel<decltype(a)::value, decltype(sc)::value>
+        <<<worker_grid(), kRowWarps * 32, 0, s>>>(gu, ids, slots, c, gate_out, up_out, down_in, intermediate, hi,
+                                                  lo, scales);
+    return cudaGetLastError();
+  });
+}
+
+cudaError_t launch_joined_finish(const float* v, const int32_t* slot_row, const uint32_t* ids, int tokens,
+                                 int features, int experts, const void* out_scale, int scale_dtype,
+                                 const float* scores, const void* residual, int act_dtype, void* out, cudaStream_t s) {
+  if (tokens == 0) return cudaSuccess;
+  return dispatch_types(act_dtype, scale_dtype, [&](auto a, auto sc) {
+    joined_finish_kernel<decltype(a)::value, decltype(sc)::value><<<tokens, 288, 0, s>>>(
+        v, slot_row, ids, features, experts, out_scale, scores, residual, out);
+    return cudaGetLastError();
+  });
 }
 
 cudaError_t launch_mx_prepare_scales(const uint8_t* in, int64_t rows, int kblocks, uint8_t* out, cudaStream_t s) {

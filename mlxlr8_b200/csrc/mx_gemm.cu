@@ -31,7 +31,7 @@ namespace exlr8 {
 
 namespace {
 
-constexpr int kStages = 2;
+constexpr int kStages = 3;
 constexpr int kSchedSlots = 4;
 constexpr uint32_t kTileA = 128 * 128;                       // one weight tile image (E2M1 with gaps)
 constexpr uint32_t kTileB = kMxMaxN * 128;                   // one activation plane tile

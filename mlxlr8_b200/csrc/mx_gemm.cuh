@@ -7,7 +7,7 @@
 
 namespace exlr8 {
 
-constexpr int kMxMaxN = 240;    // slot rows per chunk (MMA N)
+constexpr int kMxMaxN = 160;    // slot rows per chunk (MMA N)
 constexpr int kMxKTile = 128;   // K values per pipeline stage
 constexpr int kMxRowAlign = 128;  // expert segments start on this row multiple
 

@@ -49,6 +49,23 @@ def router(x: torch.Tensor, gate_weight: torch.Tensor, bias: torch.Tensor):
     return logits, ids, scores
 
 
+def router_logits(x: torch.Tensor, gate_weight: torch.Tensor) -> torch.Tensor:
+    """``x.float() @ gate_weight.T`` on the tensor cores (the prefill gate product)."""
+    device = _lib.require_cuda(x, gate_weight)
+    hidden = x.shape[-1]
+    if tuple(gate_weight.shape) != (256, hidden):
+        raise ValueError("gate weight must be [256, hidden]")
+    tokens = x.numel() // hidden
+    x = x.contiguous()
+    w = gate_weight.to(torch.float32).contiguous()
+    logits = torch.empty(tuple(x.shape[:-1]) + (256,), dtype=torch.float32, device=device)
+    ws = _lib.workspace(_lib.lib().exlr8_router_logits_workspace(tokens, hidden, _lib.act_code(x)), device)
+    _lib.check(_lib.lib().exlr8_router_logits(x.data_ptr(), _lib.act_code(x), tokens, hidden, w.data_ptr(),
+                                              logits.data_ptr(), ws.data_ptr(), ws.numel(),
+                                              _lib.stream_handle(device)))
+    return logits
+
+
 def compiled_finish(experts, gate, bias):
     """Return ``call(x, residual) -> residual + routed + shared`` for one layer.
 

@@ -46,9 +46,9 @@ def _oracle_slots(j, x, ids, dtype="bfloat16"):
 def _chunks(rows):
     if rows <= 0:
         return 0
-    if rows <= 240:
+    if rows <= 160:
         return 1
-    return (rows - 240 + 127) // 128 + 1
+    return (rows - 160 + 127) // 128 + 1
 
 
 @pytest.mark.parametrize("dtype", ["bfloat16", "float16", "float32"])
@@ -91,12 +91,13 @@ def test_finish_matches_oracle():
 
 
 def test_ragged_segments_and_chunk_boundaries():
-    """Experts with 0, 1, 127, 128, 240, 241, 300 and 520 rows: empty
-    segments, partial MMA columns, the one-chunk limit and the 128-row
-    chunking of larger segments (fast_prefill.py:19-46 ragged segments)."""
+    """Experts with 0, 1, 127, 128, 160, 161, 300 and 520 rows: empty
+    segments, partial MMA columns, the one-chunk limit (160 rows) and the
+    128-row chunking of larger segments (fast_prefill.py:19-46 ragged
+    segments)."""
     import torch
 
-    counts = [0, 1, 127, 128, 240, 241, 300, 520]
+    counts = [0, 1, 127, 128, 160, 161, 300, 520]
     j, joined = _joined(seed=5, h=256, m=128, experts=len(counts))
     ids_np = np.concatenate([np.full(c, e, dtype=np.int32) for e, c in enumerate(counts)])
     rng = np.random.default_rng(0)
@@ -182,6 +183,31 @@ def test_joined_layer_routes_and_matches_oracle():
     values = _oracle_slots(j, x, e_ids)
     expected = ref.combine(values, e_scores, host(residual), "bfloat16")
     assert_mxfp4_close(host(out) - host(residual), expected - host(residual))
+
+
+def test_joined_layer_tensor_core_router():
+    """From 64 tokens the layer's gate product runs on the tensor cores; its
+    routing equals the oracle's routing of those logits."""
+    import torch
+
+    from mlxlr8_b200.fast_router import router_logits
+    from mlxlr8_b200.joined_mxfp4 import JoinedMoELayer
+
+    j, joined = _joined(seed=10, h=256, m=128, experts=257)
+    layer = JoinedMoELayer(j.gate_weight, j.bias, joined)
+    tokens = 300
+    x, residual = j.tokens(tokens)
+    out, ids, scores = layer(x, residual, return_routing=True)
+    logits = router_logits(x, j.gate_weight)
+    torch.cuda.synchronize()
+    assert layer.dispatch_header(tokens)[4] == 0
+    e_ids, e_scores = ref.route(host(logits), j.bias.cpu().numpy())
+    np.testing.assert_array_equal(ids.cpu().numpy(), e_ids)
+    np.testing.assert_allclose(scores.cpu().numpy(), e_scores, rtol=1e-6, atol=1e-7)
+    sample = np.arange(0, tokens, 7)
+    values = _oracle_slots(j, x[sample], e_ids[sample])
+    expected = ref.combine(values, e_scores[sample], host(residual)[sample], "bfloat16")
+    assert_mxfp4_close(host(out)[sample] - host(residual)[sample], expected - host(residual)[sample])
 
 
 def test_glm_prefill_shape_sampled_tokens():

@@ -54,3 +54,27 @@ def test_gate_gemv_and_route(tokens, dtype):
     e_ids, e_scores = ref.route(logits.cpu().numpy(), b.cpu().numpy())
     np.testing.assert_array_equal(ids.cpu().numpy(), e_ids)
     np.testing.assert_allclose(scores.cpu().numpy(), e_scores, rtol=1e-6, atol=1e-7)
+
+
+@pytest.mark.parametrize("dtype", ["bfloat16", "float16", "float32"])
+@pytest.mark.parametrize("tokens", [64, 300])
+def test_tensor_core_gate_product(dtype, tokens):
+    """Prefill gate product (bf16 piece products on the tensor cores) against a
+    float64 reference: float32-level agreement, and routing from it equals
+    the oracle's routing of the same logits."""
+    import torch
+
+    from helpers import torch_dtype
+    from mlxlr8_b200.fast_router import router_logits
+
+    g = torch.Generator(device="cuda")
+    g.manual_seed(tokens)
+    x = torch.randn(tokens, 6144, generator=g, device="cuda").to(torch_dtype(dtype))
+    w = 0.02 * torch.randn(256, 6144, generator=g, device="cuda")
+    logits = router_logits(x, w)
+    torch.cuda.synchronize()
+    exact = x.double().cpu().numpy() @ w.double().cpu().numpy().T
+    got = logits.double().cpu().numpy()
+    err = np.abs(got - exact).max() / np.abs(exact).max()
+    assert err < 1e-5, err  # float32 accumulation over 6144 terms: ~sqrt(6144) * 2^-24
+    np.testing.assert_allclose(got, exact, rtol=1e-4, atol=2e-5)
