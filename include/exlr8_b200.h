@@ -227,6 +227,14 @@ int exlr8_moe_layer_noalloc(const void* x, int x_dtype, const void* residual, in
  * Synchronises `stream`. */
 int exlr8_workspace_bad_ids(const void* workspace, int64_t* bad_ids, void* stream);
 
+/* Dispatch header of the last trellis prefill call (more than 16 tokens)
+ * that used `workspace` (sizes as given to that call; slots = 9 for the
+ * finish and layer entries): [0] chunks, [1] padded rows, [2..3] GEMM unit
+ * counters, [4] GEMM error code (0 = none; non-zero = a bounded wait timed
+ * out).  Synchronises `stream`. */
+int exlr8_prefill_status(const void* workspace, int64_t tokens, int slots, int intermediate, int64_t experts,
+                         int32_t* header, void* stream);
+
 /* ---- joined MXFP4 experts (prefill) -------------------------------------- */
 
 /*

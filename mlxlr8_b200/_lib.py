@@ -104,6 +104,7 @@ _SIGNATURES = {
                                        POINTER(JoinedMXFP4Weights), c_void_p, c_void_p, c_void_p, c_void_p, c_size_t,
                                        c_void_p]),
     "exlr8_joined_status": (c_int, [c_void_p, c_int64, c_int, c_int64, c_void_p, c_void_p]),
+    "exlr8_prefill_status": (c_int, [c_void_p, c_int64, c_int, c_int, c_int64, c_void_p, c_void_p]),
     "exlr8_router_logits_workspace": (c_size_t, [c_int64, c_int, c_int]),
     "exlr8_router_logits": (c_int, [c_void_p, c_int, c_int64, c_int, c_void_p, c_void_p, c_void_p, c_size_t,
                                     c_void_p]),
@@ -197,6 +198,15 @@ def profile_read() -> dict:
         check(load().exlr8_profile_read(i, ctypes.byref(n), ctypes.byref(ms)))
         out[name] = (int(n.value), float(ms.value))
     return out
+
+
+def prefill_status(workspace_tensor: torch.Tensor, tokens: int, slots: int, intermediate: int, experts: int):
+    """[chunks, padded rows, gate/up units, down units, GEMM error] of the last
+    trellis prefill call that used ``workspace_tensor``."""
+    header = torch.zeros(8, dtype=torch.int32)
+    check(load().exlr8_prefill_status(workspace_tensor.data_ptr(), tokens, slots, intermediate, experts,
+                                      header.data_ptr(), stream_handle(workspace_tensor.device)))
+    return header.tolist()[:5]
 
 
 def workspace(nbytes: int, device: torch.device) -> torch.Tensor:

@@ -5,9 +5,13 @@
 #include <cstring>
 
 #include "capi_util.cuh"
+#include "codec.cuh"
 #include "common.cuh"
 #include "dense.cuh"
+#include "joined.cuh"
+#include "mx_gemm.cuh"
 #include "router.cuh"
+#include "router_gemm.cuh"
 #include "stream.cuh"
 #include "trellis_gemv.cuh"
 
@@ -231,6 +235,161 @@ int check_dense(const exlr8_dense_expert* sh, int x_dtype, int hidden, int inter
   return EXLR8_OK;
 }
 
+// ---- prefill: grouped trellis GEMM on the tensor cores --------------------
+//
+// The reference runs fast_expert_mlp up to 16 token rows and
+// fast_prefill.grouped_expert_mlp above (experts.py:171-174).  Above the same
+// threshold the trellis MLP runs as grouped tcgen05 GEMMs: slots sorted by
+// expert in 128-row-aligned segments; per slot H(x * in_scale[e]) for gate
+// and up as E4M3 hi/lo planes; one gate+up GEMM (two projections) whose
+// decoder warps expand the trellis codes to E4M3 tiles; the gate/up finish;
+// the down GEMM; the per-slot finish or the fused combine.
+constexpr int64_t kPrefillMinTokens = 17;
+
+struct PrefillBuffers {
+  PlanView plan;
+  int32_t* counters;
+  MxChunks chunks;
+  uint8_t *ghi, *glo, *gsc, *uhi, *ulo, *usc;
+  float* gu;
+  uint8_t *dhi, *dlo, *dsc;
+  float* v;
+  // dense bf16 shared expert on the tensor cores (split partials)
+  float *dgate, *dup, *ddown;
+  void* dh;
+  int32_t* derr;
+  int dsplits_gu, dsplits_d;
+};
+
+PrefillBuffers carve_prefill(int64_t tokens, int slots, int h, int m, int64_t experts, bool dense, Carver& c) {
+  PrefillBuffers b{};
+  const int64_t rows = tokens * slots;
+  const int64_t padded = mx_padded_rows(rows, experts);
+  const int64_t max_chunks = mx_max_chunks(rows, experts);
+  b.plan = plan_view(c.take<char>(plan_bytes(static_cast<int>(rows), static_cast<int>(experts))),
+                     static_cast<int>(rows), static_cast<int>(experts));
+  b.counters = c.take<int32_t>((m / 64 + 1) * sizeof(int32_t));
+  b.plan.zero = b.counters;
+  b.plan.zero_count = m / 64;
+  b.chunks.header = c.take<int32_t>(16 * sizeof(int32_t));
+  b.chunks.chunk_start = c.take<int32_t>(max_chunks * sizeof(int32_t));
+  b.chunks.chunk_rows = c.take<int32_t>(max_chunks * sizeof(int32_t));
+  b.chunks.chunk_expert = c.take<int32_t>(max_chunks * sizeof(int32_t));
+  b.chunks.padded_start = c.take<int32_t>((experts + 1) * sizeof(int32_t));
+  b.chunks.row_slot = c.take<int32_t>(padded * sizeof(int32_t));
+  b.chunks.slot_row = c.take<int32_t>(rows * sizeof(int32_t));
+  b.ghi = c.take<uint8_t>(padded * h);
+  b.glo = c.take<uint8_t>(padded * h);
+  b.gsc = c.take<uint8_t>(padded * h / 32);
+  b.uhi = c.take<uint8_t>(padded * h);
+  b.ulo = c.take<uint8_t>(padded * h);
+  b.usc = c.take<uint8_t>(padded * h / 32);
+  b.gu = c.take<float>(padded * 2 * m * sizeof(float));
+  b.dhi = c.take<uint8_t>(padded * m);
+  b.dlo = c.take<uint8_t>(padded * m);
+  b.dsc = c.take<uint8_t>(padded * m / 32);
+  b.v = c.take<float>(padded * h * sizeof(float));
+  if (dense) {
+    const int t = static_cast<int>(tokens);
+    b.dsplits_gu = bf16_gemm_splits(t, h, m);
+    b.dsplits_d = bf16_gemm_splits(t, m, h);
+    b.dgate = c.take<float>(static_cast<size_t>(b.dsplits_gu) * tokens * m * sizeof(float));
+    b.dup = c.take<float>(static_cast<size_t>(b.dsplits_gu) * tokens * m * sizeof(float));
+    b.dh = c.take<void>(static_cast<size_t>(tokens) * m * sizeof(uint16_t));
+    b.ddown = c.take<float>(static_cast<size_t>(b.dsplits_d) * tokens * h * sizeof(float));
+    b.derr = c.take<int32_t>(16);
+  }
+  return b;
+}
+
+size_t prefill_bytes(int64_t tokens, int slots, int h, int m, int64_t experts, bool dense) {
+  Carver c(nullptr);
+  carve_prefill(tokens, slots, h, m, experts, dense, c);
+  return c.used;
+}
+
+// Everything up to the float32 down products b.v (and the dense shared
+// expert's partials when `shared` is given).
+int prefill_products(const void* x, int x_dtype, int per_slot, int slots, const uint32_t* ids, int64_t tokens,
+                     const exlr8_trellis_experts* ex, int64_t experts, const exlr8_dense_expert* shared,
+                     const PrefillBuffers& b, cudaStream_t s) {
+  const int h = ex->hidden, m = ex->intermediate;
+  const int64_t rows = tokens * slots;
+  const int64_t padded = mx_padded_rows(rows, experts);
+  const int e = static_cast<int>(experts), n = static_cast<int>(rows);
+  EXLR8_TIMED(EXLR8_KERNEL_PLAN, s, launch_plan(ids, n, e, slots, shared ? 8 : -1, b.plan, s));
+  EXLR8_TIMED(EXLR8_KERNEL_PLAN, s, launch_joined_segments(b.plan, e, n, b.chunks, s));
+  EXLR8_TIMED(EXLR8_KERNEL_PREP, s,
+              launch_trellis_prep(x, x_dtype, per_slot, slots, n, ids, b.chunks, ex->in_scale[0], ex->in_scale[1],
+                                  ex->scale_dtype, 2, h, b.ghi, b.glo, b.gsc, b.uhi, b.ulo, b.usc, s));
+  if (shared) {
+    const int t = static_cast<int>(tokens);
+    const uint16_t* xb = static_cast<const uint16_t*>(x);
+    EXLR8_TRY(cudaMemsetAsync(b.derr, 0, sizeof(int32_t), s));
+    EXLR8_TIMED(EXLR8_KERNEL_DENSE, s,
+                launch_dense_gemm(xb, t, h, static_cast<const uint16_t*>(shared->gate), m, b.dsplits_gu, b.dgate,
+                                  b.derr, s));
+    EXLR8_TIMED(EXLR8_KERNEL_DENSE, s,
+                launch_dense_gemm(xb, t, h, static_cast<const uint16_t*>(shared->up), m, b.dsplits_gu, b.dup, b.derr,
+                                  s));
+    EXLR8_TIMED(EXLR8_KERNEL_DENSE, s,
+                launch_dense_swiglu(b.dgate, b.dup, b.dsplits_gu, tokens * m, x_dtype, b.dh, s));
+    EXLR8_TIMED(EXLR8_KERNEL_DENSE, s,
+                launch_dense_gemm(static_cast<const uint16_t*>(b.dh), t, m, static_cast<const uint16_t*>(shared->down),
+                                  h, b.dsplits_d, b.ddown, b.derr, s));
+  }
+  ExpertGemmArgs g = {};
+  g.weights[0] = ex->packed[0];
+  g.weights[1] = ex->packed[1];
+  g.x_hi[0] = b.ghi;
+  g.x_lo[0] = b.glo;
+  g.x_scales[0] = b.gsc;
+  g.x_hi[1] = b.uhi;
+  g.x_lo[1] = b.ulo;
+  g.x_scales[1] = b.usc;
+  g.chunks = b.chunks;
+  g.counter_index = 2;
+  g.experts = experts;
+  g.padded_rows = padded;
+  g.in_features = h;
+  g.out_features = m;
+  g.projections = 2;
+  g.paired = 0;
+  g.trellis_k = ex->k;
+  g.side = 1;
+  g.mcg_mask = kMcgMask;
+  g.mcg_xor = kMcgXor;
+  g.unit16 = 65536u;
+  g.out = b.gu;
+  g.out_stride = 2 * m;
+  g.proj_offset = m;
+  EXLR8_TIMED(EXLR8_KERNEL_GATE_UP, s, launch_expert_gemm(g, s));
+  EXLR8_TIMED(EXLR8_KERNEL_GATE_FINISH, s,
+              launch_joined_gate_finish(b.gu, ids, n, b.chunks, ex->out_scale[0], ex->out_scale[1], ex->in_scale[2],
+                                        ex->scale_dtype, m, x_dtype, b.dhi, b.dlo, b.dsc, s));
+  g.weights[0] = ex->packed[2];
+  g.weights[1] = nullptr;
+  g.x_hi[0] = b.dhi;
+  g.x_lo[0] = b.dlo;
+  g.x_scales[0] = b.dsc;
+  g.counter_index = 3;
+  g.in_features = m;
+  g.out_features = h;
+  g.projections = 1;
+  g.side = 2;
+  g.out = b.v;
+  g.out_stride = h;
+  g.proj_offset = 0;
+  EXLR8_TIMED(EXLR8_KERNEL_DOWN, s, launch_expert_gemm(g, s));
+  return EXLR8_OK;
+}
+
+// The trellis tensor-core path is built for K = 3 and 4 (the EXLR8 layer
+// widths, experts.py:86); K = 2 keeps the streaming path.
+inline bool use_prefill(int64_t tokens, const exlr8_trellis_experts* ex) {
+  return tokens >= kPrefillMinTokens && (ex->k == 3 || ex->k == 4);
+}
+
 }  // namespace
 
 extern "C" {
@@ -376,7 +535,10 @@ int exlr8_expert_linear(const void* x, int x_dtype, int per_slot, const uint32_t
 }
 
 size_t exlr8_expert_mlp_workspace(int64_t tokens, int slots, int hidden, int intermediate, int64_t experts) {
-  return mlp_layout(tokens * slots, hidden, intermediate, experts).total();
+  const size_t decode = mlp_layout(tokens * slots, hidden, intermediate, experts).total();
+  if (tokens < kPrefillMinTokens) return decode;
+  const size_t prefill = prefill_bytes(tokens, slots, hidden, intermediate, experts, false);
+  return prefill > decode ? prefill : decode;
 }
 
 int exlr8_expert_mlp(const void* x, int x_dtype, int per_slot, const uint32_t* indices, int64_t tokens, int slots,
@@ -390,9 +552,18 @@ int exlr8_expert_mlp(const void* x, int x_dtype, int per_slot, const uint32_t* i
   if (rows == 0) return EXLR8_OK;
   if (!x || !indices || !out) return EXLR8_ERR_ARG;
   if (rows > (1 << 20)) return EXLR8_ERR_UNSUPPORTED;
-  const MlpLayout l = mlp_layout(rows, ex->hidden, ex->intermediate, experts);
-  if (!workspace || workspace_bytes < l.total()) return EXLR8_ERR_WORKSPACE;
+  if (!workspace || workspace_bytes < exlr8_expert_mlp_workspace(tokens, slots, ex->hidden, ex->intermediate, experts))
+    return EXLR8_ERR_WORKSPACE;
   cudaStream_t s = as_stream(stream);
+  if (use_prefill(tokens, ex)) {
+    Carver pc(workspace);
+    const PrefillBuffers pb = carve_prefill(tokens, slots, ex->hidden, ex->intermediate, experts, false, pc);
+    EXLR8_CHECK(prefill_products(x, x_dtype, per_slot, slots, indices, tokens, ex, experts, nullptr, pb, s));
+    ProfileScope scope(EXLR8_KERNEL_FINISH, s);
+    return cuda_status(launch_finish(pb.v, 1, pb.chunks.slot_row, indices, static_cast<int>(rows), ex->out_scale[2],
+                                     ex->scale_dtype, ex->hidden, static_cast<int>(experts), x_dtype, out, s));
+  }
+  const MlpLayout l = mlp_layout(rows, ex->hidden, ex->intermediate, experts);
   Carver c(workspace);
   const MlpBuffers b = carve_mlp(l, rows, experts, false, tokens, ex->hidden, ex->intermediate, c);
   EXLR8_TIMED(EXLR8_KERNEL_PLAN, s,
@@ -404,8 +575,25 @@ int exlr8_expert_mlp(const void* x, int x_dtype, int per_slot, const uint32_t* i
 }
 
 size_t exlr8_expert_mlp_finish_workspace(int64_t tokens, int hidden, int intermediate, int64_t experts) {
-  return mlp_layout(tokens * 9, hidden, intermediate, experts).total() +
-         dense_layout(tokens, hidden, intermediate).total();
+  const size_t decode = mlp_layout(tokens * 9, hidden, intermediate, experts).total() +
+                        dense_layout(tokens, hidden, intermediate).total();
+  if (tokens < kPrefillMinTokens) return decode;
+  const size_t prefill = prefill_bytes(tokens, 9, hidden, intermediate, experts, true);
+  return prefill > decode ? prefill : decode;
+}
+
+// Prefill counterpart of mlp_finish_after_plan (the plan runs inside).
+static int prefill_finish(const void* x, int x_dtype, const uint32_t* indices, const float* scores,
+                          const void* residual, int64_t tokens, const exlr8_trellis_experts* ex, int64_t experts,
+                          const exlr8_dense_expert* shared, void* out, void* workspace, cudaStream_t s) {
+  if (shared && !aligned16(x)) return EXLR8_ERR_ALIGN;  // tensor-map operand
+  Carver pc(workspace);
+  const PrefillBuffers pb = carve_prefill(tokens, 9, ex->hidden, ex->intermediate, experts, true, pc);
+  EXLR8_CHECK(prefill_products(x, x_dtype, 0, 9, indices, tokens, ex, experts, shared, pb, s));
+  ProfileScope scope(EXLR8_KERNEL_FINISH, s);
+  return cuda_status(launch_joined_finish(pb.v, pb.chunks.slot_row, indices, static_cast<int>(tokens), ex->hidden,
+                                          static_cast<int>(experts), ex->out_scale[2], ex->scale_dtype, scores,
+                                          residual, shared ? pb.ddown : nullptr, pb.dsplits_d, x_dtype, out, s));
 }
 
 // Nine-slot MLP + combine after the plan exists in `b`.
@@ -436,6 +624,8 @@ int exlr8_expert_mlp_finish(const void* x, int x_dtype, const uint32_t* indices,
   if (!workspace || workspace_bytes < exlr8_expert_mlp_finish_workspace(tokens, ex->hidden, ex->intermediate, experts))
     return EXLR8_ERR_WORKSPACE;
   cudaStream_t s = as_stream(stream);
+  if (use_prefill(tokens, ex))
+    return prefill_finish(x, x_dtype, indices, scores, residual, tokens, ex, experts, shared, out, workspace, s);
   const int64_t rows = tokens * 9;
   const MlpLayout l = mlp_layout(rows, ex->hidden, ex->intermediate, experts);
   Carver c(workspace);
@@ -446,9 +636,11 @@ int exlr8_expert_mlp_finish(const void* x, int x_dtype, const uint32_t* indices,
 }
 
 size_t exlr8_moe_layer_workspace(int64_t tokens, int hidden, int intermediate, int64_t experts) {
-  return exlr8_expert_mlp_finish_workspace(tokens, hidden, intermediate, experts) +
-         align_up(tokens * 256 * sizeof(float)) + align_up(tokens * 9 * sizeof(uint32_t)) +
-         align_up(tokens * 8 * sizeof(float)) + align_up(sizeof(int));
+  size_t router = align_up(tokens * 256 * sizeof(float)) + align_up(tokens * 9 * sizeof(uint32_t)) +
+                  align_up(tokens * 8 * sizeof(float)) + align_up(sizeof(int));
+  if (tokens >= kRouterGemmMinTokens)
+    router += align_up(router_gemm_workspace(static_cast<int>(tokens), hidden, EXLR8_DTYPE_F32));
+  return exlr8_expert_mlp_finish_workspace(tokens, hidden, intermediate, experts) + router;
 }
 
 int exlr8_moe_layer(const void* x, int x_dtype, const void* residual, int64_t tokens, const float* gate_weight,
@@ -481,6 +673,19 @@ int exlr8_moe_layer(const void* x, int x_dtype, const void* residual, int64_t to
   int* done = head.take<int>(sizeof(int));
   uint32_t* ids = indices ? indices : ids_buf;
   float* sc = scores ? scores : scores_buf;
+  if (use_prefill(tokens, ex)) {
+    if (tokens >= kRouterGemmMinTokens) {
+      void* router_ws = head.take<char>(router_gemm_workspace(static_cast<int>(tokens), ex->hidden, EXLR8_DTYPE_F32));
+      EXLR8_TIMED(EXLR8_KERNEL_ROUTER, s,
+                  launch_router_gemm(x, x_dtype, static_cast<int>(tokens), ex->hidden, gate_weight, logits, router_ws,
+                                     s));
+    } else {
+      EXLR8_TIMED(EXLR8_KERNEL_ROUTER, s,
+                  launch_gate_logits(x, x_dtype, static_cast<int>(tokens), ex->hidden, gate_weight, logits, 256, s));
+    }
+    EXLR8_TIMED(EXLR8_KERNEL_ROUTER, s, launch_route(logits, bias, static_cast<int>(tokens), ids, sc, 2.5f, 256u, s));
+    return prefill_finish(x, x_dtype, ids, sc, residual, tokens, ex, experts, shared, out, workspace, s);
+  }
   EXLR8_TIMED(EXLR8_KERNEL_ROUTER, s,
               launch_router_plan(x, x_dtype, static_cast<int>(tokens), ex->hidden, gate_weight, logits, bias, ids, sc,
                                  done, static_cast<int>(experts), shared ? 8 : -1, b.plan, s));
@@ -522,6 +727,16 @@ int exlr8_profile_read(int kind, int64_t* launches, double* total_ms) {
     *total_ms += ms;
   }
   return EXLR8_OK;
+}
+
+int exlr8_prefill_status(const void* workspace, int64_t tokens, int slots, int intermediate, int64_t experts,
+                         int32_t* header_out, void* stream) {
+  if (!workspace || !header_out || tokens <= 0 || slots <= 0 || intermediate <= 0) return EXLR8_ERR_ARG;
+  Carver c(const_cast<void*>(workspace));
+  const PrefillBuffers b = carve_prefill(tokens, slots, 128, intermediate, experts, false, c);
+  EXLR8_TRY(cudaMemcpyAsync(header_out, b.chunks.header, 8 * sizeof(int32_t), cudaMemcpyDeviceToHost,
+                            as_stream(stream)));
+  return cuda_status(cudaStreamSynchronize(as_stream(stream)));
 }
 
 int exlr8_workspace_bad_ids(const void* workspace, int64_t* bad_ids, void* stream) {

@@ -90,35 +90,39 @@ int joined_products(const void* x, int x_dtype, const uint32_t* ids, int64_t tok
   EXLR8_TIMED(EXLR8_KERNEL_PREP, s,
               launch_joined_prep(x, x_dtype, w->unit, w->scale_dtype, slots, static_cast<int>(tokens), b.chunks, h,
                                  b.x_hi, b.x_lo, b.x_scales, s));
-  MxGemmArgs g;
-  g.weights = w->gate_up;
-  g.weight_scales = static_cast<const uint8_t*>(w->gate_up_scales);
-  g.x_hi = b.x_hi;
-  g.x_lo = b.x_lo;
-  g.x_scales = b.x_scales;
+  ExpertGemmArgs g = {};
+  g.weights[0] = w->gate_up;
+  g.weight_scales[0] = static_cast<const uint8_t*>(w->gate_up_scales);
+  g.x_hi[0] = b.x_hi;
+  g.x_lo[0] = b.x_lo;
+  g.x_scales[0] = b.x_scales;
   g.chunks = b.chunks;
   g.counter_index = 2;
   g.experts = w->experts;
   g.padded_rows = l.padded;
   g.in_features = h;
   g.out_features = 2 * m;
+  g.projections = 1;
   g.paired = 1;
+  g.trellis_k = 0;
   g.out = b.gu;
-  EXLR8_TIMED(EXLR8_KERNEL_GATE_UP, s, launch_mx_gemm(g, s));
+  g.out_stride = 2 * m;
+  EXLR8_TIMED(EXLR8_KERNEL_GATE_UP, s, launch_expert_gemm(g, s));
   EXLR8_TIMED(EXLR8_KERNEL_GATE_FINISH, s,
               launch_joined_gate_finish(b.gu, ids, static_cast<int>(l.rows), b.chunks, w->gate_out, w->up_out,
                                         w->down_in, w->scale_dtype, m, x_dtype, b.h_hi, b.h_lo, b.h_scales, s));
-  g.weights = w->down;
-  g.weight_scales = static_cast<const uint8_t*>(w->down_scales);
-  g.x_hi = b.h_hi;
-  g.x_lo = b.h_lo;
-  g.x_scales = b.h_scales;
+  g.weights[0] = w->down;
+  g.weight_scales[0] = static_cast<const uint8_t*>(w->down_scales);
+  g.x_hi[0] = b.h_hi;
+  g.x_lo[0] = b.h_lo;
+  g.x_scales[0] = b.h_scales;
   g.counter_index = 3;
   g.in_features = m;
   g.out_features = h;
   g.paired = 0;
   g.out = b.v;
-  EXLR8_TIMED(EXLR8_KERNEL_DOWN, s, launch_mx_gemm(g, s));
+  g.out_stride = h;
+  EXLR8_TIMED(EXLR8_KERNEL_DOWN, s, launch_expert_gemm(g, s));
   return EXLR8_OK;
 }
 
@@ -185,8 +189,8 @@ int exlr8_joined_finish(const void* x, int x_dtype, const uint32_t* indices, con
   EXLR8_CHECK(joined_products(x, x_dtype, indices, tokens, 9, w, l, b, s));
   EXLR8_TIMED(EXLR8_KERNEL_FINISH, s,
               launch_joined_finish(b.v, b.chunks.slot_row, indices, static_cast<int>(tokens), w->hidden,
-                                   static_cast<int>(w->experts), w->down_out, w->scale_dtype, scores, residual, x_dtype,
-                                   out, s));
+                                   static_cast<int>(w->experts), w->down_out, w->scale_dtype, scores, residual, nullptr,
+                                   0, x_dtype, out, s));
   return EXLR8_OK;
 }
 
@@ -233,8 +237,8 @@ int exlr8_joined_moe_layer(const void* x, int x_dtype, const void* residual, int
   EXLR8_CHECK(joined_products(x, x_dtype, ids, tokens, 9, w, l, b, s));
   EXLR8_TIMED(EXLR8_KERNEL_FINISH, s,
               launch_joined_finish(b.v, b.chunks.slot_row, ids, static_cast<int>(tokens), w->hidden,
-                                   static_cast<int>(w->experts), w->down_out, w->scale_dtype, sc, residual, x_dtype,
-                                   out, s));
+                                   static_cast<int>(w->experts), w->down_out, w->scale_dtype, sc, residual, nullptr, 0,
+                                   x_dtype, out, s));
   return EXLR8_OK;
 }
 

@@ -171,7 +171,8 @@ __global__ void __launch_bounds__(256) joined_rowmap_kernel(PlanView plan, MxChu
   }
 }
 
-constexpr int kRowWarps = 8;  // warps per CTA of the row kernels
+constexpr int kRowWarps = 8;     // warps per CTA of the row kernels
+constexpr int kBlockGroup = 8;   // 128-blocks per warp item of the row kernels
 
 // xh = H(x[token] * unit), quantised once per token and stored into the
 // padded row of each of the token's slots.  Padding rows are left as they
@@ -186,10 +187,15 @@ __global__ void __launch_bounds__(kRowWarps * 32) joined_prep_kernel(const void*
   __shared__ __align__(16) float tbuf[kRowWarps][128];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int blocks = hidden / 128;
-  for (int token = blockIdx.x * kRowWarps + warp; token < tokens; token += gridDim.x * kRowWarps) {
+  const int groups = (blocks + kBlockGroup - 1) / kBlockGroup;
+  const int64_t items = static_cast<int64_t>(tokens) * groups;
+  for (int64_t item = static_cast<int64_t>(blockIdx.x) * kRowWarps + warp; item < items;
+       item += static_cast<int64_t>(gridDim.x) * kRowWarps) {
+    const int token = static_cast<int>(item / groups);
+    const int b0 = static_cast<int>(item % groups) * kBlockGroup, b1 = min(b0 + kBlockGroup, blocks);
     const int my_row = lane < slots_per_token ? c.slot_row[static_cast<int64_t>(token) * slots_per_token + lane] : -1;
     const int64_t xrow = static_cast<int64_t>(token) * hidden;
-    for (int block = 0; block < blocks; ++block) {
+    for (int block = b0; block < b1; ++block) {
       float v[4];
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
@@ -206,6 +212,47 @@ __global__ void __launch_bounds__(kRowWarps * 32) joined_prep_kernel(const void*
   }
 }
 
+// Trellis prefill inputs (fast_prefill.py:188-211 prep): per slot and
+// projection p, H(x[row] * in_scale_p[e]) quantised into the slot's padded
+// row of plane set p.  One warp per slot; x row = slot (per_slot) or
+// slot / slots_per_token.
+template <int kAct, int kScale>
+__global__ void __launch_bounds__(kRowWarps * 32) trellis_prep_kernel(
+    const void* __restrict__ x, int per_slot, int slots_per_token, int nslots, const uint32_t* __restrict__ ids,
+    MxChunks c, const void* __restrict__ in0, const void* __restrict__ in1, int projections, int hidden,
+    uint8_t* __restrict__ hi0, uint8_t* __restrict__ lo0, uint8_t* __restrict__ sc0, uint8_t* __restrict__ hi1,
+    uint8_t* __restrict__ lo1, uint8_t* __restrict__ sc1) {
+  __shared__ __align__(16) float tbuf[kRowWarps][128];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int blocks = hidden / 128;
+  const int groups = (blocks + kBlockGroup - 1) / kBlockGroup;
+  const int64_t items = static_cast<int64_t>(nslots) * groups;
+  for (int64_t item = static_cast<int64_t>(blockIdx.x) * kRowWarps + warp; item < items;
+       item += static_cast<int64_t>(gridDim.x) * kRowWarps) {
+    const int slot = static_cast<int>(item / groups);
+    const int b0 = static_cast<int>(item % groups) * kBlockGroup, b1 = min(b0 + kBlockGroup, blocks);
+    const int row = c.slot_row[slot];
+    if (row < 0) continue;
+    const int64_t e = ids[slot];
+    const int64_t xrow = static_cast<int64_t>(per_slot ? slot : slot / slots_per_token) * hidden;
+    for (int block = b0; block < b1; ++block) {
+      float xv[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) xv[j] = load_act(x, kAct, xrow + block * 128 + lane + 32 * j);
+      for (int p = 0; p < projections; ++p) {
+        const void* in = p ? in1 : in0;
+        float v[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          v[j] = __fmul_rn(xv[j], load_scale(in, kScale, e * hidden + block * 128 + lane + 32 * j));
+        hadamard128(v, lane);
+        store_words(quantize_words(v, tbuf[warp], lane), row, block, hidden, p ? hi1 : hi0, p ? lo1 : lo0,
+                    p ? sc1 : sc0, lane);
+      }
+    }
+  }
+}
+
 // metal/joined_gate_finish.metal: gate and up halves of the joined product,
 // Hadamard, out scales, typed SwiGLU, down in scale, Hadamard; quantised into
 // the down GEMM's activation planes.  One warp per padded row.
@@ -217,12 +264,17 @@ __global__ void __launch_bounds__(kRowWarps * 32) joined_gate_finish_kernel(
   __shared__ __align__(16) float tbuf[kRowWarps][128];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int blocks = intermediate / 128;
-  for (int slot = blockIdx.x * kRowWarps + warp; slot < slots; slot += gridDim.x * kRowWarps) {
+  const int groups = (blocks + kBlockGroup - 1) / kBlockGroup;
+  const int64_t items = static_cast<int64_t>(slots) * groups;
+  for (int64_t item = static_cast<int64_t>(blockIdx.x) * kRowWarps + warp; item < items;
+       item += static_cast<int64_t>(gridDim.x) * kRowWarps) {
+    const int slot = static_cast<int>(item / groups);
+    const int b0 = static_cast<int>(item % groups) * kBlockGroup, b1 = min(b0 + kBlockGroup, blocks);
     const int row = c.slot_row[slot];
     if (row < 0) continue;
     const int64_t e = ids[slot];
     const float* g_row = gu + static_cast<int64_t>(row) * 2 * intermediate + lane;
-    for (int block = 0; block < blocks; ++block) {
+    for (int block = b0; block < b1; ++block) {
       float g[4], u[4], h[4];
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
@@ -245,7 +297,7 @@ __global__ void __launch_bounds__(kRowWarps * 32) joined_gate_finish_kernel(
 }
 
 // JoinedMXFP4.finish for prefill batches: one CTA (nine warps, one per slot)
-// per token, four 128-blocks per round.  Per slot T(H(v) * down_out[e]);
+// per token and group of four 128-blocks.  Per slot T(H(v) * down_out[e]);
 // then the routed sum in the order of metal/fast_decode_finish_fused.metal
 // (slot 0, then (slot r + 0) + total for r = 1..7), T(routed),
 // T(routed + shared) and T(residual + combined).
@@ -257,26 +309,42 @@ __global__ void __launch_bounds__(288) joined_finish_kernel(const float* __restr
                                                             const uint32_t* __restrict__ ids, int features,
                                                             int experts, const void* __restrict__ out_scale,
                                                             const float* __restrict__ scores,
-                                                            const void* __restrict__ residual, void* __restrict__ out) {
+                                                            const void* __restrict__ residual,
+                                                            const float* __restrict__ shared_values, int shared_splits,
+                                                            int tokens, void* __restrict__ out) {
   __shared__ float products[9][kFinishGroup * 128];
   const int lane = threadIdx.x & 31, slot = threadIdx.x >> 5;
   const int64_t token = blockIdx.x;
+  const bool dense_shared = slot == 8 && shared_values != nullptr;
   const int64_t e = ids[token * 9 + slot];
-  const int prow = slot_row[token * 9 + slot];
+  const int prow = dense_shared ? -1 : slot_row[token * 9 + slot];
   const bool ok = e < experts && prow >= 0;
   const float score = slot < 8 ? scores[token * 8 + slot] : 1.0f;
   const float* src = v + static_cast<int64_t>(ok ? prow : 0) * features + lane;
   const int blocks = features / 128;
-  for (int b0 = 0; b0 < blocks; b0 += kFinishGroup) {
+  {
+    const int b0 = blockIdx.y * kFinishGroup;
     const int nb = min(kFinishGroup, blocks - b0);
     float val[kFinishGroup][4];
 #pragma unroll
     for (int g = 0; g < kFinishGroup; ++g)
 #pragma unroll
       for (int j = 0; j < 4; ++j) val[g][j] = (ok && g < nb) ? __ldcs(src + (b0 + g) * 128 + 32 * j) : 0.0f;
+    if (dense_shared) {
+      // Dense shared expert: float32 split partials [splits][tokens][h], summed and cast.
+      const int64_t total = static_cast<int64_t>(tokens) * features;
+      for (int g = 0; g < nb; ++g)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int64_t i = token * features + (b0 + g) * 128 + lane + 32 * j;
+          float a = 0.f;
+          for (int sp = 0; sp < shared_splits; ++sp) a += __ldcg(shared_values + sp * total + i);
+          products[8][g * 128 + lane + 32 * j] = round_to(kAct, a);
+        }
+    }
 #pragma unroll
     for (int g = 0; g < kFinishGroup; ++g) {
-      if (g >= nb) break;
+      if (g >= nb || dense_shared) break;
       hadamard128(val[g], lane);
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
@@ -373,11 +441,24 @@ cudaError_t launch_joined_gate_finish(const float* gu, const uint32_t* ids, int 
 
 cudaError_t launch_joined_finish(const float* v, const int32_t* slot_row, const uint32_t* ids, int tokens,
                                  int features, int experts, const void* out_scale, int scale_dtype,
-                                 const float* scores, const void* residual, int act_dtype, void* out, cudaStream_t s) {
+                                 const float* scores, const void* residual, const float* shared_values,
+                                 int shared_splits, int act_dtype, void* out, cudaStream_t s) {
   if (tokens == 0) return cudaSuccess;
   return dispatch_types(act_dtype, scale_dtype, [&](auto a, auto sc) {
-    joined_finish_kernel<decltype(a)::value, decltype(sc)::value><<<tokens, 288, 0, s>>>(
-        v, slot_row, ids, features, experts, out_scale, scores, residual, out);
+    const dim3 grid(tokens, (features / 128 + kFinishGroup - 1) / kFinishGroup);
+    joined_finish_kernel<decltype(a)::value, decltype(sc)::value><<<grid, 288, 0, s>>>(
+        v, slot_row, ids, features, experts, out_scale, scores, residual, shared_values, shared_splits, tokens, out);
+    return cudaGetLastError();
+  });
+}
+
+cudaError_t launch_trellis_prep(const void* x, int act_dtype, int per_slot, int slots_per_token, int nslots,
+                                const uint32_t* ids, MxChunks c, const void* in0, const void* in1, int scale_dtype,
+                                int projections, int hidden, uint8_t* hi0, uint8_t* lo0, uint8_t* sc0, uint8_t* hi1,
+                                uint8_t* lo1, uint8_t* sc1, cudaStream_t s) {
+  return dispatch_types(act_dtype, scale_dtype, [&](auto a, auto sc) {
+    trellis_prep_kernel<decltype(a)::value, decltype(sc)::value><<<worker_grid(), kRowWarps * 32, 0, s>>>(
+        x, per_slot, slots_per_token, nslots, ids, c, in0, in1, projections, hidden, hi0, lo0, sc0, hi1, lo1, sc1);
     return cudaGetLastError();
   });
 }

@@ -25,9 +25,18 @@ cudaError_t launch_joined_gate_finish(const float* gu, const uint32_t* ids, int 
 
 // Per-slot finish and routing-weighted combine with the residual (nine slots
 // per token, slot 8 = shared) reading slot rows through slot_row.
+// shared_values (nullable): float32 split partials [shared_splits][tokens][h]
+// of a dense shared expert that replaces slot 8.
 cudaError_t launch_joined_finish(const float* v, const int32_t* slot_row, const uint32_t* ids, int tokens,
                                  int features, int experts, const void* out_scale, int scale_dtype,
-                                 const float* scores, const void* residual, int act_dtype, void* out, cudaStream_t s);
+                                 const float* scores, const void* residual, const float* shared_values,
+                                 int shared_splits, int act_dtype, void* out, cudaStream_t s);
+
+// Trellis prefill GEMM inputs: per slot and projection, H(x * in_scale[e]).
+cudaError_t launch_trellis_prep(const void* x, int act_dtype, int per_slot, int slots_per_token, int nslots,
+                                const uint32_t* ids, MxChunks c, const void* in0, const void* in1, int scale_dtype,
+                                int projections, int hidden, uint8_t* hi0, uint8_t* lo0, uint8_t* sc0, uint8_t* hi1,
+                                uint8_t* lo1, uint8_t* sc1, cudaStream_t s);
 
 cudaError_t launch_mx_prepare_scales(const uint8_t* in, int64_t rows, int kblocks, uint8_t* out, cudaStream_t s);
 

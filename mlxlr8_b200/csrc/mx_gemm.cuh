@@ -7,8 +7,8 @@
 
 namespace exlr8 {
 
-constexpr int kMxMaxN = 160;    // slot rows per chunk (MMA N)
-constexpr int kMxKTile = 128;   // K values per pipeline stage
+constexpr int kMxMaxN = 160;      // slot rows per chunk (MMA N)
+constexpr int kMxKTile = 128;     // K values per pipeline stage
 constexpr int kMxRowAlign = 128;  // expert segments start on this row multiple
 
 // Slots sorted by expert, each expert's segment padded to a multiple of
@@ -30,25 +30,36 @@ inline int64_t mx_padded_rows(int64_t slots, int64_t experts) {
 }
 inline int64_t mx_max_chunks(int64_t slots, int64_t experts) { return slots / kMxRowAlign + experts + 1; }
 
-// One grouped projection: out[p][o] = sum_k W_e[o][k] X[p][k] for every
-// padded row p of every chunk (expert e) and every output o < out_features,
-// where W is E2M1 x E8M0 (per 32 values of k) and X = (hi + lo) E4M3 planes
-// sharing one E8M0 scale per 32 values.  Weight and activation scales are in
-// the 512-byte block layout (mx_scale_offset).
-struct MxGemmArgs {
-  const void* weights;         // [experts * out_features][in_features / 2] packed E2M1
-  const uint8_t* weight_scales;  // [experts * out_features / 128][in_features / 128][512]
-  const uint8_t* x_hi;         // [padded rows][in_features] E4M3
-  const uint8_t* x_lo;
-  const uint8_t* x_scales;     // [padded rows / 128][in_features / 128][512]
+// One grouped product: for every projection p, chunk (expert e) and output
+// row o < out_features of p:  out[r][p * proj_offset + o] =
+// sum_k W_pe[o][k] X_p[r][k] over the chunk's padded rows r, where
+// X = (hi + lo) E4M3 planes sharing one E8M0 scale per 32 values of k, and
+// W is either
+//   * MXFP4 (trellis_k == 0): E2M1 codes [experts * out][in / 2] with E8M0
+//     scales per 32 values in the 512-byte block layout (mx_scale_offset), or
+//   * trellis codes (trellis_k == 3 or 4, EXLR8 packed bytes, storage side
+//     `side`), decoded in the kernel to their exact E4M3 values.
+struct ExpertGemmArgs {
+  const void* weights[2];
+  const uint8_t* weight_scales[2];  // MXFP4 only
+  const uint8_t* x_hi[2];           // [padded rows][in_features] E4M3, per projection
+  const uint8_t* x_lo[2];
+  const uint8_t* x_scales[2];       // [padded rows / 128][in_features / 128][512]
   MxChunks chunks;
-  int counter_index;           // header slot of this launch's unit counter
+  int counter_index;                // header slot of this launch's unit counter
   int64_t experts;
-  int64_t padded_rows;         // allocated rows of x_hi / x_lo
+  int64_t padded_rows;              // allocated rows of the activation planes
   int in_features;
-  int out_features;
-  int paired;                  // accumulator 1 covers rows out_features / 2 + (those of accumulator 0)
-  float* out;                  // [padded rows][out_features]
+  int out_features;                 // per projection
+  int projections;                  // 1 or 2
+  int paired;                       // MXFP4 joined gate|up: accumulator 1 covers rows out_features / 2 + ...
+  int trellis_k;                    // 0, 3 or 4
+  int side;                         // trellis storage side (1: gate/up, 2: down)
+  uint32_t mcg_mask, mcg_xor;       // trellis hash constants (kept in registers for one LOP3)
+  uint32_t unit16;                  // 65536 (see decode_tile)
+  float* out;
+  int64_t out_stride;               // floats between consecutive rows of out
+  int64_t proj_offset;              // column offset of projection 1
 };
 
 // Byte of the scale of (row, k-block kb) inside the 512-byte block layout
@@ -57,7 +68,6 @@ __host__ __device__ inline int64_t mx_scale_offset(int64_t row, int64_t kb, int6
   return ((row / 128) * (k_blocks / 4) + kb / 4) * 512 + (row % 32) * 16 + ((row % 128) / 32) * 4 + kb % 4;
 }
 
-cudaError_t launch_mx_gemm(const MxGemmArgs& args, cudaStream_t s);
-int mx_gemm_status();  // 0, or a driver error from tensor-map encoding
+cudaError_t launch_expert_gemm(const ExpertGemmArgs& args, cudaStream_t s);
 
 }  // namespace exlr8

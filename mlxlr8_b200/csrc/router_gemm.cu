@@ -42,10 +42,12 @@ struct RgShared {
   uint32_t tmem;
 };
 
+// partial[split][row][n0 + c] (row stride n) of x . W^T over this CTA's K
+// range; the weight piece j occupies rows [j * n, (j + 1) * n) of wmap.
 __global__ void __launch_bounds__(kRgThreads, 1)
-    router_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap wmap,
-                       int x_pieces, int tokens, int hidden, int ktiles_per_split, float* __restrict__ partial,
-                       int32_t* __restrict__ error) {
+    bf16_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap wmap,
+                     int x_pieces, int w_pieces, int tokens, int hidden, int n, int ktiles_per_split,
+                     float* __restrict__ partial, int32_t* __restrict__ error) {
   extern __shared__ uint8_t smem_raw[];
   __shared__ RgShared sh;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -68,7 +70,7 @@ __global__ void __launch_bounds__(kRgThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = sh.tmem;
-  const uint32_t stage_bytes = (x_pieces + 3) * kRgTile;
+  const uint32_t stage_bytes = (x_pieces + w_pieces) * kRgTile;
 
   if (warp == 0) {
     if (lane == 0) {
@@ -83,7 +85,7 @@ __global__ void __launch_bounds__(kRgThreads, 1)
         const int k = (kt0 + kt) * kRgKTile;
         mbar_arrive_expect_tx(&sh.full[s], stage_bytes);
         for (int i = 0; i < x_pieces; ++i) tma_load_2d(st + i * kRgTile, &xmap, k, i * tokens + m0, &sh.full[s]);
-        for (int j = 0; j < 3; ++j) tma_load_2d(st + (kRgMaxA + j) * kRgTile, &wmap, k, j * 256 + n0, &sh.full[s]);
+        for (int j = 0; j < w_pieces; ++j) tma_load_2d(st + (kRgMaxA + j) * kRgTile, &wmap, k, j * n + n0, &sh.full[s]);
       }
       // Copies still in flight must land before the CTA exits.
       for (int u = max(0, kt - kRgStages); u < kt; ++u)
@@ -103,7 +105,7 @@ __global__ void __launch_bounds__(kRgThreads, 1)
         tc_fence_after();
         const uint32_t st = smem_u32(smem + s * kRgStageBytes);
         for (int i = 0; i < x_pieces; ++i) {
-          for (int j = 0; i + j <= 2; ++j) {
+          for (int j = 0; j < w_pieces && i + j <= 2; ++j) {
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk) {
               tc_mma_f16(tmem, umma_desc_sw128(st + i * kRgTile + kk * 32),
@@ -123,7 +125,7 @@ __global__ void __launch_bounds__(kRgThreads, 1)
     if (!ok && lane == 0) atomicCAS(error, 0, 4);
     tc_fence_after();
     if (ok) {
-      float* dst = partial + static_cast<int64_t>(split) * tokens * 256;
+      float* dst = partial + static_cast<int64_t>(split) * tokens * n;
 #pragma unroll 1
       for (int c0 = 0; c0 < 128; c0 += 16) {
         uint32_t v[16];
@@ -131,7 +133,7 @@ __global__ void __launch_bounds__(kRgThreads, 1)
         tc_wait_ld();
         const int row = m0 + 32 * quad + lane;
         if (row < tokens) {
-          float4* out = reinterpret_cast<float4*>(dst + static_cast<int64_t>(row) * 256 + n0 + c0);
+          float4* out = reinterpret_cast<float4*>(dst + static_cast<int64_t>(row) * n + n0 + c0);
 #pragma unroll
           for (int q = 0; q < 4; ++q)
             out[q] = ktiles > 0 ? make_float4(__uint_as_float(v[4 * q]), __uint_as_float(v[4 * q + 1]),
@@ -176,6 +178,21 @@ __global__ void router_x_pieces_kernel(const void* __restrict__ x, int x_dtype, 
   }
 }
 
+// h[t][j] = T(SwiGLU(T(sum g), T(sum u))) over split partials [splits][t][m]
+// (the dense shared expert's gate/up finish; sums in split order).
+__global__ void dense_swiglu_kernel(const float* __restrict__ gp, const float* __restrict__ up, int splits, int64_t n,
+                                    int act_dtype, void* __restrict__ h) {
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    float g = gp[i], u = up[i];
+    for (int k = 1; k < splits; ++k) {
+      g += gp[k * n + i];
+      u += up[k * n + i];
+    }
+    store_act(h, act_dtype, i, swiglu_typed(act_dtype, g, u));
+  }
+}
+
 // logits = sum over splits in split order.
 __global__ void router_sum_kernel(const float* __restrict__ partial, int splits, int64_t n, float* __restrict__ logits) {
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
@@ -204,6 +221,7 @@ EncodeTiledFn rg_encode_fn() {
 }
 
 bool rg_encode(CUtensorMap* map, const void* base, uint64_t inner, uint64_t rows) {
+  if (rows == 0) return false;
   EncodeTiledFn fn = rg_encode_fn();
   if (!fn) return false;
   const cuuint64_t dims[2] = {inner, rows};
@@ -227,18 +245,28 @@ int sm_count() {
 
 }  // namespace
 
+cudaError_t launch_dense_swiglu(const float* gate_partial, const float* up_partial, int splits, int64_t n,
+                                int act_dtype, void* h, cudaStream_t s) {
+  if (n == 0) return cudaSuccess;
+  dense_swiglu_kernel<<<sm_count() * 8, 256, 0, s>>>(gate_partial, up_partial, splits, n, act_dtype, h);
+  return cudaGetLastError();
+}
+
 // K splits so that the grid covers the SMs; every split gets at least one
 // 64-wide K tile.
-int router_gemm_splits(int tokens, int hidden) {
+int bf16_gemm_splits(int tokens, int k, int n) {
   const int mtiles = (tokens + 127) / 128;
-  const int ktiles = hidden / kRgKTile;
-  int splits = (sm_count() + 2 * mtiles - 1) / (2 * mtiles);
+  const int ntiles = n / 128;
+  const int ktiles = k / kRgKTile;
+  int splits = (sm_count() + mtiles * ntiles - 1) / (mtiles * ntiles);
   if (splits > 8) splits = 8;
   if (splits > ktiles) splits = ktiles;
   if (splits < 1) splits = 1;
   const int per = (ktiles + splits - 1) / splits;
   return (ktiles + per - 1) / per;
 }
+
+int router_gemm_splits(int tokens, int hidden) { return bf16_gemm_splits(tokens, hidden, 256); }
 
 size_t router_gemm_workspace(int tokens, int hidden, int x_dtype) {
   const int pieces = x_dtype == kBF16 ? 0 : (x_dtype == kF16 ? 2 : 3);
@@ -248,13 +276,34 @@ size_t router_gemm_workspace(int tokens, int hidden, int x_dtype) {
          up(splits * tokens * 256 * 4) + up(16);
 }
 
-cudaError_t launch_router_gemm(const void* x, int x_dtype, int tokens, int hidden, const float* gate_weight,
-                               float* logits, void* workspace, cudaStream_t s) {
+static cudaError_t configure_bf16_gemm() {
   static bool configured = false;
   if (!configured) {
-    cudaError_t err = cudaFuncSetAttribute(router_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kRgSmem);
+    cudaError_t err = cudaFuncSetAttribute(bf16_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kRgSmem);
     if (err != cudaSuccess) return err;
     configured = true;
+  }
+  return cudaSuccess;
+}
+
+cudaError_t launch_dense_gemm(const uint16_t* a, int rows, int k, const uint16_t* b, int n, int splits,
+                              float* partial, int32_t* error, cudaStream_t s) {
+  cudaError_t err = configure_bf16_gemm();
+  if (err != cudaSuccess) return err;
+  CUtensorMap amap, bmap;
+  if (!rg_encode(&amap, a, k, rows) || !rg_encode(&bmap, b, k, n)) return cudaErrorInvalidValue;
+  const int ktiles = k / kRgKTile;
+  const int per = (ktiles + splits - 1) / splits;
+  dim3 grid((rows + 127) / 128, n / 128, splits);
+  bf16_gemm_kernel<<<grid, kRgThreads, kRgSmem, s>>>(amap, bmap, 1, 1, rows, k, n, per, partial, error);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_router_gemm(const void* x, int x_dtype, int tokens, int hidden, const float* gate_weight,
+                               float* logits, void* workspace, cudaStream_t s) {
+  {
+    const cudaError_t err = configure_bf16_gemm();
+    if (err != cudaSuccess) return err;
   }
   auto up = [](size_t v) { return (v + 255) / 256 * 256; };
   char* ws = static_cast<char*>(workspace);
@@ -284,8 +333,8 @@ cudaError_t launch_router_gemm(const void* x, int x_dtype, int tokens, int hidde
   const int ktiles = hidden / kRgKTile;
   const int per = (ktiles + splits - 1) / splits;
   dim3 grid((tokens + 127) / 128, 2, splits);
-  router_gemm_kernel<<<grid, kRgThreads, kRgSmem, s>>>(xmap, wmap, pieces, tokens, hidden, per,
-                                                       splits == 1 ? logits : partial, error);
+  bf16_gemm_kernel<<<grid, kRgThreads, kRgSmem, s>>>(xmap, wmap, pieces, 3, tokens, hidden, 256, per,
+                                                     splits == 1 ? logits : partial, error);
   err = cudaGetLastError();
   if (err != cudaSuccess || splits == 1) return err;
   const int64_t n = static_cast<int64_t>(tokens) * 256;

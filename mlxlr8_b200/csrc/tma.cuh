@@ -8,7 +8,7 @@
 
 namespace exlr8 {
 
-constexpr uint32_t kSpinLimit = 1u << 16;
+constexpr uint32_t kSpinLimit = 1u << 14;  // at most ~1.6 s of 0.1 ms polls
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));

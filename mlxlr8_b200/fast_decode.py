@@ -62,11 +62,13 @@ def fast_expert_linear(x, indices, packed, in_scale, out_scale, k, in_features, 
 
 
 def fast_expert_mlp(x, indices, packed, scales, k, hidden, intermediate, *, reuse=False, fp8=None,
-                    expert_to_slot=None):
+                    expert_to_slot=None, workspace=None):
     """Gate/up, typed SwiGLU, down for every slot; ``[*indices.shape, hidden]``.
 
     Mirrors ``fast_expert_mlp`` (fast_decode.py:208-221).  The static FP8 hot
-    cache (``fp8``/``expert_to_slot``) is not part of this build.
+    cache (``fp8``/``expert_to_slot``) is not part of this build.  An optional
+    uint8 ``workspace`` tensor is used instead of a fresh one when it is large
+    enough (its dispatch header stays readable after the call).
     """
     if fp8 is not None or expert_to_slot is not None:
         raise NotImplementedError("the static FP8 expert cache is not implemented in the B200 build")
@@ -86,7 +88,8 @@ def fast_expert_mlp(x, indices, packed, scales, k, hidden, intermediate, *, reus
     x = x.contiguous()
     out = torch.empty(tuple(indices.shape) + (hidden,), dtype=x.dtype, device=device)
     lib = _lib.lib()
-    ws = _lib.workspace(lib.exlr8_expert_mlp_workspace(tokens, slots, hidden, intermediate, experts), device)
+    need = lib.exlr8_expert_mlp_workspace(tokens, slots, hidden, intermediate, experts)
+    ws = workspace if workspace is not None and workspace.numel() >= need else _lib.workspace(need, device)
     _lib.check(lib.exlr8_expert_mlp(x.data_ptr(), _lib.act_code(x), per_slot, ids.data_ptr(), tokens, slots,
                                     st, out.data_ptr(), ws.data_ptr(), ws.numel(), _lib.stream_handle(device)))
     return out
