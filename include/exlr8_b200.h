@@ -235,6 +235,48 @@ int exlr8_workspace_bad_ids(const void* workspace, int64_t* bad_ids, void* strea
 int exlr8_prefill_status(const void* workspace, int64_t tokens, int slots, int intermediate, int64_t experts,
                          int32_t* header, void* stream);
 
+/* ---- expert parallelism ------------------------------------------------------ */
+
+/*
+ * The routed experts sharded over `ranks` devices (rank r owns experts
+ * [r * experts_per_rank, (r + 1) * experts_per_rank)), each rank holding its
+ * own tokens.  One layer on one rank:
+ *   exlr8_router                         ids [tokens][9], scores [tokens][8]
+ *   exlr8_ep_dispatch                    per-destination rows (below)
+ *   all-to-all of send_x and send_meta   (NCCL; the caller's collective)
+ *   exlr8_expert_mlp on the received rows (slots = 1, ids = received meta;
+ *                                         empty rows carry id -1 -> zeros)
+ *   all-to-all of the slot values back
+ *   exlr8_shared_expert (or the shared trellis expert) on the local tokens
+ *   exlr8_ep_combine                     routed sum + shared + residual
+ * The reference runs all experts on one device (model.py:385-418); this
+ * split keeps its arithmetic: each slot value is computed exactly as in
+ * exlr8_expert_mlp and combined in the same order.
+ *
+ * exlr8_ep_dispatch: send_x [ranks][capacity][hidden] (x dtype),
+ * send_meta int32 [ranks][capacity] (local expert id, -1 = empty row),
+ * slot_pos int32 [tokens * 8] (destination * capacity + row, -1 for ids
+ * outside [0, ranks * experts_per_rank)), counts int32 [ranks], status int32
+ * [1] (slots lost to overflow; capacity = tokens * 8 never overflows).  Rows
+ * keep slot order per destination.  hidden * element size % 16 == 0.
+ */
+int exlr8_ep_dispatch(const uint32_t* indices, int64_t tokens, const void* x, int x_dtype, int hidden, int ranks,
+                      int experts_per_rank, int capacity, void* send_x, int32_t* send_meta, int32_t* slot_pos,
+                      int32_t* counts, int32_t* status, void* stream);
+
+/* values [ranks * capacity][hidden] (the returned slot values, x dtype),
+ * shared [tokens][hidden] typed shared-expert output, residual and out
+ * [tokens][hidden]. */
+int exlr8_ep_combine(const void* values, int x_dtype, const int32_t* slot_pos, const float* scores, const void* shared,
+                     const void* residual, int64_t tokens, int hidden, void* out, void* stream);
+
+/* Typed output of the dense bf16 shared expert for every token (slot 8 of
+ * the combine): T(down(SwiGLU(T(x Wg^T), T(x Wu^T)))). */
+size_t exlr8_shared_expert_workspace(int64_t tokens, int hidden, int intermediate);
+int exlr8_shared_expert(const void* x, int x_dtype, int64_t tokens, int hidden, int intermediate,
+                        const exlr8_dense_expert* shared, void* out, void* workspace, size_t workspace_bytes,
+                        void* stream);
+
 /* ---- joined MXFP4 experts (prefill) -------------------------------------- */
 
 /*

@@ -105,6 +105,13 @@ _SIGNATURES = {
                                        c_void_p]),
     "exlr8_joined_status": (c_int, [c_void_p, c_int64, c_int, c_int64, c_void_p, c_void_p]),
     "exlr8_prefill_status": (c_int, [c_void_p, c_int64, c_int, c_int, c_int64, c_void_p, c_void_p]),
+    "exlr8_ep_dispatch": (c_int, [c_void_p, c_int64, c_void_p, c_int, c_int, c_int, c_int, c_int, c_void_p, c_void_p,
+                                  c_void_p, c_void_p, c_void_p, c_void_p]),
+    "exlr8_ep_combine": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int, c_void_p,
+                                 c_void_p]),
+    "exlr8_shared_expert_workspace": (c_size_t, [c_int64, c_int, c_int]),
+    "exlr8_shared_expert": (c_int, [c_void_p, c_int, c_int64, c_int, c_int, POINTER(DenseExpert), c_void_p, c_void_p,
+                                    c_size_t, c_void_p]),
     "exlr8_router_logits_workspace": (c_size_t, [c_int64, c_int, c_int]),
     "exlr8_router_logits": (c_int, [c_void_p, c_int, c_int64, c_int, c_void_p, c_void_p, c_void_p, c_size_t,
                                     c_void_p]),

@@ -8,6 +8,7 @@
 #include "codec.cuh"
 #include "common.cuh"
 #include "dense.cuh"
+#include "ep.cuh"
 #include "joined.cuh"
 #include "mx_gemm.cuh"
 #include "router.cuh"
@@ -727,6 +728,99 @@ int exlr8_profile_read(int kind, int64_t* launches, double* total_ms) {
     *total_ms += ms;
   }
   return EXLR8_OK;
+}
+
+// ---- expert parallelism ---------------------------------------------------
+
+int exlr8_ep_dispatch(const uint32_t* indices, int64_t tokens, const void* x, int x_dtype, int hidden, int ranks,
+                      int experts_per_rank, int capacity, void* send_x, int32_t* send_meta, int32_t* slot_pos,
+                      int32_t* counts, int32_t* status, void* stream) {
+  if (!valid_act(x_dtype)) return EXLR8_ERR_DTYPE;
+  if (tokens < 0 || hidden <= 0 || ranks <= 0 || ranks > 32 || experts_per_rank <= 0 || capacity < 0)
+    return EXLR8_ERR_ARG;
+  if ((hidden * (x_dtype == EXLR8_DTYPE_F32 ? 4 : 2)) % 16) return EXLR8_ERR_DIMS;
+  if (tokens * 8 > (int64_t(1) << 24)) return EXLR8_ERR_UNSUPPORTED;
+  if (!send_x || !send_meta || !counts || !status || (tokens > 0 && (!indices || !x || !slot_pos)))
+    return EXLR8_ERR_ARG;
+  if (!aligned16(x) || !aligned16(send_x)) return EXLR8_ERR_ALIGN;
+  return cuda_status(launch_ep_dispatch(indices, static_cast<int>(tokens), x, x_dtype, hidden, ranks,
+                                        experts_per_rank, capacity, send_x, send_meta, slot_pos, counts, status,
+                                        as_stream(stream)));
+}
+
+int exlr8_ep_combine(const void* values, int x_dtype, const int32_t* slot_pos, const float* scores, const void* shared,
+                     const void* residual, int64_t tokens, int hidden, void* out, void* stream) {
+  if (!valid_act(x_dtype)) return EXLR8_ERR_DTYPE;
+  if (tokens < 0 || hidden <= 0) return EXLR8_ERR_ARG;
+  if (tokens == 0) return EXLR8_OK;
+  if (!values || !slot_pos || !scores || !shared || !residual || !out) return EXLR8_ERR_ARG;
+  return cuda_status(launch_ep_combine(values, x_dtype, slot_pos, scores, shared, residual, static_cast<int>(tokens),
+                                       hidden, out, as_stream(stream)));
+}
+
+size_t exlr8_shared_expert_workspace(int64_t tokens, int hidden, int intermediate) {
+  if (tokens <= 0) return 0;
+  if (tokens < kPrefillMinTokens)
+    return dense_layout(tokens, hidden, intermediate).total() + align_up((intermediate / 64 + 1) * sizeof(int32_t));
+  const int t = static_cast<int>(tokens);
+  const size_t sgu = bf16_gemm_splits(t, hidden, intermediate), sd = bf16_gemm_splits(t, intermediate, hidden);
+  return 2 * align_up(sgu * tokens * intermediate * sizeof(float)) + align_up(tokens * intermediate * 2) +
+         align_up(sd * tokens * hidden * sizeof(float)) + align_up(16);
+}
+
+// T(down(SwiGLU(T(x Wg^T), T(x Wu^T)))) of the dense bf16 shared expert for
+// every token: the typed slot-8 value of the combine (model.py:415-418).
+int exlr8_shared_expert(const void* x, int x_dtype, int64_t tokens, int hidden, int intermediate,
+                        const exlr8_dense_expert* shared, void* out, void* workspace, size_t workspace_bytes,
+                        void* stream) {
+  if (!shared) return EXLR8_ERR_ARG;
+  EXLR8_CHECK(check_dense(shared, x_dtype, hidden, intermediate));
+  if (tokens < 0) return EXLR8_ERR_ROWS;
+  if (tokens == 0) return EXLR8_OK;
+  if (!x || !out) return EXLR8_ERR_ARG;
+  if (!aligned16(x)) return EXLR8_ERR_ALIGN;
+  if (tokens > (int64_t(1) << 20)) return EXLR8_ERR_UNSUPPORTED;
+  if (!workspace || workspace_bytes < exlr8_shared_expert_workspace(tokens, hidden, intermediate))
+    return EXLR8_ERR_WORKSPACE;
+  cudaStream_t s = as_stream(stream);
+  const int t = static_cast<int>(tokens);
+  const uint16_t* xb = static_cast<const uint16_t*>(x);
+  Carver c(workspace);
+  if (tokens < kPrefillMinTokens) {
+    const DenseLayout dl = dense_layout(tokens, hidden, intermediate);
+    float* dg = c.take<float>(dl.gate);
+    float* du = c.take<float>(dl.up);
+    void* dh = c.take<void>(dl.h);
+    float* dd = c.take<float>(dl.down);
+    int32_t* counters = c.take<int32_t>((intermediate / 64 + 1) * sizeof(int32_t));
+    EXLR8_TRY(cudaMemsetAsync(counters, 0, (intermediate / 64 + 1) * sizeof(int32_t), s));
+    EXLR8_TIMED(EXLR8_KERNEL_DENSE, s,
+                launch_dense_gate_up(xb, t, static_cast<const uint16_t*>(shared->gate),
+                                     static_cast<const uint16_t*>(shared->up), intermediate, hidden,
+                                     kDenseGateUpSplits, dg, du, counters, x_dtype, dh, s));
+    EXLR8_TIMED(EXLR8_KERNEL_DENSE, s,
+                launch_dense_gemv(static_cast<const uint16_t*>(dh), t, static_cast<const uint16_t*>(shared->down),
+                                  hidden, intermediate, kDenseDownSplits, dd, s));
+    return cuda_status(launch_sum_cast(dd, kDenseDownSplits, tokens * hidden, x_dtype, out, s));
+  }
+  const int sgu = bf16_gemm_splits(t, hidden, intermediate), sd = bf16_gemm_splits(t, intermediate, hidden);
+  float* dg = c.take<float>(static_cast<size_t>(sgu) * tokens * intermediate * sizeof(float));
+  float* du = c.take<float>(static_cast<size_t>(sgu) * tokens * intermediate * sizeof(float));
+  void* dh = c.take<void>(static_cast<size_t>(tokens) * intermediate * 2);
+  float* dd = c.take<float>(static_cast<size_t>(sd) * tokens * hidden * sizeof(float));
+  int32_t* err = c.take<int32_t>(16);
+  EXLR8_TRY(cudaMemsetAsync(err, 0, sizeof(int32_t), s));
+  EXLR8_TIMED(EXLR8_KERNEL_DENSE, s,
+              launch_dense_gemm(xb, t, hidden, static_cast<const uint16_t*>(shared->gate), intermediate, sgu, dg, err,
+                                s));
+  EXLR8_TIMED(EXLR8_KERNEL_DENSE, s,
+              launch_dense_gemm(xb, t, hidden, static_cast<const uint16_t*>(shared->up), intermediate, sgu, du, err,
+                                s));
+  EXLR8_TIMED(EXLR8_KERNEL_DENSE, s, launch_dense_swiglu(dg, du, sgu, tokens * intermediate, x_dtype, dh, s));
+  EXLR8_TIMED(EXLR8_KERNEL_DENSE, s,
+              launch_dense_gemm(static_cast<const uint16_t*>(dh), t, intermediate,
+                                static_cast<const uint16_t*>(shared->down), hidden, sd, dd, err, s));
+  return cuda_status(launch_sum_cast(dd, sd, tokens * hidden, x_dtype, out, s));
 }
 
 int exlr8_prefill_status(const void* workspace, int64_t tokens, int slots, int intermediate, int64_t experts,

@@ -1,0 +1,154 @@
+"""Expert-parallel layer on one GPU: dispatch positions against a plain
+restatement, and the whole exchange (dispatch, all-to-all, grouped expert
+MLP on the owner, all-to-all back, combine) with N emulated ranks against the
+oracle of the single-device MoE layer (model.py:385-418).
+
+The all-to-all of N ranks is emulated by stacking the ranks' send buffers;
+the NCCL exchange itself runs in test_gpu_ep_multi.py on two GPUs.
+"""
+
+import numpy as np
+import pytest
+
+from helpers import host, rel_l2
+from oracle import trellis_oracle as ref
+
+pytestmark = pytest.mark.gpu
+
+
+def _positions_reference(ids, ranks, per_rank, capacity):
+    """Destination rank * capacity + row of every routed slot, rows in slot order."""
+    ids = np.asarray(ids)
+    tokens = ids.shape[0]
+    pos = np.full(tokens * 8, -1, np.int64)
+    meta = np.full((ranks, capacity), -1, np.int64)
+    fill = [0] * ranks
+    for i in range(tokens * 8):
+        e = int(ids[i // 8, i % 8])
+        if e >= ranks * per_rank:
+            continue
+        d = e // per_rank
+        if fill[d] < capacity:
+            pos[i] = d * capacity + fill[d]
+            meta[d, fill[d]] = e % per_rank
+        fill[d] += 1
+    return pos, meta, fill
+
+
+def _dispatch(ids, x, ranks, per_rank, capacity):
+    import torch
+
+    from mlxlr8_b200 import _lib
+
+    tokens, h = x.shape
+    send_x = torch.empty(ranks, capacity, h, dtype=x.dtype, device="cuda")
+    send_meta = torch.empty(ranks, capacity, dtype=torch.int32, device="cuda")
+    slot_pos = torch.empty(max(tokens * 8, 1), dtype=torch.int32, device="cuda")
+    counts = torch.empty(ranks, dtype=torch.int32, device="cuda")
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    _lib.check(_lib.lib().exlr8_ep_dispatch(ids.data_ptr(), tokens, x.data_ptr(), _lib.act_code(x), h, ranks,
+                                            per_rank, capacity, send_x.data_ptr(), send_meta.data_ptr(),
+                                            slot_pos.data_ptr(), counts.data_ptr(), status.data_ptr(),
+                                            _lib.stream_handle(x.device)))
+    return send_x, send_meta, slot_pos[:tokens * 8], counts, status
+
+
+@pytest.mark.parametrize("tokens, ranks, capacity", [(5, 2, 40), (300, 8, 2400), (37, 4, 20)])
+def test_dispatch_positions_match_restatement(tokens, ranks, capacity):
+    import torch
+
+    rng = np.random.default_rng(tokens)
+    per_rank = 256 // ranks
+    ids = np.concatenate([rng.integers(0, 260, (tokens, 8)), np.full((tokens, 1), 256)], axis=1).astype(np.int32)
+    x = torch.randn(tokens, 256, device="cuda").to(torch.bfloat16)
+    send_x, send_meta, slot_pos, counts, status = _dispatch(torch.from_numpy(ids).cuda(), x, ranks, per_rank,
+                                                           capacity)
+    torch.cuda.synchronize()
+    pos, meta, fill = _positions_reference(ids, ranks, per_rank, capacity)
+    np.testing.assert_array_equal(slot_pos.cpu().numpy(), pos)
+    np.testing.assert_array_equal(send_meta.cpu().numpy(), meta)
+    np.testing.assert_array_equal(counts.cpu().numpy(), np.minimum(fill, capacity))
+    assert status.item() == sum(max(f - capacity, 0) for f in fill)
+    xs = x.cpu()
+    flat = send_x.reshape(-1, 256).cpu()
+    for i in np.nonzero(pos >= 0)[0][:200]:
+        assert torch.equal(flat[pos[i]], xs[i // 8])
+
+
+def _emulated_layer(layer, x, residual, world):
+    """The expert-parallel layer over `world` emulated ranks on one GPU."""
+    import torch
+
+    from mlxlr8_b200 import _lib
+    from mlxlr8_b200.ep import ExpertParallelMoE, shard_experts, shared_trellis
+    from mlxlr8_b200.fast_decode import fast_expert_mlp
+
+    e = layer.experts
+    tokens, h = x.shape
+    tl = tokens // world
+    shared_layer = shared_trellis(e) if e.shared is None else None
+    ranks = [ExpertParallelMoE(layer.gate_weight, layer.bias, shard_experts(e, r, world), r, world,
+                               shared=e.shared, shared_layer=shared_layer) for r in range(world)]
+    cap = tl * 8
+    sends, routing = [], []
+    for r, m in enumerate(ranks):
+        xr = x[r * tl:(r + 1) * tl].contiguous()
+        ids, scores = m.route(xr)
+        send_x, send_meta, slot_pos, counts, status = _dispatch(ids, xr, world, 256 // world, cap)
+        sends.append((send_x, send_meta))
+        routing.append((ids, scores, slot_pos, status))
+    back_parts = [[None] * world for _ in range(world)]
+    for r, m in enumerate(ranks):
+        recv_x = torch.stack([sends[s][0][r] for s in range(world)])
+        recv_meta = torch.stack([sends[s][1][r] for s in range(world)])
+        values = fast_expert_mlp(recv_x.reshape(-1, h), recv_meta.reshape(-1, 1), m.local.packed, m.local.scales,
+                                 m.local.k, h, m.local.intermediate).reshape(world, cap, h)
+        for s in range(world):
+            back_parts[s][r] = values[s]
+    outs, all_ids, all_scores = [], [], []
+    for r, m in enumerate(ranks):
+        xr = x[r * tl:(r + 1) * tl].contiguous()
+        res = residual[r * tl:(r + 1) * tl].contiguous()
+        ids, scores, slot_pos, status = routing[r]
+        assert status.item() == 0
+        back = torch.stack(back_parts[r])
+        shared = m.shared_values(xr)
+        out = torch.empty_like(res)
+        _lib.check(_lib.lib().exlr8_ep_combine(back.data_ptr(), _lib.act_code(xr), slot_pos.data_ptr(),
+                                               scores.data_ptr(), shared.data_ptr(), res.data_ptr(), tl, h,
+                                               out.data_ptr(), _lib.stream_handle(x.device)))
+        outs.append(out)
+        all_ids.append(ids)
+        all_scores.append(scores)
+    return torch.cat(outs), torch.cat(all_ids), torch.cat(all_scores)
+
+
+@pytest.mark.parametrize("world", [2, 4])
+@pytest.mark.parametrize("shared", ["bf16", "trellis"])
+@pytest.mark.parametrize("tokens_per_rank", [2, 24])
+def test_emulated_expert_parallel_layer_matches_oracle(world, shared, tokens_per_rank):
+    import torch
+
+    from mlxlr8_b200.fast_router import router, router_logits
+    from mlxlr8_b200.synthetic import host_copy, make_layer
+
+    layer = make_layer(seed=31, hidden=256, intermediate=128, shared=shared)
+    tokens = world * tokens_per_rank
+    x, residual = layer.tokens(tokens)
+    out, ids, scores = _emulated_layer(layer, x, residual, world)
+    torch.cuda.synchronize()
+    # Routing is per rank; each rank's logits come from the same gate product.
+    if tokens_per_rank >= 64:
+        logits = router_logits(x, layer.gate_weight)
+    else:
+        logits, _, _ = router(x, layer.gate_weight, layer.bias)
+    ids_np = ids.cpu().numpy()
+    hc = host_copy(layer, np.unique(ids_np[:, :8] if shared == "bf16" else ids_np))
+    e_out, e_ids, e_scores = ref.moe_layer(host(x), host(residual), hc["gate_weight"], hc["bias"], hc["packed"],
+                                           hc["scales"], 4, 256, 128, shared=hc["shared"], dtype="bfloat16",
+                                           logits=host(logits))
+    np.testing.assert_array_equal(ids_np, e_ids)
+    got, want = host(out) - host(residual), e_out - host(residual)
+    scale = float(np.max(np.abs(want)))
+    assert float(np.max(np.abs(got - want))) <= 1e-2 * scale
+    assert rel_l2(got, want) < 5e-3
