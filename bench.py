@@ -70,6 +70,8 @@ def parse():
                         "--tokens tokens, top-8 uniform routing (about 4 GB on the device at 129 experts and 2048 "
                         "tokens)")
     p.add_argument("--experts", type=int, default=129)
+    p.add_argument("--no-extras", action="store_true",
+                   help="skip the single-GPU extras (decode at T=8/32, the prefill configurations)")
     p.add_argument("--calls", type=int, default=5)
     return p.parse_args()
 
@@ -237,7 +239,99 @@ def reference_arm(args, world, rank):
 
 
 def unique_experts(ids_list):
-    return [len(set(int(e) for e in ids[:, :8].reshape(-1).tolist())) for ids in ids_list]
+    return [len(set(int(e) for e in ids[:, :8].reshape(-1).tolist() if e >= 0)) for ids in ids_list]
+
+
+def time_calls(fn, steps, warmup, stream):
+    """Milliseconds per call of fn() on `stream` (CUDA events, after warm-up)."""
+    import torch
+
+    with torch.cuda.stream(stream):
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            fn()
+        e1.record(stream)
+        e1.synchronize()
+    return e0.elapsed_time(e1) / steps
+
+
+def decode_batches(layers, moes, batches, steps, stream):
+    """Single-GPU decode tokens/s at other batch sizes of configs[1], graph replay over the same layers."""
+    import torch
+
+    out = {}
+    L = len(layers)
+    for T in batches:
+        xs = [layer.tokens(T, seed_offset=50 + i) for i, layer in enumerate(layers)]
+        graphs = []
+        with torch.cuda.stream(stream):
+            for i in range(L):
+                moes[i](*xs[i])
+            torch.cuda.synchronize()
+            for i in range(L):
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=stream):
+                    moes[i](*xs[i])
+                graphs.append(g)
+        state = {"s": 0}
+
+        def replay():
+            graphs[state["s"] % L].replay()
+            state["s"] += 1
+
+        ms = time_calls(replay, steps, 5, stream)
+        out[f"T{T}"] = {"tokens_per_s": T / (ms / 1000.0), "ms_per_step": ms}
+        del graphs
+    return out
+
+
+def prefill_configs(layer_k4, steps, stream, peak_tflops):
+    """configs[2] (joined MXFP4, 4096 tokens) and configs[4] (128 tokens, K4 and the K3 layer-78 width)."""
+    import torch
+
+    from mlxlr8_b200 import _lib
+    from mlxlr8_b200.joined_mxfp4 import JoinedMoELayer, JoinedMXFP4
+    from mlxlr8_b200.moe import MoELayer
+    from mlxlr8_b200.synthetic import make_joined, make_layer
+
+    res = {}
+    j = make_joined(seed=5)
+    joined = JoinedMoELayer(j.gate_weight, j.bias, JoinedMXFP4(j.unit, j.weights, j.scales, j.hidden, j.intermediate))
+    x, r = j.tokens(4096)
+    ms = time_calls(lambda: joined(x, r), steps, 3, stream)
+    with torch.cuda.stream(stream):
+        _lib.profile_enable(True)
+        joined(x, r)
+        torch.cuda.synchronize()
+        prof = _lib.profile_read()
+        _lib.profile_enable(False)
+    gemm_ms = prof["gate_up"][1] + prof["down"][1]
+    flops = 2.0 * 4096 * 9 * 3 * HIDDEN * INTER  # routed + shared slot, gate/up/down
+    res["joined_mxfp4_T4096"] = {
+        "tokens_per_s": 4096 / (ms / 1000.0), "ms_per_layer": ms,
+        "useful_tflops": flops / (ms / 1000.0) / 1e12,
+        "gemm_ms": gemm_ms, "gemm_useful_tflops": flops / (gemm_ms / 1000.0) / 1e12,
+        "gemm_frac_of_bf16_peak": flops / (gemm_ms / 1000.0) / 1e12 / peak_tflops,
+        "kernel_ms": {k: v[1] for k, v in prof.items() if v[0]},
+        "note": "block-scaled tcgen05 MMA (kind::mxf8f6f4, E2M1 weights x E4M3 hi/lo activations); useful FLOPs "
+                "count each product once (the hi/lo planes issue twice as many MMA FLOPs)"}
+    del joined, j, x, r
+    torch.cuda.empty_cache()
+    for k, layer in (("k4", layer_k4), ("k3", None)):
+        if layer is None:
+            layer = make_layer(seed=78, k=3)
+        moe = MoELayer(layer.gate_weight, layer.bias, layer.experts)
+        x, r = layer.tokens(128, seed_offset=9)
+        ms = time_calls(lambda: moe(x, r), steps, 3, stream)
+        res[f"trellis_{k}_T128"] = {"tokens_per_s": 128 / (ms / 1000.0), "ms_per_layer": ms,
+                                     "path": "grouped tcgen05 GEMM with in-kernel trellis decode"}
+        del moe
+    torch.cuda.empty_cache()
+    return res
 
 
 def main():
@@ -249,6 +343,7 @@ def main():
     if args.impl == "reference":
         reference_arm(args, world, rank)
         return
+    import numpy as np
     import torch
     import torch.distributed as dist
 
@@ -262,29 +357,51 @@ def main():
         dist.init_process_group("nccl", init_method="env://", device_id=device)
     T, L = args.tokens, args.layers
 
+    # Every rank builds the same seeded layers; with N > 1 it keeps its block
+    # of 256 / N routed experts (expert parallelism) and the shared expert,
+    # and draws its own tokens.
     layers, moes, xs, rs = [], [], [], []
     for i in range(L):
-        layer = make_layer(seed=1000 + 97 * i + 7919 * rank, device=device)
-        layers.append(layer)
-        moes.append(MoELayer(layer.gate_weight, layer.bias, layer.experts))
-        x, r = layer.tokens(T, seed_offset=i)
+        layer = make_layer(seed=1000 + 97 * i, device=device)
+        if world == 1:
+            moes.append(MoELayer(layer.gate_weight, layer.bias, layer.experts))
+        else:
+            from mlxlr8_b200.ep import ExpertParallelMoE, shard_experts
+
+            shard = shard_experts(layer.experts, rank, world)
+            for p in ("gate", "up", "down"):
+                shard.packed[p] = shard.packed[p].clone()
+            moes.append(ExpertParallelMoE(layer.gate_weight, layer.bias, shard, rank, world,
+                                          shared=layer.experts.shared))
+        x, r = layer.tokens(T, seed_offset=i * world + rank)
         xs.append(x)
         rs.append(r)
+        if world > 1:
+            del layer.experts.packed  # only the shard stays resident
+        layers.append(layer)
     torch.cuda.synchronize()
 
-    # CUDA graphs of one layer call each (inputs resident in HBM).
+    # One GPU: CUDA graphs of one layer call each (inputs resident in HBM).
+    # Several GPUs: eager layer calls (the NCCL exchange runs on the stream).
     outs, graphs = [], []
     stream = torch.cuda.Stream(device)
     with torch.cuda.stream(stream):
         for i in range(L):
             moes[i](xs[i], rs[i])  # allocate the cached workspace before capture
         torch.cuda.synchronize()
-        for i in range(L):
-            g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g, stream=stream):
-                outs.append(moes[i](xs[i], rs[i]))
-            graphs.append(g)
+        if world == 1:
+            for i in range(L):
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=stream):
+                    outs.append(moes[i](xs[i], rs[i]))
+                graphs.append(g)
     torch.cuda.synchronize()
+
+    def step(s):
+        if graphs:
+            graphs[s % L].replay()
+        else:
+            moes[s % L](xs[s % L], rs[s % L])
 
     def barrier():
         if world > 1:
@@ -294,14 +411,14 @@ def main():
     # ---- headline: graph replay, device-resident inputs ----
     with torch.cuda.stream(stream):
         for s in range(args.warmup):
-            graphs[s % L].replay()
+            step(s)
     barrier()
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clocks:
         with torch.cuda.stream(stream):
             start.record(stream)
             for s in range(args.steps):
-                graphs[s % L].replay()
+                step(s)
             stop.record(stream)
         stop.synchronize()
     barrier()
@@ -328,7 +445,14 @@ def main():
         _lib.profile_enable(False)
         for i in range(L):
             _, ids, _ = moes[i](xs[i], rs[i], return_routing=True)
-            routing.append(ids.cpu().numpy())
+            ids_np = ids.cpu().numpy()
+            if world > 1:  # this rank streams the experts it owns, of every rank's tokens
+                per = EXPERTS // world
+                parts = [torch.empty_like(ids) for _ in range(world)]
+                dist.all_gather(parts, ids)
+                ids_np = torch.cat(parts).cpu().numpy()
+                ids_np = np.where((ids_np // per) == rank, ids_np, -1)
+            routing.append(ids_np)
     launches_per_step = sum(n for n, _ in prof.values()) / max(prof_steps, 1)
     u = unique_experts(routing)
     u_mean = sum(u) / len(u)
@@ -375,6 +499,15 @@ def main():
     h2d = 2 * T * HIDDEN * 2
     d2h = T * HIDDEN * 2
 
+    extras = {}
+    if world == 1 and not args.no_extras:
+        extras["decode_batches"] = decode_batches(layers, moes, [8, 32], min(args.steps, 200), stream)
+        bf16_peak = 1645.3
+        peaks_path = ROOT / "MEASURED_PEAKS.json"
+        if peaks_path.exists():
+            bf16_peak = float(json.loads(peaks_path.read_text()).get("bf16_tflops", bf16_peak))
+        extras["prefill"] = prefill_configs(layers[0], 10, stream, bf16_peak)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         steps_done, dt, cores = cpu_baseline(layers[0], T, args.cpu_seconds)
@@ -388,11 +521,14 @@ def main():
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": f"decode T={T}, one GLM-5-shape MoE layer (256 K4 trellis experts + bf16 shared "
-                                   f"expert, fp32 router)", "tokens": T, "hidden": HIDDEN, "intermediate": INTER,
-                       "experts": EXPERTS, "k_bits": K_BITS, "layers_cycled": L,
+            "config": {"workload": f"decode T={T} tokens per GPU, one GLM-5-shape MoE layer (256 K4 trellis experts + "
+                                   f"bf16 shared expert, fp32 router)", "tokens_per_gpu": T, "global_batch": T * world,
+                       "hidden": HIDDEN, "intermediate": INTER, "experts": EXPERTS, "k_bits": K_BITS,
+                       "layers_cycled": L,
                        "l2": "inputs larger than L2: each step is a different layer (>233 MB touched per step)",
-                       "parallelism": f"replicas x{world}" if world > 1 else "single GPU"},
+                       "parallelism": (f"expert parallel x{world}: {EXPERTS // world} routed experts per GPU, NCCL "
+                                       "all-to-all dispatch/combine, shared expert replicated") if world > 1
+                       else "single GPU"},
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "steps": e2e_steps},
             "roofline": {"bound": "hbm", "kernel": "trellis_stream_kernel<4> (gate/up)", "achieved": achieved,
@@ -407,6 +543,7 @@ def main():
             "clocks": clocks.summary(),
             "cpu_baseline": cpu,
         }
+        line.update(extras)
         print(json.dumps(line), flush=True)
     # Release graphs before tearing down the process group.
     del graphs
