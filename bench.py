@@ -25,8 +25,11 @@ cpu_baseline: the C restatement of the layer (oracle/c, OpenMP) on the host's
        (unavailable here), so the reference arm is that same CPU restatement
        of the reference's arithmetic, on all host threads.
 
-Under torchrun (N > 1) every rank runs its own layers (replicas, weak
-scaling); time is the max over ranks.
+Under torchrun (N > 1) the same layers are expert-parallel: each GPU holds
+256 / N routed experts of every layer and the replicated shared expert, takes
+T tokens of its own (global batch T * N, weak scaling), and the dispatch and
+combine are NCCL exchanges inside each layer's CUDA graph; time is the max
+over ranks.  (`--tokens 8 --gpus 8` is configs[3]'s batch of 64 per layer.)
 """
 
 from __future__ import annotations
@@ -63,12 +66,14 @@ def parse():
     p.add_argument("--impl", choices=("b200", "reference"), default="b200")
     p.add_argument("--cpu-seconds", type=float, default=10.0)
     p.add_argument("--no-cpu-baseline", action="store_true")
-    p.add_argument("--ncu-driver", choices=("layer", "mlp", "joined"), default=None,
+    p.add_argument("--ncu-driver", choices=("layer", "mlp", "joined", "trellis"), default=None,
                    help="untimed run for an ncu capture: 'layer' calls one resident layer --calls times; 'mlp' "
                         "runs the nine-expert fast_expert_mlp at full size (about 170 MB of weights); 'joined' "
                         "runs JoinedMXFP4.finish at full width over --experts experts (the last one shared) with "
                         "--tokens tokens, top-8 uniform routing (about 4 GB on the device at 129 experts and 2048 "
-                        "tokens)")
+                        "tokens); 'trellis' runs the grouped trellis prefill (expert_mlp_finish with the dense bf16 "
+                        "shared expert) over --experts K4 experts with --tokens tokens, plus the tensor-core router "
+                        "gate product")
     p.add_argument("--experts", type=int, default=129)
     p.add_argument("--no-extras", action="store_true",
                    help="skip the single-GPU extras (decode at T=8/32, the prefill configurations)")
@@ -100,6 +105,22 @@ def ncu_driver(args):
         x, r = j.tokens(t)
         for _ in range(args.calls):
             joined.finish(x, ids, scores, r)
+    elif args.ncu_driver == "trellis":
+        from mlxlr8_b200.fast_decode import expert_mlp_finish
+        from mlxlr8_b200.fast_router import router_logits
+
+        layer = make_layer(seed=1, routed=args.experts, shared="bf16")
+        e = layer.experts
+        t = args.tokens
+        g = torch.Generator(device="cuda")
+        g.manual_seed(2)
+        routed = torch.rand(t, args.experts, generator=g, device="cuda").argsort(dim=1)[:, :8].int()
+        ids = torch.cat([routed, torch.full((t, 1), 256, dtype=torch.int32, device="cuda")], dim=1)
+        scores = torch.rand(t, 8, generator=g, device="cuda")
+        x, r = layer.tokens(t)
+        for _ in range(args.calls):
+            router_logits(x, layer.gate_weight)
+            expert_mlp_finish(x, ids, scores, r, e.packed, e.scales, K_BITS, HIDDEN, INTER, shared=e.shared)
     elif args.ncu_driver == "layer":
         layer = make_layer(seed=1)
         moe = MoELayer(layer.gate_weight, layer.bias, layer.experts)
@@ -268,15 +289,19 @@ def decode_batches(layers, moes, batches, steps, stream):
     for T in batches:
         xs = [layer.tokens(T, seed_offset=50 + i) for i, layer in enumerate(layers)]
         graphs = []
+
+        def capture(i):
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=stream):
+                moes[i](*xs[i])
+            return graph
+
         with torch.cuda.stream(stream):
             for i in range(L):
                 moes[i](*xs[i])
             torch.cuda.synchronize()
             for i in range(L):
-                g = torch.cuda.CUDAGraph()
-                with torch.cuda.graph(g, stream=stream):
-                    moes[i](*xs[i])
-                graphs.append(g)
+                graphs.append(capture(i))
         state = {"s": 0}
 
         def replay():
@@ -285,7 +310,7 @@ def decode_batches(layers, moes, batches, steps, stream):
 
         ms = time_calls(replay, steps, 5, stream)
         out[f"T{T}"] = {"tokens_per_s": T / (ms / 1000.0), "ms_per_step": ms}
-        del graphs
+        graphs.clear()
     return out
 
 
@@ -381,20 +406,26 @@ def main():
         layers.append(layer)
     torch.cuda.synchronize()
 
-    # One GPU: CUDA graphs of one layer call each (inputs resident in HBM).
-    # Several GPUs: eager layer calls (the NCCL exchange runs on the stream).
+    # CUDA graphs of one layer call each (inputs resident in HBM); with several
+    # GPUs the graphs hold the NCCL exchange too.  Graph references live only
+    # in `graphs`, which is cleared before the process group goes away.
     outs, graphs = [], []
     stream = torch.cuda.Stream(device)
+
+    def capture(i):
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            outs.append(moes[i](xs[i], rs[i]))
+        return graph
+
     with torch.cuda.stream(stream):
         for i in range(L):
             moes[i](xs[i], rs[i])  # allocate the cached workspace before capture
         torch.cuda.synchronize()
-        if world == 1:
-            for i in range(L):
-                g = torch.cuda.CUDAGraph()
-                with torch.cuda.graph(g, stream=stream):
-                    outs.append(moes[i](xs[i], rs[i]))
-                graphs.append(g)
+        if world > 1:
+            dist.barrier()
+        for i in range(L):
+            graphs.append(capture(i))
     torch.cuda.synchronize()
 
     def step(s):
@@ -545,9 +576,12 @@ def main():
         }
         line.update(extras)
         print(json.dumps(line), flush=True)
-    # Release graphs before tearing down the process group.
-    del graphs
+    # Release graphs (they hold NCCL work) before tearing down the process group.
+    graphs.clear()
+    outs.clear()
+    torch.cuda.synchronize()
     if world > 1:
+        dist.barrier()
         dist.destroy_process_group()
 
 

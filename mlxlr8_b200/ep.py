@@ -54,19 +54,34 @@ def shared_trellis(layer: ExpertLayer, index: int = 256) -> ExpertLayer | None:
 
 
 class Exchange:
-    """Equal-split all-to-all over dim 0 of [world, ...] tensors."""
+    """Equal-split all-to-all over dim 0 of [world, ...] tensors.  Several
+    tensors go in one grouped set of NCCL sends and receives."""
 
-    def __init__(self, world: int, group=None):
-        self.world, self.group = world, group
+    def __init__(self, world: int, group=None, rank: int = 0):
+        self.world, self.group, self.rank = world, group, rank
 
-    def __call__(self, t: torch.Tensor) -> torch.Tensor:
+    def __call__(self, *tensors: torch.Tensor):
         if self.world == 1:
-            return t
+            return tensors[0] if len(tensors) == 1 else tensors
         import torch.distributed as dist
 
-        out = torch.empty_like(t)
-        dist.all_to_all_single(out, t.contiguous(), group=self.group)
-        return out
+        outs = [torch.empty_like(t) for t in tensors]
+        if len(tensors) == 1:
+            dist.all_to_all_single(outs[0], tensors[0].contiguous(), group=self.group)
+            return outs[0]
+        ops = []
+        for t, o in zip(tensors, outs):
+            t = t.contiguous()
+            for peer in range(self.world):
+                if peer == self.rank:
+                    o[peer].copy_(t[peer])
+                    continue
+                gpeer = peer if self.group is None else dist.get_global_rank(self.group, peer)
+                ops.append(dist.P2POp(dist.isend, t[peer], gpeer, self.group))
+                ops.append(dist.P2POp(dist.irecv, o[peer], gpeer, self.group))
+        for work in dist.batch_isend_irecv(ops):
+            work.wait()
+        return tuple(outs)
 
 
 class ExpertParallelMoE:
@@ -86,7 +101,8 @@ class ExpertParallelMoE:
         self.per_rank = routed // world
         self.shared = None if shared is None else tuple(t.contiguous() for t in shared)
         self.shared_layer = shared_layer
-        self.exchange = Exchange(world, group)
+        self.exchange = Exchange(world, group, rank)
+        self._side = None
         self._shared_struct = None
         if self.shared is not None:
             self._shared_struct, self._keep = dense_expert(self.shared)
@@ -133,14 +149,22 @@ class ExpertParallelMoE:
         _lib.check(lib.exlr8_ep_dispatch(ids.data_ptr(), tokens, xr.data_ptr(), _lib.act_code(xr), h, self.world,
                                          self.per_rank, cap, send_x.data_ptr(), send_meta.data_ptr(),
                                          slot_pos.data_ptr(), counts.data_ptr(), status.data_ptr(), stream))
-        recv_x = self.exchange(send_x)
-        recv_meta = self.exchange(send_meta)
+        # The replicated shared expert runs on a side stream, overlapping the
+        # exchange and the owner's expert products.
+        main = torch.cuda.current_stream(device)
+        if self._side is None or self._side.device != device:
+            self._side = torch.cuda.Stream(device)
+        self._side.wait_stream(main)
+        with torch.cuda.stream(self._side):
+            shared = self.shared_values(xr)
+        recv_x, recv_meta = self.exchange(send_x, send_meta)
         rows = self.world * cap
         local = self.local
         values = fast_expert_mlp(recv_x.reshape(rows, h), recv_meta.reshape(rows, 1), local.packed, local.scales,
                                  local.k, h, local.intermediate)
         back = self.exchange(values.reshape(self.world, cap, h))
-        shared = self.shared_values(xr)
+        main.wait_stream(self._side)
+        shared.record_stream(main)
         out = torch.empty_like(res)
         _lib.check(lib.exlr8_ep_combine(back.data_ptr(), _lib.act_code(xr), slot_pos.data_ptr(), scores.data_ptr(),
                                         shared.data_ptr(), res.data_ptr(), tokens, h, out.data_ptr(), stream))

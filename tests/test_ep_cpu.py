@@ -28,10 +28,14 @@ def _exchange_worker(rank, world, port, queue):
         # send[d][row] = 100 * source + 10 * destination + row
         send = torch.stack([torch.full((cap, h), 100.0 * rank + 10.0 * d) + torch.arange(cap)[:, None]
                             for d in range(world)])
-        recv = Exchange(world)(send)
-        meta = Exchange(world)(torch.full((world, cap), rank, dtype=torch.int32))
-        back = Exchange(world)(recv)
-        queue.put((rank, recv.tolist(), meta.tolist(), torch.equal(back, send)))
+        ex = Exchange(world, rank=rank)
+        recv = ex(send)
+        meta = ex(torch.full((world, cap), rank, dtype=torch.int32))
+        back = ex(recv)
+        # Two tensors in one grouped exchange (rows and their expert ids).
+        recv2, meta2 = ex(send, torch.full((world, cap), rank, dtype=torch.int32))
+        grouped = torch.equal(recv2, recv) and torch.equal(meta2, meta)
+        queue.put((rank, recv.tolist(), meta.tolist(), torch.equal(back, send) and grouped))
     finally:
         dist.destroy_process_group()
 
