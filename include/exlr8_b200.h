@@ -213,7 +213,7 @@ int exlr8_profile_read(int kind, int64_t* launches, double* total_ms);
  * EXLR8_NOALLOC_SCRATCH_BYTES inside the library (held on every GPU that
  * loads it until exit); nothing is allocated.  Requests whose
  * exlr8_moe_layer_workspace() exceeds that size return
- * EXLR8_ERR_STATIC_LIMIT (at GLM-5 size: up to 7 tokens).  The first call on
+ * EXLR8_ERR_STATIC_LIMIT (at GLM-5 size: up to 5 tokens).  The first call on
  * a device looks up the array's device address; make it before any stream
  * capture.  All calls share the array: calls that overlap on the GPU race
  * and must be serialised by the caller. */

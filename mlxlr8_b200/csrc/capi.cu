@@ -62,8 +62,8 @@ int format_status(int64_t packed_bytes, int k, int in_f, int out_f, int side, in
 // Workspace of the trellis MLP over `rows` slots.
 struct MlpLayout {
   Splits s1, s2;
-  size_t plan, counters, frag_gu, unscale_gu, gu, frag_d, unscale_d, dpart;
-  size_t total() const { return plan + counters + frag_gu + unscale_gu + gu + frag_d + unscale_d + dpart; }
+  size_t plan, frag_gu, gu, frag_d, dpart;
+  size_t total() const { return plan + frag_gu + gu + frag_d + dpart; }
 };
 
 // bf16 shared expert: K splits of the gate/up and down passes (enough warps
@@ -76,19 +76,16 @@ MlpLayout mlp_layout(int64_t rows, int hidden, int inter, int64_t experts) {
   l.s1 = gate_up_splits(hidden);
   l.s2 = down_splits(inter);
   l.plan = align_up(plan_bytes(static_cast<int>(rows), static_cast<int>(experts)));
-  l.counters = align_up((static_cast<size_t>(inter) / 64 + 1) * sizeof(int32_t));
-  l.frag_gu = align_up(2 * rows * (hidden / 16) * static_cast<size_t>(64));
-  l.unscale_gu = align_up(2 * rows * l.s1.count * sizeof(float));
+  l.frag_gu = align_up(frag_bytes(rows, hidden, 2));
   l.gu = align_up(2 * rows * l.s1.count * static_cast<size_t>(inter) * sizeof(float));
-  l.frag_d = align_up(rows * (inter / 16) * static_cast<size_t>(64));
-  l.unscale_d = align_up(rows * l.s2.count * sizeof(float));
+  l.frag_d = align_up(frag_bytes(rows, inter, 1));
   l.dpart = align_up(rows * l.s2.count * static_cast<size_t>(hidden) * sizeof(float));
   return l;
 }
 
 struct DenseLayout {
-  size_t gate, up, h, down;
-  size_t total() const { return gate + up + h + down; }
+  size_t gate, up, h, down, counters;
+  size_t total() const { return gate + up + h + down + counters; }
 };
 
 DenseLayout dense_layout(int64_t tokens, int hidden, int inter) {
@@ -97,6 +94,7 @@ DenseLayout dense_layout(int64_t tokens, int hidden, int inter) {
   l.up = l.gate;
   l.h = align_up(tokens * static_cast<size_t>(inter) * sizeof(float));
   l.down = align_up(kDenseDownSplits * tokens * static_cast<size_t>(hidden) * sizeof(float));
+  l.counters = align_up((static_cast<size_t>(inter) / 64 + 1) * sizeof(int32_t));
   return l;
 }
 
@@ -134,12 +132,9 @@ StreamParams stream_params(const exlr8_trellis_experts* ex, PlanView plan, int c
 // Buffers of one MLP call carved from the workspace.
 struct MlpBuffers {
   PlanView plan;
-  int32_t* counters;
-  uint2* frag_gu;
-  float* unscale_gu;
+  unsigned char* frag_gu;
   float* gu;
-  uint2* frag_d;
-  float* unscale_d;
+  unsigned char* frag_d;
   float* dpart;
   // dense shared expert (null when absent)
   float* dgate;
@@ -153,15 +148,10 @@ MlpBuffers carve_mlp(const MlpLayout& l, int64_t rows, int64_t experts, bool den
   MlpBuffers b{};
   const int n = static_cast<int>(rows), e = static_cast<int>(experts);
   b.plan = plan_view(c.take<int32_t>(l.plan), n, e);
-  b.counters = c.take<int32_t>(l.counters);
-  b.frag_gu = c.take<uint2>(l.frag_gu);
-  b.unscale_gu = c.take<float>(l.unscale_gu);
+  b.frag_gu = c.take<unsigned char>(l.frag_gu);
   b.gu = c.take<float>(l.gu);
-  b.frag_d = c.take<uint2>(l.frag_d);
-  b.unscale_d = c.take<float>(l.unscale_d);
+  b.frag_d = c.take<unsigned char>(l.frag_d);
   b.dpart = c.take<float>(l.dpart);
-  b.plan.zero = b.counters;
-  b.plan.zero_count = inter / 64;
   if (dense) {
     const DenseLayout dl = dense_layout(tokens, hidden, inter);
     b.dgate = c.take<float>(dl.gate);
@@ -172,23 +162,41 @@ MlpBuffers carve_mlp(const MlpLayout& l, int64_t rows, int64_t experts, bool den
   return b;
 }
 
+// The bf16 shared expert of a few tokens on its own (exlr8_shared_expert):
+// gate/up with the SwiGLU into h, then the down partials
+// [kDenseDownSplits][tokens][hidden].
+int launch_dense_decode(const void* x, int x_dtype, int64_t tokens, const exlr8_dense_expert* shared, int h, int m,
+                        float* dgate, float* dup, void* dh, float* ddown, int32_t* counters, cudaStream_t s) {
+  const int t = static_cast<int>(tokens);
+  EXLR8_TRY(cudaMemsetAsync(counters, 0, (m / 64 + 1) * sizeof(int32_t), s));
+  EXLR8_TIMED(EXLR8_KERNEL_DENSE, s,
+              launch_dense_gate_up(static_cast<const uint16_t*>(x), t, static_cast<const uint16_t*>(shared->gate),
+                                   static_cast<const uint16_t*>(shared->up), m, h, kDenseGateUpSplits, dgate, dup,
+                                   counters, x_dtype, dh, 0, s));
+  EXLR8_TIMED(EXLR8_KERNEL_DENSE, s,
+              launch_dense_gemv(static_cast<const uint16_t*>(dh), t, static_cast<const uint16_t*>(shared->down), h, m,
+                                kDenseDownSplits, ddown, 0, s));
+  return EXLR8_OK;
+}
+
 // The trellis MLP over all slots of `ids` ([rows] = tokens*slots) after the
-// plan: activation fragments, the gate/up stream (with the gate/up finish as
-// its epilogue), the down stream.  With `shared` the bf16 shared expert runs
-// as dense units of the same two kernels.  Leaves fp32 down partials.
+// plan: activation fragments, the gate/up stream, the gate/up finish into the
+// down fragments, the down stream.  Leaves fp32 down partials.  With
+// `shared` the bf16 shared expert of the `tokens` rows of x runs as dense
+// units of the two stream launches (its SwiGLU in the gate/up finish) and
+// leaves its down partials [l.s2.count][tokens][hidden] in b.ddown.
 int run_mlp_after_plan(const void* x, int x_dtype, int per_slot, int slots, const uint32_t* ids, int64_t rows,
                        const exlr8_trellis_experts* ex, int64_t experts, const exlr8_dense_expert* shared,
                        int64_t tokens, const MlpLayout& l, const MlpBuffers& b, cudaStream_t s) {
   const int h = ex->hidden, m = ex->intermediate;
-  const int n = static_cast<int>(rows), e = static_cast<int>(experts);
+  const int n = static_cast<int>(rows), e = static_cast<int>(experts), t = static_cast<int>(tokens);
   EXLR8_TIMED(EXLR8_KERNEL_PREP, s,
               launch_prep_frag(x, x_dtype, per_slot, slots, ids, n, ex->in_scale[0], ex->in_scale[1],
-                               ex->scale_dtype, h, e, 2, l.s1.kt, l.s1.count, b.frag_gu, b.unscale_gu, s));
+                               ex->scale_dtype, h, e, 2, b.frag_gu, s));
   StreamParams gp = stream_params(ex, b.plan, 2, n);
   gp.packed[0] = static_cast<const uint32_t*>(ex->packed[0]);
   gp.packed[1] = static_cast<const uint32_t*>(ex->packed[1]);
   gp.frag = b.frag_gu;
-  gp.unscale = b.unscale_gu;
   gp.partial = b.gu;
   gp.side = 1;
   gp.in_features = h;
@@ -196,26 +204,19 @@ int run_mlp_after_plan(const void* x, int x_dtype, int per_slot, int slots, cons
   gp.kt_per_split = l.s1.kt;
   gp.splits = l.s1.count;
   gp.projections = 2;
-  if (shared) {
-    EXLR8_TIMED(EXLR8_KERNEL_DENSE, s,
-                launch_dense_gate_up(static_cast<const uint16_t*>(x), static_cast<int>(tokens),
-                                     static_cast<const uint16_t*>(shared->gate),
-                                     static_cast<const uint16_t*>(shared->up), m, h, kDenseGateUpSplits, b.dgate,
-                                     b.dup, b.counters, x_dtype, b.dh, s));
-    EXLR8_TIMED(EXLR8_KERNEL_DENSE, s,
-                launch_dense_gemv(static_cast<const uint16_t*>(b.dh), static_cast<int>(tokens),
-                                  static_cast<const uint16_t*>(shared->down), h, m, kDenseDownSplits, b.ddown, s));
-  }
+  if (shared)
+    gp.dense = DenseUnits{static_cast<const uint16_t*>(shared->gate), static_cast<const uint16_t*>(shared->up),
+                          static_cast<const uint16_t*>(x), b.dgate, b.dup, m, h, t, l.s1.count,
+                          (m / 128) * l.s1.count};
   EXLR8_TIMED(EXLR8_KERNEL_GATE_UP, s, launch_stream(gp, s));
   EXLR8_TIMED(EXLR8_KERNEL_GATE_FINISH, s,
               launch_gate_finish_frag(b.gu, l.s1.count, ids, n, ex->out_scale[0], ex->out_scale[1], ex->in_scale[2],
-                                      ex->scale_dtype, m, e, x_dtype, l.s2.kt, l.s2.count, b.frag_d, b.unscale_d,
-                                      s));
+                                      ex->scale_dtype, m, e, x_dtype, b.frag_d, b.dgate, b.dup, l.s1.count,
+                                      shared ? t : 0, shared ? b.dh : nullptr, s));
   StreamParams dp = stream_params(ex, b.plan, 3, n);
   dp.packed[0] = static_cast<const uint32_t*>(ex->packed[2]);
   dp.packed[1] = nullptr;
   dp.frag = b.frag_d;
-  dp.unscale = b.unscale_d;
   dp.partial = b.dpart;
   dp.side = 2;
   dp.in_features = m;
@@ -223,6 +224,9 @@ int run_mlp_after_plan(const void* x, int x_dtype, int per_slot, int slots, cons
   dp.kt_per_split = l.s2.kt;
   dp.splits = l.s2.count;
   dp.projections = 1;
+  if (shared)
+    dp.dense = DenseUnits{static_cast<const uint16_t*>(shared->down), nullptr, static_cast<const uint16_t*>(b.dh),
+                          b.ddown, nullptr, h, m, t, l.s2.count, (h / 128) * l.s2.count};
   EXLR8_TIMED(EXLR8_KERNEL_DOWN, s, launch_stream(dp, s));
   return EXLR8_OK;
 }
@@ -486,8 +490,7 @@ size_t exlr8_expert_linear_workspace(int64_t tokens, int slots, int in_features,
   const int64_t rows = tokens * slots;
   const Splits sp = linear_splits(in_features);
   return align_up(plan_bytes(static_cast<int>(rows), static_cast<int>(experts))) +
-         align_up(rows * (in_features / 16) * static_cast<size_t>(64)) +
-         align_up(rows * sp.count * sizeof(float)) +
+         align_up(frag_bytes(rows, in_features, 1)) +
          align_up(rows * sp.count * static_cast<size_t>(out_features) * sizeof(float));
 }
 
@@ -512,18 +515,16 @@ int exlr8_expert_linear(const void* x, int x_dtype, int per_slot, const uint32_t
   const int n = static_cast<int>(rows), e = static_cast<int>(experts);
   Carver c(workspace);
   PlanView plan = plan_view(c.take<int32_t>(plan_bytes(n, e)), n, e);
-  uint2* frag = c.take<uint2>(rows * (in_features / 16) * static_cast<size_t>(64));
-  float* unscale = c.take<float>(rows * sp.count * sizeof(float));
+  unsigned char* frag = c.take<unsigned char>(frag_bytes(rows, in_features, 1));
   float* part = c.take<float>(rows * sp.count * static_cast<size_t>(out_features) * sizeof(float));
   EXLR8_TRY(launch_plan(indices, n, e, slots, -1, plan, s));
   EXLR8_TRY(launch_prep_frag(x, x_dtype, per_slot, slots, indices, n, in_scale, in_scale, scale_dtype, in_features, e,
-                             1, sp.kt, sp.count, frag, unscale, s));
+                             1, frag, s));
   StreamParams gp = stream_params(nullptr, plan, 2, n);
   gp.k = k;
   gp.packed[0] = static_cast<const uint32_t*>(packed);
   gp.packed[1] = nullptr;
   gp.frag = frag;
-  gp.unscale = unscale;
   gp.partial = part;
   gp.side = sharded_side;
   gp.in_features = in_features;
@@ -607,7 +608,7 @@ static int mlp_finish_after_plan(const void* x, int x_dtype, const uint32_t* ind
   ProfileScope scope(EXLR8_KERNEL_FINISH, s);
   return cuda_status(launch_finish_fused(b.dpart, l.s2.count, nullptr, indices, static_cast<int>(tokens), ex->out_scale[2],
                                          ex->scale_dtype, ex->hidden, static_cast<int>(experts), scores, residual,
-                                         shared ? b.ddown : nullptr, kDenseDownSplits, x_dtype, out, s));
+                                         shared ? b.ddown : nullptr, l.s2.count, x_dtype, out, s));
 }
 
 int exlr8_expert_mlp_finish(const void* x, int x_dtype, const uint32_t* indices, const float* scores,
@@ -761,7 +762,7 @@ int exlr8_ep_combine(const void* values, int x_dtype, const int32_t* slot_pos, c
 size_t exlr8_shared_expert_workspace(int64_t tokens, int hidden, int intermediate) {
   if (tokens <= 0) return 0;
   if (tokens < kPrefillMinTokens)
-    return dense_layout(tokens, hidden, intermediate).total() + align_up((intermediate / 64 + 1) * sizeof(int32_t));
+    return dense_layout(tokens, hidden, intermediate).total();
   const int t = static_cast<int>(tokens);
   const size_t sgu = bf16_gemm_splits(t, hidden, intermediate), sd = bf16_gemm_splits(t, intermediate, hidden);
   return 2 * align_up(sgu * tokens * intermediate * sizeof(float)) + align_up(tokens * intermediate * 2) +
@@ -792,15 +793,8 @@ int exlr8_shared_expert(const void* x, int x_dtype, int64_t tokens, int hidden, 
     float* du = c.take<float>(dl.up);
     void* dh = c.take<void>(dl.h);
     float* dd = c.take<float>(dl.down);
-    int32_t* counters = c.take<int32_t>((intermediate / 64 + 1) * sizeof(int32_t));
-    EXLR8_TRY(cudaMemsetAsync(counters, 0, (intermediate / 64 + 1) * sizeof(int32_t), s));
-    EXLR8_TIMED(EXLR8_KERNEL_DENSE, s,
-                launch_dense_gate_up(xb, t, static_cast<const uint16_t*>(shared->gate),
-                                     static_cast<const uint16_t*>(shared->up), intermediate, hidden,
-                                     kDenseGateUpSplits, dg, du, counters, x_dtype, dh, s));
-    EXLR8_TIMED(EXLR8_KERNEL_DENSE, s,
-                launch_dense_gemv(static_cast<const uint16_t*>(dh), t, static_cast<const uint16_t*>(shared->down),
-                                  hidden, intermediate, kDenseDownSplits, dd, s));
+    int32_t* counters = c.take<int32_t>(dl.counters);
+    EXLR8_CHECK(launch_dense_decode(x, x_dtype, tokens, shared, hidden, intermediate, dg, du, dh, dd, counters, s));
     return cuda_status(launch_sum_cast(dd, kDenseDownSplits, tokens * hidden, x_dtype, out, s));
   }
   const int sgu = bf16_gemm_splits(t, hidden, intermediate), sd = bf16_gemm_splits(t, intermediate, hidden);

@@ -114,7 +114,9 @@ cudaError_t launch_dequantize(const float* inner, const void* suh, const void* s
 
 constexpr int kDenseWarps = 4;
 
-// Gate and up products in one pass over x, split along k; the CTA that
+// Gate and up products in one pass over x, split along k.  Work items are
+// (64-row block, split), taken in a grid-stride loop so that the grid can be
+// capped (one CTA per SM runs beside the trellis stream kernel); the CTA that
 // completes the last split of a 64-row block writes h = SwiGLU(T(g), T(u))
 // for it.  `counters` ([n/64]) must be zero at launch.
 __global__ void __launch_bounds__(kDenseWarps * 32) dense_gate_up_kernel(
@@ -123,63 +125,74 @@ __global__ void __launch_bounds__(kDenseWarps * 32) dense_gate_up_kernel(
     int act_dtype, void* __restrict__ h) {
   __shared__ int s_last;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int n0 = (blockIdx.x * kDenseWarps + warp) * 16;
-  const int split = blockIdx.y;
+  const int row_blocks = (n / 16 + kDenseWarps - 1) / kDenseWarps;
   const int steps = k / 32;
   const int per = (steps + splits - 1) / splits;
-  const int s0 = split * per, s1 = min(s0 + per, steps);
   const int64_t total = static_cast<int64_t>(tokens) * n;
-  if (n0 < n) dense_rows(x, tokens, wg, wu, n, k, n0, s0, s1, gp + split * total, up + split * total, lane);
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    __threadfence();
-    s_last = atomicAdd(&counters[blockIdx.x], 1) == splits - 1;
-  }
-  __syncthreads();
-  if (!s_last) return;
-  __threadfence();
-  const int rows = min(kDenseWarps * 16, n - static_cast<int>(blockIdx.x) * kDenseWarps * 16);
-  for (int idx = threadIdx.x; idx < tokens * rows; idx += blockDim.x) {
-    const int t = idx / rows;
-    const int64_t i = static_cast<int64_t>(t) * n + blockIdx.x * kDenseWarps * 16 + idx % rows;
-    float g = 0.f, u = 0.f;
-#pragma unroll 8
-    for (int sp = 0; sp < splits; ++sp) {
-      g += __ldcg(gp + sp * total + i);
-      u += __ldcg(up + sp * total + i);
+  for (int item = blockIdx.x; item < row_blocks * splits; item += gridDim.x) {
+    const int rb = item % row_blocks, split = item / row_blocks;
+    const int n0 = (rb * kDenseWarps + warp) * 16;
+    const int s0 = split * per, s1 = min(s0 + per, steps);
+    if (n0 < n) dense_rows(x, tokens, wg, wu, n, k, n0, s0, s1, gp + split * total, up + split * total, lane);
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      __threadfence();
+      s_last = atomicAdd(&counters[rb], 1) == splits - 1;
     }
-    store_act(h, act_dtype, i, swiglu_typed(act_dtype, g, u));
+    __syncthreads();
+    if (s_last) {
+      __threadfence();
+      const int rows = min(kDenseWarps * 16, n - rb * kDenseWarps * 16);
+      for (int idx = threadIdx.x; idx < tokens * rows; idx += blockDim.x) {
+        const int t = idx / rows;
+        const int64_t i = static_cast<int64_t>(t) * n + rb * kDenseWarps * 16 + idx % rows;
+        float g = 0.f, u = 0.f;
+#pragma unroll 8
+        for (int sp = 0; sp < splits; ++sp) {
+          g += __ldcg(gp + sp * total + i);
+          u += __ldcg(up + sp * total + i);
+        }
+        store_act(h, act_dtype, i, swiglu_typed(act_dtype, g, u));
+      }
+    }
+    __syncthreads();  // s_last is rewritten by the next item
   }
 }
+
+static int capped_grid(int items, int max_ctas) { return max_ctas > 0 && items > max_ctas ? max_ctas : items; }
 
 cudaError_t launch_dense_gate_up(const uint16_t* x, int tokens, const uint16_t* wg, const uint16_t* wu, int n, int k,
                                  int splits, float* gate_partial, float* up_partial, int* counters, int act_dtype,
-                                 void* h, cudaStream_t s) {
-  dim3 grid((n / 16 + kDenseWarps - 1) / kDenseWarps, splits);
-  dense_gate_up_kernel<<<grid, kDenseWarps * 32, 0, s>>>(x, tokens, wg, wu, n, k, splits, gate_partial, up_partial,
-                                                          counters, act_dtype, h);
+                                 void* h, int max_ctas, cudaStream_t s) {
+  const int items = (n / 16 + kDenseWarps - 1) / kDenseWarps * splits;
+  dense_gate_up_kernel<<<capped_grid(items, max_ctas), kDenseWarps * 32, 0, s>>>(
+      x, tokens, wg, wu, n, k, splits, gate_partial, up_partial, counters, act_dtype, h);
   return cudaGetLastError();
 }
 
-// y partials [splits][tokens][n] of x @ W^T, W bf16 [n][k].
+// y partials [splits][tokens][n] of x @ W^T, W bf16 [n][k]; items are
+// (64-row block, split) in a grid-stride loop.
 __global__ void __launch_bounds__(kDenseWarps * 32) dense_gemv_kernel(const uint16_t* __restrict__ x, int tokens,
                                                                       const uint16_t* __restrict__ w, int n, int k,
                                                                       int splits, float* __restrict__ partial) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int n0 = (blockIdx.x * kDenseWarps + warp) * 16;
-  if (n0 >= n) return;
-  const int split = blockIdx.y;
+  const int row_blocks = (n / 16 + kDenseWarps - 1) / kDenseWarps;
   const int steps = k / 32;
   const int per = (steps + splits - 1) / splits;
-  const int s0 = split * per, s1 = min(s0 + per, steps);
-  dense_rows(x, tokens, w, nullptr, n, k, n0, s0, s1, partial + split * static_cast<int64_t>(tokens) * n, nullptr,
-             lane);
+  for (int item = blockIdx.x; item < row_blocks * splits; item += gridDim.x) {
+    const int rb = item % row_blocks, split = item / row_blocks;
+    const int n0 = (rb * kDenseWarps + warp) * 16;
+    if (n0 >= n) continue;
+    const int s0 = split * per, s1 = min(s0 + per, steps);
+    dense_rows(x, tokens, w, nullptr, n, k, n0, s0, s1, partial + split * static_cast<int64_t>(tokens) * n, nullptr,
+               lane);
+  }
 }
 
 cudaError_t launch_dense_gemv(const uint16_t* x, int tokens, const uint16_t* w, int n, int k, int splits,
-                              float* partial, cudaStream_t s) {
-  dim3 grid((n / 16 + kDenseWarps - 1) / kDenseWarps, splits);
-  dense_gemv_kernel<<<grid, kDenseWarps * 32, 0, s>>>(x, tokens, w, n, k, splits, partial);
+                              float* partial, int max_ctas, cudaStream_t s) {
+  const int items = (n / 16 + kDenseWarps - 1) / kDenseWarps * splits;
+  dense_gemv_kernel<<<capped_grid(items, max_ctas), kDenseWarps * 32, 0, s>>>(x, tokens, w, n, k, splits, partial);
   return cudaGetLastError();
 }
 

@@ -15,10 +15,11 @@ cudaError_t launch_dequantize(const float* inner, const void* suh, const void* s
 // bf16 shared expert.  Gate and up in one pass, the last CTA of each 64-row
 // block writing h = SwiGLU(T(g), T(u)) in the activation type; `counters`
 // ([n/64] ints) must be zero at launch.  Partials are [splits][tokens][n].
+// max_ctas > 0 caps the grid (the kernels loop over their work items).
 cudaError_t launch_dense_gate_up(const uint16_t* x, int tokens, const uint16_t* wg, const uint16_t* wu, int n, int k,
                                  int splits, float* gate_partial, float* up_partial, int* counters, int act_dtype,
-                                 void* h, cudaStream_t s);
+                                 void* h, int max_ctas, cudaStream_t s);
 cudaError_t launch_dense_gemv(const uint16_t* x, int tokens, const uint16_t* w, int n, int k, int splits,
-                              float* partial, cudaStream_t s);
+                              float* partial, int max_ctas, cudaStream_t s);
 
 }  // namespace exlr8

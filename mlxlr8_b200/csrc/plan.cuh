@@ -108,4 +108,70 @@ __device__ __forceinline__ void plan_body(const uint32_t* __restrict__ ids, int 
   }
 }
 
+// Plan of at most kSmallPlanRows slots (decode batches) whose ids are already
+// in shared memory: one thread per slot ranks it by (expert id, slot) against
+// every other slot, so the sort needs no global round trip.  Produces the
+// same order, groups and header as plan_body (the per-expert counts and
+// starts, which only the prefill path reads, are not written).  `scratch`
+// holds 4 * rows ints of shared memory.
+constexpr int kSmallPlanRows = 256;
+
+__device__ __forceinline__ void small_plan_body(const uint32_t* s_ids, int rows, int experts, int period,
+                                                int skip_slot, PlanView plan, int* scratch) {
+  __shared__ int s_bad, s_groups;
+  uint32_t* key = reinterpret_cast<uint32_t*>(scratch);
+  int* rank = scratch + rows;
+  int* within = rank + rows;
+  int* count = within + rows;
+  const int tid = threadIdx.x;
+  if (tid == 0) {
+    s_bad = 0;
+    s_groups = 0;
+  }
+  for (int i = tid; i < rows; i += blockDim.x) {
+    const uint32_t e = s_ids[i];
+    const bool skipped = skip_slot >= 0 && i % period == skip_slot;
+    key[i] = !skipped && e < static_cast<uint32_t>(experts) ? e : 0xFFFFFFFFu;
+  }
+  __syncthreads();
+  for (int i = tid; i < rows; i += blockDim.x) {
+    const uint32_t k = key[i];
+    if (k == 0xFFFFFFFFu) {
+      if (!(skip_slot >= 0 && i % period == skip_slot)) atomicAdd(&s_bad, 1);
+      continue;
+    }
+    int r = 0, w = 0, c = 0;
+    for (int j = 0; j < rows; ++j) {
+      const uint32_t kj = key[j];
+      r += kj < k || (kj == k && j < i);
+      w += kj == k && j < i;
+      c += kj == k;
+    }
+    rank[i] = r;
+    within[i] = w;
+    count[i] = c;
+    plan.order[r] = i;
+  }
+  __syncthreads();
+  for (int i = tid; i < rows; i += blockDim.x) {
+    const uint32_t k = key[i];
+    if (k == 0xFFFFFFFFu || within[i] % kMaxGroupRows != 0) continue;
+    int g = within[i] / kMaxGroupRows;  // groups of this expert before this one
+    for (int j = 0; j < rows; ++j)      // plus every group of the smaller ids
+      if (key[j] < k && within[j] == 0) g += (count[j] + kMaxGroupRows - 1) / kMaxGroupRows;
+    plan.group_expert[g] = static_cast<int>(k);
+    plan.group_start[g] = rank[i];
+    plan.group_count[g] = min(kMaxGroupRows, count[i] - within[i]);
+    atomicAdd(&s_groups, 1);
+  }
+  __syncthreads();
+  if (tid == 0) {
+    plan.header[0] = s_groups;
+    plan.header[1] = rows;
+    for (int c = 2; c < 8; ++c) plan.header[c] = 0;
+    plan.header[8] = s_bad;
+    plan.header[9] = 0;
+  }
+}
+
 }  // namespace exlr8

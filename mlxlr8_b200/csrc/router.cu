@@ -2,6 +2,8 @@
 // selection with renormalisation (exlr8 fast_router.metal:1-42,
 // model.py:111-132).
 
+#include <cuda/atomic>
+
 #include "common.cuh"
 #include "router.cuh"
 #include "plan.cuh"
@@ -94,10 +96,14 @@ cudaError_t launch_gate_logits(const void* x, int x_dtype, int tokens, int hidde
 // Selection for one row of 256 logits by one warp.  Lane l owns experts
 // i*32 + l.  Each of the eight rounds takes the largest remaining
 // sigmoid(l)+bias (lowest expert id on a tie), records its sigmoid, and
-// removes it.  Weights are divided by 1e-20 + their sum (accumulated in rank
-// order) and multiplied by `scale`; slot 8 holds the shared expert id.
+// removes it; lane r keeps the round-r winner.  Weights are divided by
+// 1e-20 + their sum (accumulated in rank order) and multiplied by `scale`;
+// slot 8 holds the shared expert id.  With `ids_copy` the nine ids are also
+// written there (shared memory).  The rounds stay a loop: the routing runs
+// once per launch on one SM, where straight-line code would be fetched cold.
 __device__ __forceinline__ void route_warp(const float* logits, const float* __restrict__ bias, uint32_t* ids,
-                                           float* scores, float scale, uint32_t shared_id, int lane) {
+                                           float* scores, float scale, uint32_t shared_id, int lane,
+                                           uint32_t* ids_copy = nullptr) {
   float original[8], choice[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
@@ -105,9 +111,9 @@ __device__ __forceinline__ void route_warp(const float* logits, const float* __r
     original[i] = sigmoid_select(__ldcg(logits + e));
     choice[i] = __fadd_rn(original[i], bias[e]);
   }
-  float selected[8];
-  uint32_t winners[8];
-#pragma unroll
+  float my_selected = 0.0f;
+  uint32_t my_winner = 0u;
+#pragma unroll 1
   for (int rank = 0; rank < 8; ++rank) {
     float best = -INFINITY;
     uint32_t index = 256u;
@@ -128,24 +134,27 @@ __device__ __forceinline__ void route_warp(const float* logits, const float* __r
 #pragma unroll
     for (int i = 1; i < 8; ++i)
       if (i == slot) mine = original[i];
-    selected[rank] = __shfl_sync(0xffffffffu, mine, winner & 31);
-    winners[rank] = winner;
+    const float selected = __shfl_sync(0xffffffffu, mine, winner & 31);
+    if (lane == rank) {
+      my_selected = selected;
+      my_winner = winner;
+    }
     if (lane == static_cast<int>(winner & 31)) {
 #pragma unroll
       for (int i = 0; i < 8; ++i)
         if (i == slot) choice[i] = -INFINITY;
     }
   }
-  if (lane == 0) {
-    float total = 1e-20f;
+  float total = 1e-20f;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) total = __fadd_rn(total, selected[i]);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      ids[i] = winners[i];
-      scores[i] = __fmul_rn(__fdiv_rn(selected[i], total), scale);
-    }
+  for (int r = 0; r < 8; ++r) total = __fadd_rn(total, __shfl_sync(0xffffffffu, my_selected, r));
+  if (lane < 8) {
+    ids[lane] = my_winner;
+    scores[lane] = __fmul_rn(__fdiv_rn(my_selected, total), scale);
+    if (ids_copy) ids_copy[lane] = my_winner;
+  } else if (lane == 8) {
     ids[8] = shared_id;
+    if (ids_copy) ids_copy[8] = shared_id;
   }
 }
 
@@ -219,23 +228,38 @@ __global__ void __launch_bounds__(kGateWarps * 32) router_plan_kernel(
     }
     __syncthreads();
   }
-  __threadfence();
-  __syncthreads();
-  if (threadIdx.x == 0) s_last = atomicAdd(done, 1) == static_cast<int>(gridDim.x) - 1;
+  // The barrier orders this CTA's logit stores before thread 0's
+  // acquire-release arrival; the last CTA's arrival acquires every other
+  // CTA's stores, and its barrier passes them on to its threads.
+  if (threadIdx.x == 0) {
+    cuda::atomic_ref<int, cuda::thread_scope_device> arrivals(*done);
+    s_last = arrivals.fetch_add(1, cuda::memory_order_acq_rel) == static_cast<int>(gridDim.x) - 1;
+  }
   __syncthreads();
   if (!s_last) return;
-  __threadfence();
+  const int rows = tokens * 9;
+  if (rows <= kSmallPlanRows) {
+    // Decode batches: the ids stay in shared memory for the plan.
+    uint32_t* s_ids = reinterpret_cast<uint32_t*>(sm);
+    for (int t = warp; t < tokens; t += kGateWarps)
+      route_warp(logits + static_cast<int64_t>(t) * 256, bias, ids + static_cast<int64_t>(t) * 9,
+                 scores + static_cast<int64_t>(t) * 8, 2.5f, 256u, lane, s_ids + t * 9);
+    __syncthreads();
+    small_plan_body(s_ids, rows, plan_experts, 9, skip_slot, plan, sm + rows);
+    return;
+  }
   for (int t = warp; t < tokens; t += kGateWarps)
     route_warp(logits + static_cast<int64_t>(t) * 256, bias, ids + static_cast<int64_t>(t) * 9,
                scores + static_cast<int64_t>(t) * 8, 2.5f, 256u, lane);
   __syncthreads();
-  plan_body(ids, tokens * 9, plan_experts, 9, skip_slot, plan, sm);
+  plan_body(ids, rows, plan_experts, 9, skip_slot, plan, sm);
 }
 
 cudaError_t launch_router_plan(const void* x, int x_dtype, int tokens, int hidden, const float* wg, float* logits,
                                const float* bias, uint32_t* ids, float* scores, int* done, int plan_experts,
                                int skip_slot, PlanView plan, cudaStream_t s) {
-  const size_t smem = plan_smem_bytes(plan_experts, kGateWarps);
+  size_t smem = plan_smem_bytes(plan_experts, kGateWarps);
+  if (smem < 5 * kSmallPlanRows * sizeof(int)) smem = 5 * kSmallPlanRows * sizeof(int);
   if (smem > 48 * 1024) {
     cudaError_t err = cudaFuncSetAttribute(router_plan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                            static_cast<int>(smem));

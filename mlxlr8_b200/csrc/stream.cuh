@@ -8,17 +8,41 @@
 
 namespace exlr8 {
 
-// Activation fragments: for every (projection, slot, K tile) 64 bytes =
-// [piece hi/lo][tig 0..3] uint2, the mma.sync m16n8k16 B-fragment words of
-// one row: {x[2t], x[2t+1]} and {x[2t+8], x[2t+9]} as float16 pieces.  Each
-// (projection, slot, K split) has one power-of-two scale; `unscale` holds its
-// inverse.
+// Activation fragments: one 528-byte record per (projection, slot, 128-wide
+// K block): eight K tiles of 64 bytes -- [piece hi/lo][tig 0..3] uint2, the
+// mma.sync m16n8k16 B-fragment words of one row, {x[2t], x[2t+1]} and
+// {x[2t+8], x[2t+9]} as float16 pieces of the block's values times 2^-ex --
+// then a 16-byte header whose first float is the block's unscale 2^ex.  The
+// power-of-two scale is chosen per block (the scaled block maximum lies in
+// [2^14, 2^15)), so every block is produced independently.
+constexpr int kFragBlockBytes = 8 * 64 + 16;
+
+inline size_t frag_bytes(int64_t rows, int features, int projections) {
+  return static_cast<size_t>(projections) * static_cast<size_t>(rows) * static_cast<size_t>(features / 128) *
+         kFragBlockBytes;
+}
+
+// The bf16 shared expert rides along as dense units: units [0, units) of a
+// launch are dense, the trellis units follow.  A dense unit is (128-row block
+// of W, K split); each consumer warp streams 16 rows of W (and of W1, which
+// shares the x loads) with 128-bit loads straight from global memory and
+// writes float32 partials [splits][tokens][n].  The HBM-bound dense rows thus
+// overlap the trellis units, which are bound by their decode arithmetic.
+struct DenseUnits {
+  const uint16_t* w0;  // [n][k] bf16 (gate, or down)
+  const uint16_t* w1;  // [n][k] bf16 (up) or null
+  const uint16_t* x;   // [tokens][k] bf16
+  float* p0;           // [splits][tokens][n] partials of w0
+  float* p1;           // same for w1
+  int n, k, tokens, splits, units;  // units = (n / 128) * splits, 0 = none
+};
+
 struct StreamParams {
   const uint32_t* packed[2];
-  const uint2* frag;     // [proj][nslots][in_tiles][8]
-  const float* unscale;  // [proj][nslots][splits]
-  float* partial;        // [proj][nslots][splits][out_features]
+  const unsigned char* frag;  // [proj][nslots][in_features / 128] records of kFragBlockBytes
+  float* partial;             // [proj][nslots][splits][out_features]
   PlanView plan;
+  DenseUnits dense;
   int counter;
   int k, side, in_features, out_features, kt_per_split, splits, projections, nslots;
   uint32_t unit16;  // 65536
@@ -37,17 +61,22 @@ inline int split_count(int in_features, int per) { return (in_features / 16 + pe
 
 cudaError_t launch_stream(const StreamParams& p, cudaStream_t s);
 
-// xh = H(x[row] * in_scale_p[e]) written as fragments + unscales
-// (metal/fast_decode_prep.metal).
+// xh = H(x[row] * in_scale_p[e]) written as fragment records
+// (metal/fast_decode_prep.metal).  frag holds frag_bytes(nslots, features,
+// projections).
 cudaError_t launch_prep_frag(const void* x, int x_dtype, int per_slot, int slots_per_token, const uint32_t* ids,
                              int nslots, const void* in0, const void* in1, int scale_dtype, int features, int experts,
-                             int projections, int kt_split, int splits, uint2* frag, float* unscale, cudaStream_t s);
+                             int projections, unsigned char* frag, cudaStream_t s);
 
 // gate/up finish (metal/fast_decode_gate_finish.metal) producing the down
-// projection's fragments + unscales.
+// projection's fragment records (frag_bytes(nslots, features, 1)).  With
+// dense_tokens > 0 it also writes the bf16 shared expert's
+// h = SwiGLU(T(g), T(u)) [dense_tokens][features] (activation type) from its
+// split partials dense_g/dense_u [dense_splits][dense_tokens][features].
 cudaError_t launch_gate_finish_frag(const float* partial, int gu_splits, const uint32_t* ids, int nslots,
                                     const void* out_gate, const void* out_up, const void* in_down, int scale_dtype,
-                                    int features, int experts, int act_dtype, int kt_split, int splits, uint2* frag,
-                                    float* unscale, cudaStream_t s);
+                                    int features, int experts, int act_dtype, unsigned char* frag,
+                                    const float* dense_g, const float* dense_u, int dense_splits, int dense_tokens,
+                                    void* dense_h, cudaStream_t s);
 
 }  // namespace exlr8

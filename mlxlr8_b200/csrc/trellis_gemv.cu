@@ -77,13 +77,13 @@ cudaError_t launch_plan(const uint32_t* ids, int rows, int experts, int period, 
 }
 
 // ---------------------------------------------------------------------------
-// Activation fragments.  One CTA per (K split, slot, projection): the split's
-// 128-wide blocks are transformed into shared memory, the split maximum picks
-// a power-of-two scale, and the scaled values are written as float16 hi/lo
-// B fragments (see stream.cuh).
+// Activation fragments.  One warp per (projection, slot, 128-wide block):
+// the block is transformed in registers, its maximum picks a power-of-two
+// scale, and the scaled values are written as a float16 hi/lo fragment record
+// (see stream.cuh) with the block's unscale in the record header.
 // ---------------------------------------------------------------------------
 
-constexpr int kFragThreads = 256;
+constexpr int kFragWarps = 4;
 
 __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
   __half2 h = __floats2half2_rn(lo, hi);
@@ -95,7 +95,7 @@ __device__ __forceinline__ float split_piece(float v, int piece) {
   return piece ? v - hi : hi;
 }
 
-// Scale exponent for a split maximum: the scaled maximum lies in [2^14, 2^15).
+// Scale exponent for a block maximum: the scaled maximum lies in [2^14, 2^15).
 __device__ __forceinline__ int piece_exponent(float m) {
   int ex = 0;
   if (m > 0.0f && m < 3.0e38f) {
@@ -105,155 +105,175 @@ __device__ __forceinline__ int piece_exponent(float m) {
   return ex;
 }
 
-// vals: the split's transformed values (kt_count*16 floats) in shared memory.
-__device__ __forceinline__ void write_fragments(const float* vals, int kt_count, float scale, uint2* dst) {
-  for (int idx = threadIdx.x; idx < kt_count * 8; idx += blockDim.x) {
-    const int ktl = idx >> 3, piece = (idx >> 2) & 1, tig = idx & 3;
-    const float* v = vals + ktl * 16;
-    uint2 b;
-    b.x = pack_half2(split_piece(v[2 * tig] * scale, piece), split_piece(v[2 * tig + 1] * scale, piece));
-    b.y = pack_half2(split_piece(v[2 * tig + 8] * scale, piece), split_piece(v[2 * tig + 9] * scale, piece));
-    dst[idx] = b;
+// v: the warp's transformed block (lane l holds element l + 32j); stage: 128
+// floats of this warp's shared memory; dst: the block's fragment record.
+__device__ __forceinline__ void write_block_record(const float v[4], float* stage, int lane, unsigned char* dst) {
+  float m = 0.0f;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    stage[lane + 32 * j] = v[j];
+    m = fmaxf(m, fabsf(v[j]));
   }
-}
-
-__device__ __forceinline__ float block_max(float m, float* red) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
-  if (lane == 0) red[warp] = m;
-  __syncthreads();
-  float r = 0.0f;
-  for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) r = fmaxf(r, red[w]);
-  return r;
+  const int ex = piece_exponent(m);
+  const float scale = ldexpf(1.0f, -ex);
+  __syncwarp();
+  uint2* out = reinterpret_cast<uint2*>(dst);
+#pragma unroll
+  for (int q = 0; q < 2; ++q) {
+    const int idx = lane + 32 * q;
+    const int ktl = idx >> 3, piece = (idx >> 2) & 1, tig = idx & 3;
+    const float* w = stage + ktl * 16;
+    uint2 b;
+    b.x = pack_half2(split_piece(w[2 * tig] * scale, piece), split_piece(w[2 * tig + 1] * scale, piece));
+    b.y = pack_half2(split_piece(w[2 * tig + 8] * scale, piece), split_piece(w[2 * tig + 9] * scale, piece));
+    out[idx] = b;
+  }
+  if (lane < 4) reinterpret_cast<float*>(dst + 512)[lane] = lane == 0 ? ldexpf(1.0f, ex) : 0.0f;
+  __syncwarp();
 }
 
-__global__ void __launch_bounds__(kFragThreads) prep_frag_kernel(
+__global__ void __launch_bounds__(kFragWarps * 32) prep_frag_kernel(
     const void* __restrict__ x, int x_dtype, int per_slot, int slots_per_token, const uint32_t* __restrict__ ids,
     int nslots, const void* __restrict__ in0, const void* __restrict__ in1, int scale_dtype, int features,
-    int experts, int kt_split, int splits, uint2* __restrict__ frag, float* __restrict__ unscale) {
-  extern __shared__ float vals[];
-  __shared__ float red[kFragThreads / 32];
-  const int split = blockIdx.x, slot = blockIdx.y, proj = blockIdx.z;
+    int experts, int projections, unsigned char* __restrict__ frag) {
+  __shared__ float stage[kFragWarps][128];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int it = features / 16;
-  const int kt0 = split * kt_split;
-  const int kt_count = min(kt_split, it - kt0);
+  const int blocks = features / 128;
+  const int64_t task = static_cast<int64_t>(blockIdx.x) * kFragWarps + warp;  // (proj * nslots + slot) * blocks + b
+  if (task >= static_cast<int64_t>(projections) * nslots * blocks) return;
+  const int b = static_cast<int>(task % blocks);
+  const int64_t ps = task / blocks;
+  const int slot = static_cast<int>(ps % nslots), proj = static_cast<int>(ps / nslots);
+  const int64_t row = per_slot ? slot : slot / slots_per_token;
+  const int c0 = b * 128 + lane;
+  float xv[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) xv[j] = load_act(x, x_dtype, row * features + c0 + 32 * j);
   const uint32_t e = ids[slot];
   const bool ok = e < static_cast<uint32_t>(experts);
-  const int64_t row = per_slot ? slot : slot / slots_per_token;
   const void* scale = proj ? in1 : in0;
-  float m = 0.0f;
-  for (int b = warp; b < kt_count / 8; b += kFragThreads / 32) {
-    const int c0 = kt0 * 16 + b * 128;
-    float v[4];
+  float v[4];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int col = c0 + lane + 32 * j;
-      v[j] = ok ? __fmul_rn(load_act(x, x_dtype, row * features + col),
-                            load_scale(scale, scale_dtype, static_cast<int64_t>(e) * features + col))
-                : 0.0f;
-    }
-    hadamard128(v, lane);
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      vals[b * 128 + lane + 32 * j] = v[j];
-      m = fmaxf(m, fabsf(v[j]));
-    }
-  }
-  const float mx = block_max(m, red);  // contains the barrier that publishes vals
-  const int ex = piece_exponent(mx);
-  const int64_t rbase = static_cast<int64_t>(proj) * nslots + slot;
-  write_fragments(vals, kt_count, ldexpf(1.0f, -ex), frag + (rbase * it + kt0) * 8);
-  if (threadIdx.x == 0) unscale[rbase * splits + split] = ldexpf(1.0f, ex);
+  for (int j = 0; j < 4; ++j)
+    v[j] = ok ? __fmul_rn(xv[j], load_scale(scale, scale_dtype, static_cast<int64_t>(e) * features + c0 + 32 * j))
+              : 0.0f;
+  hadamard128(v, lane);
+  write_block_record(v, stage[warp], lane, frag + task * kFragBlockBytes);
 }
 
 cudaError_t launch_prep_frag(const void* x, int x_dtype, int per_slot, int slots_per_token, const uint32_t* ids,
                              int nslots, const void* in0, const void* in1, int scale_dtype, int features, int experts,
-                             int projections, int kt_split, int splits, uint2* frag, float* unscale, cudaStream_t s) {
-  const size_t smem = static_cast<size_t>(kt_split) * 16 * sizeof(float);
-  if (smem > 48 * 1024) {
-    cudaError_t err =
-        cudaFuncSetAttribute(prep_frag_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-    if (err != cudaSuccess) return err;
-  }
-  dim3 grid(splits, nslots, projections);
-  prep_frag_kernel<<<grid, kFragThreads, smem, s>>>(x, x_dtype, per_slot, slots_per_token, ids, nslots, in0, in1,
-                                                     scale_dtype, features, experts, kt_split, splits, frag, unscale);
+                             int projections, unsigned char* frag, cudaStream_t s) {
+  const int64_t tasks = static_cast<int64_t>(projections) * nslots * (features / 128);
+  if (tasks == 0) return cudaSuccess;
+  const int64_t grid = (tasks + kFragWarps - 1) / kFragWarps;
+  prep_frag_kernel<<<static_cast<unsigned>(grid), kFragWarps * 32, 0, s>>>(
+      x, x_dtype, per_slot, slots_per_token, ids, nslots, in0, in1, scale_dtype, features, experts, projections, frag);
   return cudaGetLastError();
 }
 
 // gate/up split sum, Hadamard, output scales, typed SwiGLU, down input scale,
-// Hadamard -> down fragments.  One CTA per (down K split, slot).
-__global__ void __launch_bounds__(kFragThreads) gate_finish_frag_kernel(
+// Hadamard -> down fragment record.  One warp per (slot, 128-wide block of
+// the intermediate features).  All split partials of a warp are loaded
+// before the first add (one round trip; they do not depend on the expert id)
+// and summed in split order.  Warps past the slots' blocks form the bf16
+// shared expert's h = SwiGLU(T(g), T(u)), one per (token, 128-wide block).
+constexpr int kGateFinishSplits = 8;  // splits loaded per round trip
+
+__global__ void __launch_bounds__(kFragWarps * 32) gate_finish_frag_kernel(
     const float* __restrict__ partial, int gu_splits, const uint32_t* __restrict__ ids, int nslots,
     const void* __restrict__ out_gate, const void* __restrict__ out_up, const void* __restrict__ in_down,
-    int scale_dtype, int features, int experts, int act_dtype, int kt_split, int splits, uint2* __restrict__ frag,
-    float* __restrict__ unscale) {
-  extern __shared__ float vals[];
-  __shared__ float red[kFragThreads / 32];
-  const int split = blockIdx.x, slot = blockIdx.y;
+    int scale_dtype, int features, int experts, int act_dtype, unsigned char* __restrict__ frag,
+    const float* __restrict__ dense_g, const float* __restrict__ dense_u, int dense_splits, int dense_tokens,
+    void* __restrict__ dense_h) {
+  __shared__ float stage[kFragWarps][128];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int it = features / 16;
-  const int kt0 = split * kt_split;
-  const int kt_count = min(kt_split, it - kt0);
-  const int64_t e = ids[slot];
-  const bool ok = e < experts;
-  float m = 0.0f;
-  for (int b = warp; b < kt_count / 8; b += kFragThreads / 32) {
-    const int c0 = kt0 * 16 + b * 128;
-    float gate[4] = {0.f, 0.f, 0.f, 0.f}, up[4] = {0.f, 0.f, 0.f, 0.f};
-    if (ok) {
-      // Splits outer, columns inner, unrolled: all loads of a step in flight.
-      const float* pg = partial + static_cast<int64_t>(slot) * gu_splits * features + c0 + lane;
-      const float* pu = partial + (static_cast<int64_t>(nslots) + slot) * gu_splits * features + c0 + lane;
-#pragma unroll 4
-      for (int s = 0; s < gu_splits; ++s) {
+  const int blocks = features / 128;
+  const int64_t task = static_cast<int64_t>(blockIdx.x) * kFragWarps + warp;  // slot * blocks + b
+  const int64_t slot_tasks = static_cast<int64_t>(nslots) * blocks;
+  if (task >= slot_tasks) {
+    const int64_t d = task - slot_tasks;  // token * blocks + b
+    if (d >= static_cast<int64_t>(dense_tokens) * blocks) return;
+    const int64_t total = static_cast<int64_t>(dense_tokens) * features;
+    const int64_t i0 = (d / blocks) * features + (d % blocks) * 128 + lane;
+    float g[4] = {0.f, 0.f, 0.f, 0.f}, u[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 8
+    for (int sp = 0; sp < dense_splits; ++sp) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        g[j] += __ldcg(dense_g + sp * total + i0 + 32 * j);
+        u[j] += __ldcg(dense_u + sp * total + i0 + 32 * j);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) store_act(dense_h, act_dtype, i0 + 32 * j, swiglu_typed(act_dtype, g[j], u[j]));
+    return;
+  }
+  const int b = static_cast<int>(task % blocks);
+  const int slot = static_cast<int>(task / blocks);
+  const int c0 = b * 128 + lane;
+  const float* pg = partial + static_cast<int64_t>(slot) * gu_splits * features + c0;
+  const float* pu = partial + (static_cast<int64_t>(nslots) + slot) * gu_splits * features + c0;
+  const uint32_t id = ids[slot];
+  float gate[4] = {0.f, 0.f, 0.f, 0.f}, up[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int s0 = 0; s0 < gu_splits; s0 += kGateFinishSplits) {
+    float lg[kGateFinishSplits][4], lu[kGateFinishSplits][4];
+#pragma unroll
+    for (int sp = 0; sp < kGateFinishSplits; ++sp) {
+      const bool have = s0 + sp < gu_splits;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int64_t o = static_cast<int64_t>(s0 + sp) * features + 32 * j;
+        lg[sp][j] = have ? __ldcg(pg + o) : 0.0f;
+        lu[sp][j] = have ? __ldcg(pu + o) : 0.0f;
+      }
+    }
+#pragma unroll
+    for (int sp = 0; sp < kGateFinishSplits; ++sp) {
+      if (s0 + sp < gu_splits) {
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          gate[j] += pg[static_cast<int64_t>(s) * features + 32 * j];
-          up[j] += pu[static_cast<int64_t>(s) * features + 32 * j];
+          gate[j] += lg[sp][j];
+          up[j] += lu[sp][j];
         }
       }
     }
-    hadamard128(gate, lane);
-    hadamard128(up, lane);
-    float act[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int64_t si = e * features + c0 + lane + 32 * j;
-      act[j] = ok ? __fmul_rn(swiglu_typed(act_dtype, __fmul_rn(gate[j], load_scale(out_gate, scale_dtype, si)),
-                                           __fmul_rn(up[j], load_scale(out_up, scale_dtype, si))),
-                              load_scale(in_down, scale_dtype, si))
-                  : 0.0f;
-    }
-    hadamard128(act, lane);
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      vals[b * 128 + lane + 32 * j] = act[j];
-      m = fmaxf(m, fabsf(act[j]));
-    }
   }
-  const float mx = block_max(m, red);
-  const int ex = piece_exponent(mx);
-  write_fragments(vals, kt_count, ldexpf(1.0f, -ex), frag + (static_cast<int64_t>(slot) * it + kt0) * 8);
-  if (threadIdx.x == 0) unscale[static_cast<int64_t>(slot) * splits + split] = ldexpf(1.0f, ex);
+  const int64_t e = id;
+  const bool ok = e < experts;
+  float sg[4], su[4], sd[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int64_t si = (ok ? e : 0) * features + c0 + 32 * j;
+    sg[j] = load_scale(out_gate, scale_dtype, si);
+    su[j] = load_scale(out_up, scale_dtype, si);
+    sd[j] = load_scale(in_down, scale_dtype, si);
+  }
+  hadamard128(gate, lane);
+  hadamard128(up, lane);
+  float act[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+    act[j] = ok ? __fmul_rn(swiglu_typed(act_dtype, __fmul_rn(gate[j], sg[j]), __fmul_rn(up[j], su[j])), sd[j])
+                : 0.0f;
+  hadamard128(act, lane);
+  write_block_record(act, stage[warp], lane, frag + task * kFragBlockBytes);
 }
 
 cudaError_t launch_gate_finish_frag(const float* partial, int gu_splits, const uint32_t* ids, int nslots,
                                     const void* out_gate, const void* out_up, const void* in_down, int scale_dtype,
-                                    int features, int experts, int act_dtype, int kt_split, int splits, uint2* frag,
-                                    float* unscale, cudaStream_t s) {
-  const size_t smem = static_cast<size_t>(kt_split) * 16 * sizeof(float);
-  if (smem > 48 * 1024) {
-    cudaError_t err = cudaFuncSetAttribute(gate_finish_frag_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           static_cast<int>(smem));
-    if (err != cudaSuccess) return err;
-  }
-  dim3 grid(splits, nslots);
-  gate_finish_frag_kernel<<<grid, kFragThreads, smem, s>>>(partial, gu_splits, ids, nslots, out_gate, out_up, in_down,
-                                                            scale_dtype, features, experts, act_dtype, kt_split,
-                                                            splits, frag, unscale);
+                                    int features, int experts, int act_dtype, unsigned char* frag,
+                                    const float* dense_g, const float* dense_u, int dense_splits, int dense_tokens,
+                                    void* dense_h, cudaStream_t s) {
+  if (!dense_h) dense_tokens = 0;
+  const int64_t tasks = (static_cast<int64_t>(nslots) + dense_tokens) * (features / 128);
+  if (tasks == 0) return cudaSuccess;
+  const int64_t grid = (tasks + kFragWarps - 1) / kFragWarps;
+  gate_finish_frag_kernel<<<static_cast<unsigned>(grid), kFragWarps * 32, 0, s>>>(
+      partial, gu_splits, ids, nslots, out_gate, out_up, in_down, scale_dtype, features, experts, act_dtype, frag,
+      dense_g, dense_u, dense_splits, dense_tokens, dense_h);
   return cudaGetLastError();
 }
 
@@ -325,12 +345,20 @@ __global__ void __launch_bounds__(288) finish_fused_kernel(const float* __restri
   const int lane = threadIdx.x & 31, slot = threadIdx.x >> 5;
   const int block = blockIdx.x, token = blockIdx.y;
   const int row = token * 9 + slot;
+  const int64_t off0 = static_cast<int64_t>(token) * features + block * 128 + lane;
+  // Loads that do not depend on the expert id go out first (one round trip),
+  // then the id-dependent output scales.
+  float res[4] = {0.f, 0.f, 0.f, 0.f};
+  if (slot == 0) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) res[j] = load_act(residual, act_dtype, off0 + 32 * j);
+  }
   if (slot == 8 && shared_values != nullptr) {
     // Dense shared expert: float32 split partials [shared_splits][tokens][h].
     const int64_t total = static_cast<int64_t>(tokens) * features;
     float a[4] = {0.f, 0.f, 0.f, 0.f};
-    const float* sv = static_cast<const float*>(shared_values) + static_cast<int64_t>(token) * features + block * 128 + lane;
-#pragma unroll 4
+    const float* sv = static_cast<const float*>(shared_values) + off0;
+#pragma unroll 8
     for (int sp = 0; sp < shared_splits; ++sp) {
 #pragma unroll
       for (int j = 0; j < 4; ++j) a[j] += __ldcg(sv + sp * total + 32 * j);
@@ -339,24 +367,27 @@ __global__ void __launch_bounds__(288) finish_fused_kernel(const float* __restri
     for (int j = 0; j < 4; ++j) products[8][lane + 32 * j] = round_to(act_dtype, a[j]);
   } else {
     const int64_t e = ids[row];
+    const float weight = slot < 8 ? scores[token * 8 + slot] : 1.0f;
     const int64_t prow = row_map ? row_map[row] : static_cast<int64_t>(row) * splits;
-    const bool ok = e < experts && prow >= 0;  // an out-of-range id contributes zero
     float v[4] = {0.f, 0.f, 0.f, 0.f};
-    if (ok) {
+    if (prow >= 0) {
       const float* ps = partial + prow * features + block * 128 + lane;
 #pragma unroll 4
       for (int s = 0; s < splits; ++s) {
 #pragma unroll
-        for (int j = 0; j < 4; ++j) v[j] += ps[static_cast<int64_t>(s) * features + 32 * j];
+        for (int j = 0; j < 4; ++j) v[j] += __ldcg(ps + static_cast<int64_t>(s) * features + 32 * j);
       }
     }
+    const bool ok = e < experts && prow >= 0;  // an out-of-range id contributes zero
+    float sc[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      sc[j] = load_scale(out_scale, scale_dtype, (ok ? e : 0) * features + block * 128 + lane + 32 * j);
     hadamard128(v, lane);
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      const int col = block * 128 + lane + 32 * j;
-      const float value =
-          ok ? round_to(act_dtype, __fmul_rn(v[j], load_scale(out_scale, scale_dtype, e * features + col))) : 0.0f;
-      products[slot][lane + 32 * j] = slot < 8 ? __fmul_rn(value, scores[token * 8 + slot]) : value;
+      const float value = ok ? round_to(act_dtype, __fmul_rn(v[j], sc[j])) : 0.0f;
+      products[slot][lane + 32 * j] = slot < 8 ? __fmul_rn(value, weight) : value;
     }
   }
   __syncthreads();
@@ -367,10 +398,9 @@ __global__ void __launch_bounds__(288) finish_fused_kernel(const float* __restri
     float total = __fadd_rn(products[0][c], 0.0f);
 #pragma unroll
     for (int r = 1; r < 8; ++r) total = __fadd_rn(__fadd_rn(products[r][c], 0.0f), total);
-    const int64_t off = static_cast<int64_t>(token) * features + block * 128 + c;
     const float routed = round_to(act_dtype, total);
     const float combined = round_to(act_dtype, __fadd_rn(routed, round_to(act_dtype, products[8][c])));
-    store_act(out, act_dtype, off, __fadd_rn(load_act(residual, act_dtype, off), combined));
+    store_act(out, act_dtype, off0 + 32 * j, __fadd_rn(res[j], combined));
   }
 }
 

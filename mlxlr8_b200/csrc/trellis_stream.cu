@@ -6,9 +6,11 @@
 //   producer: takes work units (row group of one expert, projection, 128-wide
 //     output block, K split) from a global counter and streams each unit's
 //     packed tiles -- one contiguous run of 8 output tiles per K tile -- plus
-//     the unit rows' activation fragments into a ring of shared-memory stages
-//     with 1-D bulk copies (cp.async.bulk, no multicast) completing on
-//     mbarriers.  Units follow each other through the ring without draining.
+//     the unit rows' activation fragment records (one per 128-wide K block,
+//     with the block's unscale) into a ring of shared-memory stages with 1-D
+//     bulk copies (cp.async.bulk, no multicast) completing on mbarriers.  A
+//     stage is one 128-wide K block.  Units follow each other through the
+//     ring without draining.
 //   consumers: each of the eight warps owns one of the eight 16x16 output
 //     tiles and takes the stage's 8 K tiles at once (eight independent decode
 //     chains per warp).  A lane reads word l and word l-1 of a tile; every 32-bit window
@@ -17,11 +19,17 @@
 //     codeword masks disappear.  The half sums are rounded to E4M3 and placed
 //     directly in mma.sync m16n8k16 A fragments (the trellis tensor-core
 //     permutation is that layout); B holds float16 hi/lo pieces of up to four
-//     rows (eight columns) per fragment group; float32 accumulation.
+//     rows (eight columns) per fragment group; each stage's float32 products
+//     are added into the unit's accumulators times the block's unscale.
 //   output: per unit, float32 partial sums [proj][slot][split][out].
+//   dense units (the bf16 shared expert, stream.cuh DenseUnits) come first
+//   in the unit order: the producer passes each one through the ring as a
+//   stage without data, and the eight consumer warps stream its weight rows
+//   from global memory while the producer fills the next stages.
 
 #include "codec.cuh"
 #include "common.cuh"
+#include "dense_warp.cuh"
 #include "stream.cuh"
 #include "tma.cuh"
 
@@ -32,8 +40,9 @@ constexpr int kStreamThreads = (kConsumers + 1) * 32;
 constexpr int kStages = 4;
 constexpr int kStageTiles = 8;                       // K tiles per stage
 constexpr int kFragRowBytes = kStageTiles * 64 + 64;  // padded: rows hit different banks
+static_assert(kFragRowBytes >= kFragBlockBytes, "a fragment record fits its stage row");
 
-enum : int { kFirst = 1, kLast = 2, kEnd = 4 };
+enum : int { kFirst = 1, kLast = 2, kEnd = 4, kDense = 8 };
 
 template <int K>
 struct StageGeometry {
@@ -123,21 +132,32 @@ __global__ void __launch_bounds__(kStreamThreads, 2) trellis_stream_kernel(Strea
     // ---------------- producer ----------------
     if (lane != 0) return;
     const int groups = p.plan.header[0];
-    const int64_t total = static_cast<int64_t>(groups) * p.projections * nblocks * p.splits;
+    const int64_t dense_total = p.dense.units;
+    const int64_t total = dense_total + static_cast<int64_t>(groups) * p.projections * nblocks * p.splits;
     int stage = 0;
     uint32_t phase = 0;
     bool failed = false;
     for (;;) {
-      const int64_t unit = atomicAdd(&p.plan.header[p.counter], 1);
+      const int64_t next = atomicAdd(&p.plan.header[p.counter], 1);
       if (!mbar_wait(&empty_bar[stage], phase ^ 1u)) {
         failed = true;
         break;
       }
-      if (unit >= total) {
+      if (next >= total) {
         meta[stage] = make_int4(0, 0, 0, kEnd);
         mbar_arrive(&full_bar[stage]);
         break;
       }
+      if (next < dense_total) {
+        meta[stage] = make_int4(static_cast<int>(next), 0, 0, kDense);
+        mbar_arrive(&full_bar[stage]);
+        if (++stage == kStages) {
+          stage = 0;
+          phase ^= 1u;
+        }
+        continue;
+      }
+      const int64_t unit = next - dense_total;
       const UnitInfo u = decode_unit(unit, p, nblocks);
       const int expert = p.plan.group_expert[u.group];
       const int start = p.plan.group_start[u.group];
@@ -157,14 +177,14 @@ __global__ void __launch_bounds__(kStreamThreads, 2) trellis_stream_kernel(Strea
                                 (kt == kt0 ? kFirst : 0) | (kt + kStageTiles >= kt1 ? kLast : 0));
         unsigned char* base = smem + stage * G::kStageBytes;
         const uint32_t code_bytes = static_cast<uint32_t>(n) * 8u * G::kTileWords * 4u;
-        mbar_arrive_expect_tx(&full_bar[stage], code_bytes + static_cast<uint32_t>(nr) * n * 64u);
+        mbar_arrive_expect_tx(&full_bar[stage], code_bytes + static_cast<uint32_t>(nr) * kFragBlockBytes);
         const uint32_t* src = words + tile_index(expert, kt, u.nb * 8, it, ot, p.side) * G::kTileWords;
         bulk_copy_g2s(base, src, code_bytes, &full_bar[stage]);
         for (int r = 0; r < nr; ++r) {
           const int slot = p.plan.order[start + r];
-          const uint2* fsrc = p.frag + ((static_cast<int64_t>(u.proj) * p.nslots + slot) * it + kt) * 8;
-          bulk_copy_g2s(base + G::kCodeBytes + r * kFragRowBytes, fsrc, static_cast<uint32_t>(n) * 64u,
-                        &full_bar[stage]);
+          const unsigned char* fsrc =
+              p.frag + ((static_cast<int64_t>(u.proj) * p.nslots + slot) * (it / 8) + kt / 8) * kFragBlockBytes;
+          bulk_copy_g2s(base + G::kCodeBytes + r * kFragRowBytes, fsrc, kFragBlockBytes, &full_bar[stage]);
         }
         if (++stage == kStages) {
           stage = 0;
@@ -194,7 +214,6 @@ __global__ void __launch_bounds__(kStreamThreads, 2) trellis_stream_kernel(Strea
     for (int i = 0; i < 4; ++i) acc[c][i] = 0.0f;
   UnitInfo u{};
   int nr = 0, ncg = 1, slot_a = -1, slot_b = -1;
-  float unscale_a = 1.0f, unscale_b = 1.0f;
   GenericGeometry geo;
   if (K != 4) geo = generic_geometry(K, lane);
   const int r0 = gid >> 1, fpos = (gid & 1) * 4 + tig;
@@ -206,6 +225,25 @@ __global__ void __launch_bounds__(kStreamThreads, 2) trellis_stream_kernel(Strea
     }
     const int4 m = meta[stage];
     if (m.w & kEnd) break;
+    if (m.w & kDense) {
+      // The stage carries no data: release it, then stream this warp's 16
+      // rows of the unit's 128-row block over the unit's K split.
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty_bar[stage]);
+      const DenseUnits& d = p.dense;
+      const int rbs = d.n / 128;
+      const int rb = m.x % rbs, split = m.x / rbs;
+      const int steps = d.k / 32, per = (steps + d.splits - 1) / d.splits;
+      const int s0 = split * per, s1 = min(s0 + per, steps);
+      const int64_t part = static_cast<int64_t>(split) * d.tokens * d.n;
+      dense_rows<2>(d.x, d.tokens, d.w0, d.w1, d.n, d.k, rb * 128 + warp * 16, s0, s1, d.p0 + part,
+                    d.w1 ? d.p1 + part : nullptr, lane);
+      if (++stage == kStages) {
+        stage = 0;
+        phase ^= 1u;
+      }
+      continue;
+    }
     if (m.w & kFirst) {
       u = decode_unit(m.x, p, nblocks);
       const int start = p.plan.group_start[u.group];
@@ -213,17 +251,19 @@ __global__ void __launch_bounds__(kStreamThreads, 2) trellis_stream_kernel(Strea
       ncg = (nr + 3) >> 2;
       slot_a = tig < nr ? p.plan.order[start + tig] : -1;
       slot_b = 4 + tig < nr ? p.plan.order[start + 4 + tig] : -1;
-      const int64_t ubase = static_cast<int64_t>(u.proj) * p.nslots;
-      unscale_a = slot_a >= 0 ? p.unscale[(ubase + slot_a) * p.splits + u.split] : 1.0f;
-      unscale_b = slot_b >= 0 ? p.unscale[(ubase + slot_b) * p.splits + u.split] : 1.0f;
     }
     const unsigned char* base = smem + stage * G::kStageBytes;
     const uint32_t* codes = reinterpret_cast<const uint32_t*>(base);
     const uint2* frag = reinterpret_cast<const uint2*>(base + G::kCodeBytes);
-    // Every stage holds kStageTiles K tiles (splits are whole 128-wide blocks).
+    // Every stage holds one 128-wide K block (kStageTiles K tiles).
     const bool has0 = r0 < nr, has1 = 4 + r0 < nr;
     const uint2* f0 = frag + (r0 * kFragRowBytes) / 8 + fpos;
     const uint2* f1 = frag + ((4 + r0) * kFragRowBytes) / 8 + fpos;
+    float st[2][4];
+#pragma unroll
+    for (int c = 0; c < 2; ++c)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) st[c][i] = 0.0f;
     if (K == 4) {
       uint32_t word[kStageTiles], prior[kStageTiles];
 #pragma unroll
@@ -237,15 +277,15 @@ __global__ void __launch_bounds__(kStreamThreads, 2) trellis_stream_kernel(Strea
         for (int kk = 0; kk < kStageTiles; ++kk) {
           uint32_t a[4];
           k4_fragment(word[kk], prior[kk], unit16, mcg_mask, mcg_xor, a);
-          mma_f16(acc[0], a, has0 ? f0[kk * 8] : make_uint2(0u, 0u));
-          mma_f16(acc[1], a, has1 ? f1[kk * 8] : make_uint2(0u, 0u));
+          mma_f16(st[0], a, has0 ? f0[kk * 8] : make_uint2(0u, 0u));
+          mma_f16(st[1], a, has1 ? f1[kk * 8] : make_uint2(0u, 0u));
         }
       } else {
 #pragma unroll
         for (int kk = 0; kk < kStageTiles; ++kk) {
           uint32_t a[4];
           k4_fragment(word[kk], prior[kk], unit16, mcg_mask, mcg_xor, a);
-          mma_f16(acc[0], a, has0 ? f0[kk * 8] : make_uint2(0u, 0u));
+          mma_f16(st[0], a, has0 ? f0[kk * 8] : make_uint2(0u, 0u));
         }
       }
     } else {
@@ -254,9 +294,20 @@ __global__ void __launch_bounds__(kStreamThreads, 2) trellis_stream_kernel(Strea
         uint32_t cw[8], a[4];
         generic_codewords(codes + (kk * 8 + warp) * G::kTileWords, K, geo, cw);
         tile_fragment(cw, a);
-        mma_f16(acc[0], a, has0 ? f0[kk * 8] : make_uint2(0u, 0u));
-        if (ncg > 1) mma_f16(acc[1], a, has1 ? f1[kk * 8] : make_uint2(0u, 0u));
+        mma_f16(st[0], a, has0 ? f0[kk * 8] : make_uint2(0u, 0u));
+        if (ncg > 1) mma_f16(st[1], a, has1 ? f1[kk * 8] : make_uint2(0u, 0u));
       }
+    }
+    // This lane's accumulator columns belong to unit rows tig and 4 + tig;
+    // their block unscales sit in the fragment record headers.
+    const float* hdr = reinterpret_cast<const float*>(base + G::kCodeBytes + 512);
+    const float us0 = tig < nr ? hdr[tig * (kFragRowBytes / 4)] : 0.0f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) acc[0][i] = fmaf(st[0][i], us0, acc[0][i]);
+    if (ncg > 1) {
+      const float us1 = 4 + tig < nr ? hdr[(4 + tig) * (kFragRowBytes / 4)] : 0.0f;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) acc[1][i] = fmaf(st[1][i], us1, acc[1][i]);
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty_bar[stage]);
@@ -266,11 +317,10 @@ __global__ void __launch_bounds__(kStreamThreads, 2) trellis_stream_kernel(Strea
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
         const int slot = c == 0 ? slot_a : slot_b;
-        const float us = c == 0 ? unscale_a : unscale_b;
         if (slot >= 0) {
           float* dst = p.partial + ((ubase + slot) * p.splits + u.split) * p.out_features + col;
-          dst[0] = (acc[c][0] + acc[c][1]) * us;
-          dst[8] = (acc[c][2] + acc[c][3]) * us;
+          dst[0] = acc[c][0] + acc[c][1];
+          dst[8] = acc[c][2] + acc[c][3];
         }
 #pragma unroll
         for (int i = 0; i < 4; ++i) acc[c][i] = 0.0f;
