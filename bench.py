@@ -50,10 +50,14 @@ HIDDEN, INTER, EXPERTS, K_BITS = 6144, 2048, 256, 4
 METRIC = "MoE-layer tokens/s (decode GB/s vs HBM; prefill TFLOPS) at 1/2/4/8 B200"
 
 # dram__bytes_read.sum + dram__bytes_write.sum of one gate/up streaming-GEMV
-# launch from an ncu capture of a nine-expert case (18 expert matrices,
-# profiles/trellis_stream_gate_up_decode.md), per expert matrix; the bench
-# scales it by the matrices its own launches stream.
-TRAFFIC_PER_MATRIX = (113_755_904 + 4_150_784) / 18
+# launch from the ncu capture in profiles/trellis_stream_gate_up_decode.md:
+# 8 distinct experts (16 matrices) plus the bf16 shared expert's gate/up rows,
+# which the same launch streams.  The bench splits it into a per-matrix part
+# (the codes scale with the matrices its own launches stream) and the shared
+# expert's part, taken as its algorithmic bytes.
+DENSE_GATE_UP_BYTES = 2 * 6144 * 2048 * 2
+GATE_UP_TRAFFIC_8 = 151_501_568 + 5_826_560
+TRAFFIC_PER_MATRIX = (GATE_UP_TRAFFIC_8 - DENSE_GATE_UP_BYTES) / 16
 
 
 def parse():
@@ -490,7 +494,10 @@ def main():
     codes_per_matrix = HIDDEN * INTER * K_BITS // 8
     gate_up_n, gate_up_ms = prof["gate_up"]
     gate_up_avg_ms = gate_up_ms / max(gate_up_n, 1)
-    gate_up_bytes = u_mean * 2 * codes_per_matrix
+    # The single-GPU layer streams the bf16 shared expert's gate/up rows in the
+    # same launch (its dense warp); expert-parallel ranks run it separately.
+    dense_bytes = DENSE_GATE_UP_BYTES if world == 1 else 0
+    gate_up_bytes = u_mean * 2 * codes_per_matrix + dense_bytes
     achieved = gate_up_bytes / (gate_up_avg_ms / 1000.0) / 1e9
     peak, peak_kind = measured_peaks()
     share = {k: round(ms / max(sum(v for _, v in prof.values()), 1e-9), 4) for k, (n, ms) in prof.items()}
@@ -562,9 +569,10 @@ def main():
                        else "single GPU"},
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "steps": e2e_steps},
-            "roofline": {"bound": "hbm", "kernel": "trellis_stream_kernel<4> (gate/up)", "achieved": achieved,
-                         "peak": peak, "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peak,
-                         "traffic": TRAFFIC_PER_MATRIX * 2 * u_mean,
+            "roofline": {"bound": "hbm", "kernel": ("trellis_stream_kernel<4> (gate/up" +
+                                                    (" + bf16 shared gate/up rows)" if dense_bytes else ")")),
+                         "achieved": achieved, "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": TRAFFIC_PER_MATRIX * 2 * u_mean + dense_bytes,
                          "algorithmic_bytes_per_launch": gate_up_bytes, "avg_launch_ms": gate_up_avg_ms,
                          "unique_experts_mean": u_mean},
             "step_roofline": {"algorithmic_bytes": step_bytes, "achieved_gbs": step_bytes / (ms_per_step / 1000) / 1e9,

@@ -8,6 +8,7 @@
 #include "codec.cuh"
 #include "common.cuh"
 #include "dense.cuh"
+#include "dense_stream.cuh"
 #include "ep.cuh"
 #include "joined.cuh"
 #include "mx_gemm.cuh"
@@ -25,23 +26,48 @@ thread_local Profiler g_prof;
 
 namespace {
 
+constexpr int64_t kStreamCtasHint = 296;  // persistent stream CTAs on a B200 (2 per SM)
+
 // K splits.  Gate/up follow fast_decode.py:216 (min(8, max(1, hidden // 768)));
 // the down product splits once per 1024 inputs.  Splits are rounded to whole
 // 128-wide blocks (stream.cuh kt_per_split).
 struct Splits {
   int kt, count;
 };
-inline Splits make_splits(int in_features, int nominal) {
+inline Splits make_splits(int in_features, int nominal, int cap = 8) {
   if (nominal < 1) nominal = 1;
-  if (nominal > 8) nominal = 8;
+  if (nominal > cap) nominal = cap;
   Splits s;
   s.kt = kt_per_split(in_features, nominal);
   s.count = split_count(in_features, s.kt);
   return s;
 }
-inline Splits gate_up_splits(int hidden) { return make_splits(hidden, hidden / 768); }
-inline Splits down_splits(int intermediate) { return make_splits(intermediate, intermediate / 1024); }
+// Gate/up: at least the reference's count, and for small batches enough
+// splits for >= 12 units per stream CTA (units are (row group, projection,
+// 128-wide output block, split); the row count bounds the groups).
+inline Splits gate_up_splits(int hidden, int intermediate, int64_t rows) {
+  int nominal = hidden / 768;
+  const int64_t per_split = (rows > 0 ? rows : 1) * 2 * (intermediate / 128);
+  const int64_t want = (12 * kStreamCtasHint + per_split - 1) / per_split;
+  if (want > nominal) nominal = static_cast<int>(want < 16 ? want : 16);
+  return make_splits(hidden, nominal, 16);
+}
+// The down product splits once per 1024 inputs, and more for small batches:
+// its units are (row group, 128-wide output block, split), and with few row
+// groups whole-unit granularity would leave the last wave of the persistent
+// stream CTAs (2 per SM, 296 on a B200) unbalanced.  Aim for >= 8 units per CTA.
+inline Splits down_splits(int intermediate, int hidden, int64_t rows) {
+  int nominal = intermediate / 1024;
+  const int64_t per_split = (rows > 0 ? rows : 1) * (hidden / 128);
+  const int64_t want = (8 * kStreamCtasHint + per_split - 1) / per_split;
+  if (want > nominal) nominal = static_cast<int>(want < 8 ? want : 8);
+  return make_splits(intermediate, nominal);
+}
 inline Splits linear_splits(int in_features) { return make_splits(in_features, in_features / 768); }
+// K splits of the bf16 shared expert streamed beside the trellis units
+// (units of 16 rows x one split; the partials are summed in split order).
+inline int dense_gate_up_splits(int hidden) { return dense_split_count(hidden, 4); }
+inline int dense_down_splits(int intermediate) { return dense_split_count(intermediate, 2); }
 // The dense bf16 GEMV splits K into 384-wide pieces (enough warps in flight
 // to stream the weights at full bandwidth for one to a few tokens).
 inline int dense_splits(int k) {
@@ -73,8 +99,8 @@ constexpr int kDenseDownSplits = 8;
 
 MlpLayout mlp_layout(int64_t rows, int hidden, int inter, int64_t experts) {
   MlpLayout l;
-  l.s1 = gate_up_splits(hidden);
-  l.s2 = down_splits(inter);
+  l.s1 = gate_up_splits(hidden, inter, rows);
+  l.s2 = down_splits(inter, hidden, rows);
   l.plan = align_up(plan_bytes(static_cast<int>(rows), static_cast<int>(experts)));
   l.frag_gu = align_up(frag_bytes(rows, hidden, 2));
   l.gu = align_up(2 * rows * l.s1.count * static_cast<size_t>(inter) * sizeof(float));
@@ -204,14 +230,15 @@ int run_mlp_after_plan(const void* x, int x_dtype, int per_slot, int slots, cons
   gp.kt_per_split = l.s1.kt;
   gp.splits = l.s1.count;
   gp.projections = 2;
+  const int dsplits_gu = dense_gate_up_splits(h), dsplits_d = dense_down_splits(m);
   if (shared)
     gp.dense = DenseUnits{static_cast<const uint16_t*>(shared->gate), static_cast<const uint16_t*>(shared->up),
-                          static_cast<const uint16_t*>(x), b.dgate, b.dup, m, h, t, l.s1.count,
-                          (m / 128) * l.s1.count};
+                          static_cast<const uint16_t*>(x), b.dgate, b.dup, m, h, t, dsplits_gu,
+                          (m / kDenseRows) * dsplits_gu, 4};
   EXLR8_TIMED(EXLR8_KERNEL_GATE_UP, s, launch_stream(gp, s));
   EXLR8_TIMED(EXLR8_KERNEL_GATE_FINISH, s,
               launch_gate_finish_frag(b.gu, l.s1.count, ids, n, ex->out_scale[0], ex->out_scale[1], ex->in_scale[2],
-                                      ex->scale_dtype, m, e, x_dtype, b.frag_d, b.dgate, b.dup, l.s1.count,
+                                      ex->scale_dtype, m, e, x_dtype, b.frag_d, b.dgate, b.dup, dsplits_gu,
                                       shared ? t : 0, shared ? b.dh : nullptr, s));
   StreamParams dp = stream_params(ex, b.plan, 3, n);
   dp.packed[0] = static_cast<const uint32_t*>(ex->packed[2]);
@@ -226,7 +253,7 @@ int run_mlp_after_plan(const void* x, int x_dtype, int per_slot, int slots, cons
   dp.projections = 1;
   if (shared)
     dp.dense = DenseUnits{static_cast<const uint16_t*>(shared->down), nullptr, static_cast<const uint16_t*>(b.dh),
-                          b.ddown, nullptr, h, m, t, l.s2.count, (h / 128) * l.s2.count};
+                          b.ddown, nullptr, h, m, t, dsplits_d, (h / kDenseRows) * dsplits_d, 5};
   EXLR8_TIMED(EXLR8_KERNEL_DOWN, s, launch_stream(dp, s));
   return EXLR8_OK;
 }
@@ -608,7 +635,8 @@ static int mlp_finish_after_plan(const void* x, int x_dtype, const uint32_t* ind
   ProfileScope scope(EXLR8_KERNEL_FINISH, s);
   return cuda_status(launch_finish_fused(b.dpart, l.s2.count, nullptr, indices, static_cast<int>(tokens), ex->out_scale[2],
                                          ex->scale_dtype, ex->hidden, static_cast<int>(experts), scores, residual,
-                                         shared ? b.ddown : nullptr, l.s2.count, x_dtype, out, s));
+                                         shared ? b.ddown : nullptr, dense_down_splits(ex->intermediate), x_dtype,
+                                         out, s));
 }
 
 int exlr8_expert_mlp_finish(const void* x, int x_dtype, const uint32_t* indices, const float* scores,
@@ -619,6 +647,7 @@ int exlr8_expert_mlp_finish(const void* x, int x_dtype, const uint32_t* indices,
   EXLR8_CHECK(check_experts(ex, &experts));
   if (!valid_act(x_dtype)) return EXLR8_ERR_DTYPE;
   EXLR8_CHECK(check_dense(shared, x_dtype, ex->hidden, ex->intermediate));
+  if (shared && x && !aligned16(x)) return EXLR8_ERR_ALIGN;  // bulk-copied x rows of the shared expert
   if (tokens < 0) return EXLR8_ERR_ROWS;
   if (tokens == 0) return EXLR8_OK;
   if (!x || !indices || !scores || !residual || !out) return EXLR8_ERR_ARG;

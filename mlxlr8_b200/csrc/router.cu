@@ -8,6 +8,7 @@
 #include "router.cuh"
 #include "plan.cuh"
 #include "trellis_gemv.cuh"
+#include "launch.cuh"
 
 namespace exlr8 {
 
@@ -175,6 +176,7 @@ __global__ void __launch_bounds__(kGateWarps * 32) router_plan_kernel(
     const void* __restrict__ x, int x_dtype, int tokens, int hidden, const float* __restrict__ wg,
     float* __restrict__ logits, const float* __restrict__ bias, uint32_t* __restrict__ ids,
     float* __restrict__ scores, int* __restrict__ done, int plan_experts, int skip_slot, PlanView plan) {
+  pdl_launch_dependents();  // the prep kernel may launch and wait for this grid
   extern __shared__ int sm[];
   __shared__ float red[kGateWarps][kGateTokens];
   __shared__ int s_last;
@@ -265,6 +267,8 @@ cudaError_t launch_router_plan(const void* x, int x_dtype, int tokens, int hidde
                                            static_cast<int>(smem));
     if (err != cudaSuccess) return err;
   }
+  static const cudaError_t carve = prefer_shared_carveout(router_plan_kernel);
+  if (carve != cudaSuccess) return carve;
   cudaError_t err = cudaMemsetAsync(done, 0, sizeof(int), s);
   if (err != cudaSuccess) return err;
   router_plan_kernel<<<256, kGateWarps * 32, smem, s>>>(x, x_dtype, tokens, hidden, wg, logits, bias, ids, scores,

@@ -22,19 +22,19 @@ inline size_t frag_bytes(int64_t rows, int features, int projections) {
          kFragBlockBytes;
 }
 
-// The bf16 shared expert rides along as dense units: units [0, units) of a
-// launch are dense, the trellis units follow.  A dense unit is (128-row block
-// of W, K split); each consumer warp streams 16 rows of W (and of W1, which
-// shares the x loads) with 128-bit loads straight from global memory and
-// writes float32 partials [splits][tokens][n].  The HBM-bound dense rows thus
-// overlap the trellis units, which are bound by their decode arithmetic.
+// The bf16 shared expert rides along as dense units, streamed by one extra
+// warp per CTA (dense_stream.cuh) beside the trellis warps.  A dense unit is
+// (16-row group of W, K split); W1 (optional) shares the x rows.  Partials
+// are float32 [splits][tokens][n].  Requirements: n % 16 == 0, k a multiple
+// of 128 * splits, W, W1 and x 16-byte aligned.
 struct DenseUnits {
   const uint16_t* w0;  // [n][k] bf16 (gate, or down)
   const uint16_t* w1;  // [n][k] bf16 (up) or null
   const uint16_t* x;   // [tokens][k] bf16
   float* p0;           // [splits][tokens][n] partials of w0
   float* p1;           // same for w1
-  int n, k, tokens, splits, units;  // units = (n / 128) * splits, 0 = none
+  int n, k, tokens, splits, units;  // units = (n / 16) * splits, 0 = none
+  int counter;                      // plan header slot of the dense unit counter
 };
 
 struct StreamParams {

@@ -18,6 +18,7 @@
 #include "stream.cuh"
 #include "trellis_gemv.cuh"
 #include "plan.cuh"
+#include "launch.cuh"
 
 namespace exlr8 {
 
@@ -60,6 +61,8 @@ constexpr int kPlanThreads = 1024;
 
 __global__ void __launch_bounds__(kPlanThreads) plan_kernel(const uint32_t* __restrict__ ids, int rows,
                                                             int experts, int period, int skip_slot, PlanView plan) {
+  pdl_launch_dependents();
+  pdl_wait();
   extern __shared__ int sm[];
   plan_body(ids, rows, experts, period, skip_slot, plan, sm);
 }
@@ -72,8 +75,10 @@ cudaError_t launch_plan(const uint32_t* ids, int rows, int experts, int period, 
                                            static_cast<int>(smem));
     if (err != cudaSuccess) return err;
   }
-  plan_kernel<<<1, kPlanThreads, smem, s>>>(ids, rows, experts, period > 0 ? period : 1, skip_slot, plan);
-  return cudaGetLastError();
+  static const cudaError_t carve = prefer_shared_carveout(plan_kernel);
+  if (carve != cudaSuccess) return carve;
+  return launch_pdl(plan_kernel, dim3(1), dim3(kPlanThreads), smem, s, ids, rows, experts, period > 0 ? period : 1,
+                    skip_slot, plan);
 }
 
 // ---------------------------------------------------------------------------
@@ -138,6 +143,8 @@ __global__ void __launch_bounds__(kFragWarps * 32) prep_frag_kernel(
     const void* __restrict__ x, int x_dtype, int per_slot, int slots_per_token, const uint32_t* __restrict__ ids,
     int nslots, const void* __restrict__ in0, const void* __restrict__ in1, int scale_dtype, int features,
     int experts, int projections, unsigned char* __restrict__ frag) {
+  pdl_launch_dependents();
+  pdl_wait();
   __shared__ float stage[kFragWarps][128];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int blocks = features / 128;
@@ -169,9 +176,10 @@ cudaError_t launch_prep_frag(const void* x, int x_dtype, int per_slot, int slots
   const int64_t tasks = static_cast<int64_t>(projections) * nslots * (features / 128);
   if (tasks == 0) return cudaSuccess;
   const int64_t grid = (tasks + kFragWarps - 1) / kFragWarps;
-  prep_frag_kernel<<<static_cast<unsigned>(grid), kFragWarps * 32, 0, s>>>(
-      x, x_dtype, per_slot, slots_per_token, ids, nslots, in0, in1, scale_dtype, features, experts, projections, frag);
-  return cudaGetLastError();
+  static const cudaError_t carve = prefer_shared_carveout(prep_frag_kernel);
+  if (carve != cudaSuccess) return carve;
+  return launch_pdl(prep_frag_kernel, dim3(static_cast<unsigned>(grid)), dim3(kFragWarps * 32), 0, s, x, x_dtype,
+                    per_slot, slots_per_token, ids, nslots, in0, in1, scale_dtype, features, experts, projections, frag);
 }
 
 // gate/up split sum, Hadamard, output scales, typed SwiGLU, down input scale,
@@ -188,6 +196,8 @@ __global__ void __launch_bounds__(kFragWarps * 32) gate_finish_frag_kernel(
     int scale_dtype, int features, int experts, int act_dtype, unsigned char* __restrict__ frag,
     const float* __restrict__ dense_g, const float* __restrict__ dense_u, int dense_splits, int dense_tokens,
     void* __restrict__ dense_h) {
+  pdl_launch_dependents();
+  pdl_wait();
   __shared__ float stage[kFragWarps][128];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int blocks = features / 128;
@@ -271,10 +281,11 @@ cudaError_t launch_gate_finish_frag(const float* partial, int gu_splits, const u
   const int64_t tasks = (static_cast<int64_t>(nslots) + dense_tokens) * (features / 128);
   if (tasks == 0) return cudaSuccess;
   const int64_t grid = (tasks + kFragWarps - 1) / kFragWarps;
-  gate_finish_frag_kernel<<<static_cast<unsigned>(grid), kFragWarps * 32, 0, s>>>(
-      partial, gu_splits, ids, nslots, out_gate, out_up, in_down, scale_dtype, features, experts, act_dtype, frag,
-      dense_g, dense_u, dense_splits, dense_tokens, dense_h);
-  return cudaGetLastError();
+  static const cudaError_t carve = prefer_shared_carveout(gate_finish_frag_kernel);
+  if (carve != cudaSuccess) return carve;
+  return launch_pdl(gate_finish_frag_kernel, dim3(static_cast<unsigned>(grid)), dim3(kFragWarps * 32), 0, s, partial,
+                    gu_splits, ids, nslots, out_gate, out_up, in_down, scale_dtype, features, experts, act_dtype, frag,
+                    dense_g, dense_u, dense_splits, dense_tokens, dense_h);
 }
 
 // ---------------------------------------------------------------------------
@@ -288,6 +299,8 @@ __global__ void __launch_bounds__(128) finish_kernel(const float* __restrict__ p
                                                      const void* __restrict__ out_scale, int scale_dtype,
                                                      int features, int experts, int act_dtype,
                                                      void* __restrict__ out) {
+  pdl_launch_dependents();
+  pdl_wait();
   const int lane = threadIdx.x & 31;
   const int block = blockIdx.x * 4 + (threadIdx.x >> 5);
   const int slot = blockIdx.y;
@@ -319,9 +332,10 @@ cudaError_t launch_finish(const float* partial, int splits, const int32_t* row_m
                           const void* out_scale, int scale_dtype, int features, int experts, int act_dtype, void* out,
                           cudaStream_t s) {
   dim3 grid((features / 128 + 3) / 4, nslots);
-  finish_kernel<<<grid, 128, 0, s>>>(partial, splits, row_map, ids, nslots, out_scale, scale_dtype, features, experts,
-                                     act_dtype, out);
-  return cudaGetLastError();
+  static const cudaError_t carve = prefer_shared_carveout(finish_kernel);
+  if (carve != cudaSuccess) return carve;
+  return launch_pdl(finish_kernel, grid, dim3(128), 0, s, partial, splits, row_map, ids, nslots, out_scale,
+                    scale_dtype, features, experts, act_dtype, out);
 }
 
 // Nine slots per token (eight routed + shared), one warp per slot: expert
@@ -341,6 +355,8 @@ __global__ void __launch_bounds__(288) finish_fused_kernel(const float* __restri
                                                            const void* __restrict__ residual,
                                                            const void* __restrict__ shared_values, int shared_splits,
                                                            int act_dtype, void* __restrict__ out) {
+  pdl_launch_dependents();
+  pdl_wait();
   __shared__ float products[9][128];
   const int lane = threadIdx.x & 31, slot = threadIdx.x >> 5;
   const int block = blockIdx.x, token = blockIdx.y;
@@ -409,9 +425,10 @@ cudaError_t launch_finish_fused(const float* partial, int splits, const int32_t*
                                 const float* scores, const void* residual, const void* shared_values,
                                 int shared_splits, int act_dtype, void* out, cudaStream_t s) {
   dim3 grid(features / 128, tokens);
-  finish_fused_kernel<<<grid, 288, 0, s>>>(partial, splits, row_map, ids, tokens, out_scale, scale_dtype, features, experts,
-                                           scores, residual, shared_values, shared_splits, act_dtype, out);
-  return cudaGetLastError();
+  static const cudaError_t carve = prefer_shared_carveout(finish_fused_kernel);
+  if (carve != cudaSuccess) return carve;
+  return launch_pdl(finish_fused_kernel, grid, dim3(288), 0, s, partial, splits, row_map, ids, tokens, out_scale,
+                    scale_dtype, features, experts, scores, residual, shared_values, shared_splits, act_dtype, out);
 }
 
 }  // namespace exlr8

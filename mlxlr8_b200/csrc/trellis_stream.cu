@@ -22,27 +22,29 @@
 //     rows (eight columns) per fragment group; each stage's float32 products
 //     are added into the unit's accumulators times the block's unscale.
 //   output: per unit, float32 partial sums [proj][slot][split][out].
-//   dense units (the bf16 shared expert, stream.cuh DenseUnits) come first
-//   in the unit order: the producer passes each one through the ring as a
-//   stage without data, and the eight consumer warps stream its weight rows
-//   from global memory while the producer fills the next stages.
+//   dense warp (warp 9): the bf16 shared expert's rows (stream.cuh
+//   DenseUnits, dense_stream.cuh), streamed beside the trellis units.
 
 #include "codec.cuh"
 #include "common.cuh"
-#include "dense_warp.cuh"
+#include "dense_stream.cuh"
+#include "launch.cuh"
 #include "stream.cuh"
 #include "tma.cuh"
 
 namespace exlr8 {
 
 constexpr int kConsumers = 8;
-constexpr int kStreamThreads = (kConsumers + 1) * 32;
+constexpr int kProducerWarp = kConsumers;
+constexpr int kDenseWarp = kConsumers + 1;
+constexpr int kStreamThreads = (kConsumers + 2) * 32;
 constexpr int kStages = 4;
+constexpr int kPlanCache = 160;  // plan groups / slots cached in shared memory (decode: <= 144 slots)
 constexpr int kStageTiles = 8;                       // K tiles per stage
 constexpr int kFragRowBytes = kStageTiles * 64 + 64;  // padded: rows hit different banks
 static_assert(kFragRowBytes >= kFragBlockBytes, "a fragment record fits its stage row");
 
-enum : int { kFirst = 1, kLast = 2, kEnd = 4, kDense = 8 };
+enum : int { kFirst = 1, kLast = 2, kEnd = 4 };
 
 template <int K>
 struct StageGeometry {
@@ -50,6 +52,8 @@ struct StageGeometry {
   static constexpr int kCodeBytes = kStageTiles * 8 * kTileWords * 4;
   static constexpr int kFragBytes = kMaxGroupRows * kFragRowBytes;
   static constexpr int kStageBytes = kCodeBytes + kFragBytes;
+  static constexpr int kRingBytes = kStages * kStageBytes;
+  static constexpr int kSmemBytes = kRingBytes + kDenseSmemBytes;  // ring, then the dense warp's buffers
 };
 
 __device__ __forceinline__ void mma_f16(float c[4], const uint32_t a[4], uint2 b) {
@@ -77,7 +81,9 @@ __device__ __forceinline__ uint32_t pair_from_products(uint32_t pa, uint32_t pb,
 
 // A fragment of one K4 tile from tile word l and word l-1.  `unit16` is the
 // runtime value 65536: it keeps the high-half extraction an IMAD.HI on the
-// multiply pipe instead of a shift on the integer pipe.
+// multiply pipe instead of a shift on the integer pipe.  (The window shifts
+// stay funnel shifts: moving them to IMADs as well measured slower, the
+// multiply pipe being the busier one per instruction.)
 __device__ __forceinline__ void k4_fragment(uint32_t word, uint32_t prior, uint32_t unit16, uint32_t mask,
                                             uint32_t xorv, uint32_t a[4]) {
   const uint32_t v0 = word;                              // (cw3 : cw7)
@@ -116,55 +122,85 @@ __global__ void __launch_bounds__(kStreamThreads, 2) trellis_stream_kernel(Strea
   __shared__ __align__(8) uint64_t full_bar[kStages];
   __shared__ __align__(8) uint64_t empty_bar[kStages];
   __shared__ int4 meta[kStages];  // unit, first K tile, K tiles, flags
+  // First stage of a unit: [0] rows of the unit's group, [1 + r] slot of row r
+  // (the consumers read the group from here, not from the global plan).
+  __shared__ int unit_rows[kStages][kMaxGroupRows + 1];
+  __shared__ __align__(8) uint64_t dense_bar[kDenseBuffers];
+  __shared__ int plan_cache[4][kPlanCache];  // group expert, start, count; slot order (producer)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int it = p.in_features / 16, ot = p.out_features / 16, nblocks = ot / 8;
+  pdl_launch_dependents();
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&full_bar[s], 1);
       mbar_init(&empty_bar[s], kConsumers);
     }
+    for (int b = 0; b < kDenseBuffers; ++b) mbar_init(&dense_bar[b], 1);
     mbar_fence_init();
   }
   __syncthreads();
+  pdl_wait();  // the plan, fragments and partial buffers belong to earlier kernels
 
-  if (warp == kConsumers) {
+  if (warp == kDenseWarp) {
+    // ---------------- dense warp ----------------
+    if (p.dense.units > 0 &&
+        !dense_warp_run(p.dense, &p.plan.header[p.dense.counter], smem + G::kRingBytes, dense_bar, lane)) {
+      if (lane == 0) atomicOr(&p.plan.header[9], 4);
+      // Copies already issued target valid addresses and land within
+      // microseconds; give them that time before this warp retires.
+      for (int i = 0; i < 1000; ++i) __nanosleep(1000);
+    }
+    return;
+  }
+
+  if (warp == kProducerWarp) {
     // ---------------- producer ----------------
-    if (lane != 0) return;
+    // The plan's groups and slot order (decode batches: at most kPlanCache of
+    // each) are cached in shared memory by the whole warp, so that a unit
+    // boundary costs no global round trip; larger plans are read in place.
     const int groups = p.plan.header[0];
-    const int64_t dense_total = p.dense.units;
-    const int64_t total = dense_total + static_cast<int64_t>(groups) * p.projections * nblocks * p.splits;
+    const bool cached = groups <= kPlanCache && p.nslots <= kPlanCache;
+    if (cached) {
+      for (int g = lane; g < groups; g += 32) {
+        plan_cache[0][g] = p.plan.group_expert[g];
+        plan_cache[1][g] = p.plan.group_start[g];
+        plan_cache[2][g] = p.plan.group_count[g];
+      }
+      for (int i = lane; i < p.nslots; i += 32) plan_cache[3][i] = p.plan.order[i];
+      __syncwarp();
+    }
+    if (lane != 0) return;
+    const int64_t total = static_cast<int64_t>(groups) * p.projections * nblocks * p.splits;
     int stage = 0;
     uint32_t phase = 0;
     bool failed = false;
+    // Each CTA's first unit is its index; later units come from the counter,
+    // fetched one unit ahead so that the atomic's round trip overlaps the
+    // current unit's stages.
+    int64_t unit = blockIdx.x;
     for (;;) {
-      const int64_t next = atomicAdd(&p.plan.header[p.counter], 1);
+      const int64_t next = static_cast<int64_t>(gridDim.x) + atomicAdd(&p.plan.header[p.counter], 1);
       if (!mbar_wait(&empty_bar[stage], phase ^ 1u)) {
         failed = true;
         break;
       }
-      if (next >= total) {
+      if (unit >= total) {
         meta[stage] = make_int4(0, 0, 0, kEnd);
         mbar_arrive(&full_bar[stage]);
         break;
       }
-      if (next < dense_total) {
-        meta[stage] = make_int4(static_cast<int>(next), 0, 0, kDense);
-        mbar_arrive(&full_bar[stage]);
-        if (++stage == kStages) {
-          stage = 0;
-          phase ^= 1u;
-        }
-        continue;
-      }
-      const int64_t unit = next - dense_total;
       const UnitInfo u = decode_unit(unit, p, nblocks);
-      const int expert = p.plan.group_expert[u.group];
-      const int start = p.plan.group_start[u.group];
-      const int nr = p.plan.group_count[u.group];
+      const int expert = cached ? plan_cache[0][u.group] : p.plan.group_expert[u.group];
+      const int start = cached ? plan_cache[1][u.group] : p.plan.group_start[u.group];
+      const int nr = cached ? plan_cache[2][u.group] : p.plan.group_count[u.group];
       const int kt0 = u.split * p.kt_per_split;
       const int kt1 = min(kt0 + p.kt_per_split, it);
       const uint32_t* words = p.packed[u.proj];
+      int slots[kMaxGroupRows];
+#pragma unroll
+      for (int r = 0; r < kMaxGroupRows; ++r)
+        slots[r] = r < nr ? (cached ? plan_cache[3][start + r] : p.plan.order[start + r]) : -1;
       for (int kt = kt0; kt < kt1; kt += kStageTiles) {
         if (kt != kt0) {
           if (!mbar_wait(&empty_bar[stage], phase ^ 1u)) {
@@ -175,13 +211,20 @@ __global__ void __launch_bounds__(kStreamThreads, 2) trellis_stream_kernel(Strea
         const int n = min(kStageTiles, kt1 - kt);
         meta[stage] = make_int4(static_cast<int>(unit), kt, n,
                                 (kt == kt0 ? kFirst : 0) | (kt + kStageTiles >= kt1 ? kLast : 0));
+        if (kt == kt0) {
+          unit_rows[stage][0] = nr;
+#pragma unroll
+          for (int r = 0; r < kMaxGroupRows; ++r) unit_rows[stage][1 + r] = slots[r];
+        }
         unsigned char* base = smem + stage * G::kStageBytes;
         const uint32_t code_bytes = static_cast<uint32_t>(n) * 8u * G::kTileWords * 4u;
         mbar_arrive_expect_tx(&full_bar[stage], code_bytes + static_cast<uint32_t>(nr) * kFragBlockBytes);
         const uint32_t* src = words + tile_index(expert, kt, u.nb * 8, it, ot, p.side) * G::kTileWords;
         bulk_copy_g2s(base, src, code_bytes, &full_bar[stage]);
-        for (int r = 0; r < nr; ++r) {
-          const int slot = p.plan.order[start + r];
+#pragma unroll
+        for (int r = 0; r < kMaxGroupRows; ++r) {
+          if (r >= nr) break;
+          const int slot = slots[r];
           const unsigned char* fsrc =
               p.frag + ((static_cast<int64_t>(u.proj) * p.nslots + slot) * (it / 8) + kt / 8) * kFragBlockBytes;
           bulk_copy_g2s(base + G::kCodeBytes + r * kFragRowBytes, fsrc, kFragBlockBytes, &full_bar[stage]);
@@ -192,6 +235,7 @@ __global__ void __launch_bounds__(kStreamThreads, 2) trellis_stream_kernel(Strea
         }
       }
       if (failed) break;
+      unit = next;
     }
     if (failed) {
       atomicOr(&p.plan.header[9], 1);
@@ -225,32 +269,12 @@ __global__ void __launch_bounds__(kStreamThreads, 2) trellis_stream_kernel(Strea
     }
     const int4 m = meta[stage];
     if (m.w & kEnd) break;
-    if (m.w & kDense) {
-      // The stage carries no data: release it, then stream this warp's 16
-      // rows of the unit's 128-row block over the unit's K split.
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&empty_bar[stage]);
-      const DenseUnits& d = p.dense;
-      const int rbs = d.n / 128;
-      const int rb = m.x % rbs, split = m.x / rbs;
-      const int steps = d.k / 32, per = (steps + d.splits - 1) / d.splits;
-      const int s0 = split * per, s1 = min(s0 + per, steps);
-      const int64_t part = static_cast<int64_t>(split) * d.tokens * d.n;
-      dense_rows<2>(d.x, d.tokens, d.w0, d.w1, d.n, d.k, rb * 128 + warp * 16, s0, s1, d.p0 + part,
-                    d.w1 ? d.p1 + part : nullptr, lane);
-      if (++stage == kStages) {
-        stage = 0;
-        phase ^= 1u;
-      }
-      continue;
-    }
     if (m.w & kFirst) {
       u = decode_unit(m.x, p, nblocks);
-      const int start = p.plan.group_start[u.group];
-      nr = p.plan.group_count[u.group];
+      nr = unit_rows[stage][0];
       ncg = (nr + 3) >> 2;
-      slot_a = tig < nr ? p.plan.order[start + tig] : -1;
-      slot_b = 4 + tig < nr ? p.plan.order[start + 4 + tig] : -1;
+      slot_a = unit_rows[stage][1 + tig];
+      slot_b = unit_rows[stage][5 + tig];
     }
     const unsigned char* base = smem + stage * G::kStageBytes;
     const uint32_t* codes = reinterpret_cast<const uint32_t*>(base);
@@ -338,7 +362,7 @@ static cudaError_t launch_stream_k(const StreamParams& p, cudaStream_t s) {
   // Attribute and occupancy are queried once per process (the launch shape is
   // fixed: one persistent CTA per resident slot).
   static int grid = 0;
-  const int smem = kStages * StageGeometry<K>::kStageBytes;
+  const int smem = StageGeometry<K>::kSmemBytes;
   if (grid == 0) {
     cudaError_t err =
         cudaFuncSetAttribute(trellis_stream_kernel<K>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
@@ -346,13 +370,13 @@ static cudaError_t launch_stream_k(const StreamParams& p, cudaStream_t s) {
     int device = 0, sms = 0, per_sm = 0;
     if ((err = cudaGetDevice(&device)) != cudaSuccess) return err;
     if ((err = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device)) != cudaSuccess) return err;
+    if ((err = prefer_shared_carveout(trellis_stream_kernel<K>)) != cudaSuccess) return err;
     if ((err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, trellis_stream_kernel<K>, kStreamThreads,
                                                              smem)) != cudaSuccess)
       return err;
     grid = sms * (per_sm < 1 ? 1 : per_sm);
   }
-  trellis_stream_kernel<K><<<grid, kStreamThreads, smem, s>>>(p);
-  return cudaGetLastError();
+  return launch_pdl(trellis_stream_kernel<K>, dim3(grid), dim3(kStreamThreads), static_cast<size_t>(smem), s, p);
 }
 
 cudaError_t launch_stream(const StreamParams& p, cudaStream_t s) {
