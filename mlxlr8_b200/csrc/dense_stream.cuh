@@ -94,22 +94,16 @@ __device__ __forceinline__ void dense_chunk_products(const unsigned char* src, b
   }
 }
 
-// The dense warp's loop over its units.  `buf` is kDenseSmemBytes of shared
-// memory, `bars` kDenseBuffers mbarriers initialised with count 1.  Returns
-// false when a bounded wait timed out (copies it issued have landed or been
-// waited for up to the limit).
-__device__ __forceinline__ bool dense_warp_run(const DenseUnits& d, int* counter, unsigned char* buf, uint64_t* bars,
-                                               int lane) {
+// The dense warp's loop over its units: CTA b takes units b, b + grid, ...
+// (a static assignment: no counter to reset between calls).  `buf` is
+// kDenseSmemBytes of shared memory, `bars` kDenseBuffers mbarriers
+// initialised with count 1.  Returns false when a bounded wait timed out.
+__device__ __forceinline__ bool dense_warp_run(const DenseUnits& d, unsigned char* buf, uint64_t* bars, int lane) {
   const int groups = d.n / kDenseRows;
   const int chunks = d.k / d.splits / kDenseChunk;
   const bool two = d.w1 != nullptr;
   uint32_t issued = 0, consumed = 0;  // chunk sequence numbers (buffer = seq % kDenseBuffers)
-  int unit = 0;
-  if (lane == 0) unit = atomicAdd(counter, 1);
-  unit = __shfl_sync(0xffffffffu, unit, 0);
-  while (unit < d.units) {
-    int next = 0;
-    if (lane == 0) next = atomicAdd(counter, 1);  // in flight while this unit streams
+  for (int unit = blockIdx.x; unit < d.units; unit += gridDim.x) {
     const int g = unit % groups, split = unit / groups;
     const int n0 = g * kDenseRows, k0 = split * (d.k / d.splits);
     for (int t0 = 0; t0 < d.tokens; t0 += kDenseTokens) {
@@ -156,7 +150,6 @@ __device__ __forceinline__ bool dense_warp_run(const DenseUnits& d, int* counter
         }
       }
     }
-    unit = __shfl_sync(0xffffffffu, next, 0);
   }
   return true;
 }

@@ -34,7 +34,11 @@ struct DenseUnits {
   float* p0;           // [splits][tokens][n] partials of w0
   float* p1;           // same for w1
   int n, k, tokens, splits, units;  // units = (n / 16) * splits, 0 = none
-  int counter;                      // plan header slot of the dense unit counter
+  // 1: the inputs (W, W1, x) and outputs (p0, p1) do not depend on the
+  // kernels launched since the head of the call's kernel chain, so the dense
+  // warp starts without waiting for its predecessor grid (launch.cuh).  The
+  // chain head is launched with full stream ordering, which makes that safe.
+  int early;
 };
 
 struct StreamParams {

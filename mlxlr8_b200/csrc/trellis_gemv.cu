@@ -75,10 +75,12 @@ cudaError_t launch_plan(const uint32_t* ids, int rows, int experts, int period, 
                                            static_cast<int>(smem));
     if (err != cudaSuccess) return err;
   }
+  // The plan heads its call's kernel chain: a plain launch, fully ordered
+  // after earlier work in the stream (later kernels of the chain rely on it).
   static const cudaError_t carve = prefer_shared_carveout(plan_kernel);
   if (carve != cudaSuccess) return carve;
-  return launch_pdl(plan_kernel, dim3(1), dim3(kPlanThreads), smem, s, ids, rows, experts, period > 0 ? period : 1,
-                    skip_slot, plan);
+  plan_kernel<<<1, kPlanThreads, smem, s>>>(ids, rows, experts, period > 0 ? period : 1, skip_slot, plan);
+  return cudaGetLastError();
 }
 
 // ---------------------------------------------------------------------------

@@ -140,12 +140,14 @@ __global__ void __launch_bounds__(kStreamThreads, 2) trellis_stream_kernel(Strea
     mbar_fence_init();
   }
   __syncthreads();
-  pdl_wait();  // the plan, fragments and partial buffers belong to earlier kernels
 
   if (warp == kDenseWarp) {
     // ---------------- dense warp ----------------
-    if (p.dense.units > 0 &&
-        !dense_warp_run(p.dense, &p.plan.header[p.dense.counter], smem + G::kRingBytes, dense_bar, lane)) {
+    // The gate/up launch's dense rows need nothing from the kernels before
+    // it in the chain (stream.cuh DenseUnits::early): they stream while the
+    // routing and the fragment prep finish.
+    if (!p.dense.early) pdl_wait();
+    if (p.dense.units > 0 && !dense_warp_run(p.dense, smem + G::kRingBytes, dense_bar, lane)) {
       if (lane == 0) atomicOr(&p.plan.header[9], 4);
       // Copies already issued target valid addresses and land within
       // microseconds; give them that time before this warp retires.
@@ -153,6 +155,8 @@ __global__ void __launch_bounds__(kStreamThreads, 2) trellis_stream_kernel(Strea
     }
     return;
   }
+
+  pdl_wait();  // the plan, fragments and partial buffers belong to earlier kernels
 
   if (warp == kProducerWarp) {
     // ---------------- producer ----------------
