@@ -82,6 +82,9 @@ def parse():
     p.add_argument("--no-extras", action="store_true",
                    help="skip the single-GPU extras (decode at T=8/32, the prefill configurations)")
     p.add_argument("--calls", type=int, default=5)
+    p.add_argument("--ep-exchange", choices=("peer", "nccl"), default="peer",
+                   help="N > 1: the expert-parallel exchange, over peer memory (NVLink stores + epoch flags) or "
+                        "NCCL all-to-all")
     return p.parse_args()
 
 
@@ -401,7 +404,7 @@ def main():
             for p in ("gate", "up", "down"):
                 shard.packed[p] = shard.packed[p].clone()
             moes.append(ExpertParallelMoE(layer.gate_weight, layer.bias, shard, rank, world,
-                                          shared=layer.experts.shared))
+                                          shared=layer.experts.shared, exchange=args.ep_exchange, max_tokens=T))
         x, r = layer.tokens(T, seed_offset=i * world + rank)
         xs.append(x)
         rs.append(r)
@@ -409,6 +412,12 @@ def main():
             del layer.experts.packed  # only the shard stays resident
         layers.append(layer)
     torch.cuda.synchronize()
+    if world > 1:
+        # One eager call per layer, in the same order on every rank: the
+        # peer-memory exchange maps its regions (a collective) on first use.
+        for i in range(L):
+            moes[i](xs[i], rs[i])
+        torch.cuda.synchronize()
 
     # CUDA graphs of one layer call each (inputs resident in HBM); with several
     # GPUs the graphs hold the NCCL exchange too.  Graph references live only
@@ -464,6 +473,9 @@ def main():
         elapsed = float(t.item())
     ms_per_step = elapsed / args.steps
     value = world * T * args.steps / (elapsed / 1000.0)
+    for m in moes:  # a peer exchange that timed out or lost slots invalidates the run
+        if getattr(m, "peer", None) is not None:
+            m.peer.check()
 
     # ---- profiled pass: per-kernel CUDA events on the launching stream ----
     routing = []
@@ -564,8 +576,10 @@ def main():
                        "hidden": HIDDEN, "intermediate": INTER, "experts": EXPERTS, "k_bits": K_BITS,
                        "layers_cycled": L,
                        "l2": "inputs larger than L2: each step is a different layer (>233 MB touched per step)",
-                       "parallelism": (f"expert parallel x{world}: {EXPERTS // world} routed experts per GPU, NCCL "
-                                       "all-to-all dispatch/combine, shared expert replicated") if world > 1
+                       "parallelism": (f"expert parallel x{world}: {EXPERTS // world} routed experts per GPU, "
+                                       + ("peer-memory (NVLink) dispatch/combine" if args.ep_exchange == "peer"
+                                          else "NCCL all-to-all dispatch/combine")
+                                       + ", shared expert replicated") if world > 1
                        else "single GPU"},
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "steps": e2e_steps},
@@ -589,6 +603,9 @@ def main():
     outs.clear()
     torch.cuda.synchronize()
     if world > 1:
+        for m in moes:
+            if getattr(m, "peer", None) is not None:
+                m.peer.close()
         dist.barrier()
         dist.destroy_process_group()
 

@@ -270,8 +270,59 @@ int exlr8_ep_dispatch(const uint32_t* indices, int64_t tokens, const void* x, in
 int exlr8_ep_combine(const void* values, int x_dtype, const int32_t* slot_pos, const float* scores, const void* shared,
                      const void* residual, int64_t tokens, int hidden, void* out, void* stream);
 
+/*
+ * Peer-memory exchange for the expert-parallel layer (in place of the
+ * dispatch + NCCL all-to-all + all-to-all back).  Each rank creates one
+ * region (exlr8_ep_peer_create: the one entry point here that allocates
+ * device memory, once per layer), publishes its 64-byte CUDA IPC handle to
+ * the other ranks (the caller's collective) and opens theirs
+ * (exlr8_ep_peer_open).  `peers` is a device array of `ranks` uint64 region
+ * addresses as seen from this rank (its own region at [rank]).  Per layer
+ * call, on every rank with the same token count:
+ *   exlr8_ep_send    routed rows -> owners' regions; waits for the rows
+ *                    addressed to this rank (received rows at offset `rows`
+ *                    [ranks][C][hidden], local expert ids at `meta` [ranks][C])
+ *   exlr8_expert_mlp_shared on those rows (ids -1 = empty)
+ *   exlr8_ep_return  values [ranks * C][hidden] -> sources' regions; waits
+ *                    for this rank's values (offset `back`), then advances
+ *                    the region's epoch
+ *   exlr8_ep_combine with values = region + back
+ * C = tokens * 8 <= max_capacity <= 4096; ranks <= 64; hidden * element size
+ * a multiple of 16.  status int32 [2]: [0] slots lost to overflow, [1] bit 0
+ * / bit 1 when a wait for a peer timed out (about 1 s; the call's outputs are
+ * then invalid).  Regions start zeroed; all ranks must make the same calls.
+ */
+size_t exlr8_ep_peer_bytes(int ranks, int max_capacity, int hidden, int x_dtype);
+int exlr8_ep_peer_offsets(int ranks, int max_capacity, int hidden, int x_dtype, size_t* meta, size_t* rows,
+                          size_t* back);
+int exlr8_ep_peer_create(size_t bytes, void** region, void* ipc_handle);
+int exlr8_ep_peer_open(const void* ipc_handle, void** region);
+int exlr8_ep_peer_close(void* region);
+int exlr8_ep_peer_destroy(void* region);
+int exlr8_ep_send(const uint32_t* indices, int64_t tokens, const void* x, int x_dtype, int hidden, int ranks, int rank,
+                  int experts_per_rank, int max_capacity, const uint64_t* peers, void* region, int32_t* slot_pos,
+                  int32_t* status, void* stream);
+int exlr8_ep_return(const void* values, int x_dtype, int hidden, int ranks, int rank, int64_t tokens,
+                    int max_capacity, const uint64_t* peers, void* region, int32_t* status, void* stream);
+
 /* Typed output of the dense bf16 shared expert for every token (slot 8 of
  * the combine): T(down(SwiGLU(T(x Wg^T), T(x Wu^T)))). */
+/* The owner's half of an expert-parallel layer in one call: the trellis
+ * expert MLP over `rows` received rows (x [rows][hidden], one expert id per
+ * row in indices [rows]; ids outside [0, experts) give zeros), written to
+ * out [rows][hidden] as exlr8_expert_mlp with slots = 1 would, and the bf16
+ * shared expert over the rank's own tokens (shared_x [shared_tokens][hidden])
+ * written typed to shared_out [shared_tokens][hidden] as exlr8_shared_expert
+ * would.  Up to 4096 rows the shared expert's rows stream inside the trellis
+ * kernels (bound by their decode arithmetic, not by HBM); beyond that the two
+ * run one after the other.  bf16 activations; x, shared_x 16-byte aligned. */
+size_t exlr8_expert_mlp_shared_workspace(int64_t rows, int hidden, int intermediate, int64_t experts,
+                                         int64_t shared_tokens);
+int exlr8_expert_mlp_shared(const void* x, int x_dtype, const uint32_t* indices, int64_t rows,
+                            const exlr8_trellis_experts* experts, const void* shared_x, int64_t shared_tokens,
+                            const exlr8_dense_expert* shared, void* out, void* shared_out, void* workspace,
+                            size_t workspace_bytes, void* stream);
+
 size_t exlr8_shared_expert_workspace(int64_t tokens, int hidden, int intermediate);
 int exlr8_shared_expert(const void* x, int x_dtype, int64_t tokens, int hidden, int intermediate,
                         const exlr8_dense_expert* shared, void* out, void* workspace, size_t workspace_bytes,

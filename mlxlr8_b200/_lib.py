@@ -109,6 +109,20 @@ _SIGNATURES = {
                                   c_void_p, c_void_p, c_void_p, c_void_p]),
     "exlr8_ep_combine": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int, c_void_p,
                                  c_void_p]),
+    "exlr8_ep_peer_bytes": (c_size_t, [c_int, c_int, c_int, c_int]),
+    "exlr8_ep_peer_offsets": (c_int, [c_int, c_int, c_int, c_int, POINTER(c_size_t), POINTER(c_size_t),
+                                      POINTER(c_size_t)]),
+    "exlr8_ep_peer_create": (c_int, [c_size_t, POINTER(c_void_p), c_void_p]),
+    "exlr8_ep_peer_open": (c_int, [c_void_p, POINTER(c_void_p)]),
+    "exlr8_ep_peer_close": (c_int, [c_void_p]),
+    "exlr8_ep_peer_destroy": (c_int, [c_void_p]),
+    "exlr8_ep_send": (c_int, [c_void_p, c_int64, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_void_p,
+                              c_void_p, c_void_p, c_void_p, c_void_p]),
+    "exlr8_ep_return": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_int64, c_int, c_void_p, c_void_p, c_void_p,
+                                c_void_p]),
+    "exlr8_expert_mlp_shared_workspace": (c_size_t, [c_int64, c_int, c_int, c_int64, c_int64]),
+    "exlr8_expert_mlp_shared": (c_int, [c_void_p, c_int, c_void_p, c_int64, POINTER(TrellisExperts), c_void_p, c_int64,
+                                        POINTER(DenseExpert), c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),
     "exlr8_shared_expert_workspace": (c_size_t, [c_int64, c_int, c_int]),
     "exlr8_shared_expert": (c_int, [c_void_p, c_int, c_int64, c_int, c_int, POINTER(DenseExpert), c_void_p, c_void_p,
                                     c_size_t, c_void_p]),

@@ -208,12 +208,14 @@ int launch_dense_decode(const void* x, int x_dtype, int64_t tokens, const exlr8_
 // The trellis MLP over all slots of `ids` ([rows] = tokens*slots) after the
 // plan: activation fragments, the gate/up stream, the gate/up finish into the
 // down fragments, the down stream.  Leaves fp32 down partials.  With
-// `shared` the bf16 shared expert of the `tokens` rows of x runs as dense
-// units of the two stream launches (its SwiGLU in the gate/up finish) and
-// leaves its down partials [l.s2.count][tokens][hidden] in b.ddown.
+// `shared` the bf16 shared expert of the `tokens` rows of dense_x runs as
+// dense units of the two stream launches (its SwiGLU in the gate/up finish)
+// and leaves its down partials [dense_down_splits][tokens][hidden] in
+// b.ddown.
 int run_mlp_after_plan(const void* x, int x_dtype, int per_slot, int slots, const uint32_t* ids, int64_t rows,
                        const exlr8_trellis_experts* ex, int64_t experts, const exlr8_dense_expert* shared,
-                       int64_t tokens, const MlpLayout& l, const MlpBuffers& b, cudaStream_t s) {
+                       const void* dense_x, int64_t tokens, const MlpLayout& l, const MlpBuffers& b,
+                       cudaStream_t s) {
   const int h = ex->hidden, m = ex->intermediate;
   const int n = static_cast<int>(rows), e = static_cast<int>(experts), t = static_cast<int>(tokens);
   EXLR8_TIMED(EXLR8_KERNEL_PREP, s,
@@ -233,7 +235,7 @@ int run_mlp_after_plan(const void* x, int x_dtype, int per_slot, int slots, cons
   const int dsplits_gu = dense_gate_up_splits(h), dsplits_d = dense_down_splits(m);
   if (shared)
     gp.dense = DenseUnits{static_cast<const uint16_t*>(shared->gate), static_cast<const uint16_t*>(shared->up),
-                          static_cast<const uint16_t*>(x), b.dgate, b.dup, m, h, t, dsplits_gu,
+                          static_cast<const uint16_t*>(dense_x), b.dgate, b.dup, m, h, t, dsplits_gu,
                           (m / kDenseRows) * dsplits_gu, 1};
   EXLR8_TIMED(EXLR8_KERNEL_GATE_UP, s, launch_stream(gp, s));
   EXLR8_TIMED(EXLR8_KERNEL_GATE_FINISH, s,
@@ -597,7 +599,8 @@ int exlr8_expert_mlp(const void* x, int x_dtype, int per_slot, const uint32_t* i
   const MlpBuffers b = carve_mlp(l, rows, experts, false, tokens, ex->hidden, ex->intermediate, c);
   EXLR8_TIMED(EXLR8_KERNEL_PLAN, s,
               launch_plan(indices, static_cast<int>(rows), static_cast<int>(experts), slots, -1, b.plan, s));
-  EXLR8_CHECK(run_mlp_after_plan(x, x_dtype, per_slot, slots, indices, rows, ex, experts, nullptr, tokens, l, b, s));
+  EXLR8_CHECK(
+      run_mlp_after_plan(x, x_dtype, per_slot, slots, indices, rows, ex, experts, nullptr, nullptr, tokens, l, b, s));
   ProfileScope scope(EXLR8_KERNEL_FINISH, s);
   return cuda_status(launch_finish(b.dpart, l.s2.count, nullptr, indices, static_cast<int>(rows), ex->out_scale[2],
                                    ex->scale_dtype, ex->hidden, static_cast<int>(experts), x_dtype, out, s));
@@ -631,7 +634,7 @@ static int mlp_finish_after_plan(const void* x, int x_dtype, const uint32_t* ind
                                  int64_t experts, const exlr8_dense_expert* shared, void* out, const MlpLayout& l,
                                  const MlpBuffers& b, cudaStream_t s) {
   const int64_t rows = tokens * 9;
-  EXLR8_CHECK(run_mlp_after_plan(x, x_dtype, 0, 9, indices, rows, ex, experts, shared, tokens, l, b, s));
+  EXLR8_CHECK(run_mlp_after_plan(x, x_dtype, 0, 9, indices, rows, ex, experts, shared, x, tokens, l, b, s));
   ProfileScope scope(EXLR8_KERNEL_FINISH, s);
   return cuda_status(launch_finish_fused(b.dpart, l.s2.count, nullptr, indices, static_cast<int>(tokens), ex->out_scale[2],
                                          ex->scale_dtype, ex->hidden, static_cast<int>(experts), scores, residual,
@@ -786,6 +789,142 @@ int exlr8_ep_combine(const void* values, int x_dtype, const int32_t* slot_pos, c
   if (!values || !slot_pos || !scores || !shared || !residual || !out) return EXLR8_ERR_ARG;
   return cuda_status(launch_ep_combine(values, x_dtype, slot_pos, scores, shared, residual, static_cast<int>(tokens),
                                        hidden, out, as_stream(stream)));
+}
+
+// ---- peer-memory exchange of the expert-parallel layer ---------------------
+
+namespace {
+int elem_size(int x_dtype) { return x_dtype == EXLR8_DTYPE_F32 ? 4 : 2; }
+int check_peer_shape(int ranks, int max_capacity, int hidden, int x_dtype) {
+  if (!valid_act(x_dtype)) return EXLR8_ERR_DTYPE;
+  if (ranks < 1 || ranks > kPeerMaxRanks || max_capacity < 0 || max_capacity > 4096 || hidden <= 0)
+    return EXLR8_ERR_ARG;
+  if ((static_cast<int64_t>(hidden) * elem_size(x_dtype)) % 16) return EXLR8_ERR_DIMS;
+  return EXLR8_OK;
+}
+}  // namespace
+
+size_t exlr8_ep_peer_bytes(int ranks, int max_capacity, int hidden, int x_dtype) {
+  if (check_peer_shape(ranks, max_capacity, hidden, x_dtype) != EXLR8_OK) return 0;
+  return peer_layout(ranks, max_capacity, hidden, elem_size(x_dtype)).total;
+}
+
+int exlr8_ep_peer_offsets(int ranks, int max_capacity, int hidden, int x_dtype, size_t* meta, size_t* rows,
+                          size_t* back) {
+  EXLR8_CHECK(check_peer_shape(ranks, max_capacity, hidden, x_dtype));
+  if (!meta || !rows || !back) return EXLR8_ERR_ARG;
+  const PeerLayout l = peer_layout(ranks, max_capacity, hidden, elem_size(x_dtype));
+  *meta = l.meta;
+  *rows = l.rows;
+  *back = l.back;
+  return EXLR8_OK;
+}
+
+int exlr8_ep_peer_create(size_t bytes, void** region, void* ipc_handle) {
+  if (!region || !ipc_handle || bytes == 0) return EXLR8_ERR_ARG;
+  void* p = nullptr;
+  EXLR8_TRY(cudaMalloc(&p, bytes));
+  cudaError_t err = cudaMemset(p, 0, bytes);
+  cudaIpcMemHandle_t handle;
+  if (err == cudaSuccess) err = cudaIpcGetMemHandle(&handle, p);
+  if (err != cudaSuccess) {
+    cudaFree(p);
+    return cuda_status(err);
+  }
+  std::memcpy(ipc_handle, &handle, sizeof(handle));
+  *region = p;
+  return EXLR8_OK;
+}
+
+int exlr8_ep_peer_open(const void* ipc_handle, void** region) {
+  if (!ipc_handle || !region) return EXLR8_ERR_ARG;
+  cudaIpcMemHandle_t handle;
+  std::memcpy(&handle, ipc_handle, sizeof(handle));
+  return cuda_status(cudaIpcOpenMemHandle(region, handle, cudaIpcMemLazyEnablePeerAccess));
+}
+
+int exlr8_ep_peer_close(void* region) { return region ? cuda_status(cudaIpcCloseMemHandle(region)) : EXLR8_OK; }
+
+int exlr8_ep_peer_destroy(void* region) { return region ? cuda_status(cudaFree(region)) : EXLR8_OK; }
+
+int exlr8_ep_send(const uint32_t* indices, int64_t tokens, const void* x, int x_dtype, int hidden, int ranks, int rank,
+                  int experts_per_rank, int max_capacity, const uint64_t* peers, void* region, int32_t* slot_pos,
+                  int32_t* status, void* stream) {
+  EXLR8_CHECK(check_peer_shape(ranks, max_capacity, hidden, x_dtype));
+  if (tokens < 0 || tokens * 8 > max_capacity) return EXLR8_ERR_ROWS;
+  if (rank < 0 || rank >= ranks || experts_per_rank <= 0) return EXLR8_ERR_ARG;
+  if (!peers || !region || !status || (tokens > 0 && (!indices || !x || !slot_pos))) return EXLR8_ERR_ARG;
+  if ((x && !aligned16(x)) || !aligned16(region)) return EXLR8_ERR_ALIGN;
+  return cuda_status(launch_ep_send(indices, static_cast<int>(tokens), x, x_dtype, hidden, ranks, rank,
+                                    experts_per_rank, static_cast<int>(tokens * 8), max_capacity, peers, region,
+                                    slot_pos, status, as_stream(stream)));
+}
+
+int exlr8_ep_return(const void* values, int x_dtype, int hidden, int ranks, int rank, int64_t tokens,
+                    int max_capacity, const uint64_t* peers, void* region, int32_t* status, void* stream) {
+  EXLR8_CHECK(check_peer_shape(ranks, max_capacity, hidden, x_dtype));
+  if (tokens < 0 || tokens * 8 > max_capacity) return EXLR8_ERR_ROWS;
+  if (rank < 0 || rank >= ranks) return EXLR8_ERR_ARG;
+  if (!peers || !region || !status || (tokens > 0 && !values)) return EXLR8_ERR_ARG;
+  if ((values && !aligned16(values)) || !aligned16(region)) return EXLR8_ERR_ALIGN;
+  return cuda_status(launch_ep_return(values, x_dtype, hidden, ranks, rank, static_cast<int>(tokens * 8),
+                                      max_capacity, peers, region, status, as_stream(stream)));
+}
+
+// ---- owner's half of an expert-parallel layer -----------------------------
+
+constexpr int64_t kFusedSharedMaxRows = 4096;  // stream path with dense units up to this many rows
+
+size_t exlr8_expert_mlp_shared_workspace(int64_t rows, int hidden, int intermediate, int64_t experts,
+                                         int64_t shared_tokens) {
+  if (rows <= kFusedSharedMaxRows)
+    return mlp_layout(rows, hidden, intermediate, experts).total() +
+           dense_layout(shared_tokens, hidden, intermediate).total();
+  return align_up(exlr8_expert_mlp_workspace(rows, 1, hidden, intermediate, experts)) +
+         exlr8_shared_expert_workspace(shared_tokens, hidden, intermediate);
+}
+
+int exlr8_expert_mlp_shared(const void* x, int x_dtype, const uint32_t* indices, int64_t rows,
+                            const exlr8_trellis_experts* ex, const void* shared_x, int64_t shared_tokens,
+                            const exlr8_dense_expert* shared, void* out, void* shared_out, void* workspace,
+                            size_t workspace_bytes, void* stream) {
+  int64_t experts = 0;
+  EXLR8_CHECK(check_experts(ex, &experts));
+  if (!valid_act(x_dtype)) return EXLR8_ERR_DTYPE;
+  if (!shared) return EXLR8_ERR_ARG;
+  EXLR8_CHECK(check_dense(shared, x_dtype, ex->hidden, ex->intermediate));
+  if (rows < 0 || shared_tokens < 0) return EXLR8_ERR_ROWS;
+  if ((rows > 0 && (!x || !indices || !out)) || (shared_tokens > 0 && (!shared_x || !shared_out)))
+    return EXLR8_ERR_ARG;
+  if ((x && !aligned16(x)) || (shared_x && !aligned16(shared_x))) return EXLR8_ERR_ALIGN;
+  if (rows > (1 << 20) || shared_tokens > (1 << 20)) return EXLR8_ERR_UNSUPPORTED;
+  if (!workspace ||
+      workspace_bytes < exlr8_expert_mlp_shared_workspace(rows, ex->hidden, ex->intermediate, experts, shared_tokens))
+    return EXLR8_ERR_WORKSPACE;
+  cudaStream_t s = as_stream(stream);
+  const int h = ex->hidden, m = ex->intermediate;
+  if (rows > kFusedSharedMaxRows) {
+    const size_t mlp_bytes = align_up(exlr8_expert_mlp_workspace(rows, 1, h, m, experts));
+    EXLR8_CHECK(exlr8_expert_mlp(x, x_dtype, 1, indices, rows, 1, ex, out, workspace, mlp_bytes, stream));
+    if (shared_tokens == 0) return EXLR8_OK;
+    return exlr8_shared_expert(shared_x, x_dtype, shared_tokens, h, m, shared, shared_out,
+                               static_cast<char*>(workspace) + mlp_bytes, workspace_bytes - mlp_bytes, stream);
+  }
+  if (rows == 0 && shared_tokens == 0) return EXLR8_OK;
+  const MlpLayout l = mlp_layout(rows, h, m, experts);
+  Carver c(workspace);
+  const MlpBuffers b = carve_mlp(l, rows, experts, true, shared_tokens, h, m, c);
+  const int n = static_cast<int>(rows), e = static_cast<int>(experts);
+  EXLR8_TIMED(EXLR8_KERNEL_PLAN, s, launch_plan(indices, n, e, 1, -1, b.plan, s));
+  EXLR8_CHECK(run_mlp_after_plan(x, x_dtype, 1, 1, indices, rows, ex, experts, shared_tokens > 0 ? shared : nullptr,
+                                 shared_x, shared_tokens, l, b, s));
+  if (rows > 0) {
+    ProfileScope scope(EXLR8_KERNEL_FINISH, s);
+    EXLR8_TRY(launch_finish(b.dpart, l.s2.count, nullptr, indices, n, ex->out_scale[2], ex->scale_dtype, h, e,
+                            x_dtype, out, s));
+  }
+  if (shared_tokens == 0) return EXLR8_OK;
+  return cuda_status(launch_sum_cast(b.ddown, dense_down_splits(m), shared_tokens * h, x_dtype, shared_out, s));
 }
 
 size_t exlr8_shared_expert_workspace(int64_t tokens, int hidden, int intermediate) {

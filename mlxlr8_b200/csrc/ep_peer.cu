@@ -1,0 +1,181 @@
+// Expert-parallel exchange over peer memory (NVLink): the dispatch stores each
+// routed row straight into its owner's region, the owner's values go back the
+// same way, and per-source epoch flags (release stores, acquire loads at
+// system scope) tell each side that a peer's rows have landed.  One kernel per
+// direction replaces a dispatch kernel plus an NCCL all-to-all.
+//
+// Every wait is bounded: after kPeerSpinLimit polls the waiting CTA records a
+// timeout in the status word for the host and returns.  Kernels of different
+// ranks run on different GPUs; no two kernels that wait on each other share a
+// GPU.  No TMA or multicast loads are used: remote memory is written with
+// plain 16-byte stores and read only through the local region.
+//
+// Ordering across calls needs no double buffering: a source writes an
+// owner's rows for call c + 1 only after it received the owner's values for
+// call c, which the owner sends after its expert products of call c have read
+// those rows; likewise for the values.
+
+#include "common.cuh"
+#include "ep.cuh"
+
+namespace exlr8 {
+
+namespace {
+
+constexpr int kPeerThreads = 256;
+constexpr uint32_t kPeerSpinLimit = 1u << 20;  // about 1 s of polling
+
+__device__ __forceinline__ uint32_t load_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void store_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Waits until *flag reaches `target` (epochs only grow); false on timeout.
+__device__ bool wait_epoch(const uint32_t* flag, uint32_t target) {
+  for (uint32_t i = 0; i < kPeerSpinLimit; ++i) {
+    if (static_cast<int32_t>(load_acquire_sys(flag) - target) >= 0) return true;
+    __nanosleep(i < 64 ? 32 : 1000);
+  }
+  return false;
+}
+
+__device__ __forceinline__ uint32_t* flags_at(unsigned char* region, int which) {
+  return reinterpret_cast<uint32_t*>(region + 256 * which);  // which: 1 arrived, 2 returned
+}
+
+// CTA d sends this rank's rows routed to owner d (slot order) and their local
+// expert ids into d's region, then this rank's arrival flag there; then waits
+// until rank d's rows for this call have arrived in this rank's region.
+__global__ void __launch_bounds__(kPeerThreads) ep_send_kernel(
+    const uint32_t* __restrict__ ids, int tokens, const uint4* __restrict__ x, int row_vecs, int ranks, int rank,
+    int experts_per_rank, int capacity, PeerLayout layout, const uint64_t* __restrict__ peers,
+    unsigned char* __restrict__ local, int32_t* __restrict__ slot_pos, int32_t* __restrict__ status) {
+  extern __shared__ int s_list[];  // [capacity] token of each row, [capacity] local expert id
+  __shared__ int s_warp[kPeerThreads / 32];
+  __shared__ int s_base;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int d = blockIdx.x;
+  const uint32_t target = *reinterpret_cast<volatile uint32_t*>(local) + 1u;
+  unsigned char* owner = reinterpret_cast<unsigned char*>(peers[d]);
+  const int slots = tokens * 8;
+  const int routed = ranks * experts_per_rank;
+  if (tid == 0) s_base = 0;
+  __syncthreads();
+  for (int chunk = 0; chunk < slots; chunk += kPeerThreads) {
+    const int i = chunk + tid;
+    int dest = -1, loc = -1;
+    if (i < slots) {
+      const uint32_t e = ids[static_cast<int64_t>(i / 8) * 9 + i % 8];
+      if (e < static_cast<uint32_t>(routed)) {
+        dest = static_cast<int>(e) / experts_per_rank;
+        loc = static_cast<int>(e) % experts_per_rank;
+      }
+    }
+    const unsigned m = __ballot_sync(0xffffffffu, dest == d);
+    if (lane == 0) s_warp[warp] = __popc(m);
+    __syncthreads();
+    if (dest == d) {
+      int pos = s_base + __popc(m & ((1u << lane) - 1u));
+      for (int w = 0; w < warp; ++w) pos += s_warp[w];
+      if (pos < capacity) {
+        s_list[pos] = i / 8;
+        s_list[capacity + pos] = loc;
+        slot_pos[i] = d * capacity + pos;
+      } else {
+        slot_pos[i] = -1;
+        atomicAdd(&status[0], 1);  // capacity overflow: the slot is lost
+      }
+    } else if (d == 0 && dest < 0 && i < slots) {
+      slot_pos[i] = -1;  // id out of range: contributes zero
+    }
+    __syncthreads();
+    if (tid == 0) {
+      int add = 0;
+      for (int w = 0; w < kPeerThreads / 32; ++w) add += s_warp[w];
+      s_base += add;
+    }
+    __syncthreads();
+  }
+  const int count = min(s_base, capacity);
+  int32_t* meta = reinterpret_cast<int32_t*>(owner + layout.meta) + static_cast<int64_t>(rank) * capacity;
+  for (int j = tid; j < capacity; j += kPeerThreads) meta[j] = j < count ? s_list[capacity + j] : -1;
+  uint4* rows = reinterpret_cast<uint4*>(owner + layout.rows) + static_cast<int64_t>(rank) * capacity * row_vecs;
+  for (int64_t idx = tid; idx < static_cast<int64_t>(count) * row_vecs; idx += kPeerThreads) {
+    const int j = static_cast<int>(idx / row_vecs), v = static_cast<int>(idx % row_vecs);
+    rows[static_cast<int64_t>(j) * row_vecs + v] = x[static_cast<int64_t>(s_list[j]) * row_vecs + v];
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (tid == 0) {
+    store_release_sys(flags_at(owner, 1) + rank, target);
+    if (!wait_epoch(flags_at(local, 1) + d, target)) atomicOr(&status[1], 1);
+  }
+  __syncthreads();
+}
+
+// CTA s returns the values of source s's rows (valid rows only) into source
+// s's `back` area, then the `returned` flag; then waits for owner s's values.
+__global__ void __launch_bounds__(kPeerThreads) ep_return_kernel(const uint4* __restrict__ values, int row_vecs,
+                                                                 int rank, int capacity, PeerLayout layout,
+                                                                 const uint64_t* __restrict__ peers,
+                                                                 unsigned char* __restrict__ local,
+                                                                 int32_t* __restrict__ status) {
+  const int tid = threadIdx.x;
+  const int src = blockIdx.x;
+  const uint32_t target = *reinterpret_cast<volatile uint32_t*>(local) + 1u;
+  unsigned char* dst_region = reinterpret_cast<unsigned char*>(peers[src]);
+  const int32_t* meta = reinterpret_cast<const int32_t*>(local + layout.meta) + static_cast<int64_t>(src) * capacity;
+  uint4* back = reinterpret_cast<uint4*>(dst_region + layout.back) + static_cast<int64_t>(rank) * capacity * row_vecs;
+  const uint4* v = values + static_cast<int64_t>(src) * capacity * row_vecs;
+  for (int64_t idx = tid; idx < static_cast<int64_t>(capacity) * row_vecs; idx += kPeerThreads) {
+    const int j = static_cast<int>(idx / row_vecs);
+    if (meta[j] >= 0) back[idx] = v[idx];
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (tid == 0) {
+    store_release_sys(flags_at(dst_region, 2) + rank, target);
+    if (!wait_epoch(flags_at(local, 2) + src, target)) atomicOr(&status[1], 2);
+  }
+}
+
+// Runs after the return kernel: this rank's exchanges of the call are done.
+__global__ void ep_epoch_kernel(unsigned char* __restrict__ local) {
+  *reinterpret_cast<uint32_t*>(local) += 1u;
+}
+
+}  // namespace
+
+cudaError_t launch_ep_send(const uint32_t* ids, int tokens, const void* x, int x_dtype, int hidden, int ranks,
+                           int rank, int experts_per_rank, int capacity, int max_capacity, const uint64_t* peers,
+                           void* local, int32_t* slot_pos, int32_t* status, cudaStream_t s) {
+  cudaError_t err = cudaMemsetAsync(status, 0, 2 * sizeof(int32_t), s);
+  if (err != cudaSuccess) return err;
+  const int elem = x_dtype == kF32 ? 4 : 2;
+  const PeerLayout layout = peer_layout(ranks, max_capacity, hidden, elem);
+  const size_t smem = 2 * static_cast<size_t>(capacity) * sizeof(int);
+  ep_send_kernel<<<ranks, kPeerThreads, smem, s>>>(ids, tokens, static_cast<const uint4*>(x), hidden * elem / 16,
+                                                   ranks, rank, experts_per_rank, capacity, layout, peers,
+                                                   static_cast<unsigned char*>(local), slot_pos, status);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_ep_return(const void* values, int x_dtype, int hidden, int ranks, int rank, int capacity,
+                             int max_capacity, const uint64_t* peers, void* local, int32_t* status, cudaStream_t s) {
+  const int elem = x_dtype == kF32 ? 4 : 2;
+  const PeerLayout layout = peer_layout(ranks, max_capacity, hidden, elem);
+  ep_return_kernel<<<ranks, kPeerThreads, 0, s>>>(static_cast<const uint4*>(values), hidden * elem / 16, rank,
+                                                  capacity, layout, peers, static_cast<unsigned char*>(local),
+                                                  status);
+  cudaError_t err = cudaGetLastError();
+  if (err != cudaSuccess) return err;
+  ep_epoch_kernel<<<1, 1, 0, s>>>(static_cast<unsigned char*>(local));
+  return cudaGetLastError();
+}
+
+}  // namespace exlr8

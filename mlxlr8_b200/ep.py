@@ -8,10 +8,14 @@ slice of the tokens, and one layer is
     router (local tokens)                      exlr8_router
     dispatch: routed rows -> owner rank        exlr8_ep_dispatch
     all-to-all of rows and local expert ids    NCCL (torch.distributed)
-    grouped expert MLP on the received rows    exlr8_expert_mlp (slots = 1)
+    grouped expert MLP on the received rows,   exlr8_expert_mlp_shared (the bf16
+      and the shared expert on the local        shared expert's rows stream inside
+      tokens                                    the trellis kernels)
     all-to-all of the typed slot values back   NCCL
-    shared expert on the local tokens          exlr8_shared_expert / trellis
     weighted combine + shared + residual       exlr8_ep_combine
+
+With a trellis shared expert the received rows go through exlr8_expert_mlp
+and the shared expert runs on a side stream.
 
 Each slot value comes from the same expert operator (exlr8_expert_mlp on the
 owner's rows) and the combine follows the single-device finish order, so the
@@ -24,11 +28,13 @@ pass the same number of tokens.
 
 from __future__ import annotations
 
+import ctypes
+
 import torch
 
 from . import _lib
 from .experts import ExpertLayer
-from .fast_decode import dense_expert, fast_expert_mlp
+from .fast_decode import dense_expert, fast_expert_mlp, trellis_experts
 
 
 def shard_experts(layer: ExpertLayer, rank: int, world: int, routed: int = 256) -> ExpertLayer:
@@ -84,13 +90,83 @@ class Exchange:
         return tuple(outs)
 
 
+class PeerExchange:
+    """The peer-memory exchange of one expert-parallel layer
+    (exlr8_ep_send / exlr8_ep_return): this rank's region, mapped by every
+    other rank through CUDA IPC, and theirs mapped here.  Construction is a
+    collective over `group` (the IPC handles are all-gathered); every rank
+    must then make the same calls with the same token count, at most
+    `max_tokens` per call."""
+
+    def __init__(self, world: int, rank: int, hidden: int, max_tokens: int, dtype: torch.dtype,
+                 device: torch.device, group=None):
+        import torch.distributed as dist
+
+        lib = _lib.lib()
+        self.world, self.rank, self.hidden = world, rank, hidden
+        self.code = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2}[dtype]
+        self.max_capacity = max_tokens * 8
+        nbytes = lib.exlr8_ep_peer_bytes(world, self.max_capacity, hidden, self.code)
+        if nbytes == 0:
+            raise ValueError("unsupported peer-exchange shape")
+        region = ctypes.c_void_p()
+        handle = (ctypes.c_ubyte * 64)()
+        _lib.check(lib.exlr8_ep_peer_create(nbytes, ctypes.byref(region), handle))
+        self.region = region.value
+        self._opened = []
+        mine = torch.tensor(list(bytes(handle)), dtype=torch.uint8, device=device)
+        handles = [torch.empty_like(mine) for _ in range(world)]
+        dist.all_gather(handles, mine, group=group)
+        addrs = []
+        for r in range(world):
+            if r == rank:
+                addrs.append(self.region)
+                continue
+            theirs = (ctypes.c_ubyte * 64).from_buffer_copy(bytes(handles[r].cpu().tolist()))
+            ptr = ctypes.c_void_p()
+            _lib.check(lib.exlr8_ep_peer_open(theirs, ctypes.byref(ptr)))
+            self._opened.append(ptr.value)
+            addrs.append(ptr.value)
+        self.peers = torch.tensor(addrs, dtype=torch.int64, device=device)
+        meta, rows, back = ctypes.c_size_t(), ctypes.c_size_t(), ctypes.c_size_t()
+        _lib.check(lib.exlr8_ep_peer_offsets(world, self.max_capacity, hidden, self.code, ctypes.byref(meta),
+                                             ctypes.byref(rows), ctypes.byref(back)))
+        self.meta, self.rows, self.back = self.region + meta.value, self.region + rows.value, self.region + back.value
+        self.status = torch.zeros(2, dtype=torch.int32, device=device)
+        self._group = group
+
+    def check(self):
+        """Raise if the last exchange lost slots or a wait for a peer timed out."""
+        lost, timeouts = (int(v) for v in self.status.cpu())
+        if timeouts:
+            raise RuntimeError(f"expert-parallel exchange: a wait for a peer timed out (flags {timeouts})")
+        if lost:
+            raise RuntimeError(f"expert-parallel exchange: {lost} routed slots exceeded the capacity")
+
+    def close(self):
+        """Unmap the peers' regions and free this rank's (a collective)."""
+        import torch.distributed as dist
+
+        if self.region is None:
+            return
+        torch.cuda.synchronize()
+        dist.barrier(group=self._group)
+        lib = _lib.lib()
+        for ptr in self._opened:
+            _lib.check(lib.exlr8_ep_peer_close(ptr))
+        dist.barrier(group=self._group)
+        _lib.check(lib.exlr8_ep_peer_destroy(self.region))
+        self._opened, self.region = [], None
+
+
 class ExpertParallelMoE:
     """One MoE layer with this rank's routed shard (`local`, from
     shard_experts) and a replicated shared expert: the dense bf16 triple
     `shared`, or the one-expert trellis layer `shared_layer`."""
 
     def __init__(self, gate_weight, bias, local: ExpertLayer, rank: int, world: int, group=None, shared=None,
-                 shared_layer: ExpertLayer | None = None, routed: int = 256):
+                 shared_layer: ExpertLayer | None = None, routed: int = 256, exchange: str = "nccl",
+                 max_tokens: int = 16):
         if (shared is None) == (shared_layer is None):
             raise ValueError("give exactly one shared expert (dense bf16 or trellis)")
         if routed % world or local.experts != routed // world:
@@ -102,10 +178,45 @@ class ExpertParallelMoE:
         self.shared = None if shared is None else tuple(t.contiguous() for t in shared)
         self.shared_layer = shared_layer
         self.exchange = Exchange(world, group, rank)
+        if exchange not in ("nccl", "peer"):
+            raise ValueError("exchange must be 'nccl' or 'peer'")
+        if exchange == "peer" and shared_layer is not None:
+            raise ValueError("the peer-memory exchange runs with the bf16 shared expert")
+        self.exchange_kind = exchange
+        self.max_tokens = max_tokens
+        self.group = group
+        self.peer = None  # PeerExchange, created on the first call (a collective)
         self._side = None
         self._shared_struct = None
+        self._owner_ws = None
         if self.shared is not None:
             self._shared_struct, self._keep = dense_expert(self.shared)
+            self._local_struct, self._local_count = trellis_experts(local.packed, local.scales, local.k, local.hidden,
+                                                                    local.intermediate)
+
+    def owner_mlp(self, recv_x, recv_meta, xr):
+        """(values [rows][hidden], shared [tokens][hidden]): the trellis MLP of
+        the received rows and the bf16 shared expert of the local tokens in one
+        call (exlr8_expert_mlp_shared)."""
+        return self._owner_mlp(recv_x.data_ptr(), recv_meta.reshape(-1).contiguous(), recv_x.shape[0], xr)
+
+    def _owner_mlp(self, recv_x_ptr, recv_meta, rows, xr):
+        local = self.local
+        h, m = local.hidden, local.intermediate
+        tokens = xr.shape[0]
+        device = xr.device
+        values = torch.empty(rows, h, dtype=xr.dtype, device=device)
+        shared = torch.empty(tokens, h, dtype=xr.dtype, device=device)
+        lib = _lib.lib()
+        need = lib.exlr8_expert_mlp_shared_workspace(rows, h, m, self._local_count, tokens)
+        if self._owner_ws is None or self._owner_ws.numel() < need or self._owner_ws.device != device:
+            self._owner_ws = _lib.workspace(need, device)
+        ids_ptr = recv_meta if isinstance(recv_meta, int) else recv_meta.data_ptr()
+        _lib.check(lib.exlr8_expert_mlp_shared(recv_x_ptr, _lib.act_code(xr), ids_ptr, rows,
+                                               self._local_struct, xr.data_ptr(), tokens, self._shared_struct,
+                                               values.data_ptr(), shared.data_ptr(), self._owner_ws.data_ptr(),
+                                               self._owner_ws.numel(), _lib.stream_handle(device)))
+        return values, shared
 
     def shared_values(self, x):
         """Typed shared-expert output [tokens][hidden] of the local tokens."""
@@ -131,6 +242,34 @@ class ExpertParallelMoE:
         _, ids, scores = router(xr, self.gate_weight, self.bias)
         return ids, scores
 
+    def _peer_call(self, xr, res, ids, scores, residual, return_routing):
+        """The layer with the peer-memory exchange (PeerExchange)."""
+        device = xr.device
+        tokens, h = xr.shape
+        if tokens > self.max_tokens:
+            raise ValueError("more tokens than the peer exchange was sized for")
+        if self.peer is None:
+            self.peer = PeerExchange(self.world, self.rank, h, self.max_tokens, xr.dtype, device, self.group)
+        peer = self.peer
+        lib = _lib.lib()
+        stream = _lib.stream_handle(device)
+        act = _lib.act_code(xr)
+        slot_pos = torch.empty(max(tokens * 8, 1), dtype=torch.int32, device=device)
+        _lib.check(lib.exlr8_ep_send(ids.data_ptr(), tokens, xr.data_ptr(), act, h, self.world, self.rank,
+                                     self.per_rank, peer.max_capacity, peer.peers.data_ptr(), peer.region,
+                                     slot_pos.data_ptr(), peer.status.data_ptr(), stream))
+        rows = self.world * tokens * 8
+        values, shared = self._owner_mlp(peer.rows, peer.meta, rows, xr)
+        _lib.check(lib.exlr8_ep_return(values.data_ptr(), act, h, self.world, self.rank, tokens, peer.max_capacity,
+                                       peer.peers.data_ptr(), peer.region, peer.status.data_ptr(), stream))
+        out = torch.empty_like(res)
+        _lib.check(lib.exlr8_ep_combine(peer.back, act, slot_pos.data_ptr(), scores.data_ptr(), shared.data_ptr(),
+                                        res.data_ptr(), tokens, h, out.data_ptr(), stream))
+        out = out.reshape(residual.shape)
+        if return_routing:
+            return out, ids, scores
+        return out
+
     def __call__(self, x, residual, return_routing=False):
         device = _lib.require_cuda(x, residual)
         h = self.local.hidden
@@ -141,6 +280,8 @@ class ExpertParallelMoE:
         lib = _lib.lib()
         stream = _lib.stream_handle(device)
         cap = tokens * 8
+        if self.exchange_kind == "peer" and self.world > 1:
+            return self._peer_call(xr, res, ids, scores, residual, return_routing)
         send_x = torch.empty(self.world, cap, h, dtype=x.dtype, device=device)
         send_meta = torch.empty(self.world, cap, dtype=torch.int32, device=device)
         slot_pos = torch.empty(max(tokens * 8, 1), dtype=torch.int32, device=device)
@@ -149,22 +290,27 @@ class ExpertParallelMoE:
         _lib.check(lib.exlr8_ep_dispatch(ids.data_ptr(), tokens, xr.data_ptr(), _lib.act_code(xr), h, self.world,
                                          self.per_rank, cap, send_x.data_ptr(), send_meta.data_ptr(),
                                          slot_pos.data_ptr(), counts.data_ptr(), status.data_ptr(), stream))
-        # The replicated shared expert runs on a side stream, overlapping the
-        # exchange and the owner's expert products.
-        main = torch.cuda.current_stream(device)
-        if self._side is None or self._side.device != device:
-            self._side = torch.cuda.Stream(device)
-        self._side.wait_stream(main)
-        with torch.cuda.stream(self._side):
-            shared = self.shared_values(xr)
-        recv_x, recv_meta = self.exchange(send_x, send_meta)
         rows = self.world * cap
         local = self.local
-        values = fast_expert_mlp(recv_x.reshape(rows, h), recv_meta.reshape(rows, 1), local.packed, local.scales,
-                                 local.k, h, local.intermediate)
-        back = self.exchange(values.reshape(self.world, cap, h))
-        main.wait_stream(self._side)
-        shared.record_stream(main)
+        if self.shared is not None:
+            recv_x, recv_meta = self.exchange(send_x, send_meta)
+            values, shared = self.owner_mlp(recv_x.reshape(rows, h), recv_meta, xr)
+            back = self.exchange(values.reshape(self.world, cap, h))
+        else:
+            # The trellis shared expert runs on a side stream, overlapping the
+            # exchange and the owner's expert products.
+            main = torch.cuda.current_stream(device)
+            if self._side is None or self._side.device != device:
+                self._side = torch.cuda.Stream(device)
+            self._side.wait_stream(main)
+            with torch.cuda.stream(self._side):
+                shared = self.shared_values(xr)
+            recv_x, recv_meta = self.exchange(send_x, send_meta)
+            values = fast_expert_mlp(recv_x.reshape(rows, h), recv_meta.reshape(rows, 1), local.packed, local.scales,
+                                     local.k, h, local.intermediate)
+            back = self.exchange(values.reshape(self.world, cap, h))
+            main.wait_stream(self._side)
+            shared.record_stream(main)
         out = torch.empty_like(res)
         _lib.check(lib.exlr8_ep_combine(back.data_ptr(), _lib.act_code(xr), slot_pos.data_ptr(), scores.data_ptr(),
                                         shared.data_ptr(), res.data_ptr(), tokens, h, out.data_ptr(), stream))

@@ -83,3 +83,28 @@ def test_shard_experts_slices_contiguous_blocks():
     assert shared_trellis(layer, index=9) is None
     with pytest.raises(ValueError):
         shard_experts(layer, 0, 3, routed=8)
+
+
+def test_peer_region_layout_and_checks():
+    """Peer-exchange region (exlr8_ep_peer_*): flags, then meta, rows and back
+    areas on 256-byte boundaries sized for ranks x max capacity rows; shapes
+    outside the supported range are refused (host-only calls)."""
+    import ctypes
+
+    from mlxlr8_b200 import _lib
+
+    lib = _lib.lib()
+    meta, rows, back = ctypes.c_size_t(), ctypes.c_size_t(), ctypes.c_size_t()
+    ranks, cap, hidden = 8, 128, 6144
+    assert lib.exlr8_ep_peer_offsets(ranks, cap, hidden, 2, ctypes.byref(meta), ctypes.byref(rows),
+                                     ctypes.byref(back)) == 0
+    total = lib.exlr8_ep_peer_bytes(ranks, cap, hidden, 2)
+    assert meta.value == 768
+    assert rows.value >= meta.value + ranks * cap * 4 and rows.value % 256 == 0
+    assert back.value == rows.value + ranks * cap * hidden * 2
+    assert total == back.value + ranks * cap * hidden * 2
+    assert lib.exlr8_ep_peer_bytes(65, cap, hidden, 2) == 0          # at most 64 ranks
+    assert lib.exlr8_ep_peer_bytes(ranks, 8192, hidden, 2) == 0      # at most 4096 rows per pair
+    assert lib.exlr8_ep_peer_bytes(ranks, cap, 100, 2) == 0          # rows of whole 16-byte vectors
+    status = lib.exlr8_ep_send(None, 3, None, 2, hidden, ranks, 0, 32, 16, None, None, None, None, None)
+    assert status != 0                                              # 3 tokens x 8 > 16 rows

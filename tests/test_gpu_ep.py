@@ -152,3 +152,81 @@ def test_emulated_expert_parallel_layer_matches_oracle(world, shared, tokens_per
     scale = float(np.max(np.abs(want)))
     assert float(np.max(np.abs(got - want))) <= 1e-2 * scale
     assert rel_l2(got, want) < 5e-3
+
+
+@pytest.mark.parametrize("rows, tokens", [(16, 2), (40, 5), (24, 0)])
+def test_owner_mlp_with_shared_matches_separate_calls(rows, tokens):
+    """exlr8_expert_mlp_shared (the owner's trellis MLP over received rows with
+    the local tokens' bf16 shared expert streamed in the same kernels) against
+    exlr8_expert_mlp (slots = 1) and exlr8_shared_expert called separately.
+    Empty rows (id -1) give zeros."""
+    import torch
+
+    from mlxlr8_b200.ep import ExpertParallelMoE, shard_experts
+    from mlxlr8_b200.fast_decode import fast_expert_mlp
+    from mlxlr8_b200.synthetic import make_layer
+
+    layer = make_layer(seed=41, hidden=256, intermediate=128, shared="bf16")
+    e = layer.experts
+    world = 4
+    moe = ExpertParallelMoE(layer.gate_weight, layer.bias, shard_experts(e, 1, world), 1, world, shared=e.shared)
+    g = torch.Generator(device="cuda")
+    g.manual_seed(rows)
+    recv_x = torch.randn(rows, 256, generator=g, device="cuda").to(torch.bfloat16)
+    meta = torch.randint(-1, 64, (rows,), generator=g, device="cuda", dtype=torch.int32)
+    xr = torch.randn(max(tokens, 1), 256, generator=g, device="cuda").to(torch.bfloat16)[:tokens]
+    values, shared = moe.owner_mlp(recv_x, meta, xr)
+    local = moe.local
+    want_values = fast_expert_mlp(recv_x, meta.reshape(rows, 1), local.packed, local.scales, local.k, 256, 128)
+    want_values = want_values.reshape(rows, 256)
+    torch.cuda.synchronize()
+    got, want = host(values), host(want_values)
+    assert np.all(got[host(meta) < 0] == 0)
+    scale = float(np.max(np.abs(want)))
+    assert float(np.max(np.abs(got - want))) <= 1e-2 * scale
+    if tokens:
+        want_shared = host(moe.shared_values(xr))
+        got_shared = host(shared)
+        s2 = float(np.max(np.abs(want_shared)))
+        # Same bf16 products; only the K-split summation order differs.
+        assert float(np.max(np.abs(got_shared - want_shared))) <= 1e-2 * s2
+        assert rel_l2(got_shared, want_shared) < 5e-3
+
+
+def test_peer_exchange_wait_times_out_and_reports():
+    """The peer exchange's waits are bounded: with a peer that never sends
+    (rank 1's region is this rank's own, and nothing sets rank 1's flags) the
+    send and return kernels give up after about a second each and set their
+    status bits; the stream stays usable."""
+    import ctypes
+
+    import torch
+
+    from mlxlr8_b200 import _lib
+
+    lib = _lib.lib()
+    ranks, max_cap, hidden = 2, 8, 256
+    nbytes = lib.exlr8_ep_peer_bytes(ranks, max_cap, hidden, 2)
+    region, handle = ctypes.c_void_p(), (ctypes.c_ubyte * 64)()
+    _lib.check(lib.exlr8_ep_peer_create(nbytes, ctypes.byref(region), handle))
+    try:
+        peers = torch.tensor([region.value, region.value], dtype=torch.int64, device="cuda")
+        ids = torch.tensor([[0, 1, 2, 3, 200, 201, 202, 203, 256]], dtype=torch.int32, device="cuda")
+        x = torch.randn(1, hidden, device="cuda").to(torch.bfloat16)
+        slot_pos = torch.empty(8, dtype=torch.int32, device="cuda")
+        status = torch.zeros(2, dtype=torch.int32, device="cuda")
+        stream = _lib.stream_handle(x.device)
+        _lib.check(lib.exlr8_ep_send(ids.data_ptr(), 1, x.data_ptr(), 2, hidden, ranks, 0, 128, max_cap,
+                                     peers.data_ptr(), region.value, slot_pos.data_ptr(), status.data_ptr(), stream))
+        torch.cuda.synchronize()
+        assert status[1].item() & 1
+        values = torch.zeros(ranks * 8, hidden, dtype=torch.bfloat16, device="cuda")
+        _lib.check(lib.exlr8_ep_return(values.data_ptr(), 2, hidden, ranks, 0, 1, max_cap, peers.data_ptr(),
+                                       region.value, status.data_ptr(), stream))
+        torch.cuda.synchronize()
+        assert status[1].item() & 2
+        assert torch.equal(slot_pos.cpu()[:4], torch.tensor([0, 1, 2, 3], dtype=torch.int32))
+        assert torch.equal(slot_pos.cpu()[4:], torch.tensor([8, 9, 10, 11], dtype=torch.int32))
+        torch.zeros(4, device="cuda").sum().item()  # the context still works
+    finally:
+        _lib.check(lib.exlr8_ep_peer_destroy(region.value))

@@ -21,8 +21,9 @@ def _gpus():
 
 
 @pytest.mark.skipif(_gpus() < 2, reason="needs two GPUs")
-@pytest.mark.parametrize("shared, tokens_per_rank", [("bf16", 3), ("trellis", 20)])
-def test_two_gpu_expert_parallel_layer(tmp_path, shared, tokens_per_rank):
+@pytest.mark.parametrize("shared, tokens_per_rank, exchange", [("bf16", 3, "nccl"), ("trellis", 20, "nccl"),
+                                                               ("bf16", 2, "peer")])
+def test_two_gpu_expert_parallel_layer(tmp_path, shared, tokens_per_rank, exchange):
     import torch
 
     from helpers import host, rel_l2
@@ -34,7 +35,7 @@ def test_two_gpu_expert_parallel_layer(tmp_path, shared, tokens_per_rank):
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
     cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
            "--master-addr=127.0.0.1", "--master-port=29517", os.path.join(ROOT, "tests", "ep_worker.py"), out_path,
-           shared, str(tokens_per_rank)]
+           shared, str(tokens_per_rank), exchange]
     subprocess.run(cmd, check=True, env=env, timeout=600)
     got = torch.load(out_path)
     layer = make_layer(seed=31, hidden=256, intermediate=128, shared=shared)
@@ -47,6 +48,11 @@ def test_two_gpu_expert_parallel_layer(tmp_path, shared, tokens_per_rank):
                                     256, 128, shared=hc["shared"], dtype="bfloat16", logits=host(logits))
     np.testing.assert_array_equal(ids_np, e_ids)
     want = e_out - res
+    if exchange == "peer":
+        # Same kernels on the same rows: the peer exchange is bit-exact against
+        # the NCCL one, and repeated calls give the same result.
+        assert torch.equal(got["ep"], got["nccl"])
+        assert torch.equal(got["ep"], got["first"])
     for key in ("ep", "single"):
         diff = host(got[key]) - res
         assert float(np.max(np.abs(diff - want))) <= 1e-2 * float(np.max(np.abs(want)))
