@@ -18,7 +18,8 @@ e2e:   the public API (MoELayer.__call__) with pinned host buffers: per step
 roofline: the dominant kernel (trellis gate/up streaming GEMV), its launch
        durations measured with CUDA events on the launching stream during a
        profiled pass of the same K steps; algorithmic bytes = packed trellis
-       codes it must stream (U experts x 2 matrices x K*h*m/8).
+       codes it must stream (U experts x 2 matrices x K*h*m/8) plus, on one
+       GPU, the bf16 shared expert's gate/up rows the same launch streams.
 cpu_baseline: the C restatement of the layer (oracle/c, OpenMP) on the host's
        cores, a bounded number of full layer steps.
 --impl reference: the reference's expert operators are Metal kernels
@@ -28,8 +29,15 @@ cpu_baseline: the C restatement of the layer (oracle/c, OpenMP) on the host's
 Under torchrun (N > 1) the same layers are expert-parallel: each GPU holds
 256 / N routed experts of every layer and the replicated shared expert, takes
 T tokens of its own (global batch T * N, weak scaling), and the dispatch and
-combine are NCCL exchanges inside each layer's CUDA graph; time is the max
-over ranks.  (`--tokens 8 --gpus 8` is configs[3]'s batch of 64 per layer.)
+combine go over peer memory (NVLink stores + epoch flags; `--ep-exchange nccl`
+for the NCCL all-to-all) inside each layer's CUDA graph; time is the max over
+ranks.  (`--tokens 8 --gpus 8` is configs[3]'s batch of 64 per layer.)
+
+Single-GPU extras: decode at T = 8 and 32, the prefill configurations
+(configs[2] joined MXFP4 at 4096 tokens, configs[4] 128 tokens at K4 and K3),
+and the MoE block stack (the layers plus the K3 layer-78 block, each behind its
+post-attention RMS norm, attention stubbed) at T = 1 and at T = 128 with
+Zipf(1.1)-skewed routing.
 """
 
 from __future__ import annotations
@@ -366,6 +374,47 @@ def prefill_configs(layer_k4, steps, stream, peak_tflops):
     return res
 
 
+def stack_configs(layers, steps, stream):
+    """The MoE block stack with the attention stubbed: the bench's
+    layers (K4) plus the K3 layer-78 block, each behind its post-attention RMS
+    norm, as one CUDA graph per stack call.  T = 1 (decode) and T = 128 with
+    Zipf(1.1)-skewed routing (configs[4], the speculative-verify step)."""
+    import torch
+
+    from mlxlr8_b200.moe import MoELayer
+    from mlxlr8_b200.stack import MoEStack
+    from mlxlr8_b200.synthetic import make_layer, zipf_bias
+
+    k3 = make_layer(seed=78, k=3)
+    blocks = list(layers) + [k3]
+    g = torch.Generator(device="cuda")
+    g.manual_seed(11)
+    norms = [(1.0 + 0.1 * torch.randn(HIDDEN, generator=g, device="cuda")).to(torch.bfloat16) for _ in blocks]
+    res = {}
+    for tokens, skew in ((1, False), (128, True)):
+        moes = [MoELayer(l.gate_weight, zipf_bias(300 + i) if skew else l.bias, l.experts)
+                for i, l in enumerate(blocks)]
+        stack = MoEStack(list(zip(norms, moes)))
+        h = (torch.randn(tokens, HIDDEN, generator=g, device="cuda")).to(torch.bfloat16)
+        with torch.cuda.stream(stream):
+            for _ in range(2):
+                stack(h)  # eager warm-up: workspaces, kernel attributes
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            stack(h)
+        ms = time_calls(graph.replay, steps, 3, stream)
+        del graph
+        res[f"stack_{len(blocks)}blocks_T{tokens}"] = {
+            "tokens_per_s": tokens / (ms / 1000.0), "ms_per_stack": ms, "ms_per_block": ms / len(blocks),
+            "blocks": f"{len(layers)} K4 blocks + the K3 layer-78 block, post-attention RMS norm each",
+            "routing": "Zipf(1.1)-skewed router bias" if skew else "uniform"}
+        del stack, moes
+    del k3
+    torch.cuda.empty_cache()
+    return res
+
+
 def main():
     args = parse()
     if args.ncu_driver:
@@ -557,6 +606,7 @@ def main():
         if peaks_path.exists():
             bf16_peak = float(json.loads(peaks_path.read_text()).get("bf16_tflops", bf16_peak))
         extras["prefill"] = prefill_configs(layers[0], 10, stream, bf16_peak)
+        extras["stack"] = stack_configs(layers, 20, stream)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

@@ -401,6 +401,15 @@ size_t exlr8_router_logits_workspace(int64_t tokens, int hidden, int x_dtype);
 int exlr8_router_logits(const void* x, int x_dtype, int64_t tokens, int hidden, const float* gate_weight,
                         float* logits, void* workspace, size_t workspace_bytes, void* stream);
 
+/* Residual add + RMS norm in front of each MoE block (model.py:373-384,
+ * the fused form of exlr8/fast_norm.py residual_rms_pair): per row,
+ *   h   = T(x + residual)                      (h = x when residual is null)
+ *   out = T(w * T(h * rsqrt(sum(h * h) / hidden + eps)))
+ * with the sum of squares in float32; h_out (nullable) receives h.  x,
+ * residual, h_out and out [rows][hidden] in x_dtype; w [hidden] in x_dtype. */
+int exlr8_residual_rms_norm(const void* x, const void* residual, const void* weight, int x_dtype, int64_t rows,
+                            int hidden, float eps, void* h_out, void* out, void* stream);
+
 /* Dispatch header of the last joined call that used `workspace` (sizes as
  * given to that call): [0] chunks, [1] padded rows, [2..3] GEMM unit counters,
  * [4] GEMM error code (0 = none; non-zero = a bounded wait timed out).

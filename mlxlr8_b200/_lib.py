@@ -109,6 +109,8 @@ _SIGNATURES = {
                                   c_void_p, c_void_p, c_void_p, c_void_p]),
     "exlr8_ep_combine": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int, c_void_p,
                                  c_void_p]),
+    "exlr8_residual_rms_norm": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int64, c_int, c_float, c_void_p,
+                                        c_void_p, c_void_p]),
     "exlr8_ep_peer_bytes": (c_size_t, [c_int, c_int, c_int, c_int]),
     "exlr8_ep_peer_offsets": (c_int, [c_int, c_int, c_int, c_int, POINTER(c_size_t), POINTER(c_size_t),
                                       POINTER(c_size_t)]),

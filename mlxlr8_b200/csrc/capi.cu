@@ -12,6 +12,7 @@
 #include "ep.cuh"
 #include "joined.cuh"
 #include "mx_gemm.cuh"
+#include "norm.cuh"
 #include "router.cuh"
 #include "router_gemm.cuh"
 #include "stream.cuh"
@@ -789,6 +790,19 @@ int exlr8_ep_combine(const void* values, int x_dtype, const int32_t* slot_pos, c
   if (!values || !slot_pos || !scores || !shared || !residual || !out) return EXLR8_ERR_ARG;
   return cuda_status(launch_ep_combine(values, x_dtype, slot_pos, scores, shared, residual, static_cast<int>(tokens),
                                        hidden, out, as_stream(stream)));
+}
+
+// ---- residual add + RMS norm in front of each MoE block ----------------------
+
+int exlr8_residual_rms_norm(const void* x, const void* residual, const void* weight, int x_dtype, int64_t rows,
+                            int hidden, float eps, void* h_out, void* out, void* stream) {
+  if (!valid_act(x_dtype)) return EXLR8_ERR_DTYPE;
+  if (rows < 0 || hidden <= 0) return EXLR8_ERR_ARG;
+  if (rows == 0) return EXLR8_OK;
+  if (!x || !weight || !out || !(eps >= 0.0f)) return EXLR8_ERR_ARG;
+  if (rows > 0x7fffffff) return EXLR8_ERR_UNSUPPORTED;
+  return cuda_status(launch_residual_rms(x, residual, weight, x_dtype, rows, hidden, eps, h_out, out,
+                                         as_stream(stream)));
 }
 
 // ---- peer-memory exchange of the expert-parallel layer ---------------------

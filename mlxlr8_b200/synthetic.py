@@ -216,3 +216,16 @@ def joined_host_copy(j: SyntheticJoined, experts=None):
         "gate_weight": j.gate_weight.cpu().numpy(),
         "bias": j.bias.cpu().numpy(),
     }
+
+
+def zipf_bias(seed: int, s: float = 1.1, experts: int = 256, strength: float = 0.2, device="cuda"):
+    """Router bias [experts] float32 that skews expert popularity towards a
+    Zipf(s) shape (the speculative-verify step): a seeded
+    random ranking of the experts and bias = -strength * s * log(rank + 1), so
+    the rank-k expert's chance of a top-8 slot falls off roughly as k^-s on
+    top of the gate's own spread."""
+    device = torch.device(device)
+    order = torch.randperm(experts, generator=_gen(seed, device), device=device)
+    rank = torch.empty(experts, dtype=torch.float32, device=device)
+    rank[order] = torch.arange(experts, dtype=torch.float32, device=device)
+    return (-strength * s * torch.log(rank + 1.0)).float()

@@ -536,3 +536,18 @@ def moe_layer(x, residual, gate_weight, bias, packed, scales, k, hidden, interme
         values[:, 8] = shared_bf16(x, *shared, dtype=dtype)
     out = combine(values, scores, residual, dtype)
     return out, ids, scores
+
+
+def residual_rms_norm(x, weight, eps=1e-5, residual=None, dtype="bfloat16"):
+    """Residual add + RMS norm in front of each MoE block (exlr8 model.py:373-384;
+    the fused kernel of fast_norm.py:23-34 / metal/residual_rms.metal):
+    h = T(x + residual); out = T(w * T(h * rsqrt(sum(h^2) / n + eps))), the sum
+    of squares in float32.  Returns (h, out) as float32 arrays of T values."""
+    rnd = rounder(dtype)
+    h = np.asarray(x, np.float32)
+    if residual is not None:
+        h = rnd((h + np.asarray(residual, np.float32)).astype(np.float32))
+    ss = np.sum(h * h, axis=-1, dtype=np.float32, keepdims=True)
+    inv = (np.float32(1.0) / np.sqrt(ss / np.float32(h.shape[-1]) + np.float32(eps))).astype(np.float32)
+    out = rnd((np.asarray(weight, np.float32) * rnd((h * inv).astype(np.float32))).astype(np.float32))
+    return h, out
