@@ -78,14 +78,14 @@ def parse():
     p.add_argument("--impl", choices=("b200", "reference"), default="b200")
     p.add_argument("--cpu-seconds", type=float, default=10.0)
     p.add_argument("--no-cpu-baseline", action="store_true")
-    p.add_argument("--ncu-driver", choices=("layer", "mlp", "joined", "trellis"), default=None,
+    p.add_argument("--ncu-driver", choices=("layer", "mlp", "joined", "trellis", "encode"), default=None,
                    help="untimed run for an ncu capture: 'layer' calls one resident layer --calls times; 'mlp' "
                         "runs the nine-expert fast_expert_mlp at full size (about 170 MB of weights); 'joined' "
                         "runs JoinedMXFP4.finish at full width over --experts experts (the last one shared) with "
                         "--tokens tokens, top-8 uniform routing (about 4 GB on the device at 129 experts and 2048 "
                         "tokens); 'trellis' runs the grouped trellis prefill (expert_mlp_finish with the dense bf16 "
                         "shared expert) over --experts K4 experts with --tokens tokens, plus the tensor-core router "
-                        "gate product")
+                        "gate product; 'encode' re-encodes --experts full-size K4 experts to joined MXFP4")
     p.add_argument("--experts", type=int, default=129)
     p.add_argument("--no-extras", action="store_true",
                    help="skip the single-GPU extras (decode at T=8/32, the prefill configurations)")
@@ -136,6 +136,12 @@ def ncu_driver(args):
         for _ in range(args.calls):
             router_logits(x, layer.gate_weight)
             expert_mlp_finish(x, ids, scores, r, e.packed, e.scales, K_BITS, HIDDEN, INTER, shared=e.shared)
+    elif args.ncu_driver == "encode":
+        from mlxlr8_b200.joined_mxfp4 import encode
+
+        layer = make_layer(seed=1, routed=args.experts, shared="none")
+        for _ in range(args.calls):
+            encode(layer.experts)
     elif args.ncu_driver == "layer":
         layer = make_layer(seed=1)
         moe = MoELayer(layer.gate_weight, layer.bias, layer.experts)
@@ -374,6 +380,26 @@ def prefill_configs(layer_k4, steps, stream, peak_tflops):
     return res
 
 
+def encode_config(layer, steps, stream):
+    """Load-time trellis -> MXFP4 re-encode of one K4 layer's 256 routed
+    experts (joined_mxfp4.py:12-47): three fused decode + fold +
+    quantise launches (gate and up into the joined [E, 2m, h/8] buffer, then
+    down).  Algorithmic bytes: the packed codes and gate/up in-scales read,
+    the MXFP4 codes and E8M0 scales written."""
+    from mlxlr8_b200.joined_mxfp4 import encode
+
+    e = layer.experts
+    matrices = e.packed["gate"].numel() // (HIDDEN * INTER * K_BITS // 8)
+    read = sum(t.numel() for t in e.packed.values()) + 2 * matrices * HIDDEN * e.scales["gate"][0].element_size()
+    written = matrices * (3 * HIDDEN * INTER // 2 + 3 * HIDDEN * INTER // 32)
+    ms = time_calls(lambda: encode(e), steps, 2, stream)
+    peak, peak_kind = measured_peaks()
+    achieved = (read + written) / (ms / 1000.0) / 1e9
+    return {"ms_per_layer": ms, "matrices": matrices, "bytes_read": read, "bytes_written": written,
+            "achieved_gbs": achieved, "peak_gbs": peak, "peak_kind": peak_kind, "frac": achieved / peak,
+            "kernel": "mxfp4_encode_trellis_kernel (3 launches per layer)"}
+
+
 def stack_configs(layers, steps, stream):
     """The MoE block stack with the attention stubbed: the bench's
     layers (K4) plus the K3 layer-78 block, each behind its post-attention RMS
@@ -607,6 +633,7 @@ def main():
             bf16_peak = float(json.loads(peaks_path.read_text()).get("bf16_tflops", bf16_peak))
         extras["prefill"] = prefill_configs(layers[0], 10, stream, bf16_peak)
         extras["stack"] = stack_configs(layers, 20, stream)
+        extras["encode"] = encode_config(layers[0], 5, stream)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

@@ -120,6 +120,35 @@ int exlr8_dequantize_trellis(const void* packed, int64_t packed_bytes, const voi
                              int scale_dtype, int k, int in_features, int out_features, int sharded_side,
                              float* weight, void* workspace, size_t workspace_bytes, void* stream);
 
+/* ---- MXFP4 encode (load time) ------------------------------------------ */
+
+/* MLX quantize(w, mode="mxfp4") (group 32) of float32 rows w [rows][in]:
+ * codes uint32 [rows][in / 8] (eight E2M1 codes, low nibble first) and E8M0
+ * scales uint8 [rows][in / 32].  Per block of 32: e = round(log2(amax / 6))
+ * clamped to [-127, 127], scale code e + 127 (0 for an all-zero block);
+ * elements rounded to the nearest E2M1 value of v / 2^e, ties to even,
+ * saturating at 6.  The quantisation of dense_trellis.py:97-101
+ * encode_mxfp4 and of joined_mxfp4.py:32.  w and codes 16-byte aligned. */
+int exlr8_mxfp4_quantize(const float* w, int64_t rows, int in_features, uint32_t* codes, uint8_t* scales,
+                         void* stream);
+
+/* JoinedMXFP4 load-time re-encode of one projection of every matrix in a
+ * trellis buffer (joined_mxfp4.py:12-47 encode): matrix e decoded to inner
+ * [in][out] (decode.metal), rows multiplied by in_scale[e][i] * unit[i] when
+ * in_scale is given (the gate/up fold, joined_mxfp4.py:22,30-31: the product
+ * formed in the scale dtype, then widened to float32; unit may be NULL for no
+ * sign vector), quantised as W^T [out][in] as
+ * exlr8_mxfp4_quantize.  Row o of matrix e is written at row
+ * e * rows_per_matrix + row_offset + o of codes [.][in / 8] and scales
+ * [.][in / 32], so gate (row_offset 0) and up (row_offset = out_features,
+ * rows_per_matrix 2 * out_features) land in the joined [E][2m] layout of
+ * joined_mxfp4.py:41-45.  packed and codes 16-byte aligned, scales 4-byte
+ * aligned. */
+int exlr8_mxfp4_encode_trellis(const void* packed, int64_t packed_bytes, int k, int in_features, int out_features,
+                               int sharded_side, const void* in_scale, const void* unit, int scale_dtype,
+                               uint32_t* codes, uint8_t* scales, int64_t rows_per_matrix, int64_t row_offset,
+                               void* stream);
+
 /* ---- router ----------------------------------------------------------- */
 
 /* exlr8/fast_router.py:17-24 route(logits, bias): logits float32 [rows][256],

@@ -92,6 +92,9 @@ _SIGNATURES = {
     "exlr8_moe_layer_noalloc": (c_int, [c_void_p, c_int, c_void_p, c_int64, c_void_p, c_void_p,
                                         POINTER(TrellisExperts), POINTER(DenseExpert), c_void_p, c_void_p, c_void_p,
                                         c_void_p]),
+    "exlr8_mxfp4_quantize": (c_int, [c_void_p, c_int64, c_int, c_void_p, c_void_p, c_void_p]),
+    "exlr8_mxfp4_encode_trellis": (c_int, [c_void_p, c_int64, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_int,
+                                           c_void_p, c_void_p, c_int64, c_int64, c_void_p]),
     "exlr8_mxfp4_prepared_scales_bytes": (c_size_t, [c_int64, c_int]),
     "exlr8_mxfp4_prepare_scales": (c_int, [c_void_p, c_int64, c_int, c_void_p, c_void_p]),
     "exlr8_joined_workspace": (c_size_t, [c_int64, c_int, c_int, c_int, c_int64]),

@@ -496,6 +496,30 @@ int exlr8_dequantize_trellis(const void* packed, int64_t packed_bytes, const voi
       launch_dequantize(inner, suh, svh, scale_dtype, in_features, out_features, weight, as_stream(stream)));
 }
 
+int exlr8_mxfp4_quantize(const float* w, int64_t rows, int in_features, uint32_t* codes, uint8_t* scales,
+                         void* stream) {
+  if (rows < 0 || in_features <= 0 || in_features % 32) return EXLR8_ERR_DIMS;
+  if (rows == 0) return EXLR8_OK;
+  if (!w || !codes || !scales) return EXLR8_ERR_ARG;
+  if (!aligned16(w) || !aligned16(codes)) return EXLR8_ERR_ALIGN;
+  return cuda_status(launch_mxfp4_quantize(w, rows, in_features, codes, scales, as_stream(stream)));
+}
+
+int exlr8_mxfp4_encode_trellis(const void* packed, int64_t packed_bytes, int k, int in_features, int out_features,
+                               int sharded_side, const void* in_scale, const void* unit, int scale_dtype,
+                               uint32_t* codes, uint8_t* scales, int64_t rows_per_matrix, int64_t row_offset,
+                               void* stream) {
+  int64_t count = 0;
+  EXLR8_CHECK(format_status(packed_bytes, k, in_features, out_features, sharded_side, &count));
+  if (!packed || !codes || !scales || (unit && !in_scale)) return EXLR8_ERR_ARG;
+  if (row_offset < 0 || rows_per_matrix < row_offset + out_features) return EXLR8_ERR_DIMS;
+  if (in_scale && !valid_scale(scale_dtype)) return EXLR8_ERR_DTYPE;
+  if (!aligned16(packed) || !aligned16(codes) || (reinterpret_cast<uintptr_t>(scales) & 3u)) return EXLR8_ERR_ALIGN;
+  return cuda_status(launch_mxfp4_encode_trellis(static_cast<const uint32_t*>(packed), count, k, in_features,
+                                                 out_features, sharded_side, in_scale, unit, scale_dtype, codes,
+                                                 scales, rows_per_matrix, row_offset, as_stream(stream)));
+}
+
 int exlr8_route(const float* logits, const float* bias, int64_t rows, uint32_t* indices, float* scores,
                 void* stream) {
   if (rows < 0 || (rows > 0 && (!logits || !bias || !indices || !scores))) return EXLR8_ERR_ARG;

@@ -115,4 +115,22 @@ __device__ __forceinline__ int64_t tile_index(int64_t e, int tk, int tn, int in_
   return ((e * (out_tiles / 8) + tn / 8) * in_tiles + tk) * 8 + tn % 8;
 }
 
+// Inner weight [r][c] of matrix e (decode.metal:9-35): the 16-bit codeword
+// of position (r % 16, c % 16) read from the two words its bits straddle in
+// the tile's 8k-word ring, then the codebook value.
+__device__ __forceinline__ float trellis_weight(const uint32_t* __restrict__ words, int64_t e, int k, int in_tiles,
+                                                int out_tiles, int side, int r, int c) {
+  const int lr = r & 15, lc = c & 15;
+  const uint32_t lane = (lc & 7) * 4 + ((lr & 7) >> 1);
+  const uint32_t slot = (lr & 1) + ((lr & 8) >> 2) + ((lc & 8) >> 1);
+  const uint32_t code = lane * 8 + slot;
+  const uint32_t nwords = 8u * k;
+  const uint32_t last_bit = (code + 1) * k + 256u * k;
+  const uint32_t last_word = (last_bit - 1) / 32;
+  const uint32_t shift = (last_word + 1) * 32 - last_bit;
+  const uint32_t* tile = words + tile_index(e, r >> 4, c >> 4, in_tiles, out_tiles, side) * nwords;
+  const uint64_t merged = (static_cast<uint64_t>(tile[(last_word - 1) % nwords]) << 32) | tile[last_word % nwords];
+  return decode_value(static_cast<uint32_t>(merged >> shift) & 0xFFFFu);
+}
+
 }  // namespace exlr8

@@ -37,17 +37,7 @@ __global__ void decode_matrix_kernel(const uint32_t* __restrict__ words, int64_t
   const int64_t index = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (index >= static_cast<int64_t>(in_features) * out_features) return;
   const int r = static_cast<int>(index / out_features), c = static_cast<int>(index % out_features);
-  const int tk = r >> 4, tn = c >> 4, lr = r & 15, lc = c & 15;
-  const uint32_t lane = (lc & 7) * 4 + ((lr & 7) >> 1);
-  const uint32_t slot = (lr & 1) + ((lr & 8) >> 2) + ((lc & 8) >> 1);
-  const uint32_t code = lane * 8 + slot;
-  const uint32_t nwords = 8u * k;
-  const uint32_t last_bit = (code + 1) * k + 256u * k;
-  const uint32_t last_word = (last_bit - 1) / 32;
-  const uint32_t shift = (last_word + 1) * 32 - last_bit;
-  const uint32_t* tile = words + tile_index(expert, tk, tn, in_features / 16, out_features / 16, side) * nwords;
-  const uint64_t merged = (static_cast<uint64_t>(tile[(last_word - 1) % nwords]) << 32) | tile[last_word % nwords];
-  inner[index] = decode_value(static_cast<uint32_t>(merged >> shift) & 0xFFFFu);
+  inner[index] = trellis_weight(words, expert, k, in_features / 16, out_features / 16, side, r, c);
 }
 
 cudaError_t launch_decode_matrix(const uint32_t* words, int64_t expert, int k, int in_features, int out_features,

@@ -12,6 +12,17 @@ cudaError_t launch_decode_matrix(const uint32_t* words, int64_t expert, int k, i
 cudaError_t launch_dequantize(const float* inner, const void* suh, const void* svh, int scale_dtype,
                               int in_features, int out_features, float* weight, cudaStream_t s);
 
+// MXFP4 (MLX quantize mode="mxfp4", group 32) of float rows, and the fused
+// decode + in-scale fold + quantise of every matrix of a trellis buffer
+// (W^T rows land at (e * rows_per_matrix + row_offset + o)).  Codes and the
+// float rows must be 16-byte aligned.
+cudaError_t launch_mxfp4_quantize(const float* w, int64_t rows, int in_features, uint32_t* codes, uint8_t* scales,
+                                  cudaStream_t s);
+cudaError_t launch_mxfp4_encode_trellis(const uint32_t* packed, int64_t matrices, int k, int in_features,
+                                        int out_features, int side, const void* in_scale, const void* unit,
+                                        int scale_dtype, uint32_t* codes, uint8_t* scales, int64_t rows_per_matrix,
+                                        int64_t row_offset, cudaStream_t s);
+
 // bf16 shared expert.  Gate and up in one pass, the last CTA of each 64-row
 // block writing h = SwiGLU(T(g), T(u)) in the activation type; `counters`
 // ([n/64] ints) must be zero at launch.  Partials are [splits][tokens][n].

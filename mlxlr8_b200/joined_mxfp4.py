@@ -2,11 +2,15 @@
 
 The reference builds ``JoinedMXFP4(expert)`` by re-encoding trellis experts
 to MXFP4 at load time (joined_mxfp4.py:12-47) and then runs MLX
-``gather_qmm(mode="mxfp4")`` products (joined_mxfp4.py:90-134).  Here the
-MXFP4 weights arrive encoded (the ``weights`` dictionary of the reference:
+``gather_qmm(mode="mxfp4")`` products (joined_mxfp4.py:90-134).  Here
+``encode(expert)`` re-encodes on the GPU (one fused decode + in-scale fold +
+quantise launch per projection, ``exlr8_mxfp4_encode_trellis``) into the
+``weights`` dictionary of the reference:
 ``{"gate_up": (codes, scales, None), "down": (codes, scales, None)}`` with
-uint32 codes, eight E2M1 values per word, low nibble first, and E8M0 scales
-per 32 inputs) and every product runs as a grouped block-scaled tcgen05 GEMM
+uint32 codes (held as int32 bits), eight E2M1 values per word, low nibble
+first, and E8M0 scales per 32 inputs.  ``JoinedMXFP4(expert)`` encodes;
+``JoinedMXFP4(unit, weights, scales, hidden, intermediate)`` takes weights
+already encoded.  Every product runs as a grouped block-scaled tcgen05 GEMM
 in ``libexlr8_b200.so``:
 
 * ``slots(x, ids)`` -> ``[*ids.shape, hidden]`` per-slot expert outputs in
@@ -35,13 +39,77 @@ def _prepare(scales: torch.Tensor, rows: int, in_features: int, device) -> torch
     return out
 
 
+def encode(expert):
+    """``encode(expert)`` (joined_mxfp4.py:12-47) on the GPU -> (unit, weights).
+
+    ``expert`` is a resident trellis layer (``ExpertLayer``: ``packed``,
+    ``scales``, ``k``, ``hidden``, ``intermediate``).  ``unit`` is the sign of
+    matrix 0's gate in-scale, shape [1, hidden] in the scale dtype
+    (joined_mxfp4.py:13).  Every matrix of each projection is decoded
+    (decode.metal), gate/up rows multiplied by ``in_scale[e] * unit``
+    (joined_mxfp4.py:22,30-31) and quantised transposed with MLX's mxfp4 rule;
+    gate rows land at 0..m-1 and up rows at m..2m-1 of the joined
+    [E, 2m, h/8] buffer (joined_mxfp4.py:41-45)."""
+    packed = expert.packed
+    device = _lib.require_cuda(packed["gate"], packed["up"], packed["down"])
+    h, m, k = expert.hidden, expert.intermediate, expert.k
+    matrices = packed["gate"].numel() // (h * m * k // 8)
+    gate_in = expert.scales["gate"][0]
+    unit = torch.sign(gate_in[:1]).contiguous()
+    weights = {
+        "gate_up": (torch.empty(matrices, 2 * m, h // 8, dtype=torch.int32, device=device),
+                    torch.empty(matrices, 2 * m, h // 32, dtype=torch.uint8, device=device), None),
+        "down": (torch.empty(matrices, h, m // 8, dtype=torch.int32, device=device),
+                 torch.empty(matrices, h, m // 32, dtype=torch.uint8, device=device), None),
+    }
+    stream = _lib.stream_handle(device)
+    for projection, offset in (("gate", 0), ("up", m), ("down", 0)):
+        incoming, outgoing, side = (m, h, 2) if projection == "down" else (h, m, 1)
+        codes, sc, _ = weights["down" if projection == "down" else "gate_up"]
+        src = packed[projection].contiguous()
+        in_scale = unit_arg = None
+        code = 0
+        if side == 1:
+            in_scale = expert.scales[projection][0].contiguous()
+            if tuple(in_scale.shape) != (matrices, incoming):
+                raise ValueError("expert side vectors must contain full signed channel scales")
+            unit_arg = unit.to(in_scale.dtype).contiguous()
+            code = _lib.scale_code(in_scale)
+        _lib.check(_lib.lib().exlr8_mxfp4_encode_trellis(
+            src.data_ptr(), src.numel(), k, incoming, outgoing, side,
+            in_scale.data_ptr() if in_scale is not None else None,
+            unit_arg.data_ptr() if unit_arg is not None else None, code, codes.data_ptr(), sc.data_ptr(),
+            codes.shape[1], offset, stream))
+    return unit, weights
+
+
+def quantize(w):
+    """MLX ``quantize(w, mode="mxfp4")`` of float32 rows w [..., k] ->
+    (codes [..., k/8] int32 bits of uint32, scales [..., k/32] uint8)."""
+    device = _lib.require_cuda(w)
+    k = w.shape[-1]
+    src = w.to(torch.float32).contiguous()
+    rows = src.numel() // k if k else 0
+    codes = torch.empty(tuple(w.shape[:-1]) + (k // 8,), dtype=torch.int32, device=device)
+    scales = torch.empty(tuple(w.shape[:-1]) + (k // 32,), dtype=torch.uint8, device=device)
+    _lib.check(_lib.lib().exlr8_mxfp4_quantize(src.data_ptr(), rows, k, codes.data_ptr(), scales.data_ptr(),
+                                               _lib.stream_handle(device)))
+    return codes, scales
+
+
 class JoinedMXFP4:
-    """``unit`` [hidden] sign vector; ``weights`` as above; ``scales`` the
+    """``JoinedMXFP4(expert)`` re-encodes a resident trellis layer
+    (joined_mxfp4.py:137-141); ``JoinedMXFP4(unit, weights, scales, hidden,
+    intermediate)`` takes ``unit`` [hidden] and ``weights`` as above and the
     expert scale dictionary (only ``scales["gate"][1]``, ``scales["up"][1]``,
     ``scales["down"][0]`` and ``scales["down"][1]`` are read, as in the
     reference's joined path)."""
 
-    def __init__(self, unit, weights, scales, hidden: int, intermediate: int):
+    def __init__(self, unit, weights=None, scales=None, hidden: int | None = None, intermediate: int | None = None):
+        if weights is None:
+            expert = unit
+            unit, weights = encode(expert)
+            scales, hidden, intermediate = expert.scales, expert.hidden, expert.intermediate
         codes_gu, scales_gu = weights["gate_up"][0], weights["gate_up"][1]
         codes_d, scales_d = weights["down"][0], weights["down"][1]
         device = _lib.require_cuda(unit, codes_gu, scales_gu, codes_d, scales_d)

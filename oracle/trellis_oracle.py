@@ -471,6 +471,92 @@ def mxfp4_dequantize(weights, scales):
     return (values * np.repeat(s, 32, axis=-1)).astype(F32)
 
 
+def e8m0_encode(amax):
+    """E8M0 code of blocks with largest magnitude ``amax`` under MLX 0.32.3
+    ``quantize(mode="mxfp4")`` (fp_quantize: ``scale = amax / 6`` in float32,
+    then the fp8_e8m0 conversion ``n = int(round(log2(scale)))`` clamped to
+    [-127, 127], code n + 127).  log2 is the correctly rounded float32 value
+    (through float64) and ``round`` is Metal's, half away from zero, so a
+    scale whose float32 log2 is exactly n + 1/2 rounds away from zero.
+    amax = 0 gives code 0; a non-finite amax gives 255."""
+    amax = np.asarray(amax, F32)
+    x = (amax / F32(6.0)).astype(F32)
+    with np.errstate(divide="ignore", invalid="ignore"):
+        lf = np.log2(x.astype(np.float64)).astype(F32).astype(np.float64)
+    n = np.where(lf >= 0, np.floor(lf + 0.5), np.ceil(lf - 0.5))
+    n = np.nan_to_num(n, nan=0.0, posinf=127.0, neginf=-127.0)
+    code = np.clip(n, -127, 127).astype(np.int64) + 127
+    code = np.where(amax == 0, 0, code)
+    code = np.where(np.isfinite(amax), code, 255)
+    return code.astype(np.uint8)
+
+
+def e2m1_encode(q):
+    """E2M1 code of q (MLX fp4_e2m1 conversion): nearest of 0, .5, 1, 1.5, 2,
+    3, 4, 6 with ties to the even code, saturating at 6; bit 3 = signbit(q);
+    NaN -> 7."""
+    q = np.asarray(q, F32)
+    a = np.abs(q)
+    m = ((a > 0.25).astype(np.uint32) + (a >= 0.75) + (a > 1.25) + (a >= 1.75) + (a > 2.5) + (a >= 3.5) + (a > 5.0))
+    code = np.where(np.signbit(q), np.uint32(8), np.uint32(0)) | m.astype(np.uint32)
+    return np.where(np.isnan(q), np.uint32(7), code).astype(np.uint32)
+
+
+def mxfp4_quantize(w):
+    """MLX 0.32.3 ``quantize(w, mode="mxfp4")`` (group 32, bits 4) as used by
+    joined_mxfp4.py:32 and dense_trellis.py:97-101: w [..., k] float32 ->
+    (codes [..., k/8] uint32, eight E2M1 codes per word low nibble first;
+    scales [..., k/32] uint8 E8M0).  Elements are coded from ``v / 2^e``
+    with 2^e the decoded scale (2^-127 for code 0)."""
+    w = np.asarray(w, F32)
+    k = w.shape[-1]
+    if k % 32:
+        raise ValueError("mxfp4 quantisation needs a multiple of 32 values per row")
+    g = w.reshape(w.shape[:-1] + (k // 32, 32))
+    with np.errstate(invalid="ignore"):
+        amax = np.max(np.abs(g), axis=-1)
+    scales = e8m0_encode(amax)
+    with np.errstate(over="ignore", invalid="ignore", divide="ignore"):
+        q = (g / e8m0_value(scales)[..., None]).astype(F32)
+    nib = e2m1_encode(q).reshape(w.shape[:-1] + (k // 8, 8))
+    codes = np.zeros(nib.shape[:-1], np.uint32)
+    for j in range(8):
+        codes |= nib[..., j] << np.uint32(4 * j)
+    return codes, scales
+
+
+def encode_joined(packed, scales, k, hidden, intermediate, experts=None):
+    """``encode(expert)`` (joined_mxfp4.py:12-47): ``unit = sign(gate
+    in-scale of matrix 0)``; every matrix of every projection decoded to inner
+    [in, out] (decode.metal), gate/up rows times ``in_scale[e] * unit``
+    (float32), quantised as ``inner.T`` with ``mxfp4_quantize``; gate and up
+    joined along rows ([E, 2m, h/8], gate first).  ``experts`` restricts the
+    matrices computed (the others stay zero); the fold product is formed in
+    the scale dtype (fp16 * fp16 -> fp16 for fp16 scales) before the float32
+    multiply, as the reference's MLX arrays do; returns (unit [h] float32,
+    {"gate_up": (codes, scales), "down": (codes, scales)})."""
+    h, m = hidden, intermediate
+    count = np.asarray(packed["gate"]).size // (h * m * k // 8)
+    keep = range(count) if experts is None else sorted(set(int(i) for i in experts))
+    unit_typed = np.sign(np.asarray(scales["gate"][0])[0])  # in the scale dtype
+    unit = unit_typed.astype(F32)
+    out = {"gate_up": (np.zeros((count, 2 * m, h // 8), np.uint32), np.zeros((count, 2 * m, h // 32), np.uint8)),
+           "down": (np.zeros((count, h, m // 8), np.uint32), np.zeros((count, h, m // 32), np.uint8))}
+    for projection, offset in (("gate", 0), ("up", m), ("down", 0)):
+        incoming, outgoing, side = (m, h, 2) if projection == "down" else (h, m, 1)
+        target = out["down" if projection == "down" else "gate_up"]
+        for e in keep:
+            inner = decode_trellis(packed[projection], k, incoming, outgoing, side, e).astype(F32)
+            if side == 1:
+                # (scale * unit) in the scale dtype, then float32 (joined_mxfp4.py:22)
+                fold = (np.asarray(scales[projection][0])[e] * unit_typed).astype(F32)
+                inner = inner * fold[:, None]
+            codes, sc = mxfp4_quantize(inner.T)
+            target[0][e, offset:offset + outgoing] = codes
+            target[1][e, offset:offset + outgoing] = sc
+    return unit, out
+
+
 def joined_slots(x, indices, unit, gate_up, down, scales, hidden, intermediate, dtype):
     """Joined MXFP4 slots (joined_mxfp4.py:90-134 + fast_decode_finish.metal).
 

@@ -1,0 +1,118 @@
+"""The CPU restatement of MLX ``quantize(mode="mxfp4")`` and of the joined
+re-encode (joined_mxfp4.py:12-47), checked on the properties the rule fixes:
+exactly representable blocks round-trip, E2M1 ties go to the even code, the
+E8M0 exponent is round(log2(amax / 6)) with the resulting clipping above 6,
+zero blocks take code 0, and the encode keeps the reference's orientation
+(test_joined_mxfp4.py:44-58: ``weights[i, offset:offset + out]`` equals the
+quantisation of the folded ``decode(...).T``)."""
+
+import numpy as np
+import pytest
+
+from oracle import trellis_oracle as ref
+
+F32 = np.float32
+
+
+def test_representable_blocks_round_trip():
+    rng = np.random.default_rng(5)
+    codes = rng.integers(0, 16, (64, 32)).astype(np.uint32)
+    for exp in (-20, -3, 0, 7):
+        vals = ref.e2m1_value(codes) * F32(2.0 ** exp)
+        vals[:, 0] = F32(6.0 * 2.0 ** exp)  # amax / 6 = 2^exp: scale code exp + 127
+        c, s = ref.mxfp4_quantize(vals)
+        assert np.all(s == exp + 127)
+        np.testing.assert_array_equal(ref.mxfp4_dequantize(c[None], s[None])[0], vals)
+
+
+def test_e2m1_ties_to_even_saturation_and_sign():
+    q = np.array([0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5.0, 6.0, 7.0, 1e30, np.inf,
+                  np.nextafter(F32(0.25), F32(1)), np.nextafter(F32(5.0), F32(9)), -0.0, 0.0, -0.25, -6.5, np.nan],
+                 F32)
+    want = [0, 2, 2, 4, 4, 6, 6, 7, 7, 7, 7, 1, 7, 8, 0, 8, 15, 7]
+    np.testing.assert_array_equal(ref.e2m1_encode(q), want)
+
+
+def test_e8m0_rounds_log2_of_amax_over_six():
+    amax = np.array([6.0, 3.0, 12.0, 0.0, np.inf, 6.0 * 2.0 ** -130, 6.0 * 2.0 ** 120, 3.4028235e38], F32)
+    np.testing.assert_array_equal(ref.e8m0_encode(amax), [127, 126, 128, 0, 255, 0, 247, 252])
+    # Around amax / 6 = sqrt(2) * 2^n the code steps from n to n + 1; the
+    # float32 log2 lands on n + 1/2 for a few scales, which round away from 0.
+    for n in (-5, 0, 3):
+        centre = F32(6.0 * np.sqrt(2.0) * 2.0 ** n)
+        values = centre + np.arange(-40, 41, dtype=F32) * np.spacing(centre)
+        codes = ref.e8m0_encode(values).astype(int) - 127
+        assert set(codes) == {n, n + 1}
+        assert np.all(np.diff(codes) >= 0)
+        lf = np.log2((values / F32(6)).astype(np.float64)).astype(F32)
+        at_half = lf == F32(n + 0.5)
+        if np.any(at_half):
+            assert np.all(codes[at_half] == (n + 1 if n + 0.5 > 0 else n))
+    rng = np.random.default_rng(9)
+    amax = np.exp(rng.uniform(-30, 30, 4096)).astype(F32)
+    scale = ref.e8m0_value(ref.e8m0_encode(amax)).astype(np.float64)
+    ratio = amax.astype(np.float64) / 6.0 / scale
+    assert np.all(ratio >= 2 ** -0.5 * (1 - 1e-6)) and np.all(ratio <= 2 ** 0.5 * (1 + 1e-6))
+
+
+def test_quantisation_error_bound_and_clipping():
+    rng = np.random.default_rng(11)
+    w = (rng.standard_normal((128, 256)) * np.exp(rng.uniform(-6, 3, (128, 1)))).astype(F32)
+    c, s = ref.mxfp4_quantize(w)
+    deq = ref.mxfp4_dequantize(c[None], s[None])[0]
+    scale = np.repeat(ref.e8m0_value(s), 32, axis=-1)
+    q = np.abs(w) / scale
+    # Within the E2M1 range the error is at most half the level spacing (1 at
+    # the 4..6 step); above 6 it is the clipping.
+    inside = q <= 6
+    assert np.all(np.abs(deq - w)[inside] <= scale[inside] * 1.0)
+    np.testing.assert_array_equal(np.abs(deq[~inside]), 6 * scale[~inside])
+    assert np.any(~inside)  # round(log2(amax / 6)) can put amax above 6 * 2^e
+    np.testing.assert_array_equal(np.signbit(deq) & (deq != 0), np.signbit(w) & (deq != 0))
+
+
+def test_zero_blocks_and_negative_zero():
+    w = np.zeros((2, 64), F32)
+    w[1, :32] = -0.0
+    w[1, 32] = 1.0
+    c, s = ref.mxfp4_quantize(w)
+    np.testing.assert_array_equal(s, [[0, 0], [0, ref.e8m0_encode(F32(1.0))]])
+    assert np.all(c[0] == 0)
+    assert np.all(c[1, :4] == 0x88888888)
+
+
+def test_encode_orientation_and_fold():
+    """Reference fixture layout (test_joined_mxfp4.py:18-35) at a small size."""
+    rng = np.random.default_rng(817)
+    h, m, count, k = 256, 128, 3, 4
+    signs = rng.choice([-1, 1], h).astype(np.float16)
+    packed, scales = {}, {}
+    for projection in ("gate", "up", "down"):
+        incoming, outgoing = (m, h) if projection == "down" else (h, m)
+        packed[projection] = rng.integers(0, 256, count * h * m // 2, dtype=np.uint8)
+        inc = rng.uniform(.01, .04, (count, incoming)).astype(np.float16)
+        if projection != "down":
+            block = rng.uniform(.01, .04, (count, h // 128)).astype(np.float16)
+            block *= rng.choice([-1, 1], block.shape).astype(np.float16)
+            inc = np.repeat(block, 128, axis=-1) * signs
+        scales[projection] = (inc, rng.uniform(-.5, .5, (count, outgoing)).astype(np.float16))
+    unit, weights = ref.encode_joined(packed, scales, k, h, m)
+    np.testing.assert_array_equal(unit, np.sign(scales["gate"][0][0].astype(F32)))
+    for projection, offset in (("gate", 0), ("up", m), ("down", 0)):
+        incoming, outgoing, side = (m, h, 2) if projection == "down" else (h, m, 1)
+        target = weights["down" if projection == "down" else "gate_up"]
+        for i in range(count):
+            matrix = ref.decode_trellis(packed[projection], k, incoming, outgoing, side, i).astype(F32)
+            if side == 1:
+                matrix = matrix * (scales[projection][0][i].astype(F32) * unit)[:, None]
+            codes, sc = ref.mxfp4_quantize(matrix.T)
+            np.testing.assert_array_equal(target[0][i, offset:offset + outgoing], codes)
+            np.testing.assert_array_equal(target[1][i, offset:offset + outgoing], sc)
+            deq = ref.mxfp4_dequantize(codes[None], sc[None])[0]
+            rel = np.linalg.norm(deq - matrix.T) / np.linalg.norm(matrix.T)
+            assert rel < 0.15
+
+
+def test_quantize_rejects_ragged_rows():
+    with pytest.raises(ValueError, match="multiple of 32"):
+        ref.mxfp4_quantize(np.zeros((2, 48), F32))
