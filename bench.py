@@ -400,6 +400,53 @@ def encode_config(layer, steps, stream):
             "kernel": "mxfp4_encode_trellis_kernel (3 launches per layer)"}
 
 
+def loader_config():
+    """EXLR8 checkpoint -> device (experts.py:77-148): one
+    full-size K4 layer (256 routed experts + shared, 4.85 GB of codes) written
+    to a scratch directory, then ``ExpertStore(resident=True).layer(3)`` timed
+    on the host clock around the load (and a device synchronize): read only
+    (``optimize=False``) and read + joined MXFP4 re-encode (``optimize=True``,
+    the reference's load path).  The files are dropped from the page cache
+    before each load (posix_fadvise DONTNEED), so the read comes from the
+    disk, not from memory."""
+    import shutil
+    import tempfile
+
+    import torch
+
+    from mlxlr8_b200.experts import ExpertStore
+    from mlxlr8_b200.synthetic import write_checkpoint
+
+    scratch = Path(tempfile.mkdtemp(prefix="exlr8-ckpt-"))
+    try:
+        free = shutil.disk_usage(scratch).free
+        routed = 256 if free > 12 * 2**30 else max(8, int(free / 2**30 / 12 * 256) // 8 * 8)
+        write_checkpoint(scratch, layers=(3,), routed=routed, seed=9)
+        files = sorted(p for p in scratch.rglob("*.safetensors"))
+        total = sum(p.stat().st_size for p in files)
+        res = {"routed_experts": routed, "file_bytes": total}
+        for optimize in (False, True):
+            for p in files:
+                fd = os.open(p, os.O_RDONLY)
+                os.fsync(fd)
+                os.posix_fadvise(fd, 0, 0, os.POSIX_FADV_DONTNEED)
+                os.close(fd)
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            store = ExpertStore(scratch, resident=True, optimize=optimize)
+            store.layer(3)
+            torch.cuda.synchronize()
+            dt = time.perf_counter() - t0
+            key = "read_and_reencode" if optimize else "read"
+            res[key] = {"seconds": dt, "file_gb_per_s": total / dt / 1e9,
+                        "resident_bytes": store.stats()["resident_bytes"]}
+            del store
+            torch.cuda.empty_cache()
+        return res
+    finally:
+        shutil.rmtree(scratch, ignore_errors=True)
+
+
 def stack_configs(layers, steps, stream):
     """The MoE block stack with the attention stubbed: the bench's
     layers (K4) plus the K3 layer-78 block, each behind its post-attention RMS
@@ -634,6 +681,7 @@ def main():
         extras["prefill"] = prefill_configs(layers[0], 10, stream, bf16_peak)
         extras["stack"] = stack_configs(layers, 20, stream)
         extras["encode"] = encode_config(layers[0], 5, stream)
+        extras["loader"] = loader_config()
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

@@ -229,3 +229,108 @@ def zipf_bias(seed: int, s: float = 1.1, experts: int = 256, strength: float = 0
     rank = torch.empty(experts, dtype=torch.float32, device=device)
     rank[order] = torch.arange(experts, dtype=torch.float32, device=device)
     return (-strength * s * torch.log(rank + 1.0)).float()
+
+
+# ---------------------------------------------------------------------------
+# EXLR8 checkpoint directories on disk (the loader's input format,
+# experts.py:16-33,77-124, dense.py:174-191, README.md:60-74).  Contents are
+# seeded from numpy's default_rng(seed + layer):
+#
+#   packed codes   uniform bytes, routed experts then the shared expert
+#   signs.in/out   +-1 int8 [hidden]
+#   block scales   fp16 U(0.5, 1.5), one per 128 hidden channels, random sign
+#   channel scales fp16 +-U(0.5, 1.5)
+#   router         bf16 N(0, 0.02) [256, hidden]; bias float32 N(0, 0.01)
+# ---------------------------------------------------------------------------
+
+_SAFETENSORS_DTYPES = {"uint8": "U8", "int8": "I8", "int32": "I32", "float16": "F16", "float32": "F32"}
+
+
+def _write_safetensors(path, entries, chunk=64 << 20):
+    """Write a safetensors file from (name, dtype, shape, source) entries
+    without holding big tensors in memory: ``source`` is a numpy array, or a
+    callable ``source(n) -> bytes`` streamed in chunks for uint8 tensors.
+    bf16 tensors are passed as uint16 bit patterns with dtype ``"BF16"``."""
+    import json
+    import struct
+
+    import numpy as np
+
+    header, offset = {}, 0
+    for name, dtype, shape, _ in entries:
+        itemsize = {"U8": 1, "I8": 1, "F16": 2, "BF16": 2, "I32": 4, "F32": 4}[dtype]
+        size = int(np.prod(shape, dtype=np.int64)) * itemsize
+        header[name] = {"dtype": dtype, "shape": list(shape), "data_offsets": [offset, offset + size]}
+        offset += size
+    blob = json.dumps(header, separators=(",", ":")).encode()
+    blob += b" " * (-len(blob) % 8)
+    with open(path, "wb") as out:
+        out.write(struct.pack("<Q", len(blob)))
+        out.write(blob)
+        for name, dtype, shape, source in entries:
+            begin, end = header[name]["data_offsets"]
+            if callable(source):
+                left = end - begin
+                while left:
+                    n = min(chunk, left)
+                    out.write(source(n))
+                    left -= n
+            else:
+                out.write(np.ascontiguousarray(source).tobytes())
+
+
+def write_checkpoint(path, layers=(3,), hidden: int = 6144, intermediate: int = 2048, routed: int = 256,
+                     seed: int = 0, router_format: int = 6):
+    """Write an EXLR8 checkpoint directory holding the expert and router
+    files of ``layers`` (K3 for layer 78, K4 otherwise, as the up1 manifest
+    selects) and return its path.  A full-size layer is 4.85 GB of codes."""
+    import json
+    from pathlib import Path
+
+    import numpy as np
+
+    root = Path(path)
+    for sub in ("manifests", "experts", "dense"):
+        (root / sub).mkdir(parents=True, exist_ok=True)
+    plans = {}
+    h, m = hidden, intermediate
+    for number in layers:
+        k = 3 if number == 78 else 4
+        plans[str(number)] = {"gate": [[k]] * routed, "up": [[k]] * routed, "down": [k] * routed,
+                              "shared": {"gate": [k], "up": [k], "down": k}}
+        rng = np.random.default_rng(seed + number)
+        nbytes = h * m * k // 8
+        entries = []
+        for projection in ("gate", "up", "down"):
+            entries.append((f"trellis.{projection}", "U8", (routed * nbytes,), rng.bytes))
+            entries.append((f"shared.trellis.{projection}", "U8", (nbytes,), rng.bytes))
+        _write_safetensors(root / "experts" / f"exlr8-layer-{number:03d}.k{k}.safetensors", entries)
+
+        def signed(shape):
+            return (rng.uniform(0.5, 1.5, shape) * rng.choice([-1.0, 1.0], shape)).astype(np.float16)
+
+        index = [("signs.in", "I8", (h,), rng.choice([-1, 1], h).astype(np.int8)),
+                 ("signs.out", "I8", (h,), rng.choice([-1, 1], h).astype(np.int8))]
+        for projection in ("gate", "up", "down"):
+            block_name = "sv_block" if projection == "down" else "su_block"
+            channel_name = "suh" if projection == "down" else "svh"
+            other = m
+            for prefix, count in ((f"k{k}", routed), (f"shared.k{k}", 1)):
+                index.append((f"{prefix}.{projection}.{block_name}", "F16", (count, h // 128),
+                              signed((count, h // 128))))
+                index.append((f"{prefix}.{projection}.{channel_name}", "F16", (count, other), signed((count, other))))
+        _write_safetensors(root / "experts" / f"exlr8-layer-{number:03d}.index.safetensors", index)
+
+        gate = (rng.standard_normal((256, h)) * 0.02).astype(np.float32)
+        dense = [("mlp.gate.record", "I32", (5,), np.array([router_format, 256, h, 0, 0], np.int32))]
+        if router_format == 6:
+            bits = gate.view(np.uint32)
+            bf16 = ((bits + 0x7FFF + ((bits >> 16) & 1)) >> 16).astype(np.uint16)
+            dense.append(("mlp.gate.bf16", "BF16", (256, h), bf16))
+        else:
+            dense.append(("mlp.gate.fp32", "F32", (256, h), gate))
+        dense.append(("mlp.gate.e_score_correction_bias", "F32", (256,),
+                      (rng.standard_normal(256) * 0.01).astype(np.float32)))
+        _write_safetensors(root / "dense" / f"exlr8-dense-{number:03d}.safetensors", dense)
+    (root / "manifests" / "exlr8-manifest-up1.json").write_text(json.dumps({"name": "up1", "layers": plans}))
+    return root
