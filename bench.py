@@ -335,6 +335,58 @@ def decode_batches(layers, moes, batches, steps, stream):
     return out
 
 
+def joined_decode_configs(steps, stream):
+    """Decode batches on the joined MXFP4 experts (the reference's resident
+    path for K4 layers, experts.py:134-148): the router + MXFP4 streaming GEMV
+    chain, one CUDA graph per layer cycled over 4 layers.  GB/s counts the
+    MXFP4 codes and E8M0 scales of the distinct experts touched (routed +
+    the shared expert 256) per step."""
+    import torch
+
+    from mlxlr8_b200.joined_mxfp4 import JoinedMoELayer, JoinedMXFP4
+    from mlxlr8_b200.synthetic import make_joined
+
+    peak, peak_kind = measured_peaks()
+    per_expert = 3 * HIDDEN * INTER // 2 + 3 * HIDDEN * INTER // 32
+    layers = []
+    for i in range(4):
+        j = make_joined(seed=200 + i)
+        layers.append((j, JoinedMoELayer(j.gate_weight, j.bias,
+                                         JoinedMXFP4(j.unit, j.weights, j.scales, j.hidden, j.intermediate))))
+    res = {}
+    for T in (1, 8):
+        xs = [j.tokens(T, seed_offset=60 + i) for i, (j, _) in enumerate(layers)]
+        uniq = []
+        with torch.cuda.stream(stream):
+            for (j, moe), (x, r) in zip(layers, xs):
+                _, ids, _ = moe(x, r, return_routing=True)
+                uniq.append(len(set(int(e) for e in ids.reshape(-1).tolist())))
+            torch.cuda.synchronize()
+            graphs = []
+            for (j, moe), (x, r) in zip(layers, xs):
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=stream):
+                    moe(x, r)
+                graphs.append(g)
+        state = {"s": 0}
+
+        def replay():
+            graphs[state["s"] % len(graphs)].replay()
+            state["s"] += 1
+
+        ms = time_calls(replay, steps, 5, stream)
+        gbs = statistics.mean(uniq) * per_expert / (ms / 1000.0) / 1e9
+        res[f"joined_T{T}"] = {"tokens_per_s": T / (ms / 1000.0), "ms_per_layer": ms,
+                               "experts_touched_mean": statistics.mean(uniq), "weight_gb_per_s": gbs,
+                               "frac_of_hbm": gbs / peak, "peak_kind": peak_kind,
+                               "path": "router_plan -> prep -> MXFP4 stream (gate/up) -> gate finish -> "
+                                       "MXFP4 stream (down) -> fused finish"}
+        del graphs
+    del layers
+    torch.cuda.empty_cache()
+    return res
+
+
 def prefill_configs(layer_k4, steps, stream, peak_tflops):
     """configs[2] (joined MXFP4, 4096 tokens) and configs[4] (128 tokens, K4 and the K3 layer-78 width)."""
     import torch
@@ -680,6 +732,7 @@ def main():
             bf16_peak = float(json.loads(peaks_path.read_text()).get("bf16_tflops", bf16_peak))
         extras["prefill"] = prefill_configs(layers[0], 10, stream, bf16_peak)
         extras["stack"] = stack_configs(layers, 20, stream)
+        extras["joined_decode"] = joined_decode_configs(min(args.steps, 200), stream)
         extras["encode"] = encode_config(layers[0], 5, stream)
         extras["loader"] = loader_config()
 

@@ -395,6 +395,14 @@ typedef struct exlr8_joined_mxfp4 {
 size_t exlr8_mxfp4_prepared_scales_bytes(int64_t rows, int in_features);
 int exlr8_mxfp4_prepare_scales(const uint8_t* scales, int64_t rows, int in_features, uint8_t* prepared, void* stream);
 
+/* The joined calls below pick their path by batch size, as the reference's
+ * _inner does (joined_mxfp4.py:90-134): up to 16 token rows a streaming
+ * MXFP4 GEMV over the selected experts (float16 hi/lo activations, float32
+ * accumulation, E8M0 scales applied per 32-block), above it the grouped
+ * block-scaled tensor-core GEMM (E4M3 hi/lo activations).  Both read the
+ * prepared scales; the stream also reads gate_up / down through 2-D tensor
+ * maps (rows of in_features / 2 bytes). */
+
 /* JoinedMXFP4.slots(x, ids) (joined_mxfp4.py:147-150): x [tokens][hidden],
  * indices uint32 [tokens][slots] -> out [tokens][slots][hidden] in x's dtype,
  * each slot T(H(v) * down_out[e]).  Ids outside [0, experts) give zeros.

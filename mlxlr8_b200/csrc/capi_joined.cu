@@ -10,9 +10,11 @@
 #include "capi_util.cuh"
 #include "common.cuh"
 #include "joined.cuh"
+#include "joined_stream.cuh"
 #include "mx_gemm.cuh"
 #include "router.cuh"
 #include "router_gemm.cuh"
+#include "stream.cuh"
 #include "trellis_gemv.cuh"
 
 using namespace exlr8;
@@ -76,6 +78,118 @@ int check_joined(const exlr8_joined_mxfp4* w) {
     return EXLR8_ERR_ARG;
   if (!aligned32(w->gate_up) || !aligned32(w->down) || !aligned16(w->gate_up_scales) || !aligned16(w->down_scales))
     return EXLR8_ERR_ALIGN;
+  return EXLR8_OK;
+}
+
+// ---- decode batches: the MXFP4 streaming GEMV -----------------------------
+//
+// Up to kJoinedStreamMaxTokens token rows the joined products run as the
+// streaming GEMV of joined_stream.cu (the reference's ordered-gather GEMV and
+// small-batch gather_qmm roles): plan (expert groups of <= 8 slots) ->
+// activation records of H(x * unit) -> gate/up stream (one joined [2m]
+// matrix, written as gate and up planes) -> gate finish (Hadamard, output
+// scales, typed SwiGLU, down input scale, Hadamard -> records) -> down stream
+// -> the trellis path's finish kernels (the finishing arithmetic is the same).
+constexpr int64_t kJoinedStreamMaxTokens = 16;
+constexpr int64_t kJoinedStreamCtasHint = 296;  // persistent stream CTAs on a B200 (2 per SM)
+
+struct JoinedSplits {
+  int kb, count;
+};
+
+// K splits of a stream: enough units for >= 4 per persistent CTA, an even
+// number of 128-wide K blocks per split (a stream stage holds two).
+inline JoinedSplits joined_splits(int in_features, int64_t units_per_split, int cap) {
+  const int kblocks = in_features / 128;
+  int64_t want = (4 * kJoinedStreamCtasHint + units_per_split - 1) / (units_per_split > 0 ? units_per_split : 1);
+  if (want < 1) want = 1;
+  if (want > cap) want = cap;
+  if (want > kblocks) want = kblocks;
+  JoinedSplits sp;
+  sp.kb = (kblocks + static_cast<int>(want) - 1) / static_cast<int>(want);
+  sp.kb += sp.kb & 1;  // whole stages (two blocks each) per split
+  sp.count = (kblocks + sp.kb - 1) / sp.kb;
+  return sp;
+}
+
+struct JoinedDecodeLayout {
+  JoinedSplits s1, s2;
+  size_t plan, frag_gu, gu, frag_d, dpart;
+  size_t total() const { return plan + frag_gu + gu + frag_d + dpart; }
+};
+
+JoinedDecodeLayout joined_decode_layout(int64_t rows, int h, int m, int64_t experts) {
+  JoinedDecodeLayout l;
+  l.s1 = joined_splits(h, rows * (2 * m / 128), 16);
+  l.s2 = joined_splits(m, rows * (h / 128), 8);
+  l.plan = align_up(plan_bytes(static_cast<int>(rows), static_cast<int>(experts)));
+  l.frag_gu = align_up(frag_bytes(rows, h, 1));
+  l.gu = align_up(2 * static_cast<size_t>(rows) * l.s1.count * m * sizeof(float));
+  l.frag_d = align_up(frag_bytes(rows, m, 1));
+  l.dpart = align_up(static_cast<size_t>(rows) * l.s2.count * h * sizeof(float));
+  return l;
+}
+
+struct JoinedDecodeBuffers {
+  PlanView plan;
+  unsigned char *frag_gu, *frag_d;
+  float *gu, *dpart;
+};
+
+JoinedDecodeBuffers carve_joined_decode(const JoinedDecodeLayout& l, int64_t rows, int64_t experts, Carver& c) {
+  JoinedDecodeBuffers b;
+  b.plan = plan_view(c.take<int32_t>(l.plan), static_cast<int>(rows), static_cast<int>(experts));
+  b.frag_gu = c.take<unsigned char>(l.frag_gu);
+  b.gu = c.take<float>(l.gu);
+  b.frag_d = c.take<unsigned char>(l.frag_d);
+  b.dpart = c.take<float>(l.dpart);
+  return b;
+}
+
+inline bool use_joined_stream(int64_t tokens) { return tokens <= kJoinedStreamMaxTokens; }
+
+// Everything after the plan up to the float32 down partials in b.dpart.
+int joined_decode_products(const void* x, int x_dtype, int per_slot, int slots, const uint32_t* ids, int64_t rows,
+                           const exlr8_joined_mxfp4* w, const JoinedDecodeLayout& l, const JoinedDecodeBuffers& b,
+                           cudaStream_t s) {
+  const int h = w->hidden, m = w->intermediate;
+  const int n = static_cast<int>(rows), e = static_cast<int>(w->experts);
+  EXLR8_TIMED(EXLR8_KERNEL_PREP, s,
+              launch_prep_frag(x, x_dtype, per_slot, slots, ids, n, w->unit, w->unit, w->scale_dtype, h, e, 1,
+                               b.frag_gu, s, 0, 1));
+  JoinedStreamParams gp;
+  memset(&gp, 0, sizeof(gp));
+  if (!joined_code_map(&gp.codes, w->gate_up, w->experts * 2 * m, h)) return EXLR8_ERR_CUDA;
+  gp.scales = static_cast<const uint8_t*>(w->gate_up_scales);
+  gp.frag = b.frag_gu;
+  gp.partial = b.gu;
+  gp.plan = b.plan;
+  gp.counter = 2;
+  gp.in_features = h;
+  gp.out_features = 2 * m;
+  gp.plane_rows = m;
+  gp.kb_per_split = l.s1.kb;
+  gp.splits = l.s1.count;
+  gp.nslots = n;
+  EXLR8_TIMED(EXLR8_KERNEL_GATE_UP, s, launch_joined_stream(gp, s));
+  EXLR8_TIMED(EXLR8_KERNEL_GATE_FINISH, s,
+              launch_gate_finish_frag(b.gu, l.s1.count, ids, n, w->gate_out, w->up_out, w->down_in, w->scale_dtype, m,
+                                      e, x_dtype, b.frag_d, nullptr, nullptr, 0, 0, nullptr, s, 1));
+  JoinedStreamParams dp;
+  memset(&dp, 0, sizeof(dp));
+  if (!joined_code_map(&dp.codes, w->down, w->experts * h, m)) return EXLR8_ERR_CUDA;
+  dp.scales = static_cast<const uint8_t*>(w->down_scales);
+  dp.frag = b.frag_d;
+  dp.partial = b.dpart;
+  dp.plan = b.plan;
+  dp.counter = 3;
+  dp.in_features = m;
+  dp.out_features = h;
+  dp.plane_rows = h;
+  dp.kb_per_split = l.s2.kb;
+  dp.splits = l.s2.count;
+  dp.nslots = n;
+  EXLR8_TIMED(EXLR8_KERNEL_DOWN, s, launch_joined_stream(dp, s));
   return EXLR8_OK;
 }
 
@@ -144,6 +258,7 @@ int exlr8_mxfp4_prepare_scales(const uint8_t* scales, int64_t rows, int in_featu
 
 size_t exlr8_joined_workspace(int64_t tokens, int slots, int hidden, int intermediate, int64_t experts) {
   if (tokens <= 0 || slots <= 0) return 0;
+  if (use_joined_stream(tokens)) return joined_decode_layout(tokens * slots, hidden, intermediate, experts).total();
   Carver c(nullptr);
   carve_joined(joined_layout(tokens, slots, experts), hidden, intermediate, experts, c);
   return c.used;
@@ -161,6 +276,19 @@ int exlr8_joined_slots(const void* x, int x_dtype, const uint32_t* indices, int6
   if (!workspace || workspace_bytes < exlr8_joined_workspace(tokens, slots, w->hidden, w->intermediate, w->experts))
     return EXLR8_ERR_WORKSPACE;
   cudaStream_t s = as_stream(stream);
+  if (use_joined_stream(tokens)) {
+    const int64_t rows = tokens * slots;
+    const JoinedDecodeLayout dl = joined_decode_layout(rows, w->hidden, w->intermediate, w->experts);
+    Carver dc(workspace);
+    const JoinedDecodeBuffers db = carve_joined_decode(dl, rows, w->experts, dc);
+    EXLR8_TIMED(EXLR8_KERNEL_PLAN, s,
+                launch_plan(indices, static_cast<int>(rows), static_cast<int>(w->experts), slots, -1, db.plan, s));
+    EXLR8_CHECK(joined_decode_products(x, x_dtype, 0, slots, indices, rows, w, dl, db, s));
+    EXLR8_TIMED(EXLR8_KERNEL_FINISH, s,
+                launch_finish(db.dpart, dl.s2.count, nullptr, indices, static_cast<int>(rows), w->down_out,
+                              w->scale_dtype, w->hidden, static_cast<int>(w->experts), x_dtype, out, s));
+    return EXLR8_OK;
+  }
   const JoinedLayout l = joined_layout(tokens, slots, w->experts);
   Carver c(workspace);
   const JoinedBuffers b = carve_joined(l, w->hidden, w->intermediate, w->experts, c);
@@ -183,6 +311,20 @@ int exlr8_joined_finish(const void* x, int x_dtype, const uint32_t* indices, con
   if (!workspace || workspace_bytes < exlr8_joined_workspace(tokens, 9, w->hidden, w->intermediate, w->experts))
     return EXLR8_ERR_WORKSPACE;
   cudaStream_t s = as_stream(stream);
+  if (use_joined_stream(tokens)) {
+    const int64_t rows = tokens * 9;
+    const JoinedDecodeLayout dl = joined_decode_layout(rows, w->hidden, w->intermediate, w->experts);
+    Carver dc(workspace);
+    const JoinedDecodeBuffers db = carve_joined_decode(dl, rows, w->experts, dc);
+    EXLR8_TIMED(EXLR8_KERNEL_PLAN, s,
+                launch_plan(indices, static_cast<int>(rows), static_cast<int>(w->experts), 9, -1, db.plan, s));
+    EXLR8_CHECK(joined_decode_products(x, x_dtype, 0, 9, indices, rows, w, dl, db, s));
+    EXLR8_TIMED(EXLR8_KERNEL_FINISH, s,
+                launch_finish_fused(db.dpart, dl.s2.count, nullptr, indices, static_cast<int>(tokens), w->down_out,
+                                    w->scale_dtype, w->hidden, static_cast<int>(w->experts), scores, residual,
+                                    nullptr, 0, x_dtype, out, s));
+    return EXLR8_OK;
+  }
   const JoinedLayout l = joined_layout(tokens, 9, w->experts);
   Carver c(workspace);
   const JoinedBuffers b = carve_joined(l, w->hidden, w->intermediate, w->experts, c);
@@ -194,11 +336,34 @@ int exlr8_joined_finish(const void* x, int x_dtype, const uint32_t* indices, con
   return EXLR8_OK;
 }
 
+// Router outputs of the fused layer, carved after the expert buffers.
+struct RouterBuffers {
+  float* logits;
+  uint32_t* ids;
+  float* scores;
+  int* done;
+  void* gemm;
+};
+
+size_t router_buffers_bytes(int64_t tokens, int hidden) {
+  return align_up(tokens * 256 * sizeof(float)) + align_up(tokens * 9 * sizeof(uint32_t)) +
+         align_up(tokens * 8 * sizeof(float)) + align_up(sizeof(int)) +
+         align_up(router_gemm_workspace(static_cast<int>(tokens), hidden, EXLR8_DTYPE_F32));
+}
+
+RouterBuffers carve_router(int64_t tokens, int hidden, Carver& c) {
+  RouterBuffers r;
+  r.logits = c.take<float>(tokens * 256 * sizeof(float));
+  r.ids = c.take<uint32_t>(tokens * 9 * sizeof(uint32_t));
+  r.scores = c.take<float>(tokens * 8 * sizeof(float));
+  r.done = c.take<int>(sizeof(int));
+  r.gemm = c.take<char>(router_gemm_workspace(static_cast<int>(tokens), hidden, EXLR8_DTYPE_F32));
+  return r;
+}
+
 size_t exlr8_joined_moe_layer_workspace(int64_t tokens, int hidden, int intermediate, int64_t experts) {
   if (tokens <= 0) return 0;
-  return exlr8_joined_workspace(tokens, 9, hidden, intermediate, experts) + align_up(tokens * 256 * sizeof(float)) +
-         align_up(tokens * 9 * sizeof(uint32_t)) + align_up(tokens * 8 * sizeof(float)) +
-         align_up(router_gemm_workspace(static_cast<int>(tokens), hidden, EXLR8_DTYPE_F32));
+  return exlr8_joined_workspace(tokens, 9, hidden, intermediate, experts) + router_buffers_bytes(tokens, hidden);
 }
 
 int exlr8_joined_moe_layer(const void* x, int x_dtype, const void* residual, int64_t tokens, const float* gate_weight,
@@ -216,24 +381,40 @@ int exlr8_joined_moe_layer(const void* x, int x_dtype, const void* residual, int
       workspace_bytes < exlr8_joined_moe_layer_workspace(tokens, w->hidden, w->intermediate, w->experts))
     return EXLR8_ERR_WORKSPACE;
   cudaStream_t s = as_stream(stream);
+  if (use_joined_stream(tokens)) {
+    // Router, top-8 and the plan in one kernel, then the decode chain.
+    const int64_t rows = tokens * 9;
+    const JoinedDecodeLayout dl = joined_decode_layout(rows, w->hidden, w->intermediate, w->experts);
+    Carver dc(workspace);
+    const JoinedDecodeBuffers db = carve_joined_decode(dl, rows, w->experts, dc);
+    const RouterBuffers rb = carve_router(tokens, w->hidden, dc);
+    uint32_t* ids = indices ? indices : rb.ids;
+    float* sc = scores ? scores : rb.scores;
+    EXLR8_TIMED(EXLR8_KERNEL_ROUTER, s,
+                launch_router_plan(x, x_dtype, static_cast<int>(tokens), w->hidden, gate_weight, rb.logits, bias, ids,
+                                   sc, rb.done, static_cast<int>(w->experts), -1, db.plan, s));
+    EXLR8_CHECK(joined_decode_products(x, x_dtype, 0, 9, ids, rows, w, dl, db, s));
+    EXLR8_TIMED(EXLR8_KERNEL_FINISH, s,
+                launch_finish_fused(db.dpart, dl.s2.count, nullptr, ids, static_cast<int>(tokens), w->down_out,
+                                    w->scale_dtype, w->hidden, static_cast<int>(w->experts), sc, residual, nullptr, 0,
+                                    x_dtype, out, s));
+    return EXLR8_OK;
+  }
   const JoinedLayout l = joined_layout(tokens, 9, w->experts);
   Carver c(workspace);
   const JoinedBuffers b = carve_joined(l, w->hidden, w->intermediate, w->experts, c);
-  float* logits = c.take<float>(tokens * 256 * sizeof(float));
-  uint32_t* ids_buf = c.take<uint32_t>(tokens * 9 * sizeof(uint32_t));
-  float* scores_buf = c.take<float>(tokens * 8 * sizeof(float));
-  void* router_ws = c.take<char>(router_gemm_workspace(static_cast<int>(tokens), w->hidden, EXLR8_DTYPE_F32));
-  uint32_t* ids = indices ? indices : ids_buf;
-  float* sc = scores ? scores : scores_buf;
+  const RouterBuffers rb = carve_router(tokens, w->hidden, c);
+  uint32_t* ids = indices ? indices : rb.ids;
+  float* sc = scores ? scores : rb.scores;
   if (tokens >= kRouterGemmMinTokens) {
     EXLR8_TIMED(EXLR8_KERNEL_ROUTER, s,
-                launch_router_gemm(x, x_dtype, static_cast<int>(tokens), w->hidden, gate_weight, logits, router_ws,
+                launch_router_gemm(x, x_dtype, static_cast<int>(tokens), w->hidden, gate_weight, rb.logits, rb.gemm,
                                    s));
   } else {
     EXLR8_TIMED(EXLR8_KERNEL_ROUTER, s,
-                launch_gate_logits(x, x_dtype, static_cast<int>(tokens), w->hidden, gate_weight, logits, 256, s));
+                launch_gate_logits(x, x_dtype, static_cast<int>(tokens), w->hidden, gate_weight, rb.logits, 256, s));
   }
-  EXLR8_TIMED(EXLR8_KERNEL_ROUTER, s, launch_route(logits, bias, static_cast<int>(tokens), ids, sc, 2.5f, 256u, s));
+  EXLR8_TIMED(EXLR8_KERNEL_ROUTER, s, launch_route(rb.logits, bias, static_cast<int>(tokens), ids, sc, 2.5f, 256u, s));
   EXLR8_CHECK(joined_products(x, x_dtype, ids, tokens, 9, w, l, b, s));
   EXLR8_TIMED(EXLR8_KERNEL_FINISH, s,
               launch_joined_finish(b.v, b.chunks.slot_row, ids, static_cast<int>(tokens), w->hidden,
@@ -264,6 +445,17 @@ int exlr8_router_logits(const void* x, int x_dtype, int64_t tokens, int hidden, 
 int exlr8_joined_status(const void* workspace, int64_t tokens, int slots, int64_t experts, int32_t* header_out,
                         void* stream) {
   if (!workspace || !header_out || tokens <= 0 || slots <= 0) return EXLR8_ERR_ARG;
+  if (use_joined_stream(tokens)) {
+    // Decode chain: no GEMM chunks; [2..3] the stream unit counters, [4] the
+    // bounded-wait error bits of the stream kernels (plan header[9]).
+    int32_t plan_header[16];
+    EXLR8_TRY(cudaMemcpyAsync(plan_header, workspace, sizeof(plan_header), cudaMemcpyDeviceToHost,
+                              as_stream(stream)));
+    EXLR8_TRY(cudaStreamSynchronize(as_stream(stream)));
+    const int32_t out[8] = {0, 0, plan_header[2], plan_header[3], plan_header[9], 0, 0, 0};
+    memcpy(header_out, out, sizeof(out));
+    return EXLR8_OK;
+  }
   const JoinedLayout l = joined_layout(tokens, slots, experts);
   Carver c(const_cast<void*>(workspace));
   // Only the carve offsets are used; hidden/intermediate do not move the header.

@@ -67,10 +67,13 @@ cudaError_t launch_stream(const StreamParams& p, cudaStream_t s);
 
 // xh = H(x[row] * in_scale_p[e]) written as fragment records
 // (metal/fast_decode_prep.metal).  frag holds frag_bytes(nslots, features,
-// projections).
+// projections).  The scale of channel c is in_scale_p[e * scale_stride + c]
+// (scale_stride < 0: features; 0: one vector for every expert, the joined
+// path's unit).  mx_order writes the MXFP4 K order (joined_stream.cuh).
 cudaError_t launch_prep_frag(const void* x, int x_dtype, int per_slot, int slots_per_token, const uint32_t* ids,
                              int nslots, const void* in0, const void* in1, int scale_dtype, int features, int experts,
-                             int projections, unsigned char* frag, cudaStream_t s);
+                             int projections, unsigned char* frag, cudaStream_t s, int scale_stride = -1,
+                             int mx_order = 0);
 
 // gate/up finish (metal/fast_decode_gate_finish.metal) producing the down
 // projection's fragment records (frag_bytes(nslots, features, 1)).  With
@@ -81,6 +84,6 @@ cudaError_t launch_gate_finish_frag(const float* partial, int gu_splits, const u
                                     const void* out_gate, const void* out_up, const void* in_down, int scale_dtype,
                                     int features, int experts, int act_dtype, unsigned char* frag,
                                     const float* dense_g, const float* dense_u, int dense_splits, int dense_tokens,
-                                    void* dense_h, cudaStream_t s);
+                                    void* dense_h, cudaStream_t s, int mx_order = 0);
 
 }  // namespace exlr8

@@ -114,7 +114,11 @@ __device__ __forceinline__ int piece_exponent(float m) {
 
 // v: the warp's transformed block (lane l holds element l + 32j); stage: 128
 // floats of this warp's shared memory; dst: the block's fragment record.
-__device__ __forceinline__ void write_block_record(const float v[4], float* stage, int lane, unsigned char* dst) {
+// mx_order selects the MXFP4 K order of joined_stream.cuh (K tile s: pairs
+// 32(s/2) + 8 tig + 4(s%2) + {0,1} and + {2,3}) instead of the tensor-core
+// order (16 s + 2 tig + {0,1} and + {8,9}).
+__device__ __forceinline__ void write_block_record(const float v[4], float* stage, int lane, unsigned char* dst,
+                                                   int mx_order = 0) {
   float m = 0.0f;
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
@@ -131,10 +135,11 @@ __device__ __forceinline__ void write_block_record(const float v[4], float* stag
   for (int q = 0; q < 2; ++q) {
     const int idx = lane + 32 * q;
     const int ktl = idx >> 3, piece = (idx >> 2) & 1, tig = idx & 3;
-    const float* w = stage + ktl * 16;
+    const int o0 = mx_order ? 32 * (ktl >> 1) + 8 * tig + 4 * (ktl & 1) : ktl * 16 + 2 * tig;
+    const int o1 = mx_order ? o0 + 2 : o0 + 8;
     uint2 b;
-    b.x = pack_half2(split_piece(w[2 * tig] * scale, piece), split_piece(w[2 * tig + 1] * scale, piece));
-    b.y = pack_half2(split_piece(w[2 * tig + 8] * scale, piece), split_piece(w[2 * tig + 9] * scale, piece));
+    b.x = pack_half2(split_piece(stage[o0] * scale, piece), split_piece(stage[o0 + 1] * scale, piece));
+    b.y = pack_half2(split_piece(stage[o1] * scale, piece), split_piece(stage[o1 + 1] * scale, piece));
     out[idx] = b;
   }
   if (lane < 4) reinterpret_cast<float*>(dst + 512)[lane] = lane == 0 ? ldexpf(1.0f, ex) : 0.0f;
@@ -144,7 +149,7 @@ __device__ __forceinline__ void write_block_record(const float v[4], float* stag
 __global__ void __launch_bounds__(kFragWarps * 32) prep_frag_kernel(
     const void* __restrict__ x, int x_dtype, int per_slot, int slots_per_token, const uint32_t* __restrict__ ids,
     int nslots, const void* __restrict__ in0, const void* __restrict__ in1, int scale_dtype, int features,
-    int experts, int projections, unsigned char* __restrict__ frag) {
+    int experts, int projections, int scale_stride, int mx_order, unsigned char* __restrict__ frag) {
   pdl_launch_dependents();
   pdl_wait();
   __shared__ float stage[kFragWarps][128];
@@ -166,22 +171,24 @@ __global__ void __launch_bounds__(kFragWarps * 32) prep_frag_kernel(
   float v[4];
 #pragma unroll
   for (int j = 0; j < 4; ++j)
-    v[j] = ok ? __fmul_rn(xv[j], load_scale(scale, scale_dtype, static_cast<int64_t>(e) * features + c0 + 32 * j))
+    v[j] = ok ? __fmul_rn(xv[j], load_scale(scale, scale_dtype, static_cast<int64_t>(e) * scale_stride + c0 + 32 * j))
               : 0.0f;
   hadamard128(v, lane);
-  write_block_record(v, stage[warp], lane, frag + task * kFragBlockBytes);
+  write_block_record(v, stage[warp], lane, frag + task * kFragBlockBytes, mx_order);
 }
 
 cudaError_t launch_prep_frag(const void* x, int x_dtype, int per_slot, int slots_per_token, const uint32_t* ids,
                              int nslots, const void* in0, const void* in1, int scale_dtype, int features, int experts,
-                             int projections, unsigned char* frag, cudaStream_t s) {
+                             int projections, unsigned char* frag, cudaStream_t s, int scale_stride, int mx_order) {
+  if (scale_stride < 0) scale_stride = features;
   const int64_t tasks = static_cast<int64_t>(projections) * nslots * (features / 128);
   if (tasks == 0) return cudaSuccess;
   const int64_t grid = (tasks + kFragWarps - 1) / kFragWarps;
   static const cudaError_t carve = prefer_shared_carveout(prep_frag_kernel);
   if (carve != cudaSuccess) return carve;
   return launch_pdl(prep_frag_kernel, dim3(static_cast<unsigned>(grid)), dim3(kFragWarps * 32), 0, s, x, x_dtype,
-                    per_slot, slots_per_token, ids, nslots, in0, in1, scale_dtype, features, experts, projections, frag);
+                    per_slot, slots_per_token, ids, nslots, in0, in1, scale_dtype, features, experts, projections,
+                    scale_stride, mx_order, frag);
 }
 
 // gate/up split sum, Hadamard, output scales, typed SwiGLU, down input scale,
@@ -197,7 +204,7 @@ __global__ void __launch_bounds__(kFragWarps * 32) gate_finish_frag_kernel(
     const void* __restrict__ out_gate, const void* __restrict__ out_up, const void* __restrict__ in_down,
     int scale_dtype, int features, int experts, int act_dtype, unsigned char* __restrict__ frag,
     const float* __restrict__ dense_g, const float* __restrict__ dense_u, int dense_splits, int dense_tokens,
-    void* __restrict__ dense_h) {
+    void* __restrict__ dense_h, int mx_order) {
   pdl_launch_dependents();
   pdl_wait();
   __shared__ float stage[kFragWarps][128];
@@ -271,14 +278,14 @@ __global__ void __launch_bounds__(kFragWarps * 32) gate_finish_frag_kernel(
     act[j] = ok ? __fmul_rn(swiglu_typed(act_dtype, __fmul_rn(gate[j], sg[j]), __fmul_rn(up[j], su[j])), sd[j])
                 : 0.0f;
   hadamard128(act, lane);
-  write_block_record(act, stage[warp], lane, frag + task * kFragBlockBytes);
+  write_block_record(act, stage[warp], lane, frag + task * kFragBlockBytes, mx_order);
 }
 
 cudaError_t launch_gate_finish_frag(const float* partial, int gu_splits, const uint32_t* ids, int nslots,
                                     const void* out_gate, const void* out_up, const void* in_down, int scale_dtype,
                                     int features, int experts, int act_dtype, unsigned char* frag,
                                     const float* dense_g, const float* dense_u, int dense_splits, int dense_tokens,
-                                    void* dense_h, cudaStream_t s) {
+                                    void* dense_h, cudaStream_t s, int mx_order) {
   if (!dense_h) dense_tokens = 0;
   const int64_t tasks = (static_cast<int64_t>(nslots) + dense_tokens) * (features / 128);
   if (tasks == 0) return cudaSuccess;
@@ -287,7 +294,7 @@ cudaError_t launch_gate_finish_frag(const float* partial, int gu_splits, const u
   if (carve != cudaSuccess) return carve;
   return launch_pdl(gate_finish_frag_kernel, dim3(static_cast<unsigned>(grid)), dim3(kFragWarps * 32), 0, s, partial,
                     gu_splits, ids, nslots, out_gate, out_up, in_down, scale_dtype, features, experts, act_dtype, frag,
-                    dense_g, dense_u, dense_splits, dense_tokens, dense_h);
+                    dense_g, dense_u, dense_splits, dense_tokens, dense_h, mx_order);
 }
 
 // ---------------------------------------------------------------------------

@@ -233,3 +233,69 @@ def test_glm_prefill_shape_sampled_tokens():
     expected = ref.combine(values, scores.cpu().numpy()[sample], host(residual)[sample], "bfloat16")
     got = host(out)[sample]
     assert_mxfp4_close(got - host(residual)[sample], expected - host(residual)[sample])
+
+
+# ---- decode batches (<= 16 tokens): the MXFP4 streaming GEMV ----------------
+
+@pytest.mark.parametrize("dtype", ["bfloat16", "float32"])
+@pytest.mark.parametrize("tokens, slots", [(1, 9), (2, 3), (5, 9), (16, 9), (3, 20)])
+def test_decode_slots_match_oracle(dtype, tokens, slots):
+    """Up to 16 token rows the joined products stream through the MXFP4 GEMV
+    (groups of up to eight slots per expert, split K)."""
+    import torch
+
+    from helpers import torch_dtype
+
+    j, joined = _joined(seed=21 + tokens, h=512, m=256, experts=9)
+    g = torch.Generator(device="cuda")
+    g.manual_seed(100 + tokens)
+    ids = torch.randint(0, 9, (tokens, slots), generator=g, device="cuda", dtype=torch.int32)
+    x, _ = j.tokens(tokens, dtype=torch_dtype(dtype))
+    out = joined.slots(x, ids)
+    torch.cuda.synchronize()
+    assert joined.dispatch_header(tokens, slots)[4] == 0
+    expected = _oracle_slots(j, x, ids.cpu().numpy(), dtype)
+    assert_mxfp4_close(host(out), expected)
+
+
+@pytest.mark.parametrize("tokens", [1, 4, 16])
+def test_decode_finish_and_layer_match_oracle(tokens):
+    import torch
+
+    from mlxlr8_b200.fast_router import router
+    from mlxlr8_b200.joined_mxfp4 import JoinedMoELayer
+
+    j, joined = _joined(seed=40 + tokens, h=256, m=128, experts=257)
+    layer = JoinedMoELayer(j.gate_weight, j.bias, joined)
+    x, residual = j.tokens(tokens)
+    out, ids, scores = layer(x, residual, return_routing=True)
+    torch.cuda.synchronize()
+    assert layer.dispatch_header(tokens)[4] == 0
+    logits, _, _ = router(x, j.gate_weight, j.bias)
+    e_ids, e_scores = ref.route(host(logits), j.bias.cpu().numpy())
+    np.testing.assert_array_equal(ids.cpu().numpy(), e_ids)
+    np.testing.assert_allclose(scores.cpu().numpy(), e_scores, rtol=1e-6, atol=1e-7)
+    values = _oracle_slots(j, x, e_ids)
+    expected = ref.combine(values, e_scores, host(residual), "bfloat16")
+    assert_mxfp4_close(host(out) - host(residual), expected - host(residual))
+    fin = joined.finish(x, ids, scores, residual)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(host(fin), host(out))
+
+
+def test_decode_glm_shape_one_token():
+    """GLM-5 shape (6144 x 2048, 257 experts) at T = 1, the configs[1] decode
+    size on the joined path."""
+    import torch
+
+    from mlxlr8_b200.joined_mxfp4 import JoinedMoELayer
+
+    j, joined = _joined(seed=12, h=6144, m=2048, experts=257)
+    layer = JoinedMoELayer(j.gate_weight, j.bias, joined)
+    x, residual = j.tokens(1)
+    out, ids, scores = layer(x, residual, return_routing=True)
+    torch.cuda.synchronize()
+    assert layer.dispatch_header(1)[4] == 0
+    values = _oracle_slots(j, x, ids.cpu().numpy())
+    expected = ref.combine(values, scores.cpu().numpy(), host(residual), "bfloat16")
+    assert_mxfp4_close(host(out) - host(residual), expected - host(residual))
