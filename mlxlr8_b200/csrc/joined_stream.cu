@@ -52,37 +52,40 @@ static_assert(kJFragRowBytes >= kFragBlockBytes, "a fragment record fits its sta
 
 enum : int { kFirst = 1, kLast = 2, kEnd = 4 };
 
-__device__ __forceinline__ void mma_f16(float c[4], const uint32_t a[4], uint2 b) {
+// One 32-block of one column group: the eight E2M1 codes of rows g (w0) and
+// g + 8 (w1) converted to float16 straight into the A operands of the
+// block's two MMA steps (pairs (k, k + 1) of codes 0-3 for the first, 4-7 for
+// the second), d = A0 * b0 + A1 * b1.  One asm statement, so the converted
+// values need no register moves before the MMAs.
+__device__ __forceinline__ void block_mma(float d[4], uint32_t w0, uint32_t w1, uint2 b0, uint2 b1) {
   asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-      "{%0,%1,%2,%3};\n"
-      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b.x), "r"(b.y));
-}
-
-// Eight E2M1 codes (low nibble first) -> four float16 pairs, exact; pair i
-// holds codes 2i (low half) and 2i + 1.
-__device__ __forceinline__ void e2m1x8_to_half2(uint32_t w, uint32_t h[4]) {
-  asm("{\n"
-      " .reg .b8 b0, b1, b2, b3;\n"
-      " mov.b32 {b0, b1, b2, b3}, %4;\n"
-      " cvt.rn.f16x2.e2m1x2 %0, b0;\n"
-      " cvt.rn.f16x2.e2m1x2 %1, b1;\n"
-      " cvt.rn.f16x2.e2m1x2 %2, b2;\n"
-      " cvt.rn.f16x2.e2m1x2 %3, b3;\n"
+      "{\n"
+      " .reg .b8 p0, p1, p2, p3, q0, q1, q2, q3;\n"
+      " .reg .b32 a0, a1, a2, a3, z;\n"
+      " mov.b32 {p0, p1, p2, p3}, %4;\n"
+      " mov.b32 {q0, q1, q2, q3}, %5;\n"
+      " mov.b32 z, 0;\n"
+      " cvt.rn.f16x2.e2m1x2 a0, p0;\n"
+      " cvt.rn.f16x2.e2m1x2 a1, q0;\n"
+      " cvt.rn.f16x2.e2m1x2 a2, p1;\n"
+      " cvt.rn.f16x2.e2m1x2 a3, q1;\n"
+      " mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {a0,a1,a2,a3}, {%6,%7}, {z,z,z,z};\n"
+      " cvt.rn.f16x2.e2m1x2 a0, p2;\n"
+      " cvt.rn.f16x2.e2m1x2 a1, q2;\n"
+      " cvt.rn.f16x2.e2m1x2 a2, p3;\n"
+      " cvt.rn.f16x2.e2m1x2 a3, q3;\n"
+      " mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {a0,a1,a2,a3}, {%8,%9}, {%0,%1,%2,%3};\n"
       "}\n"
-      : "=r"(h[0]), "=r"(h[1]), "=r"(h[2]), "=r"(h[3])
-      : "r"(w));
+      : "=&f"(d[0]), "=&f"(d[1]), "=&f"(d[2]), "=&f"(d[3])
+      : "r"(w0), "r"(w1), "r"(b0.x), "r"(b0.y), "r"(b1.x), "r"(b1.y));
 }
 
-// First MMA step of a 32-block: C = A * B (no accumulator input).
-__device__ __forceinline__ void mma_f16_first(float c[4], const uint32_t a[4], uint2 b) {
-  const float z = 0.0f;
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-      "{%10,%10,%10,%10};\n"
-      : "=f"(c[0]), "=f"(c[1]), "=f"(c[2]), "=f"(c[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b.x), "r"(b.y), "f"(z));
+// Four 8x16-byte shared-memory matrices; lane l gives the row address of
+// matrix l / 8, row l % 8, and receives word (l % 4) of row (l / 4) of each.
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& d0, uint32_t& d1, uint32_t& d2, uint32_t& d3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(d0), "=r"(d1), "=r"(d2), "=r"(d3)
+               : "r"(addr));
 }
 
 // 2^(s - 127) of the four E8M0 bytes of a scale word: each byte moved to the
@@ -118,8 +121,9 @@ __global__ void __launch_bounds__(kJThreads, 2) joined_stream_kernel(const __gri
   __shared__ int unit_rows[kJStages][kMaxGroupRows + 1];
   __shared__ int plan_cache[4][kJPlanCache];
   // The 128-byte swizzle repeats every 1024 bytes: stages start on 1024.
-  unsigned char* ring = reinterpret_cast<unsigned char*>(
-      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  // (Offsetting the shared array itself keeps the pointer in the shared
+  // window, so the stage reads compile to shared-memory loads.)
+  unsigned char* ring = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int kblocks = p.in_features / 128, nblocks = p.out_features / 128;
   pdl_launch_dependents();
@@ -227,10 +231,17 @@ __global__ void __launch_bounds__(kJThreads, 2) joined_stream_kernel(const __gri
   // ---------------- consumers ----------------
   const int gid = lane >> 2, tig = lane & 3;
   const int r0 = warp * 16 + gid, r1 = r0 + 8;  // rows of the 128-row block
-  // Swizzled byte offsets of this lane's code word in 32-block c of the
-  // stage's 256 inputs: 16-byte chunk c of row r sits at chunk c ^ (r & 7).
-  const int row0_off = r0 * kJRowBytes + tig * 4, row1_off = r1 * kJRowBytes + tig * 4;
-  const int sw = gid & 7;  // r0 & 7 == r1 & 7 == gid
+  // Code words come in by ldmatrix: for each pair of 32-blocks (c, c + 1) of
+  // the stage's 256 inputs, matrices 0-3 are (rows 0-7, c), (rows 8-15, c),
+  // (rows 0-7, c + 1), (rows 8-15, c + 1) of the warp's 16 rows, so lane
+  // (g, tig) receives word tig of rows g and g + 8 of both blocks.  Lane l
+  // addresses row (l % 8) + 8 ((l / 8) % 2) of block c + l / 16; 16-byte
+  // chunk c of row r sits at chunk c ^ (r & 7) (128-byte swizzle).
+  const int lrow = warp * 16 + (lane & 7) + 8 * ((lane >> 3) & 1);
+  uint32_t code_off[2 * kJBlocks];  // [q * 2 + pair]
+#pragma unroll
+  for (int cp = 0; cp < 2 * kJBlocks; ++cp)
+    code_off[cp] = static_cast<uint32_t>(lrow * kJRowBytes + (((2 * cp + (lane >> 4)) ^ (lane & 7)) << 4));
   const int sc0_off = kJCodeBytes + (r0 & 31) * 16 + (r0 >> 5) * 4;
   const int sc1_off = kJCodeBytes + (r1 & 31) * 16 + (r1 >> 5) * 4;
   int stage = 0;
@@ -273,12 +284,9 @@ __global__ void __launch_bounds__(kJThreads, 2) joined_stream_kernel(const __gri
     for (int q = 0; q < kJBlocks; ++q) {
       if (q < m.z) {
       uint32_t w0[4], w1[4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int chunk = ((q * 4 + j) ^ sw) << 4;
-        w0[j] = *reinterpret_cast<const uint32_t*>(base + row0_off + chunk);
-        w1[j] = *reinterpret_cast<const uint32_t*>(base + row1_off + chunk);
-      }
+      const uint32_t sbase = smem_u32(base);
+      ldsm_x4(sbase + code_off[q * 2], w0[0], w1[0], w0[1], w1[1]);
+      ldsm_x4(sbase + code_off[q * 2 + 1], w0[2], w1[2], w0[3], w1[3]);
       float fs0[4], fs1[4];
       e8m0x4(*reinterpret_cast<const uint32_t*>(base + sc0_off + q * 512), fs0);
       e8m0x4(*reinterpret_cast<const uint32_t*>(base + sc1_off + q * 512), fs1);
@@ -291,24 +299,16 @@ __global__ void __launch_bounds__(kJThreads, 2) joined_stream_kernel(const __gri
         for (int i = 0; i < 4; ++i) st[c][i] = 0.0f;
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        uint32_t h0[4], h1[4];
-        e2m1x8_to_half2(w0[j], h0);
-        e2m1x8_to_half2(w1[j], h1);
-        // A fragments of the block's two MMA steps: rows g / g + 8, pairs
-        // (k 8tig + 4h .. +1) and (8tig + 4h + 2 .. +3).
-        const uint32_t a_lo[4] = {h0[0], h1[0], h0[1], h1[1]};
-        const uint32_t a_hi[4] = {h0[2], h1[2], h0[3], h1[3]};
+        // Rows g / g + 8; A pairs (k 8tig + 4h .. +1) and (8tig + 4h + 2 .. +3).
         float blk[4];
-        mma_f16_first(blk, a_lo, f0[(2 * j) * 8]);
-        mma_f16(blk, a_hi, f0[(2 * j + 1) * 8]);
+        block_mma(blk, w0[j], w1[j], f0[(2 * j) * 8], f0[(2 * j + 1) * 8]);
         st[0][0] = fmaf(blk[0], fs0[j], st[0][0]);
         st[0][1] = fmaf(blk[1], fs0[j], st[0][1]);
         st[0][2] = fmaf(blk[2], fs1[j], st[0][2]);
         st[0][3] = fmaf(blk[3], fs1[j], st[0][3]);
         if (ncg > 1) {
           float blk1[4];
-          mma_f16_first(blk1, a_lo, f1[(2 * j) * 8]);
-          mma_f16(blk1, a_hi, f1[(2 * j + 1) * 8]);
+          block_mma(blk1, w0[j], w1[j], f1[(2 * j) * 8], f1[(2 * j + 1) * 8]);
           st[1][0] = fmaf(blk1[0], fs0[j], st[1][0]);
           st[1][1] = fmaf(blk1[1], fs0[j], st[1][1]);
           st[1][2] = fmaf(blk1[2], fs1[j], st[1][2]);
