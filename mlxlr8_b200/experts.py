@@ -13,6 +13,9 @@ checkpoint directory (``manifests/exlr8-manifest-up1.json``,
   With ``optimize`` a K4 layer of GLM-5 size is re-encoded to joined MXFP4 on
   the GPU (experts.py:134-148) and its trellis codes and gate/up in-scales
   are released.
+* ``store.shard(n, rank, world)`` reads one rank's contiguous block of routed
+  experts plus the shared expert (expert parallelism; ``store.ep_layer``
+  builds the sharded MoE layer).
 * Without ``resident``, ``store._get(layer, expert)`` reads one expert's
   three matrices into a byte-bounded LRU cache on the device
   (experts.py:40-64), and the layer gathers the selected experts per call
@@ -90,6 +93,25 @@ class ExpertStore:
             self.cache_bytes += size
         return arrays
 
+    def shard(self, number, rank, world, routed=256):
+        """(routed shard, shared expert) of layer ``number`` for expert
+        parallelism over ``world`` ranks: this rank's contiguous block of
+        routed / world experts and the shared expert (matrix 256), read from
+        the checkpoint by their byte ranges only, so a rank holds 1 / world
+        of the routed codes."""
+        return _load_shard(self, number, rank, world, routed)
+
+    def ep_layer(self, number, rank, world, group=None, routed=256):
+        """The MoE branch of layer ``number`` sharded over ``world`` ranks
+        (``ep.ExpertParallelMoE``, NCCL exchange, the trellis shared expert
+        replicated on every rank)."""
+        from .ep import ExpertParallelMoE
+
+        gate_weight, bias = self.router(number)
+        local, shared = self.shard(number, rank, world, routed)
+        return ExpertParallelMoE(gate_weight, bias, local, rank, world, group=group, shared_layer=shared,
+                                 routed=routed, exchange="nccl")
+
     def router(self, number):
         """(gate weight float32 [256, hidden], bias float32 [256]) of layer
         ``number`` from ``dense/exlr8-dense-NNN.safetensors`` (model.py:361-371)."""
@@ -161,8 +183,9 @@ def _layer_scales(index, k, device):
     return scales
 
 
-def _load_layer(store, number):
-    """``ExpertLayer(store, number)`` of experts.py:77-148."""
+def _layer_files(store, number):
+    """(k, weights file, index file, hidden, intermediate) of layer ``number``
+    after the manifest's uniform-K check (experts.py:80-94)."""
     from .weights import SafeTensorFile
 
     plan = store.manifest["layers"][str(number)]
@@ -179,6 +202,37 @@ def _load_layer(store, number):
     index = SafeTensorFile(directory / f"exlr8-layer-{number:03d}.index.safetensors")
     hidden = index.header["signs.in"]["shape"][0]
     intermediate = index.header[f"k{k}.gate.svh"]["shape"][-1]
+    return k, weights, index, hidden, intermediate
+
+
+def _load_shard(store, number, rank, world, routed):
+    """Routed experts [rank * routed / world, (rank + 1) * routed / world) and
+    the shared expert of layer ``number`` as two resident layers, reading only
+    those experts' byte ranges of the weights file."""
+    if routed % world or not 0 <= rank < world:
+        raise ValueError("routed experts must divide evenly over the ranks")
+    k, weights, index, hidden, intermediate = _layer_files(store, number)
+    scales = _layer_scales(index, k, store.device)
+    per = routed // world
+    lo, hi = rank * per, (rank + 1) * per
+    nbytes = hidden * intermediate * k // 8
+    local, shared = {}, {}
+    for projection in ("gate", "up", "down"):
+        buf = torch.empty(per * nbytes, dtype=torch.uint8, device=store.device)
+        weights.read_into("trellis." + projection, buf, lo * nbytes, per * nbytes)
+        local[projection] = buf
+        one = torch.empty(nbytes, dtype=torch.uint8, device=store.device)
+        weights.read_into("shared.trellis." + projection, one)
+        shared[projection] = one
+    local_scales = {p: tuple(v[lo:hi].contiguous() for v in pair) for p, pair in scales.items()}
+    shared_scales = {p: tuple(v[-1:].contiguous() for v in pair) for p, pair in scales.items()}
+    return (ExpertLayer(local, local_scales, k, hidden, intermediate, number=number),
+            ExpertLayer(shared, shared_scales, k, hidden, intermediate, number=number))
+
+
+def _load_layer(store, number):
+    """``ExpertLayer(store, number)`` of experts.py:77-148."""
+    k, weights, index, hidden, intermediate = _layer_files(store, number)
     scales = _layer_scales(index, k, store.device)
     packed = None
     if store.resident:

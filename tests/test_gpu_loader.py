@@ -173,3 +173,28 @@ def test_glm5_layer_reencodes_to_joined_mxfp4(tmp_path):
     assert isinstance(moe, JoinedMoELayer)
     gate_weight, bias = store.router(3)
     assert gate_weight.dtype == torch.float32 and tuple(gate_weight.shape) == (256, h)
+
+
+def test_expert_parallel_layer_from_checkpoint_shards(tmp_path):
+    """ExpertStore.ep_layer at one rank (the whole routed set as its shard, the
+    trellis shared expert replicated) against the resident single-device
+    layer built from the same checkpoint."""
+    import torch
+
+    from helpers import assert_bf16_close
+    from mlxlr8_b200.experts import ExpertStore
+    from mlxlr8_b200.synthetic import write_checkpoint
+
+    write_checkpoint(tmp_path, layers=(3,), hidden=256, intermediate=128, routed=256, seed=8)
+    store = ExpertStore(tmp_path, resident=True, optimize=False)
+    single = store.moe_layer(3)
+    ep = store.ep_layer(3, 0, 1)
+    g = torch.Generator(device="cuda")
+    g.manual_seed(3)
+    x = torch.randn(4, 256, generator=g, device="cuda").to(torch.bfloat16)
+    r = torch.randn(4, 256, generator=g, device="cuda").to(torch.bfloat16)
+    out, ids, _ = single(x, r, return_routing=True)
+    out_ep, ids_ep, _ = ep(x, r, return_routing=True)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(ids.cpu().numpy(), ids_ep.cpu().numpy())
+    assert_bf16_close(host(out_ep) - host(r), host(out) - host(r))

@@ -126,3 +126,25 @@ def test_synthetic_checkpoint_layers_and_router(tmp_path):
     weight, _ = load_router(tmp_path / "f32", 5, "cpu")
     np.testing.assert_array_equal(
         weight.numpy(), SafeTensorFile(tmp_path / "f32" / "dense" / "exlr8-dense-005.safetensors").raw("mlp.gate.fp32"))
+
+
+def test_shard_reads_only_the_rank_experts(reference_checkpoint):
+    """Expert-parallel shards: rank r of 4 holds experts [64 r, 64 r + 64)
+    and the shared expert, with the matching signed side vectors."""
+    path, raw, _ = reference_checkpoint
+    store = ExpertStore(path, device="cpu")
+    full = store.layer(3)
+    for rank in (0, 3):
+        local, shared = store.shard(3, rank, 4)
+        assert local.experts == 64 and shared.experts == 1
+        lo = 64 * rank
+        for projection in ("gate", "up", "down"):
+            np.testing.assert_array_equal(local.packed[projection].numpy(),
+                                          raw["trellis." + projection][lo * 8192:(lo + 64) * 8192])
+            np.testing.assert_array_equal(shared.packed[projection].numpy(), raw["shared.trellis." + projection])
+            for a, b in zip(local.scales[projection], full.scales[projection]):
+                np.testing.assert_array_equal(a.numpy(), b[lo:lo + 64].numpy())
+            for a, b in zip(shared.scales[projection], full.scales[projection]):
+                np.testing.assert_array_equal(a.numpy(), b[256:257].numpy())
+    with pytest.raises(ValueError, match="divide evenly"):
+        store.shard(3, 0, 3)
