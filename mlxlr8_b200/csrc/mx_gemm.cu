@@ -228,7 +228,10 @@ __global__ void __launch_bounds__(GemmTraits<kK>::kThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   __shared__ GemmShared<kStages, kCodeStages> sh;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // Offsetting the shared array itself (not an integer round trip) keeps the
+  // pointer in the shared window: the stage accesses compile to shared loads
+  // and stores.
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint8_t* code_ring = smem + kStages * T::kStageBytes;
   uint8_t* unit_scales = code_ring + kCodeStages * T::kCodeStageBytes;  // trellis: 512 bytes of E8M0 1.0
   int32_t* header = g.chunks.header;

@@ -51,7 +51,10 @@ __global__ void __launch_bounds__(kRgThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   __shared__ RgShared sh;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // Offsetting the shared array itself (not an integer round trip) keeps the
+  // pointer in the shared window: the stage accesses compile to shared loads
+  // and stores.
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   const int m0 = blockIdx.x * 128, n0 = blockIdx.y * 128, split = blockIdx.z;
   const int kt0 = split * ktiles_per_split;
   const int ktiles = min(ktiles_per_split, hidden / kRgKTile - kt0);

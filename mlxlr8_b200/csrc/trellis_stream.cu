@@ -283,8 +283,9 @@ __global__ void __launch_bounds__(kStreamThreads, 2) trellis_stream_kernel(Strea
     const unsigned char* base = smem + stage * G::kStageBytes;
     const uint32_t* codes = reinterpret_cast<const uint32_t*>(base);
     const uint2* frag = reinterpret_cast<const uint2*>(base + G::kCodeBytes);
-    // Every stage holds one 128-wide K block (kStageTiles K tiles).
-    const bool has0 = r0 < nr, has1 = 4 + r0 < nr;
+    // Every stage holds one 128-wide K block (kStageTiles K tiles).  Record
+    // rows past the unit's rows hold stale bytes: they only feed the
+    // accumulator columns of absent slots, which are reset and never stored.
     const uint2* f0 = frag + (r0 * kFragRowBytes) / 8 + fpos;
     const uint2* f1 = frag + ((4 + r0) * kFragRowBytes) / 8 + fpos;
     float st[2][4];
@@ -305,15 +306,15 @@ __global__ void __launch_bounds__(kStreamThreads, 2) trellis_stream_kernel(Strea
         for (int kk = 0; kk < kStageTiles; ++kk) {
           uint32_t a[4];
           k4_fragment(word[kk], prior[kk], unit16, mcg_mask, mcg_xor, a);
-          mma_f16(st[0], a, has0 ? f0[kk * 8] : make_uint2(0u, 0u));
-          mma_f16(st[1], a, has1 ? f1[kk * 8] : make_uint2(0u, 0u));
+          mma_f16(st[0], a, f0[kk * 8]);
+          mma_f16(st[1], a, f1[kk * 8]);
         }
       } else {
 #pragma unroll
         for (int kk = 0; kk < kStageTiles; ++kk) {
           uint32_t a[4];
           k4_fragment(word[kk], prior[kk], unit16, mcg_mask, mcg_xor, a);
-          mma_f16(st[0], a, has0 ? f0[kk * 8] : make_uint2(0u, 0u));
+          mma_f16(st[0], a, f0[kk * 8]);
         }
       }
     } else {
@@ -322,8 +323,8 @@ __global__ void __launch_bounds__(kStreamThreads, 2) trellis_stream_kernel(Strea
         uint32_t cw[8], a[4];
         generic_codewords(codes + (kk * 8 + warp) * G::kTileWords, K, geo, cw);
         tile_fragment(cw, a);
-        mma_f16(st[0], a, has0 ? f0[kk * 8] : make_uint2(0u, 0u));
-        if (ncg > 1) mma_f16(st[1], a, has1 ? f1[kk * 8] : make_uint2(0u, 0u));
+        mma_f16(st[0], a, f0[kk * 8]);
+        if (ncg > 1) mma_f16(st[1], a, f1[kk * 8]);
       }
     }
     // This lane's accumulator columns belong to unit rows tig and 4 + tig;
