@@ -225,10 +225,11 @@ def measured_peaks():
     return 6650.0, "fallback"
 
 
-def cpu_baseline(layer, tokens, seconds, rank0=True):
-    """Time the C restatement of the layer on host copies of one layer."""
-    import numpy as np
-
+def cpu_baseline(layer, tokens, seconds, warmup=1, steps=None):
+    """Time the C restatement of the layer on host copies of one layer:
+    ``warmup`` untimed calls (at least one, which sizes the sample), then
+    ``steps`` timed calls, at most as many as fit in ``seconds`` (at least
+    two).  Returns (timed steps, seconds, warm-up calls, threads)."""
     from mlxlr8_b200.synthetic import host_copy
     from oracle import c_oracle, trellis_oracle as ref
 
@@ -237,15 +238,18 @@ def cpu_baseline(layer, tokens, seconds, rank0=True):
     shared = tuple(ref.bf16_bits(s) for s in hc["shared"])
     xs, rs = x.float().cpu().numpy(), residual.float().cpu().numpy()
     args = (xs, rs, hc["gate_weight"], hc["bias"], hc["packed"], hc["scales"], K_BITS, HIDDEN, INTER, shared)
-    t0 = time.perf_counter()
-    c_oracle.moe_layer(*args)
-    first = time.perf_counter() - t0
-    steps = max(2, int(seconds / max(first, 1e-3)))
+    warmup = max(1, warmup)
+    for _ in range(warmup):
+        t0 = time.perf_counter()
+        c_oracle.moe_layer(*args)
+        last = time.perf_counter() - t0
+    fit = max(2, int(seconds / max(last, 1e-3)))
+    steps = fit if steps is None else max(2, min(steps, fit))
     t0 = time.perf_counter()
     for _ in range(steps):
         c_oracle.moe_layer(*args)
     dt = time.perf_counter() - t0
-    return steps, dt, c_oracle.threads()
+    return steps, dt, warmup, c_oracle.threads()
 
 
 def reference_arm(args, world, rank):
@@ -260,19 +264,18 @@ def reference_arm(args, world, rank):
     device = "cuda" if torch.cuda.is_available() else "cpu"
     layer = make_layer(seed=1000, device=device)
     budget = 60.0
-    steps_done, dt, cores = cpu_baseline(layer, args.tokens, budget)
-    # Warm-up is the first call inside cpu_baseline; steps_done full layer steps timed.
+    steps_done, dt, warm, cores = cpu_baseline(layer, args.tokens, budget, args.warmup, args.steps)
     value = steps_done * args.tokens / dt
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
-        "steps": steps_done, "warmup": 1, "ms_per_step": 1000 * dt / steps_done, "higher_is_better": True,
+        "steps": steps_done, "warmup": warm, "ms_per_step": 1000 * dt / steps_done, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
         "config": {"workload": f"decode T={args.tokens}, one GLM-5-shape MoE layer (256 K4 trellis experts + bf16 "
                                "shared expert)", "tokens": args.tokens, "hidden": HIDDEN, "intermediate": INTER,
                    "experts": EXPERTS, "k_bits": K_BITS},
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
-                         "sample": f"{steps_done} full layer steps of T={args.tokens} (about {budget:.0f} s budget; "
-                                   f"--steps {args.steps} requested)"},
+                         "sample": f"{steps_done} full layer steps of T={args.tokens} after {warm} warm-up steps "
+                                   f"(--steps {args.steps} requested, capped at about {budget:.0f} s)"},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": "exlr8's expert operators are Metal compute kernels (no CPU backend); this arm is the C restatement "
                 "of their arithmetic (oracle/c), timed on the host cores",
@@ -738,7 +741,7 @@ def main():
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        steps_done, dt, cores = cpu_baseline(layers[0], T, args.cpu_seconds)
+        steps_done, dt, _, cores = cpu_baseline(layers[0], T, args.cpu_seconds)
         cpu = {"value": steps_done * T / dt, "unit": "tokens/s", "cores": cores, "kind": "port",
                "sample": f"{steps_done} full layer steps of T={T} on host copies of one layer"}
 

@@ -21,7 +21,7 @@ namespace exlr8 {
 // 32-bit code word (eight E2M1 values, k = 32j + 8 tig .. + 7) of a weight
 // row feeds both steps of its block.
 struct JoinedStreamParams {
-  CUtensorMap codes;         // uint8 [experts * out_features][in_features / 2]: box 64 x 128, 64-byte swizzle
+  CUtensorMap codes;         // uint8 [experts * out_features][in_features / 2]: box 128 B x 128 rows, 128-byte swizzle
   const uint8_t* scales;     // E8M0 of the same rows in the 512-byte block layout (mx_scale_offset)
   const unsigned char* frag; // [nslots][in_features / 128] activation records, MXFP4 K order
   float* partial;            // [out_features / plane_rows][nslots][splits][plane_rows]
