@@ -291,6 +291,7 @@ def time_calls(fn, steps, warmup, stream):
     """Milliseconds per call of fn() on `stream` (CUDA events, after warm-up)."""
     import torch
 
+    stream.wait_stream(torch.cuda.current_stream())
     with torch.cuda.stream(stream):
         for _ in range(warmup):
             fn()
@@ -382,7 +383,7 @@ def joined_decode_configs(steps, stream):
         res[f"joined_T{T}"] = {"tokens_per_s": T / (ms / 1000.0), "ms_per_layer": ms,
                                "experts_touched_mean": statistics.mean(uniq), "weight_gb_per_s": gbs,
                                "frac_of_hbm": gbs / peak, "peak_kind": peak_kind,
-                               "path": "router_plan -> prep -> MXFP4 stream (gate/up) -> gate finish -> "
+                               "path": "gate logits -> route + plan -> prep -> MXFP4 stream (gate/up) -> gate finish -> "
                                        "MXFP4 stream (down) -> fused finish"}
         del graphs
     del layers
@@ -524,6 +525,7 @@ def stack_configs(layers, steps, stream):
                 for i, l in enumerate(blocks)]
         stack = MoEStack(list(zip(norms, moes)))
         h = (torch.randn(tokens, HIDDEN, generator=g, device="cuda")).to(torch.bfloat16)
+        stream.wait_stream(torch.cuda.current_stream())  # weights and h come from the default stream
         with torch.cuda.stream(stream):
             for _ in range(2):
                 stack(h)  # eager warm-up: workspaces, kernel attributes

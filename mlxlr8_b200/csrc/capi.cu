@@ -703,7 +703,7 @@ int exlr8_expert_mlp_finish(const void* x, int x_dtype, const uint32_t* indices,
 
 size_t exlr8_moe_layer_workspace(int64_t tokens, int hidden, int intermediate, int64_t experts) {
   size_t router = align_up(tokens * 256 * sizeof(float)) + align_up(tokens * 9 * sizeof(uint32_t)) +
-                  align_up(tokens * 8 * sizeof(float)) + align_up(sizeof(int));
+                  align_up(tokens * 8 * sizeof(float));
   if (tokens >= kRouterGemmMinTokens)
     router += align_up(router_gemm_workspace(static_cast<int>(tokens), hidden, EXLR8_DTYPE_F32));
   return exlr8_expert_mlp_finish_workspace(tokens, hidden, intermediate, experts) + router;
@@ -736,7 +736,6 @@ int exlr8_moe_layer(const void* x, int x_dtype, const void* residual, int64_t to
   float* logits = head.take<float>(tokens * 256 * sizeof(float));
   uint32_t* ids_buf = head.take<uint32_t>(tokens * 9 * sizeof(uint32_t));
   float* scores_buf = head.take<float>(tokens * 8 * sizeof(float));
-  int* done = head.take<int>(sizeof(int));
   uint32_t* ids = indices ? indices : ids_buf;
   float* sc = scores ? scores : scores_buf;
   if (use_prefill(tokens, ex)) {
@@ -753,8 +752,10 @@ int exlr8_moe_layer(const void* x, int x_dtype, const void* residual, int64_t to
     return prefill_finish(x, x_dtype, ids, sc, residual, tokens, ex, experts, shared, out, workspace, s);
   }
   EXLR8_TIMED(EXLR8_KERNEL_ROUTER, s,
-              launch_router_plan(x, x_dtype, static_cast<int>(tokens), ex->hidden, gate_weight, logits, bias, ids, sc,
-                                 done, static_cast<int>(experts), shared ? 8 : -1, b.plan, s));
+              launch_gate_logits(x, x_dtype, static_cast<int>(tokens), ex->hidden, gate_weight, logits, 256, s));
+  EXLR8_TIMED(EXLR8_KERNEL_PLAN, s,
+              launch_route_plan(logits, bias, static_cast<int>(tokens), ids, sc, static_cast<int>(experts),
+                                shared ? 8 : -1, b.plan, s));
   return mlp_finish_after_plan(x, x_dtype, ids, sc, residual, tokens, ex, experts, shared, out, l, b, s);
 }
 

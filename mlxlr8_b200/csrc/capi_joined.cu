@@ -341,14 +341,12 @@ struct RouterBuffers {
   float* logits;
   uint32_t* ids;
   float* scores;
-  int* done;
   void* gemm;
 };
 
 size_t router_buffers_bytes(int64_t tokens, int hidden) {
   return align_up(tokens * 256 * sizeof(float)) + align_up(tokens * 9 * sizeof(uint32_t)) +
-         align_up(tokens * 8 * sizeof(float)) + align_up(sizeof(int)) +
-         align_up(router_gemm_workspace(static_cast<int>(tokens), hidden, EXLR8_DTYPE_F32));
+         align_up(tokens * 8 * sizeof(float)) + align_up(router_gemm_workspace(static_cast<int>(tokens), hidden, EXLR8_DTYPE_F32));
 }
 
 RouterBuffers carve_router(int64_t tokens, int hidden, Carver& c) {
@@ -356,7 +354,6 @@ RouterBuffers carve_router(int64_t tokens, int hidden, Carver& c) {
   r.logits = c.take<float>(tokens * 256 * sizeof(float));
   r.ids = c.take<uint32_t>(tokens * 9 * sizeof(uint32_t));
   r.scores = c.take<float>(tokens * 8 * sizeof(float));
-  r.done = c.take<int>(sizeof(int));
   r.gemm = c.take<char>(router_gemm_workspace(static_cast<int>(tokens), hidden, EXLR8_DTYPE_F32));
   return r;
 }
@@ -382,7 +379,7 @@ int exlr8_joined_moe_layer(const void* x, int x_dtype, const void* residual, int
     return EXLR8_ERR_WORKSPACE;
   cudaStream_t s = as_stream(stream);
   if (use_joined_stream(tokens)) {
-    // Router, top-8 and the plan in one kernel, then the decode chain.
+    // Gate product, then top-8 and the plan, then the decode chain.
     const int64_t rows = tokens * 9;
     const JoinedDecodeLayout dl = joined_decode_layout(rows, w->hidden, w->intermediate, w->experts);
     Carver dc(workspace);
@@ -391,8 +388,10 @@ int exlr8_joined_moe_layer(const void* x, int x_dtype, const void* residual, int
     uint32_t* ids = indices ? indices : rb.ids;
     float* sc = scores ? scores : rb.scores;
     EXLR8_TIMED(EXLR8_KERNEL_ROUTER, s,
-                launch_router_plan(x, x_dtype, static_cast<int>(tokens), w->hidden, gate_weight, rb.logits, bias, ids,
-                                   sc, rb.done, static_cast<int>(w->experts), -1, db.plan, s));
+                launch_gate_logits(x, x_dtype, static_cast<int>(tokens), w->hidden, gate_weight, rb.logits, 256, s));
+    EXLR8_TIMED(EXLR8_KERNEL_PLAN, s,
+                launch_route_plan(rb.logits, bias, static_cast<int>(tokens), ids, sc, static_cast<int>(w->experts), -1,
+                                  db.plan, s));
     EXLR8_CHECK(joined_decode_products(x, x_dtype, 0, 9, ids, rows, w, dl, db, s));
     EXLR8_TIMED(EXLR8_KERNEL_FINISH, s,
                 launch_finish_fused(db.dpart, dl.s2.count, nullptr, ids, static_cast<int>(tokens), w->down_out,

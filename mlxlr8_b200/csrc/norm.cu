@@ -3,9 +3,12 @@
 //   h   = T(x + residual)
 //   out = T(w * T(h * rsqrt(sum(h * h) / hidden + eps)))
 // T() rounds to the activation type; the sum of squares is float32 (plain
-// multiply and add, no contraction), reduced over the CTA.
+// multiply and add, no contraction), reduced over the CTA.  Launched with
+// programmatic dependent launch: in a block stack the next block's gate
+// kernel becomes resident (and prefetches its weights) while this one runs.
 
 #include "common.cuh"
+#include "launch.cuh"
 
 namespace exlr8 {
 
@@ -19,8 +22,10 @@ __global__ void __launch_bounds__(kNormThreads) residual_rms_kernel(const void* 
                                                                     const void* __restrict__ w, int hidden,
                                                                     float eps, void* __restrict__ h_out,
                                                                     void* __restrict__ out) {
+  pdl_launch_dependents();
   __shared__ float red[kNormThreads / 32];
   __shared__ float s_inv;
+  pdl_wait();
   const int64_t base = static_cast<int64_t>(blockIdx.x) * hidden;
   float acc = 0.0f;
   for (int i = threadIdx.x; i < hidden; i += kNormThreads) {
@@ -55,12 +60,13 @@ cudaError_t launch_residual_rms(const void* x, const void* residual, const void*
   if (rows == 0) return cudaSuccess;
   const dim3 grid(static_cast<unsigned>(rows));
   if (act_dtype == kF32)
-    residual_rms_kernel<kF32><<<grid, kNormThreads, 0, s>>>(x, residual, w, hidden, eps, h_out, out);
-  else if (act_dtype == kF16)
-    residual_rms_kernel<kF16><<<grid, kNormThreads, 0, s>>>(x, residual, w, hidden, eps, h_out, out);
-  else
-    residual_rms_kernel<kBF16><<<grid, kNormThreads, 0, s>>>(x, residual, w, hidden, eps, h_out, out);
-  return cudaGetLastError();
+    return launch_pdl(residual_rms_kernel<kF32>, grid, dim3(kNormThreads), 0, s, x, residual, w, hidden, eps, h_out,
+                      out);
+  if (act_dtype == kF16)
+    return launch_pdl(residual_rms_kernel<kF16>, grid, dim3(kNormThreads), 0, s, x, residual, w, hidden, eps, h_out,
+                      out);
+  return launch_pdl(residual_rms_kernel<kBF16>, grid, dim3(kNormThreads), 0, s, x, residual, w, hidden, eps, h_out,
+                    out);
 }
 
 }  // namespace exlr8

@@ -2,8 +2,6 @@
 // selection with renormalisation (exlr8 fast_router.metal:1-42,
 // model.py:111-132).
 
-#include <cuda/atomic>
-
 #include "common.cuh"
 #include "router.cuh"
 #include "plan.cuh"
@@ -31,10 +29,14 @@ __device__ __forceinline__ float4 load_act4(const void* base, int dtype, int64_t
 
 // One CTA per expert row of Wg; the 8 warps split the hidden dimension; each
 // warp keeps partial dot products for up to kGateTokens tokens at a time.
+// In the decode chain this kernel is the chain head: a plain launch, fully
+// ordered after earlier work in the stream (later kernels of the chain rely
+// on it); it lets the routing kernel launch early.
 __global__ void __launch_bounds__(kGateWarps * 32) gate_logits_kernel(const void* __restrict__ x, int x_dtype,
                                                                       int tokens, int hidden,
                                                                       const float* __restrict__ wg,
                                                                       float* __restrict__ logits, int experts) {
+  pdl_launch_dependents();  // the routing kernel may launch and wait for this grid
   __shared__ float red[kGateWarps][kGateTokens];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int e = blockIdx.x;
@@ -90,6 +92,8 @@ __global__ void __launch_bounds__(kGateWarps * 32) gate_logits_kernel(const void
 
 cudaError_t launch_gate_logits(const void* x, int x_dtype, int tokens, int hidden, const float* wg, float* logits,
                                int experts, cudaStream_t s) {
+  static const cudaError_t carve = prefer_shared_carveout(gate_logits_kernel);
+  if (carve != cudaSuccess) return carve;
   gate_logits_kernel<<<experts, kGateWarps * 32, 0, s>>>(x, x_dtype, tokens, hidden, wg, logits, experts);
   return cudaGetLastError();
 }
@@ -169,76 +173,17 @@ __global__ void __launch_bounds__(128) route_kernel(const float* __restrict__ lo
              scores + static_cast<int64_t>(row) * 8, scale, shared_id, lane);
 }
 
-// Gate GEMV (one CTA per expert row, as gate_logits_kernel) whose last CTA to
-// finish routes every token and builds the dispatch plan of the 9*tokens
-// slots.  `done` must be zero at launch.
-__global__ void __launch_bounds__(kGateWarps * 32) router_plan_kernel(
-    const void* __restrict__ x, int x_dtype, int tokens, int hidden, const float* __restrict__ wg,
-    float* __restrict__ logits, const float* __restrict__ bias, uint32_t* __restrict__ ids,
-    float* __restrict__ scores, int* __restrict__ done, int plan_experts, int skip_slot, PlanView plan) {
+// Routing and dispatch plan of the decode chain: one CTA, launched with
+// programmatic dependent launch after gate_logits_kernel; it waits for the
+// gate grid, routes every token (one warp per token) and builds the plan of
+// the 9 * tokens slots in place of a separate plan kernel.
+__global__ void __launch_bounds__(kGateWarps * 32) route_plan_kernel(
+    const float* __restrict__ logits, const float* __restrict__ bias, int tokens, uint32_t* __restrict__ ids,
+    float* __restrict__ scores, int plan_experts, int skip_slot, PlanView plan) {
   pdl_launch_dependents();  // the prep kernel may launch and wait for this grid
   extern __shared__ int sm[];
-  __shared__ float red[kGateWarps][kGateTokens];
-  __shared__ int s_last;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int e = blockIdx.x;
-  const float* w = wg + static_cast<int64_t>(e) * hidden;
-  const int per_warp = (hidden / 4 + kGateWarps - 1) / kGateWarps;
-  const int g0 = warp * per_warp;
-  const int g1 = min(g0 + per_warp, hidden / 4);
-  for (int t0 = 0; t0 < tokens; t0 += kGateTokens) {
-    float acc[kGateTokens];
-#pragma unroll
-    for (int t = 0; t < kGateTokens; ++t) acc[t] = 0.f;
-    // All of a lane's weight loads of a chunk are issued before any use.
-    for (int gc = g0 + lane; gc < g1; gc += 32 * kGateChunk) {
-      float4 wv[kGateChunk];
-#pragma unroll
-      for (int i = 0; i < kGateChunk; ++i)
-        wv[i] = gc + 32 * i < g1 ? reinterpret_cast<const float4*>(w)[gc + 32 * i] : make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-      for (int t = 0; t < kGateTokens; ++t) {
-        if (t0 + t < tokens) {
-#pragma unroll
-          for (int i = 0; i < kGateChunk; ++i) {
-            if (gc + 32 * i < g1) {
-              const float4 xv = load_act4(x, x_dtype, static_cast<int64_t>(t0 + t) * hidden + 4 * (gc + 32 * i));
-              acc[t] = fmaf(xv.x, wv[i].x, acc[t]);
-              acc[t] = fmaf(xv.y, wv[i].y, acc[t]);
-              acc[t] = fmaf(xv.z, wv[i].z, acc[t]);
-              acc[t] = fmaf(xv.w, wv[i].w, acc[t]);
-            }
-          }
-        }
-      }
-    }
-#pragma unroll
-    for (int t = 0; t < kGateTokens; ++t) {
-#pragma unroll
-      for (int off = 16; off > 0; off >>= 1) acc[t] += __shfl_xor_sync(0xffffffffu, acc[t], off);
-    }
-    if (lane == 0) {
-#pragma unroll
-      for (int t = 0; t < kGateTokens; ++t) red[warp][t] = acc[t];
-    }
-    __syncthreads();
-    if (threadIdx.x < kGateTokens && t0 + static_cast<int>(threadIdx.x) < tokens) {
-      float s = 0.f;
-#pragma unroll
-      for (int w2 = 0; w2 < kGateWarps; ++w2) s += red[w2][threadIdx.x];
-      logits[static_cast<int64_t>(t0 + threadIdx.x) * 256 + e] = s;
-    }
-    __syncthreads();
-  }
-  // The barrier orders this CTA's logit stores before thread 0's
-  // acquire-release arrival; the last CTA's arrival acquires every other
-  // CTA's stores, and its barrier passes them on to its threads.
-  if (threadIdx.x == 0) {
-    cuda::atomic_ref<int, cuda::thread_scope_device> arrivals(*done);
-    s_last = arrivals.fetch_add(1, cuda::memory_order_acq_rel) == static_cast<int>(gridDim.x) - 1;
-  }
-  __syncthreads();
-  if (!s_last) return;
+  pdl_wait();
   const int rows = tokens * 9;
   if (rows <= kSmallPlanRows) {
     // Decode batches: the ids stay in shared memory for the plan.
@@ -257,23 +202,19 @@ __global__ void __launch_bounds__(kGateWarps * 32) router_plan_kernel(
   plan_body(ids, rows, plan_experts, 9, skip_slot, plan, sm);
 }
 
-cudaError_t launch_router_plan(const void* x, int x_dtype, int tokens, int hidden, const float* wg, float* logits,
-                               const float* bias, uint32_t* ids, float* scores, int* done, int plan_experts,
-                               int skip_slot, PlanView plan, cudaStream_t s) {
+cudaError_t launch_route_plan(const float* logits, const float* bias, int tokens, uint32_t* ids, float* scores,
+                              int plan_experts, int skip_slot, PlanView plan, cudaStream_t s) {
   size_t smem = plan_smem_bytes(plan_experts, kGateWarps);
   if (smem < 5 * kSmallPlanRows * sizeof(int)) smem = 5 * kSmallPlanRows * sizeof(int);
   if (smem > 48 * 1024) {
-    cudaError_t err = cudaFuncSetAttribute(router_plan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           static_cast<int>(smem));
+    cudaError_t err =
+        cudaFuncSetAttribute(route_plan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (err != cudaSuccess) return err;
   }
-  static const cudaError_t carve = prefer_shared_carveout(router_plan_kernel);
+  static const cudaError_t carve = prefer_shared_carveout(route_plan_kernel);
   if (carve != cudaSuccess) return carve;
-  cudaError_t err = cudaMemsetAsync(done, 0, sizeof(int), s);
-  if (err != cudaSuccess) return err;
-  router_plan_kernel<<<256, kGateWarps * 32, smem, s>>>(x, x_dtype, tokens, hidden, wg, logits, bias, ids, scores,
-                                                         done, plan_experts, skip_slot, plan);
-  return cudaGetLastError();
+  return launch_pdl(route_plan_kernel, dim3(1), dim3(kGateWarps * 32), smem, s, logits, bias, tokens, ids, scores,
+                    plan_experts, skip_slot, plan);
 }
 
 cudaError_t launch_route(const float* logits, const float* bias, int rows, uint32_t* ids, float* scores,

@@ -85,3 +85,70 @@ def test_stack_blocks_match_oracle(tokens):
         scale = float(np.max(np.abs(want)))
         assert float(np.max(np.abs(got - want))) <= 1e-2 * scale
         assert rel_l2(got, want) < 5e-3
+
+
+def _graph_matches_eager(stack, h0, replays=4):
+    """The stack captured as one CUDA graph (its kernels launched back to back,
+    so chained launches overlap as far as their dependencies allow) gives the
+    eager result bit for bit on every replay."""
+    import torch
+
+    stream = torch.cuda.Stream()
+    torch.cuda.synchronize()  # weights and h0 were made on the default stream
+    with torch.cuda.stream(stream):
+        want = stack(h0).clone()  # eager; also allocates the workspaces
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            out = stack(h0)
+        for _ in range(replays):
+            out.zero_()
+            graph.replay()
+            stream.synchronize()
+            np.testing.assert_array_equal(host(out), host(want))
+    del graph
+
+
+@pytest.mark.parametrize("tokens", [1, 3])
+def test_stack_graph_matches_eager_trellis(tokens):
+    """Four GLM-5-size K4 blocks (bf16 shared expert streamed beside the
+    trellis units) in one graph: every block's kernel chain starts only after
+    the previous block, including the shared expert's rows that stream
+    without waiting for the routing."""
+    import torch
+
+    from mlxlr8_b200.moe import MoELayer
+    from mlxlr8_b200.stack import MoEStack
+    from mlxlr8_b200.synthetic import make_layer
+
+    layers = [make_layer(seed=400 + i) for i in range(4)]
+    g = torch.Generator(device="cuda")
+    g.manual_seed(41 + tokens)
+    norms = [(1.0 + 0.1 * torch.randn(6144, generator=g, device="cuda")).to(torch.bfloat16) for _ in layers]
+    stack = MoEStack([(w, MoELayer(l.gate_weight, l.bias, l.experts)) for w, l in zip(norms, layers)])
+    h0 = torch.randn(tokens, 6144, generator=g, device="cuda").to(torch.bfloat16)
+    _graph_matches_eager(stack, h0)
+    del stack, layers
+    torch.cuda.empty_cache()
+
+
+def test_stack_graph_matches_eager_joined():
+    """Two GLM-5-size joined MXFP4 blocks at one token in one graph."""
+    import torch
+
+    from mlxlr8_b200.joined_mxfp4 import JoinedMoELayer, JoinedMXFP4
+    from mlxlr8_b200.stack import MoEStack
+    from mlxlr8_b200.synthetic import make_joined
+
+    blocks = []
+    g = torch.Generator(device="cuda")
+    g.manual_seed(43)
+    for i in range(2):
+        j = make_joined(seed=500 + i)
+        w = (1.0 + 0.1 * torch.randn(6144, generator=g, device="cuda")).to(torch.bfloat16)
+        blocks.append((w, JoinedMoELayer(j.gate_weight, j.bias,
+                                         JoinedMXFP4(j.unit, j.weights, j.scales, j.hidden, j.intermediate))))
+    h0 = torch.randn(1, 6144, generator=g, device="cuda").to(torch.bfloat16)
+    _graph_matches_eager(MoEStack(blocks), h0)
+    del blocks
+    torch.cuda.empty_cache()
