@@ -283,45 +283,45 @@ __global__ void __launch_bounds__(kJThreads, 2) joined_stream_kernel(const __gri
 #pragma unroll
     for (int q = 0; q < kJBlocks; ++q) {
       if (q < m.z) {
-      uint32_t w0[4], w1[4];
-      const uint32_t sbase = smem_u32(base);
-      ldsm_x4(sbase + code_off[q * 2], w0[0], w1[0], w0[1], w1[1]);
-      ldsm_x4(sbase + code_off[q * 2 + 1], w0[2], w1[2], w0[3], w1[3]);
-      float fs0[4], fs1[4];
-      e8m0x4(*reinterpret_cast<const uint32_t*>(base + sc0_off + q * 512), fs0);
-      e8m0x4(*reinterpret_cast<const uint32_t*>(base + sc1_off + q * 512), fs1);
-      const uint2* f0 = frag + ((q * kMaxGroupRows + rr0) * kJFragRowBytes) / 8 + fpos;
-      const uint2* f1 = frag + ((q * kMaxGroupRows + 4 + rr0) * kJFragRowBytes) / 8 + fpos;
-      float st[2][4];
+        uint32_t w0[4], w1[4];
+        const uint32_t sbase = smem_u32(base);
+        ldsm_x4(sbase + code_off[q * 2], w0[0], w1[0], w0[1], w1[1]);
+        ldsm_x4(sbase + code_off[q * 2 + 1], w0[2], w1[2], w0[3], w1[3]);
+        float fs0[4], fs1[4];
+        e8m0x4(*reinterpret_cast<const uint32_t*>(base + sc0_off + q * 512), fs0);
+        e8m0x4(*reinterpret_cast<const uint32_t*>(base + sc1_off + q * 512), fs1);
+        const uint2* f0 = frag + ((q * kMaxGroupRows + rr0) * kJFragRowBytes) / 8 + fpos;
+        const uint2* f1 = frag + ((q * kMaxGroupRows + 4 + rr0) * kJFragRowBytes) / 8 + fpos;
+        float st[2][4];
 #pragma unroll
-      for (int c = 0; c < 2; ++c)
+        for (int c = 0; c < 2; ++c)
 #pragma unroll
-        for (int i = 0; i < 4; ++i) st[c][i] = 0.0f;
+          for (int i = 0; i < 4; ++i) st[c][i] = 0.0f;
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        // Rows g / g + 8; A pairs (k 8tig + 4h .. +1) and (8tig + 4h + 2 .. +3).
-        float blk[4];
-        block_mma(blk, w0[j], w1[j], f0[(2 * j) * 8], f0[(2 * j + 1) * 8]);
-        st[0][0] = fmaf(blk[0], fs0[j], st[0][0]);
-        st[0][1] = fmaf(blk[1], fs0[j], st[0][1]);
-        st[0][2] = fmaf(blk[2], fs1[j], st[0][2]);
-        st[0][3] = fmaf(blk[3], fs1[j], st[0][3]);
-        if (ncg > 1) {
-          float blk1[4];
-          block_mma(blk1, w0[j], w1[j], f1[(2 * j) * 8], f1[(2 * j + 1) * 8]);
-          st[1][0] = fmaf(blk1[0], fs0[j], st[1][0]);
-          st[1][1] = fmaf(blk1[1], fs0[j], st[1][1]);
-          st[1][2] = fmaf(blk1[2], fs1[j], st[1][2]);
-          st[1][3] = fmaf(blk1[3], fs1[j], st[1][3]);
+        for (int j = 0; j < 4; ++j) {
+          // Rows g / g + 8; A pairs (k 8tig + 4h .. +1) and (8tig + 4h + 2 .. +3).
+          float blk[4];
+          block_mma(blk, w0[j], w1[j], f0[(2 * j) * 8], f0[(2 * j + 1) * 8]);
+          st[0][0] = fmaf(blk[0], fs0[j], st[0][0]);
+          st[0][1] = fmaf(blk[1], fs0[j], st[0][1]);
+          st[0][2] = fmaf(blk[2], fs1[j], st[0][2]);
+          st[0][3] = fmaf(blk[3], fs1[j], st[0][3]);
+          if (ncg > 1) {
+            float blk1[4];
+            block_mma(blk1, w0[j], w1[j], f1[(2 * j) * 8], f1[(2 * j + 1) * 8]);
+            st[1][0] = fmaf(blk1[0], fs0[j], st[1][0]);
+            st[1][1] = fmaf(blk1[1], fs0[j], st[1][1]);
+            st[1][2] = fmaf(blk1[2], fs1[j], st[1][2]);
+            st[1][3] = fmaf(blk1[3], fs1[j], st[1][3]);
+          }
         }
-      }
-      // Each 128-wide block's products times its activation unscale.
+        // Each 128-wide block's products times its activation unscale.
 #pragma unroll
-      for (int i = 0; i < 4; ++i) acc[0][i] = fmaf(st[0][i], us[0][q], acc[0][i]);
-      if (ncg > 1) {
+        for (int i = 0; i < 4; ++i) acc[0][i] = fmaf(st[0][i], us[0][q], acc[0][i]);
+        if (ncg > 1) {
 #pragma unroll
-        for (int i = 0; i < 4; ++i) acc[1][i] = fmaf(st[1][i], us[1][q], acc[1][i]);
-      }
+          for (int i = 0; i < 4; ++i) acc[1][i] = fmaf(st[1][i], us[1][q], acc[1][i]);
+        }
       }
     }
     __syncwarp();
