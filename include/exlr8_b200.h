@@ -113,6 +113,14 @@ int exlr8_check_format(int64_t packed_bytes, int k, int in_features, int out_fea
 int exlr8_decode_trellis(const void* packed, int64_t packed_bytes, int64_t matrix, int k, int in_features,
                          int out_features, int sharded_side, float* inner, void* stream);
 
+/* Static hot-expert cache (exlr8/static_cache.py:29-42 expand_static_trellis):
+ * the exact E4M3 bytes of every stored tile of a packed buffer, tile order
+ * kept, 256 bytes per 16x16 tile (in_features * out_features bytes per
+ * matrix); byte p of a tile is the E4M3 code of its codeword p (codeword j
+ * of lane l at p = 8 l + j).  packed and out 4-byte aligned. */
+int exlr8_expand_static_trellis(const void* packed, int64_t packed_bytes, int k, int in_features, int out_features,
+                                int sharded_side, uint8_t* out, void* stream);
+
 /* Public dense matrix float32 [out][in] of a single-matrix buffer
  * (exlr8/trellis.py:199-214 dequantize_trellis). */
 size_t exlr8_dequantize_trellis_workspace(int in_features, int out_features);

@@ -66,6 +66,7 @@ _SIGNATURES = {
     "exlr8_codebook": (c_int, [c_void_p, c_void_p, c_int64, c_int, c_void_p]),
     "exlr8_check_format": (c_int, [c_int64, c_int, c_int, c_int, c_int, POINTER(c_int64)]),
     "exlr8_decode_trellis": (c_int, [c_void_p, c_int64, c_int64, c_int, c_int, c_int, c_int, c_void_p, c_void_p]),
+    "exlr8_expand_static_trellis": (c_int, [c_void_p, c_int64, c_int, c_int, c_int, c_int, c_void_p, c_void_p]),
     "exlr8_dequantize_trellis_workspace": (c_size_t, [c_int, c_int]),
     "exlr8_dequantize_trellis": (c_int, [c_void_p, c_int64, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int,
                                          c_void_p, c_void_p, c_size_t, c_void_p]),

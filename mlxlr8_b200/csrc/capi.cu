@@ -482,6 +482,16 @@ int exlr8_decode_trellis(const void* packed, int64_t packed_bytes, int64_t matri
                                           sharded_side, inner, as_stream(stream)));
 }
 
+int exlr8_expand_static_trellis(const void* packed, int64_t packed_bytes, int k, int in_features, int out_features,
+                                int sharded_side, uint8_t* out, void* stream) {
+  int64_t count = 0;
+  EXLR8_CHECK(format_status(packed_bytes, k, in_features, out_features, sharded_side, &count));
+  if (!packed || !out) return EXLR8_ERR_ARG;
+  if ((reinterpret_cast<uintptr_t>(packed) | reinterpret_cast<uintptr_t>(out)) & 3u) return EXLR8_ERR_ALIGN;
+  return cuda_status(launch_expand_static(static_cast<const uint32_t*>(packed), packed_bytes / (32 * k), k,
+                                          reinterpret_cast<uint32_t*>(out), as_stream(stream)));
+}
+
 size_t exlr8_dequantize_trellis_workspace(int in_features, int out_features) {
   return align_up(static_cast<size_t>(in_features) * out_features * sizeof(float));
 }

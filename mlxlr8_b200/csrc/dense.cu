@@ -48,6 +48,51 @@ cudaError_t launch_decode_matrix(const uint32_t* words, int64_t expert, int k, i
   return cudaGetLastError();
 }
 
+// E4M3 byte of a float16 that is already an E4M3 number: sign in bit 7; a
+// float16 exponent field of 9 or more is a normal number (field - 8, top three
+// fraction bits); fields 6..8 are the subnormals m * 2^-9; zero keeps its sign.
+__device__ __forceinline__ uint32_t e4m3_byte(uint32_t h) {
+  const uint32_t field = (h >> 10) & 31u, fraction = h & 1023u;
+  uint32_t code = (h >> 8) & 0x80u;
+  if (field >= 9u) {
+    code |= ((field - 8u) << 3) | (fraction >> 7);
+  } else if (field >= 6u) {
+    code |= (1024u + fraction) >> (16u - field);
+  }
+  return code;
+}
+
+// Static hot-expert cache expansion (static_cache.py:29-42): every stored
+// tile of 8k words becomes 256 bytes in place of its index, byte p the E4M3
+// code of codeword p of the tile's cyclic bitstream.  One thread per four
+// codewords (one output word).
+__global__ void expand_static_kernel(const uint32_t* __restrict__ words, int64_t tiles, int k,
+                                     uint32_t* __restrict__ out) {
+  const int64_t index = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (index >= tiles * 64) return;
+  const uint32_t nwords = 8u * static_cast<uint32_t>(k);
+  const uint32_t* tile = words + (index >> 6) * nwords;
+  const uint32_t q = static_cast<uint32_t>(index & 63);
+  uint32_t packed = 0;
+#pragma unroll
+  for (uint32_t j = 0; j < 4; ++j) {
+    const uint32_t last_bit = (4u * q + j + 1u) * k + 256u * k;
+    const uint32_t last_word = (last_bit - 1u) / 32u;
+    const uint32_t shift = (last_word + 1u) * 32u - last_bit;
+    const uint64_t merged = (static_cast<uint64_t>(tile[(last_word - 1u) % nwords]) << 32) | tile[last_word % nwords];
+    const uint32_t cw = static_cast<uint32_t>(merged >> shift) & 0xFFFFu;
+    packed |= e4m3_byte(decode_pair(cw, cw) & 0xFFFFu) << (8u * j);
+  }
+  out[index] = packed;
+}
+
+cudaError_t launch_expand_static(const uint32_t* words, int64_t tiles, int k, uint32_t* out, cudaStream_t s) {
+  const int64_t n = tiles * 64;
+  if (n == 0) return cudaSuccess;
+  expand_static_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, s>>>(words, tiles, k, out);
+  return cudaGetLastError();
+}
+
 // weight[o][i] = H_i(H_o(inner)^T)[o][i] * svh[o] * suh[i], one CTA per
 // 128x128 block (trellis.py:105-109 order: transform along out, transpose,
 // transform along in, then the two scales).

@@ -7,6 +7,8 @@
 namespace exlr8 {
 
 cudaError_t launch_codebook(const uint32_t* states, float* values, int64_t n, int paired, cudaStream_t s);
+// Exact E4M3 bytes of `tiles` stored trellis tiles (256 bytes per tile, tile order kept).
+cudaError_t launch_expand_static(const uint32_t* words, int64_t tiles, int k, uint32_t* out, cudaStream_t s);
 cudaError_t launch_decode_matrix(const uint32_t* words, int64_t expert, int k, int in_features, int out_features,
                                  int side, float* inner, cudaStream_t s);
 cudaError_t launch_dequantize(const float* inner, const void* suh, const void* svh, int scale_dtype,

@@ -65,13 +65,18 @@ def fast_expert_mlp(x, indices, packed, scales, k, hidden, intermediate, *, reus
                     expert_to_slot=None, workspace=None):
     """Gate/up, typed SwiGLU, down for every slot; ``[*indices.shape, hidden]``.
 
-    Mirrors ``fast_expert_mlp`` (fast_decode.py:208-221).  The static FP8 hot
-    cache (``fp8``/``expert_to_slot``) is not part of this build.  An optional
-    uint8 ``workspace`` tensor is used instead of a fresh one when it is large
-    enough (its dispatch header stays readable after the call).
+    Mirrors ``fast_expert_mlp`` (fast_decode.py:208-221).  ``fp8`` (cached
+    gate/up/down E4M3 bytes in tile order, ``static_cache.StaticExpertCache``)
+    and ``expert_to_slot`` hold the same weights as the cached experts' codes;
+    the products here come from the codes, which gives the bit-equal outputs
+    the reference requires of the cache.  An optional uint8 ``workspace``
+    tensor is used instead of a fresh one when it is large enough (its dispatch
+    header stays readable after the call).
     """
-    if fp8 is not None or expert_to_slot is not None:
-        raise NotImplementedError("the static FP8 expert cache is not implemented in the B200 build")
+    if (fp8 is None) != (expert_to_slot is None):
+        raise ValueError("fp8 bytes and expert_to_slot go together")
+    if fp8 is not None and set(fp8) != {"gate", "up", "down"}:
+        raise ValueError("fp8 must hold gate, up and down bytes")
     device = _lib.require_cuda(x, indices)
     if x.shape[-1] != hidden:
         raise ValueError("activation width does not match in_features")

@@ -234,6 +234,34 @@ class DecodedCache:
 # Operators
 # ---------------------------------------------------------------------------
 
+def e4m3_code(values):
+    """E4M3 byte of float16 values that are already E4M3 numbers
+    (static_cache.py:11-22): sign in bit 7; a float16 exponent field of 9 or
+    more is a normal E4M3 number (exponent field minus 8, top three fraction
+    bits); fields 6..8 are the E4M3 subnormals m * 2^-9; zero keeps its sign."""
+    bits = np.asarray(values, dtype=np.float16).view(np.uint16).astype(np.uint32)
+    field = (bits >> 10) & 31
+    fraction = bits & 1023
+    code = (bits >> 8) & 0x80
+    normal = field >= 9
+    code = np.where(normal, code | ((field - 8) << 3) | (fraction >> 7), code)
+    sub = (field >= 6) & (field < 9)
+    shift = np.where(sub, 16 - field, 0)
+    code = np.where(sub, code | ((1024 + fraction) >> shift), code)
+    return code.astype(np.uint8)
+
+
+def expand_static(packed, k, in_features, out_features, sharded_side=1):
+    """Exact E4M3 bytes of every stored tile, in storage order
+    (static_cache.py:29-42): tile t of the packed buffer becomes 256 bytes at
+    256 * t, byte p holding the E4M3 code of the tile's codeword p (codeword
+    8 * lane + j of the trellis order)."""
+    raw = np.ascontiguousarray(np.asarray(packed)).view(np.uint8).reshape(-1)
+    check_format(raw.size, k, in_features, out_features, sharded_side)
+    words = raw.view(np.uint32).reshape(-1, 8 * k)
+    return e4m3_code(mcg_codebook())[decode_codewords(words, k)].reshape(-1)
+
+
 def slot_rows(x, indices, features):
     """Broadcast one row per token to one row per slot (trellis.py:185-190)."""
     x = np.asarray(x, dtype=F32)

@@ -8,14 +8,16 @@ It imports the reference's NumPy-only functions (``exlr8/trellis.py``:
 ``round_e4m3``, ``mcg_codebook``, ``hadamard_reference``,
 ``decode_trellis_reference``, ``dequantize_reference``) and the vendored
 PonyExl3 CPU reference (``third_party/ponyexl3/ref/{trellis,perm,codebook}.py``)
-by file path -- MLX is not needed for these -- and evaluates them on seeded
-inputs.  Expected values for composite operators use the same formulas as the
+by file path, and ``exlr8/static_cache.py`` (``expand_static_reference``,
+``codebook_codes``) as a package module -- MLX is not needed for these -- and
+evaluates them on seeded inputs.  Expected values for composite operators use the same formulas as the
 reference's own tests (cited beside each case).  The output is
 ``tests/golden/golden.npz``; the tests never read the reference at run time.
 """
 
 from __future__ import annotations
 
+import importlib
 import importlib.util
 import sys
 from pathlib import Path
@@ -149,6 +151,21 @@ def main(reference_root: str) -> None:
             out[f"route_{case}_{rows}_bias"] = bias
             out[f"route_{case}_{rows}_ids"] = expected.astype(np.uint32)
             out[f"route_{case}_{rows}_scores"] = weights.astype(np.float32)
+
+    # Static hot-expert cache: exact E4M3 bytes in the stored tile order
+    # (static_cache.py:11-45, expand_static_reference and codebook_codes; the
+    # module needs the package for its relative import, and MLX only inside
+    # functions not called here).
+    sys.path.insert(0, str(root))
+    static = importlib.import_module("exlr8.static_cache")
+    out["static_codebook_codes"] = np.asarray(static.codebook_codes()).copy()
+    r = np.random.default_rng(991)
+    for k in (2, 3, 4):
+        for side in (1, 2):
+            a, b = (128, 256) if side == 1 else (256, 128)
+            packed = r.integers(0, 256, 2 * a * b * k // 8, dtype=np.uint8)
+            out[f"static_k{k}_s{side}_packed"] = packed
+            out[f"static_k{k}_s{side}_bytes"] = np.asarray(static.expand_static_reference(packed, k, a, b, side))
 
     target = Path(__file__).with_name("golden.npz")
     np.savez_compressed(target, **out)

@@ -114,3 +114,23 @@ def test_combine_order_and_casts():
     # Summation order may move a result by at most one bf16 step.
     np.testing.assert_allclose(out, expected, rtol=8e-3, atol=1e-6)
     assert np.array_equal(out, ref.round_bf16(out))
+
+
+def test_static_codebook_codes_match_reference(golden):
+    """E4M3 bytes of all 65,536 codebook values (static_cache.py:11-26):
+    decoding each byte as E4M3 gives the codebook value back."""
+    codes = ref.e4m3_code(ref.mcg_codebook())
+    np.testing.assert_array_equal(codes, golden["static_codebook_codes"])
+    levels = np.concatenate([ref.e4m3_levels(), [np.nan]])
+    back = np.where(codes & 0x80, -1.0, 1.0) * levels[codes & 0x7F]
+    np.testing.assert_array_equal(back.astype(np.float16), ref.mcg_codebook())
+
+
+@pytest.mark.parametrize("k", [2, 3, 4])
+@pytest.mark.parametrize("side", [1, 2])
+def test_static_expansion_matches_reference(golden, k, side):
+    """Exact E4M3 expansion of two stored matrices in tile order
+    (static_cache.py:29-42)."""
+    a, b = (128, 256) if side == 1 else (256, 128)
+    got = ref.expand_static(golden[f"static_k{k}_s{side}_packed"], k, a, b, side)
+    np.testing.assert_array_equal(got, golden[f"static_k{k}_s{side}_bytes"])
