@@ -456,6 +456,45 @@ def encode_config(layer, steps, stream):
             "kernel": "mxfp4_encode_trellis_kernel (3 launches per layer)"}
 
 
+def static_cache_config(layer, steps, stream):
+    """Static hot-expert cache (static_cache.py): the selected-
+    expert MLP of one decode token over eight routed experts, all cached as
+    exact E4M3 bytes, against the same call decoding their trellis codes.  Two
+    disjoint expert sets alternate, so no call finds its weights in L2.
+    Algorithmic bytes: the weight bytes streamed (3 * h * m per cached expert,
+    K * h * m * 3 / 8 per coded one)."""
+    import torch
+
+    from mlxlr8_b200.fast_decode import fast_expert_mlp
+    from mlxlr8_b200.static_cache import StaticExpertCache
+
+    e = layer.experts
+    sets = [list(range(0, 8)), list(range(8, 16))]
+    cache = StaticExpertCache(e, sets[0] + sets[1])
+    idx = [torch.tensor([s], dtype=torch.int32, device="cuda") for s in sets]
+    x, _ = layer.tokens(1, seed_offset=91)
+    turn = [0]
+
+    def call(cached):
+        i = turn[0] = turn[0] ^ 1
+        if cached:
+            return fast_expert_mlp(x, idx[i], e.packed, e.scales, e.k, e.hidden, e.intermediate, fp8=cache.fp8,
+                                   expert_to_slot=cache.expert_to_slot)
+        return fast_expert_mlp(x, idx[i], e.packed, e.scales, e.k, e.hidden, e.intermediate)
+
+    coded_ms = time_calls(lambda: call(False), steps, 3, stream)
+    cached_ms = time_calls(lambda: call(True), steps, 3, stream)
+    peak, peak_kind = measured_peaks()
+    cached_bytes = 8 * 3 * HIDDEN * INTER
+    coded_bytes = 8 * 3 * HIDDEN * INTER * K_BITS // 8
+    del cache
+    torch.cuda.empty_cache()
+    return {"experts": 8, "coded_ms": coded_ms, "cached_ms": cached_ms,
+            "coded_weight_gbs": coded_bytes / (coded_ms / 1000.0) / 1e9,
+            "cached_weight_gbs": cached_bytes / (cached_ms / 1000.0) / 1e9,
+            "cached_frac_of_hbm": cached_bytes / (cached_ms / 1000.0) / 1e9 / peak, "peak_kind": peak_kind}
+
+
 def loader_config():
     """EXLR8 checkpoint -> device (experts.py:77-148): one
     full-size K4 layer (256 routed experts + shared, 4.85 GB of codes) written
@@ -739,6 +778,7 @@ def main():
         extras["stack"] = stack_configs(layers, 20, stream)
         extras["joined_decode"] = joined_decode_configs(min(args.steps, 200), stream)
         extras["encode"] = encode_config(layers[0], 5, stream)
+        extras["static_cache"] = static_cache_config(layers[0], min(args.steps, 200), stream)
         extras["loader"] = loader_config()
 
     cpu = None

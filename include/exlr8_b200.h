@@ -193,6 +193,26 @@ int exlr8_expert_mlp(const void* x, int x_dtype, int per_slot, const uint32_t* i
                      const exlr8_trellis_experts* experts, void* out, void* workspace, size_t workspace_bytes,
                      void* stream);
 
+/* Static hot-expert cache (exlr8/static_cache.py:91-134 StaticExpertCache,
+ * the fp8 / expert_to_slot arguments of fast_expert_mlp): fp8[p] holds the
+ * exact E4M3 bytes of the cached experts of projection p (gate, up, down) as
+ * exlr8_expand_static_trellis writes them, in_features * out_features bytes
+ * per slot, 16-byte aligned; expert_to_slot[e] is the slot of expert e or -1
+ * (the uint32 0xFFFFFFFF of the reference). */
+typedef struct exlr8_static_cache {
+  const uint8_t* fp8[3];
+  const int32_t* expert_to_slot;
+  int64_t slots;
+} exlr8_static_cache;
+
+/* exlr8_expert_mlp with a static cache: the streaming decode reads the cached
+ * experts' bytes instead of decoding their codes; outputs are bit-equal to
+ * exlr8_expert_mlp (the bytes are the same weights, taken in the same order).
+ * Batches on the tensor-core prefill path decode the codes as before. */
+int exlr8_expert_mlp_cached(const void* x, int x_dtype, int per_slot, const uint32_t* indices, int64_t tokens,
+                            int slots, const exlr8_trellis_experts* experts, const exlr8_static_cache* cache,
+                            void* out, void* workspace, size_t workspace_bytes, void* stream);
+
 /* exlr8/fast_decode.py:224-244 compiled_expert_mlp_finish: nine slots per
  * token (eight routed, slot 8 shared), scores float32 [tokens][8], residual
  * [tokens][hidden]; out = residual + T(T(sum_r v_r*score_r) + v_shared).

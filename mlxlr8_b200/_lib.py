@@ -37,6 +37,10 @@ class TrellisExperts(ctypes.Structure):
     ]
 
 
+class StaticCache(ctypes.Structure):
+    _fields_ = [("fp8", c_void_p * 3), ("expert_to_slot", c_void_p), ("slots", c_int64)]
+
+
 class DenseExpert(ctypes.Structure):
     _fields_ = [("gate", c_void_p), ("up", c_void_p), ("down", c_void_p)]
 
@@ -80,6 +84,8 @@ _SIGNATURES = {
     "exlr8_expert_mlp_workspace": (c_size_t, [c_int64, c_int, c_int, c_int, c_int64]),
     "exlr8_expert_mlp": (c_int, [c_void_p, c_int, c_int, c_void_p, c_int64, c_int, POINTER(TrellisExperts),
                                  c_void_p, c_void_p, c_size_t, c_void_p]),
+    "exlr8_expert_mlp_cached": (c_int, [c_void_p, c_int, c_int, c_void_p, c_int64, c_int, POINTER(TrellisExperts),
+                                        POINTER(StaticCache), c_void_p, c_void_p, c_size_t, c_void_p]),
     "exlr8_expert_mlp_finish_workspace": (c_size_t, [c_int64, c_int, c_int, c_int64]),
     "exlr8_expert_mlp_finish": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_int64,
                                         POINTER(TrellisExperts), POINTER(DenseExpert), c_void_p, c_void_p, c_size_t,

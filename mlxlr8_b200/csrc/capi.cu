@@ -216,7 +216,7 @@ int launch_dense_decode(const void* x, int x_dtype, int64_t tokens, const exlr8_
 int run_mlp_after_plan(const void* x, int x_dtype, int per_slot, int slots, const uint32_t* ids, int64_t rows,
                        const exlr8_trellis_experts* ex, int64_t experts, const exlr8_dense_expert* shared,
                        const void* dense_x, int64_t tokens, const MlpLayout& l, const MlpBuffers& b,
-                       cudaStream_t s) {
+                       cudaStream_t s, const exlr8_static_cache* cache = nullptr) {
   const int h = ex->hidden, m = ex->intermediate;
   const int n = static_cast<int>(rows), e = static_cast<int>(experts), t = static_cast<int>(tokens);
   EXLR8_TIMED(EXLR8_KERNEL_PREP, s,
@@ -233,6 +233,12 @@ int run_mlp_after_plan(const void* x, int x_dtype, int per_slot, int slots, cons
   gp.kt_per_split = l.s1.kt;
   gp.splits = l.s1.count;
   gp.projections = 2;
+  if (cache) {
+    gp.hot[0] = cache->fp8[0];
+    gp.hot[1] = cache->fp8[1];
+    gp.expert_to_slot = cache->expert_to_slot;
+    gp.hot_slots = cache->slots;
+  }
   const int dsplits_gu = dense_gate_up_splits(h), dsplits_d = dense_down_splits(m);
   if (shared)
     gp.dense = DenseUnits{static_cast<const uint16_t*>(shared->gate), static_cast<const uint16_t*>(shared->up),
@@ -254,6 +260,11 @@ int run_mlp_after_plan(const void* x, int x_dtype, int per_slot, int slots, cons
   dp.kt_per_split = l.s2.kt;
   dp.splits = l.s2.count;
   dp.projections = 1;
+  if (cache) {
+    dp.hot[0] = cache->fp8[2];
+    dp.expert_to_slot = cache->expert_to_slot;
+    dp.hot_slots = cache->slots;
+  }
   if (shared)
     dp.dense = DenseUnits{static_cast<const uint16_t*>(shared->down), nullptr, static_cast<const uint16_t*>(b.dh),
                           b.ddown, nullptr, h, m, t, dsplits_d, (h / kDenseRows) * dsplits_d, 0};
@@ -614,9 +625,9 @@ size_t exlr8_expert_mlp_workspace(int64_t tokens, int slots, int hidden, int int
   return prefill > decode ? prefill : decode;
 }
 
-int exlr8_expert_mlp(const void* x, int x_dtype, int per_slot, const uint32_t* indices, int64_t tokens, int slots,
-                     const exlr8_trellis_experts* ex, void* out, void* workspace, size_t workspace_bytes,
-                     void* stream) {
+static int expert_mlp(const void* x, int x_dtype, int per_slot, const uint32_t* indices, int64_t tokens, int slots,
+                      const exlr8_trellis_experts* ex, const exlr8_static_cache* cache, void* out, void* workspace,
+                      size_t workspace_bytes, void* stream) {
   int64_t experts = 0;
   EXLR8_CHECK(check_experts(ex, &experts));
   if (!valid_act(x_dtype)) return EXLR8_ERR_DTYPE;
@@ -641,11 +652,29 @@ int exlr8_expert_mlp(const void* x, int x_dtype, int per_slot, const uint32_t* i
   const MlpBuffers b = carve_mlp(l, rows, experts, false, tokens, ex->hidden, ex->intermediate, c);
   EXLR8_TIMED(EXLR8_KERNEL_PLAN, s,
               launch_plan(indices, static_cast<int>(rows), static_cast<int>(experts), slots, -1, b.plan, s));
-  EXLR8_CHECK(
-      run_mlp_after_plan(x, x_dtype, per_slot, slots, indices, rows, ex, experts, nullptr, nullptr, tokens, l, b, s));
+  EXLR8_CHECK(run_mlp_after_plan(x, x_dtype, per_slot, slots, indices, rows, ex, experts, nullptr, nullptr, tokens,
+                                 l, b, s, cache));
   ProfileScope scope(EXLR8_KERNEL_FINISH, s);
   return cuda_status(launch_finish(b.dpart, l.s2.count, nullptr, indices, static_cast<int>(rows), ex->out_scale[2],
                                    ex->scale_dtype, ex->hidden, static_cast<int>(experts), x_dtype, out, s));
+}
+
+int exlr8_expert_mlp(const void* x, int x_dtype, int per_slot, const uint32_t* indices, int64_t tokens, int slots,
+                     const exlr8_trellis_experts* ex, void* out, void* workspace, size_t workspace_bytes,
+                     void* stream) {
+  return expert_mlp(x, x_dtype, per_slot, indices, tokens, slots, ex, nullptr, out, workspace, workspace_bytes,
+                    stream);
+}
+
+int exlr8_expert_mlp_cached(const void* x, int x_dtype, int per_slot, const uint32_t* indices, int64_t tokens,
+                            int slots, const exlr8_trellis_experts* ex, const exlr8_static_cache* cache, void* out,
+                            void* workspace, size_t workspace_bytes, void* stream) {
+  if (!cache || !cache->expert_to_slot || cache->slots <= 0) return EXLR8_ERR_ARG;
+  for (int p = 0; p < 3; ++p) {
+    if (!cache->fp8[p]) return EXLR8_ERR_ARG;
+    if (!aligned16(cache->fp8[p])) return EXLR8_ERR_ALIGN;
+  }
+  return expert_mlp(x, x_dtype, per_slot, indices, tokens, slots, ex, cache, out, workspace, workspace_bytes, stream);
 }
 
 size_t exlr8_expert_mlp_finish_workspace(int64_t tokens, int hidden, int intermediate, int64_t experts) {

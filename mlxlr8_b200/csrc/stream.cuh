@@ -43,6 +43,13 @@ struct DenseUnits {
 
 struct StreamParams {
   const uint32_t* packed[2];
+  // Static hot-expert cache (optional): the exact E4M3 bytes of the cached
+  // experts per projection, the stored tile order with 256 bytes per tile and
+  // in_features * out_features bytes per cache slot; expert_to_slot[e] is the
+  // slot of expert e or -1.  Units of cached experts stream these bytes.
+  const unsigned char* hot[2];
+  const int32_t* expert_to_slot;
+  int64_t hot_slots;  // slots in hot[]: a map entry outside [0, hot_slots) reads as "not cached"
   const unsigned char* frag;  // [proj][nslots][in_features / 128] records of kFragBlockBytes
   float* partial;             // [proj][nslots][splits][out_features]
   PlanView plan;

@@ -44,7 +44,10 @@ constexpr int kStageTiles = 8;                       // K tiles per stage
 constexpr int kFragRowBytes = kStageTiles * 64 + 64;  // padded: rows hit different banks
 static_assert(kFragRowBytes >= kFragBlockBytes, "a fragment record fits its stage row");
 
-enum : int { kFirst = 1, kLast = 2, kEnd = 4 };
+// kHot: a stage of static-cache bytes covering kHotTiles K tiles; kBlockStart
+// / kBlockEnd: the stage opens / closes its 128-wide K block (code stages do
+// both).
+enum : int { kFirst = 1, kLast = 2, kEnd = 4, kHot = 8, kBlockStart = 16, kBlockEnd = 32 };
 
 template <int K>
 struct StageGeometry {
@@ -54,7 +57,22 @@ struct StageGeometry {
   static constexpr int kStageBytes = kCodeBytes + kFragBytes;
   static constexpr int kRingBytes = kStages * kStageBytes;
   static constexpr int kSmemBytes = kRingBytes + kDenseSmemBytes;  // ring, then the dense warp's buffers
+  // K tiles of static-cache bytes per stage (8 output tiles x 256 bytes per
+  // K tile) that fit the code area: a power of two dividing kStageTiles.
+  static constexpr int kHotTiles = kCodeBytes >= 4 * 8 * 256 ? 4 : 2;
+  static_assert(kHotTiles * 8 * 256 <= kCodeBytes, "a hot stage fits the code area");
 };
+
+// A fragment of one tile from its static-cache bytes: lane l's eight bytes are
+// codewords 0-7 of the lane in order, E4M3-coded; the exact float16 values go
+// to the same registers as the codec's (j0,j1 | j4,j5 | j2,j3 | j6,j7).
+__device__ __forceinline__ void e4m3_fragment(uint2 b, uint32_t a[4]) {
+  asm("{\n .reg .b16 l0, h0, l1, h1;\n mov.b32 {l0, h0}, %4;\n mov.b32 {l1, h1}, %5;\n"
+      " cvt.rn.f16x2.e4m3x2 %0, l0;\n cvt.rn.f16x2.e4m3x2 %1, l1;\n"
+      " cvt.rn.f16x2.e4m3x2 %2, h0;\n cvt.rn.f16x2.e4m3x2 %3, h1;\n}\n"
+      : "=r"(a[0]), "=r"(a[1]), "=r"(a[2]), "=r"(a[3])
+      : "r"(b.x), "r"(b.y));
+}
 
 __device__ __forceinline__ void mma_f16(float c[4], const uint32_t a[4], uint2 b) {
   asm volatile(
@@ -205,26 +223,42 @@ __global__ void __launch_bounds__(kStreamThreads, 2) trellis_stream_kernel(Strea
 #pragma unroll
       for (int r = 0; r < kMaxGroupRows; ++r)
         slots[r] = r < nr ? (cached ? plan_cache[3][start + r] : p.plan.order[start + r]) : -1;
-      for (int kt = kt0; kt < kt1; kt += kStageTiles) {
+      // A cached expert streams its E4M3 bytes, kHotTiles K tiles per stage
+      // (twice the bytes of K4 codes, no decode); others stream codes, one
+      // 128-wide K block per stage.
+      int hslot = p.expert_to_slot != nullptr ? p.expert_to_slot[expert] : -1;
+      if (hslot >= p.hot_slots) hslot = -1;
+      const int step = hslot >= 0 ? G::kHotTiles : kStageTiles;
+      for (int kt = kt0; kt < kt1; kt += step) {
         if (kt != kt0) {
           if (!mbar_wait(&empty_bar[stage], phase ^ 1u)) {
             failed = true;
             break;
           }
         }
-        const int n = min(kStageTiles, kt1 - kt);
+        const int n = min(step, kt1 - kt);
+        const int block_flags = (kt % kStageTiles == 0 ? kBlockStart : 0) |
+                                ((kt + n) % kStageTiles == 0 || kt + n >= kt1 ? kBlockEnd : 0);
         meta[stage] = make_int4(static_cast<int>(unit), kt, n,
-                                (kt == kt0 ? kFirst : 0) | (kt + kStageTiles >= kt1 ? kLast : 0));
+                                (kt == kt0 ? kFirst : 0) | (kt + step >= kt1 ? kLast : 0) | block_flags |
+                                    (hslot >= 0 ? kHot : 0));
         if (kt == kt0) {
           unit_rows[stage][0] = nr;
 #pragma unroll
           for (int r = 0; r < kMaxGroupRows; ++r) unit_rows[stage][1 + r] = slots[r];
         }
         unsigned char* base = smem + stage * G::kStageBytes;
-        const uint32_t code_bytes = static_cast<uint32_t>(n) * 8u * G::kTileWords * 4u;
-        mbar_arrive_expect_tx(&full_bar[stage], code_bytes + static_cast<uint32_t>(nr) * kFragBlockBytes);
-        const uint32_t* src = words + tile_index(expert, kt, u.nb * 8, it, ot, p.side) * G::kTileWords;
-        bulk_copy_g2s(base, src, code_bytes, &full_bar[stage]);
+        if (hslot >= 0) {
+          const uint32_t hot_bytes = static_cast<uint32_t>(n) * 8u * 256u;
+          mbar_arrive_expect_tx(&full_bar[stage], hot_bytes + static_cast<uint32_t>(nr) * kFragBlockBytes);
+          const unsigned char* src = p.hot[u.proj] + tile_index(hslot, kt, u.nb * 8, it, ot, p.side) * 256;
+          bulk_copy_g2s(base, src, hot_bytes, &full_bar[stage]);
+        } else {
+          const uint32_t code_bytes = static_cast<uint32_t>(n) * 8u * G::kTileWords * 4u;
+          mbar_arrive_expect_tx(&full_bar[stage], code_bytes + static_cast<uint32_t>(nr) * kFragBlockBytes);
+          const uint32_t* src = words + tile_index(expert, kt, u.nb * 8, it, ot, p.side) * G::kTileWords;
+          bulk_copy_g2s(base, src, code_bytes, &full_bar[stage]);
+        }
 #pragma unroll
         for (int r = 0; r < kMaxGroupRows; ++r) {
           if (r >= nr) break;
@@ -262,6 +296,7 @@ __global__ void __launch_bounds__(kStreamThreads, 2) trellis_stream_kernel(Strea
     for (int i = 0; i < 4; ++i) acc[c][i] = 0.0f;
   UnitInfo u{};
   int nr = 0, ncg = 1, slot_a = -1, slot_b = -1;
+  float st[2][4];  // the current 128-wide K block's products (hot stages carry them across stages)
   GenericGeometry geo;
   if (K != 4) geo = generic_geometry(K, lane);
   const int r0 = gid >> 1, fpos = (gid & 1) * 4 + tig;
@@ -288,12 +323,25 @@ __global__ void __launch_bounds__(kStreamThreads, 2) trellis_stream_kernel(Strea
     // accumulator columns of absent slots, which are reset and never stored.
     const uint2* f0 = frag + (r0 * kFragRowBytes) / 8 + fpos;
     const uint2* f1 = frag + ((4 + r0) * kFragRowBytes) / 8 + fpos;
-    float st[2][4];
+    if (m.w & kBlockStart) {
 #pragma unroll
-    for (int c = 0; c < 2; ++c)
+      for (int c = 0; c < 2; ++c)
 #pragma unroll
-      for (int i = 0; i < 4; ++i) st[c][i] = 0.0f;
-    if (K == 4) {
+        for (int i = 0; i < 4; ++i) st[c][i] = 0.0f;
+    }
+    if (m.w & kHot) {
+      // Static-cache bytes: the same values in the same MMA order as the
+      // codec path, so a cached expert's products are bit-equal.
+      const int kb = m.y % kStageTiles;
+#pragma unroll
+      for (int kk = 0; kk < G::kHotTiles; ++kk) {
+        const uint2 b = *reinterpret_cast<const uint2*>(base + (kk * 8 + warp) * 256 + lane * 8);
+        uint32_t a[4];
+        e4m3_fragment(b, a);
+        mma_f16(st[0], a, f0[(kb + kk) * 8]);
+        if (ncg > 1) mma_f16(st[1], a, f1[(kb + kk) * 8]);
+      }
+    } else if (K == 4) {
       uint32_t word[kStageTiles], prior[kStageTiles];
 #pragma unroll
       for (int kk = 0; kk < kStageTiles; ++kk) {
@@ -329,14 +377,16 @@ __global__ void __launch_bounds__(kStreamThreads, 2) trellis_stream_kernel(Strea
     }
     // This lane's accumulator columns belong to unit rows tig and 4 + tig;
     // their block unscales sit in the fragment record headers.
-    const float* hdr = reinterpret_cast<const float*>(base + G::kCodeBytes + 512);
-    const float us0 = tig < nr ? hdr[tig * (kFragRowBytes / 4)] : 0.0f;
+    if (m.w & kBlockEnd) {
+      const float* hdr = reinterpret_cast<const float*>(base + G::kCodeBytes + 512);
+      const float us0 = tig < nr ? hdr[tig * (kFragRowBytes / 4)] : 0.0f;
 #pragma unroll
-    for (int i = 0; i < 4; ++i) acc[0][i] = fmaf(st[0][i], us0, acc[0][i]);
-    if (ncg > 1) {
-      const float us1 = 4 + tig < nr ? hdr[(4 + tig) * (kFragRowBytes / 4)] : 0.0f;
+      for (int i = 0; i < 4; ++i) acc[0][i] = fmaf(st[0][i], us0, acc[0][i]);
+      if (ncg > 1) {
+        const float us1 = 4 + tig < nr ? hdr[(4 + tig) * (kFragRowBytes / 4)] : 0.0f;
 #pragma unroll
-      for (int i = 0; i < 4; ++i) acc[1][i] = fmaf(st[1][i], us1, acc[1][i]);
+        for (int i = 0; i < 4; ++i) acc[1][i] = fmaf(st[1][i], us1, acc[1][i]);
+      }
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty_bar[stage]);

@@ -11,6 +11,8 @@ the flag is accepted for compatibility.  ``packed`` and ``scales`` are the
 
 from __future__ import annotations
 
+import ctypes
+
 import torch
 
 from . import _lib
@@ -67,11 +69,12 @@ def fast_expert_mlp(x, indices, packed, scales, k, hidden, intermediate, *, reus
 
     Mirrors ``fast_expert_mlp`` (fast_decode.py:208-221).  ``fp8`` (cached
     gate/up/down E4M3 bytes in tile order, ``static_cache.StaticExpertCache``)
-    and ``expert_to_slot`` hold the same weights as the cached experts' codes;
-    the products here come from the codes, which gives the bit-equal outputs
-    the reference requires of the cache.  An optional uint8 ``workspace``
-    tensor is used instead of a fresh one when it is large enough (its dispatch
-    header stays readable after the call).
+    and ``expert_to_slot`` (uint32 or int32 [experts], 0xFFFFFFFF = not cached)
+    make the streaming decode read the cached experts' bytes instead of
+    decoding their codes; the outputs are bit-equal either way, as the
+    reference requires of the cache.  An optional uint8 ``workspace`` tensor is
+    used instead of a fresh one when it is large enough (its dispatch header
+    stays readable after the call).
     """
     if (fp8 is None) != (expert_to_slot is None):
         raise ValueError("fp8 bytes and expert_to_slot go together")
@@ -95,8 +98,29 @@ def fast_expert_mlp(x, indices, packed, scales, k, hidden, intermediate, *, reus
     lib = _lib.lib()
     need = lib.exlr8_expert_mlp_workspace(tokens, slots, hidden, intermediate, experts)
     ws = workspace if workspace is not None and workspace.numel() >= need else _lib.workspace(need, device)
-    _lib.check(lib.exlr8_expert_mlp(x.data_ptr(), _lib.act_code(x), per_slot, ids.data_ptr(), tokens, slots,
-                                    st, out.data_ptr(), ws.data_ptr(), ws.numel(), _lib.stream_handle(device)))
+    if fp8 is None:
+        _lib.check(lib.exlr8_expert_mlp(x.data_ptr(), _lib.act_code(x), per_slot, ids.data_ptr(), tokens, slots,
+                                        st, out.data_ptr(), ws.data_ptr(), ws.numel(), _lib.stream_handle(device)))
+        return out
+    slot_map = _ids(expert_to_slot.reshape(-1))
+    if slot_map.numel() != experts:
+        raise ValueError("expert_to_slot needs one entry per expert")
+    size = hidden * intermediate
+    cache = _lib.StaticCache()
+    counts = set()
+    for i, p in enumerate(("gate", "up", "down")):
+        b = fp8[p].reshape(-1)
+        if b.dtype != torch.uint8 or b.device != device or b.numel() % size or not b.is_contiguous():
+            raise ValueError("fp8 bytes must be contiguous uint8 with hidden * intermediate bytes per slot")
+        counts.add(b.numel() // size)
+        cache.fp8[i] = b.data_ptr()
+    if len(counts) != 1:
+        raise ValueError("fp8 gate, up and down must hold the same slots")
+    cache.expert_to_slot = slot_map.data_ptr()
+    cache.slots = counts.pop()
+    _lib.check(lib.exlr8_expert_mlp_cached(x.data_ptr(), _lib.act_code(x), per_slot, ids.data_ptr(), tokens, slots,
+                                           st, ctypes.byref(cache), out.data_ptr(), ws.data_ptr(), ws.numel(),
+                                           _lib.stream_handle(device)))
     return out
 
 

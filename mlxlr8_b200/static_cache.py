@@ -9,10 +9,12 @@ so a cached expert gives the same products as its codes.
 
 ``StaticExpertCache(layer, expert_ids)`` expands the listed experts of a
 resident layer once (``static_cache.py:91-134``) and keeps the GPU map
-``expert_to_slot`` (0xFFFFFFFF for an uncached expert).  Its decode runs the
-layer's fused expert MLP; the cached experts' products come from the same
-trellis weights, bit for bit, as the reference's test of the cache requires
-(``test_static_cache.py`` bit-equality with cached and uncached experts).
+``expert_to_slot`` (0xFFFFFFFF for an uncached expert).  Its decode is the
+layer's streaming expert MLP with the cache attached: units of cached experts
+stream their bytes (twice the bytes of K4 codes, one conversion per two
+weights instead of the trellis codec) in the codec path's MMA order, so the
+outputs are bit-equal to the uncached decode, as the reference's test of the
+cache requires (``test_static_cache.py``).
 """
 
 from __future__ import annotations

@@ -84,3 +84,48 @@ def test_static_cache_needs_resident_codes():
     layer.packed = None
     with pytest.raises(ValueError, match="resident packed weights"):
         StaticExpertCache(layer, [1])
+
+
+def _bit_equal_cached(layer, hot, ids, x):
+    import torch
+
+    from mlxlr8_b200.fast_decode import fast_expert_mlp
+    from mlxlr8_b200.static_cache import StaticExpertCache
+
+    cache = StaticExpertCache(layer, hot)
+    expected = fast_expert_mlp(x, ids, layer.packed, layer.scales, layer.k, layer.hidden, layer.intermediate)
+    actual = cache(x, ids)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(host(actual).view(np.uint32), host(expected).view(np.uint32))
+
+
+def test_static_decode_k2_and_shared_rows():
+    """K2 (two K tiles per hot stage) with eight rows on one cached expert,
+    which fills both fragment column groups of a unit."""
+    import torch
+
+    from mlxlr8_b200.synthetic import make_layer
+
+    layer = make_layer(seed=12, k=2, hidden=256, intermediate=384, routed=12, shared="none").experts
+    ids = torch.tensor([[10, 3, 5]] * 8, dtype=torch.int32, device="cuda")
+    g = torch.Generator(device="cuda")
+    g.manual_seed(16)
+    x = torch.randn(8, 256, generator=g, device="cuda").to(torch.bfloat16)
+    _bit_equal_cached(layer, [10, 3], ids, x)
+
+
+@pytest.mark.parametrize("dtype", ["float32", "bfloat16"])
+def test_static_decode_full_glm_dimensions(dtype):
+    """GLM-5 size (6144 x 2048, K4) with one cached expert among the eight of
+    a token (fast_decode tests' full-size case)."""
+    import torch
+
+    from helpers import torch_dtype
+    from mlxlr8_b200.synthetic import make_layer
+
+    layer = make_layer(seed=13, routed=24, shared="none").experts
+    ids = torch.tensor([[8, 1, 2, 3, 4, 5, 6, 7, 23]], dtype=torch.int32, device="cuda")
+    g = torch.Generator(device="cuda")
+    g.manual_seed(17)
+    x = torch.randn(1, 6144, generator=g, device="cuda").to(torch_dtype(dtype))
+    _bit_equal_cached(layer, [8, 23], ids, x)
