@@ -21,6 +21,9 @@
 //     permutation is that layout); B holds float16 hi/lo pieces of up to four
 //     rows (eight columns) per fragment group; each stage's float32 products
 //     are added into the unit's accumulators times the block's unscale.
+//   static cache: a unit whose expert is cached (StreamParams::hot) streams
+//     the expert's exact E4M3 bytes instead, kHotTiles K tiles per stage, and
+//     its consumers convert them into the same A fragments (bit-equal).
 //   output: per unit, float32 partial sums [proj][slot][split][out].
 //   dense warp (warp 9): the bf16 shared expert's rows (stream.cuh
 //   DenseUnits, dense_stream.cuh), streamed beside the trellis units.
@@ -318,7 +321,8 @@ __global__ void __launch_bounds__(kStreamThreads, 2) trellis_stream_kernel(Strea
     const unsigned char* base = smem + stage * G::kStageBytes;
     const uint32_t* codes = reinterpret_cast<const uint32_t*>(base);
     const uint2* frag = reinterpret_cast<const uint2*>(base + G::kCodeBytes);
-    // Every stage holds one 128-wide K block (kStageTiles K tiles).  Record
+    // A code stage holds one 128-wide K block (kStageTiles K tiles), a hot
+    // stage kHotTiles K tiles of one; both carry the block's records.  Record
     // rows past the unit's rows hold stale bytes: they only feed the
     // accumulator columns of absent slots, which are reset and never stored.
     const uint2* f0 = frag + (r0 * kFragRowBytes) / 8 + fpos;
