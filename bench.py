@@ -778,7 +778,10 @@ def main():
         extras["stack"] = stack_configs(layers, 20, stream)
         extras["joined_decode"] = joined_decode_configs(min(args.steps, 200), stream)
         extras["encode"] = encode_config(layers[0], 5, stream)
-        extras["static_cache"] = static_cache_config(layers[0], min(args.steps, 200), stream)
+        try:  # a failure here must not cost the lines above
+            extras["static_cache"] = static_cache_config(layers[0], min(args.steps, 200), stream)
+        except Exception as exc:  # noqa: BLE001 - reported in the JSON line
+            extras["static_cache"] = {"error": f"{type(exc).__name__}: {exc}"}
         extras["loader"] = loader_config()
 
     cpu = None
