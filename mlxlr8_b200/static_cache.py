@@ -15,9 +15,19 @@ stream their bytes (twice the bytes of K4 codes, one conversion per two
 weights instead of the trellis codec) in the codec path's MMA order, so the
 outputs are bit-equal to the uncached decode, as the reference's test of the
 cache requires (``test_static_cache.py``).
+
+``fixed_hot_lists`` picks the cached experts from a routing trace
+(``tools/static_cache_routes.py``): the most frequent routed experts of a
+training split, scored on a held-out split; ``python -m
+mlxlr8_b200.static_cache TRACE --output OUT`` writes the lists.
 """
 
 from __future__ import annotations
+
+import argparse
+import json
+from collections import Counter
+from pathlib import Path
 
 import numpy as np
 import torch
@@ -98,3 +108,76 @@ class StaticExpertCache:
         return {"expert_ids": list(self.expert_ids),
                 "weight_bytes": sum(t.numel() for t in self.fp8.values()),
                 "map_bytes": self.expert_to_slot.numel() * 4}
+
+
+def _hit_counts(rows, hot, shared):
+    """Selections served by the cache in ``rows`` (lists of expert ids)."""
+    cached = set(hot)
+    hits = routed_hits = full_rows = 0
+    for row in rows:
+        inside = [e in cached for e in row]
+        hits += sum(inside)
+        routed_hits += sum(1 for e, hit in zip(row, inside) if hit and e != shared)
+        full_rows += all(inside)
+    return {"hits": hits, "routed_hits": routed_hits, "all_selected_hit_tokens": full_rows}
+
+
+def fixed_hot_lists(trace, split=256, shared=256, capacities=(1, 9, 12, 18)):
+    """Hot-expert lists per layer and capacity from a routing trace
+    (tools/static_cache_routes.py:16-52).
+
+    ``trace["layers"][n]["routes"]`` holds ``2 * split`` rows of selected
+    expert ids.  The first ``split`` rows rank the routed experts by
+    frequency (ties: lowest id); a capacity-``c`` list is the shared expert
+    plus the ``c - 1`` highest ranked.  Each list is scored on both splits
+    (hits, routed hits, rows served entirely from the cache), and the totals
+    over layers carry the hit rates.
+    """
+    sections = ("train", "heldout")
+    fields = ("tokens", "selections", "routed_selections", "hits", "routed_hits", "all_selected_hit_tokens")
+    totals = {name: {str(c): dict.fromkeys(fields, 0) for c in capacities} for name in sections}
+    layers = {}
+    for number, source in trace["layers"].items():
+        routes = source["routes"]
+        if len(routes) != 2 * split:
+            raise ValueError(f"layer {number} needs {2 * split} routes, got {len(routes)}")
+        parts = {"train": routes[:split], "heldout": routes[split:]}
+        frequency = Counter(e for row in parts["train"] for e in row if e != shared)
+        ranked = sorted(frequency, key=lambda e: (-frequency[e], e))
+        layers[number] = {}
+        for capacity in capacities:
+            hot = [shared] + ranked[:capacity - 1]
+            entry = {"expert_ids": hot}
+            for name in sections:
+                rows = parts[name]
+                counts = _hit_counts(rows, hot, shared)
+                entry[name] = counts
+                total = totals[name][str(capacity)]
+                total["tokens"] += len(rows)
+                total["selections"] += sum(len(row) for row in rows)
+                total["routed_selections"] += sum(1 for row in rows for e in row if e != shared)
+                for key, value in counts.items():
+                    total[key] += value
+            layers[number][str(capacity)] = entry
+    for section in totals.values():
+        for total in section.values():
+            total["hit_rate"] = total["hits"] / total["selections"]
+            total["routed_hit_rate"] = total["routed_hits"] / total["routed_selections"]
+            total["all_selected_hit_token_rate"] = total["all_selected_hit_tokens"] / total["tokens"]
+    return {"train_tokens_per_layer": split, "heldout_tokens_per_layer": split, "shared_expert": shared,
+            "tie_break": "lowest expert ID", "totals": totals, "layers": layers}
+
+
+def main(argv=None):
+    parser = argparse.ArgumentParser(description="Choose fixed hot experts from a routing trace.")
+    parser.add_argument("trace")
+    parser.add_argument("--output", required=True)
+    args = parser.parse_args(argv)
+    result = fixed_hot_lists(json.loads(Path(args.trace).read_text()))
+    result["source"] = args.trace
+    Path(args.output).write_text(json.dumps(result, separators=(",", ":")) + "\n")
+    print(json.dumps(result["totals"], indent=2))
+
+
+if __name__ == "__main__":
+    main()

@@ -62,3 +62,39 @@ def test_fast_expert_mlp_takes_cache_bytes_and_map_together():
         fast_expert_mlp(x, ids, {}, {}, 4, 256, 384, fp8={"gate": x, "up": x, "down": x})
     with pytest.raises(ValueError, match="gate, up and down"):
         fast_expert_mlp(x, ids, {}, {}, 4, 256, 384, fp8={"gate": x}, expert_to_slot=ids)
+
+
+def test_hot_lists_use_train_routes_only_and_break_ties_by_id():
+    """tools/static_cache_routes.py via test_static_cache.py's trace."""
+    from mlxlr8_b200.static_cache import fixed_hot_lists
+
+    trace = {"layers": {"3": {"routes": [[8, 4, 256], [4, 8, 256], [17, 8, 256], [17, 4, 256]]}}}
+    result = fixed_hot_lists(trace, split=2, capacities=(1, 2, 3))
+    assert result["layers"]["3"]["2"]["expert_ids"] == [256, 4]
+    assert result["layers"]["3"]["3"]["expert_ids"] == [256, 4, 8]
+    assert result["totals"]["heldout"]["3"]["hit_rate"] == 4 / 6
+    assert result["totals"]["heldout"]["3"]["routed_hit_rate"] == 2 / 4
+    assert result["totals"]["heldout"]["1"]["all_selected_hit_token_rate"] == 0
+    assert result["totals"]["train"]["3"]["all_selected_hit_token_rate"] == 1
+
+
+def test_hot_lists_require_a_complete_split():
+    from mlxlr8_b200.static_cache import fixed_hot_lists
+
+    with pytest.raises(ValueError, match="needs 2 routes"):
+        fixed_hot_lists({"layers": {"3": {"routes": [[0, 256]]}}}, split=1)
+
+
+def test_hot_list_command_writes_the_lists(tmp_path, capsys):
+    import json
+
+    from mlxlr8_b200.static_cache import main
+
+    routes = [[e % 5, (e + 1) % 5, 256] for e in range(512)]
+    (tmp_path / "trace.json").write_text(json.dumps({"layers": {"5": {"routes": routes}}}))
+    main([str(tmp_path / "trace.json"), "--output", str(tmp_path / "hot.json")])
+    result = json.loads((tmp_path / "hot.json").read_text())
+    assert result["layers"]["5"]["9"]["expert_ids"][:1] == [256]
+    assert len(result["layers"]["5"]["9"]["expert_ids"]) == 6  # five routed ids in the trace
+    assert result["source"].endswith("trace.json")
+    assert "heldout" in capsys.readouterr().out
