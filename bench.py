@@ -33,11 +33,17 @@ combine go over peer memory (NVLink stores + epoch flags; `--ep-exchange nccl`
 for the NCCL all-to-all) inside each layer's CUDA graph; time is the max over
 ranks.  (`--tokens 8 --gpus 8` is configs[3]'s batch of 64 per layer.)
 
-Single-GPU extras: decode at T = 8 and 32, the prefill configurations
-(configs[2] joined MXFP4 at 4096 tokens, configs[4] 128 tokens at K4 and K3),
-and the MoE block stack (the layers plus the K3 layer-78 block, each behind its
-post-attention RMS norm, attention stubbed) at T = 1 and at T = 128 with
-Zipf(1.1)-skewed routing.
+Single-GPU extras:
+- decode at T = 8 and 32;
+- the prefill configurations: configs[2], joined MXFP4 at 4096 tokens;
+  configs[4], 128 tokens at K4 and K3;
+- the MoE block stack: the layers plus the K3 layer-78 block, each behind its
+  post-attention RMS norm, attention stubbed; at T = 1, and at T = 128 with
+  Zipf(1.1)-skewed routing;
+- the joined MXFP4 decode;
+- the load-time trellis -> MXFP4 re-encode;
+- the static hot-expert cache against the codes;
+- the checkpoint load.
 """
 
 from __future__ import annotations
