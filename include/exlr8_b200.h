@@ -128,6 +128,12 @@ int exlr8_dequantize_trellis(const void* packed, int64_t packed_bytes, const voi
                              int scale_dtype, int k, int in_features, int out_features, int sharded_side,
                              float* weight, void* workspace, size_t workspace_bytes, void* stream);
 
+/* Normalised Hadamard transform in independent 128-value blocks of each row
+ * (exlr8/trellis.py:134-137 _hadamard, mx.hadamard_transform scale
+ * 1/sqrt(128); the reference transform hadamard_reference, trellis.py:67-75).
+ * x, out: float32 [rows][features], features a multiple of 128; out may be x. */
+int exlr8_hadamard128(const float* x, int64_t rows, int features, float* out, void* stream);
+
 /* ---- MXFP4 encode (load time) ------------------------------------------ */
 
 /* MLX quantize(w, mode="mxfp4") (group 32) of float32 rows w [rows][in]:

@@ -99,6 +99,7 @@ _SIGNATURES = {
     "exlr8_moe_layer_noalloc": (c_int, [c_void_p, c_int, c_void_p, c_int64, c_void_p, c_void_p,
                                         POINTER(TrellisExperts), POINTER(DenseExpert), c_void_p, c_void_p, c_void_p,
                                         c_void_p]),
+    "exlr8_hadamard128": (c_int, [c_void_p, c_int64, c_int, c_void_p, c_void_p]),
     "exlr8_mxfp4_quantize": (c_int, [c_void_p, c_int64, c_int, c_void_p, c_void_p, c_void_p]),
     "exlr8_mxfp4_encode_trellis": (c_int, [c_void_p, c_int64, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_int,
                                            c_void_p, c_void_p, c_int64, c_int64, c_void_p]),

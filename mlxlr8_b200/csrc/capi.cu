@@ -144,6 +144,17 @@ int check_experts(const exlr8_trellis_experts* ex, int64_t* matrices) {
   return EXLR8_OK;
 }
 
+}  // namespace
+
+int exlr8::moe_layer_preflight(const exlr8_trellis_experts* ex, int64_t tokens, int64_t* experts) {
+  EXLR8_CHECK(check_experts(ex, experts));
+  if (tokens < 0) return EXLR8_ERR_ROWS;
+  if (tokens > (1 << 20) || tokens * 9 > (1 << 20)) return EXLR8_ERR_UNSUPPORTED;
+  return EXLR8_OK;
+}
+
+namespace {
+
 StreamParams stream_params(const exlr8_trellis_experts* ex, PlanView plan, int counter, int rows) {
   StreamParams sp{};
   sp.plan = plan;
@@ -524,6 +535,13 @@ int exlr8_dequantize_trellis(const void* packed, int64_t packed_bytes, const voi
       launch_dequantize(inner, suh, svh, scale_dtype, in_features, out_features, weight, as_stream(stream)));
 }
 
+int exlr8_hadamard128(const float* x, int64_t rows, int features, float* out, void* stream) {
+  if (rows < 0 || features <= 0 || features % 128) return EXLR8_ERR_DIMS;
+  if (rows == 0) return EXLR8_OK;
+  if (!x || !out) return EXLR8_ERR_ARG;
+  return cuda_status(launch_hadamard128(x, rows * (features / 128), out, as_stream(stream)));
+}
+
 int exlr8_mxfp4_quantize(const float* w, int64_t rows, int in_features, uint32_t* codes, uint8_t* scales,
                          void* stream) {
   if (rows < 0 || in_features <= 0 || in_features % 32) return EXLR8_ERR_DIMS;
@@ -569,6 +587,7 @@ int exlr8_router(const void* x, int x_dtype, int64_t tokens, int hidden, const f
 }
 
 size_t exlr8_expert_linear_workspace(int64_t tokens, int slots, int in_features, int out_features, int64_t experts) {
+  if (!sizes_ok(tokens, slots, in_features, out_features, experts)) return kBadSize;
   const int64_t rows = tokens * slots;
   const Splits sp = linear_splits(in_features);
   return align_up(plan_bytes(static_cast<int>(rows), static_cast<int>(experts))) +
@@ -619,6 +638,7 @@ int exlr8_expert_linear(const void* x, int x_dtype, int per_slot, const uint32_t
 }
 
 size_t exlr8_expert_mlp_workspace(int64_t tokens, int slots, int hidden, int intermediate, int64_t experts) {
+  if (!sizes_ok(tokens, slots, hidden, intermediate, experts)) return kBadSize;
   const size_t decode = mlp_layout(tokens * slots, hidden, intermediate, experts).total();
   if (tokens < kPrefillMinTokens) return decode;
   const size_t prefill = prefill_bytes(tokens, slots, hidden, intermediate, experts, false);
@@ -678,6 +698,7 @@ int exlr8_expert_mlp_cached(const void* x, int x_dtype, int per_slot, const uint
 }
 
 size_t exlr8_expert_mlp_finish_workspace(int64_t tokens, int hidden, int intermediate, int64_t experts) {
+  if (!sizes_ok(tokens, 9, hidden, intermediate, experts)) return kBadSize;
   const size_t decode = mlp_layout(tokens * 9, hidden, intermediate, experts).total() +
                         dense_layout(tokens, hidden, intermediate).total();
   if (tokens < kPrefillMinTokens) return decode;
@@ -741,6 +762,7 @@ int exlr8_expert_mlp_finish(const void* x, int x_dtype, const uint32_t* indices,
 }
 
 size_t exlr8_moe_layer_workspace(int64_t tokens, int hidden, int intermediate, int64_t experts) {
+  if (!sizes_ok(tokens, 9, hidden, intermediate, experts)) return kBadSize;
   size_t router = align_up(tokens * 256 * sizeof(float)) + align_up(tokens * 9 * sizeof(uint32_t)) +
                   align_up(tokens * 8 * sizeof(float));
   if (tokens >= kRouterGemmMinTokens)
@@ -962,6 +984,8 @@ constexpr int64_t kFusedSharedMaxRows = 4096;  // stream path with dense units u
 
 size_t exlr8_expert_mlp_shared_workspace(int64_t rows, int hidden, int intermediate, int64_t experts,
                                          int64_t shared_tokens) {
+  if (!sizes_ok(rows, 1, hidden, intermediate, experts) || !sizes_ok(shared_tokens, 1, hidden, intermediate, 0))
+    return kBadSize;
   if (rows <= kFusedSharedMaxRows)
     return mlp_layout(rows, hidden, intermediate, experts).total() +
            dense_layout(shared_tokens, hidden, intermediate).total();
@@ -1013,6 +1037,7 @@ int exlr8_expert_mlp_shared(const void* x, int x_dtype, const uint32_t* indices,
 }
 
 size_t exlr8_shared_expert_workspace(int64_t tokens, int hidden, int intermediate) {
+  if (!sizes_ok(tokens, 1, hidden, intermediate, 0)) return kBadSize;
   if (tokens <= 0) return 0;
   if (tokens < kPrefillMinTokens)
     return dense_layout(tokens, hidden, intermediate).total();

@@ -257,7 +257,8 @@ int exlr8_mxfp4_prepare_scales(const uint8_t* scales, int64_t rows, int in_featu
 }
 
 size_t exlr8_joined_workspace(int64_t tokens, int slots, int hidden, int intermediate, int64_t experts) {
-  if (tokens <= 0 || slots <= 0) return 0;
+  if (!sizes_ok(tokens, slots, hidden, intermediate, experts)) return kBadSize;
+  if (tokens <= 0) return 0;
   if (use_joined_stream(tokens)) return joined_decode_layout(tokens * slots, hidden, intermediate, experts).total();
   Carver c(nullptr);
   carve_joined(joined_layout(tokens, slots, experts), hidden, intermediate, experts, c);
@@ -359,6 +360,7 @@ RouterBuffers carve_router(int64_t tokens, int hidden, Carver& c) {
 }
 
 size_t exlr8_joined_moe_layer_workspace(int64_t tokens, int hidden, int intermediate, int64_t experts) {
+  if (!sizes_ok(tokens, 9, hidden, intermediate, experts)) return kBadSize;
   if (tokens <= 0) return 0;
   return exlr8_joined_workspace(tokens, 9, hidden, intermediate, experts) + router_buffers_bytes(tokens, hidden);
 }

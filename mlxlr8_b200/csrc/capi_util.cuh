@@ -67,6 +67,19 @@ inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 inline bool valid_act(int d) { return d == EXLR8_DTYPE_F32 || d == EXLR8_DTYPE_F16 || d == EXLR8_DTYPE_BF16; }
 inline bool valid_scale(int d) { return d == EXLR8_DTYPE_F32 || d == EXLR8_DTYPE_F16; }
 
+// Workspace queries answer kBadSize for sizes that no call accepts, so that
+// a query made before the call's own checks never divides by a zero split
+// count or overflows.  Rows (tokens x slots) are at most 2^20 in every call.
+constexpr size_t kBadSize = ~static_cast<size_t>(0);
+inline bool sizes_ok(int64_t tokens, int64_t slots, int a, int b, int64_t experts) {
+  return tokens >= 0 && slots > 0 && tokens <= (1 << 20) && slots <= 64 && tokens * slots <= (1 << 20) && a > 0 &&
+         b > 0 && a % 128 == 0 && b % 128 == 0 && experts >= 0 && experts <= (1 << 20);
+}
+
+// The checks exlr8_moe_layer makes on its expert struct and token count
+// before sizing anything (capi.cu); writes the matrix count.
+int moe_layer_preflight(const exlr8_trellis_experts* ex, int64_t tokens, int64_t* experts);
+
 constexpr size_t kAlign = 256;
 inline size_t align_up(size_t v) { return (v + kAlign - 1) / kAlign * kAlign; }
 

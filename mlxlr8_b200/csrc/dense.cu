@@ -31,6 +31,26 @@ cudaError_t launch_codebook(const uint32_t* states, float* values, int64_t n, in
   return cudaGetLastError();
 }
 
+// One warp per 128-value block; lane l holds elements l + 32 j, the layout of
+// every in-kernel use of hadamard128.
+__global__ void hadamard128_kernel(const float* __restrict__ x, int64_t blocks, float* __restrict__ out) {
+  const int64_t block = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + threadIdx.x / 32;
+  const int lane = threadIdx.x & 31;
+  if (block >= blocks) return;
+  float v[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) v[j] = x[block * 128 + lane + 32 * j];
+  hadamard128(v, lane);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) out[block * 128 + lane + 32 * j] = v[j];
+}
+
+cudaError_t launch_hadamard128(const float* x, int64_t blocks, float* out, cudaStream_t s) {
+  if (blocks == 0) return cudaSuccess;
+  hadamard128_kernel<<<static_cast<unsigned>((blocks + 7) / 8), 256, 0, s>>>(x, blocks, out);
+  return cudaGetLastError();
+}
+
 // One thread per weight of matrix `expert`: inner[r][c] (decode.metal:9-35).
 __global__ void decode_matrix_kernel(const uint32_t* __restrict__ words, int64_t expert, int k, int in_features,
                                      int out_features, int side, float* __restrict__ inner) {

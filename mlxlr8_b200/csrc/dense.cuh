@@ -11,6 +11,10 @@ cudaError_t launch_codebook(const uint32_t* states, float* values, int64_t n, in
 cudaError_t launch_expand_static(const uint32_t* words, int64_t tiles, int k, uint32_t* out, cudaStream_t s);
 cudaError_t launch_decode_matrix(const uint32_t* words, int64_t expert, int k, int in_features, int out_features,
                                  int side, float* inner, cudaStream_t s);
+// Normalised Hadamard-128 of every 128-value block of `blocks` blocks
+// (float32 in and out; in place allowed): the warp transform the expert
+// kernels apply to their inputs and outputs.
+cudaError_t launch_hadamard128(const float* x, int64_t blocks, float* out, cudaStream_t s);
 cudaError_t launch_dequantize(const float* inner, const void* suh, const void* svh, int scale_dtype,
                               int in_features, int out_features, float* weight, cudaStream_t s);
 

@@ -31,6 +31,8 @@ cudaError_t launch_sum_cast(const float* partial, int splits, int64_t n, int act
 //   [0, 4)          epoch: exchanges this rank has completed
 //   [256, 512)      arrived[src]: epoch + 1 once src's rows for this call landed
 //   [512, 768)      returned[owner]: epoch + 1 once owner's values landed
+//   [768, 1024)     caps[src]: the row capacity C src used for this call (all
+//                   ranks must agree: they pass the same token count)
 //   meta            int32 [ranks][C]: local expert id of each received row, -1 empty
 //   rows            [ranks][C][hidden]: received activation rows
 //   back            [ranks][C][hidden]: slot values returned by each owner
@@ -43,7 +45,7 @@ struct PeerLayout {
 __host__ __device__ inline PeerLayout peer_layout(int ranks, int max_capacity, int hidden, int elem) {
   PeerLayout l;
   const size_t rows_bytes = static_cast<size_t>(ranks) * max_capacity * hidden * elem;
-  l.meta = 768;
+  l.meta = 1024;
   l.rows = l.meta + ((static_cast<size_t>(ranks) * max_capacity * 4 + 255) / 256) * 256;
   l.back = l.rows + ((rows_bytes + 255) / 256) * 256;
   l.total = l.back + ((rows_bytes + 255) / 256) * 256;
@@ -55,7 +57,8 @@ __host__ __device__ inline PeerLayout peer_layout(int ranks, int max_capacity, i
 // launch_ep_dispatch, then the `arrived` flag of this rank in every owner's
 // region; then waits (bounded) until every source's rows for this call have
 // arrived here.  status[0] counts slots lost to capacity overflow, status[1]
-// gets bit 0 when a wait timed out.
+// gets bit 0 when a wait timed out and bit 2 when a source used another
+// capacity (token count) than this rank.
 cudaError_t launch_ep_send(const uint32_t* ids, int tokens, const void* x, int x_dtype, int hidden, int ranks,
                            int rank, int experts_per_rank, int capacity, int max_capacity, const uint64_t* peers,
                            void* local, int32_t* slot_pos, int32_t* status, cudaStream_t s);

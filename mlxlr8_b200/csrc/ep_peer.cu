@@ -45,7 +45,7 @@ __device__ bool wait_epoch(const uint32_t* flag, uint32_t target) {
 }
 
 __device__ __forceinline__ uint32_t* flags_at(unsigned char* region, int which) {
-  return reinterpret_cast<uint32_t*>(region + 256 * which);  // which: 1 arrived, 2 returned
+  return reinterpret_cast<uint32_t*>(region + 256 * which);  // which: 1 arrived, 2 returned, 3 caps
 }
 
 // CTA d sends this rank's rows routed to owner d (slot order) and their local
@@ -109,11 +109,16 @@ __global__ void __launch_bounds__(kPeerThreads) ep_send_kernel(
     const int j = static_cast<int>(idx / row_vecs), v = static_cast<int>(idx % row_vecs);
     rows[static_cast<int64_t>(j) * row_vecs + v] = x[static_cast<int64_t>(s_list[j]) * row_vecs + v];
   }
+  if (tid == 0) flags_at(owner, 3)[rank] = static_cast<uint32_t>(capacity);
   __threadfence_system();
   __syncthreads();
   if (tid == 0) {
     store_release_sys(flags_at(owner, 1) + rank, target);
-    if (!wait_epoch(flags_at(local, 1) + d, target)) atomicOr(&status[1], 1);
+    if (!wait_epoch(flags_at(local, 1) + d, target)) {
+      atomicOr(&status[1], 1);
+    } else if (flags_at(local, 3)[d] != static_cast<uint32_t>(capacity)) {
+      atomicOr(&status[1], 4);  // source d's rows use another stride: its rows are misread
+    }
   }
   __syncthreads();
 }

@@ -28,6 +28,7 @@
 #include <mutex>
 
 #include "../../include/exlr8_b200.h"
+#include "capi_util.cuh"
 
 namespace {
 
@@ -58,10 +59,12 @@ extern "C" int exlr8_moe_layer_noalloc(const void* x, int x_dtype, const void* r
                                        const float* gate_weight, const float* bias,
                                        const exlr8_trellis_experts* experts, const exlr8_dense_expert* shared,
                                        void* out, uint32_t* indices, float* scores, void* stream) {
-  if (experts == nullptr) return EXLR8_ERR_ARG;
-  if (tokens < 0) return EXLR8_ERR_ROWS;
-  const size_t need =
-      exlr8_moe_layer_workspace(tokens, experts->hidden, experts->intermediate, experts->scale_experts);
+  // The struct and the token count are validated before anything is sized
+  // from them, with the same checks and status codes as exlr8_moe_layer.
+  int64_t count = 0;
+  const int checked = exlr8::moe_layer_preflight(experts, tokens, &count);
+  if (checked != EXLR8_OK) return checked;
+  const size_t need = exlr8_moe_layer_workspace(tokens, experts->hidden, experts->intermediate, count);
   if (need > EXLR8_NOALLOC_SCRATCH_BYTES) return EXLR8_ERR_STATIC_LIMIT;
   void* scratch = nullptr;
   const int status = noalloc_scratch(&scratch);

@@ -134,12 +134,22 @@ class PeerExchange:
         self.meta, self.rows, self.back = self.region + meta.value, self.region + rows.value, self.region + back.value
         self.status = torch.zeros(2, dtype=torch.int32, device=device)
         self._group = group
+        self.broken = False
 
     def check(self):
-        """Raise if the last exchange lost slots or a wait for a peer timed out."""
+        """Raise if the last exchange lost slots or a wait for a peer timed out
+        (synchronises the status word to the host).
+
+        After a timeout the ranks' epoch flags no longer agree, so the
+        exchange is marked unusable: later calls raise until it is closed and
+        a new one is created."""
         lost, timeouts = (int(v) for v in self.status.cpu())
-        if timeouts:
-            raise RuntimeError(f"expert-parallel exchange: a wait for a peer timed out (flags {timeouts})")
+        if timeouts & 3:
+            self.broken = True
+            raise RuntimeError(f"expert-parallel exchange: a wait for a peer timed out (flags {timeouts}); "
+                               "the exchange must be re-created")
+        if timeouts & 4:
+            raise RuntimeError("expert-parallel exchange: ranks passed different token counts")
         if lost:
             raise RuntimeError(f"expert-parallel exchange: {lost} routed slots exceeded the capacity")
 
@@ -162,7 +172,14 @@ class PeerExchange:
 class ExpertParallelMoE:
     """One MoE layer with this rank's routed shard (`local`, from
     shard_experts) and a replicated shared expert: the dense bf16 triple
-    `shared`, or the one-expert trellis layer `shared_layer`."""
+    `shared`, or the one-expert trellis layer `shared_layer`.
+
+    With the peer-memory exchange a bounded wait that times out (a peer that
+    stopped) or a capacity overflow leaves partial rows in the output.  Eager
+    calls therefore read the exchange status after every call (`check`, a
+    host synchronisation) and raise; calls made while a CUDA graph is being
+    captured cannot, so whoever replays such a graph must call
+    ``self.peer.check()`` after the replays (bench.py does)."""
 
     def __init__(self, gate_weight, bias, local: ExpertLayer, rank: int, world: int, group=None, shared=None,
                  shared_layer: ExpertLayer | None = None, routed: int = 256, exchange: str = "nccl",
@@ -251,6 +268,8 @@ class ExpertParallelMoE:
         if self.peer is None:
             self.peer = PeerExchange(self.world, self.rank, h, self.max_tokens, xr.dtype, device, self.group)
         peer = self.peer
+        if peer.broken:
+            raise RuntimeError("expert-parallel exchange is unusable after a timed-out wait; re-create the layer")
         lib = _lib.lib()
         stream = _lib.stream_handle(device)
         act = _lib.act_code(xr)
@@ -266,6 +285,8 @@ class ExpertParallelMoE:
         _lib.check(lib.exlr8_ep_combine(peer.back, act, slot_pos.data_ptr(), scores.data_ptr(), shared.data_ptr(),
                                         res.data_ptr(), tokens, h, out.data_ptr(), stream))
         out = out.reshape(residual.shape)
+        if not torch.cuda.is_current_stream_capturing():
+            peer.check()
         if return_routing:
             return out, ids, scores
         return out

@@ -45,6 +45,21 @@ def _ids(indices: torch.Tensor) -> torch.Tensor:
     return indices.contiguous()
 
 
+def _hadamard(x: torch.Tensor) -> torch.Tensor:
+    """Normalised Hadamard transform of each 128-value block of the last axis
+    (exlr8/trellis.py:134-137 ``_hadamard``), computed in float32 on the GPU."""
+    device = _lib.require_cuda(x)
+    features = x.shape[-1]
+    if features % 128:
+        raise ValueError("trellis dimensions must be positive multiples of 128")
+    rows = x.numel() // features if features else 0
+    src = x.to(torch.float32).contiguous()
+    out = torch.empty_like(src)
+    _lib.check(_lib.lib().exlr8_hadamard128(src.data_ptr(), rows, features, out.data_ptr(),
+                                            _lib.stream_handle(device)))
+    return out
+
+
 def mcg_codebook(device=None, paired: bool = False) -> torch.Tensor:
     """All 65,536 codeword values as float16, evaluated by the CUDA decoder.
 

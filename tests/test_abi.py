@@ -68,3 +68,52 @@ def test_operators_fail_loudly_without_cuda(monkeypatch):
     monkeypatch.setattr(torch.cuda, "is_available", lambda: False)
     with pytest.raises(RuntimeError, match="no CPU fallback"):
         trellis.mcg_codebook()
+
+
+def _bad_struct(hidden=6144, intermediate=64, experts=257):
+    """An expert struct whose dimensions no call accepts (intermediate 64)."""
+    st = _lib.TrellisExperts()
+    for i in range(3):
+        st.packed[i] = 16
+        st.packed_bytes[i] = experts * hidden * intermediate // 2
+        st.in_scale[i] = 16
+        st.out_scale[i] = 16
+    st.scale_dtype = 1
+    st.scale_experts = experts
+    st.k = 4
+    st.hidden = hidden
+    st.intermediate = intermediate
+    return st
+
+
+@pytest.mark.parametrize("query, args", [
+    ("exlr8_moe_layer_workspace", (1, 6144, 64, 257)),
+    ("exlr8_moe_layer_workspace", (1, 100, 2048, 257)),
+    ("exlr8_moe_layer_workspace", (-1, 6144, 2048, 257)),
+    ("exlr8_expert_mlp_finish_workspace", (1, 6144, 0, 257)),
+    ("exlr8_expert_mlp_workspace", (1, 9, 6144, 64, 257)),
+    ("exlr8_expert_mlp_workspace", (1, 0, 6144, 2048, 257)),
+    ("exlr8_expert_linear_workspace", (1, 9, 6144, 64, 257)),
+    ("exlr8_shared_expert_workspace", (1, 6144, 64)),
+    ("exlr8_joined_moe_layer_workspace", (1, 6144, 64, 257)),
+])
+def test_workspace_queries_reject_unusable_sizes(query, args):
+    """Sizes no call accepts answer SIZE_MAX instead of dividing by a zero
+    split count (the process used to die with SIGFPE)."""
+    value = getattr(_lib.load(), query)(*args)
+    assert value == ctypes.c_size_t(-1).value
+
+
+def test_noalloc_rejects_a_bad_struct_before_sizing():
+    """A malformed expert struct gets the same status as exlr8_moe_layer
+    (trellis dimensions not multiples of 128), checked on the host before
+    any size is derived from it, so no GPU is needed."""
+    lib = _lib.load()
+    st = _bad_struct()
+    status = lib.exlr8_moe_layer_noalloc(16, 2, 16, 1, 16, 16, ctypes.byref(st), None, 16, None, None, None)
+    assert status == 2
+    assert lib.exlr8_status_string(status).decode() == "trellis dimensions must be positive multiples of 128"
+    assert lib.exlr8_moe_layer_noalloc(16, 2, 16, 1, 16, 16, None, None, 16, None, None, None) == 11
+    good = _bad_struct(hidden=256, intermediate=128)
+    good.scale_experts = 3
+    assert lib.exlr8_moe_layer_noalloc(16, 2, 16, 1, 16, 16, ctypes.byref(good), None, 16, None, None, None) == 5
