@@ -2,7 +2,7 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--tokens T] [--impl {b200,reference}]
 
-Workload (decode): T tokens (default 1) through one MoE
+Workload (single-layer decode, uniform routing): T tokens (default 1) through one MoE
 layer -- router (fp32 gate 6144->256, sigmoid + bias top-8, renormalised x2.5),
 256 routed K4-trellis SwiGLU experts (6144 -> 2048 -> 6144), the bf16 shared
 expert and the combine with the residual.  Weights are seeded synthetic
@@ -444,7 +444,7 @@ def prefill_configs(layer_k4, steps, stream, peak_tflops):
 
 def encode_config(layer, steps, stream):
     """Load-time trellis -> MXFP4 re-encode of one K4 layer's 256 routed
-    experts (SURVEY f2; joined_mxfp4.py:12-47): three fused decode + fold +
+    experts (joined_mxfp4.py:12-47): three fused decode + fold +
     quantise launches (gate and up into the joined [E, 2m, h/8] buffer, then
     down).  Algorithmic bytes: the packed codes and gate/up in-scales read,
     the MXFP4 codes and E8M0 scales written."""
@@ -463,7 +463,7 @@ def encode_config(layer, steps, stream):
 
 
 def static_cache_config(layer, steps, stream):
-    """Static hot-expert cache (static_cache.py): the selected-
+    """Static hot-expert cache (static_cache.py:91-134): the selected-
     expert MLP of one decode token over eight routed experts, all cached as
     exact E4M3 bytes, against the same call decoding their trellis codes.  Two
     disjoint expert sets alternate, so no call finds its weights in L2.
@@ -502,7 +502,7 @@ def static_cache_config(layer, steps, stream):
 
 
 def loader_config():
-    """EXLR8 checkpoint -> device (SURVEY f3; experts.py:77-148): one
+    """EXLR8 checkpoint -> device (experts.py:77-148): one
     full-size K4 layer (256 routed experts + shared, 4.85 GB of codes) written
     to a scratch directory, then ``ExpertStore(resident=True).layer(3)`` timed
     on the host clock around the load (and a device synchronize): read only
@@ -549,7 +549,7 @@ def loader_config():
 
 
 def stack_configs(layers, steps, stream):
-    """The MoE block stack with the attention stubbed: the bench's
+    """The MoE block stack with the attention stubbed (model.py:373-418): the bench's
     layers (K4) plus the K3 layer-78 block, each behind its post-attention RMS
     norm, as one CUDA graph per stack call.  T = 1 (decode) and T = 128 with
     Zipf(1.1)-skewed routing (configs[4], the speculative-verify step)."""
@@ -738,7 +738,7 @@ def main():
     peak, peak_kind = measured_peaks()
     share = {k: round(ms / max(sum(v for _, v in prof.values()), 1e-9), 4) for k, (n, ms) in prof.items()}
 
-    # Whole-step algorithmic bytes (SURVEY decode formula) for context.
+    # Whole-step algorithmic bytes (codes, scales, shared expert, router, activations) for context.
     step_bytes = u_mean * 3 * codes_per_matrix + u_mean * 49152 + 3 * HIDDEN * INTER * 2 + 256 * HIDDEN * 4 + 4 * T * HIDDEN
 
     # ---- e2e through the public API with host buffers ----

@@ -85,7 +85,7 @@ typedef struct exlr8_trellis_experts {
 } exlr8_trellis_experts;
 
 /*
- * Dense bf16 shared expert (the BASELINE layout; the reference keeps the
+ * Dense bf16 shared expert (row-major bf16 weights; the reference keeps the
  * shared expert as trellis matrix 256, experts.py:116-124, which
  * exlr8_trellis_experts also supports).  Row-major [out][in] bf16 matrices:
  * gate/up [intermediate][hidden], down [hidden][intermediate].
@@ -276,7 +276,9 @@ int exlr8_profile_read(int kind, int64_t* launches, double* total_ms);
  * EXLR8_NOALLOC_SCRATCH_BYTES inside the library (held on every GPU that
  * loads it until exit); nothing is allocated.  Requests whose
  * exlr8_moe_layer_workspace() exceeds that size return
- * EXLR8_ERR_STATIC_LIMIT (at GLM-5 size: up to 5 tokens).  The first call on
+ * EXLR8_ERR_STATIC_LIMIT: at GLM-5 size up to 5 tokens fit, and the
+ * grouped-GEMM path (more than 16 tokens) never fits, so calls through this
+ * entry point always take the streaming decode path.  The first call on
  * a device looks up the array's device address; make it before any stream
  * capture.  All calls share the array: calls that overlap on the GPU race
  * and must be serialised by the caller. */

@@ -164,7 +164,7 @@ cudaError_t launch_dequantize(const float* inner, const void* suh, const void* s
 }
 
 // ---------------------------------------------------------------------------
-// bf16 shared expert (the BASELINE layout of the shared expert).
+// bf16 shared expert (row-major bf16 [out][in] weights).
 // ---------------------------------------------------------------------------
 
 constexpr int kDenseWarps = 4;

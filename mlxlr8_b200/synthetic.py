@@ -218,17 +218,79 @@ def joined_host_copy(j: SyntheticJoined, experts=None):
     }
 
 
-def zipf_bias(seed: int, s: float = 1.1, experts: int = 256, strength: float = 0.2, device="cuda"):
-    """Router bias [experts] float32 that skews expert popularity towards a
-    Zipf(s) shape (the speculative-verify step): a seeded
-    random ranking of the experts and bias = -strength * s * log(rank + 1), so
-    the rank-k expert's chance of a top-8 slot falls off roughly as k^-s on
-    top of the gate's own spread."""
+# ---------------------------------------------------------------------------
+# Skewed expert popularity for the speculative-verify workload (128 tokens,
+# Zipf(1.1) expert selection).  The router bias of expert e is
+#   bias_e = -gamma * s * ln(rank_e + 1)
+# over a seeded random ranking of the experts.  gamma is calibrated once by
+# bisection (calibrate_zipf_gamma) so that the top-8 selection frequencies of
+# 10^5 seeded tokens fit Zipf(s): the least-squares slope of log(frequency)
+# against log(rank + 1) over the experts equals -s.  The tokens' logits are
+# drawn from the distribution the synthetic layers produce (x ~ N(0, I),
+# gate weight ~ N(0, 0.02) of seed ZIPF_SEED: logits ~ N(0, W W^T)).
+# ---------------------------------------------------------------------------
+
+ZIPF_S = 1.1
+ZIPF_SEED = 4242
+ZIPF_TOKENS = 100_000
+ZIPF_GAMMA = 0.038376  # calibrate_zipf_gamma() with the defaults above
+
+
+def _zipf_logits(seed: int, tokens: int, hidden: int = 6144, experts: int = 256):
+    import numpy as np
+
+    rng = np.random.default_rng(seed)
+    w = 0.02 * rng.standard_normal((experts, hidden))
+    chol = np.linalg.cholesky(w @ w.T)
+    return (rng.standard_normal((tokens, experts)) @ chol.T).astype(np.float32)
+
+
+def zipf_selection_slope(logits, bias, rank, top_k: int = 8):
+    """(slope, frequencies): per-expert top-k selection frequency of
+    ``sigmoid(logits) + bias`` and its least-squares log-log slope against
+    ``rank + 1`` (experts never selected left out)."""
+    import numpy as np
+
+    choice = 1.0 / (1.0 + np.exp(-np.asarray(logits, np.float64))) + np.asarray(bias, np.float64)[None, :]
+    chosen = np.argpartition(-choice, top_k - 1, axis=1)[:, :top_k]
+    freq = np.bincount(chosen.ravel(), minlength=choice.shape[1]) / choice.shape[0]
+    keep = freq > 0
+    slope = np.polyfit(np.log(np.asarray(rank, np.float64)[keep] + 1.0), np.log(freq[keep]), 1)[0]
+    return float(slope), freq
+
+
+def calibrate_zipf_gamma(seed: int = ZIPF_SEED, tokens: int = ZIPF_TOKENS, s: float = ZIPF_S,
+                         lo: float = 0.0, hi: float = 0.1, tol: float = 1e-5) -> float:
+    """Bisection on gamma in [lo, hi] (the slope falls monotonically there)
+    until the selection slope of ``tokens`` seeded tokens equals -s."""
+    import numpy as np
+
+    logits = _zipf_logits(seed, tokens)
+    rank = np.random.default_rng(seed + 1).permutation(logits.shape[1]).astype(np.float64)
+    while hi - lo > tol:
+        mid = 0.5 * (lo + hi)
+        slope, _ = zipf_selection_slope(logits, -mid * s * np.log(rank + 1.0), rank)
+        if slope > -s:
+            lo = mid
+        else:
+            hi = mid
+    return 0.5 * (lo + hi)
+
+
+def zipf_ranks(seed: int, experts: int = 256, device="cuda"):
+    """Seeded popularity rank of every expert (0 = most popular), float32."""
     device = torch.device(device)
     order = torch.randperm(experts, generator=_gen(seed, device), device=device)
     rank = torch.empty(experts, dtype=torch.float32, device=device)
     rank[order] = torch.arange(experts, dtype=torch.float32, device=device)
-    return (-strength * s * torch.log(rank + 1.0)).float()
+    return rank
+
+
+def zipf_bias(seed: int, s: float = ZIPF_S, experts: int = 256, gamma: float = ZIPF_GAMMA, device="cuda"):
+    """Router bias [experts] float32 giving Zipf(s) expert selection
+    (the calibrated gamma above) over the ranking ``zipf_ranks(seed)``."""
+    rank = zipf_ranks(seed, experts, device)
+    return (-gamma * s * torch.log(rank + 1.0)).float()
 
 
 # ---------------------------------------------------------------------------

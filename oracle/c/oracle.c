@@ -290,9 +290,12 @@ int oracle_moe_layer(const float* x, const float* residual, int tokens, const fl
                      const uint32_t* gate, const uint32_t* up, const uint32_t* down, const void* const* in_scale,
                      const void* const* out_scale, int scale_dtype, int k, int hidden, int inter,
                      const uint16_t* shared_gate, const uint16_t* shared_up, const uint16_t* shared_down, int dtype,
-                     const float* codebook, float* out, uint32_t* ids, float* scores) {
+                     const float* codebook, float* out, uint32_t* ids, float* scores, const float* logits_in) {
+  /* logits_in (optional, [tokens][256]) replaces the float32 gate product,
+   * so that a checker can route from another implementation's logits. */
   float* logits = malloc(sizeof(float) * tokens * 256);
-  oracle_router_logits(x, tokens, hidden, wg, logits);
+  if (logits_in) memcpy(logits, logits_in, sizeof(float) * tokens * 256);
+  else oracle_router_logits(x, tokens, hidden, wg, logits);
   oracle_route(logits, bias, tokens, ids, scores);
   free(logits);
   float* values = malloc(sizeof(float) * (int64_t)tokens * 9 * hidden);

@@ -30,7 +30,7 @@ def lib():
     so.oracle_moe_layer.restype = c_int
     so.oracle_moe_layer.argtypes = [c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                     POINTER(c_void_p), POINTER(c_void_p), c_int, c_int, c_int, c_int, c_void_p,
-                                    c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p]
+                                    c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]
     so.oracle_threads.restype = c_int
     return so
 
@@ -77,8 +77,10 @@ def expert_mlp_rows(x, expert, packed, scales, k, hidden, intermediate, dtype="f
     return out
 
 
-def moe_layer(x, residual, gate_weight, bias, packed, scales, k, hidden, intermediate, shared=None, dtype="bfloat16"):
-    """Whole MoE layer (model.py:385-418); ``shared`` bf16 triple as uint16 bit arrays or None."""
+def moe_layer(x, residual, gate_weight, bias, packed, scales, k, hidden, intermediate, shared=None, dtype="bfloat16",
+              logits=None):
+    """Whole MoE layer (model.py:385-418); ``shared`` bf16 triple as uint16 bit arrays or None.
+    ``logits`` [tokens][256] float32, if given, replaces the oracle's own gate product."""
     x = np.ascontiguousarray(np.asarray(x, np.float32).reshape(-1, hidden))
     residual = np.ascontiguousarray(np.asarray(residual, np.float32).reshape(-1, hidden))
     tokens = x.shape[0]
@@ -90,11 +92,12 @@ def moe_layer(x, residual, gate_weight, bias, packed, scales, k, hidden, interme
     wg = np.ascontiguousarray(gate_weight, np.float32)
     b = np.ascontiguousarray(bias, np.float32)
     sh = [None, None, None] if shared is None else [np.ascontiguousarray(s, np.uint16) for s in shared]
+    lg = None if logits is None else np.ascontiguousarray(np.asarray(logits, np.float32).reshape(tokens, 256))
     st = lib().oracle_moe_layer(_p(x), _p(residual), tokens, _p(wg), _p(b), _p(words[0]), _p(words[1]), _p(words[2]),
                                 ins, outs, code, k, hidden, intermediate,
                                 None if sh[0] is None else _p(sh[0]), None if sh[1] is None else _p(sh[1]),
                                 None if sh[2] is None else _p(sh[2]), DTYPE[dtype], _p(codebook_f32()), _p(out),
-                                _p(ids), _p(scores))
+                                _p(ids), _p(scores), None if lg is None else _p(lg))
     if st:
         raise ValueError("C oracle rejected the arguments")
     return out, ids, scores

@@ -457,7 +457,7 @@ def combine(values, scores, residual, dtype):
 
 
 # ---------------------------------------------------------------------------
-# bf16 shared expert (BASELINE configuration; the reference stores it as
+# bf16 shared expert (dense bf16 weights; the reference stores it as
 # trellis slot 256, experts.py:116-124 -- both forms are supported)
 # ---------------------------------------------------------------------------
 

@@ -3,6 +3,8 @@
 import numpy as np
 import pytest
 
+from oracle import trellis_oracle as ref
+
 pytestmark = pytest.mark.gpu
 
 
@@ -52,3 +54,31 @@ def test_dequantize_rejects_several_matrices(golden):
     s = torch.ones(128, dtype=torch.float16, device="cuda")
     with pytest.raises(ValueError, match="one matrix"):
         dequantize_trellis(packed, s, torch.ones(256, dtype=torch.float16, device="cuda"), 4, 128, 256, 1)
+
+
+def test_hadamard128_bit_exact_against_reference(golden):
+    """The device Hadamard-128 (the transform inside every expert kernel) is
+    bit-identical to the reference's hadamard_reference (trellis.py:67-75)."""
+    import torch
+
+    from mlxlr8_b200.trellis import _hadamard
+
+    x = torch.from_numpy(golden["hadamard_in"]).cuda()
+    out = _hadamard(x).cpu().numpy()
+    np.testing.assert_array_equal(out.view(np.uint32), golden["hadamard_out"].view(np.uint32))
+
+
+def test_hadamard128_large_rows_match_oracle():
+    """Many rows of 6144 values (the hidden width) against the oracle's
+    restatement, bit for bit, and the transform is an involution."""
+    import torch
+
+    from mlxlr8_b200.trellis import _hadamard
+
+    g = torch.Generator(device="cuda")
+    g.manual_seed(5)
+    x = torch.randn(37, 6144, generator=g, device="cuda")
+    out = _hadamard(x)
+    np.testing.assert_array_equal(out.cpu().numpy().view(np.uint32),
+                                  ref.hadamard128(x.cpu().numpy()).view(np.uint32))
+    np.testing.assert_allclose(_hadamard(out).cpu().numpy(), x.cpu().numpy(), atol=3e-6)

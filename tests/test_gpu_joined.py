@@ -284,7 +284,7 @@ def test_decode_finish_and_layer_match_oracle(tokens):
 
 
 def test_decode_glm_shape_one_token():
-    """GLM-5 shape (6144 x 2048, 257 experts) at T = 1, the configs[1] decode
+    """GLM-5 shape (6144 x 2048, 257 experts) at T = 1, the single-token decode
     size on the joined path."""
     import torch
 

@@ -123,30 +123,36 @@ def test_prefill_layer_matches_oracle(tokens, shared):
     assert_prefill_close(host(out) - host(residual), e_out - host(residual))
 
 
+@pytest.mark.parametrize("skew", ["uniform", "zipf"])
 @pytest.mark.parametrize("k", [4, 3])
-def test_glm_prefill_sampled_tokens(k):
-    """GLM shape at the speculative-verify size (128 tokens, configs[4]; K3 is
-    the layer-78 width): the layer runs on the GPU, the C oracle checks the
-    routed experts of sampled tokens (each token's output depends only on its
-    own slots)."""
+def test_glm_prefill_sampled_tokens(k, skew):
+    """GLM shape at the speculative-verify size (128 tokens; K3 is the
+    layer-78 width), with the router's own bias or the calibrated Zipf(1.1)
+    skew (the popular experts then get many rows): the layer runs on the
+    GPU, the C oracle checks the routed experts of sampled tokens (each
+    token's output depends only on its own slots)."""
     import torch
 
     from mlxlr8_b200.fast_router import router_logits
     from mlxlr8_b200.moe import MoELayer
-    from mlxlr8_b200.synthetic import host_copy, make_layer
+    from mlxlr8_b200.synthetic import host_copy, make_layer, zipf_bias
     from oracle import c_oracle
 
     layer = make_layer(seed=23, k=k)
+    bias = zipf_bias(303) if skew == "zipf" else layer.bias
     tokens = 128
     x, residual = layer.tokens(tokens)
-    moe = MoELayer(layer.gate_weight, layer.bias, layer.experts)
+    moe = MoELayer(layer.gate_weight, bias, layer.experts)
     out, ids, scores = moe(x, residual, return_routing=True)
     logits = router_logits(x, layer.gate_weight)
     torch.cuda.synchronize()
     gemm_ok(moe._workspace, tokens, 9, 2048, layer.experts.experts)
-    e_ids, e_scores = ref.route(host(logits), layer.bias.cpu().numpy())
+    e_ids, e_scores = ref.route(host(logits), bias.cpu().numpy())
     np.testing.assert_array_equal(ids.cpu().numpy(), e_ids)
-    sample = np.array([0, 77])
+    if skew == "zipf":
+        counts = np.bincount(e_ids[:, :8].ravel(), minlength=256)
+        assert counts.max() >= 40  # the head experts carry many rows
+    sample = np.array([0, 77, 101])
     hc = host_copy(layer, np.unique(e_ids[sample, :8]))
     xs = host(x)[sample]
     values = np.zeros((sample.size, 9, 6144), np.float32)

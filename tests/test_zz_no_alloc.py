@@ -37,7 +37,8 @@ def _noalloc(lib, moe, x, residual):
     return status, out, ids, scores
 
 
-@pytest.mark.parametrize("hidden, intermediate, tokens", [(256, 128, 3), (6144, 2048, 2)])
+@pytest.mark.parametrize("hidden, intermediate, tokens", [(256, 128, 3), (256, 128, 16), (6144, 2048, 2),
+                                                      (6144, 2048, 5)])
 def test_noalloc_matches_workspace_entry_point_on_two_calls(hidden, intermediate, tokens):
     import torch
     from mlxlr8_b200 import _lib
@@ -58,17 +59,20 @@ def test_noalloc_matches_workspace_entry_point_on_two_calls(hidden, intermediate
         assert_bf16_close(host(out), host(expected))
 
 
-def test_noalloc_refuses_requests_beyond_its_fixed_scratch():
+@pytest.mark.parametrize("hidden, intermediate, tokens", [(6144, 2048, 6), (6144, 2048, 64), (256, 128, 24)])
+def test_noalloc_refuses_requests_beyond_its_fixed_scratch(hidden, intermediate, tokens):
+    """Six tokens at GLM-5 width need 16.5 MB; above 16 tokens the layer takes
+    the grouped-GEMM path, whose workspace (over 100 MB even at width 256)
+    never fits, so that path is never taken through this entry point."""
     import torch
     from mlxlr8_b200 import _lib
     from mlxlr8_b200.moe import MoELayer
     from mlxlr8_b200.synthetic import make_layer
 
     lib = _lib.load()
-    layer = make_layer(seed=22, hidden=6144, intermediate=2048)
+    layer = make_layer(seed=22, hidden=hidden, intermediate=intermediate)
     moe = MoELayer(layer.gate_weight, layer.bias, layer.experts)
-    tokens = 64
-    assert lib.exlr8_moe_layer_workspace(tokens, 6144, 2048, 256) > 16 * 1024 * 1024
+    assert lib.exlr8_moe_layer_workspace(tokens, hidden, intermediate, 256) > 16 * 1024 * 1024
     x, residual = layer.tokens(tokens)
     status, out, _, _ = _noalloc(lib, moe, x, residual)
     assert status == 15
