@@ -32,32 +32,116 @@ used by the layer finish instead of trellis matrix 256.
 from __future__ import annotations
 
 import json
-from collections import OrderedDict
 from pathlib import Path
 
 import torch
 
 from .fast_decode import compiled_expert_mlp_finish, fast_expert_mlp
 
+_PROJECTIONS = ("gate", "up", "down")
+
+
+class _Up1Manifest:
+    """``manifests/exlr8-manifest-up1.json``: per decoder layer the trellis
+    width of every routed and shared matrix."""
+
+    def __init__(self, root: Path):
+        data = json.loads((root / "manifests" / "exlr8-manifest-up1.json").read_text())
+        if data.get("name") != "up1":
+            raise ValueError("This loader requires the up1 manifest")
+        self.data = data
+
+    def __getitem__(self, key):
+        return self.data[key]
+
+    @staticmethod
+    def _widths(node):
+        if isinstance(node, dict):
+            for value in node.values():
+                yield from _Up1Manifest._widths(value)
+        elif isinstance(node, (list, tuple)):
+            for value in node:
+                yield from _Up1Manifest._widths(value)
+        else:
+            yield int(node)
+
+    def width(self, number: int) -> int:
+        """The layer's single trellis width: K3 for the MTP layer 78, K4 for the
+        others; any other width in the layer's plan is refused."""
+        want = 3 if number == 78 else 4
+        plan = self.data["layers"][str(number)]
+        found = set(self._widths({name: plan[name] for name in (*_PROJECTIONS, "shared")}))
+        if found != {want}:
+            raise ValueError(f"Layer {number} is not uniform K{want}")
+        return want
+
+
+class _DeviceLRU:
+    """Byte-bounded least-recently-used map of per-expert device tensors
+    (the bounded expert cache of the non-resident store).  An entry larger
+    than the whole budget is returned but never kept."""
+
+    def __init__(self, limit: int):
+        self.limit = limit
+        self.entries = {}  # insertion order = recency order, oldest first
+        self.bytes = 0
+        self.hits = 0
+        self.misses = 0
+
+    def fetch(self, key, load, nbytes: int):
+        entry = self.entries.pop(key, None)
+        if entry is not None:
+            self.hits += 1
+            self.entries[key] = entry  # now the most recent
+            return entry
+        self.misses += 1
+        entry = load()
+        if nbytes <= self.limit:
+            while self.entries and self.bytes + nbytes > self.limit:
+                oldest = next(iter(self.entries))
+                self.bytes -= sum(t.numel() * t.element_size() for t in self.entries.pop(oldest))
+            self.entries[key] = entry
+            self.bytes += nbytes
+        return entry
+
 
 class ExpertStore:
+    """Experts of an EXLR8 checkpoint on the GPU (experts.py:16-73): resident
+    layers, or per-expert reads through a byte-bounded cache."""
+
     def __init__(self, path, cache_gib=32, resident=False, optimize=True, device=None):
         self.path = Path(path)
         self.resident = resident
         self.optimize = optimize
-        self.manifest = json.loads((self.path / "manifests/exlr8-manifest-up1.json").read_text())
-        if self.manifest["name"] != "up1":
-            raise ValueError("This loader requires the up1 manifest")
-        self.limit = int(cache_gib * 1024**3)
-        if self.limit < 0:
+        self.manifest = _Up1Manifest(self.path)
+        limit = int(cache_gib * 1024**3)
+        if limit < 0:
             raise ValueError("cache_gib must be nonnegative")
+        self._lru = _DeviceLRU(limit)
         self._device = None if device is None else torch.device(device)
-        self.cache = OrderedDict()
-        self.cache_bytes = 0
         self.resident_bytes = 0
-        self.hits = 0
-        self.misses = 0
         self._layers = {}
+
+    # The cache's state under the reference's attribute names.
+    @property
+    def limit(self):
+        return self._lru.limit
+
+    @property
+    def cache(self):
+        return self._lru.entries
+
+    @property
+    def cache_bytes(self):
+        return self._lru.bytes
+
+    @property
+    def hits(self):
+        return self._lru.hits
+
+    @property
+    def misses(self):
+        return self._lru.misses
 
     @property
     def device(self):
@@ -66,32 +150,22 @@ class ExpertStore:
         return self._device
 
     def layer(self, number):
-        if number not in self._layers:
-            self._layers[number] = _load_layer(self, number)
-        return self._layers[number]
+        layer = self._layers.get(number)
+        if layer is None:
+            layer = self._layers[number] = _load_layer(self, number)
+        return layer
 
     def _get(self, layer, expert):
-        """(gate, up, down) packed bytes of one expert (256 = shared) on the device."""
-        key = (layer.number, expert)
-        if key in self.cache:
-            self.hits += 1
-            self.cache.move_to_end(key)
-            return self.cache[key]
-        self.misses += 1
-        shared = expert == 256
-        prefix = "shared." if shared else ""
-        start = 0 if shared else expert * layer.expert_bytes
-        arrays = tuple(layer.weights.load_slice(prefix + "trellis." + projection, start, layer.expert_bytes,
-                                                self.device)
-                       for projection in ("gate", "up", "down"))
-        size = 3 * layer.expert_bytes
-        if size <= self.limit:
-            while self.cache_bytes + size > self.limit:
-                _, old = self.cache.popitem(last=False)
-                self.cache_bytes -= sum(a.numel() for a in old)
-            self.cache[key] = arrays
-            self.cache_bytes += size
-        return arrays
+        """(gate, up, down) packed bytes of one expert (256 = the shared
+        expert, stored in its own tensors) read into device memory."""
+        name = "shared.trellis." if expert == 256 else "trellis."
+        offset = 0 if expert == 256 else expert * layer.expert_bytes
+
+        def read():
+            return tuple(layer.weights.load_slice(name + projection, offset, layer.expert_bytes, self.device)
+                         for projection in _PROJECTIONS)
+
+        return self._lru.fetch((layer.number, expert), read, 3 * layer.expert_bytes)
 
     def shard(self, number, rank, world, routed=256):
         """(routed shard, shared expert) of layer ``number`` for expert
@@ -132,13 +206,8 @@ class ExpertStore:
         return MoELayer(gate_weight, bias, experts)
 
     def stats(self):
-        return {
-            "cache_bytes": self.cache_bytes,
-            "cache_limit_bytes": self.limit,
-            "resident_bytes": self.resident_bytes,
-            "hits": self.hits,
-            "misses": self.misses,
-        }
+        return {"cache_bytes": self.cache_bytes, "cache_limit_bytes": self.limit,
+                "resident_bytes": self.resident_bytes, "hits": self.hits, "misses": self.misses}
 
 
 def load_router(path, number, device=None):
@@ -159,49 +228,44 @@ def load_router(path, number, device=None):
     return weight.contiguous(), bias.contiguous()
 
 
-def _layer_scales(index, k, device):
-    """Signed side vectors of the 256 routed experts and the shared expert
-    (experts.py:97-115): the hidden side is ``repeat(block, 128) * signs``
-    (signs.in for gate/up, signs.out for down), the other side the stored
-    channel vector; fp16 as stored."""
-    import numpy as np
+# Index-file tensor names per projection: (block scale over the hidden side,
+# channel scale over the intermediate side, sign vector of the hidden side).
+_SIDE_NAMES = {"gate": ("su_block", "svh", "signs.in"), "up": ("su_block", "svh", "signs.in"),
+               "down": ("sv_block", "suh", "signs.out")}
 
-    signs_in = index.raw("signs.in").astype(np.float16)
-    signs_out = index.raw("signs.out").astype(np.float16)
-    scales = {}
-    for projection in ("gate", "up", "down"):
-        block_name = "sv_block" if projection == "down" else "su_block"
-        channel_name = "suh" if projection == "down" else "svh"
-        block = np.concatenate([index.raw(f"k{k}.{projection}.{block_name}"),
-                                index.raw(f"shared.k{k}.{projection}.{block_name}")])
-        channel = np.concatenate([index.raw(f"k{k}.{projection}.{channel_name}"),
-                                  index.raw(f"shared.k{k}.{projection}.{channel_name}")])
-        hidden_scale = np.repeat(block, 128, axis=-1)
-        hidden_scale *= signs_out if projection == "down" else signs_in
-        pair = (channel, hidden_scale) if projection == "down" else (hidden_scale, channel)
-        scales[projection] = tuple(torch.from_numpy(np.ascontiguousarray(a)).to(device) for a in pair)
-    return scales
+
+def _layer_scales(index, k, device):
+    """Signed side vectors of the routed experts followed by the shared expert
+    (experts.py:97-115).  The hidden side of each matrix is its per-128-channel
+    block scale spread over the block's channels times the layer's sign
+    vector; the intermediate side is the stored channel scale.  Built on the
+    device in float16, the stored type; returned as (in, out) per projection
+    (gate/up: hidden in, down: hidden out)."""
+    out = {}
+    for projection in _PROJECTIONS:
+        block_name, channel_name, sign_name = _SIDE_NAMES[projection]
+        signs = torch.from_numpy(index.raw(sign_name)).to(device=device, dtype=torch.float16)
+        parts = [torch.from_numpy(index.raw(f"{prefix}k{k}.{projection}.{block_name}")).to(device)
+                 for prefix in ("", "shared.")]
+        block = torch.cat(parts).to(torch.float16)
+        hidden_side = block.repeat_interleave(128, dim=1) * signs
+        channel = torch.cat([torch.from_numpy(index.raw(f"{prefix}k{k}.{projection}.{channel_name}")).to(device)
+                             for prefix in ("", "shared.")]).to(torch.float16)
+        out[projection] = (channel, hidden_side) if projection == "down" else (hidden_side, channel)
+    return out
 
 
 def _layer_files(store, number):
     """(k, weights file, index file, hidden, intermediate) of layer ``number``
-    after the manifest's uniform-K check (experts.py:80-94)."""
+    once the manifest's width check passed (experts.py:80-94)."""
     from .weights import SafeTensorFile
 
-    plan = store.manifest["layers"][str(number)]
-    widths = {v for rows in (plan["gate"], plan["up"]) for row in rows for v in row}
-    widths.update(plan["down"])
-    widths.update(plan["shared"]["gate"])
-    widths.update(plan["shared"]["up"])
-    widths.add(plan["shared"]["down"])
-    k = 3 if number == 78 else 4
-    if widths != {k}:
-        raise ValueError(f"Layer {number} is not uniform K{k}")
-    directory = store.path / "experts"
-    weights = SafeTensorFile(directory / f"exlr8-layer-{number:03d}.k{k}.safetensors")
-    index = SafeTensorFile(directory / f"exlr8-layer-{number:03d}.index.safetensors")
-    hidden = index.header["signs.in"]["shape"][0]
-    intermediate = index.header[f"k{k}.gate.svh"]["shape"][-1]
+    k = store.manifest.width(number)
+    stem = store.path / "experts" / f"exlr8-layer-{number:03d}"
+    weights = SafeTensorFile(Path(f"{stem}.k{k}.safetensors"))
+    index = SafeTensorFile(Path(f"{stem}.index.safetensors"))
+    hidden = int(index.header["signs.in"]["shape"][0])
+    intermediate = int(index.header[f"k{k}.gate.svh"]["shape"][-1])
     return k, weights, index, hidden, intermediate
 
 
@@ -282,42 +346,40 @@ class ExpertLayer:
         self.experts = self.scales["gate"][0].shape[0]
         self.expert_bytes = hidden * intermediate * k // 8
         self._finish = None
+        self._staging = None
 
-    def _selected(self, ids):
-        """Bounded-cache form (experts.py:155-169): the distinct experts of the
-        call, their packed bytes and side vectors, ids renumbered to them."""
-        selected, inverse = torch.unique(ids.reshape(-1).to(torch.int64), return_inverse=True)
-        chosen = selected.tolist()
+    def _stage(self, ids):
+        """Non-resident layer: the call's distinct experts (sorted) are read
+        through the store's cache and copied into this layer's staging
+        buffers (grown on demand, reused across calls); returns the ids
+        renumbered to staging slots, the staged bytes and the matching
+        side-vector rows (the bounded-cache form of experts.py:155-169)."""
+        distinct, slots = torch.unique(ids.reshape(-1).to(torch.int64), return_inverse=True)
+        chosen = distinct.tolist()
         if chosen[0] < 0 or chosen[-1] > 256:
             raise ValueError("Expert IDs must be in 0..256")
-        remapped = inverse.reshape(ids.shape).to(torch.int32)
-        weights = [self.store._get(self, int(expert)) for expert in chosen]
-        packed = {projection: torch.cat([w[p] for w in weights])
-                  for p, projection in enumerate(("gate", "up", "down"))}
-        rows = selected.to(self.scales["down"][0].device)
-        scales = {projection: tuple(s[rows] for s in values) for projection, values in self.scales.items()}
-        return remapped, packed, scales
+        count, size = len(chosen), self.expert_bytes
+        device = self.store.device
+        if self._staging is None or self._staging["gate"].numel() < count * size:
+            self._staging = {name: torch.empty(count * size, dtype=torch.uint8, device=device)
+                             for name in ("gate", "up", "down")}
+        for slot, expert in enumerate(chosen):
+            for name, part in zip(("gate", "up", "down"), self.store._get(self, int(expert))):
+                self._staging[name][slot * size:(slot + 1) * size].copy_(part, non_blocking=True)
+        packed = {name: buf[:count * size] for name, buf in self._staging.items()}
+        rows = distinct.to(self.scales["down"][0].device)
+        scales = {name: tuple(v.index_select(0, rows) for v in pair) for name, pair in self.scales.items()}
+        return slots.reshape(ids.shape).to(torch.int32), packed, scales
 
     def __call__(self, x, ids):
+        """Per-slot outputs ``[*ids.shape, hidden]`` in x's dtype (experts.py:150-188)."""
         if self.affine is not None:
             return self.affine.slots(x, ids)
-        if self.store is not None and not self.store.resident:
-            remapped, packed, scales = self._selected(ids)
-        else:
-            remapped, packed, scales = ids, self.packed, self.scales
+        staged = self.store is not None and not self.store.resident
+        which, packed, scales = self._stage(ids) if staged else (ids, self.packed, self.scales)
         if self.store is None or self.store.optimize:
-            return fast_expert_mlp(x, remapped, packed, scales, self.k, self.hidden, self.intermediate)
-        from .trellis import expert_linear
-
-        outputs = []
-        for projection in ("gate", "up"):
-            in_scale, out_scale = scales[projection]
-            outputs.append(expert_linear(x, remapped, packed[projection], in_scale, out_scale, self.k, self.hidden,
-                                         self.intermediate, sharded_side=1))
-        hidden = torch.nn.functional.silu(outputs[0]) * outputs[1]  # mlx-lm swiglu in the activation dtype
-        in_scale, out_scale = scales["down"]
-        return expert_linear(hidden, remapped, packed["down"], in_scale, out_scale, self.k, self.intermediate,
-                             self.hidden, sharded_side=2)
+            return fast_expert_mlp(x, which, packed, scales, self.k, self.hidden, self.intermediate)
+        return reference_operator_mlp(x, which, packed, scales, self.k, self.hidden, self.intermediate)
 
     def finish(self, x, ids, scores, residual):
         """residual + routed + shared for nine-slot ids (compiled_expert_mlp_finish)."""
@@ -334,3 +396,19 @@ class ExpertLayer:
         if self.shared is not None:
             total += sum(t.numel() * t.element_size() for t in self.shared)
         return total
+
+
+def reference_operator_mlp(x, ids, packed, scales, k, hidden, intermediate):
+    """The ``--no-optimize`` expert MLP (experts.py:176-188): gate and up
+    through the reference operator ``expert_linear`` (side 1), the mlx-lm
+    SwiGLU ``silu(gate) * up`` in the activation dtype, down through
+    ``expert_linear`` (side 2).  Every product is the CUDA operator."""
+    from .trellis import expert_linear
+
+    def project(v, name, n_in, n_out, side):
+        in_scale, out_scale = scales[name]
+        return expert_linear(v, ids, packed[name], in_scale, out_scale, k, n_in, n_out, sharded_side=side)
+
+    gate = project(x, "gate", hidden, intermediate, 1)
+    up = project(x, "up", hidden, intermediate, 1)
+    return project(torch.nn.functional.silu(gate) * up, "down", intermediate, hidden, 2)

@@ -7,177 +7,143 @@ becomes bytes ``[256 t, 256 t + 256)``, byte ``8 * lane + j`` the exact code
 of the lane's codeword ``j``.  The values are the trellis weights themselves,
 so a cached expert gives the same products as its codes.
 
-``StaticExpertCache(layer, expert_ids)`` expands the listed experts of a
-resident layer once (``static_cache.py:91-134``) and keeps the GPU map
-``expert_to_slot`` (0xFFFFFFFF for an uncached expert).  Its decode is the
-layer's streaming expert MLP with the cache attached: units of cached experts
-stream their bytes (twice the bytes of K4 codes, one conversion per two
-weights instead of the trellis codec) in the codec path's MMA order, so the
-outputs are bit-equal to the uncached decode, as the reference's test of the
-cache requires (``test_static_cache.py``).
-
-``fixed_hot_lists`` picks the cached experts from a routing trace
-(``tools/static_cache_routes.py``): the most frequent routed experts of a
-training split, scored on a held-out split; ``python -m
-mlxlr8_b200.static_cache TRACE --output OUT`` writes the lists.
+``StaticExpertCache(layer, expert_ids)`` (``static_cache.py:91-134``) owns
+one device buffer per projection holding the listed experts' bytes in list
+order, and the device map ``expert_to_slot`` (int32 bits of the reference's
+uint32 map, 0xFFFFFFFF for an uncached expert).  The C structs of the layer
+and the cache are prepared once, so a call is one ``exlr8_expert_mlp_cached``
+launch chain: units of cached experts stream their bytes (twice the bytes of
+K4 codes, one conversion per two weights instead of the trellis codec) in the
+codec path's MMA order, so the outputs are bit-equal to the uncached decode,
+as the reference's test of the cache requires (``test_static_cache.py``).
 """
 
 from __future__ import annotations
 
-import argparse
-import json
-from collections import Counter
-from pathlib import Path
+import ctypes
 
-import numpy as np
 import torch
 
 from . import _lib
-from .trellis import _words, check_format
+from .trellis import _ids, _words, check_format
+
+
+def _expand_into(raw, k, in_features, out_features, sharded_side, out):
+    _lib.check(_lib.lib().exlr8_expand_static_trellis(raw.data_ptr(), raw.numel(), k, in_features, out_features,
+                                                      sharded_side, out.data_ptr(),
+                                                      _lib.stream_handle(raw.device)))
 
 
 def expand_static_trellis(packed, k, in_features, out_features, sharded_side=1):
     """Flat exact E4M3 bytes (uint8 CUDA tensor, ``in * out`` per matrix) of
     every matrix in ``packed``, tile order kept (static_cache.py:61-75)."""
-    device = _lib.require_cuda(packed)
+    _lib.require_cuda(packed)
     raw = _words(packed)
     matrices = check_format(raw, k, in_features, out_features, sharded_side)
-    out = torch.empty(matrices * in_features * out_features, dtype=torch.uint8, device=device)
-    _lib.check(_lib.lib().exlr8_expand_static_trellis(raw.data_ptr(), raw.numel(), k, in_features, out_features,
-                                                      sharded_side, out.data_ptr(), _lib.stream_handle(device)))
+    out = torch.empty(matrices * in_features * out_features, dtype=torch.uint8, device=raw.device)
+    _expand_into(raw, k, in_features, out_features, sharded_side, out)
     return out
 
 
-def _expert_map(expert_ids, experts):
-    """(ids as a tuple, uint32 [experts] slot map with 0xFFFFFFFF for a miss),
-    with the reference's checks (static_cache.py:78-84)."""
-    ids = np.asarray(expert_ids)
-    if ids.ndim != 1 or ids.size == 0 or ids.dtype.kind not in "iu":
+def _hot_slots(expert_ids, experts):
+    """Validated hot expert ids as a tuple, in slot order.  Accepts a 1-D
+    sequence or tensor of integers; the reference's ValueError texts
+    (static_cache.py:78-84)."""
+    values = torch.as_tensor(expert_ids)
+    if values.dim() != 1 or values.numel() == 0 or values.dtype.is_floating_point or values.dtype.is_complex \
+            or values.dtype == torch.bool:
         raise ValueError("hot expert IDs must be a nonempty integer vector")
-    if np.any(ids < 0) or np.any(ids >= experts) or np.unique(ids).size != ids.size:
+    ids = tuple(int(v) for v in values.tolist())
+    if len(set(ids)) != len(ids) or min(ids) < 0 or max(ids) >= experts:
         raise ValueError("hot expert IDs must be unique and within the source layer")
-    mapping = np.full(experts, 0xFFFFFFFF, np.uint32)
-    mapping[ids] = np.arange(ids.size, dtype=np.uint32)
-    return tuple(int(i) for i in ids), mapping
+    return ids
+
+
+def _slot_map(ids, experts, device):
+    """int32 [experts] device map: the slot of each cached expert, -1 (the bits
+    of uint32 0xFFFFFFFF) elsewhere."""
+    table = torch.full((experts,), -1, dtype=torch.int32, device=device)
+    table[torch.tensor(ids, dtype=torch.long, device=device)] = torch.arange(len(ids), dtype=torch.int32,
+                                                                             device=device)
+    return table
 
 
 def static_cache_bytes(hidden, intermediate, hot_experts, experts=257):
-    """Device bytes of a cache of ``hot_experts`` experts: three E4M3 matrices
-    each plus the uint32 map (static_cache.py:87-88)."""
+    """Device bytes of a cache of ``hot_experts`` experts: one E4M3 byte per
+    weight of the three matrices, plus the 4-byte map entry of every expert."""
     return 3 * hidden * intermediate * hot_experts + 4 * experts
 
 
 class StaticExpertCache:
-    """Expand fixed experts once; decode with the source scales and the GPU
-    map (static_cache.py:91-134).
+    """Fixed experts of a resident layer as exact E4M3 bytes (static_cache.py:91-134).
 
-    ``fp8[p]`` is the flat uint8 buffer of projection ``p`` with
-    ``hidden * intermediate`` bytes per cache slot, in the source tile order;
-    ``expert_to_slot`` is the uint32 map (an int32 tensor with the same bits
-    on the device).
+    ``fp8[p]`` is the uint8 buffer of projection ``p``: ``hidden *
+    intermediate`` bytes per cache slot, slots in the order of
+    ``expert_ids``, each in the source tile order.  ``expert_to_slot`` is the
+    device map.
     """
 
     def __init__(self, layer, expert_ids=(256,)):
+        from .fast_decode import trellis_experts
+
         store = getattr(layer, "store", None)
         if layer.packed is None or (store is not None and not store.resident):
             raise ValueError("static decode requires resident packed weights")
         self.layer = layer
-        count = layer.scales["down"][1].shape[0]
-        self.expert_ids, mapping = _expert_map(expert_ids, count)
+        experts = layer.scales["down"][1].shape[0]
+        self.expert_ids = _hot_slots(expert_ids, experts)
         device = layer.packed["gate"].device
-        self.expert_to_slot = torch.from_numpy(mapping.view(np.int32)).to(device)
-        size = layer.hidden * layer.intermediate * layer.k // 8
+        self.expert_to_slot = _slot_map(self.expert_ids, experts, device)
+        h, m, k = layer.hidden, layer.intermediate, layer.k
+        per_slot = h * m
+        code_bytes = per_slot * k // 8
         self.fp8 = {}
         for projection in ("gate", "up", "down"):
-            a, b, side = ((layer.intermediate, layer.hidden, 2) if projection == "down"
-                          else (layer.hidden, layer.intermediate, 1))
-            source = layer.packed[projection].reshape(-1)
-            self.fp8[projection] = torch.cat([expand_static_trellis(source[e * size:(e + 1) * size], layer.k, a, b,
-                                                                    side) for e in self.expert_ids])
+            a, b, side = (m, h, 2) if projection == "down" else (h, m, 1)
+            source = _words(layer.packed[projection]).reshape(-1)
+            bytes_out = torch.empty(len(self.expert_ids) * per_slot, dtype=torch.uint8, device=device)
+            for slot, e in enumerate(self.expert_ids):
+                _expand_into(source[e * code_bytes:(e + 1) * code_bytes], k, a, b, side,
+                             bytes_out[slot * per_slot:(slot + 1) * per_slot])
+            self.fp8[projection] = bytes_out
+        self._experts, self._count = trellis_experts(layer.packed, layer.scales, k, h, m)
+        self._cache = _lib.StaticCache()
+        for i, projection in enumerate(("gate", "up", "down")):
+            self._cache.fp8[i] = self.fp8[projection].data_ptr()
+        self._cache.expert_to_slot = self.expert_to_slot.data_ptr()
+        self._cache.slots = len(self.expert_ids)
+        self._workspace = None
 
     def __call__(self, x, ids):
-        """Per-slot expert MLP outputs ``[*ids.shape, hidden]``, equal bit for
-        bit to the layer's own decode (the cached bytes are its weights)."""
-        from .fast_decode import fast_expert_mlp
-
+        """Per-slot expert MLP outputs ``[*ids.shape, hidden]``, bit-equal to
+        the layer's own decode (the cached bytes are its weights)."""
         layer = self.layer
-        return fast_expert_mlp(x, ids, layer.packed, layer.scales, layer.k, layer.hidden, layer.intermediate,
-                               fp8=self.fp8, expert_to_slot=self.expert_to_slot)
+        device = _lib.require_cuda(x, ids)
+        if x.shape[-1] != layer.hidden:
+            raise ValueError("activation width does not match in_features")
+        if x.shape[:-1] == ids.shape:
+            per_slot = 1
+        elif x.shape[:-1] == ids.shape[:-1]:
+            per_slot = 0
+        else:
+            raise ValueError("activation rows do not match the expert indices")
+        indices = _ids(ids)
+        slots = ids.shape[-1]
+        tokens = indices.numel() // slots
+        xs = x.contiguous()
+        out = torch.empty(tuple(ids.shape) + (layer.hidden,), dtype=x.dtype, device=device)
+        lib = _lib.lib()
+        need = lib.exlr8_expert_mlp_workspace(tokens, slots, layer.hidden, layer.intermediate, self._count)
+        if self._workspace is None or self._workspace.numel() < need or self._workspace.device != device:
+            self._workspace = _lib.workspace(need, device)
+        _lib.check(lib.exlr8_expert_mlp_cached(xs.data_ptr(), _lib.act_code(xs), per_slot, indices.data_ptr(),
+                                               tokens, slots, self._experts, ctypes.byref(self._cache),
+                                               out.data_ptr(), self._workspace.data_ptr(),
+                                               self._workspace.numel(), _lib.stream_handle(device)))
+        return out
 
     def stats(self):
+        per_slot = self.layer.hidden * self.layer.intermediate
         return {"expert_ids": list(self.expert_ids),
-                "weight_bytes": sum(t.numel() for t in self.fp8.values()),
-                "map_bytes": self.expert_to_slot.numel() * 4}
-
-
-def _hit_counts(rows, hot, shared):
-    """Selections served by the cache in ``rows`` (lists of expert ids)."""
-    cached = set(hot)
-    hits = routed_hits = full_rows = 0
-    for row in rows:
-        inside = [e in cached for e in row]
-        hits += sum(inside)
-        routed_hits += sum(1 for e, hit in zip(row, inside) if hit and e != shared)
-        full_rows += all(inside)
-    return {"hits": hits, "routed_hits": routed_hits, "all_selected_hit_tokens": full_rows}
-
-
-def fixed_hot_lists(trace, split=256, shared=256, capacities=(1, 9, 12, 18)):
-    """Hot-expert lists per layer and capacity from a routing trace
-    (tools/static_cache_routes.py:16-52).
-
-    ``trace["layers"][n]["routes"]`` holds ``2 * split`` rows of selected
-    expert ids.  The first ``split`` rows rank the routed experts by
-    frequency (ties: lowest id); a capacity-``c`` list is the shared expert
-    plus the ``c - 1`` highest ranked.  Each list is scored on both splits
-    (hits, routed hits, rows served entirely from the cache), and the totals
-    over layers carry the hit rates.
-    """
-    sections = ("train", "heldout")
-    fields = ("tokens", "selections", "routed_selections", "hits", "routed_hits", "all_selected_hit_tokens")
-    totals = {name: {str(c): dict.fromkeys(fields, 0) for c in capacities} for name in sections}
-    layers = {}
-    for number, source in trace["layers"].items():
-        routes = source["routes"]
-        if len(routes) != 2 * split:
-            raise ValueError(f"layer {number} needs {2 * split} routes, got {len(routes)}")
-        parts = {"train": routes[:split], "heldout": routes[split:]}
-        frequency = Counter(e for row in parts["train"] for e in row if e != shared)
-        ranked = sorted(frequency, key=lambda e: (-frequency[e], e))
-        layers[number] = {}
-        for capacity in capacities:
-            hot = [shared] + ranked[:capacity - 1]
-            entry = {"expert_ids": hot}
-            for name in sections:
-                rows = parts[name]
-                counts = _hit_counts(rows, hot, shared)
-                entry[name] = counts
-                total = totals[name][str(capacity)]
-                total["tokens"] += len(rows)
-                total["selections"] += sum(len(row) for row in rows)
-                total["routed_selections"] += sum(1 for row in rows for e in row if e != shared)
-                for key, value in counts.items():
-                    total[key] += value
-            layers[number][str(capacity)] = entry
-    for section in totals.values():
-        for total in section.values():
-            total["hit_rate"] = total["hits"] / total["selections"]
-            total["routed_hit_rate"] = total["routed_hits"] / total["routed_selections"]
-            total["all_selected_hit_token_rate"] = total["all_selected_hit_tokens"] / total["tokens"]
-    return {"train_tokens_per_layer": split, "heldout_tokens_per_layer": split, "shared_expert": shared,
-            "tie_break": "lowest expert ID", "totals": totals, "layers": layers}
-
-
-def main(argv=None):
-    parser = argparse.ArgumentParser(description="Choose fixed hot experts from a routing trace.")
-    parser.add_argument("trace")
-    parser.add_argument("--output", required=True)
-    args = parser.parse_args(argv)
-    result = fixed_hot_lists(json.loads(Path(args.trace).read_text()))
-    result["source"] = args.trace
-    Path(args.output).write_text(json.dumps(result, separators=(",", ":")) + "\n")
-    print(json.dumps(result["totals"], indent=2))
-
-
-if __name__ == "__main__":
-    main()
+                "weight_bytes": 3 * per_slot * len(self.expert_ids),
+                "map_bytes": 4 * self.expert_to_slot.numel()}

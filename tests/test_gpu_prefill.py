@@ -151,7 +151,7 @@ def test_glm_prefill_sampled_tokens(k, skew):
     np.testing.assert_array_equal(ids.cpu().numpy(), e_ids)
     if skew == "zipf":
         counts = np.bincount(e_ids[:, :8].ravel(), minlength=256)
-        assert counts.max() >= 40  # the head experts carry many rows
+        assert counts.max() >= 20  # the head experts carry many rows (~0.24 x 128 for the first)
     sample = np.array([0, 77, 101])
     hc = host_copy(layer, np.unique(e_ids[sample, :8]))
     xs = host(x)[sample]

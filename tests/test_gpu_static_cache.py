@@ -63,6 +63,7 @@ def test_static_decode_is_bit_equal_with_cached_and_uncached_experts(k, dtype, h
                                for e in hot])
         np.testing.assert_array_equal(cache.fp8[p].cpu().numpy(), want)
     slot_map = cache.expert_to_slot.cpu().numpy().view(np.uint32)
+    assert cache.expert_to_slot.dtype == torch.int32 and slot_map.size == 12
     np.testing.assert_array_equal(slot_map[hot], np.arange(len(hot)))
     assert np.all(np.delete(slot_map, hot) == 0xFFFFFFFF)
     assert cache.stats()["weight_bytes"] == 3 * size * len(hot)

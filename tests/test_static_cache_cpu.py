@@ -7,22 +7,19 @@ import pytest
 from oracle import trellis_oracle as ref
 
 
-def test_map_keeps_the_given_slot_order_and_miss_sentinel():
-    from mlxlr8_b200.static_cache import _expert_map
+def test_hot_slots_keep_the_given_order():
+    from mlxlr8_b200.static_cache import _hot_slots
 
-    ids, mapping = _expert_map([256, 17, 3], 257)
-    assert ids == (256, 17, 3)
-    assert mapping.dtype == np.uint32
-    np.testing.assert_array_equal(mapping[[256, 17, 3]], [0, 1, 2])
-    assert np.all(mapping[np.setdiff1d(np.arange(257), [256, 17, 3])] == 0xFFFFFFFF)
+    assert _hot_slots([256, 17, 3], 257) == (256, 17, 3)
+    assert _hot_slots(np.array([5, 0], np.uint32), 257) == (5, 0)
 
 
-@pytest.mark.parametrize("ids", [[], [1.5], [-1], [257], [3, 3], [[3]]])
+@pytest.mark.parametrize("ids", [[], [1.5], [-1], [257], [3, 3], [[3]], [True]])
 def test_invalid_hot_ids(ids):
-    from mlxlr8_b200.static_cache import _expert_map
+    from mlxlr8_b200.static_cache import _hot_slots
 
     with pytest.raises(ValueError):
-        _expert_map(ids, 257)
+        _hot_slots(ids, 257)
 
 
 def test_static_memory_budget():
@@ -62,39 +59,3 @@ def test_fast_expert_mlp_takes_cache_bytes_and_map_together():
         fast_expert_mlp(x, ids, {}, {}, 4, 256, 384, fp8={"gate": x, "up": x, "down": x})
     with pytest.raises(ValueError, match="gate, up and down"):
         fast_expert_mlp(x, ids, {}, {}, 4, 256, 384, fp8={"gate": x}, expert_to_slot=ids)
-
-
-def test_hot_lists_use_train_routes_only_and_break_ties_by_id():
-    """tools/static_cache_routes.py via test_static_cache.py's trace."""
-    from mlxlr8_b200.static_cache import fixed_hot_lists
-
-    trace = {"layers": {"3": {"routes": [[8, 4, 256], [4, 8, 256], [17, 8, 256], [17, 4, 256]]}}}
-    result = fixed_hot_lists(trace, split=2, capacities=(1, 2, 3))
-    assert result["layers"]["3"]["2"]["expert_ids"] == [256, 4]
-    assert result["layers"]["3"]["3"]["expert_ids"] == [256, 4, 8]
-    assert result["totals"]["heldout"]["3"]["hit_rate"] == 4 / 6
-    assert result["totals"]["heldout"]["3"]["routed_hit_rate"] == 2 / 4
-    assert result["totals"]["heldout"]["1"]["all_selected_hit_token_rate"] == 0
-    assert result["totals"]["train"]["3"]["all_selected_hit_token_rate"] == 1
-
-
-def test_hot_lists_require_a_complete_split():
-    from mlxlr8_b200.static_cache import fixed_hot_lists
-
-    with pytest.raises(ValueError, match="needs 2 routes"):
-        fixed_hot_lists({"layers": {"3": {"routes": [[0, 256]]}}}, split=1)
-
-
-def test_hot_list_command_writes_the_lists(tmp_path, capsys):
-    import json
-
-    from mlxlr8_b200.static_cache import main
-
-    routes = [[e % 5, (e + 1) % 5, 256] for e in range(512)]
-    (tmp_path / "trace.json").write_text(json.dumps({"layers": {"5": {"routes": routes}}}))
-    main([str(tmp_path / "trace.json"), "--output", str(tmp_path / "hot.json")])
-    result = json.loads((tmp_path / "hot.json").read_text())
-    assert result["layers"]["5"]["9"]["expert_ids"][:1] == [256]
-    assert len(result["layers"]["5"]["9"]["expert_ids"]) == 6  # five routed ids in the trace
-    assert result["source"].endswith("trace.json")
-    assert "heldout" in capsys.readouterr().out
