@@ -161,7 +161,6 @@ StreamParams stream_params(const exlr8_trellis_experts* ex, PlanView plan, int c
   sp.counter = counter;
   sp.k = ex ? ex->k : 4;
   sp.nslots = rows;
-  sp.unit16 = 65536u;
   sp.mcg_mask = 0x8FFF8FFFu;
   sp.mcg_xor = 0x3B603B60u;
   return sp;
@@ -416,7 +415,6 @@ int prefill_products(const void* x, int x_dtype, int per_slot, int slots, const 
   g.side = 1;
   g.mcg_mask = kMcgMask;
   g.mcg_xor = kMcgXor;
-  g.unit16 = 65536u;
   g.out = b.gu;
   g.out_stride = 2 * m;
   g.proj_offset = m;

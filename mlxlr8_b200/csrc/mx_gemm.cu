@@ -168,20 +168,19 @@ __device__ __forceinline__ uint32_t e4m3_pair_from_products(uint32_t pa, uint32_
 // the SW128 E4M3 image of the weight tile A[o][k]: lane l = 4g + t writes
 // A[g][2t..2t+1], A[g+8][2t..], A[g][2t+8..], A[g+8][2t+8..] (the trellis
 // lane/slot -> (row, col) map of trellis.py:97-99).
-// `unit16` is the runtime value 65536: the high-half extraction becomes an
-// IMAD.HI on the multiply pipe instead of a shift on the integer pipe, which
-// the hash's PRMT/LOP3 work already saturates.
+// The high codeword of each window is a plain shift (a 32-bit multiply-high
+// runs well below the half rate of the other integer operations on B200).
 template <int kK>
 __device__ __forceinline__ void decode_tile(const uint32_t* __restrict__ tile, uint8_t* __restrict__ a_img, int tk,
-                                            int tn, int lane, uint32_t mask, uint32_t xorv, uint32_t unit16,
+                                            int tn, int lane, uint32_t mask, uint32_t xorv,
                                             const GenericGeometry& geo) {
   uint32_t p[4];
   if constexpr (kK == 4) {
     const uint32_t word = tile[lane], prior = tile[(lane + 31) & 31];
     const uint32_t v0 = word, v4 = __funnelshift_r(word, prior, 4);
     const uint32_t v8 = __funnelshift_r(word, prior, 8), v12 = __funnelshift_r(word, prior, 12);
-    const uint32_t ph0 = __umulhi(v0, unit16) * kMcgMul, ph4 = __umulhi(v4, unit16) * kMcgMul;
-    const uint32_t ph8 = __umulhi(v8, unit16) * kMcgMul, ph12 = __umulhi(v12, unit16) * kMcgMul;
+    const uint32_t ph0 = (v0 >> 16) * kMcgMul, ph4 = (v4 >> 16) * kMcgMul;
+    const uint32_t ph8 = (v8 >> 16) * kMcgMul, ph12 = (v12 >> 16) * kMcgMul;
     // Low codeword's product: v * C minus the high codeword's product * 2^16.
     const uint32_t pl0 = v0 * kMcgMul + ph0 * 0xFFFF0000u, pl4 = v4 * kMcgMul + ph4 * 0xFFFF0000u;
     const uint32_t pl8 = v8 * kMcgMul + ph8 * 0xFFFF0000u, pl12 = v12 * kMcgMul + ph12 * 0xFFFF0000u;
@@ -507,7 +506,7 @@ __global__ void __launch_bounds__(GemmTraits<kK>::kThreads, 1)
       const int dw = warp - 7;
       const int tn = dw & 7, acc = dw >> 3;
       const GenericGeometry geo = generic_geometry(kK == 4 ? 3 : kK, lane);
-      const uint32_t mask = g.mcg_mask, xorv = g.mcg_xor, unit16 = g.unit16;
+      const uint32_t mask = g.mcg_mask, xorv = g.mcg_xor;
       for (uint32_t use = 0;; ++use) {
         const int c = use % kCodeStages, s = use % kStages;
         if (!mbar_wait(&sh.codes_full[c], (use / kCodeStages) & 1)) {
@@ -527,7 +526,7 @@ __global__ void __launch_bounds__(GemmTraits<kK>::kThreads, 1)
           uint8_t* img = st + (acc ? T::kOffA1 : T::kOffA0);
 #pragma unroll 4
           for (int tk = 0; tk < 8; ++tk)
-            decode_tile<kK>(codes + (tk * 8 + tn) * (T::kTrellisTile / 4), img, tk, tn, lane, mask, xorv, unit16,
+            decode_tile<kK>(codes + (tk * 8 + tn) * (T::kTrellisTile / 4), img, tk, tn, lane, mask, xorv,
                             geo);
         }
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");

@@ -56,7 +56,6 @@ struct ExpertGemmArgs {
   int trellis_k;                    // 0, 3 or 4
   int side;                         // trellis storage side (1: gate/up, 2: down)
   uint32_t mcg_mask, mcg_xor;       // trellis hash constants (kept in registers for one LOP3)
-  uint32_t unit16;                  // 65536 (see decode_tile)
   float* out;
   int64_t out_stride;               // floats between consecutive rows of out
   int64_t proj_offset;              // column offset of projection 1

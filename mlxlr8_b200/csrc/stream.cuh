@@ -56,7 +56,6 @@ struct StreamParams {
   DenseUnits dense;
   int counter;
   int k, side, in_features, out_features, kt_per_split, splits, projections, nslots;
-  uint32_t unit16;  // 65536
   uint32_t mcg_mask, mcg_xor;  // 0x8FFF8FFF, 0x3B603B60 (runtime values: one LOP3 each)
 };
 
