@@ -1,15 +1,16 @@
-"""Benchmark: one GLM-5-shape routed-MoE layer step (exlr8 MoE branch) on B200.
+"""Benchmark: the GLM-5-shape routed-MoE layer (exlr8 MoE branch) on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--tokens T] [--impl {b200,reference}]
 
-Workload (single-layer decode, uniform routing): T tokens (default 1) through one MoE
-layer -- router (fp32 gate 6144->256, sigmoid + bias top-8, renormalised x2.5),
-256 routed K4-trellis SwiGLU experts (6144 -> 2048 -> 6144), the bf16 shared
-expert and the combine with the residual.  Weights are seeded synthetic
-tensors of that shape (no checkpoints here), one independent layer per step,
-cycling through --layers layers so each step streams weights that are not in
-L2 (every step touches > 233 MB; 8 layers hold ~39 GB).  A "step" is one layer
-pass over one batch of T tokens; the metric is tokens per second.
+Headline (single-layer decode, uniform routing): T tokens per GPU (default 1)
+through one MoE layer -- router (fp32 gate 6144->256, sigmoid + bias top-8,
+renormalised x2.5), 256 routed K4-trellis SwiGLU experts (6144 -> 2048 ->
+6144), the bf16 shared expert and the combine with the residual.  Weights
+are seeded synthetic tensors of that shape (no checkpoints here), one
+independent layer per step, cycling through --layers layers so each step
+streams weights that are not in L2 (every step touches > 233 MB; 8 layers
+hold ~39 GB).  A "step" is one layer pass over one batch; the metric is
+tokens per second.
 
 value: device-resident inputs, the layer call replayed from a CUDA graph.
 e2e:   the public API (MoELayer.__call__) with pinned host buffers: per step
@@ -24,19 +25,29 @@ cpu_baseline: the C restatement of the layer (oracle/c, OpenMP) on the host's
        cores, a bounded number of full layer steps.
 --impl reference: the reference's expert operators are Metal kernels
        (unavailable here), so the reference arm is that same CPU restatement
-       of the reference's arithmetic, on all host threads.
+       of the reference's arithmetic, on all host threads, on the same
+       workload (all GPUs' tokens per step).
 
-Under torchrun (N > 1) the same layers are expert-parallel: each GPU holds
-256 / N routed experts of every layer and the replicated shared expert, takes
-T tokens of its own (global batch T * N, weak scaling), and the dispatch and
-combine go over peer memory (NVLink stores + epoch flags; `--ep-exchange nccl`
-for the NCCL all-to-all) inside each layer's CUDA graph; time is the max over
-ranks.  (`--tokens 8 --gpus 8` is configs[3]'s batch of 64 per layer.)
+Under torchrun (N > 1) the headline layers are expert-parallel: each GPU
+holds 256 / N routed experts of every layer and the replicated shared expert,
+takes T tokens of its own (global batch T * N, weak scaling), and dispatch
+and combine go over peer memory (NVLink stores + epoch flags; `--ep-exchange
+nccl` for the NCCL all-to-all) inside each layer's CUDA graph; time is the
+max over ranks.
+
+ep_stack (every N): the 75-layer expert stack (layers 3-77; attention and the
+three dense layers stubbed) at a fixed global batch of 64 decode tokens
+(strong scaling: 64 / N tokens per GPU), each block a post-attention RMS norm
+and the MoE layer; one CUDA graph per stack step.  One GPU runs the fused
+single-device layer; N > 1 the expert-parallel layer over one shared
+peer-memory exchange.  Where 75 layers of weights do not fit in HBM (N = 1,
+2) the stack cycles the resident layers.  Reported: tokens/s, per-phase
+device times, and the fraction of the per-layer max(HBM, NVLink) time.
 
 Single-GPU extras:
-- decode at T = 8 and 32;
-- the prefill configurations: configs[2], joined MXFP4 at 4096 tokens;
-  configs[4], 128 tokens at K4 and K3;
+- decode at T = 4 (the parity configuration), 8 and 32;
+- the prefill configurations: joined MXFP4 at 4096 tokens; 128 tokens at K4
+  and K3;
 - the MoE block stack: the layers plus the K3 layer-78 block, each behind its
   post-attention RMS norm, attention stubbed; at T = 1, and at T = 128 with
   Zipf(1.1)-skewed routing;
@@ -96,6 +107,12 @@ def parse():
     p.add_argument("--no-extras", action="store_true",
                    help="skip the single-GPU extras (decode at T=8/32, the prefill configurations)")
     p.add_argument("--calls", type=int, default=5)
+    p.add_argument("--no-stack", action="store_true", help="skip the 75-layer expert-parallel stack")
+    p.add_argument("--stack-layers", type=int, default=75)
+    p.add_argument("--stack-batch", type=int, default=64, help="global decode batch of the stack (strong scaling)")
+    p.add_argument("--stack-steps", type=int, default=5)
+    p.add_argument("--stack-budget-gb", type=float, default=110.0,
+                   help="device memory for resident stack layers; beyond it the stack cycles resident layers")
     p.add_argument("--ep-exchange", choices=("peer", "nccl"), default="peer",
                    help="N > 1: the expert-parallel exchange, over peer memory (NVLink stores + epoch flags) or "
                         "NCCL all-to-all")
@@ -173,7 +190,9 @@ def dist_setup():
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+    """nvidia-smi clocks and throttle reasons, sampled every 50 ms from just
+    before the warm-up until after the last timed pass (a short timed region
+    alone would often fall between two samples)."""
 
     QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -182,31 +201,46 @@ class ClockSampler:
     def __init__(self, device_index):
         self.device_index = device_index
         self.proc = None
+        self.lines = []
 
-    def __enter__(self):
+    def start(self):
+        import threading
+
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.device_index}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
-                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                 "-lms", "50"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
+            return self
+        first = threading.Event()
+
+        def reader():
+            for line in self.proc.stdout:
+                if line.strip():
+                    self.lines.append(line)
+                    first.set()
+
+        self.thread = threading.Thread(target=reader, daemon=True)
+        self.thread.start()
+        first.wait(timeout=5.0)  # the first sample lands before the measured work starts
         return self
 
-    def __exit__(self, *exc):
-        self.lines = []
+    def stop(self):
         if self.proc is not None:
             self.proc.terminate()
             try:
-                out, _ = self.proc.communicate(timeout=5)
+                self.proc.wait(timeout=5)
             except subprocess.TimeoutExpired:
                 self.proc.kill()
-                out, _ = self.proc.communicate()
-            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+                self.proc.wait()
+            self.thread.join(timeout=5)
+            self.proc = None
 
     def summary(self):
         sm, mx, reasons = [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in getattr(self, "lines", []):
+        for ln in list(self.lines):
             f = [x.strip() for x in ln.split(",")]
             if len(f) < 9:
                 continue
@@ -220,7 +254,22 @@ class ClockSampler:
                     reasons.add(name)
         if not sm:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons), "samples": len(sm)}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons), "samples": len(sm),
+                "window": "from the warm-up before the timed steps to the end of the e2e pass, every 50 ms"}
+
+
+def workload_config(args, world):
+    """The config of the JSON line: identical in both arms."""
+    T = args.tokens
+    return {"workload": f"decode, T={T} tokens per GPU through one GLM-5-shape MoE layer (router, 256 K4 trellis "
+                        f"experts, bf16 shared expert, combine)",
+            "tokens_per_gpu": T, "global_batch": T * world, "hidden": HIDDEN, "intermediate": INTER,
+            "experts": EXPERTS, "k_bits": K_BITS, "layers_cycled": args.layers,
+            "l2": "inputs larger than L2: each step is a different layer (>233 MB touched per step)",
+            "parallelism": (f"expert parallel x{world}: {EXPERTS // world} routed experts per GPU, "
+                            + ("peer-memory (NVLink) dispatch/combine" if args.ep_exchange == "peer"
+                               else "NCCL all-to-all dispatch/combine")
+                            + ", shared expert replicated") if world > 1 else "single GPU"}
 
 
 def measured_peaks():
@@ -259,7 +308,9 @@ def cpu_baseline(layer, tokens, seconds, warmup=1, steps=None):
 
 
 def reference_arm(args, world, rank):
-    """CPU restatement of the reference operators (the Metal kernels cannot run here)."""
+    """CPU restatement of the reference operators (the Metal kernels cannot
+    run here), on the same workload: each step is all GPUs' tokens of one
+    layer (T * N tokens)."""
     if rank != 0:
         return
     import torch
@@ -270,17 +321,16 @@ def reference_arm(args, world, rank):
     device = "cuda" if torch.cuda.is_available() else "cpu"
     layer = make_layer(seed=1000, device=device)
     budget = 60.0
-    steps_done, dt, warm, cores = cpu_baseline(layer, args.tokens, budget, args.warmup, args.steps)
-    value = steps_done * args.tokens / dt
+    tokens = args.tokens * world
+    steps_done, dt, warm, cores = cpu_baseline(layer, tokens, budget, args.warmup, args.steps)
+    value = steps_done * tokens / dt
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
         "steps": steps_done, "warmup": warm, "ms_per_step": 1000 * dt / steps_done, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": f"decode T={args.tokens}, one GLM-5-shape MoE layer (256 K4 trellis experts + bf16 "
-                               "shared expert)", "tokens": args.tokens, "hidden": HIDDEN, "intermediate": INTER,
-                   "experts": EXPERTS, "k_bits": K_BITS},
+        "config": workload_config(args, world),
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
-                         "sample": f"{steps_done} full layer steps of T={args.tokens} after {warm} warm-up steps "
+                         "sample": f"{steps_done} full layer steps of {tokens} tokens after {warm} warm-up steps "
                                    f"(--steps {args.steps} requested, capped at about {budget:.0f} s)"},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": "exlr8's expert operators are Metal compute kernels (no CPU backend); this arm is the C restatement "
@@ -397,7 +447,31 @@ def joined_decode_configs(steps, stream):
     return res
 
 
-def prefill_configs(layer_k4, steps, stream, peak_tflops):
+def tensor_peaks(device):
+    """tcgen05.mma throughput of the two kinds the GEMMs issue (exlr8_tensor_peak),
+    M = 128, N = 128 and 256, all SMs, dense TFLOP/s."""
+    import ctypes
+
+    import torch
+
+    from mlxlr8_b200 import _lib
+
+    status = torch.zeros(1, dtype=torch.int32, device=device)
+    out = {}
+    for kind, name in ((0, "bf16"), (1, "mxf8f6f4_e4m3")):
+        for n in (128, 256):
+            v = ctypes.c_double(0.0)
+            _lib.check(_lib.lib().exlr8_tensor_peak(kind, n, 20000, ctypes.byref(v), status.data_ptr(),
+                                                     torch.cuda.current_stream(device).cuda_stream))
+            if int(status.item()):
+                raise RuntimeError("tensor peak probe: the bounded wait timed out")
+            out[f"{name}_n{n}_tflops"] = v.value
+    out["note"] = ("tcgen05.mma issued back to back from shared tiles on every SM (kind::f16 bf16 and "
+                   "kind::mxf8f6f4.block_scale E4M3 x E4M3), CUDA events; no clock or power changes")
+    return out
+
+
+def prefill_configs(layer_k4, steps, stream, peak_tflops, mx_peak_tflops=None):
     """configs[2] (joined MXFP4, 4096 tokens) and configs[4] (128 tokens, K4 and the K3 layer-78 width)."""
     import torch
 
@@ -424,6 +498,11 @@ def prefill_configs(layer_k4, steps, stream, peak_tflops):
         "useful_tflops": flops / (ms / 1000.0) / 1e12,
         "gemm_ms": gemm_ms, "gemm_useful_tflops": flops / (gemm_ms / 1000.0) / 1e12,
         "gemm_frac_of_bf16_peak": flops / (gemm_ms / 1000.0) / 1e12 / peak_tflops,
+        "mxf8f6f4_peak_tflops": mx_peak_tflops,
+        "gemm_frac_of_mxf8f6f4_peak_useful": (flops / (gemm_ms / 1000.0) / 1e12 / mx_peak_tflops
+                                              if mx_peak_tflops else None),
+        "gemm_frac_of_mxf8f6f4_peak_issued": (2 * flops / (gemm_ms / 1000.0) / 1e12 / mx_peak_tflops
+                                              if mx_peak_tflops else None),
         "kernel_ms": {k: v[1] for k, v in prof.items() if v[0]},
         "note": "block-scaled tcgen05 MMA (kind::mxf8f6f4, E2M1 weights x E4M3 hi/lo activations); useful FLOPs "
                 "count each product once (the hi/lo planes issue twice as many MMA FLOPs)"}
@@ -590,6 +669,200 @@ def stack_configs(layers, steps, stream):
     return res
 
 
+def measured_bandwidths():
+    """(HBM GB/s, kind) and the peer-store figure used for NVLink."""
+    hbm, kind = measured_peaks()
+    return hbm, kind
+
+
+def peer_store_bandwidth(world, rank, device, nbytes=256 << 20, reps=20):
+    """Per-direction NVLink store bandwidth: every rank writes `nbytes` into
+    the next rank's buffer (CUDA IPC mapping, 16-byte SM stores, the exchange
+    kernels' store path) at the same time; GB/s per GPU, min over ranks."""
+    import ctypes
+
+    import torch
+    import torch.distributed as dist
+
+    from mlxlr8_b200 import _lib
+
+    lib = _lib.lib()
+    region = ctypes.c_void_p()
+    handle = (ctypes.c_ubyte * 64)()
+    _lib.check(lib.exlr8_ep_peer_create(nbytes, ctypes.byref(region), handle))
+    mine = torch.tensor(list(bytes(handle)), dtype=torch.uint8, device=device)
+    handles = [torch.empty_like(mine) for _ in range(world)]
+    dist.all_gather(handles, mine)
+    nxt = (rank + 1) % world
+    theirs = (ctypes.c_ubyte * 64).from_buffer_copy(bytes(handles[nxt].cpu().tolist()))
+    peer = ctypes.c_void_p()
+    _lib.check(lib.exlr8_ep_peer_open(theirs, ctypes.byref(peer)))
+    src = torch.empty(nbytes, dtype=torch.uint8, device=device).fill_(rank)
+    stream = torch.cuda.current_stream(device).cuda_stream
+    for _ in range(3):
+        _lib.check(lib.exlr8_peer_write(peer.value, src.data_ptr(), nbytes, stream))
+    torch.cuda.synchronize()
+    dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        _lib.check(lib.exlr8_peer_write(peer.value, src.data_ptr(), nbytes, stream))
+    e1.record()
+    e1.synchronize()
+    gbs = torch.tensor([nbytes * reps / (e0.elapsed_time(e1) / 1000.0) / 1e9], device=device)
+    dist.all_reduce(gbs, op=dist.ReduceOp.MIN)
+    torch.cuda.synchronize()
+    dist.barrier()
+    _lib.check(lib.exlr8_ep_peer_close(peer.value))
+    dist.barrier()
+    _lib.check(lib.exlr8_ep_peer_destroy(region.value))
+    return float(gbs.item())
+
+
+def ep_stack(args, world, rank, device, stream):
+    """The 75-layer expert stack at a fixed global batch (strong scaling)."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    from mlxlr8_b200 import _lib
+    from mlxlr8_b200.fast_router import router
+    from mlxlr8_b200.stack import MoEStack, residual_rms_norm
+    from mlxlr8_b200.synthetic import make_shard
+
+    G = args.stack_batch
+    if G % world:
+        return {"error": f"global batch {G} does not divide over {world} GPUs"}
+    T = G // world
+    per = EXPERTS // world
+    codes = HIDDEN * INTER * K_BITS // 8
+    per_layer = per * 3 * codes + per * 49152 + 3 * HIDDEN * INTER * 2 + 256 * HIDDEN * 4
+    resident = max(1, min(args.stack_layers, int(args.stack_budget_gb * 1e9 // per_layer)))
+    shards = [make_shard(seed=5000 + 31 * i, rank=rank, world=world, device=device) for i in range(resident)]
+    peer = None
+    if world == 1:
+        from mlxlr8_b200.moe import MoELayer
+
+        moes = [MoELayer(sh.gate_weight, sh.bias, sh.experts) for sh in shards]
+    else:
+        from mlxlr8_b200.ep import ExpertParallelMoE, PeerExchange
+
+        peer = PeerExchange(world, rank, HIDDEN, T, torch.bfloat16, device)
+        moes = [ExpertParallelMoE(sh.gate_weight, sh.bias, sh.experts, rank, world, shared=sh.shared,
+                                  exchange="peer", max_tokens=T, peer=peer) for sh in shards]
+    g = torch.Generator(device=device)
+    g.manual_seed(77)
+    norms = [(1.0 + 0.1 * torch.randn(HIDDEN, generator=g, device=device)).to(torch.bfloat16)
+             for _ in range(args.stack_layers)]
+    stack = MoEStack([(norms[i], moes[i % resident]) for i in range(args.stack_layers)])
+    g.manual_seed(1000 + rank)
+    h0 = torch.randn(T, HIDDEN, generator=g, device=device).to(torch.bfloat16)
+    torch.cuda.synchronize()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    # Eager pass: workspaces, kernel attributes, the exchange's first epochs.
+    stream.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(stream):
+        stack(h0)
+    barrier()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        stack(h0)
+    barrier()
+    with torch.cuda.stream(stream):
+        for _ in range(2):
+            graph.replay()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(args.stack_steps):
+            graph.replay()
+        e1.record(stream)
+    e1.synchronize()
+    barrier()
+    ms = e0.elapsed_time(e1) / args.stack_steps
+    if world > 1:
+        t = torch.tensor([ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        peer.check()
+
+    # Per-phase device time of one eager stack step (events around each library
+    # launch), the max over ranks per phase; and the routing of every block.
+    with torch.cuda.stream(stream):
+        _lib.profile_enable(True, capacity=args.stack_layers * 24 + 64)
+        _, trace = stack(h0, trace=True)
+        torch.cuda.synchronize()
+        prof = _lib.profile_read()
+        _lib.profile_enable(False)
+    kinds = list(prof)
+    phase = torch.tensor([prof[k][1] for k in kinds], dtype=torch.float64, device=device)
+    launches = sum(n for n, _ in prof.values())
+    if world > 1:
+        dist.all_reduce(phase, op=dist.ReduceOp.MAX)
+    phase_ms = {k: round(float(v), 4) for k, v in zip(kinds, phase.tolist()) if v > 0}
+    hbm_bw, hbm_kind = measured_bandwidths()
+    nvl_bw = peer_store_bandwidth(world, rank, device) if world > 1 else None
+    ideal_s, hbm_bytes_total, nvl_bytes_total = 0.0, 0.0, 0.0
+    u_owned = []
+    for i in range(min(resident, args.stack_layers)):
+        _, xn, _ = trace[i]
+        sh = shards[i]
+        ids = router(xn, sh.gate_weight, sh.bias)[1][:, :8].contiguous()
+        if world > 1:
+            parts = [torch.empty_like(ids) for _ in range(world)]
+            dist.all_gather(parts, ids)
+            every = torch.stack(parts).cpu().numpy()  # [src rank][token][8]
+        else:
+            every = ids.cpu().numpy()[None]
+        owner = every // per
+        worst = 0.0
+        for r in range(world):
+            mine = np.unique(every[owner == r])
+            u_owned.append(len(mine))
+            hbm = len(mine) * (3 * codes + 49152) + 3 * HIDDEN * INTER * 2 + 256 * HIDDEN * 4 + 4 * T * HIDDEN
+            # rows r sends to other owners plus rows others send to r, each way one bf16 row
+            sent = int(((owner[r] != r)).sum())
+            received = int(sum(((owner[q] == r)).sum() for q in range(world) if q != r))
+            nvl = (sent + received) * HIDDEN * 2
+            t_hbm = hbm / (hbm_bw * 1e9)
+            t_nvl = nvl / (nvl_bw * 1e9) if nvl_bw else 0.0
+            worst = max(worst, t_hbm, t_nvl)
+            hbm_bytes_total += hbm
+            nvl_bytes_total += nvl
+        ideal_s += worst
+    layers_sampled = min(resident, args.stack_layers)
+    ideal_step_ms = ideal_s / layers_sampled * args.stack_layers * 1000.0
+    del graph, stack, moes, shards, trace
+    torch.cuda.synchronize()
+    if peer is not None:
+        peer.close()
+    torch.cuda.empty_cache()
+    return {
+        "tokens_per_s": G / (ms / 1000.0), "ms_per_step": ms, "global_batch": G, "tokens_per_gpu": T,
+        "layers": args.stack_layers, "resident_layers": resident,
+        "layers_note": ("all layers resident" if resident >= args.stack_layers else
+                        f"{resident} distinct layers resident (75 do not fit at {per} experts per GPU); the stack cycles "
+                        "them, each layer > L2, so no step reuses cached weights"),
+        "steps": args.stack_steps, "scaling": "strong",
+        "parallelism": (f"expert parallel x{world}, {per} routed experts per GPU, peer-memory exchange"
+                        if world > 1 else "single GPU, fused layer (grouped GEMM path at 64 tokens)"),
+        "phase_ms_per_step": phase_ms, "library_launches_per_step": launches,
+        "roofline": {"ideal_ms_per_step": ideal_step_ms, "frac": ideal_step_ms / ms,
+                     "hbm_gbs": hbm_bw, "hbm_kind": hbm_kind, "nvlink_store_gbs": nvl_bw,
+                     "owned_experts_touched_mean": float(np.mean(u_owned)),
+                     "owned_experts_touched_max": int(np.max(u_owned)),
+                     "definition": "per layer max over ranks of max(HBM bytes / HBM GB/s, NVLink bytes / peer-store "
+                                   "GB/s); HBM bytes = owned experts touched x 3 K4 matrices + scales + shared expert + "
+                                   "router + activations; NVLink bytes = bf16 rows this rank sends and receives"},
+    }
+
+
 def main():
     args = parse()
     if args.ncu_driver:
@@ -677,18 +950,18 @@ def main():
         torch.cuda.synchronize()
 
     # ---- headline: graph replay, device-resident inputs ----
+    clocks = ClockSampler(local).start()
     with torch.cuda.stream(stream):
         for s in range(args.warmup):
             step(s)
     barrier()
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clocks:
-        with torch.cuda.stream(stream):
-            start.record(stream)
-            for s in range(args.steps):
-                step(s)
-            stop.record(stream)
-        stop.synchronize()
+    with torch.cuda.stream(stream):
+        start.record(stream)
+        for s in range(args.steps):
+            step(s)
+        stop.record(stream)
+    stop.synchronize()
     barrier()
     elapsed = start.elapsed_time(stop)
     if world > 1:
@@ -772,15 +1045,22 @@ def main():
     e2e_value = world * T * e2e_steps / (e2e_ms / 1000.0)
     h2d = 2 * T * HIDDEN * 2
     d2h = T * HIDDEN * 2
+    clocks.stop()
 
     extras = {}
     if world == 1 and not args.no_extras:
-        extras["decode_batches"] = decode_batches(layers, moes, [8, 32], min(args.steps, 200), stream)
+        extras["decode_batches"] = decode_batches(layers, moes, [4, 8, 32], min(args.steps, 200), stream)
         bf16_peak = 1645.3
         peaks_path = ROOT / "MEASURED_PEAKS.json"
         if peaks_path.exists():
             bf16_peak = float(json.loads(peaks_path.read_text()).get("bf16_tflops", bf16_peak))
-        extras["prefill"] = prefill_configs(layers[0], 10, stream, bf16_peak)
+        try:
+            extras["tensor_peaks"] = tensor_peaks(device)
+            mx_peak = extras["tensor_peaks"]["mxf8f6f4_e4m3_n256_tflops"]
+        except Exception as exc:  # noqa: BLE001 - reported in the JSON line
+            extras["tensor_peaks"] = {"error": f"{type(exc).__name__}: {exc}"}
+            mx_peak = None
+        extras["prefill"] = prefill_configs(layers[0], 10, stream, bf16_peak, mx_peak)
         extras["stack"] = stack_configs(layers, 20, stream)
         extras["joined_decode"] = joined_decode_configs(min(args.steps, 200), stream)
         extras["encode"] = encode_config(layers[0], 5, stream)
@@ -789,6 +1069,27 @@ def main():
         except Exception as exc:  # noqa: BLE001 - reported in the JSON line
             extras["static_cache"] = {"error": f"{type(exc).__name__}: {exc}"}
         extras["loader"] = loader_config()
+
+    if not args.no_stack:
+        # The headline's layers and graphs make room for the stack's resident layers.
+        graphs.clear()
+        outs.clear()
+        for m in moes:
+            if getattr(m, "peer", None) is not None:
+                m.peer.close()
+        del moes[:]
+        if world > 1:
+            del layers[:]
+        else:
+            del layers[1:]
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
+        try:
+            extras["ep_stack"] = ep_stack(args, world, rank, device, stream)
+        except Exception as exc:  # noqa: BLE001 - reported in the JSON line
+            extras["ep_stack"] = {"error": f"{type(exc).__name__}: {exc}"}
+            if world > 1:
+                raise
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -803,16 +1104,7 @@ def main():
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": f"decode T={T} tokens per GPU, one GLM-5-shape MoE layer (256 K4 trellis experts + "
-                                   f"bf16 shared expert, fp32 router)", "tokens_per_gpu": T, "global_batch": T * world,
-                       "hidden": HIDDEN, "intermediate": INTER, "experts": EXPERTS, "k_bits": K_BITS,
-                       "layers_cycled": L,
-                       "l2": "inputs larger than L2: each step is a different layer (>233 MB touched per step)",
-                       "parallelism": (f"expert parallel x{world}: {EXPERTS // world} routed experts per GPU, "
-                                       + ("peer-memory (NVLink) dispatch/combine" if args.ep_exchange == "peer"
-                                          else "NCCL all-to-all dispatch/combine")
-                                       + ", shared expert replicated") if world > 1
-                       else "single GPU"},
+            "config": workload_config(args, world),
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "steps": e2e_steps},
             "roofline": {"bound": "hbm", "kernel": ("trellis_stream_kernel<4> (gate/up" +
@@ -836,7 +1128,7 @@ def main():
     torch.cuda.synchronize()
     if world > 1:
         for m in moes:
-            if getattr(m, "peer", None) is not None:
+            if getattr(m, "peer", None) is not None and m.peer.region is not None:
                 m.peer.close()
         dist.barrier()
         dist.destroy_process_group()

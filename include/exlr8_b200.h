@@ -252,7 +252,11 @@ enum exlr8_kernel_kind {
   EXLR8_KERNEL_DOWN = 5,         /* trellis down streaming GEMV */
   EXLR8_KERNEL_FINISH = 6,       /* output finish / combine */
   EXLR8_KERNEL_DENSE = 7,        /* bf16 shared expert */
-  EXLR8_KERNEL_KINDS = 8
+  EXLR8_KERNEL_EP_SEND = 8,      /* expert-parallel dispatch over peer memory (includes the wait for peers) */
+  EXLR8_KERNEL_EP_RETURN = 9,    /* expert-parallel return over peer memory (includes the wait for owners) */
+  EXLR8_KERNEL_EP_COMBINE = 10,  /* expert-parallel weighted combine */
+  EXLR8_KERNEL_NORM = 11,        /* residual add + RMS norm */
+  EXLR8_KERNEL_KINDS = 12
 };
 
 /* Opt-in per-launch timing (the reference prints per-layer seconds with
@@ -262,6 +266,18 @@ enum exlr8_kernel_kind {
  * events and returns the launch count and total milliseconds of one kind. */
 int exlr8_profile_enable(int enable, int capacity);
 int exlr8_profile_read(int kind, int64_t* launches, double* total_ms);
+
+/* ---- measurement ---------------------------------------------------------- */
+
+/* Tensor-core peak probe, no counterpart in the reference: the throughput
+ * of tcgen05.mma issued back to back on every SM from zero-filled shared
+ * tiles (M = 128, N = n, n a multiple of 16 up to 256), timed with CUDA
+ * events on `stream` (synchronises it).  kind 0: kind::f16 (bf16 x bf16,
+ * float32 accumulation); kind 1: kind::mxf8f6f4.block_scale (E4M3 x E4M3,
+ * E8M0 scales), the kind the block-scaled GEMMs issue.  Writes dense
+ * TFLOP/s; status (device int32) is non-zero if the bounded wait for the
+ * tensor pipe timed out. */
+int exlr8_tensor_peak(int kind, int n, int iters, double* tflops, int32_t* status, void* stream);
 
 /* ---- no-allocation variant ------------------------------------------------ */
 
@@ -369,6 +385,13 @@ int exlr8_ep_send(const uint32_t* indices, int64_t tokens, const void* x, int x_
                   int32_t* status, void* stream);
 int exlr8_ep_return(const void* values, int x_dtype, int hidden, int ranks, int rank, int64_t tokens,
                     int max_capacity, const uint64_t* peers, void* region, int32_t* status, void* stream);
+
+/* Measurement helper, no counterpart in the reference: copies `bytes` (a
+ * multiple of 16) from local device memory to `dst` with the 16-byte SM
+ * stores the exchange kernels use; `dst` may be another GPU's memory mapped
+ * through exlr8_ep_peer_open.  Timing it gives the per-direction NVLink
+ * store bandwidth that bounds the exchange. */
+int exlr8_peer_write(void* dst, const void* src, int64_t bytes, void* stream);
 
 /* Typed output of the dense bf16 shared expert for every token (slot 8 of
  * the combine): T(down(SwiGLU(T(x Wg^T), T(x Wu^T)))). */

@@ -8,7 +8,7 @@ raises if the library is missing or no CUDA device is present.
 from __future__ import annotations
 
 import ctypes
-from ctypes import POINTER, c_char_p, c_float, c_int, c_int64, c_size_t, c_uint32, c_void_p
+from ctypes import c_double, POINTER, c_char_p, c_float, c_int, c_int64, c_size_t, c_uint32, c_void_p
 from functools import lru_cache
 from pathlib import Path
 
@@ -99,6 +99,8 @@ _SIGNATURES = {
     "exlr8_moe_layer_noalloc": (c_int, [c_void_p, c_int, c_void_p, c_int64, c_void_p, c_void_p,
                                         POINTER(TrellisExperts), POINTER(DenseExpert), c_void_p, c_void_p, c_void_p,
                                         c_void_p]),
+    "exlr8_tensor_peak": (c_int, [c_int, c_int, c_int, POINTER(c_double), c_void_p, c_void_p]),
+    "exlr8_peer_write": (c_int, [c_void_p, c_void_p, c_int64, c_void_p]),
     "exlr8_hadamard128": (c_int, [c_void_p, c_int64, c_int, c_void_p, c_void_p]),
     "exlr8_mxfp4_quantize": (c_int, [c_void_p, c_int64, c_int, c_void_p, c_void_p, c_void_p]),
     "exlr8_mxfp4_encode_trellis": (c_int, [c_void_p, c_int64, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_int,
@@ -215,7 +217,8 @@ def scale_code(t: torch.Tensor) -> int:
         raise ValueError(f"unsupported side-scale dtype {t.dtype}") from None
 
 
-KERNEL_KINDS = ("router", "plan", "prep", "gate_up", "gate_finish", "down", "finish", "dense")
+KERNEL_KINDS = ("router", "plan", "prep", "gate_up", "gate_finish", "down", "finish", "dense", "ep_send",
+                "ep_return", "ep_combine", "norm")
 
 
 def profile_enable(enable: bool, capacity: int = 65536) -> None:

@@ -879,8 +879,10 @@ int exlr8_ep_combine(const void* values, int x_dtype, const int32_t* slot_pos, c
   if (tokens < 0 || hidden <= 0) return EXLR8_ERR_ARG;
   if (tokens == 0) return EXLR8_OK;
   if (!values || !slot_pos || !scores || !shared || !residual || !out) return EXLR8_ERR_ARG;
-  return cuda_status(launch_ep_combine(values, x_dtype, slot_pos, scores, shared, residual, static_cast<int>(tokens),
-                                       hidden, out, as_stream(stream)));
+  EXLR8_TIMED(EXLR8_KERNEL_EP_COMBINE, as_stream(stream),
+              launch_ep_combine(values, x_dtype, slot_pos, scores, shared, residual, static_cast<int>(tokens), hidden,
+                                out, as_stream(stream)));
+  return EXLR8_OK;
 }
 
 // ---- residual add + RMS norm in front of each MoE block ----------------------
@@ -892,8 +894,9 @@ int exlr8_residual_rms_norm(const void* x, const void* residual, const void* wei
   if (rows == 0) return EXLR8_OK;
   if (!x || !weight || !out || !(eps >= 0.0f)) return EXLR8_ERR_ARG;
   if (rows > 0x7fffffff) return EXLR8_ERR_UNSUPPORTED;
-  return cuda_status(launch_residual_rms(x, residual, weight, x_dtype, rows, hidden, eps, h_out, out,
-                                         as_stream(stream)));
+  EXLR8_TIMED(EXLR8_KERNEL_NORM, as_stream(stream),
+              launch_residual_rms(x, residual, weight, x_dtype, rows, hidden, eps, h_out, out, as_stream(stream)));
+  return EXLR8_OK;
 }
 
 // ---- peer-memory exchange of the expert-parallel layer ---------------------
@@ -960,9 +963,19 @@ int exlr8_ep_send(const uint32_t* indices, int64_t tokens, const void* x, int x_
   if (rank < 0 || rank >= ranks || experts_per_rank <= 0) return EXLR8_ERR_ARG;
   if (!peers || !region || !status || (tokens > 0 && (!indices || !x || !slot_pos))) return EXLR8_ERR_ARG;
   if ((x && !aligned16(x)) || !aligned16(region)) return EXLR8_ERR_ALIGN;
-  return cuda_status(launch_ep_send(indices, static_cast<int>(tokens), x, x_dtype, hidden, ranks, rank,
-                                    experts_per_rank, static_cast<int>(tokens * 8), max_capacity, peers, region,
-                                    slot_pos, status, as_stream(stream)));
+  EXLR8_TIMED(EXLR8_KERNEL_EP_SEND, as_stream(stream),
+              launch_ep_send(indices, static_cast<int>(tokens), x, x_dtype, hidden, ranks, rank, experts_per_rank,
+                             static_cast<int>(tokens * 8), max_capacity, peers, region, slot_pos, status,
+                             as_stream(stream)));
+  return EXLR8_OK;
+}
+
+int exlr8_peer_write(void* dst, const void* src, int64_t bytes, void* stream) {
+  if (bytes < 0 || bytes % 16) return EXLR8_ERR_ARG;
+  if (bytes == 0) return EXLR8_OK;
+  if (!dst || !src) return EXLR8_ERR_ARG;
+  if (!aligned16(dst) || !aligned16(src)) return EXLR8_ERR_ALIGN;
+  return cuda_status(launch_peer_write(dst, src, bytes, as_stream(stream)));
 }
 
 int exlr8_ep_return(const void* values, int x_dtype, int hidden, int ranks, int rank, int64_t tokens,
@@ -972,8 +985,10 @@ int exlr8_ep_return(const void* values, int x_dtype, int hidden, int ranks, int 
   if (rank < 0 || rank >= ranks) return EXLR8_ERR_ARG;
   if (!peers || !region || !status || (tokens > 0 && !values)) return EXLR8_ERR_ARG;
   if ((values && !aligned16(values)) || !aligned16(region)) return EXLR8_ERR_ALIGN;
-  return cuda_status(launch_ep_return(values, x_dtype, hidden, ranks, rank, static_cast<int>(tokens * 8),
-                                      max_capacity, peers, region, status, as_stream(stream)));
+  EXLR8_TIMED(EXLR8_KERNEL_EP_RETURN, as_stream(stream),
+              launch_ep_return(values, x_dtype, hidden, ranks, rank, static_cast<int>(tokens * 8), max_capacity, peers,
+                               region, status, as_stream(stream)));
+  return EXLR8_OK;
 }
 
 // ---- owner's half of an expert-parallel layer -----------------------------

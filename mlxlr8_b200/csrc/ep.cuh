@@ -70,4 +70,8 @@ cudaError_t launch_ep_send(const uint32_t* ids, int tokens, const void* x, int x
 cudaError_t launch_ep_return(const void* values, int x_dtype, int hidden, int ranks, int rank, int capacity,
                              int max_capacity, const uint64_t* peers, void* local, int32_t* status, cudaStream_t s);
 
+// 16-byte stores of `bytes` (a multiple of 16) from src to dst (dst may be a
+// peer GPU's memory mapped with CUDA IPC).
+cudaError_t launch_peer_write(void* dst, const void* src, int64_t bytes, cudaStream_t s);
+
 }  // namespace exlr8

@@ -149,6 +149,14 @@ __global__ void __launch_bounds__(kPeerThreads) ep_return_kernel(const uint4* __
   }
 }
 
+// Grid-stride 16-byte copy from local memory to `dst`, which may be another
+// GPU's memory mapped into this process (CUDA IPC): the store path the
+// exchange kernels use, for measuring the per-direction NVLink bandwidth.
+__global__ void peer_write_kernel(uint4* __restrict__ dst, const uint4* __restrict__ src, int64_t vecs) {
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < vecs; i += stride) dst[i] = src[i];
+}
+
 // Runs after the return kernel: this rank's exchanges of the call are done.
 __global__ void ep_epoch_kernel(unsigned char* __restrict__ local) {
   *reinterpret_cast<uint32_t*>(local) += 1u;
@@ -180,6 +188,17 @@ cudaError_t launch_ep_return(const void* values, int x_dtype, int hidden, int ra
   cudaError_t err = cudaGetLastError();
   if (err != cudaSuccess) return err;
   ep_epoch_kernel<<<1, 1, 0, s>>>(static_cast<unsigned char*>(local));
+  return cudaGetLastError();
+}
+
+cudaError_t launch_peer_write(void* dst, const void* src, int64_t bytes, cudaStream_t s) {
+  const int64_t vecs = bytes / 16;
+  if (vecs == 0) return cudaSuccess;
+  int device = 0, sms = 0;
+  cudaError_t err = cudaGetDevice(&device);
+  if (err == cudaSuccess) err = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+  if (err != cudaSuccess) return err;
+  peer_write_kernel<<<sms * 4, 512, 0, s>>>(static_cast<uint4*>(dst), static_cast<const uint4*>(src), vecs);
   return cudaGetLastError();
 }
 

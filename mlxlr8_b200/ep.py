@@ -183,7 +183,7 @@ class ExpertParallelMoE:
 
     def __init__(self, gate_weight, bias, local: ExpertLayer, rank: int, world: int, group=None, shared=None,
                  shared_layer: ExpertLayer | None = None, routed: int = 256, exchange: str = "nccl",
-                 max_tokens: int = 16):
+                 max_tokens: int = 16, peer: "PeerExchange | None" = None):
         if (shared is None) == (shared_layer is None):
             raise ValueError("give exactly one shared expert (dense bf16 or trellis)")
         if routed % world or local.experts != routed // world:
@@ -202,7 +202,15 @@ class ExpertParallelMoE:
         self.exchange_kind = exchange
         self.max_tokens = max_tokens
         self.group = group
-        self.peer = None  # PeerExchange, created on the first call (a collective)
+        # PeerExchange: given (shared by the layers of a stack, which run one
+        # after another on one stream, so one region serves them all: a
+        # source writes the next layer's rows only after the previous
+        # layer's values came back), or created on the first call (a
+        # collective).
+        self.peer = peer
+        if peer is not None and (peer.world != world or peer.rank != rank or peer.hidden != local.hidden
+                                 or peer.max_capacity < max_tokens * 8):
+            raise ValueError("the shared peer exchange does not fit this layer")
         self._side = None
         self._shared_struct = None
         self._owner_ws = None

@@ -87,6 +87,67 @@ def make_layer(seed: int = 0, k: int = 4, hidden: int = 6144, intermediate: int 
     return SyntheticLayer(layer, gate_weight.float(), bias.float(), seed)
 
 
+@dataclass
+class SyntheticShard:
+    """One rank's part of a synthetic layer for expert parallelism: the
+    routed experts [rank * E / world, (rank + 1) * E / world) and the
+    replicated router and bf16 shared expert."""
+    experts: ExpertLayer
+    gate_weight: torch.Tensor
+    bias: torch.Tensor
+    shared: tuple
+    rank: int
+    world: int
+    seed: int
+
+
+def make_shard(seed: int, rank: int = 0, world: int = 1, k: int = 4, hidden: int = 6144, intermediate: int = 2048,
+               routed: int = 256, device="cuda", scale_sigma: float = 0.1) -> SyntheticShard:
+    """Expert-parallel shard of a synthetic layer.  Every routed expert's
+    codes come from their own seed (layer seed, expert, projection), so the
+    shards of all ranks together are the same layer whatever ``world`` is;
+    side scales, router and shared expert are drawn whole and sliced."""
+    if routed % world or not 0 <= rank < world:
+        raise ValueError("routed experts must divide evenly over the ranks")
+    device = torch.device(device)
+    per = routed // world
+    lo = rank * per
+    nbytes = hidden * intermediate * k // 8
+    packed = {}
+    for i, p in enumerate(("gate", "up", "down")):
+        buf = torch.empty(per * nbytes, dtype=torch.uint8, device=device)
+        for j in range(per):
+            e = lo + j
+            buf[j * nbytes:(j + 1) * nbytes] = torch.randint(
+                0, 256, (nbytes,), dtype=torch.uint8, generator=_gen(seed * 7919 + e * 3 + i, device), device=device)
+        packed[p] = buf
+    signs_in = torch.where(torch.rand(hidden, generator=_gen(seed + 20, device), device=device) < 0.5, -1.0, 1.0)
+
+    def mag(rows, cols, sd):
+        return (1.0 + scale_sigma * torch.randn(rows, cols, generator=_gen(sd, device), device=device)).abs()
+
+    def signs(rows, cols, sd):
+        return torch.where(torch.rand(rows, cols, generator=_gen(sd, device), device=device) < 0.5, -1.0, 1.0)
+
+    def rows_of(t):
+        return t[lo:lo + per].contiguous()
+
+    scales = {}
+    for i, p in enumerate(("gate", "up")):
+        inn = (mag(routed, hidden, seed + 21 + i) * signs_in).to(torch.float16)
+        out = (mag(routed, intermediate, seed + 23 + i) * signs(routed, intermediate, seed + 40 + i)).to(torch.float16)
+        scales[p] = (rows_of(inn), rows_of(out))
+    down_in = (mag(routed, intermediate, seed + 25) * signs(routed, intermediate, seed + 42)).to(torch.float16)
+    down_out = (mag(routed, hidden, seed + 26) * signs(routed, hidden, seed + 43)).to(torch.float16)
+    scales["down"] = (rows_of(down_in), rows_of(down_out))
+    shared = tuple((0.02 * torch.randn(*shape, generator=_gen(seed + 30 + i, device), device=device)).to(torch.bfloat16)
+                   for i, shape in enumerate(((intermediate, hidden), (intermediate, hidden), (hidden, intermediate))))
+    gate_weight = (0.02 * torch.randn(256, hidden, generator=_gen(seed + 3, device), device=device)).float()
+    bias = (0.01 * torch.randn(256, generator=_gen(seed + 4, device), device=device)).float()
+    layer = ExpertLayer(packed, scales, k, hidden, intermediate, shared=shared if world == 1 else None)
+    return SyntheticShard(layer, gate_weight, bias, shared, rank, world, seed)
+
+
 def host_copy(layer: SyntheticLayer, experts=None):
     """NumPy copies for CPU checks: packed bytes of the listed experts only
     (others zero-filled, so buffer offsets keep their meaning), all scales,
