@@ -107,6 +107,8 @@ def parse():
     p.add_argument("--no-extras", action="store_true",
                    help="skip the single-GPU extras (decode at T=8/32, the prefill configurations)")
     p.add_argument("--calls", type=int, default=5)
+    p.add_argument("--peaks", action="store_true",
+                   help="print the tensor-core and trellis-codec peak probes of GPU 0 as one JSON line and exit")
     p.add_argument("--no-stack", action="store_true", help="skip the 75-layer expert-parallel stack")
     p.add_argument("--stack-layers", type=int, default=75)
     p.add_argument("--stack-batch", type=int, default=64, help="global decode batch of the stack (strong scaling)")
@@ -466,8 +468,16 @@ def tensor_peaks(device):
             if int(status.item()):
                 raise RuntimeError("tensor peak probe: the bounded wait timed out")
             out[f"{name}_n{n}_tflops"] = v.value
+    sink = torch.zeros(1, dtype=torch.float32, device=device)
+    w = ctypes.c_double(0.0)
+    _lib.check(_lib.lib().exlr8_codec_peak(4000, ctypes.byref(w), sink.data_ptr(),
+                                           torch.cuda.current_stream(device).cuda_stream))
+    out["trellis_codec_weights_per_s"] = w.value
+    out["trellis_codec_k4_code_gbs"] = w.value * K_BITS / 8 / 1e9
     out["note"] = ("tcgen05.mma issued back to back from shared tiles on every SM (kind::f16 bf16 and "
-                   "kind::mxf8f6f4.block_scale E4M3 x E4M3), CUDA events; no clock or power changes")
+                   "kind::mxf8f6f4.block_scale E4M3 x E4M3), CUDA events; the trellis codec figure runs the decode "
+                   "GEMV's inner loop (exact K4 decode + mma.sync) on codes in shared memory at the stream kernel's "
+                   "occupancy: the compute ceiling of the decode; no clock or power changes")
     return out
 
 
@@ -867,6 +877,12 @@ def main():
     args = parse()
     if args.ncu_driver:
         ncu_driver(args)
+        return
+    if args.peaks:
+        import torch
+
+        torch.cuda.set_device(0)
+        print(json.dumps(tensor_peaks(torch.device("cuda", 0))), flush=True)
         return
     world, rank, local = dist_setup()
     if args.impl == "reference":

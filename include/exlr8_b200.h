@@ -279,6 +279,14 @@ int exlr8_profile_read(int kind, int64_t* launches, double* total_ms);
  * tensor pipe timed out. */
 int exlr8_tensor_peak(int kind, int n, int iters, double* tflops, int32_t* status, void* stream);
 
+/* Trellis decode compute probe, no counterpart in the reference: the decode
+ * GEMV's inner loop (exact K4 codec + mma.sync) over codes held in shared
+ * memory, at the streaming kernel's occupancy, timed with CUDA events on
+ * `stream` (synchronises it).  Writes decoded weights per second: the
+ * decode's compute ceiling on this GPU, whatever HBM delivers.  `sink` is a
+ * device float the kernel writes so that the work is kept. */
+int exlr8_codec_peak(int iters, double* weights_per_s, float* sink, void* stream);
+
 /* ---- no-allocation variant ------------------------------------------------ */
 
 /* Size of the fixed device scratch used by exlr8_moe_layer_noalloc. */

@@ -99,6 +99,7 @@ _SIGNATURES = {
     "exlr8_moe_layer_noalloc": (c_int, [c_void_p, c_int, c_void_p, c_int64, c_void_p, c_void_p,
                                         POINTER(TrellisExperts), POINTER(DenseExpert), c_void_p, c_void_p, c_void_p,
                                         c_void_p]),
+    "exlr8_codec_peak": (c_int, [c_int, POINTER(c_double), c_void_p, c_void_p]),
     "exlr8_tensor_peak": (c_int, [c_int, c_int, c_int, POINTER(c_double), c_void_p, c_void_p]),
     "exlr8_peer_write": (c_int, [c_void_p, c_void_p, c_int64, c_void_p]),
     "exlr8_hadamard128": (c_int, [c_void_p, c_int64, c_int, c_void_p, c_void_p]),

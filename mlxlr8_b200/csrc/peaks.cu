@@ -10,10 +10,18 @@
 //   kind 0: kind::f16, bf16 x bf16 -> f32, K = 16 per MMA
 //   kind 1: kind::mxf8f6f4.block_scale, E4M3 x E4M3 with E8M0 scales, K = 32
 // No TMA, no multicast, no global memory traffic.
+//
+// Codec probe: the decode GEMV's inner loop (stream_codec.cuh k4_fragment,
+// the exact E4M3 trellis decode of a K4 tile, and its mma.sync) run on
+// codes held in shared memory, with the stream kernel's occupancy (two CTAs
+// of eight decoding warps per SM), each warp taking eight tiles per step.
+// Its rate in weights per second is the compute ceiling of the trellis
+// decode on this GPU, independent of HBM.
 
 #include <cuda_runtime.h>
 
 #include "capi_util.cuh"
+#include "stream_codec.cuh"
 #include "umma.cuh"
 
 namespace exlr8 {
@@ -76,11 +84,68 @@ __global__ void __launch_bounds__(kPeakThreads, 1) mma_peak_kernel(int kind, int
   if (warp == 0) tmem_free(tmem, kPeakTmemCols);
 }
 
+constexpr int kCodecThreads = 256;
+constexpr int kCodecTiles = 64;  // K4 tiles of 32 words in shared memory
+
+__global__ void __launch_bounds__(kCodecThreads, 2) codec_peak_kernel(int iters, uint32_t seed,
+                                                                      float* __restrict__ sink) {
+  __shared__ uint32_t codes[kCodecTiles * 32];
+  for (int i = threadIdx.x; i < kCodecTiles * 32; i += kCodecThreads)
+    codes[i] = (seed + static_cast<uint32_t>(i)) * 0x9E3779B9u ^ (static_cast<uint32_t>(blockIdx.x) << 16);
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t mask = 0x8FFF8FFFu ^ (seed & 0x10u), xorv = 0x3B603B60u;  // runtime operands, as in the kernel
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  const uint2 b = make_uint2(0x3C003C00u ^ lane, 0x38003800u ^ lane);
+  for (int it = 0; it < iters; ++it) {
+    uint32_t word[8], prior[8];
+#pragma unroll
+    for (int kk = 0; kk < 8; ++kk) {
+      const uint32_t* tile = codes + ((warp * 8 + kk + it) & (kCodecTiles - 1)) * 32;
+      word[kk] = tile[lane];
+      prior[kk] = tile[(lane + 31) & 31];
+    }
+#pragma unroll
+    for (int kk = 0; kk < 8; ++kk) {
+      uint32_t a[4];
+      k4_fragment(word[kk], prior[kk], mask, xorv, a);
+      mma_f16(acc, a, b);
+    }
+  }
+  if (threadIdx.x == 0) sink[0] = acc[0] + acc[1] + acc[2] + acc[3];
+}
+
 }  // namespace
 
 }  // namespace exlr8
 
 using namespace exlr8;
+
+extern "C" int exlr8_codec_peak(int iters, double* weights_per_s, float* sink, void* stream) {
+  if (iters <= 0 || !weights_per_s || !sink) return EXLR8_ERR_ARG;
+  cudaStream_t s = as_stream(stream);
+  int device = 0, sms = 0;
+  EXLR8_TRY(cudaGetDevice(&device));
+  EXLR8_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device));
+  const int grid = 2 * sms;
+  cudaEvent_t e0, e1;
+  EXLR8_TRY(cudaEventCreate(&e0));
+  EXLR8_TRY(cudaEventCreate(&e1));
+  codec_peak_kernel<<<grid, kCodecThreads, 0, s>>>(iters / 10 + 1, 7u, sink);  // warm-up
+  cudaEventRecord(e0, s);
+  codec_peak_kernel<<<grid, kCodecThreads, 0, s>>>(iters, 7u, sink);
+  cudaEventRecord(e1, s);
+  cudaError_t err = cudaGetLastError();
+  if (err == cudaSuccess) err = cudaEventSynchronize(e1);
+  float ms = 0.f;
+  if (err == cudaSuccess) err = cudaEventElapsedTime(&ms, e0, e1);
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  EXLR8_TRY(err);
+  const double weights = static_cast<double>(grid) * (kCodecThreads / 32) * 8.0 * iters * 256.0;
+  *weights_per_s = weights / (ms * 1e-3);
+  return EXLR8_OK;
+}
 
 extern "C" int exlr8_tensor_peak(int kind, int n, int iters, double* tflops, int32_t* status, void* stream) {
   if ((kind != 0 && kind != 1) || n < 16 || n > 256 || n % 16 || iters <= 0 || !tflops || !status)
