@@ -19,10 +19,6 @@ constexpr uint32_t kMcgMul = 0xCBAC1FEDu;
 constexpr uint32_t kMcgMask = 0x8FFF8FFFu;
 constexpr uint32_t kMcgXor = 0x3B603B60u;
 
-__device__ __forceinline__ uint32_t lop_mask_xor(uint32_t v) {
-  return (v & kMcgMask) ^ kMcgXor;
-}
-
 // Round an f16x2 to the nearest E4M3 pair and widen it back to f16x2.
 __device__ __forceinline__ uint32_t round_e4m3_f16x2(uint32_t h2) {
   uint32_t r;
@@ -32,14 +28,27 @@ __device__ __forceinline__ uint32_t round_e4m3_f16x2(uint32_t h2) {
   return r;
 }
 
+// Float16 half sums of two hashed products pa = cw_a * C, pb = cw_b * C,
+// packed as an f16x2 (low half = a): each product is masked as a whole (its
+// two halves are the two float16 numbers of its codeword) and the halves of
+// each product are added, then the two sums are packed.  One mask per
+// product and one pack per pair cost one integer-pipe instruction less per
+// pair than gathering the low and the high halves of both products first,
+// and the float16 additions are the same, so the result is identical.
+__device__ __forceinline__ uint32_t hashed_pair_sum(uint32_t pa, uint32_t pb, uint32_t mask, uint32_t xorv) {
+  uint32_t qa, qb, r;
+  asm("lop3.b32 %0, %1, %2, %3, 0x6A;" : "=r"(qa) : "r"(pa), "r"(mask), "r"(xorv));
+  asm("lop3.b32 %0, %1, %2, %3, 0x6A;" : "=r"(qb) : "r"(pb), "r"(mask), "r"(xorv));
+  asm("{\n .reg .b16 al, ah, bl, bh, sa, sb;\n mov.b32 {al, ah}, %1;\n mov.b32 {bl, bh}, %2;\n"
+      " add.rn.f16 sa, al, ah;\n add.rn.f16 sb, bl, bh;\n mov.b32 %0, {sa, sb};\n}\n"
+      : "=r"(r)
+      : "r"(qa), "r"(qb));
+  return r;
+}
+
 // Values of two 16-bit states as an f16x2 (low half = state a).
 __device__ __forceinline__ uint32_t decode_pair(uint32_t cw_a, uint32_t cw_b) {
-  uint32_t pa = cw_a * kMcgMul;
-  uint32_t pb = cw_b * kMcgMul;
-  uint32_t lo = lop_mask_xor(__byte_perm(pa, pb, 0x5410));  // (pb.lo : pa.lo)
-  uint32_t hi = lop_mask_xor(__byte_perm(pa, pb, 0x7632));  // (pb.hi : pa.hi)
-  __half2 s = __hadd2(*reinterpret_cast<__half2*>(&lo), *reinterpret_cast<__half2*>(&hi));
-  return round_e4m3_f16x2(*reinterpret_cast<uint32_t*>(&s));
+  return round_e4m3_f16x2(hashed_pair_sum(cw_a * kMcgMul, cw_b * kMcgMul, kMcgMask, kMcgXor));
 }
 
 __device__ __forceinline__ float decode_value(uint32_t cw) {

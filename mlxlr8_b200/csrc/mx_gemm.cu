@@ -155,12 +155,8 @@ __device__ __forceinline__ int acc_row(const ExpertGemmArgs& g, const UnitInfo& 
 // E4M3 pair of two hashed products (low byte = a), the exact value of the
 // codewords (fast_decode_common.metal:4-26 exlr8_decode2).
 __device__ __forceinline__ uint32_t e4m3_pair_from_products(uint32_t pa, uint32_t pb, uint32_t mask, uint32_t xorv) {
-  uint32_t lo, hi;
-  asm("lop3.b32 %0, %1, %2, %3, 0x6A;" : "=r"(lo) : "r"(__byte_perm(pa, pb, 0x5410)), "r"(mask), "r"(xorv));
-  asm("lop3.b32 %0, %1, %2, %3, 0x6A;" : "=r"(hi) : "r"(__byte_perm(pa, pb, 0x7632)), "r"(mask), "r"(xorv));
-  __half2 s = __hadd2(*reinterpret_cast<__half2*>(&lo), *reinterpret_cast<__half2*>(&hi));
   uint16_t r;
-  asm("cvt.rn.satfinite.e4m3x2.f16x2 %0, %1;" : "=h"(r) : "r"(*reinterpret_cast<uint32_t*>(&s)));
+  asm("cvt.rn.satfinite.e4m3x2.f16x2 %0, %1;" : "=h"(r) : "r"(hashed_pair_sum(pa, pb, mask, xorv)));
   return r;
 }
 

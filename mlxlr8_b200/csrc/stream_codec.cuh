@@ -30,19 +30,9 @@ __device__ __forceinline__ void mma_f16(float c[4], const uint32_t a[4], uint2 b
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b.x), "r"(b.y));
 }
 
-// (v & mask) ^ xor as a single three-input logic op.
-__device__ __forceinline__ uint32_t lop_and_xor(uint32_t v, uint32_t mask, uint32_t xorv) {
-  uint32_t r;
-  asm("lop3.b32 %0, %1, %2, %3, 0x6A;" : "=r"(r) : "r"(v), "r"(mask), "r"(xorv));
-  return r;
-}
-
-// f16x2 value pair of two hashed products (low half = a).
+// Exact E4M3 values (as f16x2, low half = a) of two hashed products.
 __device__ __forceinline__ uint32_t pair_from_products(uint32_t pa, uint32_t pb, uint32_t mask, uint32_t xorv) {
-  uint32_t lo = lop_and_xor(__byte_perm(pa, pb, 0x5410), mask, xorv);
-  uint32_t hi = lop_and_xor(__byte_perm(pa, pb, 0x7632), mask, xorv);
-  __half2 s = __hadd2(*reinterpret_cast<__half2*>(&lo), *reinterpret_cast<__half2*>(&hi));
-  return round_e4m3_f16x2(*reinterpret_cast<uint32_t*>(&s));
+  return round_e4m3_f16x2(hashed_pair_sum(pa, pb, mask, xorv));
 }
 
 // A fragment of one K4 tile from tile word l and word l-1.  The high

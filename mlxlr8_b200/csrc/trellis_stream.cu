@@ -71,12 +71,18 @@ struct UnitInfo {
   int group, proj, nb, split;
 };
 
-__device__ __forceinline__ UnitInfo decode_unit(int64_t unit, const StreamParams& p, int nblocks) {
+// Unit indices stay below 2^31 (rows <= 2^20, projections <= 2, 128-wide
+// output blocks <= 48 at GLM size, splits <= 16), so 32-bit arithmetic
+// suffices; the producer decodes each unit once and passes its fields to
+// the consumers through shared memory.
+__device__ __forceinline__ UnitInfo decode_unit(uint32_t unit, const StreamParams& p, uint32_t nblocks) {
   UnitInfo u;
-  u.split = static_cast<int>(unit % p.splits);
-  u.nb = static_cast<int>((unit / p.splits) % nblocks);
-  u.proj = static_cast<int>((unit / (static_cast<int64_t>(p.splits) * nblocks)) % p.projections);
-  u.group = static_cast<int>(unit / (static_cast<int64_t>(p.splits) * nblocks * p.projections));
+  const uint32_t splits = static_cast<uint32_t>(p.splits), projections = static_cast<uint32_t>(p.projections);
+  const uint32_t a = unit / splits, b = a / nblocks;
+  u.split = static_cast<int>(unit - a * splits);
+  u.nb = static_cast<int>(a - b * nblocks);
+  u.proj = static_cast<int>(b % projections);
+  u.group = static_cast<int>(b / projections);
   return u;
 }
 
@@ -87,9 +93,11 @@ __global__ void __launch_bounds__(kStreamThreads, 2) trellis_stream_kernel(Strea
   __shared__ __align__(8) uint64_t full_bar[kStages];
   __shared__ __align__(8) uint64_t empty_bar[kStages];
   __shared__ int4 meta[kStages];  // unit, first K tile, K tiles, flags
-  // First stage of a unit: [0] rows of the unit's group, [1 + r] slot of row r
-  // (the consumers read the group from here, not from the global plan).
-  __shared__ int unit_rows[kStages][kMaxGroupRows + 1];
+  // First stage of a unit: [0] rows of the unit's group, [1 + r] slot of row r,
+  // then the unit's projection, output block and split (the consumers read
+  // the unit from here, not from the global plan).
+  constexpr int kUnitProj = kMaxGroupRows + 1, kUnitBlock = kMaxGroupRows + 2, kUnitSplit = kMaxGroupRows + 3;
+  __shared__ int unit_rows[kStages][kMaxGroupRows + 4];
   __shared__ __align__(8) uint64_t dense_bar[kDenseBuffers];
   __shared__ int plan_cache[4][kPlanCache];  // group expert, start, count; slot order (producer)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -159,7 +167,7 @@ __global__ void __launch_bounds__(kStreamThreads, 2) trellis_stream_kernel(Strea
         mbar_arrive(&full_bar[stage]);
         break;
       }
-      const UnitInfo u = decode_unit(unit, p, nblocks);
+      const UnitInfo u = decode_unit(static_cast<uint32_t>(unit), p, static_cast<uint32_t>(nblocks));
       const int expert = cached ? plan_cache[0][u.group] : p.plan.group_expert[u.group];
       const int start = cached ? plan_cache[1][u.group] : p.plan.group_start[u.group];
       const int nr = cached ? plan_cache[2][u.group] : p.plan.group_count[u.group];
@@ -193,6 +201,9 @@ __global__ void __launch_bounds__(kStreamThreads, 2) trellis_stream_kernel(Strea
           unit_rows[stage][0] = nr;
 #pragma unroll
           for (int r = 0; r < kMaxGroupRows; ++r) unit_rows[stage][1 + r] = slots[r];
+          unit_rows[stage][kUnitProj] = u.proj;
+          unit_rows[stage][kUnitBlock] = u.nb;
+          unit_rows[stage][kUnitSplit] = u.split;
         }
         unsigned char* base = smem + stage * G::kStageBytes;
         if (hslot >= 0) {
@@ -256,7 +267,9 @@ __global__ void __launch_bounds__(kStreamThreads, 2) trellis_stream_kernel(Strea
     const int4 m = meta[stage];
     if (m.w & kEnd) break;
     if (m.w & kFirst) {
-      u = decode_unit(m.x, p, nblocks);
+      u.proj = unit_rows[stage][kUnitProj];
+      u.nb = unit_rows[stage][kUnitBlock];
+      u.split = unit_rows[stage][kUnitSplit];
       nr = unit_rows[stage][0];
       ncg = (nr + 3) >> 2;
       slot_a = unit_rows[stage][1 + tig];
