@@ -103,11 +103,15 @@ struct UnitInfo {
   int group, nb, split;
 };
 
-__device__ __forceinline__ UnitInfo decode_unit(int64_t unit, int splits, int nblocks) {
+// Unit indices stay below 2^31, so 32-bit arithmetic suffices; the producer
+// decodes each unit once and hands its fields to the consumers through
+// shared memory.
+__device__ __forceinline__ UnitInfo decode_unit(uint32_t unit, uint32_t splits, uint32_t nblocks) {
   UnitInfo u;
-  u.split = static_cast<int>(unit % splits);
-  u.nb = static_cast<int>((unit / splits) % nblocks);
-  u.group = static_cast<int>(unit / (static_cast<int64_t>(splits) * nblocks));
+  const uint32_t a = unit / splits;
+  u.split = static_cast<int>(unit - a * splits);
+  u.group = static_cast<int>(a / nblocks);
+  u.nb = static_cast<int>(a - static_cast<uint32_t>(u.group) * nblocks);
   return u;
 }
 
@@ -118,7 +122,9 @@ __global__ void __launch_bounds__(kJThreads, 2) joined_stream_kernel(const __gri
   __shared__ __align__(8) uint64_t full_bar[kJStages];
   __shared__ __align__(8) uint64_t empty_bar[kJStages];
   __shared__ int4 meta[kJStages];  // unit, first K block, K blocks (1 or 2), flags
-  __shared__ int unit_rows[kJStages][kMaxGroupRows + 1];
+  // First stage of a unit: rows, slots, then the unit's output block and split.
+  constexpr int kUnitBlock = kMaxGroupRows + 1, kUnitSplit = kMaxGroupRows + 2;
+  __shared__ int unit_rows[kJStages][kMaxGroupRows + 3];
   __shared__ int plan_cache[4][kJPlanCache];
   // The 128-byte swizzle repeats every 1024 bytes: stages start on 1024.
   // (Offsetting the shared array itself keeps the pointer in the shared
@@ -169,7 +175,8 @@ __global__ void __launch_bounds__(kJThreads, 2) joined_stream_kernel(const __gri
         mbar_arrive(&full_bar[stage]);
         break;
       }
-      const UnitInfo u = decode_unit(unit, p.splits, nblocks);
+      const UnitInfo u = decode_unit(static_cast<uint32_t>(unit), static_cast<uint32_t>(p.splits),
+                                     static_cast<uint32_t>(nblocks));
       const int expert = cached ? plan_cache[0][u.group] : p.plan.group_expert[u.group];
       const int start = cached ? plan_cache[1][u.group] : p.plan.group_start[u.group];
       const int nr = cached ? plan_cache[2][u.group] : p.plan.group_count[u.group];
@@ -195,6 +202,8 @@ __global__ void __launch_bounds__(kJThreads, 2) joined_stream_kernel(const __gri
           unit_rows[stage][0] = nr;
 #pragma unroll
           for (int r = 0; r < kMaxGroupRows; ++r) unit_rows[stage][1 + r] = slots[r];
+          unit_rows[stage][kUnitBlock] = u.nb;
+          unit_rows[stage][kUnitSplit] = u.split;
         }
         unsigned char* base = ring + stage * kJStageBytes;
         // The tensor tile is always 128 x 128 bytes: past the end of a row it
@@ -263,7 +272,8 @@ __global__ void __launch_bounds__(kJThreads, 2) joined_stream_kernel(const __gri
     const int4 m = meta[stage];
     if (m.w & kEnd) break;
     if (m.w & kFirst) {
-      u = decode_unit(m.x, p.splits, nblocks);
+      u.nb = unit_rows[stage][kUnitBlock];
+      u.split = unit_rows[stage][kUnitSplit];
       nr = unit_rows[stage][0];
       ncg = (nr + 3) >> 2;
       slot_a = unit_rows[stage][1 + tig];
