@@ -28,11 +28,25 @@ namespace exlr8 {
 
 static inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
+// Large row counts (prefill) are planned by several CTAs: a histogram per
+// chunk of kPlanChunk slots, one CTA for the scans, and a stable scatter per
+// chunk; smaller plans run in one CTA (plan_body).
+constexpr int kPlanChunk = 4096;
+constexpr int kPlanMultiMinRows = 4096;
+constexpr int kPlanMultiMaxExperts = 2048;  // the scatter's shared counters: 17 x experts ints <= 139 KB
+constexpr int kPlanChunkThreads = 512;
+
+inline bool plan_multi(int rows, int experts) {
+  return rows > kPlanMultiMinRows && experts <= kPlanMultiMaxExperts;
+}
+inline int plan_chunks(int rows) { return (rows + kPlanChunk - 1) / kPlanChunk; }
+
 size_t plan_bytes(int rows, int experts) {
   size_t n = 16;                              // header
   n += static_cast<size_t>(rows);             // order
   n += 3 * static_cast<size_t>(rows);         // groups (at most one per row)
   n += 2 * static_cast<size_t>(experts);      // expert count / start
+  if (plan_multi(rows, experts)) n += static_cast<size_t>(plan_chunks(rows)) * (experts + 1);  // chunk histograms
   return align_up(n * sizeof(int32_t), 256);
 }
 
@@ -52,6 +66,8 @@ PlanView plan_view(void* base, int rows, int experts) {
   v.expert_count = p;
   p += experts;
   v.expert_start = p;
+  p += experts;
+  v.chunk_hist = plan_multi(rows, experts) ? p : nullptr;
   v.zero = nullptr;
   v.zero_count = 0;
   return v;
@@ -67,8 +83,165 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(const uint32_t* __re
   plan_body(ids, rows, experts, period, skip_slot, plan, sm);
 }
 
+// Multi-CTA plan, step 1: per chunk of kPlanChunk slots, the slot count of
+// every expert (and, in column `experts`, the ids out of range).
+__global__ void __launch_bounds__(kPlanChunkThreads) plan_hist_kernel(const uint32_t* __restrict__ ids, int rows,
+                                                                      int experts, int period, int skip_slot,
+                                                                      int32_t* __restrict__ chunk_hist) {
+  extern __shared__ int hist[];  // [experts + 1]
+  for (int e = threadIdx.x; e <= experts; e += blockDim.x) hist[e] = 0;
+  __syncthreads();
+  const int begin = blockIdx.x * kPlanChunk, end = min(begin + kPlanChunk, rows);
+  for (int i = begin + threadIdx.x; i < end; i += blockDim.x) {
+    if (skip_slot >= 0 && i % period == skip_slot) continue;
+    const uint32_t e = ids[i];
+    atomicAdd(&hist[e < static_cast<uint32_t>(experts) ? e : static_cast<uint32_t>(experts)], 1);
+  }
+  __syncthreads();
+  int32_t* row = chunk_hist + static_cast<int64_t>(blockIdx.x) * (experts + 1);
+  for (int e = threadIdx.x; e <= experts; e += blockDim.x) row[e] = hist[e];
+}
+
+// Step 2 (one CTA): expert totals and starts, groups of at most
+// kMaxGroupRows rows, the header, and each chunk's first output position per
+// expert (written over its histogram).
+__global__ void __launch_bounds__(1024) plan_scan_kernel(int rows, int experts, int chunks, PlanView plan) {
+  __shared__ int warp_rows[32], warp_groups[32];
+  __shared__ int s_bad;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int nwarps = blockDim.x >> 5;
+  for (int i = tid; i < plan.zero_count; i += blockDim.x) plan.zero[i] = 0;
+  if (tid == 0) s_bad = 0;
+  __syncthreads();
+  if (tid < chunks) atomicAdd(&s_bad, plan.chunk_hist[static_cast<int64_t>(tid) * (experts + 1) + experts]);
+  // Experts in blocks of blockDim: per expert its total and group count, a
+  // block-wide exclusive scan, carried across blocks.
+  int row_carry = 0, group_carry = 0;
+  for (int e0 = 0; e0 < experts; e0 += blockDim.x) {
+    const int e = e0 + tid;
+    int total = 0;
+    if (e < experts) {
+      for (int c = 0; c < chunks; ++c) {
+        int32_t* cell = plan.chunk_hist + static_cast<int64_t>(c) * (experts + 1) + e;
+        const int n = *cell;
+        *cell = total;  // offset of chunk c inside the expert's rows
+        total += n;
+      }
+    }
+    const int groups = (total + kMaxGroupRows - 1) / kMaxGroupRows;
+    int r = total, g = groups;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const int ru = __shfl_up_sync(0xffffffffu, r, off), gu = __shfl_up_sync(0xffffffffu, g, off);
+      if (lane >= off) {
+        r += ru;
+        g += gu;
+      }
+    }
+    if (lane == 31) {
+      warp_rows[warp] = r;
+      warp_groups[warp] = g;
+    }
+    __syncthreads();
+    if (warp == 0) {
+      int wr = lane < nwarps ? warp_rows[lane] : 0, wg = lane < nwarps ? warp_groups[lane] : 0;
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) {
+        const int ru = __shfl_up_sync(0xffffffffu, wr, off), gu = __shfl_up_sync(0xffffffffu, wg, off);
+        if (lane >= off) {
+          wr += ru;
+          wg += gu;
+        }
+      }
+      if (lane < nwarps) {
+        warp_rows[lane] = wr;
+        warp_groups[lane] = wg;
+      }
+    }
+    __syncthreads();
+    const int row_base = row_carry + (warp > 0 ? warp_rows[warp - 1] : 0) + r - total;
+    const int group_base = group_carry + (warp > 0 ? warp_groups[warp - 1] : 0) + g - groups;
+    if (e < experts) {
+      plan.expert_start[e] = row_base;
+      plan.expert_count[e] = total;
+      for (int c = 0; c < groups; ++c) {
+        plan.group_expert[group_base + c] = e;
+        plan.group_start[group_base + c] = row_base + c * kMaxGroupRows;
+        plan.group_count[group_base + c] = min(kMaxGroupRows, total - c * kMaxGroupRows);
+      }
+      for (int c = 0; c < chunks; ++c) plan.chunk_hist[static_cast<int64_t>(c) * (experts + 1) + e] += row_base;
+    }
+    row_carry += warp_rows[nwarps - 1];
+    group_carry += warp_groups[nwarps - 1];
+    __syncthreads();
+  }
+  if (tid == 0) {
+    plan.header[0] = group_carry;
+    plan.header[1] = rows;
+    for (int c = 2; c < 8; ++c) plan.header[c] = 0;
+    plan.header[8] = s_bad;
+    plan.header[9] = 0;
+  }
+}
+
+// Step 3: each chunk scatters its slots in slot order to the positions the
+// scan gave it (stable: earlier slots of an expert come first).
+__global__ void __launch_bounds__(kPlanChunkThreads) plan_scatter_kernel(const uint32_t* __restrict__ ids, int rows,
+                                                                         int experts, int period, int skip_slot,
+                                                                         PlanView plan) {
+  extern __shared__ int sm[];
+  int* next = sm;                 // [experts] next output position per expert
+  int* wcount = sm + experts;     // [warps][experts]
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int nwarps = blockDim.x >> 5;
+  const int32_t* start = plan.chunk_hist + static_cast<int64_t>(blockIdx.x) * (experts + 1);
+  for (int e = tid; e < experts; e += blockDim.x) next[e] = start[e];
+  const unsigned lt_mask = (1u << lane) - 1u;
+  const int begin = blockIdx.x * kPlanChunk, end = min(begin + kPlanChunk, rows);
+  for (int chunk = begin; chunk < end; chunk += blockDim.x) {
+    for (int j = tid; j < nwarps * experts; j += blockDim.x) wcount[j] = 0;
+    __syncthreads();
+    const int i = chunk + tid;
+    const bool skipped = i < end && skip_slot >= 0 && i % period == skip_slot;
+    const uint32_t raw = (i < end && !skipped) ? ids[i] : 0xFFFFFFFFu;
+    const bool valid = raw < static_cast<uint32_t>(experts);
+    const uint32_t key = valid ? raw : 0xFFFFFFFFu;
+    const unsigned peers = __match_any_sync(0xffffffffu, key);
+    const int leader = __ffs(peers) - 1;
+    const int rank = __popc(peers & lt_mask);
+    if (valid && lane == leader) wcount[warp * experts + key] = __popc(peers);
+    __syncthreads();
+    if (valid) {
+      int prior = 0;
+      for (int w = 0; w < warp; ++w) prior += wcount[w * experts + key];
+      plan.order[next[key] + prior + rank] = i;
+    }
+    __syncthreads();
+    if (valid && lane == leader) atomicAdd(&next[key], __popc(peers));
+    __syncthreads();
+  }
+}
+
 cudaError_t launch_plan(const uint32_t* ids, int rows, int experts, int period, int skip_slot, PlanView plan,
                         cudaStream_t s) {
+  if (plan_multi(rows, experts) && plan.chunk_hist != nullptr) {
+    // Plain launches: the plan heads its call's kernel chain.
+    const int chunks = plan_chunks(rows);
+    const int per = period > 0 ? period : 1;
+    const size_t hist_smem = static_cast<size_t>(experts + 1) * sizeof(int);
+    const size_t scatter_smem = static_cast<size_t>(1 + kPlanChunkThreads / 32) * experts * sizeof(int);
+    static const cudaError_t attr = cudaFuncSetAttribute(
+        plan_scatter_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        static_cast<int>((1 + kPlanChunkThreads / 32) * kPlanMultiMaxExperts * sizeof(int)));
+    if (attr != cudaSuccess) return attr;
+    plan_hist_kernel<<<chunks, kPlanChunkThreads, hist_smem, s>>>(ids, rows, experts, per, skip_slot, plan.chunk_hist);
+    cudaError_t err = cudaGetLastError();
+    if (err != cudaSuccess) return err;
+    plan_scan_kernel<<<1, 1024, 0, s>>>(rows, experts, chunks, plan);
+    if ((err = cudaGetLastError()) != cudaSuccess) return err;
+    plan_scatter_kernel<<<chunks, kPlanChunkThreads, scatter_smem, s>>>(ids, rows, experts, per, skip_slot, plan);
+    return cudaGetLastError();
+  }
   const size_t smem = plan_smem_bytes(experts, kPlanThreads / 32);
   if (smem > 48 * 1024) {
     cudaError_t err = cudaFuncSetAttribute(plan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,

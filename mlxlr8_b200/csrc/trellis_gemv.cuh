@@ -20,6 +20,7 @@ struct PlanView {
   int32_t* expert_start;  // [experts] first position in order
   int32_t* zero;          // counters of later kernels, zeroed by the plan (may be null)
   int zero_count;
+  int32_t* chunk_hist;    // [chunks][experts + 1] scratch of the multi-CTA plan (large row counts)
 };
 
 // Shared memory of plan_body for `warps` warps.

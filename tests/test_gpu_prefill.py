@@ -94,9 +94,10 @@ def test_prefill_ragged_chunks():
             assert_prefill_close(actual[sel], expected[sel])
 
 
-@pytest.mark.parametrize("tokens", [24, 40, 130])
+@pytest.mark.parametrize("tokens", [24, 40, 130, 600])
 @pytest.mark.parametrize("shared", ["bf16", "trellis"])
 def test_prefill_layer_matches_oracle(tokens, shared):
+    """600 tokens (5,400 slots) takes the multi-CTA dispatch plan."""
     import torch
 
     from mlxlr8_b200.fast_router import router, router_logits
