@@ -1027,6 +1027,21 @@ def main():
     peak, peak_kind = measured_peaks()
     share = {k: round(ms / max(sum(v for _, v in prof.values()), 1e-9), 4) for k, (n, ms) in prof.items()}
 
+    # The trellis decode's compute ceiling on this GPU (codes held in shared
+    # memory): the codes part of the dominant launch against it.
+    codec_ceiling = None
+    try:
+        import ctypes
+
+        sink = torch.zeros(1, dtype=torch.float32, device=device)
+        w = ctypes.c_double(0.0)
+        _lib.check(_lib.lib().exlr8_codec_peak(4000, ctypes.byref(w), sink.data_ptr(),
+                                               torch.cuda.current_stream(device).cuda_stream))
+        codec_ceiling = w.value * K_BITS / 8 / 1e9
+    except Exception:  # noqa: BLE001 - the line carries null then
+        codec_ceiling = None
+    codes_gbs = u_mean * 2 * codes_per_matrix / (gate_up_avg_ms / 1000.0) / 1e9
+
     # Whole-step algorithmic bytes (codes, scales, shared expert, router, activations) for context.
     step_bytes = u_mean * 3 * codes_per_matrix + u_mean * 49152 + 3 * HIDDEN * INTER * 2 + 256 * HIDDEN * 4 + 4 * T * HIDDEN
 
@@ -1128,7 +1143,12 @@ def main():
                          "achieved": achieved, "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": TRAFFIC_PER_MATRIX * 2 * u_mean + dense_bytes,
                          "algorithmic_bytes_per_launch": gate_up_bytes, "avg_launch_ms": gate_up_avg_ms,
-                         "unique_experts_mean": u_mean},
+                         "unique_experts_mean": u_mean,
+                         "codes_gbs": codes_gbs, "codec_ceiling_gbs": codec_ceiling,
+                         "frac_of_codec_ceiling": codes_gbs / codec_ceiling if codec_ceiling else None,
+                         "codec_ceiling_note": "exlr8_codec_peak: the exact K4 decode + mma.sync on codes in shared "
+                                               "memory at the kernel's occupancy; the decode cannot stream codes "
+                                               "faster than this on this GPU"},
             "step_roofline": {"algorithmic_bytes": step_bytes, "achieved_gbs": step_bytes / (ms_per_step / 1000) / 1e9,
                               "frac": step_bytes / (ms_per_step / 1000) / 1e9 / peak},
             "kernel_share": share,

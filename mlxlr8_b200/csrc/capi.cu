@@ -254,6 +254,7 @@ int run_mlp_after_plan(const void* x, int x_dtype, int per_slot, int slots, cons
     gp.dense = DenseUnits{static_cast<const uint16_t*>(shared->gate), static_cast<const uint16_t*>(shared->up),
                           static_cast<const uint16_t*>(dense_x), b.dgate, b.dup, m, h, t, dsplits_gu,
                           (m / kDenseRows) * dsplits_gu, 1};
+  if (!encode_dense_maps(gp)) return EXLR8_ERR_CUDA;
   EXLR8_TIMED(EXLR8_KERNEL_GATE_UP, s, launch_stream(gp, s));
   EXLR8_TIMED(EXLR8_KERNEL_GATE_FINISH, s,
               launch_gate_finish_frag(b.gu, l.s1.count, ids, n, ex->out_scale[0], ex->out_scale[1], ex->in_scale[2],
@@ -278,6 +279,7 @@ int run_mlp_after_plan(const void* x, int x_dtype, int per_slot, int slots, cons
   if (shared)
     dp.dense = DenseUnits{static_cast<const uint16_t*>(shared->down), nullptr, static_cast<const uint16_t*>(b.dh),
                           b.ddown, nullptr, h, m, t, dsplits_d, (h / kDenseRows) * dsplits_d, 0};
+  if (!encode_dense_maps(dp)) return EXLR8_ERR_CUDA;
   EXLR8_TIMED(EXLR8_KERNEL_DOWN, s, launch_stream(dp, s));
   return EXLR8_OK;
 }

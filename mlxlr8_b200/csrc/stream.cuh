@@ -1,6 +1,7 @@
 // Streaming trellis GEMV, activation-fragment producers and their layouts.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -26,7 +27,8 @@ inline size_t frag_bytes(int64_t rows, int features, int projections) {
 // warp per CTA (dense_stream.cuh) beside the trellis warps.  A dense unit is
 // (16-row group of W, K split); W1 (optional) shares the x rows.  Partials
 // are float32 [splits][tokens][n].  Requirements: n % 16 == 0, k a multiple
-// of 128 * splits, W, W1 and x 16-byte aligned.
+// of 128 * splits, W, W1 and x 16-byte aligned (the tensor maps of W, W1
+// need k * 2 bytes between rows, a multiple of 16).
 struct DenseUnits {
   const uint16_t* w0;  // [n][k] bf16 (gate, or down)
   const uint16_t* w1;  // [n][k] bf16 (up) or null
@@ -42,6 +44,10 @@ struct DenseUnits {
 };
 
 struct StreamParams {
+  // Tensor maps of the dense rows W0 / W1 ([n][k] bf16; boxes of 16 rows x 64
+  // values, 128-byte swizzle), read by the dense warp; encoded on the host
+  // when dense.units > 0 (encode_dense_maps).
+  CUtensorMap dense_w0, dense_w1;
   const uint32_t* packed[2];
   // Static hot-expert cache (optional): the exact E4M3 bytes of the cached
   // experts per projection, the stored tile order with 256 bytes per tile and
@@ -70,6 +76,10 @@ inline int kt_per_split(int in_features, int splits) {
 inline int split_count(int in_features, int per) { return (in_features / 16 + per - 1) / per; }
 
 cudaError_t launch_stream(const StreamParams& p, cudaStream_t s);
+
+// Encodes p.dense_w0 / p.dense_w1 for p.dense (no-op without dense units);
+// false when the encode fails.
+bool encode_dense_maps(StreamParams& p);
 
 // xh = H(x[row] * in_scale_p[e]) written as fragment records
 // (metal/fast_decode_prep.metal).  frag holds frag_bytes(nslots, features,

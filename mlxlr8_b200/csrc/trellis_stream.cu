@@ -35,6 +35,7 @@
 #include "launch.cuh"
 #include "stream.cuh"
 #include "tma.cuh"
+#include "tensor_map.cuh"
 
 namespace exlr8 {
 
@@ -87,7 +88,7 @@ __device__ __forceinline__ UnitInfo decode_unit(uint32_t unit, const StreamParam
 }
 
 template <int K>
-__global__ void __launch_bounds__(kStreamThreads, 2) trellis_stream_kernel(StreamParams p) {
+__global__ void __launch_bounds__(kStreamThreads, 2) trellis_stream_kernel(const __grid_constant__ StreamParams p) {
   using G = StageGeometry<K>;
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ __align__(8) uint64_t full_bar[kStages];
@@ -120,7 +121,7 @@ __global__ void __launch_bounds__(kStreamThreads, 2) trellis_stream_kernel(Strea
     // it in the chain (stream.cuh DenseUnits::early): they stream while the
     // routing and the fragment prep finish.
     if (!p.dense.early) pdl_wait();
-    if (p.dense.units > 0 && !dense_warp_run(p.dense, smem + G::kRingBytes, dense_bar, lane)) {
+    if (p.dense.units > 0 && !dense_warp_run(p.dense, &p.dense_w0, &p.dense_w1, smem + G::kRingBytes, dense_bar, lane)) {
       if (lane == 0) atomicOr(&p.plan.header[9], 4);
       // Copies already issued target valid addresses and land within
       // microseconds; give them that time before this warp retires.
@@ -393,6 +394,21 @@ static cudaError_t launch_stream_k(const StreamParams& p, cudaStream_t s) {
     grid = sms * (per_sm < 1 ? 1 : per_sm);
   }
   return launch_pdl(trellis_stream_kernel<K>, dim3(grid), dim3(kStreamThreads), static_cast<size_t>(smem), s, p);
+}
+
+bool encode_dense_maps(StreamParams& p) {
+  const DenseUnits& d = p.dense;
+  if (d.units <= 0) return true;
+  const uint64_t row_bytes = static_cast<uint64_t>(d.k) * 2;
+  if (!encode_tiled_2d(&p.dense_w0, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, d.w0, static_cast<uint64_t>(d.k),
+                       static_cast<uint64_t>(d.n), row_bytes, 64, kDenseRows, CU_TENSOR_MAP_SWIZZLE_128B))
+    return false;
+  if (d.w1 == nullptr) {
+    p.dense_w1 = p.dense_w0;
+    return true;
+  }
+  return encode_tiled_2d(&p.dense_w1, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, d.w1, static_cast<uint64_t>(d.k),
+                         static_cast<uint64_t>(d.n), row_bytes, 64, kDenseRows, CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
 cudaError_t launch_stream(const StreamParams& p, cudaStream_t s) {
