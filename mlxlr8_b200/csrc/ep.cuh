@@ -33,6 +33,10 @@ cudaError_t launch_sum_cast(const float* partial, int splits, int64_t n, int act
 //   [512, 768)      returned[owner]: epoch + 1 once owner's values landed
 //   [768, 1024)     caps[src]: the row capacity C src used for this call (all
 //                   ranks must agree: they pass the same token count)
+//   [1024, 1280)    sent[dst]: CTAs of this rank's send kernels done with dst
+//   [1280, 1536)    back[src]: CTAs of this rank's return kernels done with src
+//                   (the last CTA of a peer raises the flag and resets the
+//                   count for the next call)
 //   meta            int32 [ranks][C]: local expert id of each received row, -1 empty
 //   rows            [ranks][C][hidden]: received activation rows
 //   back            [ranks][C][hidden]: slot values returned by each owner
@@ -45,7 +49,7 @@ struct PeerLayout {
 __host__ __device__ inline PeerLayout peer_layout(int ranks, int max_capacity, int hidden, int elem) {
   PeerLayout l;
   const size_t rows_bytes = static_cast<size_t>(ranks) * max_capacity * hidden * elem;
-  l.meta = 1024;
+  l.meta = 1536;
   l.rows = l.meta + ((static_cast<size_t>(ranks) * max_capacity * 4 + 255) / 256) * 256;
   l.back = l.rows + ((rows_bytes + 255) / 256) * 256;
   l.total = l.back + ((rows_bytes + 255) / 256) * 256;

@@ -23,6 +23,13 @@ namespace exlr8 {
 namespace {
 
 constexpr int kPeerThreads = 256;
+
+// CTAs per peer in the send and return kernels: one per 16 rows of capacity,
+// at most 16 (a single CTA per peer copied at a few tens of GB/s).
+inline int peer_split(int capacity) {
+  const int split = (capacity + 15) / 16;
+  return split < 1 ? 1 : (split > 16 ? 16 : split);
+}
 constexpr uint32_t kPeerSpinLimit = 1u << 20;  // about 1 s of polling
 
 __device__ __forceinline__ uint32_t load_acquire_sys(const uint32_t* p) {
@@ -48,9 +55,28 @@ __device__ __forceinline__ uint32_t* flags_at(unsigned char* region, int which) 
   return reinterpret_cast<uint32_t*>(region + 256 * which);  // which: 1 arrived, 2 returned, 3 caps
 }
 
-// CTA d sends this rank's rows routed to owner d (slot order) and their local
-// expert ids into d's region, then this rank's arrival flag there; then waits
-// until rank d's rows for this call have arrived in this rank's region.
+__device__ __forceinline__ uint32_t* counters_at(unsigned char* region, int which) {
+  return reinterpret_cast<uint32_t*>(region + 1024 + 256 * which);  // which: 0 sent, 1 back
+}
+
+// One more CTA of this call is done with a peer (its copies fenced at system
+// scope before); true for the last of the `split` CTAs of the peer, which
+// resets the count for the next call (kernels of one stream run one after
+// another, whatever split the next call uses) and orders everything after
+// the others' copies.
+__device__ __forceinline__ bool last_of_peer(uint32_t* counter, int split) {
+  const uint32_t before = atomicAdd(counter, 1u);
+  if (before != static_cast<uint32_t>(split) - 1u) return false;
+  *counter = 0u;
+  __threadfence_system();
+  return true;
+}
+
+// CTAs (d, q) for owner d: every CTA ranks this rank's routed slots for d in
+// slot order (the same ranking in each); CTA q copies rows q, q + split, ...
+// (and q = 0 the local expert ids and slot positions) into d's region.  The
+// last CTA of d then stores this rank's capacity and arrival flag there and
+// waits until rank d's rows for this call have arrived in this rank's region.
 __global__ void __launch_bounds__(kPeerThreads) ep_send_kernel(
     const uint32_t* __restrict__ ids, int tokens, const uint4* __restrict__ x, int row_vecs, int ranks, int rank,
     int experts_per_rank, int capacity, PeerLayout layout, const uint64_t* __restrict__ peers,
@@ -59,7 +85,7 @@ __global__ void __launch_bounds__(kPeerThreads) ep_send_kernel(
   __shared__ int s_warp[kPeerThreads / 32];
   __shared__ int s_base;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int d = blockIdx.x;
+  const int d = blockIdx.x, q = blockIdx.y, split = gridDim.y;
   const uint32_t target = *reinterpret_cast<volatile uint32_t*>(local) + 1u;
   unsigned char* owner = reinterpret_cast<unsigned char*>(peers[d]);
   const int slots = tokens * 8;
@@ -85,12 +111,12 @@ __global__ void __launch_bounds__(kPeerThreads) ep_send_kernel(
       if (pos < capacity) {
         s_list[pos] = i / 8;
         s_list[capacity + pos] = loc;
-        slot_pos[i] = d * capacity + pos;
-      } else {
+        if (q == 0) slot_pos[i] = d * capacity + pos;
+      } else if (q == 0) {
         slot_pos[i] = -1;
         atomicAdd(&status[0], 1);  // capacity overflow: the slot is lost
       }
-    } else if (d == 0 && dest < 0 && i < slots) {
+    } else if (q == 0 && d == 0 && dest < 0 && i < slots) {
       slot_pos[i] = -1;  // id out of range: contributes zero
     }
     __syncthreads();
@@ -102,17 +128,20 @@ __global__ void __launch_bounds__(kPeerThreads) ep_send_kernel(
     __syncthreads();
   }
   const int count = min(s_base, capacity);
-  int32_t* meta = reinterpret_cast<int32_t*>(owner + layout.meta) + static_cast<int64_t>(rank) * capacity;
-  for (int j = tid; j < capacity; j += kPeerThreads) meta[j] = j < count ? s_list[capacity + j] : -1;
-  uint4* rows = reinterpret_cast<uint4*>(owner + layout.rows) + static_cast<int64_t>(rank) * capacity * row_vecs;
-  for (int64_t idx = tid; idx < static_cast<int64_t>(count) * row_vecs; idx += kPeerThreads) {
-    const int j = static_cast<int>(idx / row_vecs), v = static_cast<int>(idx % row_vecs);
-    rows[static_cast<int64_t>(j) * row_vecs + v] = x[static_cast<int64_t>(s_list[j]) * row_vecs + v];
+  if (q == 0) {
+    int32_t* meta = reinterpret_cast<int32_t*>(owner + layout.meta) + static_cast<int64_t>(rank) * capacity;
+    for (int j = tid; j < capacity; j += kPeerThreads) meta[j] = j < count ? s_list[capacity + j] : -1;
   }
-  if (tid == 0) flags_at(owner, 3)[rank] = static_cast<uint32_t>(capacity);
+  uint4* rows = reinterpret_cast<uint4*>(owner + layout.rows) + static_cast<int64_t>(rank) * capacity * row_vecs;
+  for (int j = q; j < count; j += split) {
+    const uint4* src = x + static_cast<int64_t>(s_list[j]) * row_vecs;
+    uint4* dst = rows + static_cast<int64_t>(j) * row_vecs;
+    for (int v = tid; v < row_vecs; v += kPeerThreads) dst[v] = src[v];
+  }
   __threadfence_system();
   __syncthreads();
-  if (tid == 0) {
+  if (tid == 0 && last_of_peer(counters_at(local, 0) + d, split)) {
+    flags_at(owner, 3)[rank] = static_cast<uint32_t>(capacity);
     store_release_sys(flags_at(owner, 1) + rank, target);
     if (!wait_epoch(flags_at(local, 1) + d, target)) {
       atomicOr(&status[1], 1);
@@ -120,30 +149,31 @@ __global__ void __launch_bounds__(kPeerThreads) ep_send_kernel(
       atomicOr(&status[1], 4);  // source d's rows use another stride: its rows are misread
     }
   }
-  __syncthreads();
 }
 
-// CTA s returns the values of source s's rows (valid rows only) into source
-// s's `back` area, then the `returned` flag; then waits for owner s's values.
+// CTAs (s, q) for source s: CTA q returns the values of source s's valid rows
+// q, q + split, ... into s's `back` area; the last CTA of s raises the
+// `returned` flag there and waits for owner s's values in this region.
 __global__ void __launch_bounds__(kPeerThreads) ep_return_kernel(const uint4* __restrict__ values, int row_vecs,
                                                                  int rank, int capacity, PeerLayout layout,
                                                                  const uint64_t* __restrict__ peers,
                                                                  unsigned char* __restrict__ local,
                                                                  int32_t* __restrict__ status) {
   const int tid = threadIdx.x;
-  const int src = blockIdx.x;
+  const int src = blockIdx.x, q = blockIdx.y, split = gridDim.y;
   const uint32_t target = *reinterpret_cast<volatile uint32_t*>(local) + 1u;
   unsigned char* dst_region = reinterpret_cast<unsigned char*>(peers[src]);
   const int32_t* meta = reinterpret_cast<const int32_t*>(local + layout.meta) + static_cast<int64_t>(src) * capacity;
   uint4* back = reinterpret_cast<uint4*>(dst_region + layout.back) + static_cast<int64_t>(rank) * capacity * row_vecs;
   const uint4* v = values + static_cast<int64_t>(src) * capacity * row_vecs;
-  for (int64_t idx = tid; idx < static_cast<int64_t>(capacity) * row_vecs; idx += kPeerThreads) {
-    const int j = static_cast<int>(idx / row_vecs);
-    if (meta[j] >= 0) back[idx] = v[idx];
+  for (int j = q; j < capacity; j += split) {
+    if (meta[j] < 0) continue;  // rows are filled in order: the rest are empty as well
+    for (int c = tid; c < row_vecs; c += kPeerThreads)
+      back[static_cast<int64_t>(j) * row_vecs + c] = v[static_cast<int64_t>(j) * row_vecs + c];
   }
   __threadfence_system();
   __syncthreads();
-  if (tid == 0) {
+  if (tid == 0 && last_of_peer(counters_at(local, 1) + src, split)) {
     store_release_sys(flags_at(dst_region, 2) + rank, target);
     if (!wait_epoch(flags_at(local, 2) + src, target)) atomicOr(&status[1], 2);
   }
@@ -172,9 +202,9 @@ cudaError_t launch_ep_send(const uint32_t* ids, int tokens, const void* x, int x
   const int elem = x_dtype == kF32 ? 4 : 2;
   const PeerLayout layout = peer_layout(ranks, max_capacity, hidden, elem);
   const size_t smem = 2 * static_cast<size_t>(capacity) * sizeof(int);
-  ep_send_kernel<<<ranks, kPeerThreads, smem, s>>>(ids, tokens, static_cast<const uint4*>(x), hidden * elem / 16,
-                                                   ranks, rank, experts_per_rank, capacity, layout, peers,
-                                                   static_cast<unsigned char*>(local), slot_pos, status);
+  ep_send_kernel<<<dim3(ranks, peer_split(capacity)), kPeerThreads, smem, s>>>(
+      ids, tokens, static_cast<const uint4*>(x), hidden * elem / 16, ranks, rank, experts_per_rank, capacity, layout,
+      peers, static_cast<unsigned char*>(local), slot_pos, status);
   return cudaGetLastError();
 }
 
@@ -182,9 +212,9 @@ cudaError_t launch_ep_return(const void* values, int x_dtype, int hidden, int ra
                              int max_capacity, const uint64_t* peers, void* local, int32_t* status, cudaStream_t s) {
   const int elem = x_dtype == kF32 ? 4 : 2;
   const PeerLayout layout = peer_layout(ranks, max_capacity, hidden, elem);
-  ep_return_kernel<<<ranks, kPeerThreads, 0, s>>>(static_cast<const uint4*>(values), hidden * elem / 16, rank,
-                                                  capacity, layout, peers, static_cast<unsigned char*>(local),
-                                                  status);
+  ep_return_kernel<<<dim3(ranks, peer_split(capacity)), kPeerThreads, 0, s>>>(
+      static_cast<const uint4*>(values), hidden * elem / 16, rank, capacity, layout, peers,
+      static_cast<unsigned char*>(local), status);
   cudaError_t err = cudaGetLastError();
   if (err != cudaSuccess) return err;
   ep_epoch_kernel<<<1, 1, 0, s>>>(static_cast<unsigned char*>(local));

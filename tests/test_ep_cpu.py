@@ -99,7 +99,7 @@ def test_peer_region_layout_and_checks():
     assert lib.exlr8_ep_peer_offsets(ranks, cap, hidden, 2, ctypes.byref(meta), ctypes.byref(rows),
                                      ctypes.byref(back)) == 0
     total = lib.exlr8_ep_peer_bytes(ranks, cap, hidden, 2)
-    assert meta.value == 1024                                       # epoch, flags, capacities
+    assert meta.value == 1536                                       # epoch, flags, capacities, counters
     assert rows.value >= meta.value + ranks * cap * 4 and rows.value % 256 == 0
     assert back.value == rows.value + ranks * cap * hidden * 2
     assert total == back.value + ranks * cap * hidden * 2
