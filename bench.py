@@ -81,7 +81,7 @@ METRIC = "MoE-layer tokens/s (decode GB/s vs HBM; prefill TFLOPS) at 1/2/4/8 B20
 # (the codes scale with the matrices its own launches stream) and the shared
 # expert's part, taken as its algorithmic bytes.
 DENSE_GATE_UP_BYTES = 2 * 6144 * 2048 * 2
-GATE_UP_TRAFFIC_8 = 151_501_568 + 5_826_560
+GATE_UP_TRAFFIC_8 = 151_499_520 + 6_107_136
 TRAFFIC_PER_MATRIX = (GATE_UP_TRAFFIC_8 - DENSE_GATE_UP_BYTES) / 16
 
 
