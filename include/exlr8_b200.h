@@ -267,6 +267,17 @@ enum exlr8_kernel_kind {
 int exlr8_profile_enable(int enable, int capacity);
 int exlr8_profile_read(int kind, int64_t* launches, double* total_ms);
 
+/* ---- tuning ---------------------------------------------------------------- */
+
+/* Block-scaled (MXFP4) grouped GEMMs whose shape allows it (one projection,
+ * out_features a multiple of 512) run on SM pairs: a two-CTA cluster issuing
+ * M = 256 tcgen05 MMAs (cta_group::2) with the activation tile split between
+ * the two SMs.  The one-SM kernel issues the same MMAs in the same order per
+ * accumulator.  exlr8_gemm_pair(0 or 1) selects the form for later calls and
+ * returns the previous setting; a negative argument only reads it.  Default
+ * 1.  No counterpart in the reference. */
+int exlr8_gemm_pair(int enable);
+
 /* ---- measurement ---------------------------------------------------------- */
 
 /* Tensor-core peak probe, no counterpart in the reference: the throughput

@@ -100,6 +100,7 @@ _SIGNATURES = {
                                         POINTER(TrellisExperts), POINTER(DenseExpert), c_void_p, c_void_p, c_void_p,
                                         c_void_p]),
     "exlr8_codec_peak": (c_int, [c_int, POINTER(c_double), c_void_p, c_void_p]),
+    "exlr8_gemm_pair": (c_int, [c_int]),
     "exlr8_tensor_peak": (c_int, [c_int, c_int, c_int, POINTER(c_double), c_void_p, c_void_p]),
     "exlr8_peer_write": (c_int, [c_void_p, c_void_p, c_int64, c_void_p]),
     "exlr8_hadamard128": (c_int, [c_void_p, c_int64, c_int, c_void_p, c_void_p]),

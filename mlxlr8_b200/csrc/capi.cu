@@ -1129,4 +1129,6 @@ int exlr8_workspace_bad_ids(const void* workspace, int64_t* bad_ids, void* strea
   return EXLR8_OK;
 }
 
+int exlr8_gemm_pair(int enable) { return set_gemm_pair(enable); }
+
 }  // extern "C"

@@ -24,7 +24,10 @@
 //               planes and scales, TMA (MXFP4) or bulk copy (trellis codes)
 //               of the weights
 //   warp 1      MMA issuer (one thread) and TMEM owner
-//   warps 2-5   epilogue: TMEM -> float32 rows of `out`
+//   epilogue    TMEM -> float32 rows of `out`: 8 warps for MXFP4 (two per
+//               TMEM sub-partition, alternating 16-column groups, so the
+//               accumulators drain in half the time while the MMA waits),
+//               4 warps for trellis (warps 2-5)
 //   warp 6      (trellis) code producer: bulk copies of trellis codes into a
 //               4-stage ring ahead of the decoders
 //   warps 7-22  (trellis) decoders: codes -> E4M3 weight tiles
@@ -33,6 +36,7 @@
 
 #include <cuda.h>
 
+#include <atomic>
 #include <cstring>
 #include <mutex>
 
@@ -80,7 +84,9 @@ struct GemmTraits {
   static constexpr int kStages = kTrellis ? 2 : 3;       // operand ring (weight image + activation planes)
   static constexpr int kCodeStages = kTrellis ? 4 : 0;   // trellis code ring, ahead of the decoders
   static constexpr int kDecoderWarps = kTrellis ? 16 : 0;
-  static constexpr int kThreads = 192 + (kTrellis ? 32 + 32 * kDecoderWarps : 0);
+  static constexpr int kEpiWarps = kTrellis ? 4 : 8;    // a multiple of 4 (one per TMEM sub-partition)
+  static constexpr int kCodeWarp = 2 + kEpiWarps;       // trellis code producer
+  static constexpr int kThreads = 64 + 32 * kEpiWarps + (kTrellis ? 32 + 32 * kDecoderWarps : 0);
   static constexpr uint32_t kTileA = 128 * 128;          // one 128-row weight tile image
   static constexpr uint32_t kTileB = kMxMaxN * 128;      // one activation plane tile
   static constexpr uint32_t kTrellisTile = 32 * (kK > 0 ? kK : 1);  // bytes of one 16x16 trellis tile
@@ -254,10 +260,10 @@ __global__ void __launch_bounds__(GemmTraits<kK>::kThreads, 1)
       sh.two[c] = 1;
     }
     mbar_init(&sh.acc_full, 1);
-    mbar_init(&sh.acc_empty, 4);
+    mbar_init(&sh.acc_empty, T::kEpiWarps);
     for (int i = 0; i < kSchedSlots; ++i) {
       mbar_init(&sh.sched_full[i], 1);
-      mbar_init(&sh.sched_empty[i], 5 + (T::kTrellis ? 1 : 0));
+      mbar_init(&sh.sched_empty[i], 1 + T::kEpiWarps + (T::kTrellis ? 1 : 0));
     }
     mbar_init(&sh.drain, 1);
     mbar_fence_init();
@@ -400,9 +406,11 @@ __global__ void __launch_bounds__(GemmTraits<kK>::kThreads, 1)
       tc_commit(&sh.drain);
       if (!mbar_wait(&sh.drain, 0)) record_error(header, kErrDrain);
     }
-  } else if (warp < 6) {
-    // ---------------- epilogue (warps 2-5) ----------------
-    const int quad = warp & 3;  // TMEM sub-partition this warp may read
+  } else if (warp < 2 + T::kEpiWarps) {
+    // ---------------- epilogue ----------------
+    constexpr int kParts = T::kEpiWarps / 4;
+    const int quad = warp & 3;         // TMEM sub-partition this warp may read
+    const int part = (warp - 2) >> 2;  // its 16-column groups: part, part + kParts, ...
     for (int j = 0;; ++j) {
       const int slot = j % kSchedSlots;
       if (!mbar_wait(&sh.sched_full[slot], (j / kSchedSlots) & 1)) {
@@ -419,18 +427,25 @@ __global__ void __launch_bounds__(GemmTraits<kK>::kThreads, 1)
         break;
       }
       tc_fence_after();
+      const int64_t base = static_cast<int64_t>(u.proj) * g.proj_offset + 32 * quad + lane;
+      float* dst0 = g.out + static_cast<int64_t>(u.start) * g.out_stride + base + acc_row(g, u, 0);
+      float* dst1 = g.out + static_cast<int64_t>(u.start) * g.out_stride + base + acc_row(g, u, 1);
+      const uint32_t lane_addr = tmem + (static_cast<uint32_t>(32 * quad) << 16);
 #pragma unroll 1
-      for (int a = 0; a < (u.two ? 2 : 1); ++a) {
-        const int64_t feature = static_cast<int64_t>(u.proj) * g.proj_offset + acc_row(g, u, a) + 32 * quad + lane;
-        float* dst = g.out + static_cast<int64_t>(u.start) * g.out_stride + feature;
-#pragma unroll 1
-        for (int c0 = 0; c0 < u.n16; c0 += 8) {
-          uint32_t v[8];
-          tc_ld8(tmem + (static_cast<uint32_t>(32 * quad) << 16) + a * kTmemAcc1 + c0, v);
-          tc_wait_ld();
+      for (int c0 = 16 * part; c0 < u.n16; c0 += 16 * kParts) {
+        // Both accumulators' 16 columns in flight before one wait.
+        uint32_t v0[16], v1[16];
+        tc_ld16(lane_addr + c0, v0);
+        if (u.two) tc_ld16(lane_addr + kTmemAcc1 + c0, v1);
+        tc_wait_ld();
+        const int n = min(16, u.rows - c0);
 #pragma unroll
-          for (int c = 0; c < 8; ++c)
-            if (c0 + c < u.rows) dst[static_cast<int64_t>(c0 + c) * g.out_stride] = __uint_as_float(v[c]);
+        for (int c = 0; c < 16; ++c)
+          if (c < n) dst0[static_cast<int64_t>(c0 + c) * g.out_stride] = __uint_as_float(v0[c]);
+        if (u.two) {
+#pragma unroll
+          for (int c = 0; c < 16; ++c)
+            if (c < n) dst1[static_cast<int64_t>(c0 + c) * g.out_stride] = __uint_as_float(v1[c]);
         }
       }
       tc_fence_before();
@@ -438,7 +453,7 @@ __global__ void __launch_bounds__(GemmTraits<kK>::kThreads, 1)
       if (lane == 0) mbar_arrive(&sh.acc_empty);
     }
   } else if constexpr (T::kTrellis) {
-    if (warp == 6) {
+    if (warp == T::kCodeWarp) {
       if (lane == 0) {
         // ---------------- code producer (trellis) ----------------
         uint32_t cuse = 0;
@@ -499,7 +514,7 @@ __global__ void __launch_bounds__(GemmTraits<kK>::kThreads, 1)
     } else {
       // ---------------- decoders (warps 7-22) ----------------
       // Warp d decodes tile column d % 8 of accumulator d / 8.
-      const int dw = warp - 7;
+      const int dw = warp - (T::kCodeWarp + 1);
       const int tn = dw & 7, acc = dw >> 3;
       const GenericGeometry geo = generic_geometry(kK == 4 ? 3 : kK, lane);
       const uint32_t mask = g.mcg_mask, xorv = g.mcg_xor;
@@ -540,6 +555,316 @@ __global__ void __launch_bounds__(GemmTraits<kK>::kThreads, 1)
   if (warp == 1) tmem_free(tmem, kTmemCols);
 }
 
+// ---------------------------------------------------------------------------
+// MXFP4 on an SM pair (cta_group::2).  A pair unit is (chunk, pair block):
+// CTA r of the two-CTA cluster owns weight block 2 * pair_block + r (two
+// accumulators of 128 rows, as in the one-SM kernel) and stages half of the
+// chunk's activation rows (B columns r * N/2 ...); one M = 256 MMA covers
+// both CTAs' rows.  Against the one-SM kernel each CTA stages half the
+// activation bytes per K step, so four stages fit instead of three, and the
+// tensor core reads half of B from each SM's shared memory.  The even CTA's
+// producer takes pair units from the launch's global counter and hands each
+// to both CTAs through a small ring (a remote shared store plus a remote
+// arrive for the odd CTA), so pairs stay balanced however uneven the chunks.
+//
+//   warp 0      producer (each CTA): its weight tiles and scales, its half
+//               of both activation planes and the activation scales, all
+//               counted on the even CTA's full barrier; the even CTA's also
+//               schedules
+//   warp 1      MMA issuer (even CTA), TMEM owner (both)
+//   warps 2-9   epilogue (each CTA): its TMEM -> float32 rows of `out`
+// Every wait is bounded as in the one-SM kernel; the CTAs leave together
+// through a cluster barrier, after every copy and commit that targets the
+// other CTA has landed.
+// ---------------------------------------------------------------------------
+struct PairTraits {
+  static constexpr int kStages = 4;
+  static constexpr int kEpiWarps = 8;
+  static constexpr int kThreads = 64 + 32 * kEpiWarps;
+  static constexpr uint32_t kTileA = 128 * 128;
+  static constexpr uint32_t kTileB = (kMxMaxN / 2) * 128;  // this CTA's half of a plane
+  static constexpr uint32_t kOffA0 = 0, kOffA1 = kTileA;
+  static constexpr uint32_t kOffBhi = 2 * kTileA, kOffBlo = 2 * kTileA + kTileB;
+  static constexpr uint32_t kOffSfa = 2 * kTileA + 2 * kTileB;  // 2 x 512
+  static constexpr uint32_t kOffSfb = kOffSfa + 1024;           // 2 x 512 (N <= 160)
+  static constexpr uint32_t kStageBytes = (kOffSfb + 1024 + 1023) / 1024 * 1024;
+  static constexpr uint32_t kSmemBytes = kStages * kStageBytes + 1024;
+};
+static_assert(PairTraits::kOffBlo % 1024 == 0 && PairTraits::kOffBhi % 1024 == 0, "SW128 tiles start on 1 KB");
+static_assert(PairTraits::kSmemBytes + 256 <= 232448, "pair stages exceed shared memory");
+
+struct PairMaps {
+  CUtensorMap w;       // E2M1 weights, box 128 rows x 128 values
+  CUtensorMap wsc;     // weight scale blocks viewed as [blocks][256] u16, box one 512-byte block
+  CUtensorMap hi, lo;  // activation planes, box 8 rows x 128 values
+  CUtensorMap xsc;     // activation scale blocks, as wsc
+};
+
+struct PairShared {
+  uint64_t full[PairTraits::kStages];   // even CTA: both CTAs' bytes of a stage
+  uint64_t empty[PairTraits::kStages];  // each CTA: its stage may be refilled
+  uint64_t acc_full;                    // each CTA: its accumulators hold a unit
+  uint64_t acc_empty;                   // even CTA: both CTAs' epilogues drained them
+  uint64_t sched_full[kSchedSlots];     // each CTA: sched[slot] holds the next unit
+  uint64_t sched_empty[kSchedSlots];    // even CTA: every reader of the slot in both CTAs is done
+  uint64_t drain;
+  int sched[kSchedSlots];               // pair unit, -1 = no more
+  uint32_t tmem;
+};
+
+// Readers of a schedule slot, all counted on the even CTA's sched_empty: its
+// MMA issuer and epilogue warps, the odd CTA's producer and epilogue warps.
+constexpr int kPairSchedReaders = 2 + 2 * PairTraits::kEpiWarps;
+
+// Next pair unit of this CTA's reader number j: waits for slot j % kSchedSlots
+// (acquire at cluster scope: the even CTA wrote it) and reads it.  Returns
+// -2 on timeout.
+__device__ __forceinline__ int pair_sched_take(PairShared& sh, int j) {
+  const int slot = j % kSchedSlots;
+  if (!mbar_wait_cluster(&sh.sched_full[slot], (j / kSchedSlots) & 1)) return -2;
+  return static_cast<volatile int*>(sh.sched)[slot];
+}
+
+// Releases slot j % kSchedSlots (one arrival on the even CTA's sched_empty).
+__device__ __forceinline__ void pair_sched_release(PairShared& sh, int j) {
+  mbar_arrive_cluster(cluster_addr(smem_u32(&sh.sched_empty[j % kSchedSlots]), 0));
+}
+
+__device__ __forceinline__ UnitInfo pair_unit(const ExpertGemmArgs& g, int unit, int pair_blocks, uint32_t rank) {
+  const MxChunks& c = g.chunks;
+  UnitInfo u;
+  u.proj = 0;
+  u.chunk = unit / pair_blocks;
+  u.block = 2 * (unit % pair_blocks) + static_cast<int>(rank);
+  u.expert = c.chunk_expert[u.chunk];
+  u.start = c.chunk_start[u.chunk];
+  u.rows = c.chunk_rows[u.chunk];
+  u.n16 = (u.rows + 15) & ~15;
+  u.two = true;
+  return u;
+}
+
+__global__ void __launch_bounds__(PairTraits::kThreads, 1)
+    expert_gemm_pair_kernel(const __grid_constant__ PairMaps maps, const ExpertGemmArgs g) {
+  using T = PairTraits;
+  constexpr int kStages = T::kStages;
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ PairShared sh;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  int32_t* header = g.chunks.header;
+  const uint32_t rank = cluster_rank();
+  const int pair_blocks = g.out_features / 512;
+  const int ktiles = g.in_features / kMxKTile;
+  const int kb4 = g.in_features / kMxKTile;  // 512-byte scale blocks per 128 rows
+  const int total = header[0] * pair_blocks;
+
+  for (uint32_t i = threadIdx.x; i < kStages * T::kStageBytes / 16; i += T::kThreads)
+    reinterpret_cast<uint4*>(smem)[i] = make_uint4(0, 0, 0, 0);
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&sh.full[s], 1);
+      mbar_init(&sh.empty[s], 1);
+    }
+    mbar_init(&sh.acc_full, 1);
+    mbar_init(&sh.acc_empty, 2 * T::kEpiWarps);
+    for (int i = 0; i < kSchedSlots; ++i) {
+      mbar_init(&sh.sched_full[i], 1);
+      mbar_init(&sh.sched_empty[i], kPairSchedReaders);
+    }
+    mbar_init(&sh.drain, 1);
+    mbar_fence_init();
+    prefetch_tensor_map(&maps.w);
+    prefetch_tensor_map(&maps.wsc);
+    prefetch_tensor_map(&maps.hi);
+    prefetch_tensor_map(&maps.lo);
+    prefetch_tensor_map(&maps.xsc);
+  }
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  if (warp == 1) tmem_alloc2(&sh.tmem, kTmemCols);
+  tc_fence_before();
+  cluster_sync();  // both CTAs' barriers initialised and TMEM allocated
+  tc_fence_after();
+  const uint32_t tmem = sh.tmem;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- producer (each CTA; the even one schedules) ----------------
+      uint32_t use = 0;
+      bool failed = false;
+      for (int i = 0; !failed; ++i) {
+        int unit;
+        if (rank == 0) {
+          unit = atomicAdd(&header[g.counter_index], 1);
+          if (unit >= total) unit = -1;
+          const int slot = i % kSchedSlots;
+          if (i >= kSchedSlots && !mbar_wait_cluster(&sh.sched_empty[slot], ((i / kSchedSlots) - 1) & 1)) {
+            record_error(header, kErrSched);
+            unit = -1;
+            failed = true;
+          }
+          // This CTA's copy, then the odd CTA's (remote store, ordered before
+          // the remote arrive by its release).
+          sh.sched[slot] = unit;
+          const uint32_t peer_slot = cluster_addr(smem_u32(&sh.sched[slot]), 1);
+          asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(peer_slot), "r"(unit) : "memory");
+          mbar_arrive(&sh.sched_full[slot]);
+          mbar_arrive_cluster(cluster_addr(smem_u32(&sh.sched_full[slot]), 1));
+        } else {
+          unit = pair_sched_take(sh, i);
+          if (unit == -2) {
+            record_error(header, kErrSched);
+            break;
+          }
+          pair_sched_release(sh, i);
+        }
+        if (unit < 0) break;
+        const UnitInfo u = pair_unit(g, unit, pair_blocks, rank);
+        const int64_t w0 = static_cast<int64_t>(u.expert) * g.out_features + acc_row(g, u, 0);
+        const int64_t w1 = static_cast<int64_t>(u.expert) * g.out_features + acc_row(g, u, 1);
+        const int half = u.n16 / 2, nb = (u.n16 + 127) / 128;
+        // Bytes of one CTA; the even CTA expects both CTAs' (the same shape).
+        const uint32_t bytes = 2 * (128 * 64 + 512) + 2 * half * 128 + nb * 512;
+        const int row0 = u.start + static_cast<int>(rank) * half;
+        for (int kt = 0; kt < ktiles; ++kt, ++use) {
+          const int s = use % kStages;
+          if (use >= kStages && !mbar_wait(&sh.empty[s], ((use / kStages) - 1) & 1)) {
+            record_error(header, kErrStage);
+            failed = true;
+            break;
+          }
+          uint8_t* st = smem + s * T::kStageBytes;
+          const uint32_t bar = cluster_addr(smem_u32(&sh.full[s]), 0);
+          if (rank == 0) mbar_arrive_expect_tx(&sh.full[s], 2 * bytes);
+          tma2_load_2d(st + T::kOffA0, &maps.w, kt * kMxKTile, static_cast<int>(w0), bar);
+          tma2_load_2d(st + T::kOffSfa, &maps.wsc, 0, static_cast<int>((w0 / 128) * kb4 + kt), bar);
+          tma2_load_2d(st + T::kOffA1, &maps.w, kt * kMxKTile, static_cast<int>(w1), bar);
+          tma2_load_2d(st + T::kOffSfa + 512, &maps.wsc, 0, static_cast<int>((w1 / 128) * kb4 + kt), bar);
+          for (int r = 0; r < half; r += 8) {
+            tma2_load_2d(st + T::kOffBhi + r * 128, &maps.hi, kt * kMxKTile, row0 + r, bar);
+            tma2_load_2d(st + T::kOffBlo + r * 128, &maps.lo, kt * kMxKTile, row0 + r, bar);
+          }
+          for (int b = 0; b < nb; ++b)
+            tma2_load_2d(st + T::kOffSfb + b * 512, &maps.xsc, 0, (u.start / 128 + b) * kb4 + kt, bar);
+        }
+      }
+      // The MMA issuer's last commits to this CTA's stages (they follow the
+      // MMAs, which followed both CTAs' copies of those stages).
+      for (uint32_t k = 1; k <= static_cast<uint32_t>(kStages) && k <= use; ++k) {
+        const uint32_t last = use - k;
+        if (!mbar_wait(&sh.empty[last % kStages], (last / kStages) & 1)) record_error(header, kErrDrain);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && rank == 0) {
+      // ---------------- MMA issuer (even CTA) ----------------
+      uint32_t use = 0;
+      for (int j = 0;; ++j) {
+        const int unit = pair_sched_take(sh, j);
+        if (unit == -2) {
+          record_error(header, kErrSched);
+          break;
+        }
+        pair_sched_release(sh, j);
+        if (unit < 0) break;
+        const UnitInfo u = pair_unit(g, unit, pair_blocks, rank);
+        if (j >= 1 && !mbar_wait_cluster(&sh.acc_empty, (j - 1) & 1)) {
+          record_error(header, kErrAccEmpty);
+          break;
+        }
+        tc_fence_after();
+        const uint32_t idesc = mx_idesc_pair(kFmtE2M1, kFmtE4M3, u.n16);
+        const int nb = (u.n16 + 127) / 128;
+        bool ok = true;
+        for (int kt = 0; kt < ktiles; ++kt, ++use) {
+          const int s = use % kStages;
+          if (!mbar_wait(&sh.full[s], (use / kStages) & 1)) {
+            record_error(header, kErrFull);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t st = smem_u32(smem + s * T::kStageBytes);
+          tc2_copy_scales(tmem + kTmemSfa, umma_desc_rows16(st + T::kOffSfa));
+          tc2_copy_scales(tmem + kTmemSfa + 4, umma_desc_rows16(st + T::kOffSfa + 512));
+          for (int b = 0; b < nb; ++b)
+            tc2_copy_scales(tmem + kTmemSfb + 4 * b, umma_desc_rows16(st + T::kOffSfb + 512 * b));
+#pragma unroll
+          for (int a = 0; a < 2; ++a) {
+#pragma unroll
+            for (int t = 0; t < 2; ++t) {
+#pragma unroll
+              for (int kk = 0; kk < 4; ++kk) {
+                const uint32_t id = idesc | (static_cast<uint32_t>(kk) << 4) | (static_cast<uint32_t>(kk) << 29);
+                const uint64_t da = umma_desc_sw128(st + (a ? T::kOffA1 : T::kOffA0) + kk * 32);
+                const uint64_t db = umma_desc_sw128(st + (t ? T::kOffBlo : T::kOffBhi) + kk * 32);
+                tc2_mma_mx(tmem + a * kTmemAcc1, da, db, id,
+                           (tmem + kTmemSfa + 4 * a) | (static_cast<uint32_t>(kk) << 30),
+                           (tmem + kTmemSfb) | (static_cast<uint32_t>(kk) << 30), (kt | t | kk) != 0);
+              }
+            }
+          }
+          tc2_commit(cluster_addr(smem_u32(&sh.empty[s]), 0));
+          tc2_commit(cluster_addr(smem_u32(&sh.empty[s]), 1));
+        }
+        if (!ok) break;
+        tc2_commit(cluster_addr(smem_u32(&sh.acc_full), 0));
+        tc2_commit(cluster_addr(smem_u32(&sh.acc_full), 1));
+      }
+      tc2_commit(cluster_addr(smem_u32(&sh.drain), 0));
+      if (!mbar_wait(&sh.drain, 0)) record_error(header, kErrDrain);
+    }
+  } else {
+    // ---------------- epilogue (each CTA, warps 2-9) ----------------
+    constexpr int kParts = T::kEpiWarps / 4;
+    const int quad = warp & 3;
+    const int part = (warp - 2) >> 2;
+    const uint32_t lead_acc_empty = cluster_addr(smem_u32(&sh.acc_empty), 0);
+    for (int j = 0;; ++j) {
+      const int unit = pair_sched_take(sh, j);
+      __syncwarp();
+      if (unit == -2) {
+        if (lane == 0) record_error(header, kErrSched);
+        break;
+      }
+      if (lane == 0) pair_sched_release(sh, j);
+      if (unit < 0) break;
+      const UnitInfo u = pair_unit(g, unit, pair_blocks, rank);
+      if (!mbar_wait(&sh.acc_full, j & 1)) {
+        if (lane == 0) record_error(header, kErrAcc);
+        break;
+      }
+      tc_fence_after();
+      const int64_t base = 32 * quad + lane;
+      float* dst0 = g.out + static_cast<int64_t>(u.start) * g.out_stride + base + acc_row(g, u, 0);
+      float* dst1 = g.out + static_cast<int64_t>(u.start) * g.out_stride + base + acc_row(g, u, 1);
+      const uint32_t lane_addr = tmem + (static_cast<uint32_t>(32 * quad) << 16);
+#pragma unroll 1
+      for (int c0 = 16 * part; c0 < u.n16; c0 += 16 * kParts) {
+        uint32_t v0[16], v1[16];
+        tc_ld16(lane_addr + c0, v0);
+        tc_ld16(lane_addr + kTmemAcc1 + c0, v1);
+        tc_wait_ld();
+        const int n = min(16, u.rows - c0);
+#pragma unroll
+        for (int c = 0; c < 16; ++c)
+          if (c < n) dst0[static_cast<int64_t>(c0 + c) * g.out_stride] = __uint_as_float(v0[c]);
+#pragma unroll
+        for (int c = 0; c < 16; ++c)
+          if (c < n) dst1[static_cast<int64_t>(c0 + c) * g.out_stride] = __uint_as_float(v1[c]);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(lead_acc_empty);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // no copy, commit or arrive still targets the other CTA
+  tc_fence_after();
+  if (warp == 1) tmem_free2(tmem, kTmemCols);
+}
+
 bool encode_2d(CUtensorMap* map, CUtensorMapDataType type, const void* base, uint64_t inner, uint64_t rows,
                uint64_t row_bytes, uint32_t box_inner, uint32_t box_rows) {
   return encode_tiled_2d(map, type, base, inner, rows, row_bytes, box_inner, box_rows, CU_TENSOR_MAP_SWIZZLE_128B);
@@ -569,9 +894,63 @@ cudaError_t launch_variant(const ExpertGemmArgs& args, const GemmMaps& maps, cud
   return cudaGetLastError();
 }
 
+// The SM-pair form for MXFP4 when the shape allows it: one projection,
+// weight blocks in pairs (out_features a multiple of 512) and an even SM count.
+bool pair_eligible(const ExpertGemmArgs& a) {
+  return a.trellis_k == 0 && a.projections == 1 && a.out_features % 512 == 0 && a.in_features % kMxKTile == 0 &&
+         sm_count_cached() % 2 == 0 && gemm_pair_enabled();
+}
+
+cudaError_t launch_pair(const ExpertGemmArgs& args, cudaStream_t s) {
+  using T = PairTraits;
+  PairMaps maps;
+  memset(&maps, 0, sizeof(maps));
+  const uint64_t wrows = static_cast<uint64_t>(args.experts) * args.out_features;
+  const uint64_t kb4 = static_cast<uint64_t>(args.in_features) / kMxKTile;
+  if (!encode_2d(&maps.w, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, args.weights[0], args.in_features, wrows,
+                 args.in_features / 2, 128, 128) ||
+      !encode_tiled_2d(&maps.wsc, CU_TENSOR_MAP_DATA_TYPE_UINT16, args.weight_scales[0], 256, wrows / 128 * kb4, 512,
+                       256, 1, CU_TENSOR_MAP_SWIZZLE_NONE) ||
+      !encode_2d(&maps.hi, CU_TENSOR_MAP_DATA_TYPE_UINT8, args.x_hi[0], args.in_features, args.padded_rows,
+                 args.in_features, 128, 8) ||
+      !encode_2d(&maps.lo, CU_TENSOR_MAP_DATA_TYPE_UINT8, args.x_lo[0], args.in_features, args.padded_rows,
+                 args.in_features, 128, 8) ||
+      !encode_tiled_2d(&maps.xsc, CU_TENSOR_MAP_DATA_TYPE_UINT16, args.x_scales[0], 256,
+                       static_cast<uint64_t>(args.padded_rows) / 128 * kb4, 512, 256, 1, CU_TENSOR_MAP_SWIZZLE_NONE))
+    return cudaErrorInvalidValue;
+  static bool configured = false;
+  if (!configured) {
+    const cudaError_t err = cudaFuncSetAttribute(expert_gemm_pair_kernel,
+                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, T::kSmemBytes);
+    if (err != cudaSuccess) return err;
+    configured = true;
+  }
+  cudaLaunchConfig_t cfg;
+  memset(&cfg, 0, sizeof(cfg));
+  cfg.gridDim = dim3(static_cast<unsigned>(sm_count_cached()));
+  cfg.blockDim = dim3(T::kThreads);
+  cfg.dynamicSmemBytes = T::kSmemBytes;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, expert_gemm_pair_kernel, maps, args);
+}
+
 }  // namespace
 
+static std::atomic<int> g_gemm_pair{1};
+
+bool gemm_pair_enabled() { return g_gemm_pair.load(std::memory_order_relaxed) != 0; }
+
+int set_gemm_pair(int enable) { return enable < 0 ? g_gemm_pair.load() : g_gemm_pair.exchange(enable != 0 ? 1 : 0); }
+
 cudaError_t launch_expert_gemm(const ExpertGemmArgs& args, cudaStream_t s) {
+  if (pair_eligible(args)) return launch_pair(args, s);
   GemmMaps maps;
   memset(&maps, 0, sizeof(maps));
   if (args.trellis_k == 0) {

@@ -69,4 +69,11 @@ __host__ __device__ inline int64_t mx_scale_offset(int64_t row, int64_t kb, int6
 
 cudaError_t launch_expert_gemm(const ExpertGemmArgs& args, cudaStream_t s);
 
+// Whether MXFP4 products whose shape allows it run on SM pairs
+// (cta_group::2); on by default.  The one-SM kernel computes the same sums.
+bool gemm_pair_enabled();
+// Sets the switch (enable 0 or 1) and returns its previous value; enable < 0
+// only reads it.
+int set_gemm_pair(int enable);
+
 }  // namespace exlr8

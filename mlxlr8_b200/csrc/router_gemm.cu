@@ -13,7 +13,10 @@
 // Tile: 128 tokens (M) x 128 experts (N); the K range is split over
 // gridDim.z CTAs whose float32 partials are summed in split order by
 // router_sum_kernel.  Warp 0 loads (TMA), warp 1 issues the MMAs, warps 2-5
-// drain TMEM.  Waits are bounded; a timeout sets error[0].
+// drain TMEM.  A stage holds the pieces of one 64-wide K tile, and the ring
+// has as many stages as twelve 16 KB tiles allow (three for bf16 tokens
+// against the three weight pieces, six for the plain bf16 GEMM).  Waits are
+// bounded; a timeout sets error[0].
 
 #include <cuda.h>
 #include <cuda_bf16.h>
@@ -27,17 +30,16 @@ namespace exlr8 {
 
 namespace {
 
-constexpr int kRgStages = 2;
 constexpr int kRgKTile = 64;                  // bf16 values per 128-byte row
 constexpr uint32_t kRgTile = 128 * 128;       // one 128-row operand tile
-constexpr int kRgMaxA = 3, kRgMaxB = 3;
-constexpr uint32_t kRgStageBytes = (kRgMaxA + kRgMaxB) * kRgTile;
-constexpr uint32_t kRgSmem = kRgStages * kRgStageBytes + 1024;
+constexpr int kRgRingTiles = 12;              // tiles of all stages together
+constexpr int kRgMaxStages = 6;
+constexpr uint32_t kRgSmem = kRgRingTiles * kRgTile + 1024;
 constexpr int kRgThreads = 192;
 
 struct RgShared {
-  uint64_t full[kRgStages];
-  uint64_t empty[kRgStages];
+  uint64_t full[kRgMaxStages];
+  uint64_t empty[kRgMaxStages];
   uint64_t acc_full;
   uint32_t tmem;
 };
@@ -58,8 +60,11 @@ __global__ void __launch_bounds__(kRgThreads, 1)
   const int m0 = blockIdx.x * 128, n0 = blockIdx.y * 128, split = blockIdx.z;
   const int kt0 = split * ktiles_per_split;
   const int ktiles = min(ktiles_per_split, hidden / kRgKTile - kt0);
+  const int stage_tiles = x_pieces + w_pieces;
+  const int stages = min(kRgMaxStages, kRgRingTiles / stage_tiles);
+  const uint32_t stage_stride = stage_tiles * kRgTile;
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kRgStages; ++s) {
+    for (int s = 0; s < stages; ++s) {
       mbar_init(&sh.full[s], 1);
       mbar_init(&sh.empty[s], 1);
     }
@@ -73,46 +78,47 @@ __global__ void __launch_bounds__(kRgThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = sh.tmem;
-  const uint32_t stage_bytes = (x_pieces + w_pieces) * kRgTile;
+  const uint32_t stage_bytes = stage_tiles * kRgTile;
 
   if (warp == 0) {
     if (lane == 0) {
       int kt = 0;
       for (; kt < ktiles; ++kt) {
-        const int s = kt % kRgStages;
-        if (kt >= kRgStages && !mbar_wait(&sh.empty[s], ((kt / kRgStages) - 1) & 1)) {
+        const int s = kt % stages;
+        if (kt >= stages && !mbar_wait(&sh.empty[s], ((kt / stages) - 1) & 1)) {
           atomicCAS(error, 0, 1);
           break;
         }
-        uint8_t* st = smem + s * kRgStageBytes;
+        uint8_t* st = smem + s * stage_stride;
         const int k = (kt0 + kt) * kRgKTile;
         mbar_arrive_expect_tx(&sh.full[s], stage_bytes);
         for (int i = 0; i < x_pieces; ++i) tma_load_2d(st + i * kRgTile, &xmap, k, i * tokens + m0, &sh.full[s]);
-        for (int j = 0; j < w_pieces; ++j) tma_load_2d(st + (kRgMaxA + j) * kRgTile, &wmap, k, j * n + n0, &sh.full[s]);
+        for (int j = 0; j < w_pieces; ++j)
+          tma_load_2d(st + (x_pieces + j) * kRgTile, &wmap, k, j * n + n0, &sh.full[s]);
       }
       // Copies still in flight must land before the CTA exits.
-      for (int u = max(0, kt - kRgStages); u < kt; ++u)
-        if (!mbar_wait(&sh.full[u % kRgStages], (u / kRgStages) & 1)) atomicCAS(error, 0, 2);
+      for (int u = max(0, kt - stages); u < kt; ++u)
+        if (!mbar_wait(&sh.full[u % stages], (u / stages) & 1)) atomicCAS(error, 0, 2);
     }
   } else if (warp == 1) {
     if (lane == 0) {
       const uint32_t idesc = bf16_idesc(128);
       bool ok = true;
       for (int kt = 0; kt < ktiles; ++kt) {
-        const int s = kt % kRgStages;
-        if (!mbar_wait(&sh.full[s], (kt / kRgStages) & 1)) {
+        const int s = kt % stages;
+        if (!mbar_wait(&sh.full[s], (kt / stages) & 1)) {
           atomicCAS(error, 0, 3);
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t st = smem_u32(smem + s * kRgStageBytes);
+        const uint32_t st = smem_u32(smem + s * stage_stride);
         for (int i = 0; i < x_pieces; ++i) {
           for (int j = 0; j < w_pieces && i + j <= 2; ++j) {
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk) {
               tc_mma_f16(tmem, umma_desc_sw128(st + i * kRgTile + kk * 32),
-                         umma_desc_sw128(st + (kRgMaxA + j) * kRgTile + kk * 32), idesc,
+                         umma_desc_sw128(st + (x_pieces + j) * kRgTile + kk * 32), idesc,
                          (kt | i | j | kk) != 0);
             }
           }
@@ -255,13 +261,14 @@ cudaError_t launch_dense_swiglu(const float* gate_partial, const float* up_parti
   return cudaGetLastError();
 }
 
-// K splits so that the grid covers the SMs; every split gets at least one
-// 64-wide K tile.
+// K splits so that the grid fills the SMs in one wave (one CTA per SM: the
+// ring takes most of shared memory); every split gets at least one 64-wide
+// K tile.
 int bf16_gemm_splits(int tokens, int k, int n) {
   const int mtiles = (tokens + 127) / 128;
   const int ntiles = n / 128;
   const int ktiles = k / kRgKTile;
-  int splits = (sm_count() + mtiles * ntiles - 1) / (mtiles * ntiles);
+  int splits = sm_count() / (mtiles * ntiles);
   if (splits > 8) splits = 8;
   if (splits > ktiles) splits = ktiles;
   if (splits < 1) splits = 1;

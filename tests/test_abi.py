@@ -117,3 +117,16 @@ def test_noalloc_rejects_a_bad_struct_before_sizing():
     good = _bad_struct(hidden=256, intermediate=128)
     good.scale_experts = 3
     assert lib.exlr8_moe_layer_noalloc(16, 2, 16, 1, 16, 16, ctypes.byref(good), None, 16, None, None, None) == 5
+
+
+def test_gemm_pair_switch_round_trips():
+    """The SM-pair GEMM switch is host state: set, read back, restored."""
+    lib = _lib.lib()
+    previous = lib.exlr8_gemm_pair(0)
+    try:
+        assert previous == 1
+        assert lib.exlr8_gemm_pair(-1) == 0
+        assert lib.exlr8_gemm_pair(1) == 0
+        assert lib.exlr8_gemm_pair(-1) == 1
+    finally:
+        lib.exlr8_gemm_pair(previous)

@@ -235,6 +235,42 @@ def test_glm_prefill_shape_sampled_tokens():
     assert_mxfp4_close(got - host(residual)[sample], expected - host(residual)[sample])
 
 
+@pytest.mark.parametrize("tokens", [700, 4096])
+def test_pair_and_single_sm_gemms_agree(tokens):
+    """The SM-pair GEMM (two-CTA clusters, M = 256 tcgen05 MMAs with the
+    activation tile split between the SMs) issues, per accumulator, the MMAs
+    of the one-SM GEMM in the same order: the layer's outputs are identical
+    bit for bit, neither form records a pipeline error, and the pair result
+    matches the oracle on sampled tokens.  700 tokens give chunks of 16-48
+    rows (odd half tiles of 8-row boxes), 4096 tokens full 160-row chunks."""
+    import torch
+
+    from mlxlr8_b200 import _lib
+    from mlxlr8_b200.joined_mxfp4 import JoinedMoELayer
+
+    lib = _lib.lib()
+    j, joined = _joined(seed=21, h=512, m=256, experts=257)
+    layer = JoinedMoELayer(j.gate_weight, j.bias, joined)
+    x, residual = j.tokens(tokens)
+    previous = lib.exlr8_gemm_pair(1)
+    try:
+        pair, ids, scores = layer(x, residual, return_routing=True)
+        pair = pair.clone()
+        torch.cuda.synchronize()
+        assert layer.dispatch_header(tokens)[4] == 0
+        lib.exlr8_gemm_pair(0)
+        single = layer(x, residual).clone()
+        torch.cuda.synchronize()
+        assert layer.dispatch_header(tokens)[4] == 0
+    finally:
+        lib.exlr8_gemm_pair(previous)
+    assert torch.equal(pair, single)
+    sample = np.arange(0, tokens, 97)
+    values = _oracle_slots(j, x[sample], ids.cpu().numpy()[sample])
+    expected = ref.combine(values, scores.cpu().numpy()[sample], host(residual)[sample], "bfloat16")
+    assert_mxfp4_close(host(pair)[sample] - host(residual)[sample], expected - host(residual)[sample])
+
+
 # ---- decode batches (<= 16 tokens): the MXFP4 streaming GEMV ----------------
 
 @pytest.mark.parametrize("dtype", ["bfloat16", "float32"])
