@@ -257,7 +257,7 @@ __global__ void __launch_bounds__(kRowWarps * 32) trellis_prep_kernel(
 // Hadamard, out scales, typed SwiGLU, down in scale, Hadamard; quantised into
 // the down GEMM's activation planes.  One warp per padded row.
 template <int kAct, int kScale>
-__global__ void __launch_bounds__(kRowWarps * 32) joined_gate_finish_kernel(
+__global__ void __launch_bounds__(kRowWarps * 32, 5) joined_gate_finish_kernel(
     const float* __restrict__ gu, const uint32_t* __restrict__ ids, int slots, MxChunks c,
     const void* __restrict__ gate_out, const void* __restrict__ up_out, const void* __restrict__ down_in,
     int intermediate, uint8_t* __restrict__ hi, uint8_t* __restrict__ lo, uint8_t* __restrict__ scales) {
@@ -275,20 +275,24 @@ __global__ void __launch_bounds__(kRowWarps * 32) joined_gate_finish_kernel(
     const int64_t e = ids[slot];
     const float* g_row = gu + static_cast<int64_t>(row) * 2 * intermediate + lane;
     for (int block = b0; block < b1; ++block) {
-      float g[4], u[4], h[4];
+      // The block's gate and up values and its three scale vectors' entries
+      // go out together (one round trip per block).
+      float g[4], u[4], h[4], sg[4], su[4], sd[4];
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         g[j] = __ldcs(g_row + block * 128 + 32 * j);
         u[j] = __ldcs(g_row + intermediate + block * 128 + 32 * j);
+        const int64_t si = e * intermediate + block * 128 + lane + 32 * j;
+        sg[j] = load_scale(gate_out, kScale, si);
+        su[j] = load_scale(up_out, kScale, si);
+        sd[j] = load_scale(down_in, kScale, si);
       }
       hadamard128(g, lane);
       hadamard128(u, lane);
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        const int64_t si = e * intermediate + block * 128 + lane + 32 * j;
-        const float act = swiglu_typed(kAct, __fmul_rn(g[j], load_scale(gate_out, kScale, si)),
-                                       __fmul_rn(u[j], load_scale(up_out, kScale, si)));
-        h[j] = __fmul_rn(act, load_scale(down_in, kScale, si));
+        const float act = swiglu_typed(kAct, __fmul_rn(g[j], sg[j]), __fmul_rn(u[j], su[j]));
+        h[j] = __fmul_rn(act, sd[j]);
       }
       hadamard128(h, lane);
       store_words(quantize_words(h, tbuf[warp], lane), row, block, intermediate, hi, lo, scales, lane);
@@ -325,6 +329,12 @@ __global__ void __launch_bounds__(288) joined_finish_kernel(const float* __restr
   {
     const int b0 = blockIdx.y * kFinishGroup;
     const int nb = min(kFinishGroup, blocks - b0);
+    // The residual of the (at most two) columns this thread sums below, loaded
+    // with the slot rows so that the sum phase waits on no memory.
+    const int64_t base = token * features + b0 * 128;
+    const int c_a = threadIdx.x, c_b = threadIdx.x + 288;
+    const float res_a = c_a < nb * 128 ? load_act(residual, kAct, base + c_a) : 0.0f;
+    const float res_b = c_b < nb * 128 ? load_act(residual, kAct, base + c_b) : 0.0f;
     float val[kFinishGroup][4];
 #pragma unroll
     for (int g = 0; g < kFinishGroup; ++g)
@@ -355,14 +365,17 @@ __global__ void __launch_bounds__(288) joined_finish_kernel(const float* __restr
       }
     }
     __syncthreads();
-    for (int c = threadIdx.x; c < nb * 128; c += 288) {
+    static_assert(kFinishGroup * 128 <= 2 * 288, "two columns per thread cover the group");
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int c = h ? c_b : c_a;
+      if (c >= nb * 128) break;
       float total = __fadd_rn(products[0][c], 0.0f);
 #pragma unroll
       for (int r = 1; r < 8; ++r) total = __fadd_rn(__fadd_rn(products[r][c], 0.0f), total);
-      const int64_t off = token * features + b0 * 128 + c;
       const float routed = round_to(kAct, total);
       const float combined = round_to(kAct, __fadd_rn(routed, round_to(kAct, products[8][c])));
-      store_act(out, kAct, off, __fadd_rn(load_act(residual, kAct, off), combined));
+      store_act(out, kAct, base + c, __fadd_rn(h ? res_b : res_a, combined));
     }
     __syncthreads();
   }

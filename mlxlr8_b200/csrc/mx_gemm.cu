@@ -572,14 +572,14 @@ __global__ void __launch_bounds__(GemmTraits<kK>::kThreads, 1)
 //               counted on the even CTA's full barrier; the even CTA's also
 //               schedules
 //   warp 1      MMA issuer (even CTA), TMEM owner (both)
-//   warps 2-9   epilogue (each CTA): its TMEM -> float32 rows of `out`
+//   warps 2-17  epilogue (each CTA): its TMEM -> float32 rows of `out`
 // Every wait is bounded as in the one-SM kernel; the CTAs leave together
 // through a cluster barrier, after every copy and commit that targets the
 // other CTA has landed.
 // ---------------------------------------------------------------------------
 struct PairTraits {
   static constexpr int kStages = 4;
-  static constexpr int kEpiWarps = 8;
+  static constexpr int kEpiWarps = 16;  // four per TMEM sub-partition: the accumulators drain in a quarter of the time
   static constexpr int kThreads = 64 + 32 * kEpiWarps;
   static constexpr uint32_t kTileA = 128 * 128;
   static constexpr uint32_t kTileB = (kMxMaxN / 2) * 128;  // this CTA's half of a plane
@@ -815,7 +815,7 @@ __global__ void __launch_bounds__(PairTraits::kThreads, 1)
       if (!mbar_wait(&sh.drain, 0)) record_error(header, kErrDrain);
     }
   } else {
-    // ---------------- epilogue (each CTA, warps 2-9) ----------------
+    // ---------------- epilogue (each CTA, warps 2-17) ----------------
     constexpr int kParts = T::kEpiWarps / 4;
     const int quad = warp & 3;
     const int part = (warp - 2) >> 2;

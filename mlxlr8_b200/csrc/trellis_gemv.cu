@@ -366,11 +366,13 @@ cudaError_t launch_prep_frag(const void* x, int x_dtype, int per_slot, int slots
 
 // gate/up split sum, Hadamard, output scales, typed SwiGLU, down input scale,
 // Hadamard -> down fragment record.  One warp per (slot, 128-wide block of
-// the intermediate features).  All split partials of a warp are loaded
-// before the first add (one round trip; they do not depend on the expert id)
-// and summed in split order.  Warps past the slots' blocks form the bf16
-// shared expert's h = SwiGLU(T(g), T(u)), one per (token, 128-wide block).
-constexpr int kGateFinishSplits = 8;  // splits loaded per round trip
+// the intermediate features).  The partials of up to kGateFinishSplits
+// splits and the id's three scale vectors are in flight together (the
+// partials do not depend on the expert id; the scales need only the id),
+// then the splits are summed in split order.  Warps past the slots' blocks
+// form the bf16 shared expert's h = SwiGLU(T(g), T(u)), one per (token,
+// 128-wide block).
+constexpr int kGateFinishSplits = 16;  // splits loaded per round trip (the most gate_up_splits chooses)
 
 __global__ void __launch_bounds__(kFragWarps * 32) gate_finish_frag_kernel(
     const float* __restrict__ partial, int gu_splits, const uint32_t* __restrict__ ids, int nslots,
@@ -410,6 +412,9 @@ __global__ void __launch_bounds__(kFragWarps * 32) gate_finish_frag_kernel(
   const float* pu = partial + (static_cast<int64_t>(nslots) + slot) * gu_splits * features + c0;
   const uint32_t id = ids[slot];
   float gate[4] = {0.f, 0.f, 0.f, 0.f}, up[4] = {0.f, 0.f, 0.f, 0.f};
+  float sg[4], su[4], sd[4];
+  const int64_t e = id;
+  const bool ok = e < experts;
   for (int s0 = 0; s0 < gu_splits; s0 += kGateFinishSplits) {
     float lg[kGateFinishSplits][4], lu[kGateFinishSplits][4];
 #pragma unroll
@@ -420,6 +425,15 @@ __global__ void __launch_bounds__(kFragWarps * 32) gate_finish_frag_kernel(
         const int64_t o = static_cast<int64_t>(s0 + sp) * features + 32 * j;
         lg[sp][j] = have ? __ldcg(pg + o) : 0.0f;
         lu[sp][j] = have ? __ldcg(pu + o) : 0.0f;
+      }
+    }
+    if (s0 == 0) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int64_t si = (ok ? e : 0) * features + c0 + 32 * j;
+        sg[j] = load_scale(out_gate, scale_dtype, si);
+        su[j] = load_scale(out_up, scale_dtype, si);
+        sd[j] = load_scale(in_down, scale_dtype, si);
       }
     }
 #pragma unroll
@@ -433,15 +447,14 @@ __global__ void __launch_bounds__(kFragWarps * 32) gate_finish_frag_kernel(
       }
     }
   }
-  const int64_t e = id;
-  const bool ok = e < experts;
-  float sg[4], su[4], sd[4];
+  if (gu_splits <= 0) {
 #pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const int64_t si = (ok ? e : 0) * features + c0 + 32 * j;
-    sg[j] = load_scale(out_gate, scale_dtype, si);
-    su[j] = load_scale(out_up, scale_dtype, si);
-    sd[j] = load_scale(in_down, scale_dtype, si);
+    for (int j = 0; j < 4; ++j) {
+      const int64_t si = (ok ? e : 0) * features + c0 + 32 * j;
+      sg[j] = load_scale(out_gate, scale_dtype, si);
+      su[j] = load_scale(out_up, scale_dtype, si);
+      sd[j] = load_scale(in_down, scale_dtype, si);
+    }
   }
   hadamard128(gate, lane);
   hadamard128(up, lane);
@@ -528,6 +541,8 @@ cudaError_t launch_finish(const float* partial, int splits, const int32_t* row_m
 // it holds the typed shared-expert output [tokens][h] and slot 8 of partial is
 // not read.  shared_values are the dense shared expert's float32 split
 // partials, summed and cast here.
+constexpr int kFinishSplits = 16;  // down-split partials loaded per round trip
+
 __global__ void __launch_bounds__(288) finish_fused_kernel(const float* __restrict__ partial, int splits,
                                                            const int32_t* __restrict__ row_map,
                                                            const uint32_t* __restrict__ ids, int tokens,
@@ -567,20 +582,31 @@ __global__ void __launch_bounds__(288) finish_fused_kernel(const float* __restri
     const int64_t e = ids[row];
     const float weight = slot < 8 ? scores[token * 8 + slot] : 1.0f;
     const int64_t prow = row_map ? row_map[row] : static_cast<int64_t>(row) * splits;
-    float v[4] = {0.f, 0.f, 0.f, 0.f};
-    if (prow >= 0) {
-      const float* ps = partial + prow * features + block * 128 + lane;
-#pragma unroll 4
-      for (int s = 0; s < splits; ++s) {
-#pragma unroll
-        for (int j = 0; j < 4; ++j) v[j] += __ldcg(ps + static_cast<int64_t>(s) * features + 32 * j);
-      }
-    }
     const bool ok = e < experts && prow >= 0;  // an out-of-range id contributes zero
+    // The output scales and up to kFinishSplits splits' partials go out
+    // together, then the splits are summed in split order.
     float sc[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j)
       sc[j] = load_scale(out_scale, scale_dtype, (ok ? e : 0) * features + block * 128 + lane + 32 * j);
+    float v[4] = {0.f, 0.f, 0.f, 0.f};
+    if (prow >= 0) {
+      const float* ps = partial + prow * features + block * 128 + lane;
+      for (int s0 = 0; s0 < splits; s0 += kFinishSplits) {
+        float lv[kFinishSplits][4];
+#pragma unroll
+        for (int sp = 0; sp < kFinishSplits; ++sp)
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            lv[sp][j] = s0 + sp < splits ? __ldcg(ps + static_cast<int64_t>(s0 + sp) * features + 32 * j) : 0.0f;
+#pragma unroll
+        for (int sp = 0; sp < kFinishSplits; ++sp)
+          if (s0 + sp < splits) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) v[j] += lv[sp][j];
+          }
+      }
+    }
     hadamard128(v, lane);
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
