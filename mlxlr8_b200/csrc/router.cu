@@ -183,31 +183,18 @@ __global__ void __launch_bounds__(kGateWarps * 32) route_plan_kernel(
   pdl_launch_dependents();  // the prep kernel may launch and wait for this grid
   extern __shared__ int sm[];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  pdl_wait();
   const int rows = tokens * 9;
   if (rows <= kSmallPlanRows) {
-    // Decode batches: the ids stay in shared memory for the plan.  This one
-    // CTA runs on one SM, where its code would be fetched cold after the gate
-    // grid completes; so the same code (one loop body, not a second copy)
-    // first runs on stand-in logits -- the bias row for every token -- while
-    // the gate grid still runs, writing ids, scores and a plan that the real
-    // pass then overwrites (nothing reads them before this grid completes:
-    // earlier work in the stream finished before the gate grid began).
+    // Decode batches: the ids stay in shared memory for the plan.
     uint32_t* s_ids = reinterpret_cast<uint32_t*>(sm);
-#pragma unroll 1
-    for (int pass = 0; pass < 2; ++pass) {
-      if (pass == 1) pdl_wait();
-      const float* src = pass ? logits : bias;
-      const int64_t stride = pass ? 256 : 0;
-      for (int t = warp; t < tokens; t += kGateWarps)
-        route_warp(src + t * stride, bias, ids + static_cast<int64_t>(t) * 9, scores + static_cast<int64_t>(t) * 8,
-                   2.5f, 256u, lane, s_ids + t * 9);
-      __syncthreads();
-      small_plan_body(s_ids, rows, plan_experts, 9, skip_slot, plan, sm + rows);
-      __syncthreads();
-    }
+    for (int t = warp; t < tokens; t += kGateWarps)
+      route_warp(logits + static_cast<int64_t>(t) * 256, bias, ids + static_cast<int64_t>(t) * 9,
+                 scores + static_cast<int64_t>(t) * 8, 2.5f, 256u, lane, s_ids + t * 9);
+    __syncthreads();
+    small_plan_body(s_ids, rows, plan_experts, 9, skip_slot, plan, sm + rows);
     return;
   }
-  pdl_wait();
   for (int t = warp; t < tokens; t += kGateWarps)
     route_warp(logits + static_cast<int64_t>(t) * 256, bias, ids + static_cast<int64_t>(t) * 9,
                scores + static_cast<int64_t>(t) * 8, 2.5f, 256u, lane);
