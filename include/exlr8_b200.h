@@ -177,6 +177,34 @@ int exlr8_route(const float* logits, const float* bias, int64_t rows, uint32_t* 
 int exlr8_router(const void* x, int x_dtype, int64_t tokens, int hidden, const float* gate_weight,
                  const float* bias, float* logits, uint32_t* indices, float* scores, void* stream);
 
+/* ---- dispatch and combine --------------------------------------------- */
+
+/* exlr8/fast_prefill.py:38-46 _plan(indices, experts, block_rows) with the
+ * block table of :19-35 _segment_table: ids uint32 [rows] (flattened slot
+ * ids) -> order uint32 [rows] (slots sorted by id, stable), sorted_ids uint32
+ * [rows] = ids[order], and table uint32 [3][table_capacity]: for each expert
+ * e in order, ceil(count_e / block_rows) columns (e, first sorted row,
+ * length <= block_rows); *count (device int32) = the number of columns.
+ * table_capacity >= min(rows, rows / block_rows + experts), the reference's
+ * width; columns past *count are not written.  Ids >= experts follow every
+ * valid id in row order and are left out of the table (the reference's
+ * argsort orders them by value; they are outside its contract).
+ * 1 <= experts <= 1024.  Workspace: exlr8_dispatch_plan_workspace. */
+size_t exlr8_dispatch_plan_workspace(int64_t rows, int experts);
+int exlr8_dispatch_plan(const uint32_t* ids, int64_t rows, int experts, int block_rows, uint32_t* order,
+                        uint32_t* sorted_ids, uint32_t* table, int64_t table_capacity, int32_t* count,
+                        void* workspace, size_t workspace_bytes, void* stream);
+
+/* exlr8/model.py:415-418 combine of per-slot expert outputs: values [tokens]
+ * [9][hidden] in `dtype` (slot 8 = the shared expert), scores float32
+ * [tokens][8], residual and out [tokens][hidden] in `dtype`:
+ * out = T(residual + T(T(sum_r values[r] * scores[r]) + values[8])), the
+ * routed sum in float32 in the order of
+ * metal/fast_decode_finish_fused.metal:52-57 (slot 0, then
+ * (slot r + 0) + total for r = 1..7). */
+int exlr8_combine(const void* values, const float* scores, const void* residual, int64_t tokens, int hidden,
+                  int dtype, void* out, void* stream);
+
 /* ---- trellis expert operators ----------------------------------------- */
 
 /* exlr8/trellis.py:172-196 expert_linear and fast_decode.py:153-165

@@ -75,6 +75,10 @@ _SIGNATURES = {
     "exlr8_dequantize_trellis": (c_int, [c_void_p, c_int64, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int,
                                          c_void_p, c_void_p, c_size_t, c_void_p]),
     "exlr8_route": (c_int, [c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_void_p]),
+    "exlr8_dispatch_plan_workspace": (c_size_t, [c_int64, c_int]),
+    "exlr8_dispatch_plan": (c_int, [c_void_p, c_int64, c_int, c_int, c_void_p, c_void_p, c_void_p, c_int64, c_void_p,
+                                    c_void_p, c_size_t, c_void_p]),
+    "exlr8_combine": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int, c_int, c_void_p, c_void_p]),
     "exlr8_router": (c_int, [c_void_p, c_int, c_int64, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                              c_void_p]),
     "exlr8_expert_linear_workspace": (c_size_t, [c_int64, c_int, c_int, c_int, c_int64]),

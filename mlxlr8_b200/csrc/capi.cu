@@ -1,6 +1,7 @@
 // extern "C" entry points of include/exlr8_b200.h: argument validation with
 // the reference's error semantics, workspace layout and kernel sequencing.
 
+#include <algorithm>
 #include <cstdio>
 #include <cstring>
 
@@ -9,6 +10,7 @@
 #include "common.cuh"
 #include "dense.cuh"
 #include "dense_stream.cuh"
+#include "dispatch.cuh"
 #include "ep.cuh"
 #include "joined.cuh"
 #include "mx_gemm.cuh"
@@ -571,6 +573,35 @@ int exlr8_route(const float* logits, const float* bias, int64_t rows, uint32_t* 
   if (rows < 0 || (rows > 0 && (!logits || !bias || !indices || !scores))) return EXLR8_ERR_ARG;
   return cuda_status(launch_route(logits, bias, static_cast<int>(rows), indices, scores, 2.5f, 256u,
                                   as_stream(stream)));
+}
+
+size_t exlr8_dispatch_plan_workspace(int64_t rows, int experts) {
+  if (rows < 0 || rows > (int64_t(1) << 30) || experts < 1 || experts > kDispatchMaxExperts) return kBadSize;
+  return align_up(plan_bytes(static_cast<int>(rows), experts));
+}
+
+int exlr8_dispatch_plan(const uint32_t* ids, int64_t rows, int experts, int block_rows, uint32_t* order,
+                        uint32_t* sorted_ids, uint32_t* table, int64_t table_capacity, int32_t* count,
+                        void* workspace, size_t workspace_bytes, void* stream) {
+  if (rows < 0 || rows > (int64_t(1) << 30) || experts < 1 || experts > kDispatchMaxExperts || block_rows < 1)
+    return EXLR8_ERR_ARG;
+  // The reference's table width: min(rows, rows / block_rows + experts) columns.
+  const int64_t need = std::min<int64_t>(rows, rows / block_rows + experts);
+  if (table_capacity < need || !count || (rows > 0 && (!ids || !order || !sorted_ids || !table)))
+    return EXLR8_ERR_ARG;
+  if (!workspace || workspace_bytes < exlr8_dispatch_plan_workspace(rows, experts)) return EXLR8_ERR_WORKSPACE;
+  const PlanView plan = plan_view(workspace, static_cast<int>(rows), experts);
+  return cuda_status(launch_dispatch_plan(ids, static_cast<int>(rows), experts, block_rows, plan, order, sorted_ids,
+                                          table, table_capacity, count, as_stream(stream)));
+}
+
+int exlr8_combine(const void* values, const float* scores, const void* residual, int64_t tokens, int hidden,
+                  int dtype, void* out, void* stream) {
+  if (!valid_act(dtype)) return EXLR8_ERR_DTYPE;
+  if (tokens < 0 || hidden <= 0) return EXLR8_ERR_ARG;
+  if (tokens == 0) return EXLR8_OK;
+  if (!values || !scores || !residual || !out) return EXLR8_ERR_ARG;
+  return cuda_status(launch_combine(values, scores, residual, tokens, hidden, dtype, out, as_stream(stream)));
 }
 
 int exlr8_router(const void* x, int x_dtype, int64_t tokens, int hidden, const float* gate_weight, const float* bias,

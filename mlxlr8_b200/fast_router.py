@@ -1,7 +1,9 @@
 """Fused router (mirror of ``exlr8/fast_router.py``).
 
 ``route`` is the sigmoid + bias top-8 with renormalisation times 2.5 and the
-shared expert id 256 appended (fast_router.metal:1-42).  ``router`` adds the
+shared expert id 256 appended (fast_router.metal:1-42); ``combine`` is the
+weighted sum of per-slot expert outputs with the shared expert and the
+residual (model.py:415-418).  ``router`` adds the
 float32 gate GEMV in front (model.py:366-371).  ``compiled_finish`` returns
 the whole MoE-layer call ``(x, residual) -> residual + moe(x)``
 (fast_router.py:27-37).  Indices are returned as int32 (torch's uint32
@@ -28,6 +30,27 @@ def route(logits: torch.Tensor, bias: torch.Tensor):
     _lib.check(_lib.lib().exlr8_route(values.data_ptr(), correction.data_ptr(), rows, ids.data_ptr(),
                                       scores.data_ptr(), _lib.stream_handle(device)))
     return ids, scores
+
+
+def combine(values: torch.Tensor, scores: torch.Tensor, residual: torch.Tensor) -> torch.Tensor:
+    """``residual + T(T(sum_r values[..., r, :] * scores[..., r]) + values[..., 8, :])``
+    (model.py:415-418) for per-slot expert outputs ``values [..., 9, h]`` in
+    the residual's dtype (slot 8 the shared expert), the routed sum in
+    float32 in the order of metal/fast_decode_finish_fused.metal:52-57."""
+    device = _lib.require_cuda(values, scores, residual)
+    h = residual.shape[-1]
+    if values.shape[-2:] != (9, h) or values.dtype != residual.dtype:
+        raise ValueError("values must be [..., 9, hidden] in the residual's dtype")
+    tokens = residual.numel() // h
+    if scores.numel() != tokens * 8:
+        raise ValueError("scores must be [..., 8]")
+    v = values.contiguous()
+    sc = scores.to(torch.float32).contiguous()
+    res = residual.contiguous()
+    out = torch.empty_like(res)
+    _lib.check(_lib.lib().exlr8_combine(v.data_ptr(), sc.data_ptr(), res.data_ptr(), tokens, h, _lib.act_code(res),
+                                        out.data_ptr(), _lib.stream_handle(device)))
+    return out
 
 
 def router(x: torch.Tensor, gate_weight: torch.Tensor, bias: torch.Tensor):

@@ -96,6 +96,9 @@ def _bad_struct(hidden=6144, intermediate=64, experts=257):
     ("exlr8_expert_linear_workspace", (1, 9, 6144, 64, 257)),
     ("exlr8_shared_expert_workspace", (1, 6144, 64)),
     ("exlr8_joined_moe_layer_workspace", (1, 6144, 64, 257)),
+    ("exlr8_dispatch_plan_workspace", (-1, 257)),
+    ("exlr8_dispatch_plan_workspace", (36864, 0)),
+    ("exlr8_dispatch_plan_workspace", (36864, 2048)),
 ])
 def test_workspace_queries_reject_unusable_sizes(query, args):
     """Sizes no call accepts answer SIZE_MAX instead of dividing by a zero
@@ -130,3 +133,18 @@ def test_gemm_pair_switch_round_trips():
         assert lib.exlr8_gemm_pair(-1) == 1
     finally:
         lib.exlr8_gemm_pair(previous)
+
+
+def test_dispatch_plan_and_combine_reject_bad_arguments_without_a_gpu():
+    """Argument checks run before any device work: a table narrower than the
+    reference's width, a block size of zero and an unknown dtype."""
+    lib = _lib.lib()
+    ws = lib.exlr8_dispatch_plan_workspace(100, 257)
+    assert 0 < ws < ctypes.c_size_t(-1).value
+    buf = ctypes.create_string_buffer(16)
+    p = ctypes.addressof(buf)
+    # width min(100, 100 // 8 + 257) = 100 columns; one fewer is refused
+    narrow = lib.exlr8_dispatch_plan(p, 100, 257, 8, p, p, p, 99, p, p, ws, None)
+    assert narrow != 0 and "argument" in lib.exlr8_status_string(narrow).decode().lower()
+    assert lib.exlr8_dispatch_plan(p, 100, 257, 0, p, p, p, 100, p, p, ws, None) == narrow
+    assert lib.exlr8_combine(p, p, p, 1, 128, 99, p, None) != 0
