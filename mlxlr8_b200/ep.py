@@ -37,15 +37,45 @@ from .experts import ExpertLayer
 from .fast_decode import dense_expert, fast_expert_mlp, trellis_experts
 
 
-def shard_experts(layer: ExpertLayer, rank: int, world: int, routed: int = 256) -> ExpertLayer:
-    """The routed experts of `rank` (contiguous blocks of routed / world)."""
+def seeded_placement(seed: int, routed: int = 256, device="cuda") -> torch.Tensor:
+    """A seeded permutation of the routed experts over the ranks:
+    ``placement[e]`` is expert e's position in the rank-major order, so rank
+    r owns the experts placed at [r * per, (r + 1) * per).  Under skewed
+    (Zipf) routing it spreads the popular experts over the ranks instead of
+    leaving the lowest ids on rank 0."""
+    g = torch.Generator(device="cpu")
+    g.manual_seed(seed)
+    return torch.randperm(routed, generator=g).to(device=device, dtype=torch.int32)
+
+
+def _owned(rank: int, world: int, routed: int, placement: torch.Tensor | None) -> list[int]:
+    per = routed // world
+    if placement is None:
+        return list(range(rank * per, (rank + 1) * per))
+    order = torch.argsort(placement.to("cpu", torch.int64)).tolist()  # position -> expert
+    return order[rank * per:(rank + 1) * per]
+
+
+def shard_experts(layer: ExpertLayer, rank: int, world: int, routed: int = 256,
+                  placement: torch.Tensor | None = None) -> ExpertLayer:
+    """The routed experts of `rank`: contiguous blocks of routed / world, or
+    with `placement` (``seeded_placement``) the experts placed at this rank's
+    positions, in position order."""
     if routed % world:
         raise ValueError("routed experts must divide evenly over the ranks")
-    per = routed // world
-    lo, hi = rank * per, (rank + 1) * per
+    if placement is not None and sorted(placement.tolist()) != list(range(routed)):
+        raise ValueError("placement must be a permutation of the routed experts")
+    owned = _owned(rank, world, routed, placement)
     nbytes = layer.expert_bytes
-    packed = {p: layer.packed[p][lo * nbytes:hi * nbytes] for p in ("gate", "up", "down")}
-    scales = {p: tuple(s[lo:hi] for s in layer.scales[p]) for p in ("gate", "up", "down")}
+    if placement is None:
+        lo, hi = owned[0], owned[-1] + 1
+        packed = {p: layer.packed[p][lo * nbytes:hi * nbytes] for p in ("gate", "up", "down")}
+        scales = {p: tuple(s[lo:hi] for s in layer.scales[p]) for p in ("gate", "up", "down")}
+    else:
+        idx = torch.tensor(owned, dtype=torch.int64, device=layer.packed["gate"].device)
+        packed = {p: torch.cat([layer.packed[p][e * nbytes:(e + 1) * nbytes] for e in owned])
+                  for p in ("gate", "up", "down")}
+        scales = {p: tuple(s.index_select(0, idx.to(s.device)) for s in layer.scales[p]) for p in ("gate", "up", "down")}
     return ExpertLayer(packed, scales, layer.k, layer.hidden, layer.intermediate)
 
 
@@ -183,7 +213,7 @@ class ExpertParallelMoE:
 
     def __init__(self, gate_weight, bias, local: ExpertLayer, rank: int, world: int, group=None, shared=None,
                  shared_layer: ExpertLayer | None = None, routed: int = 256, exchange: str = "nccl",
-                 max_tokens: int = 16, peer: "PeerExchange | None" = None):
+                 max_tokens: int = 16, peer: "PeerExchange | None" = None, placement: torch.Tensor | None = None):
         if (shared is None) == (shared_layer is None):
             raise ValueError("give exactly one shared expert (dense bf16 or trellis)")
         if routed % world or local.experts != routed // world:
@@ -191,6 +221,16 @@ class ExpertParallelMoE:
         self.gate_weight = gate_weight.to(torch.float32).contiguous()
         self.bias = bias.to(torch.float32).contiguous()
         self.local, self.rank, self.world = local, rank, world
+        # Expert placement (seeded_placement): the exchange addresses expert e
+        # by its position placement[e]; None = contiguous blocks.  The local
+        # shard must come from shard_experts with the same placement.
+        self._place = None
+        if placement is not None:
+            if placement.numel() != routed:
+                raise ValueError("placement must hold one position per routed expert")
+            lut = torch.arange(routed + 1, dtype=torch.int32, device=gate_weight.device)
+            lut[:routed] = placement.to(device=gate_weight.device, dtype=torch.int32)
+            self._place = lut  # id 256 (the shared slot) maps to itself
         self.per_rank = routed // world
         self.shared = None if shared is None else tuple(t.contiguous() for t in shared)
         self.shared_layer = shared_layer
@@ -258,6 +298,15 @@ class ExpertParallelMoE:
                                            out.data_ptr(), ws.data_ptr(), ws.numel(), _lib.stream_handle(x.device)))
         return out
 
+    def exchange_ids(self, ids: torch.Tensor) -> torch.Tensor:
+        """The ids the exchange sends by: expert positions under a placement,
+        else the ids themselves (out-of-range ids stay out of range)."""
+        if self._place is None:
+            return ids
+        routed = self._place.numel() - 1
+        safe = ids.clamp(0, routed).long()
+        return torch.where((ids >= 0) & (ids < routed), self._place[safe], ids).to(ids.dtype).contiguous()
+
     def route(self, xr):
         """(ids [tokens][9], scores [tokens][8]) of the local tokens."""
         from .fast_router import route, router, router_logits
@@ -282,7 +331,8 @@ class ExpertParallelMoE:
         stream = _lib.stream_handle(device)
         act = _lib.act_code(xr)
         slot_pos = torch.empty(max(tokens * 8, 1), dtype=torch.int32, device=device)
-        _lib.check(lib.exlr8_ep_send(ids.data_ptr(), tokens, xr.data_ptr(), act, h, self.world, self.rank,
+        xids = self.exchange_ids(ids)
+        _lib.check(lib.exlr8_ep_send(xids.data_ptr(), tokens, xr.data_ptr(), act, h, self.world, self.rank,
                                      self.per_rank, peer.max_capacity, peer.peers.data_ptr(), peer.region,
                                      slot_pos.data_ptr(), peer.status.data_ptr(), stream))
         rows = self.world * tokens * 8
@@ -316,7 +366,8 @@ class ExpertParallelMoE:
         slot_pos = torch.empty(max(tokens * 8, 1), dtype=torch.int32, device=device)
         counts = torch.empty(self.world, dtype=torch.int32, device=device)
         status = torch.zeros(1, dtype=torch.int32, device=device)
-        _lib.check(lib.exlr8_ep_dispatch(ids.data_ptr(), tokens, xr.data_ptr(), _lib.act_code(xr), h, self.world,
+        xids = self.exchange_ids(ids)
+        _lib.check(lib.exlr8_ep_dispatch(xids.data_ptr(), tokens, xr.data_ptr(), _lib.act_code(xr), h, self.world,
                                          self.per_rank, cap, send_x.data_ptr(), send_meta.data_ptr(),
                                          slot_pos.data_ptr(), counts.data_ptr(), status.data_ptr(), stream))
         rows = self.world * cap

@@ -102,22 +102,26 @@ class SyntheticShard:
 
 
 def make_shard(seed: int, rank: int = 0, world: int = 1, k: int = 4, hidden: int = 6144, intermediate: int = 2048,
-               routed: int = 256, device="cuda", scale_sigma: float = 0.1) -> SyntheticShard:
+               routed: int = 256, device="cuda", scale_sigma: float = 0.1, placement=None) -> SyntheticShard:
     """Expert-parallel shard of a synthetic layer.  Every routed expert's
     codes come from their own seed (layer seed, expert, projection), so the
     shards of all ranks together are the same layer whatever ``world`` is;
-    side scales, router and shared expert are drawn whole and sliced."""
+    side scales, router and shared expert are drawn whole and sliced.  With
+    ``placement`` (``ep.seeded_placement``) the shard holds the experts
+    placed at this rank's positions, in position order."""
+    from .ep import _owned
+
     if routed % world or not 0 <= rank < world:
         raise ValueError("routed experts must divide evenly over the ranks")
     device = torch.device(device)
     per = routed // world
-    lo = rank * per
+    owned = _owned(rank, world, routed, placement)
     nbytes = hidden * intermediate * k // 8
     packed = {}
     for i, p in enumerate(("gate", "up", "down")):
         buf = torch.empty(per * nbytes, dtype=torch.uint8, device=device)
         for j in range(per):
-            e = lo + j
+            e = owned[j]
             buf[j * nbytes:(j + 1) * nbytes] = torch.randint(
                 0, 256, (nbytes,), dtype=torch.uint8, generator=_gen(seed * 7919 + e * 3 + i, device), device=device)
         packed[p] = buf
@@ -129,8 +133,10 @@ def make_shard(seed: int, rank: int = 0, world: int = 1, k: int = 4, hidden: int
     def signs(rows, cols, sd):
         return torch.where(torch.rand(rows, cols, generator=_gen(sd, device), device=device) < 0.5, -1.0, 1.0)
 
+    owned_idx = torch.tensor(owned, dtype=torch.int64, device=device)
+
     def rows_of(t):
-        return t[lo:lo + per].contiguous()
+        return t.index_select(0, owned_idx).contiguous()
 
     scales = {}
     for i, p in enumerate(("gate", "up")):

@@ -108,3 +108,21 @@ def test_peer_region_layout_and_checks():
     assert lib.exlr8_ep_peer_bytes(ranks, cap, 100, 2) == 0          # rows of whole 16-byte vectors
     status = lib.exlr8_ep_send(None, 3, None, 2, hidden, ranks, 0, 32, 16, None, None, None, None, None)
     assert status != 0                                              # 3 tokens x 8 > 16 rows
+
+
+def test_seeded_placement_partitions_the_experts():
+    """ep.seeded_placement is a seeded permutation; rank r owns the experts
+    placed at [r * per, (r + 1) * per), every expert exactly once."""
+    from mlxlr8_b200.ep import _owned, seeded_placement
+
+    a = seeded_placement(7, device="cpu")
+    assert torch.equal(a, seeded_placement(7, device="cpu"))
+    assert sorted(a.tolist()) == list(range(256))
+    assert not torch.equal(a, seeded_placement(8, device="cpu"))
+    for world in (1, 2, 4, 8):
+        owned = [_owned(r, world, 256, a) for r in range(world)]
+        assert sorted(e for part in owned for e in part) == list(range(256))
+        for r, part in enumerate(owned):
+            assert all(a[e].item() // (256 // world) == r for e in part)
+        if world > 1:
+            assert _owned(1, world, 256, None) == list(range(256 // world, 2 * 256 // world))

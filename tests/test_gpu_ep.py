@@ -75,8 +75,9 @@ def test_dispatch_positions_match_restatement(tokens, ranks, capacity):
         assert torch.equal(flat[pos[i]], xs[i // 8])
 
 
-def _emulated_layer(layer, x, residual, world):
-    """The expert-parallel layer over `world` emulated ranks on one GPU."""
+def _emulated_layer(layer, x, residual, world, placement=None):
+    """The expert-parallel layer over `world` emulated ranks on one GPU
+    (contiguous expert blocks, or the given placement)."""
     import torch
 
     from mlxlr8_b200 import _lib
@@ -87,14 +88,15 @@ def _emulated_layer(layer, x, residual, world):
     tokens, h = x.shape
     tl = tokens // world
     shared_layer = shared_trellis(e) if e.shared is None else None
-    ranks = [ExpertParallelMoE(layer.gate_weight, layer.bias, shard_experts(e, r, world), r, world,
-                               shared=e.shared, shared_layer=shared_layer) for r in range(world)]
+    ranks = [ExpertParallelMoE(layer.gate_weight, layer.bias, shard_experts(e, r, world, placement=placement), r,
+                               world, shared=e.shared, shared_layer=shared_layer, placement=placement)
+             for r in range(world)]
     cap = tl * 8
     sends, routing = [], []
     for r, m in enumerate(ranks):
         xr = x[r * tl:(r + 1) * tl].contiguous()
         ids, scores = m.route(xr)
-        send_x, send_meta, slot_pos, counts, status = _dispatch(ids, xr, world, 256 // world, cap)
+        send_x, send_meta, slot_pos, counts, status = _dispatch(m.exchange_ids(ids), xr, world, 256 // world, cap)
         sends.append((send_x, send_meta))
         routing.append((ids, scores, slot_pos, status))
     back_parts = [[None] * world for _ in range(world)]
@@ -152,6 +154,30 @@ def test_emulated_expert_parallel_layer_matches_oracle(world, shared, tokens_per
     scale = float(np.max(np.abs(want)))
     assert float(np.max(np.abs(got - want))) <= 1e-2 * scale
     assert rel_l2(got, want) < 5e-3
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_seeded_placement_gives_the_same_layer(world):
+    """Experts placed by a seeded permutation (ep.seeded_placement) instead of
+    contiguous blocks: every slot's value comes from the same expert operator
+    on the same rows, so the layer's output is identical bit for bit, and
+    each rank holds the experts placed at its positions."""
+    import torch
+
+    from mlxlr8_b200.ep import seeded_placement
+    from mlxlr8_b200.synthetic import make_layer
+
+    layer = make_layer(seed=33, hidden=256, intermediate=128, shared="bf16")
+    x, residual = layer.tokens(world * 24)
+    plain, ids, _ = _emulated_layer(layer, x, residual, world)
+    placement = seeded_placement(7)
+    placed, ids2, _ = _emulated_layer(layer, x, residual, world, placement=placement)
+    torch.cuda.synchronize()
+    assert torch.equal(ids, ids2)
+    assert torch.equal(plain, placed)
+    per = 256 // world
+    owners = placement.cpu().numpy() // per
+    assert sorted(np.bincount(owners, minlength=world).tolist()) == [per] * world
 
 
 @pytest.mark.parametrize("rows, tokens", [(16, 2), (40, 5), (24, 0)])
