@@ -26,12 +26,30 @@ class MoELayer:
                                                     experts.intermediate)
         self._shared, self._keep = dense_expert(experts.shared)
         self._workspace = None
+        self._graphs = {}
 
     def workspace_bytes(self, tokens):
         return int(_lib.lib().exlr8_moe_layer_workspace(tokens, self.experts.hidden, self.experts.intermediate,
                                                         self._count))
 
-    def __call__(self, x, residual, return_routing=False, workspace=None):
+    def _launch(self, xr, res, out, ids, scores, workspace, tokens, device):
+        _lib.check(_lib.lib().exlr8_moe_layer(xr.data_ptr(), _lib.act_code(xr), res.data_ptr(), tokens,
+                                              self.gate_weight.data_ptr(), self.bias.data_ptr(), self._struct,
+                                              self._shared, out.data_ptr(), ids.data_ptr(), scores.data_ptr(),
+                                              workspace.data_ptr(), workspace.numel(),
+                                              _lib.stream_handle(device)))
+
+    def __call__(self, x, residual, return_routing=False, workspace=None, out=None, graph=False):
+        """``residual + moe(x)``.  ``out`` (optional) receives the result.
+
+        ``graph=True`` (with ``out``): the layer's kernel chain is captured
+        once per (x, residual, out) address triple into a CUDA graph and
+        replayed on later calls -- one launch for the seven kernels, the
+        B200 counterpart of the reference's ``mx.compile`` of the decode
+        finish (fast_decode.py:224-244).  x and residual must then be
+        contiguous and of one dtype (their contents may change between
+        calls, not their addresses); the routing ids and scores live in
+        buffers of the captured call, overwritten by every replay."""
         device = _lib.require_cuda(x, residual)
         h = self.experts.hidden
         if x.shape[-1] != h or residual.shape != x.shape:
@@ -39,7 +57,14 @@ class MoELayer:
         tokens = x.numel() // h
         xr = x.contiguous()
         res = residual.to(x.dtype).contiguous()
-        out = torch.empty_like(res)
+        if out is None:
+            out = torch.empty_like(res)
+        elif out.shape != residual.shape or out.dtype != x.dtype or not out.is_contiguous() or out.device != device:
+            raise ValueError("out must be a contiguous tensor like the residual in x's dtype")
+        if graph:
+            if xr is not x or res is not residual or workspace is not None:
+                raise ValueError("graph=True takes contiguous x and residual of one dtype and no workspace")
+            return self._graph_call(xr, res, out, tokens, device, return_routing, x.shape[:-1])
         ids = torch.empty(tokens, 9, dtype=torch.int32, device=device)
         scores = torch.empty(tokens, 8, dtype=torch.float32, device=device)
         need = self.workspace_bytes(tokens)
@@ -47,11 +72,33 @@ class MoELayer:
             if self._workspace is None or self._workspace.numel() < need or self._workspace.device != device:
                 self._workspace = _lib.workspace(need, device)
             workspace = self._workspace
-        _lib.check(_lib.lib().exlr8_moe_layer(xr.data_ptr(), _lib.act_code(xr), res.data_ptr(), tokens,
-                                              self.gate_weight.data_ptr(), self.bias.data_ptr(), self._struct,
-                                              self._shared, out.data_ptr(), ids.data_ptr(), scores.data_ptr(),
-                                              workspace.data_ptr(), workspace.numel(),
-                                              _lib.stream_handle(device)))
+        self._launch(xr, res, out, ids, scores, workspace, tokens, device)
         if return_routing:
             return out, ids.reshape(tuple(x.shape[:-1]) + (9,)), scores.reshape(tuple(x.shape[:-1]) + (8,))
         return out
+
+    def _graph_call(self, xr, res, out, tokens, device, return_routing, lead_shape):
+        key = (xr.data_ptr(), res.data_ptr(), out.data_ptr(), tokens, xr.dtype, device)
+        entry = self._graphs.get(key)
+        if entry is None:
+            # Its own workspace and routing buffers: the graph holds their
+            # addresses.  The first call runs eagerly (the result of this call,
+            # and the library's one-time launch setup), then is captured.
+            ids = torch.empty(tokens, 9, dtype=torch.int32, device=device)
+            scores = torch.empty(tokens, 8, dtype=torch.float32, device=device)
+            ws = _lib.workspace(self.workspace_bytes(tokens), device)
+            self._launch(xr, res, out, ids, scores, ws, tokens, device)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                self._launch(xr, res, out, ids, scores, ws, tokens, device)
+            entry = (g, ids, scores, ws)
+            self._graphs[key] = entry
+        else:
+            entry[0].replay()
+        if return_routing:
+            return out, entry[1].reshape(tuple(lead_shape) + (9,)), entry[2].reshape(tuple(lead_shape) + (8,))
+        return out
+
+    def clear_graphs(self):
+        """Release the captured graphs (and their buffers)."""
+        self._graphs.clear()
