@@ -49,7 +49,13 @@ class MoELayer:
         finish (fast_decode.py:224-244).  x and residual must then be
         contiguous and of one dtype (their contents may change between
         calls, not their addresses); the routing ids and scores live in
-        buffers of the captured call, overwritten by every replay."""
+        buffers of the captured call, overwritten by every replay.  In this
+        mode x, residual and out may also be pinned host tensors: the graph
+        then holds the two host-to-device copies (side by side) and the
+        device-to-host copy of the result, and ``out`` is written
+        asynchronously on the current stream."""
+        if graph and x.device.type == "cpu":
+            return self._graph_call_host(x, residual, out, return_routing)
         device = _lib.require_cuda(x, residual)
         h = self.experts.hidden
         if x.shape[-1] != h or residual.shape != x.shape:
@@ -97,6 +103,49 @@ class MoELayer:
             entry[0].replay()
         if return_routing:
             return out, entry[1].reshape(tuple(lead_shape) + (9,)), entry[2].reshape(tuple(lead_shape) + (8,))
+        return out
+
+    def _graph_call_host(self, x, residual, out, return_routing):
+        h = self.experts.hidden
+        device = self.gate_weight.device
+        if out is None or x.shape[-1] != h or residual.shape != x.shape or out.shape != x.shape:
+            raise ValueError("host graph mode takes x, residual and out of one shape [..., hidden]")
+        if not all(t.device.type == "cpu" and t.is_pinned() and t.is_contiguous() and t.dtype == x.dtype
+                   for t in (x, residual, out)):
+            raise ValueError("host graph mode takes contiguous pinned host tensors of one dtype")
+        tokens = x.numel() // h
+        key = ("host", x.data_ptr(), residual.data_ptr(), out.data_ptr(), tokens, x.dtype, device)
+        entry = self._graphs.get(key)
+        if entry is None:
+            xd = torch.empty(x.shape, dtype=x.dtype, device=device)
+            rd = torch.empty_like(xd)
+            od = torch.empty_like(xd)
+            ids = torch.empty(tokens, 9, dtype=torch.int32, device=device)
+            scores = torch.empty(tokens, 8, dtype=torch.float32, device=device)
+            ws = _lib.workspace(self.workspace_bytes(tokens), device)
+            side = torch.cuda.Stream(device)
+
+            def body():
+                main = torch.cuda.current_stream(device)
+                side.wait_stream(main)
+                with torch.cuda.stream(side):
+                    rd.copy_(residual, non_blocking=True)
+                xd.copy_(x, non_blocking=True)
+                main.wait_stream(side)
+                self._launch(xd, rd, od, ids, scores, ws, tokens, device)
+                out.copy_(od, non_blocking=True)
+
+            body()  # this call's result, and the library's one-time launch setup
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                body()
+            entry = (g, ids, scores, (ws, xd, rd, od, side))
+            self._graphs[key] = entry
+        else:
+            entry[0].replay()
+        if return_routing:
+            lead = tuple(x.shape[:-1])
+            return out, entry[1].reshape(lead + (9,)), entry[2].reshape(lead + (8,))
         return out
 
     def clear_graphs(self):

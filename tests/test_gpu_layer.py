@@ -81,3 +81,28 @@ def test_graph_mode_replays_the_eager_layer(tokens):
         assert torch.equal(got, want)
         assert torch.equal(ids, wids) and torch.equal(scores, wscores)
     moe.clear_graphs()
+
+
+def test_graph_mode_with_pinned_host_buffers():
+    """graph=True with pinned host x / residual / out: the captured graph
+    copies in, runs the layer and copies out; the host result equals the
+    eager device call bit for bit on every replay."""
+    import torch
+
+    from mlxlr8_b200.moe import MoELayer
+    from mlxlr8_b200.synthetic import make_layer
+
+    layer = make_layer(seed=19, hidden=256, intermediate=128, shared="bf16")
+    moe = MoELayer(layer.gate_weight, layer.bias, layer.experts)
+    x0, r0 = layer.tokens(2)
+    xh, rh = x0.cpu().pin_memory(), r0.cpu().pin_memory()
+    oh = torch.empty_like(xh).pin_memory()
+    for step in range(3):
+        x2, r2 = layer.tokens(2, seed_offset=70 + step)
+        xh.copy_(x2.cpu())
+        rh.copy_(r2.cpu())
+        moe(xh, rh, out=oh, graph=True)
+        want = moe(x2, r2)
+        torch.cuda.synchronize()
+        assert torch.equal(oh, want.cpu())
+    moe.clear_graphs()
