@@ -228,7 +228,7 @@ int launch_dense_decode(const void* x, int x_dtype, int64_t tokens, const exlr8_
 int run_mlp_after_plan(const void* x, int x_dtype, int per_slot, int slots, const uint32_t* ids, int64_t rows,
                        const exlr8_trellis_experts* ex, int64_t experts, const exlr8_dense_expert* shared,
                        const void* dense_x, int64_t tokens, const MlpLayout& l, const MlpBuffers& b,
-                       cudaStream_t s, const exlr8_static_cache* cache = nullptr) {
+                       cudaStream_t s, const exlr8_static_cache* cache = nullptr, int sparse = 0) {
   const int h = ex->hidden, m = ex->intermediate;
   const int n = static_cast<int>(rows), e = static_cast<int>(experts), t = static_cast<int>(tokens);
   EXLR8_TIMED(EXLR8_KERNEL_PREP, s,
@@ -261,7 +261,7 @@ int run_mlp_after_plan(const void* x, int x_dtype, int per_slot, int slots, cons
   EXLR8_TIMED(EXLR8_KERNEL_GATE_FINISH, s,
               launch_gate_finish_frag(b.gu, l.s1.count, ids, n, ex->out_scale[0], ex->out_scale[1], ex->in_scale[2],
                                       ex->scale_dtype, m, e, x_dtype, b.frag_d, b.dgate, b.dup, dsplits_gu,
-                                      shared ? t : 0, shared ? b.dh : nullptr, s));
+                                      shared ? t : 0, shared ? b.dh : nullptr, s, 0, sparse));
   StreamParams dp = stream_params(ex, b.plan, 3, n);
   dp.packed[0] = static_cast<const uint32_t*>(ex->packed[2]);
   dp.packed[1] = nullptr;
@@ -1071,8 +1071,9 @@ int exlr8_expert_mlp_shared(const void* x, int x_dtype, const uint32_t* indices,
   const MlpBuffers b = carve_mlp(l, rows, experts, true, shared_tokens, h, m, c);
   const int n = static_cast<int>(rows), e = static_cast<int>(experts);
   EXLR8_TIMED(EXLR8_KERNEL_PLAN, s, launch_plan(indices, n, e, 1, -1, b.plan, s));
+  // An owner's rows: fixed capacity per source, mostly empty at decode sizes.
   EXLR8_CHECK(run_mlp_after_plan(x, x_dtype, 1, 1, indices, rows, ex, experts, shared_tokens > 0 ? shared : nullptr,
-                                 shared_x, shared_tokens, l, b, s));
+                                 shared_x, shared_tokens, l, b, s, nullptr, 1));
   if (rows > 0) {
     ProfileScope scope(EXLR8_KERNEL_FINISH, s);
     EXLR8_TRY(launch_finish(b.dpart, l.s2.count, nullptr, indices, n, ex->out_scale[2], ex->scale_dtype, h, e,

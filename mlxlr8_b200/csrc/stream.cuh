@@ -96,10 +96,13 @@ cudaError_t launch_prep_frag(const void* x, int x_dtype, int per_slot, int slots
 // dense_tokens > 0 it also writes the bf16 shared expert's
 // h = SwiGLU(T(g), T(u)) [dense_tokens][features] (activation type) from its
 // split partials dense_g/dense_u [dense_splits][dense_tokens][features].
+// skip_empty: the slot list is sparse (most ids out of range); such slots
+// are skipped before their partials are loaded, at the cost of waiting for
+// the id first.
 cudaError_t launch_gate_finish_frag(const float* partial, int gu_splits, const uint32_t* ids, int nslots,
                                     const void* out_gate, const void* out_up, const void* in_down, int scale_dtype,
                                     int features, int experts, int act_dtype, unsigned char* frag,
                                     const float* dense_g, const float* dense_u, int dense_splits, int dense_tokens,
-                                    void* dense_h, cudaStream_t s, int mx_order = 0);
+                                    void* dense_h, cudaStream_t s, int mx_order = 0, int skip_empty = 0);
 
 }  // namespace exlr8

@@ -340,6 +340,7 @@ __global__ void __launch_bounds__(kFragWarps * 32) prep_frag_kernel(
   for (int j = 0; j < 4; ++j) xv[j] = load_act(x, x_dtype, row * features + c0 + 32 * j);
   const uint32_t e = ids[slot];
   const bool ok = e < static_cast<uint32_t>(experts);
+  if (!ok) return;  // no plan row reads the record of a slot without an expert
   const void* scale = proj ? in1 : in0;
   float v[4];
 #pragma unroll
@@ -374,6 +375,7 @@ cudaError_t launch_prep_frag(const void* x, int x_dtype, int per_slot, int slots
 // 128-wide block).
 constexpr int kGateFinishSplits = 16;  // splits loaded per round trip (the most gate_up_splits chooses)
 
+template <bool kSkipEmpty>
 __global__ void __launch_bounds__(kFragWarps * 32) gate_finish_frag_kernel(
     const float* __restrict__ partial, int gu_splits, const uint32_t* __restrict__ ids, int nslots,
     const void* __restrict__ out_gate, const void* __restrict__ out_up, const void* __restrict__ in_down,
@@ -415,6 +417,11 @@ __global__ void __launch_bounds__(kFragWarps * 32) gate_finish_frag_kernel(
   float sg[4], su[4], sd[4];
   const int64_t e = id;
   const bool ok = e < experts;
+  // Sparse slot lists (an expert-parallel owner's fixed-capacity rows, most
+  // of them empty): a slot without an expert has no plan row, so its record
+  // is never read; skip its partials instead of loading them.  (Dense lists
+  // do not wait for the id before loading.)
+  if (kSkipEmpty && !ok) return;
   for (int s0 = 0; s0 < gu_splits; s0 += kGateFinishSplits) {
     float lg[kGateFinishSplits][4], lu[kGateFinishSplits][4];
 #pragma unroll
@@ -471,16 +478,19 @@ cudaError_t launch_gate_finish_frag(const float* partial, int gu_splits, const u
                                     const void* out_gate, const void* out_up, const void* in_down, int scale_dtype,
                                     int features, int experts, int act_dtype, unsigned char* frag,
                                     const float* dense_g, const float* dense_u, int dense_splits, int dense_tokens,
-                                    void* dense_h, cudaStream_t s, int mx_order) {
+                                    void* dense_h, cudaStream_t s, int mx_order, int skip_empty) {
   if (!dense_h) dense_tokens = 0;
   const int64_t tasks = (static_cast<int64_t>(nslots) + dense_tokens) * (features / 128);
   if (tasks == 0) return cudaSuccess;
   const int64_t grid = (tasks + kFragWarps - 1) / kFragWarps;
-  static const cudaError_t carve = prefer_shared_carveout(gate_finish_frag_kernel);
-  if (carve != cudaSuccess) return carve;
-  return launch_pdl(gate_finish_frag_kernel, dim3(static_cast<unsigned>(grid)), dim3(kFragWarps * 32), 0, s, partial,
-                    gu_splits, ids, nslots, out_gate, out_up, in_down, scale_dtype, features, experts, act_dtype, frag,
-                    dense_g, dense_u, dense_splits, dense_tokens, dense_h, mx_order);
+  static const cudaError_t carve0 = prefer_shared_carveout(gate_finish_frag_kernel<false>);
+  static const cudaError_t carve1 = prefer_shared_carveout(gate_finish_frag_kernel<true>);
+  if (carve0 != cudaSuccess) return carve0;
+  if (carve1 != cudaSuccess) return carve1;
+  auto kernel = skip_empty ? gate_finish_frag_kernel<true> : gate_finish_frag_kernel<false>;
+  return launch_pdl(kernel, dim3(static_cast<unsigned>(grid)), dim3(kFragWarps * 32), 0, s, partial, gu_splits, ids,
+                    nslots, out_gate, out_up, in_down, scale_dtype, features, experts, act_dtype, frag, dense_g,
+                    dense_u, dense_splits, dense_tokens, dense_h, mx_order);
 }
 
 // ---------------------------------------------------------------------------
