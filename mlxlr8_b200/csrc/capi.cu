@@ -233,7 +233,7 @@ int run_mlp_after_plan(const void* x, int x_dtype, int per_slot, int slots, cons
   const int n = static_cast<int>(rows), e = static_cast<int>(experts), t = static_cast<int>(tokens);
   EXLR8_TIMED(EXLR8_KERNEL_PREP, s,
               launch_prep_frag(x, x_dtype, per_slot, slots, ids, n, ex->in_scale[0], ex->in_scale[1],
-                               ex->scale_dtype, h, e, 2, b.frag_gu, s));
+                               ex->scale_dtype, h, e, 2, b.frag_gu, s, -1, 0, sparse));
   StreamParams gp = stream_params(ex, b.plan, 2, n);
   gp.packed[0] = static_cast<const uint32_t*>(ex->packed[0]);
   gp.packed[1] = static_cast<const uint32_t*>(ex->packed[1]);

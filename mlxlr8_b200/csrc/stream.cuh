@@ -89,7 +89,7 @@ bool encode_dense_maps(StreamParams& p);
 cudaError_t launch_prep_frag(const void* x, int x_dtype, int per_slot, int slots_per_token, const uint32_t* ids,
                              int nslots, const void* in0, const void* in1, int scale_dtype, int features, int experts,
                              int projections, unsigned char* frag, cudaStream_t s, int scale_stride = -1,
-                             int mx_order = 0);
+                             int mx_order = 0, int skip_empty = 0);
 
 // gate/up finish (metal/fast_decode_gate_finish.metal) producing the down
 // projection's fragment records (frag_bytes(nslots, features, 1)).  With

@@ -319,6 +319,7 @@ __device__ __forceinline__ void write_block_record(const float v[4], float* stag
   __syncwarp();
 }
 
+template <bool kSkipEmpty>
 __global__ void __launch_bounds__(kFragWarps * 32) prep_frag_kernel(
     const void* __restrict__ x, int x_dtype, int per_slot, int slots_per_token, const uint32_t* __restrict__ ids,
     int nslots, const void* __restrict__ in0, const void* __restrict__ in1, int scale_dtype, int features,
@@ -335,11 +336,14 @@ __global__ void __launch_bounds__(kFragWarps * 32) prep_frag_kernel(
   const int slot = static_cast<int>(ps % nslots), proj = static_cast<int>(ps / nslots);
   const int64_t row = per_slot ? slot : slot / slots_per_token;
   const int c0 = b * 128 + lane;
+  // Sparse slot lists (an expert-parallel owner's capacity rows) check the
+  // id before loading the row; dense lists load both at once.
+  const uint32_t e = ids[slot];
+  const bool ok = e < static_cast<uint32_t>(experts);
+  if (kSkipEmpty && !ok) return;
   float xv[4];
 #pragma unroll
   for (int j = 0; j < 4; ++j) xv[j] = load_act(x, x_dtype, row * features + c0 + 32 * j);
-  const uint32_t e = ids[slot];
-  const bool ok = e < static_cast<uint32_t>(experts);
   if (!ok) return;  // no plan row reads the record of a slot without an expert
   const void* scale = proj ? in1 : in0;
   float v[4];
@@ -353,14 +357,18 @@ __global__ void __launch_bounds__(kFragWarps * 32) prep_frag_kernel(
 
 cudaError_t launch_prep_frag(const void* x, int x_dtype, int per_slot, int slots_per_token, const uint32_t* ids,
                              int nslots, const void* in0, const void* in1, int scale_dtype, int features, int experts,
-                             int projections, unsigned char* frag, cudaStream_t s, int scale_stride, int mx_order) {
+                             int projections, unsigned char* frag, cudaStream_t s, int scale_stride, int mx_order,
+                             int skip_empty) {
   if (scale_stride < 0) scale_stride = features;
   const int64_t tasks = static_cast<int64_t>(projections) * nslots * (features / 128);
   if (tasks == 0) return cudaSuccess;
   const int64_t grid = (tasks + kFragWarps - 1) / kFragWarps;
-  static const cudaError_t carve = prefer_shared_carveout(prep_frag_kernel);
-  if (carve != cudaSuccess) return carve;
-  return launch_pdl(prep_frag_kernel, dim3(static_cast<unsigned>(grid)), dim3(kFragWarps * 32), 0, s, x, x_dtype,
+  static const cudaError_t carve0 = prefer_shared_carveout(prep_frag_kernel<false>);
+  static const cudaError_t carve1 = prefer_shared_carveout(prep_frag_kernel<true>);
+  if (carve0 != cudaSuccess) return carve0;
+  if (carve1 != cudaSuccess) return carve1;
+  auto kernel = skip_empty ? prep_frag_kernel<true> : prep_frag_kernel<false>;
+  return launch_pdl(kernel, dim3(static_cast<unsigned>(grid)), dim3(kFragWarps * 32), 0, s, x, x_dtype,
                     per_slot, slots_per_token, ids, nslots, in0, in1, scale_dtype, features, experts, projections,
                     scale_stride, mx_order, frag);
 }
