@@ -163,6 +163,8 @@ class PeerExchange:
                                              ctypes.byref(rows), ctypes.byref(back)))
         self.meta, self.rows, self.back = self.region + meta.value, self.region + rows.value, self.region + back.value
         self.status = torch.zeros(2, dtype=torch.int32, device=device)
+        self._status_host = torch.zeros(2, dtype=torch.int32).pin_memory()
+        self._status_event = None
         self._group = group
         self.broken = False
 
@@ -173,7 +175,25 @@ class PeerExchange:
         After a timeout the ranks' epoch flags no longer agree, so the
         exchange is marked unusable: later calls raise until it is closed and
         a new one is created."""
-        lost, timeouts = (int(v) for v in self.status.cpu())
+        self._raise_for(self.status.cpu())
+
+    def check_deferred(self):
+        """The check of an earlier call, without synchronising: the status
+        word (cumulative over the exchange's life) is copied to pinned host
+        memory behind an event; once a copy has landed its value is checked
+        and a new copy is queued.  An error surfaces a call or two after it
+        happened."""
+        ev = self._status_event
+        if ev is not None and ev.query():
+            self._status_event = None
+            self._raise_for(self._status_host)
+        if self._status_event is None:
+            self._status_host.copy_(self.status, non_blocking=True)
+            self._status_event = torch.cuda.Event()
+            self._status_event.record()
+
+    def _raise_for(self, values):
+        lost, timeouts = (int(v) for v in values)
         if timeouts & 3:
             self.broken = True
             raise RuntimeError(f"expert-parallel exchange: a wait for a peer timed out (flags {timeouts}); "
@@ -206,14 +226,17 @@ class ExpertParallelMoE:
 
     With the peer-memory exchange a bounded wait that times out (a peer that
     stopped) or a capacity overflow leaves partial rows in the output.  Eager
-    calls therefore read the exchange status after every call (`check`, a
-    host synchronisation) and raise; calls made while a CUDA graph is being
-    captured cannot, so whoever replays such a graph must call
+    calls therefore check the exchange status and raise: by default without
+    a host synchronisation (``PeerExchange.check_deferred``: an error
+    surfaces a call or two later), with ``deferred_check=False`` after every
+    call (``check``, a synchronisation).  Calls made while a CUDA graph is
+    being captured cannot check, so whoever replays such a graph must call
     ``self.peer.check()`` after the replays (bench.py does)."""
 
     def __init__(self, gate_weight, bias, local: ExpertLayer, rank: int, world: int, group=None, shared=None,
                  shared_layer: ExpertLayer | None = None, routed: int = 256, exchange: str = "nccl",
-                 max_tokens: int = 16, peer: "PeerExchange | None" = None, placement: torch.Tensor | None = None):
+                 max_tokens: int = 16, peer: "PeerExchange | None" = None, placement: torch.Tensor | None = None,
+                 deferred_check: bool = True):
         if (shared is None) == (shared_layer is None):
             raise ValueError("give exactly one shared expert (dense bf16 or trellis)")
         if routed % world or local.experts != routed // world:
@@ -240,6 +263,7 @@ class ExpertParallelMoE:
         if exchange == "peer" and shared_layer is not None:
             raise ValueError("the peer-memory exchange runs with the bf16 shared expert")
         self.exchange_kind = exchange
+        self.deferred_check = deferred_check
         self.max_tokens = max_tokens
         self.group = group
         # PeerExchange: given (shared by the layers of a stack, which run one
@@ -344,7 +368,7 @@ class ExpertParallelMoE:
                                         res.data_ptr(), tokens, h, out.data_ptr(), stream))
         out = out.reshape(residual.shape)
         if not torch.cuda.is_current_stream_capturing():
-            peer.check()
+            peer.check_deferred() if self.deferred_check else peer.check()
         if return_routing:
             return out, ids, scores
         return out

@@ -256,3 +256,28 @@ def test_peer_exchange_wait_times_out_and_reports():
         torch.zeros(4, device="cuda").sum().item()  # the context still works
     finally:
         _lib.check(lib.exlr8_ep_peer_destroy(region.value))
+
+
+def test_deferred_status_check_raises_without_synchronising():
+    """PeerExchange.check_deferred: the first call only queues a copy of the
+    (cumulative) status word; once that copy has landed the next call raises
+    for a timed-out wait and marks the exchange unusable."""
+    import torch
+
+    from mlxlr8_b200.ep import PeerExchange
+
+    ex = PeerExchange.__new__(PeerExchange)
+    ex.status = torch.zeros(2, dtype=torch.int32, device="cuda")
+    ex._status_host = torch.zeros(2, dtype=torch.int32).pin_memory()
+    ex._status_event = None
+    ex.broken = False
+    ex.check_deferred()  # nothing wrong, a copy is queued
+    torch.cuda.synchronize()
+    ex.check_deferred()  # the clean copy is checked, the next queued
+    ex.status[1] = 2     # a return wait timed out
+    torch.cuda.synchronize()
+    ex.check_deferred()  # checks the copy made before the error; queues a new one
+    torch.cuda.synchronize()
+    with pytest.raises(RuntimeError, match="timed out"):
+        ex.check_deferred()
+    assert ex.broken
