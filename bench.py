@@ -16,9 +16,10 @@ value: device-resident inputs, the layer call replayed from a CUDA graph.
 e2e:   the public API with pinned host buffers: per step the H2D copy of x
        and residual and the D2H copy of the output are in the timed region.
        The call is MoELayer.__call__ (ExpertParallelMoE.__call__ on several
-       GPUs).  Its graph-replay mode (graph=True, also with the copies inside
-       the graph) measured the same e2e within 1%: the three small PCIe
-       copies (~24 us a step), not the launches, separate e2e from value.
+       GPUs); x and residual travel in one H2D copy of one pinned buffer.
+       The layer's graph-replay mode (graph=True, also with the copies inside
+       the graph) measured the same e2e within 1%: the small PCIe copies, not
+       the launches, separate e2e from value.
 roofline: the dominant kernel (trellis gate/up streaming GEMV), its launch
        durations measured with CUDA events on the launching stream during a
        profiled pass of the same K steps; algorithmic bytes = packed trellis
@@ -1049,17 +1050,16 @@ def main():
     step_bytes = u_mean * 3 * codes_per_matrix + u_mean * 49152 + 3 * HIDDEN * INTER * 2 + 256 * HIDDEN * 4 + 4 * T * HIDDEN
 
     # ---- e2e through the public API with host buffers ----
-    xh = [x.cpu().pin_memory() for x in xs]
-    rh = [r.cpu().pin_memory() for r in rs]
+    # x and residual of a step sit side by side in one pinned host buffer and
+    # one device buffer, so the step's inputs cross PCIe in one copy.
+    inh = [torch.stack([x.cpu(), r.cpu()]).pin_memory() for x, r in zip(xs, rs)]
+    ind = [torch.empty_like(b, device=device) for b in inh]
     oh = [torch.empty(T, HIDDEN, dtype=torch.bfloat16).pin_memory() for _ in range(L)]
-    xd = [torch.empty_like(x) for x in xs]
-    rd = [torch.empty_like(r) for r in rs]
     e2e_steps = min(args.steps, 1000)
 
     def e2e_step(i):
-        xd[i].copy_(xh[i], non_blocking=True)
-        rd[i].copy_(rh[i], non_blocking=True)
-        oh[i].copy_(moes[i](xd[i], rd[i]), non_blocking=True)
+        ind[i].copy_(inh[i], non_blocking=True)
+        oh[i].copy_(moes[i](ind[i][0], ind[i][1]), non_blocking=True)
 
     with torch.cuda.stream(stream):
         for s in range(args.warmup):
