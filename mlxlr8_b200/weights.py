@@ -15,9 +15,9 @@ from __future__ import annotations
 
 import json
 import os
-import struct
 from concurrent.futures import ThreadPoolExecutor
 from pathlib import Path
+from typing import NamedTuple
 
 import numpy as np
 import torch
@@ -108,38 +108,63 @@ def _copy_to_device(path, offset: int, count: int, dst: torch.Tensor) -> None:
         dst.record_stream(st.stream)
 
 
+class _Span(NamedTuple):
+    """Where one tensor's bytes lie in the file."""
+
+    dtype: str   # safetensors scalar type name
+    shape: tuple
+    offset: int  # absolute file offset of the first byte
+    nbytes: int
+
+
 class SafeTensorFile:
-    """Keep the header in memory; read only the requested tensor bytes."""
+    """The header parsed once into per-tensor spans; every read touches only
+    the requested bytes of the file."""
 
     def __init__(self, path: str | Path):
         self.path = Path(path)
         with self.path.open("rb") as handle:
-            size = struct.unpack("<Q", handle.read(8))[0]
-            self.header = json.loads(handle.read(size))
-        self.data_offset = 8 + size
-        self.metadata = self.header.get("__metadata__", {})
-        self.tensors = {name: info for name, info in self.header.items() if name != "__metadata__"}
+            header_len = int.from_bytes(handle.read(8), "little")
+            header = json.loads(handle.read(header_len))
+        self.header = header
+        self.data_offset = 8 + header_len
+        self.metadata = header.get("__metadata__", {})
+        self.tensors, self._spans = {}, {}
+        for name, info in header.items():
+            if name == "__metadata__":
+                continue
+            first, last = info["data_offsets"]
+            self.tensors[name] = info
+            self._spans[name] = _Span(info["dtype"], tuple(info["shape"]), self.data_offset + first, last - first)
 
     def _range(self, name: str, start_bytes: int, byte_count: int | None):
-        info = self.tensors[name]
-        begin, end = info["data_offsets"]
-        itemsize = np.dtype(_DTYPES[info["dtype"]]).itemsize
-        if byte_count is None:
-            byte_count = end - begin - start_bytes
-        if (start_bytes < 0 or byte_count < 0 or start_bytes + byte_count > end - begin
-                or start_bytes % itemsize or byte_count % itemsize):
-            raise ValueError(f"invalid byte range for {name}: {start_bytes}, {byte_count}")
-        return info, self.data_offset + begin + start_bytes, byte_count
+        """(info, absolute offset, byte count) of a checked byte range."""
+        span = self._spans[name]
+        count = span.nbytes - start_bytes if byte_count is None else byte_count
+        unit = np.dtype(_DTYPES[span.dtype]).itemsize
+        inside = 0 <= start_bytes and 0 <= count and start_bytes + count <= span.nbytes
+        if not inside or start_bytes % unit or count % unit:
+            raise ValueError(f"invalid byte range for {name}: {start_bytes}, {count}")
+        return self.tensors[name], span.offset + start_bytes, count
 
     def raw(self, name: str, start_bytes: int = 0, byte_count: int | None = None) -> np.ndarray:
-        """Read a shaped tensor, or a flat range, to host memory. BF16 keep uint16 bit patterns."""
-        whole_tensor = start_bytes == 0 and byte_count is None
-        info, offset, byte_count = self._range(name, start_bytes, byte_count)
-        dtype = np.dtype(_DTYPES[info["dtype"]])
-        result = np.fromfile(self.path, dtype=dtype, count=byte_count // dtype.itemsize, offset=offset)
-        if result.nbytes != byte_count:
+        """A tensor (shaped) or a byte range of it (flat) in host memory, one
+        positional read of exactly those bytes; BF16 stays uint16 bit patterns."""
+        _, offset, count = self._range(name, start_bytes, byte_count)
+        span = self._spans[name]
+        data = bytearray(count)
+        view, got = memoryview(data), 0
+        with self.path.open("rb", buffering=0) as handle:
+            handle.seek(offset)
+            while got < count:  # one read call returns at most ~2 GB
+                n = handle.readinto(view[got:])
+                if not n:
+                    break
+                got += n
+        if got != count:
             raise ValueError(f"truncated tensor {name} in {self.path}")
-        return result.reshape(info["shape"]) if whole_tensor else result
+        values = np.frombuffer(data, dtype=np.dtype(_DTYPES[span.dtype]))
+        return values.reshape(span.shape) if start_bytes == 0 and byte_count is None else values
 
     def read_into(self, name: str, out: torch.Tensor, start_bytes: int = 0, byte_count: int | None = None) -> None:
         """Copy a byte range of a tensor into ``out``, a contiguous tensor
