@@ -341,16 +341,33 @@ __global__ void __launch_bounds__(288) joined_finish_kernel(const float* __restr
 #pragma unroll
       for (int j = 0; j < 4; ++j) val[g][j] = (ok && g < nb) ? __ldcs(src + (b0 + g) * 128 + 32 * j) : 0.0f;
     if (dense_shared) {
-      // Dense shared expert: float32 split partials [splits][tokens][h], summed and cast.
+      // Dense shared expert: float32 split partials [splits][tokens][h], summed
+      // in split order and cast.  The group's sixteen values of one split go
+      // out together: one round trip per split, not per value.
       const int64_t total = static_cast<int64_t>(tokens) * features;
-      for (int g = 0; g < nb; ++g)
+      const float* part = shared_values + base + lane;
+      float acc[kFinishGroup][4];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const int64_t i = token * features + (b0 + g) * 128 + lane + 32 * j;
-          float a = 0.f;
-          for (int sp = 0; sp < shared_splits; ++sp) a += __ldcg(shared_values + sp * total + i);
-          products[8][g * 128 + lane + 32 * j] = round_to(kAct, a);
-        }
+      for (int g = 0; g < kFinishGroup; ++g)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[g][j] = 0.f;
+#pragma unroll 2
+      for (int sp = 0; sp < shared_splits; ++sp) {
+        float q[kFinishGroup][4];
+#pragma unroll
+        for (int g = 0; g < kFinishGroup; ++g)
+#pragma unroll
+          for (int j = 0; j < 4; ++j) q[g][j] = g < nb ? __ldcg(part + sp * total + g * 128 + 32 * j) : 0.f;
+#pragma unroll
+        for (int g = 0; g < kFinishGroup; ++g)
+#pragma unroll
+          for (int j = 0; j < 4; ++j) acc[g][j] += q[g][j];
+      }
+#pragma unroll
+      for (int g = 0; g < kFinishGroup; ++g)
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          if (g < nb) products[8][g * 128 + lane + 32 * j] = round_to(kAct, acc[g][j]);
     }
 #pragma unroll
     for (int g = 0; g < kFinishGroup; ++g) {
