@@ -71,12 +71,6 @@ inline Splits linear_splits(int in_features) { return make_splits(in_features, i
 // (units of 16 rows x one split; the partials are summed in split order).
 inline int dense_gate_up_splits(int hidden) { return dense_split_count(hidden, 4); }
 inline int dense_down_splits(int intermediate) { return dense_split_count(intermediate, 2); }
-// The dense bf16 GEMV splits K into 384-wide pieces (enough warps in flight
-// to stream the weights at full bandwidth for one to a few tokens).
-inline int dense_splits(int k) {
-  int s = k / 384;
-  return s < 1 ? 1 : (s > 16 ? 16 : s);
-}
 
 int format_status(int64_t packed_bytes, int k, int in_f, int out_f, int side, int64_t* matrices) {
   if (k != 2 && k != 3 && k != 4) return EXLR8_ERR_WIDTH;

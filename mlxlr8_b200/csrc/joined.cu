@@ -335,15 +335,12 @@ __global__ void __launch_bounds__(288) joined_finish_kernel(const float* __restr
     const int c_a = threadIdx.x, c_b = threadIdx.x + 288;
     const float res_a = c_a < nb * 128 ? load_act(residual, kAct, base + c_a) : 0.0f;
     const float res_b = c_b < nb * 128 ? load_act(residual, kAct, base + c_b) : 0.0f;
-    float val[kFinishGroup][4];
-#pragma unroll
-    for (int g = 0; g < kFinishGroup; ++g)
-#pragma unroll
-      for (int j = 0; j < 4; ++j) val[g][j] = (ok && g < nb) ? __ldcs(src + (b0 + g) * 128 + 32 * j) : 0.0f;
     if (dense_shared) {
       // Dense shared expert: float32 split partials [splits][tokens][h], summed
       // in split order and cast.  The group's sixteen values of one split go
-      // out together: one round trip per split, not per value.
+      // out together: one round trip per split, not per value.  (A branch of
+      // its own, one split in flight: the slot warps' registers stay those of
+      // the slot path alone.)
       const int64_t total = static_cast<int64_t>(tokens) * features;
       const float* part = shared_values + base + lane;
       float acc[kFinishGroup][4];
@@ -351,7 +348,7 @@ __global__ void __launch_bounds__(288) joined_finish_kernel(const float* __restr
       for (int g = 0; g < kFinishGroup; ++g)
 #pragma unroll
         for (int j = 0; j < 4; ++j) acc[g][j] = 0.f;
-#pragma unroll 2
+#pragma unroll 1
       for (int sp = 0; sp < shared_splits; ++sp) {
         float q[kFinishGroup][4];
 #pragma unroll
@@ -368,17 +365,23 @@ __global__ void __launch_bounds__(288) joined_finish_kernel(const float* __restr
 #pragma unroll
         for (int j = 0; j < 4; ++j)
           if (g < nb) products[8][g * 128 + lane + 32 * j] = round_to(kAct, acc[g][j]);
-    }
+    } else {
+      float val[kFinishGroup][4];
 #pragma unroll
-    for (int g = 0; g < kFinishGroup; ++g) {
-      if (g >= nb || dense_shared) break;
-      hadamard128(val[g], lane);
+      for (int g = 0; g < kFinishGroup; ++g)
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int col = (b0 + g) * 128 + lane + 32 * j;
-        const float value =
-            ok ? round_to(kAct, __fmul_rn(val[g][j], load_scale(out_scale, kScale, e * features + col))) : 0.0f;
-        products[slot][g * 128 + lane + 32 * j] = slot < 8 ? __fmul_rn(value, score) : value;
+        for (int j = 0; j < 4; ++j) val[g][j] = (ok && g < nb) ? __ldcs(src + (b0 + g) * 128 + 32 * j) : 0.0f;
+#pragma unroll
+      for (int g = 0; g < kFinishGroup; ++g) {
+        if (g >= nb) break;
+        hadamard128(val[g], lane);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int col = (b0 + g) * 128 + lane + 32 * j;
+          const float value =
+              ok ? round_to(kAct, __fmul_rn(val[g][j], load_scale(out_scale, kScale, e * features + col))) : 0.0f;
+          products[slot][g * 128 + lane + 32 * j] = slot < 8 ? __fmul_rn(value, score) : value;
+        }
       }
     }
     __syncthreads();
