@@ -268,6 +268,24 @@ int exlr8_moe_layer(const void* x, int x_dtype, const void* residual, int64_t to
                     void* out, uint32_t* indices, float* scores, void* workspace, size_t workspace_bytes,
                     void* stream);
 
+/* ---- pinned host buffers ------------------------------------------------ */
+
+/* Device-accessible address of a buffer the layer's kernels may read or
+ * write: device (or managed) memory as is, page-locked host memory
+ * (cudaHostAlloc / cudaHostRegister, e.g. torch pin_memory) at its mapped
+ * address.  Pageable host memory is refused (EXLR8_ERR_ARG): no kernel ever
+ * dereferences it.  Passing a page-locked `out` this way to exlr8_moe_layer
+ * makes its finishing kernel write the result to the host directly.  No
+ * counterpart in the reference (MLX's unified memory needs no transfer). */
+int exlr8_host_device_pointer(const void* ptr, void** device_ptr);
+
+/* A step's two inputs from page-locked host (or device) memory into device
+ * buffers, dst0 <- src0 and dst1 <- src1, `bytes` each, by one kernel at the
+ * head of the layer's launch chain instead of copy-engine transfers.  Every
+ * pointer 16-byte aligned and accepted by exlr8_host_device_pointer (host
+ * pointers are translated here); bytes a multiple of 16. */
+int exlr8_stage_in(const void* src0, void* dst0, const void* src1, void* dst1, int64_t bytes, void* stream);
+
 /* ---- kernel timing ----------------------------------------------------- */
 
 /* Kernel kinds reported by exlr8_profile_read. */

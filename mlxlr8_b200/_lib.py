@@ -97,6 +97,8 @@ _SIGNATURES = {
     "exlr8_moe_layer_workspace": (c_size_t, [c_int64, c_int, c_int, c_int64]),
     "exlr8_moe_layer": (c_int, [c_void_p, c_int, c_void_p, c_int64, c_void_p, c_void_p, POINTER(TrellisExperts),
                                 POINTER(DenseExpert), c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),
+    "exlr8_host_device_pointer": (c_int, [c_void_p, POINTER(c_void_p)]),
+    "exlr8_stage_in": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_void_p]),
     "exlr8_workspace_bad_ids": (c_int, [c_void_p, POINTER(c_int64), c_void_p]),
     "exlr8_profile_enable": (c_int, [c_int, c_int]),
     "exlr8_profile_read": (c_int, [c_int, POINTER(c_int64), POINTER(ctypes.c_double)]),
@@ -207,6 +209,14 @@ def ptr(t: torch.Tensor | None) -> int | None:
 
 def stream_handle(device: torch.device) -> int:
     return torch.cuda.current_stream(device).cuda_stream
+
+
+def host_device_pointer(t: torch.Tensor) -> int:
+    """Device-accessible address of a page-locked host tensor's data, for a
+    kernel that reads or writes it over PCIe (pageable memory is refused)."""
+    ptr = c_void_p(0)
+    check(load().exlr8_host_device_pointer(t.data_ptr(), ctypes.byref(ptr)))
+    return int(ptr.value)
 
 
 def act_code(t: torch.Tensor) -> int:

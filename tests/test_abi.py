@@ -148,3 +148,18 @@ def test_dispatch_plan_and_combine_reject_bad_arguments_without_a_gpu():
     assert narrow != 0 and "argument" in lib.exlr8_status_string(narrow).decode().lower()
     assert lib.exlr8_dispatch_plan(p, 100, 257, 0, p, p, p, 100, p, p, ws, None) == narrow
     assert lib.exlr8_combine(p, p, p, 1, 128, 99, p, None) != 0
+
+
+def test_host_buffer_entries_reject_bad_arguments_without_a_gpu():
+    """exlr8_stage_in / exlr8_host_device_pointer check sizes, nulls and
+    alignment before any CUDA call (codes EXLR8_ERR_ARG = 11, EXLR8_ERR_ALIGN
+    = 9)."""
+    lib = _lib.lib()
+    out = ctypes.c_void_p(0)
+    assert lib.exlr8_host_device_pointer(None, ctypes.byref(out)) == 11
+    assert lib.exlr8_host_device_pointer(4096, None) == 11
+    assert lib.exlr8_stage_in(4096, 8192, 12288, 16384, 0, None) == 0
+    assert lib.exlr8_stage_in(4096, 8192, 12288, 16384, 24, None) == 11
+    assert lib.exlr8_stage_in(4096, 8192, 12288, 16384, -16, None) == 11
+    assert lib.exlr8_stage_in(None, 8192, 12288, 16384, 16, None) == 11
+    assert lib.exlr8_stage_in(4096, 8192, 12288, 16392, 16, None) == 9

@@ -106,3 +106,57 @@ def test_graph_mode_with_pinned_host_buffers():
         torch.cuda.synchronize()
         assert torch.equal(oh, want.cpu())
     moe.clear_graphs()
+
+
+@pytest.mark.parametrize("tokens", [1, 40])
+def test_eager_host_buffers_match_the_device_call(tokens):
+    """Pinned host x / residual / out without a graph: the staging kernel
+    reads the inputs over PCIe and the finishing kernel writes ``out`` on the
+    host; equal to the device call bit for bit (40 tokens take the grouped
+    GEMM path).  Without ``out`` the result is a new pinned host tensor."""
+    import torch
+
+    from mlxlr8_b200.moe import MoELayer
+    from mlxlr8_b200.synthetic import make_layer
+
+    layer = make_layer(seed=23, hidden=256, intermediate=128, shared="bf16")
+    moe = MoELayer(layer.gate_weight, layer.bias, layer.experts)
+    x, r = layer.tokens(tokens, seed_offset=90)
+    xh, rh = x.cpu().pin_memory(), r.cpu().pin_memory()
+    oh = torch.empty_like(xh).pin_memory()
+    got, ids, scores = moe(xh, rh, out=oh, return_routing=True)
+    want, wids, wscores = moe(x, r, return_routing=True)
+    torch.cuda.synchronize()
+    assert got.data_ptr() == oh.data_ptr()
+    assert torch.equal(oh, want.cpu())
+    assert torch.equal(ids, wids) and torch.equal(scores, wscores)
+    fresh = moe(xh, rh)
+    torch.cuda.synchronize()
+    assert fresh.is_pinned() and torch.equal(fresh, want.cpu())
+
+
+def test_host_buffers_refuse_pageable_memory():
+    """Pageable host tensors are refused on the host (the layer's check, and
+    the library's pointer-kind check behind it): no kernel reads them."""
+    import ctypes
+
+    import torch
+
+    from mlxlr8_b200 import _lib
+    from mlxlr8_b200.moe import MoELayer
+    from mlxlr8_b200.synthetic import make_layer
+
+    layer = make_layer(seed=29, hidden=256, intermediate=128, shared="bf16")
+    moe = MoELayer(layer.gate_weight, layer.bias, layer.experts)
+    x, r = layer.tokens(2)
+    with pytest.raises(ValueError):
+        moe(x.cpu(), r.cpu())
+    lib = _lib.lib()
+    pageable = x.cpu()
+    dev = torch.empty_like(x)
+    ptr = ctypes.c_void_p(0)
+    assert lib.exlr8_host_device_pointer(pageable.data_ptr(), ctypes.byref(ptr)) == 11
+    nbytes = pageable.numel() * pageable.element_size()
+    assert lib.exlr8_stage_in(pageable.data_ptr(), dev.data_ptr(), pageable.data_ptr(), dev.data_ptr(), nbytes,
+                              _lib.stream_handle(dev.device)) == 11
+    assert lib.exlr8_host_device_pointer(dev.data_ptr(), ctypes.byref(ptr)) == 0 and ptr.value == dev.data_ptr()
