@@ -15,12 +15,11 @@ tokens per second.
 value: device-resident inputs, the layer call replayed from a CUDA graph.
 e2e:   the public API with pinned host buffers: per step x and residual
        cross PCIe to the GPU and the output back, inside the timed region.
-       On one GPU the call is MoELayer.__call__ with pinned host x, residual
-       and out (graph=True): the layer's first kernel reads the inputs from
-       host memory and its finishing kernel writes the output there; with
-       copy-engine copies around the device call instead, e2e was 5% lower.  On several GPUs
-       (ExpertParallelMoE.__call__) x and residual travel in one H2D copy of
-       one pinned buffer and the output in one D2H copy.
+       The call is MoELayer.__call__ (ExpertParallelMoE.__call__ on several
+       GPUs) with pinned host x, residual and out (graph=True): the layer's
+       first kernel reads the inputs from host memory and its combine writes
+       the output there; with copy-engine copies around the device call
+       instead, e2e was 5% lower on one GPU.
 roofline: the dominant kernel (trellis gate/up streaming GEMV), its launch
        durations measured with CUDA events on the launching stream during a
        profiled pass of the same K steps; algorithmic bytes = packed trellis
@@ -1051,32 +1050,23 @@ def main():
     step_bytes = u_mean * 3 * codes_per_matrix + u_mean * 49152 + 3 * HIDDEN * INTER * 2 + 256 * HIDDEN * 4 + 4 * T * HIDDEN
 
     # ---- e2e through the public API with host buffers ----
+    # The layer call (MoELayer, or ExpertParallelMoE on several GPUs) with
+    # pinned host x, residual and out, in its graph-replay mode: the graph's
+    # first kernel reads the inputs over PCIe and the combine writes the
+    # result to the pinned out (no copy-engine transfer in the chain).  Each
+    # layer's graph is captured by the priming pass below, before the warm-up,
+    # in the same order on every rank.
+    xh = [x.cpu().pin_memory() for x in xs]
+    rh = [r.cpu().pin_memory() for r in rs]
     oh = [torch.empty(T, HIDDEN, dtype=torch.bfloat16).pin_memory() for _ in range(L)]
     e2e_steps = min(args.steps, 1000)
-    if world == 1:
-        # MoELayer with pinned host x, residual and out, in its graph-replay
-        # mode: the graph's first kernel reads the inputs over PCIe and its
-        # finishing kernel writes the result to the pinned out (no copy-engine
-        # transfer in the chain).  Each layer's graph is captured by the
-        # priming pass below, before the warm-up.
-        xh = [x.cpu().pin_memory() for x in xs]
-        rh = [r.cpu().pin_memory() for r in rs]
 
-        def e2e_step(i):
-            moes[i](xh[i], rh[i], out=oh[i], graph=True)
-    else:
-        # x and residual of a step sit side by side in one pinned host buffer
-        # and one device buffer, so the step's inputs cross PCIe in one copy.
-        inh = [torch.stack([x.cpu(), r.cpu()]).pin_memory() for x, r in zip(xs, rs)]
-        ind = [torch.empty_like(b, device=device) for b in inh]
-
-        def e2e_step(i):
-            ind[i].copy_(inh[i], non_blocking=True)
-            oh[i].copy_(moes[i](ind[i][0], ind[i][1]), non_blocking=True)
+    def e2e_step(i):
+        moes[i](xh[i], rh[i], out=oh[i], graph=True)
 
     with torch.cuda.stream(stream):
         for i in range(L):
-            e2e_step(i)  # priming: every layer's first call (graph capture on one GPU)
+            e2e_step(i)  # priming: every layer's first call and its graph capture
         for s in range(args.warmup):
             e2e_step(s % L)
         barrier()
@@ -1124,6 +1114,7 @@ def main():
         graphs.clear()
         outs.clear()
         for m in moes:
+            m.clear_graphs()
             if getattr(m, "peer", None) is not None:
                 m.peer.close()
         del moes[:]
@@ -1179,6 +1170,8 @@ def main():
     # Release graphs (they hold NCCL work) before tearing down the process group.
     graphs.clear()
     outs.clear()
+    for m in moes:
+        m.clear_graphs()
     torch.cuda.synchronize()
     if world > 1:
         for m in moes:

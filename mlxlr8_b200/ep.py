@@ -276,6 +276,7 @@ class ExpertParallelMoE:
                                  or peer.max_capacity < max_tokens * 8):
             raise ValueError("the shared peer exchange does not fit this layer")
         self._side = None
+        self._host_graphs = {}
         self._shared_struct = None
         self._owner_ws = None
         if self.shared is not None:
@@ -340,8 +341,10 @@ class ExpertParallelMoE:
         _, ids, scores = router(xr, self.gate_weight, self.bias)
         return ids, scores
 
-    def _peer_call(self, xr, res, ids, scores, residual, return_routing):
-        """The layer with the peer-memory exchange (PeerExchange)."""
+    def _peer_call(self, xr, res, ids, scores, residual, return_routing, out_ptr=None):
+        """The layer with the peer-memory exchange (PeerExchange).  With
+        out_ptr (a page-locked host buffer's device address) the combine
+        writes the result there and no device output is made."""
         device = xr.device
         tokens, h = xr.shape
         if tokens > self.max_tokens:
@@ -363,17 +366,79 @@ class ExpertParallelMoE:
         values, shared = self._owner_mlp(peer.rows, peer.meta, rows, xr)
         _lib.check(lib.exlr8_ep_return(values.data_ptr(), act, h, self.world, self.rank, tokens, peer.max_capacity,
                                        peer.peers.data_ptr(), peer.region, peer.status.data_ptr(), stream))
-        out = torch.empty_like(res)
+        out = torch.empty_like(res) if out_ptr is None else None
         _lib.check(lib.exlr8_ep_combine(peer.back, act, slot_pos.data_ptr(), scores.data_ptr(), shared.data_ptr(),
-                                        res.data_ptr(), tokens, h, out.data_ptr(), stream))
-        out = out.reshape(residual.shape)
+                                        res.data_ptr(), tokens, h, out.data_ptr() if out_ptr is None else out_ptr,
+                                        stream))
+        out = None if out is None else out.reshape(residual.shape)
         if not torch.cuda.is_current_stream_capturing():
             peer.check_deferred() if self.deferred_check else peer.check()
         if return_routing:
             return out, ids, scores
         return out
 
-    def __call__(self, x, residual, return_routing=False):
+    def __call__(self, x, residual, return_routing=False, out=None, graph=False):
+        """``residual + moe(x)`` for this rank's tokens.  Every rank makes the
+        same calls in the same order (the exchange is collective).
+
+        Pinned host x and residual: the library's staging kernel reads them
+        over PCIe at the head of the launch chain and the combine writes the
+        result straight into ``out`` (a pinned host tensor, made here when not
+        given), asynchronously on the current stream.  ``graph=True`` (host
+        tensors and ``out``): the call is captured into a CUDA graph once per
+        (x, residual, out) address triple and replayed on later calls --
+        every rank must then capture and replay in the same order."""
+        if x.device.type == "cpu":
+            return self._host_call(x, residual, out, graph, return_routing)
+        if out is not None or graph:
+            raise ValueError("out= and graph=True take pinned host tensors")
+        return self._device_call(x, residual, return_routing)
+
+    def _host_call(self, x, residual, out, graph, return_routing):
+        h = self.local.hidden
+        if x.shape[-1] != h or residual.shape != x.shape or (out is not None and out.shape != x.shape):
+            raise ValueError("host buffers take x, residual and out of one shape [..., hidden]")
+        if out is None:
+            if graph:
+                raise ValueError("host graph mode takes an out tensor (the graph holds its address)")
+            out = torch.empty(x.shape, dtype=x.dtype, pin_memory=True)
+        if not all(t.device.type == "cpu" and t.is_pinned() and t.is_contiguous() and t.dtype == x.dtype
+                   for t in (x, residual, out)):
+            raise ValueError("host buffers must be contiguous page-locked (pinned) tensors of one dtype")
+        _lib.act_code(x)
+        device = self.gate_weight.device
+        tokens = x.numel() // h
+        key = (x.data_ptr(), residual.data_ptr(), out.data_ptr(), tokens, x.dtype)
+        entry = self._host_graphs.get(key) if graph else None
+        if entry is None:
+            xd = torch.empty(tokens, h, dtype=x.dtype, device=device)
+            rd = torch.empty_like(xd)
+            out_ptr = _lib.host_device_pointer(out)
+            nbytes = x.numel() * x.element_size()
+
+            def body():
+                _lib.check(_lib.lib().exlr8_stage_in(x.data_ptr(), xd.data_ptr(), residual.data_ptr(),
+                                                     rd.data_ptr(), nbytes, _lib.stream_handle(device)))
+                return self._device_call(xd, rd, True, out_ptr=out_ptr)
+
+            _, ids, scores = body()  # eager (and, for a graph, the call before its capture)
+            if graph:
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g):
+                    _, ids, scores = body()
+                self._host_graphs[key] = (g, ids, scores, xd, rd)
+        else:
+            entry[0].replay()
+            ids, scores = entry[1], entry[2]
+        if return_routing:
+            return out, ids, scores
+        return out
+
+    def clear_graphs(self):
+        """Release the host-mode graphs (before the process group goes away)."""
+        self._host_graphs.clear()
+
+    def _device_call(self, x, residual, return_routing=False, out_ptr=None):
         device = _lib.require_cuda(x, residual)
         h = self.local.hidden
         tokens = x.numel() // h
@@ -384,7 +449,7 @@ class ExpertParallelMoE:
         stream = _lib.stream_handle(device)
         cap = tokens * 8
         if self.exchange_kind == "peer" and self.world > 1:
-            return self._peer_call(xr, res, ids, scores, residual, return_routing)
+            return self._peer_call(xr, res, ids, scores, residual, return_routing, out_ptr)
         send_x = torch.empty(self.world, cap, h, dtype=x.dtype, device=device)
         send_meta = torch.empty(self.world, cap, dtype=torch.int32, device=device)
         slot_pos = torch.empty(max(tokens * 8, 1), dtype=torch.int32, device=device)
@@ -415,10 +480,11 @@ class ExpertParallelMoE:
             back = self.exchange(values.reshape(self.world, cap, h))
             main.wait_stream(self._side)
             shared.record_stream(main)
-        out = torch.empty_like(res)
+        out = torch.empty_like(res) if out_ptr is None else None
         _lib.check(lib.exlr8_ep_combine(back.data_ptr(), _lib.act_code(xr), slot_pos.data_ptr(), scores.data_ptr(),
-                                        shared.data_ptr(), res.data_ptr(), tokens, h, out.data_ptr(), stream))
-        out = out.reshape(residual.shape)
+                                        shared.data_ptr(), res.data_ptr(), tokens, h,
+                                        out.data_ptr() if out_ptr is None else out_ptr, stream))
+        out = None if out is None else out.reshape(residual.shape)
         if return_routing:
             return out, ids, scores
         return out

@@ -281,3 +281,35 @@ def test_deferred_status_check_raises_without_synchronising():
     with pytest.raises(RuntimeError, match="timed out"):
         ex.check_deferred()
     assert ex.broken
+
+
+@pytest.mark.parametrize("tokens", [1, 4])
+def test_host_buffer_modes_match_the_device_call(tokens):
+    """ExpertParallelMoE with pinned host x / residual / out (world 1, where
+    the exchange is the identity): eager and graph modes stage the inputs by
+    the library's kernel and the combine writes the pinned out; both equal
+    the device call bit for bit, and the graph replays on new contents."""
+    import torch
+
+    from mlxlr8_b200.ep import ExpertParallelMoE, shard_experts
+    from mlxlr8_b200.synthetic import make_layer
+
+    layer = make_layer(seed=43, hidden=256, intermediate=128, shared="bf16")
+    e = layer.experts
+    moe = ExpertParallelMoE(layer.gate_weight, layer.bias, shard_experts(e, 0, 1), 0, 1, shared=e.shared)
+    x, r = layer.tokens(tokens, seed_offset=5)
+    xh, rh = x.cpu().pin_memory(), r.cpu().pin_memory()
+    oh = torch.empty_like(xh).pin_memory()
+    want = moe(x, r)
+    got = moe(xh, rh, out=oh)
+    torch.cuda.synchronize()
+    assert got.data_ptr() == oh.data_ptr() and torch.equal(oh, want.cpu())
+    for step in range(3):
+        x2, r2 = layer.tokens(tokens, seed_offset=20 + step)
+        xh.copy_(x2.cpu())
+        rh.copy_(r2.cpu())
+        moe(xh, rh, out=oh, graph=True)
+        want = moe(x2, r2)
+        torch.cuda.synchronize()
+        assert torch.equal(oh, want.cpu())
+    moe.clear_graphs()
