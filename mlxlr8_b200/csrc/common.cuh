@@ -44,13 +44,17 @@ __device__ __forceinline__ float load_scale(const void* base, int dtype, int64_t
 // l + 32*j.  Stages run over index bits 1, 2, 4, ..., 64 in that order with
 // (a+b, a-b) butterflies, then a multiply by float(1/sqrt(128)); this is the
 // order of the reference transform, so results are bit-identical to it.
+// A cross-lane butterfly is one fused multiply-add with a per-lane sign:
+// fma(+1, v, o) = v + o and fma(-1, v, o) = o - v, each one rounding of the
+// exact sum (signed zeros included), the same bits as the add or subtract.
 __device__ __forceinline__ void hadamard128(float v[4], int lane) {
 #pragma unroll
   for (int bit = 1; bit < 32; bit <<= 1) {
+    const float sign = (lane & bit) ? -1.0f : 1.0f;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      float other = __shfl_xor_sync(0xffffffffu, v[j], bit);
-      v[j] = (lane & bit) ? other - v[j] : v[j] + other;
+      const float other = __shfl_xor_sync(0xffffffffu, v[j], bit);
+      v[j] = fmaf(sign, v[j], other);
     }
   }
   float a0 = v[0] + v[1], a1 = v[0] - v[1], a2 = v[2] + v[3], a3 = v[2] - v[3];
